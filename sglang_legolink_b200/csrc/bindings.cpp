@@ -1,0 +1,205 @@
+// PyTorch bindings for the sm_100a kernels.  Kernel sources (*.cu) expose
+// plain C entry points; this file checks tensors and forwards pointers and
+// the current CUDA stream.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_bf16.h>
+#include <torch/extension.h>
+
+using bf16 = __nv_bfloat16;
+
+extern "C" {
+int ll_gemm_bf16(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc, const bf16* bias, int M, int N,
+                 int K, int epilogue, int bn, int* err, cudaStream_t stream);
+int ll_gemm_bf16_small_m(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc, const bf16* bias, int M,
+                         int N, int K, int splits, float* ws, size_t ws_floats, int* tickets, int* err,
+                         cudaStream_t stream);
+int ll_gemm_small_m_splits(int N, int K);
+int ll_rmsnorm(bf16* out, const bf16* x, bf16* residual, const bf16* w, int rows, int hidden, float eps,
+               cudaStream_t stream);
+int ll_rope_qkv_write(const bf16* qkv, const int* positions, const int64_t* slots, const float* cos_sin, bf16* q_out,
+                      bf16* k_pool, bf16* v_pool, const bf16* q_norm_w, const bf16* k_norm_w, int T, int Hq, int Hkv,
+                      int head_dim, int page_size, int qkv_ld, float eps, cudaStream_t stream);
+int ll_kv_link_rope(bf16* dst_k, bf16* dst_v, const bf16* src_k, const bf16* src_v, const int64_t* src_slots,
+                    const int64_t* dst_slots, const int* local_pos, const int* global_pos, const float* cos_sin, int n,
+                    int num_layers, int Hkv, int head_dim, int src_page_size, int dst_page_size,
+                    int64_t src_layer_stride, int64_t dst_layer_stride, cudaStream_t stream);
+int ll_swiglu(bf16* out, const bf16* gu, int T, int inter, cudaStream_t stream);
+int ll_embedding(bf16* out, const int* ids, const bf16* table, int T, int hidden, int vocab_start, int vocab_end,
+                 cudaStream_t stream);
+int ll_argmax(int* out, const bf16* logits, int rows, int vocab, int ld, cudaStream_t stream);
+int ll_attn_prefill(const bf16* q, const bf16* kpool, const bf16* vpool, const int* q_indptr, const int* q_pos,
+                    const int* page_table, int pt_stride, const int* tiles, int ntiles, bf16* out, int Hq, int Hkv,
+                    int head_dim, int page_size, float scale, cudaStream_t stream);
+int ll_attn_decode(const bf16* q, const bf16* kpool, const bf16* vpool, const int* page_table, int pt_stride,
+                   const int* kv_lens, bf16* out, float* ws_o, float* ws_ml, int B, int Hq, int Hkv, int head_dim,
+                   int page_size, int nsplit, float scale, cudaStream_t stream);
+}
+
+namespace {
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bfloat16")
+#define CHECK_I32(x) TORCH_CHECK((x).scalar_type() == at::kInt, #x " must be int32")
+#define CHECK_I64(x) TORCH_CHECK((x).scalar_type() == at::kLong, #x " must be int64")
+#define CHECK_F32(x) TORCH_CHECK((x).scalar_type() == at::kFloat, #x " must be float32")
+#define CHECK_CONTIG(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
+
+inline bf16* bp(const at::Tensor& t) { return reinterpret_cast<bf16*>(t.data_ptr()); }
+inline bf16* bp_opt(const c10::optional<at::Tensor>& t) { return t.has_value() ? bp(*t) : nullptr; }
+inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_rc(int rc, const char* what) { TORCH_CHECK(rc == 0, what, " failed with code ", rc); }
+
+// out[M, N] = a[M, K] @ w[N, K]^T (+ bias).  a/out may be row-strided views.
+void gemm(const at::Tensor& a, const at::Tensor& w, const c10::optional<at::Tensor>& bias, at::Tensor& out,
+          int64_t epilogue, int64_t bn, const at::Tensor& err) {
+  CHECK_CUDA(a); CHECK_BF16(a); CHECK_BF16(w); CHECK_BF16(out); CHECK_CONTIG(w);
+  TORCH_CHECK(a.dim() == 2 && w.dim() == 2 && out.dim() == 2);
+  TORCH_CHECK(a.stride(1) == 1 && out.stride(1) == 1, "inner dim must be contiguous");
+  const int M = a.size(0), K = a.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K);
+  if (epilogue == 1) {
+    TORCH_CHECK(out.size(1) == N / 2 && out.size(0) == M);
+  } else {
+    TORCH_CHECK(out.size(1) == N && out.size(0) == M);
+  }
+  if (bias.has_value()) { CHECK_BF16(*bias); TORCH_CHECK(bias->numel() == N); }
+  c10::cuda::CUDAGuard g(a.device());
+  check_rc(ll_gemm_bf16(bp(a), a.stride(0), bp(w), w.stride(0), bp(out), out.stride(0), bp_opt(bias), M, N, K,
+                        (int)epilogue, (int)bn, err.data_ptr<int>(), cur_stream()),
+           "ll_gemm_bf16");
+}
+
+void gemm_small_m(const at::Tensor& a, const at::Tensor& w, const c10::optional<at::Tensor>& bias, at::Tensor& out,
+                  int64_t splits, at::Tensor& ws, at::Tensor& tickets, const at::Tensor& err) {
+  CHECK_CUDA(a); CHECK_BF16(a); CHECK_BF16(w); CHECK_BF16(out); CHECK_CONTIG(w); CHECK_F32(ws); CHECK_I32(tickets);
+  TORCH_CHECK(a.stride(1) == 1 && out.stride(1) == 1);
+  const int M = a.size(0), K = a.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && out.size(0) == M && out.size(1) == N);
+  c10::cuda::CUDAGuard g(a.device());
+  check_rc(ll_gemm_bf16_small_m(bp(a), a.stride(0), bp(w), w.stride(0), bp(out), out.stride(0), bp_opt(bias), M, N,
+                                K, (int)splits, ws.data_ptr<float>(), (size_t)ws.numel(), tickets.data_ptr<int>(),
+                                err.data_ptr<int>(), cur_stream()),
+           "ll_gemm_bf16_small_m");
+}
+
+int64_t gemm_small_m_splits(int64_t N, int64_t K) { return ll_gemm_small_m_splits((int)N, (int)K); }
+
+void rmsnorm(at::Tensor& out, const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w,
+             double eps) {
+  CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(out); CHECK_BF16(w); CHECK_CONTIG(x); CHECK_CONTIG(out);
+  const int hidden = x.size(-1);
+  const int rows = x.numel() / hidden;
+  bf16* res = nullptr;
+  if (residual.has_value()) { CHECK_BF16(*residual); CHECK_CONTIG(*residual); res = bp(*residual); }
+  c10::cuda::CUDAGuard g(x.device());
+  check_rc(ll_rmsnorm(bp(out), bp(x), res, bp(w), rows, hidden, (float)eps, cur_stream()), "ll_rmsnorm");
+}
+
+void rope_qkv_write(const at::Tensor& qkv, const at::Tensor& positions, const at::Tensor& slots,
+                    const at::Tensor& cos_sin, at::Tensor& q_out, at::Tensor& k_pool_l, at::Tensor& v_pool_l,
+                    const c10::optional<at::Tensor>& q_norm_w, const c10::optional<at::Tensor>& k_norm_w,
+                    int64_t Hq, int64_t Hkv, int64_t head_dim, double eps) {
+  CHECK_CUDA(qkv); CHECK_BF16(qkv); CHECK_I32(positions); CHECK_I64(slots); CHECK_F32(cos_sin);
+  CHECK_BF16(q_out); CHECK_BF16(k_pool_l); CHECK_BF16(v_pool_l);
+  TORCH_CHECK(qkv.stride(1) == 1);
+  const int T = qkv.size(0);
+  const int ps = k_pool_l.size(2);
+  c10::cuda::CUDAGuard g(qkv.device());
+  check_rc(ll_rope_qkv_write(bp(qkv), positions.data_ptr<int>(), slots.data_ptr<int64_t>(), cos_sin.data_ptr<float>(),
+                             bp(q_out), bp(k_pool_l), bp(v_pool_l), bp_opt(q_norm_w), bp_opt(k_norm_w), T, Hq, Hkv,
+                             head_dim, ps, qkv.stride(0), (float)eps, cur_stream()),
+           "ll_rope_qkv_write");
+}
+
+// Pools are [L, pages, Hkv, page_size, D].  src pools may be raw peer
+// addresses (src_k_ptr/src_v_ptr != 0) for the cross-replica link.
+void kv_link_rope(at::Tensor& k_pool, at::Tensor& v_pool, int64_t src_k_ptr, int64_t src_v_ptr,
+                  int64_t src_page_size, int64_t src_layer_stride, const at::Tensor& src_slots,
+                  const at::Tensor& dst_slots, const at::Tensor& local_pos, const at::Tensor& global_pos,
+                  const at::Tensor& cos_sin) {
+  CHECK_CUDA(k_pool); CHECK_BF16(k_pool); CHECK_BF16(v_pool); CHECK_I64(src_slots); CHECK_I64(dst_slots);
+  CHECK_I32(local_pos); CHECK_I32(global_pos); CHECK_F32(cos_sin); CHECK_CONTIG(k_pool); CHECK_CONTIG(v_pool);
+  const int L = k_pool.size(0), Hkv = k_pool.size(2), ps = k_pool.size(3), D = k_pool.size(4);
+  const int n = src_slots.numel();
+  const bf16* sk = src_k_ptr ? reinterpret_cast<const bf16*>(src_k_ptr) : bp(k_pool);
+  const bf16* sv = src_v_ptr ? reinterpret_cast<const bf16*>(src_v_ptr) : bp(v_pool);
+  const int sps = src_k_ptr ? (int)src_page_size : ps;
+  const int64_t sls = src_k_ptr ? src_layer_stride : k_pool.stride(0);
+  c10::cuda::CUDAGuard g(k_pool.device());
+  check_rc(ll_kv_link_rope(bp(k_pool), bp(v_pool), sk, sv, src_slots.data_ptr<int64_t>(), dst_slots.data_ptr<int64_t>(),
+                           local_pos.data_ptr<int>(), global_pos.data_ptr<int>(), cos_sin.data_ptr<float>(), n, L, Hkv,
+                           D, sps, ps, sls, k_pool.stride(0), cur_stream()),
+           "ll_kv_link_rope");
+}
+
+void swiglu(at::Tensor& out, const at::Tensor& gu) {
+  CHECK_CUDA(gu); CHECK_BF16(gu); CHECK_CONTIG(gu); CHECK_CONTIG(out);
+  c10::cuda::CUDAGuard g(gu.device());
+  check_rc(ll_swiglu(bp(out), bp(gu), gu.size(0), gu.size(1) / 2, cur_stream()), "ll_swiglu");
+}
+
+void embedding(at::Tensor& out, const at::Tensor& ids, const at::Tensor& table, int64_t vocab_start) {
+  CHECK_CUDA(ids); CHECK_I32(ids); CHECK_BF16(table); CHECK_CONTIG(table); CHECK_CONTIG(out);
+  c10::cuda::CUDAGuard g(ids.device());
+  check_rc(ll_embedding(bp(out), ids.data_ptr<int>(), bp(table), ids.numel(), table.size(1), (int)vocab_start,
+                        (int)(vocab_start + table.size(0)), cur_stream()),
+           "ll_embedding");
+}
+
+void argmax(at::Tensor& out, const at::Tensor& logits) {
+  CHECK_CUDA(logits); CHECK_BF16(logits); CHECK_I32(out);
+  TORCH_CHECK(logits.stride(1) == 1);
+  c10::cuda::CUDAGuard g(logits.device());
+  check_rc(ll_argmax(out.data_ptr<int>(), bp(logits), logits.size(0), logits.size(1), logits.stride(0), cur_stream()),
+           "ll_argmax");
+}
+
+void attn_prefill(const at::Tensor& q, const at::Tensor& k_pool_l, const at::Tensor& v_pool_l,
+                  const at::Tensor& q_indptr, const at::Tensor& q_pos, const at::Tensor& page_table,
+                  const at::Tensor& tiles, at::Tensor& out, double scale) {
+  CHECK_CUDA(q); CHECK_BF16(q); CHECK_CONTIG(q); CHECK_I32(q_indptr); CHECK_I32(q_pos); CHECK_I32(page_table);
+  CHECK_I32(tiles); CHECK_CONTIG(tiles); CHECK_CONTIG(out);
+  const int Hq = q.size(1), D = q.size(2);
+  const int Hkv = k_pool_l.size(1), ps = k_pool_l.size(2);
+  c10::cuda::CUDAGuard g(q.device());
+  check_rc(ll_attn_prefill(bp(q), bp(k_pool_l), bp(v_pool_l), q_indptr.data_ptr<int>(), q_pos.data_ptr<int>(),
+                           page_table.data_ptr<int>(), page_table.stride(0), tiles.data_ptr<int>(), tiles.size(0),
+                           bp(out), Hq, Hkv, D, ps, (float)scale, cur_stream()),
+           "ll_attn_prefill");
+}
+
+void attn_decode(const at::Tensor& q, const at::Tensor& k_pool_l, const at::Tensor& v_pool_l,
+                 const at::Tensor& page_table, const at::Tensor& kv_lens, at::Tensor& out, at::Tensor& ws_o,
+                 at::Tensor& ws_ml, int64_t nsplit, double scale) {
+  CHECK_CUDA(q); CHECK_BF16(q); CHECK_CONTIG(q); CHECK_I32(page_table); CHECK_I32(kv_lens); CHECK_CONTIG(out);
+  const int B = q.size(0), Hq = q.size(1), D = q.size(2);
+  const int Hkv = k_pool_l.size(1), ps = k_pool_l.size(2);
+  if (nsplit > 1) {
+    TORCH_CHECK(ws_o.numel() >= (int64_t)B * Hq * nsplit * D && ws_ml.numel() >= (int64_t)B * Hq * nsplit * 2,
+                "decode workspace too small");
+  }
+  c10::cuda::CUDAGuard g(q.device());
+  check_rc(ll_attn_decode(bp(q), bp(k_pool_l), bp(v_pool_l), page_table.data_ptr<int>(), page_table.stride(0),
+                          kv_lens.data_ptr<int>(), bp(out), ws_o.data_ptr<float>(), ws_ml.data_ptr<float>(), B, Hq,
+                          Hkv, D, ps, (int)nsplit, (float)scale, cur_stream()),
+           "ll_attn_decode");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels for the LegoLink B200 runtime";
+  m.def("gemm", &gemm);
+  m.def("gemm_small_m", &gemm_small_m);
+  m.def("gemm_small_m_splits", &gemm_small_m_splits);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("rope_qkv_write", &rope_qkv_write);
+  m.def("kv_link_rope", &kv_link_rope);
+  m.def("swiglu", &swiglu);
+  m.def("embedding", &embedding);
+  m.def("argmax", &argmax);
+  m.def("attn_prefill", &attn_prefill);
+  m.def("attn_decode", &attn_decode);
+}

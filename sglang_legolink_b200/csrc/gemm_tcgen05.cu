@@ -1,0 +1,545 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), fed by TMA.
+//
+//   C[M, N] = A[M, K] . W[N, K]^T (+ bias[N])          (nn.Linear layout)
+//
+// Two kernels share the same pipeline pieces:
+//
+// * gemm_tcgen05_kernel -- persistent, one CTA per SM, 128 x BN output tiles.
+//   warp 0 issues TMA loads of A/W k-blocks into a STAGES-deep shared-memory
+//   ring (128-byte swizzle), warp 1 allocates TMEM and one elected thread
+//   issues tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM accumulators,
+//   warps 2..5 drain the other accumulator (tcgen05.ld) so the epilogue of
+//   tile i overlaps the main loop of tile i+1.
+//   Epilogues: plain (+bias) and SwiGLU, where W's rows are interleaved in
+//   groups of 16 (gate rows, then the matching up rows) so that every
+//   32-column chunk of the accumulator yields 16 outputs silu(g) * u.
+//
+// * gemm_swapab_kernel -- for small M (decode): computes C^T = W . A^T so the
+//   weight tile fills the M=128 side of the MMA and the few activation rows
+//   sit on the N side (N = 16/32/64/128).  K is split across CTAs so that
+//   every SM streams weights; partial sums go to an fp32 workspace and the
+//   last CTA of each output tile (atomic ticket) reduces and writes bf16.
+//
+// The reference runs these GEMMs through cuBLAS via torch linear layers
+// (reference patched_sglang_files/python/sglang/srt/models/qwen2.py:63-217).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+
+namespace ll {
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+
+enum Epilogue : int { kEpiPlain = 0, kEpiSwiGLU = 1 };
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
+  static constexpr int B_BYTES = BN * GEMM_BK * 2;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        bf16* __restrict__ C, const bf16* __restrict__ bias, int M, int N, int K, int ldc,
+                        int* err) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (M + GEMM_BM - 1) / GEMM_BM;
+  const int num_n = (N + BN - 1) / BN;
+  const int ntiles = num_m * num_n;
+  const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmA);
+      prefetch_tmap(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const int mb = t % num_m, nb = t / num_m;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrSmemEmptyTimeout)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + Cfg::B_BYTES);
+          tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, &full[stage], kb * GEMM_BK, mb * GEMM_BM);
+          tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, &full[stage], kb * GEMM_BK, nb * BN);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Give in-flight bulk copies time to land before the CTA exits.
+        unsigned long long t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 2000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16_f32(GEMM_BM, BN);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, aphase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], aphase ^ 1, err, kErrTmemEmptyTimeout)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, err, kErrTmaFullTimeout)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = umma_desc_sw128_kmajor(smem_u32(sA + stage * Cfg::A_BYTES));
+          const uint64_t bd = umma_desc_sw128_kmajor(smem_u32(sB + stage * Cfg::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < GEMM_BK / 16; ++k) {
+            umma_bf16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          aphase ^= 1;
+        }
+      }
+      // Drain: wait until every MMA this thread issued has completed before
+      // the accumulator memory is released.
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0);
+    }
+    __syncwarp();
+  } else {
+    // Epilogue warps 2..5: warp (w % 4) owns TMEM lanes [32*(w%4), +32).
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t aphase = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      const int mb = t % num_m, nb = t / num_m;
+      if (!mbar_wait(&tfull[acc], aphase, err, kErrTmemFullTimeout)) break;
+      tc_fence_after();
+      const int row = mb * GEMM_BM + q * 32 + lane;
+      const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tbase + c, r);
+        tmem_ld_wait();
+        const int col0 = nb * BN + c;
+        if (row < M && col0 < N) {
+          if constexpr (EPI == kEpiSwiGLU) {
+            // 16 gate columns then the 16 matching up columns.
+            bf16* dst = C + (size_t)row * ldc + (col0 >> 1);
+            uint32_t packed[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              float g0 = __uint_as_float(r[2 * i]), g1 = __uint_as_float(r[2 * i + 1]);
+              float u0 = __uint_as_float(r[16 + 2 * i]), u1 = __uint_as_float(r[16 + 2 * i + 1]);
+              if (bias != nullptr) {
+                g0 += __bfloat162float(bias[col0 + 2 * i]);
+                g1 += __bfloat162float(bias[col0 + 2 * i + 1]);
+                u0 += __bfloat162float(bias[col0 + 16 + 2 * i]);
+                u1 += __bfloat162float(bias[col0 + 16 + 2 * i + 1]);
+              }
+              packed[i] = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
+            }
+            uint4* d4 = reinterpret_cast<uint4*>(dst);
+            d4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            d4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+          } else {
+            bf16* dst = C + (size_t)row * ldc + col0;
+            if (col0 + 32 <= N) {
+              uint32_t packed[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                float a0 = __uint_as_float(r[2 * i]), a1 = __uint_as_float(r[2 * i + 1]);
+                if (bias != nullptr) {
+                  a0 += __bfloat162float(bias[col0 + 2 * i]);
+                  a1 += __bfloat162float(bias[col0 + 2 * i + 1]);
+                }
+                packed[i] = pack_bf16x2(a0, a1);
+              }
+              uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+            } else {
+              for (int i = 0; i < 32 && col0 + i < N; ++i) {
+                float a = __uint_as_float(r[i]);
+                if (bias != nullptr) a += __bfloat162float(bias[col0 + i]);
+                dst[i] = __float2bfloat16(a);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        aphase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+}
+
+// ---------------------------------------------------------------------------
+// Small-M (swap-AB, split-K) kernel.
+//   D^T[128 features, BNX rows] = W_tile[128, K] . A[BNX, K]^T
+// grid = (feature tiles, splits); each CTA does k-blocks [kb0, kb1).
+template <int BNX>
+struct SwapCfg {
+  static constexpr int STAGES = 8;
+  static constexpr int W_BYTES = GEMM_BM * GEMM_BK * 2;  // 16 KB
+  static constexpr int X_BYTES = BNX * GEMM_BK * 2;
+  static constexpr int TMEM_COLS = BNX < 32 ? 32 : BNX;
+  static constexpr int SMEM = STAGES * (W_BYTES + X_BYTES) + 1024 + 256;
+};
+
+template <int BNX>
+__global__ void __launch_bounds__(192, 1)
+    gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                       bf16* __restrict__ C, const bf16* __restrict__ bias, int M, int N, int K, int ldc,
+                       int kb_per_split, float* __restrict__ ws, int* __restrict__ tickets, int* err) {
+  using Cfg = SwapCfg<BNX>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sW = smem;
+  uint8_t* sX = smem + STAGES * Cfg::W_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sX + STAGES * Cfg::X_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+  __shared__ int s_last;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = blockIdx.x;  // feature tile
+  const int split = blockIdx.y, nsplit = gridDim.y;
+  const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
+  const int kb0 = split * kb_per_split;
+  const int kb1 = min(num_kb, kb0 + kb_per_split);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmW);
+      prefetch_tmap(&tmX);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrSmemEmptyTimeout)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[stage], Cfg::W_BYTES + Cfg::X_BYTES);
+        tma_load_2d(sW + stage * Cfg::W_BYTES, &tmW, &full[stage], kb * GEMM_BK, nb * GEMM_BM);
+        tma_load_2d(sX + stage * Cfg::X_BYTES, &tmX, &full[stage], kb * GEMM_BK, 0);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) {
+        unsigned long long t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 2000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16_f32(GEMM_BM, BNX);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full[stage], phase, err, kErrTmaFullTimeout)) break;
+        tc_fence_after();
+        const uint64_t ad = umma_desc_sw128_kmajor(smem_u32(sW + stage * Cfg::W_BYTES));
+        const uint64_t bd = umma_desc_sw128_kmajor(smem_u32(sX + stage * Cfg::X_BYTES));
+#pragma unroll
+        for (int k = 0; k < GEMM_BK / 16; ++k)
+          umma_bf16(tmem_base, ad + 2 * k, bd + 2 * k, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+        umma_commit(&empty[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      umma_commit(tfull);
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;
+    const int feat = nb * GEMM_BM + q * 32 + lane;  // output column of C
+    bool ok = mbar_wait(tfull, 0, err, kErrTmemFullTimeout);
+    tc_fence_after();
+    const bool empty_split = (kb1 <= kb0);
+    const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16);
+#pragma unroll 1
+    for (int c = 0; c < BNX; c += 32) {
+      uint32_t r[32];
+      if constexpr (BNX >= 32) {
+        tmem_ld_32x32b_x32(tbase + c, r);
+      } else {
+        tmem_ld_32x32b_x32(tbase, r);  // columns >= BNX hold garbage; ignored
+      }
+      tmem_ld_wait();
+      if (!ok) continue;
+      const int ncols = BNX < 32 ? BNX : 32;
+      if (nsplit == 1) {
+        if (feat < N) {
+          const float b = bias != nullptr ? __bfloat162float(bias[feat]) : 0.f;
+          for (int i = 0; i < ncols; ++i) {
+            const int m = c + i;
+            if (m < M) C[(size_t)m * ldc + feat] = __float2bfloat16(__uint_as_float(r[i]) + b);
+          }
+        }
+      } else if (feat < N) {
+        float* w = ws + ((size_t)split * M) * N;
+        for (int i = 0; i < ncols; ++i) {
+          const int m = c + i;
+          if (m < M) w[(size_t)m * N + feat] = empty_split ? 0.f : __uint_as_float(r[i]);
+        }
+      }
+    }
+    if (nsplit > 1) {
+      // Split-K fix-up: the last CTA of this feature tile reduces all splits.
+      __threadfence();
+      asm volatile("bar.sync 1, 128;");
+      if (threadIdx.x == 64) {
+        const int prev = atomicAdd(&tickets[nb], 1);
+        s_last = (prev == nsplit - 1);
+      }
+      asm volatile("bar.sync 1, 128;");
+      if (s_last) {
+        __threadfence();
+        if (feat < N) {
+          const float b = bias != nullptr ? __bfloat162float(bias[feat]) : 0.f;
+          for (int m = 0; m < M; ++m) {
+            float s = b;
+            for (int sp = 0; sp < nsplit; ++sp) s += __ldcg(ws + ((size_t)sp * M + m) * N + feat);
+            C[(size_t)m * ldc + feat] = __float2bfloat16(s);
+          }
+        }
+        if (threadIdx.x == 64) tickets[nb] = 0;  // ready for the next launch / graph replay
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix (cols contiguous),
+// box = [box_rows, 64 cols], 128-byte swizzle, zero fill out of bounds.
+static int make_tmap_2d(CUtensorMap* tm, const void* ptr, int rows, int cols, int ld, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return -1;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <typename Kern>
+static void set_smem(Kern k, int bytes) {
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+}  // namespace ll
+
+using namespace ll;
+
+// Returns 0 on success, <0 on a host-side error (bad shape / tensor map).
+extern "C" int ll_gemm_bf16(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc, const bf16* bias,
+                            int M, int N, int K, int epilogue, int bn, int* err, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if ((K % 8) || (lda % 8) || (ldw % 8)) return -3;
+  if (epilogue == kEpiSwiGLU && (N % 32)) return -4;
+  CUtensorMap tA, tB;
+  const int BN = (bn == 128) ? 128 : 256;
+  if (make_tmap_2d(&tA, A, M, K, lda, GEMM_BM)) return -2;
+  if (make_tmap_2d(&tB, W, N, K, ldw, BN)) return -2;
+  const int ntiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN);
+  const int grid = ntiles < num_sms() ? ntiles : num_sms();
+#define LL_LAUNCH(BN_, EPI_)                                                                          \
+  do {                                                                                                \
+    auto kern = gemm_tcgen05_kernel<BN_, EPI_>;                                                       \
+    static bool init = false;                                                                         \
+    if (!init) {                                                                                      \
+      set_smem(kern, GemmCfg<BN_>::SMEM);                                                             \
+      init = true;                                                                                    \
+    }                                                                                                 \
+    kern<<<grid, 192, GemmCfg<BN_>::SMEM, stream>>>(tA, tB, C, bias, M, N, K, ldc, err);              \
+  } while (0)
+  if (BN == 256) {
+    if (epilogue == kEpiSwiGLU) LL_LAUNCH(256, kEpiSwiGLU); else LL_LAUNCH(256, kEpiPlain);
+  } else {
+    if (epilogue == kEpiSwiGLU) LL_LAUNCH(128, kEpiSwiGLU); else LL_LAUNCH(128, kEpiPlain);
+  }
+#undef LL_LAUNCH
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+// Small-M path.  ws must hold splits*M*N floats, tickets ceil(N/128) ints
+// (zero-initialised once; the kernel leaves them zero).  splits <= 0 picks a
+// split count that puts about one CTA on every SM.
+extern "C" int ll_gemm_bf16_small_m(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc,
+                                    const bf16* bias, int M, int N, int K, int splits, float* ws, size_t ws_floats,
+                                    int* tickets, int* err, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if (M > 128) return -3;
+  if ((K % 8) || (lda % 8) || (ldw % 8)) return -3;
+  const int ntiles = (N + GEMM_BM - 1) / GEMM_BM;
+  const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
+  if (splits <= 0) {
+    splits = (num_sms() + ntiles - 1) / ntiles;
+    if (splits > num_kb / 2) splits = num_kb / 2;
+    if (splits < 1) splits = 1;
+  }
+  int kb_per = (num_kb + splits - 1) / splits;
+  splits = (num_kb + kb_per - 1) / kb_per;
+  if (splits > 1 && (ws == nullptr || tickets == nullptr || ws_floats < (size_t)splits * M * N)) return -6;
+  const int BNX = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
+  CUtensorMap tW, tX;
+  if (make_tmap_2d(&tW, W, N, K, ldw, GEMM_BM)) return -2;
+  if (make_tmap_2d(&tX, A, M, K, lda, BNX)) return -2;
+  dim3 grid(ntiles, splits);
+#define LL_LAUNCH_S(BNX_)                                                                                \
+  do {                                                                                                   \
+    auto kern = gemm_swapab_kernel<BNX_>;                                                                \
+    static bool init = false;                                                                            \
+    if (!init) {                                                                                         \
+      set_smem(kern, SwapCfg<BNX_>::SMEM);                                                               \
+      init = true;                                                                                       \
+    }                                                                                                    \
+    kern<<<grid, 192, SwapCfg<BNX_>::SMEM, stream>>>(tW, tX, C, bias, M, N, K, ldc, kb_per, ws, tickets, \
+                                                     err);                                               \
+  } while (0)
+  switch (BNX) {
+    case 16: LL_LAUNCH_S(16); break;
+    case 32: LL_LAUNCH_S(32); break;
+    case 64: LL_LAUNCH_S(64); break;
+    default: LL_LAUNCH_S(128); break;
+  }
+#undef LL_LAUNCH_S
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+extern "C" int ll_gemm_small_m_splits(int N, int K) {
+  const int ntiles = (N + GEMM_BM - 1) / GEMM_BM;
+  const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
+  int splits = (num_sms() + ntiles - 1) / ntiles;
+  if (splits > num_kb / 2) splits = num_kb / 2;
+  if (splits < 1) splits = 1;
+  int kb_per = (num_kb + splits - 1) / splits;
+  return (num_kb + kb_per - 1) / kb_per;
+}

@@ -1,0 +1,327 @@
+"""Qwen2 / Qwen2.5 / Qwen3 dense decoder on the runtime's ops.
+
+Layer structure (reference ``patched_sglang_files/python/sglang/srt/models/
+qwen2.py:63-311``): fused-add RMSNorm -> QKV GEMM (+bias on Qwen2) -> [Qwen3:
+per-head q/k RMSNorm] -> RoPE + paged KV write -> attention -> o_proj ->
+fused-add RMSNorm -> gate_up GEMM with SwiGLU epilogue -> down_proj.
+
+One forward serves every batch kind through :class:`ForwardBatch`:
+
+* ``extend``  -- query rows at arbitrary positions of each request (a Compile
+  prefill from position 0, the sparse repair rows of a Link, a plain prefill);
+  every row's K/V is written before attention, and attention is causal by
+  position over the request's paged KV.
+* ``decode``  -- one row per request at position ``kv_len - 1``.
+
+Tensor parallelism (``tp_size > 1``) shards heads / intermediate features
+column-wise and reduces after o_proj / down_proj through ``self.comm`` (see
+:mod:`sglang_legolink_b200.parallel`).
+"""
+
+from __future__ import annotations
+
+import json
+import math
+import os
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+
+from .. import ops
+from ..ops import reference as ref
+from .config import ModelConfig
+
+
+@dataclass
+class ForwardBatch:
+    mode: str  # "extend" | "decode"
+    input_ids: torch.Tensor  # [T] int32
+    positions: torch.Tensor  # [T] int32
+    slots: torch.Tensor  # [T] int64   KV write slot of each row
+    q_indptr: torch.Tensor  # [B+1] int32  rows of request b: [q_indptr[b], q_indptr[b+1])
+    page_table: torch.Tensor  # [B, max_pages] int32
+    kv_lens: torch.Tensor  # [B] int32   keys visible to request b after this step's writes
+    logit_rows: Optional[torch.Tensor] = None  # [R] int64 rows whose logits are returned
+    tiles: Optional[torch.Tensor] = None  # prefill attention work list
+    decode_nsplit: Optional[int] = None
+
+    @property
+    def num_rows(self) -> int:
+        return int(self.input_ids.shape[0])
+
+
+class LayerWeights:
+    __slots__ = ("in_norm", "qkv_w", "qkv_b", "q_norm", "k_norm", "o_w", "post_norm", "gu_w", "down_w")
+
+
+class QwenModel:
+    def __init__(self, cfg: ModelConfig, device="cpu", dtype=torch.float32, tp_rank: int = 0, tp_size: int = 1,
+                 comm=None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        self.comm = comm
+        assert cfg.num_heads % tp_size == 0, "num_heads must divide by tp_size"
+        self.hq = cfg.num_heads // tp_size
+        # KV heads are split when possible, else replicated (each rank keeps one).
+        self.hkv = max(1, cfg.num_kv_heads // tp_size)
+        assert cfg.intermediate_size % (16 * tp_size) == 0
+        self.inter = cfg.intermediate_size // tp_size
+        self.layers: list[LayerWeights] = []
+        self.embed: Optional[torch.Tensor] = None
+        self.final_norm: Optional[torch.Tensor] = None
+        self.lm_head: Optional[torch.Tensor] = None
+        self.cos_sin: Optional[torch.Tensor] = None
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+        self._bufs: dict = {}
+
+    # ------------------------------------------------------------ weights
+    def _kv_head_range(self) -> tuple[int, int]:
+        c = self.cfg
+        if c.num_kv_heads >= self.tp_size:
+            return self.tp_rank * self.hkv, (self.tp_rank + 1) * self.hkv
+        rep = self.tp_size // c.num_kv_heads
+        h = self.tp_rank // rep
+        return h, h + 1
+
+    def shard_qkv(self, wq, wk, wv, bq=None, bk=None, bv=None):
+        c, r, D = self.cfg, self.tp_rank, self.cfg.head_dim
+        q0 = r * self.hq * D
+        k0, k1 = self._kv_head_range()
+        w = torch.cat([wq[q0 : q0 + self.hq * D], wk[k0 * D : k1 * D], wv[k0 * D : k1 * D]], 0)
+        b = None
+        if bq is not None:
+            b = torch.cat([bq[q0 : q0 + self.hq * D], bk[k0 * D : k1 * D], bv[k0 * D : k1 * D]], 0)
+        return w, b
+
+    def _place(self, t: torch.Tensor) -> torch.Tensor:
+        return t.to(device=self.device, dtype=self.dtype).contiguous()
+
+    def set_weights(self, get) -> None:
+        """``get(name)`` returns the full (unsharded) HF tensor for ``name``."""
+        c, D, r = self.cfg, self.cfg.head_dim, self.tp_rank
+        self.layers = []
+        for i in range(c.num_layers):
+            p = f"model.layers.{i}."
+            lw = LayerWeights()
+            lw.in_norm = self._place(get(p + "input_layernorm.weight"))
+            lw.post_norm = self._place(get(p + "post_attention_layernorm.weight"))
+            bq = bk = bv = None
+            if c.qkv_bias:
+                bq, bk, bv = (get(p + f"self_attn.{n}_proj.bias") for n in "qkv")
+            w, b = self.shard_qkv(get(p + "self_attn.q_proj.weight"), get(p + "self_attn.k_proj.weight"),
+                                  get(p + "self_attn.v_proj.weight"), bq, bk, bv)
+            lw.qkv_w = self._place(w)
+            lw.qkv_b = self._place(b) if b is not None else None
+            if c.qk_norm:
+                lw.q_norm = self._place(get(p + "self_attn.q_norm.weight"))
+                lw.k_norm = self._place(get(p + "self_attn.k_norm.weight"))
+            else:
+                lw.q_norm = lw.k_norm = None
+            o = get(p + "self_attn.o_proj.weight")
+            lw.o_w = self._place(o[:, r * self.hq * D : (r + 1) * self.hq * D])
+            gate = get(p + "mlp.gate_proj.weight")[r * self.inter : (r + 1) * self.inter]
+            up = get(p + "mlp.up_proj.weight")[r * self.inter : (r + 1) * self.inter]
+            lw.gu_w = self._place(ops.interleave_gate_up(gate, up))
+            lw.down_w = self._place(get(p + "mlp.down_proj.weight")[:, r * self.inter : (r + 1) * self.inter])
+            self.layers.append(lw)
+        emb = get("model.embed_tokens.weight")
+        self.embed = self._place(emb)
+        self.final_norm = self._place(get("model.norm.weight"))
+        head = emb if c.tie_word_embeddings else get("lm_head.weight")
+        v0, v1 = self.vocab_range()
+        self.lm_head = self._place(head[v0:v1])
+        self.cos_sin = ref.rope_cos_sin_table(c.max_position_embeddings, c.rotary_dim, c.rope_theta).to(self.device)
+
+    def vocab_range(self) -> tuple[int, int]:
+        v = self.cfg.vocab_size
+        per = (v + self.tp_size - 1) // self.tp_size
+        return self.tp_rank * per, min(v, (self.tp_rank + 1) * per)
+
+    @staticmethod
+    def random_hf_state(cfg: ModelConfig, seed: int = 0, dtype=torch.float32, device="cpu", std: float = 0.02):
+        """Random-init weights under HF Qwen names (generated on ``device``)."""
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        D, H = cfg.head_dim, cfg.hidden_size
+
+        def rnd(*shape, s=std):
+            return (torch.randn(*shape, generator=g, device=device, dtype=torch.float32) * s).to(dtype)
+
+        def ones(n):
+            return (1.0 + 0.1 * torch.randn(n, generator=g, device=device, dtype=torch.float32)).to(dtype)
+
+        st = {}
+        for i in range(cfg.num_layers):
+            p = f"model.layers.{i}."
+            st[p + "input_layernorm.weight"] = ones(H)
+            st[p + "post_attention_layernorm.weight"] = ones(H)
+            st[p + "self_attn.q_proj.weight"] = rnd(cfg.num_heads * D, H)
+            st[p + "self_attn.k_proj.weight"] = rnd(cfg.num_kv_heads * D, H)
+            st[p + "self_attn.v_proj.weight"] = rnd(cfg.num_kv_heads * D, H)
+            if cfg.qkv_bias:
+                st[p + "self_attn.q_proj.bias"] = rnd(cfg.num_heads * D, s=0.1)
+                st[p + "self_attn.k_proj.bias"] = rnd(cfg.num_kv_heads * D, s=0.1)
+                st[p + "self_attn.v_proj.bias"] = rnd(cfg.num_kv_heads * D, s=0.1)
+            if cfg.qk_norm:
+                st[p + "self_attn.q_norm.weight"] = ones(D)
+                st[p + "self_attn.k_norm.weight"] = ones(D)
+            st[p + "self_attn.o_proj.weight"] = rnd(H, cfg.num_heads * D)
+            st[p + "mlp.gate_proj.weight"] = rnd(cfg.intermediate_size, H)
+            st[p + "mlp.up_proj.weight"] = rnd(cfg.intermediate_size, H)
+            st[p + "mlp.down_proj.weight"] = rnd(H, cfg.intermediate_size)
+        st["model.embed_tokens.weight"] = rnd(cfg.vocab_size, H, s=1.0)
+        st["model.norm.weight"] = ones(H)
+        if not cfg.tie_word_embeddings:
+            st["lm_head.weight"] = rnd(cfg.vocab_size, H)
+        return st
+
+    @classmethod
+    def random_init(cls, cfg: ModelConfig, seed=0, device="cpu", dtype=torch.float32, tp_rank=0, tp_size=1,
+                    comm=None) -> "QwenModel":
+        m = cls(cfg, device, dtype, tp_rank, tp_size, comm)
+        # Generate per tensor on the target device to keep host memory small.
+        gen_dev = device if torch.device(device).type == "cuda" else "cpu"
+        state = cls.random_hf_state(cfg, seed, dtype=dtype, device=gen_dev)
+        m.set_weights(lambda n: state[n])
+        del state
+        return m
+
+    @classmethod
+    def from_pretrained(cls, path: str, device="cpu", dtype=torch.bfloat16, tp_rank=0, tp_size=1,
+                        comm=None) -> "QwenModel":
+        cfg = ModelConfig.from_pretrained(path)
+        m = cls(cfg, device, dtype, tp_rank, tp_size, comm)
+        m.set_weights(SafetensorsReader(path))
+        return m
+
+    def save_pretrained(self, path: str, state: dict) -> None:
+        save_safetensors_checkpoint(path, self.cfg, state)
+
+    # -------------------------------------------------------------- buffers
+    def _buf(self, name, shape, dtype=None):
+        dtype = dtype or self.dtype
+        b = self._bufs.get(name)
+        n = 1
+        for s in shape:
+            n *= s
+        if b is None or b.numel() < n or b.dtype != dtype:
+            b = torch.empty(max(n, 1), dtype=dtype, device=self.device)
+            self._bufs[name] = b
+        return b[:n].view(*shape)
+
+    # -------------------------------------------------------------- forward
+    def forward(self, fb: ForwardBatch, kv, return_hidden: bool = False) -> torch.Tensor:
+        """Runs all layers over ``fb``; returns logits [R, vocab(shard)] for
+        ``fb.logit_rows`` (all rows when None)."""
+        c = self.cfg
+        T = fb.num_rows
+        H, D = c.hidden_size, c.head_dim
+        qkv_n = (self.hq + 2 * self.hkv) * D
+        x = ops.embedding(fb.input_ids, self.embed, out=self._buf("x", (T, H)))
+        residual = self._buf("res", (T, H))
+        residual.copy_(x)
+        h = self._buf("h", (T, H))
+        ops.rmsnorm(residual, self.layers[0].in_norm, c.rms_norm_eps, out=h)
+        q = self._buf("q", (T, self.hq, D))
+        attn = self._buf("attn", (T, self.hq * D))
+        qkv = self._buf("qkv", (T, qkv_n))
+        mlp = self._buf("mlp", (T, self.inter))
+        o = self._buf("o", (T, H))
+        tiles = fb.tiles
+        if fb.mode == "extend" and tiles is None and fb.input_ids.is_cuda:
+            tiles = ops.prefill_tiles(fb.q_indptr.cpu(), fb.positions.cpu(), self.hq, self.hkv).to(self.device)
+        for li, lw in enumerate(self.layers):
+            if li > 0:
+                ops.fused_add_rmsnorm(h, residual, lw.in_norm, c.rms_norm_eps)
+            ops.linear(h, lw.qkv_w, lw.qkv_b, out=qkv)
+            ops.rope_qkv_write(qkv, fb.positions, fb.slots, self.cos_sin, q, kv.k[li], kv.v[li], self.hq, self.hkv,
+                               D, lw.q_norm, lw.k_norm, c.rms_norm_eps)
+            if fb.mode == "decode":
+                ops.attention_decode(q, kv.k[li], kv.v[li], fb.page_table, fb.kv_lens, self.scale,
+                                     nsplit=fb.decode_nsplit, out=attn)
+            else:
+                ops.attention_prefill(q, kv.k[li], kv.v[li], fb.q_indptr, fb.positions, fb.page_table, fb.kv_lens,
+                                      self.scale, tiles=tiles, out=attn)
+            self._row_parallel(attn, lw.o_w, o)
+            ops.fused_add_rmsnorm(o, residual, lw.post_norm, c.rms_norm_eps)
+            ops.linear(o, lw.gu_w, out=mlp, swiglu_epilogue=True)
+            self._row_parallel(mlp, lw.down_w, h)
+        # final: residual += h ; h = norm(residual)
+        ops.fused_add_rmsnorm(h, residual, self.final_norm, c.rms_norm_eps)
+        rows = h if fb.logit_rows is None else h.index_select(0, fb.logit_rows)
+        if return_hidden:
+            return rows
+        return self.logits(rows)
+
+    def _row_parallel(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> None:
+        if self.tp_size == 1 or self.comm is None:
+            ops.linear(x, w, out=out)
+        else:
+            self.comm.gemm_allreduce(x, w, out)
+
+    def logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        out = ops.linear(hidden, self.lm_head)
+        if self.tp_size > 1 and self.comm is not None:
+            out = self.comm.all_gather_vocab(out, self.cfg.vocab_size)
+        return out
+
+
+# ------------------------------------------------------------ safetensors IO
+class SafetensorsReader:
+    """Lazy name -> tensor reader over an HF checkpoint directory."""
+
+    def __init__(self, path: str):
+        from safetensors import safe_open
+
+        self.path = path
+        idx = os.path.join(path, "model.safetensors.index.json")
+        if os.path.exists(idx):
+            with open(idx, encoding="utf-8") as f:
+                wm = json.load(f)["weight_map"]
+            files = sorted(set(wm.values()))
+        else:
+            files = [f for f in os.listdir(path) if f.endswith(".safetensors")]
+            wm = None
+        self._handles = {f: safe_open(os.path.join(path, f), framework="pt") for f in files}
+        self._where = {}
+        for f, h in self._handles.items():
+            for k in h.keys():
+                self._where[k] = f
+
+    def __call__(self, name: str) -> torch.Tensor:
+        if name not in self._where:
+            raise KeyError(f"checkpoint has no tensor '{name}'")
+        return self._handles[self._where[name]].get_tensor(name)
+
+    def keys(self):
+        return list(self._where)
+
+
+def save_safetensors_checkpoint(path: str, cfg: ModelConfig, state: dict, shard_bytes: int = 4 << 30) -> None:
+    """Writes an HF-layout checkpoint (config.json + sharded safetensors + index)."""
+    from safetensors.torch import save_file
+
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "config.json"), "w", encoding="utf-8") as f:
+        json.dump(cfg.to_hf_dict(), f, indent=1)
+    shards, cur, size = [], {}, 0
+    for k in sorted(state):
+        t = state[k].contiguous().cpu()
+        if cur and size + t.numel() * t.element_size() > shard_bytes:
+            shards.append(cur)
+            cur, size = {}, 0
+        cur[k] = t
+        size += t.numel() * t.element_size()
+    if cur:
+        shards.append(cur)
+    wm = {}
+    for i, sh in enumerate(shards):
+        name = f"model-{i + 1:05d}-of-{len(shards):05d}.safetensors"
+        save_file(sh, os.path.join(path, name), metadata={"format": "pt"})
+        for k in sh:
+            wm[k] = name
+    with open(os.path.join(path, "model.safetensors.index.json"), "w", encoding="utf-8") as f:
+        json.dump({"metadata": {}, "weight_map": wm}, f, indent=1)

@@ -1,0 +1,312 @@
+"""Runtime ops.  CUDA tensors run the sm_100a kernels of ``legolink_cuda``
+(missing build -> :class:`ExtensionMissing`); CPU tensors run the fp32
+statements in :mod:`.reference`, which are also the test oracle.
+
+Conventions
+-----------
+* Linear weights are ``[out_features, in_features]`` (nn.Linear layout).
+* The fused gate/up weight is stored *interleaved in groups of 16 rows*:
+  rows ``[32j, 32j+16)`` are gate rows ``[16j, 16j+16)`` and rows
+  ``[32j+16, 32j+32)`` the matching up rows.  ``swiglu`` and the GEMM's
+  SwiGLU epilogue both read that layout (:func:`interleave_gate_up`).
+* KV pools are ``[layers, pages, kv_heads, page_size, head_dim]``.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import reference as ref
+from ._ext import ExtensionMissing, cuda as _cuda  # noqa: F401
+
+__all__ = [
+    "ExtensionMissing", "linear", "rmsnorm", "fused_add_rmsnorm", "rope_qkv_write", "attention_prefill",
+    "attention_decode", "swiglu", "embedding", "argmax", "kv_link_rope", "interleave_gate_up",
+    "deinterleave_gate_up", "prefill_tiles", "workspace", "check_errors",
+]
+
+SMALL_M_MAX = 128
+
+
+# ----------------------------------------------------------------- workspace
+class _Workspace:
+    """Per-device scratch: error word, split-K partials + tickets, decode
+    partials.  Sized up front by the engine so CUDA-graph replays never see a
+    reallocated buffer."""
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.gemm_ws = torch.empty(0, dtype=torch.float32, device=device)
+        self.tickets = torch.zeros(4096, dtype=torch.int32, device=device)
+        self.dec_o = torch.empty(0, dtype=torch.float32, device=device)
+        self.dec_ml = torch.empty(0, dtype=torch.float32, device=device)
+
+    def reserve_gemm(self, floats: int, tiles: int = 0) -> None:
+        if self.gemm_ws.numel() < floats:
+            self.gemm_ws = torch.empty(floats, dtype=torch.float32, device=self.device)
+        if self.tickets.numel() < tiles:
+            self.tickets = torch.zeros(tiles, dtype=torch.int32, device=self.device)
+
+    def reserve_decode(self, rows: int, nsplit: int, head_dim: int = 128) -> None:
+        need = rows * nsplit
+        if self.dec_o.numel() < need * head_dim:
+            self.dec_o = torch.empty(need * head_dim, dtype=torch.float32, device=self.device)
+            self.dec_ml = torch.empty(need * 2, dtype=torch.float32, device=self.device)
+
+
+_WS: dict[int, _Workspace] = {}
+
+
+def workspace(device) -> _Workspace:
+    device = torch.device(device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _WS.get(idx)
+    if ws is None:
+        ws = _WS[idx] = _Workspace(torch.device("cuda", idx))
+    return ws
+
+
+def check_errors(device) -> int:
+    """Read (and clear) the device error word set by bounded waits."""
+    ws = workspace(device)
+    code = int(ws.err.item())
+    if code:
+        ws.err.zero_()
+    return code
+
+
+# ------------------------------------------------------------------ weights
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, group: int = 16) -> torch.Tensor:
+    """[I, H] gate + [I, H] up -> [2I, H] interleaved in groups of ``group``."""
+    inter, hid = gate.shape
+    assert inter % group == 0, "intermediate size must be a multiple of 16"
+    g = gate.reshape(inter // group, group, hid)
+    u = up.reshape(inter // group, group, hid)
+    return torch.stack([g, u], dim=1).reshape(2 * inter, hid).contiguous()
+
+
+def deinterleave_gate_up(gu: torch.Tensor, group: int = 16):
+    two_i, hid = gu.shape
+    x = gu.reshape(two_i // (2 * group), 2, group, hid)
+    return x[:, 0].reshape(-1, hid), x[:, 1].reshape(-1, hid)
+
+
+# ---------------------------------------------------------------------- ops
+def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
+           out: Optional[torch.Tensor] = None, swiglu_epilogue: bool = False) -> torch.Tensor:
+    """``x @ w.T (+ bias)``; with ``swiglu_epilogue`` the result is
+    ``silu(gate) * up`` of the interleaved gate/up product (half width)."""
+    M, N = x.shape[0], w.shape[0]
+    if not x.is_cuda:
+        y = ref.linear(x, w, bias)
+        if swiglu_epilogue:
+            y = ref_swiglu_interleaved(y)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    ext = _cuda()
+    ws = workspace(x.device)
+    if out is None:
+        out = torch.empty(M, N // 2 if swiglu_epilogue else N, dtype=x.dtype, device=x.device)
+    if M <= SMALL_M_MAX and not (M > 64 and N >= 148 * 256):
+        if swiglu_epilogue:
+            tmp = torch.empty(M, N, dtype=x.dtype, device=x.device)
+            _small_m(ext, ws, x, w, bias, tmp)
+            ext.swiglu(out, tmp)
+        else:
+            _small_m(ext, ws, x, w, bias, out)
+        return out
+    bn = 256 if N >= 2048 else 128
+    ext.gemm(x, w, bias, out, 1 if swiglu_epilogue else 0, bn, ws.err)
+    return out
+
+
+def _small_m(ext, ws, x, w, bias, out):
+    M, K = x.shape
+    N = w.shape[0]
+    splits = ext.gemm_small_m_splits(N, K)
+    if splits > 1:
+        need = splits * M * N
+        if ws.gemm_ws.numel() < need or ws.tickets.numel() < (N + 127) // 128:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("GEMM workspace too small during CUDA graph capture; reserve it first")
+            ws.reserve_gemm(need, (N + 127) // 128)
+    ext.gemm_small_m(x, w, bias, out, splits, ws.gemm_ws, ws.tickets, ws.err)
+
+
+def ref_swiglu_interleaved(gu: torch.Tensor) -> torch.Tensor:
+    T, two_i = gu.shape
+    x = gu.float().reshape(T, two_i // 32, 2, 16)
+    y = torch.nn.functional.silu(x[:, :, 0]) * x[:, :, 1]
+    return y.reshape(T, two_i // 2).to(gu.dtype)
+
+
+def swiglu(gu: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not gu.is_cuda:
+        y = ref_swiglu_interleaved(gu)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(gu.shape[0], gu.shape[1] // 2, dtype=gu.dtype, device=gu.device)
+    _cuda().swiglu(out, gu)
+    return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not x.is_cuda:
+        y = ref.rmsnorm(x, w, eps)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty_like(x)
+    _cuda().rmsnorm(out, x, None, w, eps)
+    return out
+
+
+def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float) -> None:
+    """residual += x ; x = rmsnorm(residual) * w  (in place, fp32 math)."""
+    if not x.is_cuda:
+        ref.fused_add_rmsnorm(x, residual, w, eps)
+        return
+    _cuda().rmsnorm(x, x, residual, w, eps)
+
+
+def rope_qkv_write(qkv, positions, slots, cos_sin, q_out, k_pool_l, v_pool_l, num_heads, num_kv_heads,
+                   head_dim, q_norm_w=None, k_norm_w=None, eps=1e-6):
+    if not qkv.is_cuda:
+        q = ref.rope_qkv_write(qkv, positions, slots, cos_sin, k_pool_l, v_pool_l, num_heads, num_kv_heads,
+                               head_dim, q_norm_w, k_norm_w, eps)
+        q_out.copy_(q)
+        return q_out
+    _cuda().rope_qkv_write(qkv, positions, slots, cos_sin, q_out, k_pool_l, v_pool_l, q_norm_w, k_norm_w,
+                           num_heads, num_kv_heads, head_dim, eps)
+    return q_out
+
+
+def prefill_tiles(q_indptr_host: torch.Tensor, q_pos_host: torch.Tensor, num_heads: int, num_kv_heads: int,
+                  rows_per_tile: int = 64) -> torch.Tensor:
+    """Work list for the prefill/repair attention kernel: one int4
+    ``(request, kv_head, first_packed_row, max_position_in_tile)`` per CTA,
+    longest (largest max position) first."""
+    g = num_heads // num_kv_heads
+    tiles = []
+    B = q_indptr_host.numel() - 1
+    qi = q_indptr_host.tolist()
+    qp = q_pos_host
+    for b in range(B):
+        s, e = qi[b], qi[b + 1]
+        nrows = (e - s) * g
+        for r0 in range(0, nrows, rows_per_tile):
+            t_last = s + min(nrows, r0 + rows_per_tile) // g - (1 if min(nrows, r0 + rows_per_tile) % g == 0 else 0)
+            t_first = s + r0 // g
+            mp = int(qp[t_first : t_last + 1].max())
+            for hk in range(num_kv_heads):
+                tiles.append((b, hk, r0, mp))
+    if not tiles:
+        return torch.zeros(0, 4, dtype=torch.int32)
+    t = torch.tensor(tiles, dtype=torch.int32)
+    order = torch.argsort(t[:, 3], descending=True, stable=True)
+    return t[order].contiguous()
+
+
+def attention_prefill(q, k_pool_l, v_pool_l, q_indptr, q_pos, page_table, kv_lens, scale, tiles=None,
+                      out=None) -> torch.Tensor:
+    """q [T, Hq, D] -> [T, Hq*D]; rows attend to positions [0, q_pos] of their request."""
+    if not q.is_cuda:
+        y = ref.paged_attention(q, k_pool_l, v_pool_l, q_indptr, q_pos, page_table, kv_lens, scale)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    T, Hq, D = q.shape
+    if out is None:
+        out = torch.empty(T, Hq * D, dtype=q.dtype, device=q.device)
+    if tiles is None:
+        tiles = prefill_tiles(q_indptr.cpu(), q_pos.cpu(), Hq, k_pool_l.shape[1]).to(q.device)
+    _cuda().attn_prefill(q, k_pool_l, v_pool_l, q_indptr, q_pos, page_table, tiles, out, scale)
+    return out
+
+
+def decode_splits(batch: int, num_kv_heads: int, max_kv_len: int, num_sms: int = 148) -> int:
+    target = 4 * num_sms
+    n = max(1, math.ceil(target / max(1, batch * num_kv_heads)))
+    return int(max(1, min(n, math.ceil(max_kv_len / 64))))
+
+
+def attention_decode(q, k_pool_l, v_pool_l, page_table, kv_lens, scale, nsplit=None, out=None) -> torch.Tensor:
+    """One query token per request: q [B, Hq, D] -> [B, Hq*D]."""
+    B, Hq, D = q.shape
+    if not q.is_cuda:
+        q_indptr = torch.arange(B + 1, dtype=torch.int32)
+        q_pos = (kv_lens - 1).to(torch.int32)
+        y = ref.paged_attention(q, k_pool_l, v_pool_l, q_indptr, q_pos, page_table, kv_lens, scale)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(B, Hq * D, dtype=q.dtype, device=q.device)
+    if nsplit is None:
+        nsplit = decode_splits(B, k_pool_l.shape[1], int(kv_lens.max()))
+    ws = workspace(q.device)
+    if nsplit > 1:
+        need = B * Hq * nsplit
+        if ws.dec_o.numel() < need * D:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("decode workspace too small during CUDA graph capture; reserve it first")
+            ws.reserve_decode(B * Hq, nsplit, D)
+    _cuda().attn_decode(q, k_pool_l, v_pool_l, page_table, kv_lens, out.view(B, Hq, D), ws.dec_o, ws.dec_ml,
+                        nsplit, scale)
+    return out
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor] = None,
+              vocab_start: int = 0) -> torch.Tensor:
+    if not ids.is_cuda:
+        local = ids.long() - vocab_start
+        mine = (local >= 0) & (local < table.shape[0])
+        y = table[local.clamp(0, table.shape[0] - 1)] * mine[:, None].to(table.dtype)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=ids.device)
+    _cuda().embedding(out, ids, table, vocab_start)
+    return out
+
+
+def argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not logits.is_cuda:
+        y = ref.argmax(logits)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    _cuda().argmax(out, logits)
+    return out
+
+
+def kv_link_rope(k_pool, v_pool, src_slots, dst_slots, local_pos, global_pos, cos_sin,
+                 src_k_ptr: int = 0, src_v_ptr: int = 0, src_page_size: int = 0, src_layer_stride: int = 0,
+                 src_pools=None) -> None:
+    """Gather + RoPE delta + scatter over all layers in one launch.
+    ``src_*_ptr`` name a peer replica's pools (cross-replica link)."""
+    if not k_pool.is_cuda:
+        sk, sv = (src_pools if src_pools is not None else (None, None))
+        ref.kv_link_rope(k_pool, v_pool, src_slots, dst_slots, local_pos, global_pos, cos_sin,
+                         src_k_pool=sk, src_v_pool=sv)
+        return
+    _cuda().kv_link_rope(k_pool, v_pool, int(src_k_ptr), int(src_v_ptr), int(src_page_size),
+                         int(src_layer_stride), src_slots, dst_slots, local_pos, global_pos, cos_sin)

@@ -1,0 +1,521 @@
+"""Single-GPU (or CPU-oracle) execution engine.
+
+Operations (reference call stacks: Compile ``pic_runtime.py:2578-2718,3485``,
+Link ``pic_runtime.py:2790-2961,3742-4121``, decode ``model_runner.py:2955``):
+
+* :meth:`Engine.compile`  -- prefill a sub-context alone from position 0 into
+  fresh pages and register those pages as a LegoLink block (ownership moves
+  to the registry; no copy).
+* :meth:`Engine.link`     -- resolve the plan, reserve sources (lookup ->
+  pin -> capacity check) *before* allocating request-private pages, gather
+  every linked token of every layer with its RoPE delta rotation in one
+  kernel launch, recompute all ``imp_indices`` rows in ONE layer-outer
+  forward (each layer writes the repaired K/V before its attention, which is
+  causal by position over the request's pages), return the first token.
+  Sources are unpinned in ``finally``.
+* :meth:`Engine.prefill`  -- full prefill (the baseline a Link is compared to).
+* :meth:`Engine.decode`   -- batched greedy decode; on CUDA the step is a
+  captured CUDA graph per batch-size bucket.
+"""
+
+from __future__ import annotations
+
+import math
+import threading
+import time
+from dataclasses import dataclass, field
+from typing import Any, Callable, Optional, Sequence
+
+import torch
+
+from .. import ops
+from ..contract import ContractError, physical_token_ids_sha256, residency_recovery_message, \
+    validate_physical_token_input, LEGOLINK_POLICY_VERSION
+from ..models.qwen import ForwardBatch, QwenModel
+from ..ops import _ext
+from ..utils import launch_count
+from ..utils.trace import emit_trace, CudaTimer
+from .link_plan import ResolvedLinkPlan, resolve_link_plan
+
+
+class RuntimeErrorAbort(RuntimeError):
+    """A request-scoped failure: the request is aborted, the engine lives on."""
+
+
+class LinkSourceUnavailable(RuntimeErrorAbort):
+    """A Link source is missing / stale / incompatible; the message carries
+    the structured residency-recovery JSON."""
+
+    def __init__(self, message: str, missing=(), stale=(), incompatible=()):
+        super().__init__(message)
+        self.missing, self.stale, self.incompatible = tuple(missing), tuple(stale), tuple(incompatible)
+
+
+class CapacityError(RuntimeErrorAbort):
+    pass
+
+
+@dataclass
+class Sequence_:
+    rid: str
+    token_ids: list[int]  # prompt (+ generated) tokens whose KV is resident
+    pages: list[int]
+    length: int  # tokens with KV written
+    output_ids: list[int] = field(default_factory=list)
+    kind: str = "plain"
+    link_plan: Optional[ResolvedLinkPlan] = None
+    timings: dict = field(default_factory=dict)
+    finished: bool = False
+
+
+class KVPool:
+    def __init__(self, num_layers: int, num_pages: int, num_kv_heads: int, page_size: int, head_dim: int,
+                 dtype: torch.dtype, device: torch.device):
+        self.num_pages, self.page_size = num_pages, page_size
+        shape = (num_layers, num_pages, num_kv_heads, page_size, head_dim)
+        self.k = torch.zeros(shape, dtype=dtype, device=device)
+        self.v = torch.zeros(shape, dtype=dtype, device=device)
+        self.alloc = _ext.host().PageAllocator(num_pages)
+
+    @property
+    def bytes(self) -> int:
+        return 2 * self.k.numel() * self.k.element_size()
+
+    def slots(self, pages: Sequence[int], positions: torch.Tensor) -> torch.Tensor:
+        pt = torch.as_tensor(list(pages), dtype=torch.int64)
+        return pt[positions.long() // self.page_size] * self.page_size + positions.long() % self.page_size
+
+
+def pages_for(n: int, ps: int) -> int:
+    return (n + ps - 1) // ps
+
+
+class Engine:
+    def __init__(self, model: QwenModel, *, num_pages: Optional[int] = None, page_size: int = 16,
+                 mem_fraction: float = 0.85, max_blocks: int = 256, max_context: int = 32768,
+                 use_cuda_graphs: bool = True, residency: Optional[int] = None, legolink_only: bool = False,
+                 compat_overrides: Optional[dict] = None, kv_pool: Optional[KVPool] = None):
+        self.model = model
+        self.cfg = model.cfg
+        self.device = model.device
+        self.page_size = page_size
+        self.max_context = max_context
+        self.is_cuda = self.device.type == "cuda"
+        if kv_pool is None:
+            if num_pages is None:
+                num_pages = self._auto_pages(mem_fraction)
+            kv_pool = KVPool(self.cfg.num_layers, num_pages, model.hkv, page_size, self.cfg.head_dim, model.dtype,
+                             self.device)
+        self.kv = kv_pool
+        self.alloc = kv_pool.alloc
+        h = _ext.host()
+        self.residency = residency if residency is not None else (self.device.index or 0)
+        self.registry = h.BlockRegistry(self.alloc, max_blocks, self.residency)
+        self.radix = h.RadixIndex(self.alloc, page_size)
+        self.legolink_only = legolink_only
+        self.compat = self._compat(compat_overrides or {})
+        self.use_cuda_graphs = use_cuda_graphs and self.is_cuda
+        self._graphs: dict = {}
+        self._lock = threading.RLock()
+        self._rid = 0
+        self.stats = {"compiles": 0, "links": 0, "prefills": 0, "decode_steps": 0}
+        if self.is_cuda:
+            ws = ops.workspace(self.device)
+            ws.reserve_decode(64 * model.hq, 592, self.cfg.head_dim)
+            # split-K partials for M <= 128 rows over the widest weight
+            widest = max(2 * model.inter, (model.hq + 2 * model.hkv) * self.cfg.head_dim, self.cfg.hidden_size)
+            ws.reserve_gemm(8 * 128 * max(widest, model.lm_head.shape[0]) // 2, 4096)
+
+    # ---------------------------------------------------------------- setup
+    def _auto_pages(self, frac: float) -> int:
+        c, m = self.cfg, self.model
+        per_page = 2 * c.num_layers * m.hkv * self.page_size * c.head_dim * torch.tensor([], dtype=m.dtype).element_size()
+        if self.is_cuda:
+            free, total = torch.cuda.mem_get_info(self.device)
+            budget = int(free * frac) - (2 << 30)
+        else:
+            budget = 256 << 20
+        return max(64, budget // per_page)
+
+    def _compat(self, over: dict) -> dict:
+        c = self.cfg
+        d = {
+            "model_fingerprint": f"{c.name}@{c.fingerprint()}",
+            "tokenizer_fingerprint": f"{c.name}:{c.vocab_size}",
+            "kv_dtype": str(self.model.dtype),
+            "rope_fingerprint": f'{{"max_position_embeddings":{c.max_position_embeddings},"rope_scaling":null,'
+                                f'"rope_theta":{c.rope_theta}}}',
+            "attention_backend_fingerprint": "sglang_legolink_b200.paged_sm100a",
+            "tp_world_size": self.model.tp_size,
+            "page_size": self.page_size,
+        }
+        d.update(over)
+        return d
+
+    def compat_key(self, adapter_id=None, segmentation_policy_version=None, legolink_policy_version=None) -> str:
+        c = dict(self.compat)
+        c["adapter_id"] = str(adapter_id or "none")
+        c["segmentation_policy_version"] = str(segmentation_policy_version or "field-first-v1")
+        c["legolink_policy_version"] = str(legolink_policy_version or LEGOLINK_POLICY_VERSION)
+        return "|".join(f"{k}={c[k]}" for k in sorted(c))
+
+    def next_rid(self, prefix="req") -> str:
+        self._rid += 1
+        return f"{prefix}-{self._rid}"
+
+    # --------------------------------------------------------------- memory
+    def _alloc_pages(self, n: int) -> list[int]:
+        if self.alloc.num_free < n:
+            self.radix.evict(n - self.alloc.num_free)
+        if self.alloc.num_free < n:
+            self.registry.evict_for_capacity(n)
+        if self.alloc.num_free < n:
+            raise CapacityError(f"KV pool exhausted: need {n} pages, {self.alloc.num_free} free")
+        return list(self.alloc.alloc(n))
+
+    def free(self, seq: Sequence_) -> None:
+        if seq.pages:
+            self.alloc.release(seq.pages)
+            seq.pages = []
+
+    def _ensure_capacity(self, seq: Sequence_, new_len: int) -> None:
+        need = pages_for(new_len, self.page_size) - len(seq.pages)
+        if need > 0:
+            seq.pages.extend(self._alloc_pages(need))
+
+    # ----------------------------------------------------------- batch build
+    def _extend_batch(self, items: list[tuple[list[int], list[int], list[int], int]],
+                      logits_last_only=True) -> ForwardBatch:
+        """items: (token_ids_of_rows, positions_of_rows, pages, kv_len)."""
+        ps = self.page_size
+        ids, pos, slots, qptr = [], [], [], [0]
+        max_pages = max(len(p) for _, _, p, _ in items)
+        pt = torch.zeros(len(items), max(1, max_pages), dtype=torch.int32)
+        kvl = []
+        last_rows = []
+        for b, (t, p, pages, kv_len) in enumerate(items):
+            ids.extend(t)
+            pos.extend(p)
+            pg = torch.as_tensor(pages, dtype=torch.int64)
+            pp = torch.as_tensor(p, dtype=torch.int64)
+            slots.append(pg[pp // ps] * ps + pp % ps)
+            qptr.append(qptr[-1] + len(t))
+            pt[b, : len(pages)] = torch.as_tensor(pages, dtype=torch.int32)
+            kvl.append(kv_len)
+            last_rows.append(qptr[-1] - 1)
+        dev = self.device
+        positions = torch.as_tensor(pos, dtype=torch.int32)
+        q_indptr = torch.as_tensor(qptr, dtype=torch.int32)
+        tiles = None
+        if self.is_cuda:
+            tiles = ops.prefill_tiles(q_indptr, positions, self.model.hq, self.model.hkv).to(dev, non_blocking=True)
+        return ForwardBatch(
+            mode="extend",
+            input_ids=torch.as_tensor(ids, dtype=torch.int32).to(dev, non_blocking=True),
+            positions=positions.to(dev, non_blocking=True),
+            slots=torch.cat(slots).to(dev, non_blocking=True),
+            q_indptr=q_indptr.to(dev, non_blocking=True),
+            page_table=pt.to(dev, non_blocking=True),
+            kv_lens=torch.as_tensor(kvl, dtype=torch.int32).to(dev, non_blocking=True),
+            logit_rows=torch.as_tensor(last_rows, dtype=torch.int64).to(dev, non_blocking=True),
+            tiles=tiles,
+        )
+
+    def _sample(self, logits: torch.Tensor) -> torch.Tensor:
+        return ops.argmax(logits)
+
+    # --------------------------------------------------------------- compile
+    def compile(self, token_ids: Sequence[int], cache_key: str, *, sub_context: Optional[dict] = None,
+                block_id: Optional[str] = None) -> dict:
+        """Prefill a block alone from position 0 and register it."""
+        with self._lock:
+            sc = dict(sub_context or {})
+            override = validate_physical_token_input(sc, label="sub_context")
+            toks = [int(t) for t in (override if override is not None else token_ids)]
+            if override is not None and token_ids and list(token_ids) != override:
+                raise ContractError("Compile request tokens differ from the validated physical_input_ids override.")
+            if not toks:
+                raise ContractError("Compile requires a non-empty sub-context.")
+            ckey = self.compat_key(sc.get("adapter_id"), sc.get("segmentation_policy_version"),
+                                   sc.get("legolink_policy_version"))
+            n = len(toks)
+            pages = self._alloc_pages(pages_for(n, self.page_size))
+            try:
+                fb = self._extend_batch([(toks, list(range(n)), pages, n)])
+                logits = self.model.forward(fb, self.kv)
+                first = int(self._sample(logits)[0].item())
+            except Exception:
+                self.alloc.release(pages)
+                raise
+            status = self.registry.register_block(str(cache_key), ckey, physical_token_ids_sha256(toks), toks, pages,
+                                                  0, str(block_id or sc.get("semantic_block_id") or cache_key))
+            self.stats["compiles"] += 1
+            emit_trace("compile_registered", cache_key=str(cache_key), token_count=n, status=status)
+            return {"cache_key": str(cache_key), "status": status, "token_count": n, "first_token": first}
+
+    def block_tokens(self, cache_key: str):
+        return self.registry.tokens(cache_key)
+
+    # ------------------------------------------------------------------ link
+    def resolve(self, pic_link: dict, mutable_input_ids: Sequence[int]) -> ResolvedLinkPlan:
+        return resolve_link_plan(pic_link, mutable_input_ids, self.block_tokens)
+
+    def _preflight(self, pic_link: dict) -> None:
+        """Classify every source before anything is derived from it, so a
+        missing / stale / incompatible block aborts with the recovery JSON."""
+        keys = list(dict.fromkeys(str(k) for k in pic_link["cache_keys"]))
+        ckey = self.compat_key(pic_link.get("adapter_id"), pic_link.get("segmentation_policy_version"),
+                               pic_link.get("legolink_policy_version"))
+        res = self.registry.lookup(keys, ckey)
+        if not res["ok"]:
+            emit_trace("legolink_request_failed_closed", reason="scheduler_source_preflight_failed",
+                       missing=res["missing"], stale=res["stale"], incompatible=res["incompatible"])
+            raise LinkSourceUnavailable(
+                residency_recovery_message(res["missing"], res["stale"], res["incompatible"]),
+                res["missing"], res["stale"], res["incompatible"])
+
+    def reserve_link_sources(self, resolved: ResolvedLinkPlan, pic_link: dict) -> list[str]:
+        """lookup -> pin -> capacity check (reference ``pic_runtime.py:2790-2961``)."""
+        keys = list(dict.fromkeys(resolved.cache_keys))
+        ckey = self.compat_key(pic_link.get("adapter_id"), pic_link.get("segmentation_policy_version"),
+                               pic_link.get("legolink_policy_version"))
+        res = self.registry.lookup(keys, ckey)
+        if not res["ok"]:
+            emit_trace("legolink_request_failed_closed", reason="scheduler_source_preflight_failed",
+                       missing=res["missing"], stale=res["stale"], incompatible=res["incompatible"])
+            raise LinkSourceUnavailable(
+                residency_recovery_message(res["missing"], res["stale"], res["incompatible"]),
+                res["missing"], res["stale"], res["incompatible"])
+        self.registry.pin(keys)
+        need = pages_for(resolved.total_token_count, self.page_size)
+        allocatable = self.alloc.num_free + self.radix.evictable_pages() + self.registry.capacity_evictable_pages()
+        if need > allocatable:
+            self.registry.unpin(keys)
+            raise CapacityError(
+                "LegoLink cannot allocate request-private destination KV without evicting its reserved source "
+                f"blocks: required={resolved.total_token_count}, allocatable={allocatable * self.page_size}.")
+        pic_link["_scheduler_reserved_cache_keys"] = keys
+        return keys
+
+    def _link_rows(self, resolved: ResolvedLinkPlan, dst_pages: list[int]):
+        """Flattened (src_slot, dst_slot, local_pos, global_pos) of every
+        linked token (recomputed rows are skipped: repair rewrites them)."""
+        ps = self.page_size
+        src, dst, lp, gp = [], [], [], []
+        dpg = torch.as_tensor(dst_pages, dtype=torch.int64)
+        for key, l0, g0, cnt in resolved.linked_rows():
+            h = self.registry.handle(key)
+            spg = torch.as_tensor(h["pages"], dtype=torch.int64)
+            loc = torch.arange(l0, l0 + cnt, dtype=torch.int64)
+            sl = loc + int(h["first_page_offset"])
+            src.append(spg[sl // ps] * ps + sl % ps)
+            glob = torch.arange(g0, g0 + cnt, dtype=torch.int64)
+            dst.append(dpg[glob // ps] * ps + glob % ps)
+            lp.append(loc.to(torch.int32))
+            gp.append(glob.to(torch.int32))
+        if not src:
+            e64, e32 = torch.zeros(0, dtype=torch.int64), torch.zeros(0, dtype=torch.int32)
+            return e64, e64, e32, e32
+        return torch.cat(src), torch.cat(dst), torch.cat(lp), torch.cat(gp)
+
+    def link(self, pic_link: dict, mutable_input_ids: Sequence[int], *, rid: Optional[str] = None,
+             timer: Optional["CudaTimer"] = None) -> Sequence_:
+        """Executes one Link.  Returns a sequence whose KV holds the whole
+        linked prompt and whose ``output_ids[0]`` is the first token."""
+        with self._lock:
+            rid = rid or self.next_rid("link")
+            from ..contract import validate_pic_link_request
+
+            validate_pic_link_request(pic_link)
+            self._preflight(pic_link)
+            resolved = resolve_link_plan(pic_link, mutable_input_ids, self.block_tokens, validate=False)
+            resolved.apply_to(pic_link)
+            keys = self.reserve_link_sources(resolved, pic_link)
+            pages: list[int] = []
+            try:
+                self.registry.acquire(keys)
+                try:
+                    pages = self._alloc_pages(pages_for(resolved.total_token_count, self.page_size))
+                    seq = self._run_link(resolved, pages, rid, timer)
+                finally:
+                    self.registry.release(keys)
+            except Exception:
+                if pages:
+                    self.alloc.release(pages)
+                raise
+            finally:
+                self.registry.unpin(keys)
+                pic_link.pop("_scheduler_reserved_cache_keys", None)
+            rec = set(resolved.recompute_positions)
+            for b in resolved.block_ranges:
+                reused = sum(1 for p in range(b.start_token, b.end_token) if p not in rec)
+                self.registry.record_execution(b.cache_key, reused, b.token_count - reused)
+            self.stats["links"] += 1
+            return seq
+
+    def _run_link(self, resolved: ResolvedLinkPlan, pages: list[int], rid: str, timer) -> Sequence_:
+        dev = self.device
+        timer = timer or CudaTimer(enabled=False)
+        with timer.span("kv_link"):
+            src, dst, lp, gp = self._link_rows(resolved, pages)
+            if src.numel():
+                ops.kv_link_rope(self.kv.k, self.kv.v, src.to(dev), dst.to(dev), lp.to(dev), gp.to(dev),
+                                 self.model.cos_sin)
+        rows = list(resolved.recompute_positions)
+        toks = [resolved.linked_token_ids[p] for p in rows]
+        with timer.span("sparse_repair"):
+            fb = self._extend_batch([(toks, rows, pages, resolved.total_token_count)])
+            logits = self.model.forward(fb, self.kv)
+            first = self._sample(logits)
+        first_id = int(first[0].item())
+        emit_trace("model_link_complete", rid=rid, total_token_count=resolved.total_token_count,
+                   recompute_rows=len(rows), linked_rows=int(src.numel()))
+        return Sequence_(rid=rid, token_ids=list(resolved.linked_token_ids), pages=pages,
+                         length=resolved.total_token_count, output_ids=[first_id], kind="link", link_plan=resolved)
+
+    # --------------------------------------------------------------- prefill
+    def prefill(self, token_ids: Sequence[int], *, rid: Optional[str] = None, namespace: Optional[str] = None,
+                use_prefix_cache: bool = False) -> Sequence_:
+        """Full prefill of a plain prompt (the baseline of a Link)."""
+        with self._lock:
+            toks = [int(t) for t in token_ids]
+            n = len(toks)
+            rid = rid or self.next_rid("prefill")
+            cached: list[int] = []
+            if use_prefix_cache:
+                cached = list(self.radix.match_prefix(namespace or "", toks))
+                # keep one token to compute so the last row produces logits
+                while cached and len(cached) * self.page_size >= n:
+                    cached.pop()
+                if cached:
+                    self.alloc.incref(cached)
+            start = len(cached) * self.page_size
+            try:
+                pages = cached + self._alloc_pages(pages_for(n, self.page_size) - len(cached))
+            except Exception:
+                if cached:
+                    self.alloc.release(cached)
+                raise
+            try:
+                fb = self._extend_batch([(toks[start:], list(range(start, n)), pages, n)])
+                logits = self.model.forward(fb, self.kv)
+                first = int(self._sample(logits)[0].item())
+            except Exception:
+                self.alloc.release(pages)
+                raise
+            if use_prefix_cache:
+                self.radix.insert(namespace or "", toks, pages)
+            self.stats["prefills"] += 1
+            return Sequence_(rid=rid, token_ids=toks, pages=pages, length=n, output_ids=[first], kind="plain")
+
+    # ---------------------------------------------------------------- decode
+    def decode(self, seqs: list[Sequence_], steps: int, stop_ids: Sequence[int] = ()) -> None:
+        """Greedy-decode ``steps`` tokens for every sequence (in place).  The
+        last output token of each sequence is fed as the next input."""
+        stop = set(int(s) for s in stop_ids)
+        for _ in range(steps):
+            live = [s for s in seqs if not s.finished]
+            if not live:
+                break
+            nxt = self.decode_step(live)
+            for s, t in zip(live, nxt):
+                s.output_ids.append(int(t))
+                if int(t) in stop:
+                    s.finished = True
+
+    def decode_step(self, seqs: list[Sequence_]) -> list[int]:
+        with self._lock:
+            B = len(seqs)
+            for s in seqs:
+                self._ensure_capacity(s, s.length + 1)
+            if self.use_cuda_graphs:
+                out = self._graph_step(seqs)
+            else:
+                out = self._eager_step(seqs)
+            for s in seqs:
+                s.token_ids.append(s.output_ids[-1])
+                s.length += 1
+            self.stats["decode_steps"] += 1
+            return out
+
+    def _decode_inputs(self, seqs, bucket: int, max_pages: int):
+        ps = self.page_size
+        B = len(seqs)
+        ids = torch.zeros(bucket, dtype=torch.int32)
+        pos = torch.zeros(bucket, dtype=torch.int32)
+        slots = torch.zeros(bucket, dtype=torch.int64)
+        pt = torch.zeros(bucket, max_pages, dtype=torch.int32)
+        kvl = torch.ones(bucket, dtype=torch.int32)
+        for b, s in enumerate(seqs):
+            ids[b] = s.output_ids[-1]
+            pos[b] = s.length
+            slots[b] = s.pages[s.length // ps] * ps + s.length % ps
+            pt[b, : len(s.pages)] = torch.as_tensor(s.pages, dtype=torch.int32)
+            kvl[b] = s.length + 1
+        # padded rows write into a scratch slot of page 0 of row 0 and attend to 1 key
+        for b in range(B, bucket):
+            pt[b, 0] = seqs[0].pages[0]
+            slots[b] = int(slots[0])
+            pos[b] = 0
+        return ids, pos, slots, pt, kvl
+
+    def _eager_step(self, seqs) -> list[int]:
+        B = len(seqs)
+        max_pages = max(len(s.pages) for s in seqs)
+        ids, pos, slots, pt, kvl = self._decode_inputs(seqs, B, max_pages)
+        dev = self.device
+        fb = ForwardBatch(mode="decode", input_ids=ids.to(dev), positions=pos.to(dev), slots=slots.to(dev),
+                          q_indptr=torch.arange(B + 1, dtype=torch.int32).to(dev), page_table=pt.to(dev),
+                          kv_lens=kvl.to(dev), logit_rows=None)
+        logits = self.model.forward(fb, self.kv)
+        return self._sample(logits).tolist()
+
+    def _bucket(self, B: int) -> int:
+        for b in (1, 2, 4, 8, 16, 32, 64):
+            if B <= b:
+                return b
+        return B
+
+    def _graph_step(self, seqs) -> list[int]:
+        B = len(seqs)
+        bucket = self._bucket(B)
+        max_pages = pages_for(self.max_context, self.page_size)
+        g = self._graphs.get(bucket)
+        if g is None:
+            g = self._capture(bucket, max_pages, seqs)
+            self._graphs[bucket] = g
+        ids, pos, slots, pt, kvl = self._decode_inputs(seqs, bucket, max_pages)
+        g["ids"].copy_(ids, non_blocking=True)
+        g["pos"].copy_(pos, non_blocking=True)
+        g["slots"].copy_(slots, non_blocking=True)
+        g["pt"].copy_(pt, non_blocking=True)
+        g["kvl"].copy_(kvl, non_blocking=True)
+        g["graph"].replay()
+        launch_count.add(g["launches"])
+        return g["out"][:B].tolist()
+
+    def _capture(self, bucket: int, max_pages: int, seqs) -> dict:
+        dev = self.device
+        ids, pos, slots, pt, kvl = self._decode_inputs(seqs, bucket, max_pages)
+        st = {"ids": ids.to(dev), "pos": pos.to(dev), "slots": slots.to(dev), "pt": pt.to(dev),
+              "kvl": kvl.to(dev)}
+        nsplit = ops.decode_splits(bucket, self.model.hkv, self.max_context)
+        ops.workspace(dev).reserve_decode(bucket * self.model.hq, nsplit, self.cfg.head_dim)
+        fb = ForwardBatch(mode="decode", input_ids=st["ids"], positions=st["pos"], slots=st["slots"],
+                          q_indptr=torch.arange(bucket + 1, dtype=torch.int32, device=dev), page_table=st["pt"],
+                          kv_lens=st["kvl"], logit_rows=None, decode_nsplit=nsplit)
+        out = torch.zeros(bucket, dtype=torch.int32, device=dev)
+        # warm-up (allocates the model's scratch buffers outside the graph).
+        # The padded rows' writes land on the slot row 0 is about to fill, so
+        # the real step below overwrites them.
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                ops.argmax(self.model.forward(fb, self.kv), out=out)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with launch_count.Recorder() as rec, torch.cuda.graph(graph):
+            ops.argmax(self.model.forward(fb, self.kv), out=out)
+        st.update(graph=graph, out=out, fb=fb, launches=rec.n)
+        return st

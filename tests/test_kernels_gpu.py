@@ -1,0 +1,205 @@
+"""sm_100a kernels vs plain PyTorch fp32 statements of the same ops."""
+
+import math
+
+import pytest
+import torch
+
+from sglang_legolink_b200 import ops
+from sglang_legolink_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-6)).item()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (256, 512, 1024), (1000, 4608, 3584), (77, 640, 512),
+                                   (384, 3584, 18944), (4096, 1024, 512)])
+def test_gemm_tcgen05(M, N, K):
+    torch.manual_seed(0)
+    a = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    bias = torch.randn(N, device=DEV, dtype=torch.bfloat16)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    ops._cuda().gemm(a, w, bias, out, 0, 256 if N >= 2048 else 128, ops.workspace(DEV).err)
+    torch.cuda.synchronize()
+    assert ops.check_errors(DEV) == 0
+    exp = a.float() @ w.float().t() + bias.float()
+    assert _rel(out, exp) < 1e-2
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_tcgen05_both_tiles(bn):
+    torch.manual_seed(1)
+    M, N, K = 300, 768, 640
+    a = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    ops._cuda().gemm(a, w, None, out, 0, bn, ops.workspace(DEV).err)
+    assert _rel(out, a.float() @ w.float().t()) < 1e-2
+
+
+def test_gemm_swiglu_epilogue():
+    torch.manual_seed(2)
+    M, I, K = 333, 1024, 512
+    a = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    gate = torch.randn(I, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    up = torch.randn(I, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    gu = ops.interleave_gate_up(gate, up)
+    out = ops.linear(a, gu, swiglu_epilogue=True)
+    exp = torch.nn.functional.silu(a.float() @ gate.float().t()) * (a.float() @ up.float().t())
+    assert _rel(out, exp) < 1e-2
+
+
+@pytest.mark.parametrize("M", [1, 3, 16, 17, 64, 100, 128])
+@pytest.mark.parametrize("N,K", [(4608, 3584), (3584, 18944), (1000, 512)])
+def test_gemm_small_m(M, N, K):
+    torch.manual_seed(3)
+    a = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    bias = torch.randn(N, device=DEV, dtype=torch.bfloat16)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    ops._small_m(ops._cuda(), ops.workspace(DEV), a, w, bias, out)
+    torch.cuda.synchronize()
+    assert ops.check_errors(DEV) == 0
+    exp = a.float() @ w.float().t() + bias.float()
+    assert _rel(out, exp) < 1e-2
+    # second call reuses the tickets (must have been reset to zero)
+    out2 = torch.empty_like(out)
+    ops._small_m(ops._cuda(), ops.workspace(DEV), a, w, bias, out2)
+    assert torch.equal(out, out2)
+
+
+@pytest.mark.parametrize("hidden", [256, 3584, 5120])
+def test_rmsnorm_and_fused_add(hidden):
+    torch.manual_seed(4)
+    x = torch.randn(37, hidden, device=DEV, dtype=torch.bfloat16)
+    r = torch.randn(37, hidden, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(hidden, device=DEV, dtype=torch.bfloat16)
+    y = ops.rmsnorm(x, w, 1e-6)
+    assert _rel(y, ref.rmsnorm(x.cpu().float(), w.cpu().float(), 1e-6)) < 1e-2
+    xc, rc = x.clone(), r.clone()
+    ops.fused_add_rmsnorm(xc, rc, w, 1e-6)
+    xr, rr = x.float().cpu(), r.float().cpu()
+    ref.fused_add_rmsnorm(xr, rr, w.float().cpu(), 1e-6)
+    assert _rel(rc, rr) < 1e-2 and _rel(xc, xr) < 1e-2
+
+
+@pytest.mark.parametrize("qk_norm", [False, True])
+def test_rope_qkv_write(qk_norm):
+    torch.manual_seed(5)
+    Hq, Hkv, D, ps, T = 8, 2, 128, 16, 50
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=DEV, dtype=torch.bfloat16)
+    pos = torch.randint(0, 4000, (T,), dtype=torch.int32)
+    pages = torch.randperm(64)[:8]
+    slots = (pages[torch.arange(T) // ps] * ps + torch.arange(T) % ps).to(torch.int64)
+    cs = ref.rope_cos_sin_table(4096, D, 1e6)
+    qn = torch.randn(D, dtype=torch.bfloat16) if qk_norm else None
+    kn = torch.randn(D, dtype=torch.bfloat16) if qk_norm else None
+    kp = torch.zeros(64, Hkv, ps, D, device=DEV, dtype=torch.bfloat16)
+    vp = torch.zeros_like(kp)
+    q = torch.empty(T, Hq, D, device=DEV, dtype=torch.bfloat16)
+    ops.rope_qkv_write(qkv, pos.to(DEV), slots.to(DEV), cs.to(DEV), q, kp, vp, Hq, Hkv, D,
+                       qn.to(DEV) if qk_norm else None, kn.to(DEV) if qk_norm else None)
+    kr, vr = kp.cpu().float().zero_(), vp.cpu().float().zero_()
+    qr = ref.rope_qkv_write(qkv.cpu().float(), pos, slots, cs, kr, vr, Hq, Hkv, D,
+                            qn.float() if qk_norm else None, kn.float() if qk_norm else None)
+    assert _rel(q, qr) < 1e-2
+    assert _rel(kp, kr) < 1e-2
+    assert torch.equal(vp.cpu().float(), vr)
+
+
+@pytest.mark.parametrize("ps", [16, 64])
+def test_kv_link_rope_matches_fp32_within_one_ulp(ps):
+    torch.manual_seed(6)
+    L, P, H, D = 3, 96, 4, 128
+    k = torch.randn(L, P, H, ps, D, dtype=torch.bfloat16)
+    v = torch.randn(L, P, H, ps, D, dtype=torch.bfloat16)
+    n = 300
+    src = torch.randperm(P * ps // 2)[:n].to(torch.int64)
+    dst = (torch.randperm(P * ps // 2)[:n] + P * ps // 2).to(torch.int64)
+    lp = torch.randint(0, 8192, (n,), dtype=torch.int32)
+    gp = torch.randint(0, 32768, (n,), dtype=torch.int32)
+    gp[:10] = lp[:10]  # identity rows
+    cs = ref.rope_cos_sin_table(32768, D, 1e6)
+    kd, vd = k.to(DEV), v.to(DEV)
+    ops.kv_link_rope(kd, vd, src.to(DEV), dst.to(DEV), lp.to(DEV), gp.to(DEV), cs.to(DEV))
+    kr, vr = k.float(), v.float()
+    ref.kv_link_rope(kr, vr, src, dst, lp, gp, cs)
+    got = kd.cpu().float()
+    # compare rounded-to-bf16 oracle: within 1 bf16 ulp
+    exp = kr.to(torch.bfloat16).float()
+    ulp = torch.maximum(exp.abs(), torch.full_like(exp, 1e-30)) * 2.0**-7
+    assert bool(((got - exp).abs() <= ulp + 1e-6).all())
+    assert torch.equal(vd.cpu(), vr.to(torch.bfloat16))
+
+
+def _paged_setup(B, lens, Hkv, D, ps, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    npages = sum((n + ps - 1) // ps for n in lens) + 4
+    perm = torch.randperm(npages, generator=g)
+    kp = torch.randn(npages, Hkv, ps, D, generator=g).to(torch.bfloat16)
+    vp = torch.randn(npages, Hkv, ps, D, generator=g).to(torch.bfloat16)
+    maxp = max((n + ps - 1) // ps for n in lens)
+    pt = torch.zeros(B, maxp, dtype=torch.int32)
+    c = 0
+    for b, n in enumerate(lens):
+        k = (n + ps - 1) // ps
+        pt[b, :k] = perm[c : c + k].to(torch.int32)
+        c += k
+    return kp, vp, pt
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(28, 4), (8, 8), (64, 8), (4, 2)])
+def test_attention_prefill_sparse_rows(Hq, Hkv):
+    D, ps = 128, 16
+    lens = [700, 130, 1500]
+    kp, vp, pt = _paged_setup(3, lens, Hkv, D, ps)
+    g = torch.Generator().manual_seed(1)
+    rows, qptr = [], [0]
+    for n in lens:
+        # sparse repair rows: a prefix, windows, and the tail
+        p = sorted(set(list(range(0, 5)) + list(range(100, 140)) + list(range(n - 20, n))))
+        p = [x for x in p if x < n]
+        rows.extend(p)
+        qptr.append(qptr[-1] + len(p))
+    T = len(rows)
+    q = torch.randn(T, Hq, D, generator=g).to(torch.bfloat16)
+    qpos = torch.tensor(rows, dtype=torch.int32)
+    qi = torch.tensor(qptr, dtype=torch.int32)
+    kvl = torch.tensor(lens, dtype=torch.int32)
+    scale = 1 / math.sqrt(D)
+    out = ops.attention_prefill(q.to(DEV), kp.to(DEV), vp.to(DEV), qi.to(DEV), qpos.to(DEV), pt.to(DEV),
+                                kvl.to(DEV), scale)
+    exp = ref.paged_attention(q.float(), kp.float(), vp.float(), qi, qpos, pt, kvl, scale)
+    assert _rel(out.cpu(), exp) < 1.5e-2
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,n", [(1, 28, 4, 16000), (3, 28, 4, 1000), (16, 8, 1, 3000), (2, 64, 8, 77)])
+def test_attention_decode(B, Hq, Hkv, n):
+    D, ps = 128, 16
+    lens = [n - 3 * b for b in range(B)]
+    kp, vp, pt = _paged_setup(B, lens, Hkv, D, ps, seed=3)
+    g = torch.Generator().manual_seed(2)
+    q = torch.randn(B, Hq, D, generator=g).to(torch.bfloat16)
+    kvl = torch.tensor(lens, dtype=torch.int32)
+    scale = 1 / math.sqrt(D)
+    out = ops.attention_decode(q.to(DEV), kp.to(DEV), vp.to(DEV), pt.to(DEV), kvl.to(DEV), scale)
+    exp = ref.paged_attention(q.float(), kp.float(), vp.float(), torch.arange(B + 1, dtype=torch.int32),
+                              kvl - 1, pt, kvl, scale)
+    assert _rel(out.cpu(), exp) < 1.5e-2
+
+
+def test_swiglu_embedding_argmax():
+    torch.manual_seed(7)
+    gu = torch.randn(19, 2 * 256, device=DEV, dtype=torch.bfloat16)
+    assert _rel(ops.swiglu(gu), ops.ref_swiglu_interleaved(gu.cpu().float())) < 1e-2
+    table = torch.randn(1000, 256, device=DEV, dtype=torch.bfloat16)
+    ids = torch.randint(0, 1000, (33,), device=DEV, dtype=torch.int32)
+    assert torch.equal(ops.embedding(ids, table), table[ids.long()])
+    logits = torch.randn(5, 152064, device=DEV, dtype=torch.bfloat16)
+    assert torch.equal(ops.argmax(logits).cpu(), torch.argmax(logits.float(), -1).int().cpu())

@@ -1,0 +1,122 @@
+"""CPU fake-runtime config: Compile -> Link (permuted, RoPE remap, repair)
+-> greedy decode, compared with full prefill (torch fp32 oracle path)."""
+
+import pytest
+import torch
+
+from sglang_legolink_b200.contract import ContractError, physical_token_ids_sha256
+from sglang_legolink_b200.models.config import PRESETS
+from sglang_legolink_b200.models.qwen import QwenModel
+from sglang_legolink_b200.runtime.engine import Engine, LinkSourceUnavailable
+from sglang_legolink_b200.contract import parse_residency_recovery
+
+
+@pytest.fixture(scope="module")
+def world():
+    cfg = PRESETS["tiny-qwen2"]
+    model = QwenModel.random_init(cfg, seed=0)
+    eng = Engine(model, num_pages=1024, page_size=16)
+    g = torch.Generator().manual_seed(0)
+    lens = {"instruction": 128, "tool_schema": 256, "turn": 64, "tool_output": 512}
+    subs = {k: torch.randint(0, 1024, (n,), generator=g).tolist() for k, n in lens.items()}
+    for k, t in subs.items():
+        eng.compile(t, k)
+    suffix = torch.randint(0, 1024, (24,), generator=g).tolist()
+    return eng, subs, suffix
+
+
+def test_full_repair_equals_full_prefill(world):
+    eng, subs, suffix = world
+    order = ["tool_output", "instruction", "turn", "tool_schema"]
+    plan = {"cache_keys": order, "recompute_tokens_per_block": [len(subs[k]) for k in order]}
+    seq = eng.link(plan, suffix)
+    eng.decode([seq], 32)
+    full = eng.prefill(sum((subs[k] for k in order), []) + suffix)
+    eng.decode([full], 32)
+    assert seq.output_ids == full.output_ids
+    eng.free(seq), eng.free(full)
+
+
+def test_sparse_repair_16_per_boundary_runs(world):
+    eng, subs, suffix = world
+    order = ["turn", "tool_schema", "instruction", "tool_output"]
+    plan = {"cache_keys": order, "recompute_initial_tokens": 16, "recompute_first_block": True}
+    seq = eng.link(plan, suffix)
+    assert len(plan["imp_indices"]) == 16 * 4 + len(suffix)
+    assert plan["total_token_count"] == sum(len(subs[k]) for k in order) + len(suffix)
+    eng.decode([seq], 8)
+    assert len(seq.output_ids) == 9
+    eng.free(seq)
+
+
+def test_linked_kv_equals_compiled_at_global_position(world):
+    """Zero-window Link: linked K rows must equal K computed natively at the
+    global position (RoPE delta remap by offset, not by block ordinal)."""
+    eng, subs, suffix = world
+    order = ["instruction", "turn"]
+    plan = {"cache_keys": order, "recompute_tokens_per_block": [0, 0]}
+    seq = eng.link(plan, suffix)
+    full = eng.prefill(subs["instruction"] + subs["turn"] + suffix)
+    ps = eng.page_size
+    n0 = len(subs["instruction"])
+    # block 1 (turn) sits at offset n0: its first layer K must match the native prefill's layer-0 K
+    for p in (n0, n0 + 5, n0 + 63):
+        a = eng.kv.k[0][seq.pages[p // ps], :, p % ps]
+        b = eng.kv.k[0][full.pages[p // ps], :, p % ps]
+        assert torch.allclose(a, b, atol=1e-4), p
+    eng.free(seq), eng.free(full)
+
+
+def test_missing_block_raises_recovery_json(world):
+    eng, subs, suffix = world
+    with pytest.raises(LinkSourceUnavailable) as ei:
+        eng.link({"cache_keys": ["instruction", "nope"]}, suffix)
+    d = parse_residency_recovery(str(ei.value))
+    assert d["missing"] == ("nope",)
+
+
+def test_runtime_owned_fields_refused(world):
+    eng, subs, suffix = world
+    with pytest.raises(ContractError):
+        eng.link({"cache_keys": ["instruction"], "imp_indices": [0, 1]}, suffix)
+    with pytest.raises(ContractError):
+        eng.link({"cache_keys": ["instruction"], "bogus_field": 1}, suffix)
+
+
+def test_duplicate_compile_keeps_resident(world):
+    eng, subs, suffix = world
+    r = eng.compile(subs["turn"], "turn")
+    assert r["status"] == "duplicate"
+    with pytest.raises(ValueError):
+        eng.compile(subs["instruction"], "turn")
+
+
+def test_normalized_layout_hashes_checked(world):
+    eng, subs, suffix = world
+    prefix = [1, 2, 3]
+    ids = prefix + suffix
+    order = ["turn", "instruction"]
+    full = prefix + subs["turn"] + subs["instruction"] + suffix
+    plan = {
+        "cache_keys": order,
+        "physical_token_layout_version": "noc-single-chat-template-split-v1",
+        "physical_input_ids": ids,
+        "physical_token_count": len(ids),
+        "physical_token_ids_sha256": physical_token_ids_sha256(ids),
+        "physical_prefix_token_count": 3,
+        "physical_block_segments": [
+            {"cache_key": k, "physical_token_count": len(subs[k]),
+             "physical_token_ids_sha256": physical_token_ids_sha256(subs[k])} for k in order],
+        "expected_complete_token_count": len(full),
+        "expected_complete_token_ids_sha256": physical_token_ids_sha256(full),
+        "recompute_initial_tokens": 8,
+    }
+    seq = eng.link(dict(plan), ids)
+    assert seq.token_ids == full
+    # first block sits behind the prefix: it must be remapped (offset 3, not ordinal 0)
+    assert seq.link_plan.block_ranges[0].start_token == 3
+    eng.free(seq)
+    bad = dict(plan)
+    bad["expected_complete_token_ids_sha256"] = "0" * 64
+    with pytest.raises(ContractError):
+        eng.link(bad, ids)
