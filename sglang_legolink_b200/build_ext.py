@@ -26,6 +26,7 @@ CUDA_SOURCES = [
     "gemm_tcgen05.cu",
     "elementwise.cu",
     "attention.cu",
+    "attention_tc.cu",
 ]
 HOST_SOURCES = ["host_runtime.cpp"]
 

@@ -456,23 +456,39 @@ __global__ void __launch_bounds__(32)
   }
 }
 
-// grid (B*Hq), block 128 (one thread per head_dim element).
+// grid (B*Hq), block 128 (one thread per head_dim element).  The split
+// maxima and weights are computed cooperatively in shared memory, then each
+// thread reduces its head_dim column over the splits (coalesced reads).
+constexpr int CB_MAX_SPLITS = 1024;
 __global__ void __launch_bounds__(128) attn_combine_kernel(bf16* __restrict__ out, const float* __restrict__ ws_o,
                                                            const float* __restrict__ ws_ml, int nsplit) {
+  __shared__ float w[CB_MAX_SPLITS];
+  __shared__ float red[4];
   const size_t row = blockIdx.x;
-  const int d = threadIdx.x;
+  const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
+  const float2* ml = reinterpret_cast<const float2*>(ws_ml) + row * nsplit;
   float M = -INFINITY;
-  for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, ws_ml[(row * nsplit + sp) * 2]);
-  float num = 0.f, den = 0.f;
-  if (M != -INFINITY) {
-    for (int sp = 0; sp < nsplit; ++sp) {
-      const float m = ws_ml[(row * nsplit + sp) * 2];
-      if (m == -INFINITY) continue;
-      const float w = exp2f(m - M);
-      den += w * ws_ml[(row * nsplit + sp) * 2 + 1];
-      num += w * ws_o[(row * nsplit + sp) * AT_D + d];
-    }
+  for (int sp = d; sp < nsplit; sp += 128) M = fmaxf(M, ml[sp].x);
+  M = warp_max(M);
+  if (lane == 0) red[warp] = M;
+  __syncthreads();
+  M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  __syncthreads();
+  float den = 0.f;
+  for (int sp = d; sp < nsplit; sp += 128) {
+    const float2 v = ml[sp];
+    const float wt = (v.x == -INFINITY || M == -INFINITY) ? 0.f : exp2f(v.x - M);
+    w[sp] = wt;
+    den += wt * v.y;
   }
+  den = warp_sum(den);
+  if (lane == 0) red[warp] = den;
+  __syncthreads();
+  den = red[0] + red[1] + red[2] + red[3];
+  const float* o = ws_o + row * (size_t)nsplit * AT_D + d;
+  float num = 0.f;
+#pragma unroll 4
+  for (int sp = 0; sp < nsplit; ++sp) num += w[sp] * o[(size_t)sp * AT_D];
   out[row * AT_D + d] = __float2bfloat16(den > 0.f ? num / den : 0.f);
 }
 
@@ -503,6 +519,7 @@ extern "C" int ll_attn_decode(const bf16* q, const bf16* kpool, const bf16* vpoo
   if (B <= 0) return 0;
   if (head_dim != AT_D || Hq % Hkv || Hq / Hkv > 16) return -3;
   if (nsplit < 1) nsplit = 1;
+  if (nsplit > CB_MAX_SPLITS) return -3;
   if (nsplit > 1 && (ws_o == nullptr || ws_ml == nullptr)) return -6;
   static bool init = false;
   if (!init) {

@@ -34,6 +34,10 @@ int ll_attn_prefill(const bf16* q, const bf16* kpool, const bf16* vpool, const i
 int ll_attn_decode(const bf16* q, const bf16* kpool, const bf16* vpool, const int* page_table, int pt_stride,
                    const int* kv_lens, bf16* out, float* ws_o, float* ws_ml, int B, int Hq, int Hkv, int head_dim,
                    int page_size, int nsplit, float scale, cudaStream_t stream);
+int ll_attn_prefill_tc(const bf16* q, const bf16* k_pool, const bf16* v_pool, int L, int pages, int layer,
+                       const int* q_indptr, const int* q_pos, const int* page_table, int pt_stride, const int* tiles,
+                       int ntiles, bf16* out, int Hq, int Hkv, int head_dim, int page_size, float scale, int* err,
+                       cudaStream_t stream);
 }
 
 namespace {
@@ -170,6 +174,24 @@ void attn_prefill(const at::Tensor& q, const at::Tensor& k_pool_l, const at::Ten
            "ll_attn_prefill");
 }
 
+// k_pool / v_pool: whole pools [L, pages, Hkv, ps, D]; `layer` selects one.
+void attn_prefill_tc(const at::Tensor& q, const at::Tensor& k_pool, const at::Tensor& v_pool, int64_t layer,
+                     const at::Tensor& q_indptr, const at::Tensor& q_pos, const at::Tensor& page_table,
+                     const at::Tensor& tiles, at::Tensor& out, double scale, const at::Tensor& err) {
+  CHECK_CUDA(q); CHECK_BF16(q); CHECK_CONTIG(q); CHECK_BF16(k_pool); CHECK_BF16(v_pool); CHECK_CONTIG(k_pool);
+  CHECK_CONTIG(v_pool); CHECK_I32(q_indptr); CHECK_I32(q_pos); CHECK_I32(page_table); CHECK_I32(tiles);
+  CHECK_CONTIG(tiles); CHECK_CONTIG(out);
+  TORCH_CHECK(k_pool.dim() == 5 && k_pool.sizes() == v_pool.sizes());
+  TORCH_CHECK(layer >= 0 && layer < k_pool.size(0));
+  const int Hq = q.size(1), D = q.size(2);
+  c10::cuda::CUDAGuard g(q.device());
+  check_rc(ll_attn_prefill_tc(bp(q), bp(k_pool), bp(v_pool), k_pool.size(0), k_pool.size(1), (int)layer,
+                              q_indptr.data_ptr<int>(), q_pos.data_ptr<int>(), page_table.data_ptr<int>(),
+                              page_table.stride(0), tiles.data_ptr<int>(), tiles.size(0), bp(out), Hq,
+                              k_pool.size(2), D, k_pool.size(3), (float)scale, err.data_ptr<int>(), cur_stream()),
+           "ll_attn_prefill_tc");
+}
+
 void attn_decode(const at::Tensor& q, const at::Tensor& k_pool_l, const at::Tensor& v_pool_l,
                  const at::Tensor& page_table, const at::Tensor& kv_lens, at::Tensor& out, at::Tensor& ws_o,
                  at::Tensor& ws_ml, int64_t nsplit, double scale) {
@@ -202,4 +224,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax", &argmax);
   m.def("attn_prefill", &attn_prefill);
   m.def("attn_decode", &attn_decode);
+  m.def("attn_prefill_tc", &attn_prefill_tc);
 }

@@ -248,9 +248,10 @@ __global__ void __launch_bounds__(192, 1)
 // grid = (feature tiles, splits); each CTA does k-blocks [kb0, kb1).
 template <int BNX>
 struct SwapCfg {
-  static constexpr int STAGES = 8;
   static constexpr int W_BYTES = GEMM_BM * GEMM_BK * 2;  // 16 KB
   static constexpr int X_BYTES = BNX * GEMM_BK * 2;
+  // as deep a ring as fits in ~200 KB (8 stages for BNX <= 64, 6 for 128)
+  static constexpr int STAGES = (200 * 1024) / (W_BYTES + X_BYTES) > 8 ? 8 : (200 * 1024) / (W_BYTES + X_BYTES);
   static constexpr int TMEM_COLS = BNX < 32 ? 32 : BNX;
   static constexpr int SMEM = STAGES * (W_BYTES + X_BYTES) + 1024 + 256;
 };
@@ -449,6 +450,16 @@ static int num_sms() {
   return n;
 }
 
+static int max_smem_optin() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  }
+  return n;
+}
+
 template <typename Kern>
 static void set_smem(Kern k, int bytes) {
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
@@ -473,6 +484,7 @@ extern "C" int ll_gemm_bf16(const bf16* A, int lda, const bf16* W, int ldw, bf16
 #define LL_LAUNCH(BN_, EPI_)                                                                          \
   do {                                                                                                \
     auto kern = gemm_tcgen05_kernel<BN_, EPI_>;                                                       \
+    if (GemmCfg<BN_>::SMEM > max_smem_optin()) return -7;                                             \
     static bool init = false;                                                                         \
     if (!init) {                                                                                      \
       set_smem(kern, GemmCfg<BN_>::SMEM);                                                             \
@@ -489,6 +501,8 @@ extern "C" int ll_gemm_bf16(const bf16* A, int lda, const bf16* W, int ldw, bf16
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
+extern "C" int ll_gemm_small_m_splits(int N, int K);
+
 // Small-M path.  ws must hold splits*M*N floats, tickets ceil(N/128) ints
 // (zero-initialised once; the kernel leaves them zero).  splits <= 0 picks a
 // split count that puts about one CTA on every SM.
@@ -500,11 +514,7 @@ extern "C" int ll_gemm_bf16_small_m(const bf16* A, int lda, const bf16* W, int l
   if ((K % 8) || (lda % 8) || (ldw % 8)) return -3;
   const int ntiles = (N + GEMM_BM - 1) / GEMM_BM;
   const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
-  if (splits <= 0) {
-    splits = (num_sms() + ntiles - 1) / ntiles;
-    if (splits > num_kb / 2) splits = num_kb / 2;
-    if (splits < 1) splits = 1;
-  }
+  if (splits <= 0) splits = ll_gemm_small_m_splits(N, K);
   int kb_per = (num_kb + splits - 1) / splits;
   splits = (num_kb + kb_per - 1) / kb_per;
   if (splits > 1 && (ws == nullptr || tickets == nullptr || ws_floats < (size_t)splits * M * N)) return -6;
@@ -516,6 +526,7 @@ extern "C" int ll_gemm_bf16_small_m(const bf16* A, int lda, const bf16* W, int l
 #define LL_LAUNCH_S(BNX_)                                                                                \
   do {                                                                                                   \
     auto kern = gemm_swapab_kernel<BNX_>;                                                                \
+    if (SwapCfg<BNX_>::SMEM > max_smem_optin()) return -7;                                               \
     static bool init = false;                                                                            \
     if (!init) {                                                                                         \
       set_smem(kern, SwapCfg<BNX_>::SMEM);                                                               \
@@ -534,10 +545,12 @@ extern "C" int ll_gemm_bf16_small_m(const bf16* A, int lda, const bf16* W, int l
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
+// Split count that keeps the grid within one wave of CTAs (one per SM):
+// floor(SMs / tiles), so no SM runs a second CTA while others idle.
 extern "C" int ll_gemm_small_m_splits(int N, int K) {
   const int ntiles = (N + GEMM_BM - 1) / GEMM_BM;
   const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
-  int splits = (num_sms() + ntiles - 1) / ntiles;
+  int splits = num_sms() / ntiles;
   if (splits > num_kb / 2) splits = num_kb / 2;
   if (splits < 1) splits = 1;
   int kb_per = (num_kb + splits - 1) / splits;

@@ -1,0 +1,434 @@
+"""Reuse planning: namespaces, catalog, compile policy, the three gates and
+the planner (host stages 5-6).
+
+Pipeline of :meth:`Planner.plan` (reference ``noc_context_manager/
+scheduler.py:919-967``):
+
+1. namespace resolution -- which cache identity each sub-context uses
+   (global: content key; hard: key scoped to the task; logical: content key
+   with per-namespace aliases, so one physical block serves many tasks);
+2. provisional compile decisions (policy);
+3. Gate 1, reuse eligibility -- only standalone-compiled canonical state;
+4. Gate 2, link-layout feasibility -- the runtime executes
+   ``[linked prefix][one mutable suffix]``: reusable blocks before the first
+   compiled block are promoted to Compile so the prefix closes, compiled
+   blocks after the suffix starts are demoted to fresh text;
+5. effective decisions -> ``linked`` / ``compile_on_miss`` / ``mutable`` /
+   ``omitted`` sets and per-block planning records;
+6. Gate 3 (observe-only) reuse accounting and profitability verdict.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+import threading
+from dataclasses import dataclass, field, replace
+from enum import Enum
+from typing import Iterable, Optional, Sequence
+
+from .manager import AgentContextManifest
+from .store import SubContext
+
+LEGACY_COMPILE_POLICY_VERSION = "legacy-fixed-64-v1"
+BELOW_COMPILE_FLOOR = "below the compile token floor"
+NO_EXPECTED_REUSE = "no expected future reuse"
+
+
+# ---------------------------------------------------------------- namespaces
+class NamespaceMode(str, Enum):
+    GLOBAL = "global"
+    HARD = "hard_namespace"
+    LOGICAL = "logical_namespace"
+
+
+def physical_kv_identity(v: SubContext) -> str:
+    """The compiled KV a sub-context denotes (content + compatibility)."""
+    return v.cache_key
+
+
+class SemanticCacheIndex:
+    """Logical namespace index: (namespace, semantic identity) -> physical key,
+    with aliases; removing a physical key invalidates every alias to it."""
+
+    def __init__(self):
+        self._alias: dict[tuple[str, str], str] = {}
+        self._lock = threading.Lock()
+
+    def lookup(self, namespace: str, identity: str) -> Optional[str]:
+        return self._alias.get((namespace, identity))
+
+    def record_alias(self, namespace: str, identity: str, physical_key: str) -> None:
+        with self._lock:
+            self._alias[(namespace, identity)] = physical_key
+
+    def on_physical_removed(self, physical_key: str) -> int:
+        with self._lock:
+            dead = [k for k, v in self._alias.items() if v == physical_key]
+            for k in dead:
+                del self._alias[k]
+            return len(dead)
+
+    def snapshot(self) -> dict:
+        return {f"{ns}|{ident}": key for (ns, ident), key in self._alias.items()}
+
+
+class NamespaceResolver:
+    def __init__(self, mode: NamespaceMode = NamespaceMode.LOGICAL, index: Optional[SemanticCacheIndex] = None):
+        self.mode = NamespaceMode(mode)
+        self.index = index or SemanticCacheIndex()
+
+    def resolve(self, v: SubContext, namespace: str) -> SubContext:
+        if self.mode == NamespaceMode.GLOBAL:
+            return v
+        if self.mode == NamespaceMode.HARD:
+            key = hashlib.sha256(f"{namespace}\0{v.cache_key}".encode()).hexdigest()
+            return replace(v, cache_key=key)
+        phys = self.index.lookup(namespace, v.semantic_identity) or physical_kv_identity(v)
+        return replace(v, cache_key=phys)
+
+    def record(self, v: SubContext, namespace: str) -> None:
+        if self.mode == NamespaceMode.LOGICAL:
+            self.index.record_alias(namespace, v.semantic_identity, v.cache_key)
+
+
+# ------------------------------------------------------------------ catalog
+class CacheCatalog:
+    """Host *intent*: which keys the host believes compiled (not residency).
+    A per-key lock is held across a Compile so two callers never compile the
+    same key at once."""
+
+    def __init__(self):
+        self._entries: dict[str, dict] = {}
+        self._locks: dict[str, threading.Lock] = {}
+        self._guard = threading.Lock()
+
+    def lock(self, key: str) -> threading.Lock:
+        with self._guard:
+            return self._locks.setdefault(key, threading.Lock())
+
+    def is_compiled(self, key: str) -> bool:
+        e = self._entries.get(key)
+        return bool(e) and not e.get("stale")
+
+    def mark_compiled(self, key: str, **meta) -> None:
+        self._entries[key] = {"compiled": True, "stale": False, **meta}
+
+    def invalidate(self, key: str) -> None:
+        if key in self._entries:
+            self._entries[key]["stale"] = True
+
+    def entries(self) -> dict:
+        return dict(self._entries)
+
+
+class PersistentCacheCatalog(CacheCatalog):
+    """Append-only JSONL variant shared between processes; the file is read
+    by whole lines only (a torn last line is ignored), and deleting it resets
+    the catalog."""
+
+    def __init__(self, path: str):
+        super().__init__()
+        self.path = path
+        self._offset = 0
+        self._refresh()
+
+    def _refresh(self) -> None:
+        if not os.path.exists(self.path):
+            return
+        with open(self.path, "rb") as f:
+            f.seek(self._offset)
+            data = f.read()
+        end = data.rfind(b"\n")
+        if end < 0:
+            return
+        for line in data[: end + 1].splitlines():
+            try:
+                rec = json.loads(line)
+            except ValueError:
+                continue
+            if rec.get("op") == "compiled":
+                super().mark_compiled(rec["key"], **rec.get("meta", {}))
+            elif rec.get("op") == "invalidate":
+                super().invalidate(rec["key"])
+        self._offset += end + 1
+
+    def _append(self, rec: dict) -> None:
+        line = (json.dumps(rec, separators=(",", ":")) + "\n").encode()
+        fd = os.open(self.path, os.O_WRONLY | os.O_CREAT | os.O_APPEND, 0o644)
+        try:
+            os.write(fd, line)
+        finally:
+            os.close(fd)
+
+    def is_compiled(self, key: str) -> bool:
+        self._refresh()
+        return super().is_compiled(key)
+
+    def mark_compiled(self, key: str, **meta) -> None:
+        super().mark_compiled(key, **meta)
+        self._append({"op": "compiled", "key": key, "meta": meta})
+
+    def invalidate(self, key: str) -> None:
+        super().invalidate(key)
+        self._append({"op": "invalidate", "key": key})
+
+
+# ----------------------------------------------------------- compile policy
+class CompileAction(str, Enum):
+    COMPILE = "compile"
+    KEEP_MUTABLE = "keep_mutable"
+    DO_NOT_INCLUDE = "do_not_include"
+
+
+@dataclass(frozen=True)
+class CompileDecision:
+    sub_context_id: str
+    cache_key: str
+    action: CompileAction
+    reason: str
+    token_count: int = 0
+    policy: str = "legacy_fixed_64"
+
+
+@dataclass(frozen=True)
+class PolicyContext:
+    expected_future_reuse: int = 1
+    memory_pressure: float = 0.0
+    cache_present: bool = False
+    min_compile_model_tokens: int = 64
+    summarize_threshold_tokens: int = 8192
+
+
+class CompilePolicy:
+    """Legacy fixed floor: compile an immutable reuse candidate iff it has at
+    least ``min_compile_model_tokens`` tokens (reference
+    ``compile_policy.py:234-350``)."""
+
+    name = "legacy_fixed_64"
+
+    def decide(self, v: SubContext, ctx: PolicyContext = PolicyContext()) -> CompileDecision:
+        D = lambda a, r, n=0: CompileDecision(v.sub_context_id, v.cache_key, a, r, n, self.name)  # noqa: E731
+        if v.invalidated:
+            return D(CompileAction.DO_NOT_INCLUDE, "invalidated version")
+        if v.is_mutable:
+            return D(CompileAction.KEEP_MUTABLE, "content is mutable")
+        if not v.reuse_candidate:
+            return D(CompileAction.KEEP_MUTABLE, "not a reuse candidate")
+        if ctx.cache_present:
+            return D(CompileAction.COMPILE, "already compiled; reuse catalog entry", v.token_count)
+        return self._decide(v, ctx, D)
+
+    def _decide(self, v, ctx, D):
+        if v.token_count < ctx.min_compile_model_tokens:
+            return D(CompileAction.KEEP_MUTABLE, BELOW_COMPILE_FLOOR)
+        if ctx.expected_future_reuse < 1:
+            return D(CompileAction.KEEP_MUTABLE, NO_EXPECTED_REUSE)
+        if ctx.memory_pressure >= 0.9:
+            return D(CompileAction.KEEP_MUTABLE, "high KV memory pressure")
+        return D(CompileAction.COMPILE, "immutable reuse candidate above the floor", v.token_count)
+
+
+class CompileAllImmutablePolicy(CompilePolicy):
+    name = "compile_all_immutable"
+
+    def _decide(self, v, ctx, D):
+        return D(CompileAction.COMPILE, "ablation: every immutable block", v.token_count)
+
+
+class CostBenefitCompilePolicy(CompilePolicy):
+    """Compile when expected reuse savings exceed the one-time Compile cost.
+    ``profile`` holds measured per-token costs (ms): prefill, link, repair."""
+
+    name = "cost_benefit"
+
+    def __init__(self, profile: Optional[dict] = None, repair_window: int = 16):
+        self.profile = profile or {"prefill_ms_per_token": 0.02, "link_ms_per_token": 0.001,
+                                   "repair_ms_per_token": 0.02}
+        self.repair_window = repair_window
+
+    def _decide(self, v, ctx, D):
+        p = self.profile
+        n = v.token_count
+        saved_per_use = n * p["prefill_ms_per_token"] - (n * p["link_ms_per_token"]
+                                                          + min(n, self.repair_window) * p["repair_ms_per_token"])
+        cost = n * p["prefill_ms_per_token"]
+        if saved_per_use <= 0 or saved_per_use * max(0, ctx.expected_future_reuse) < cost:
+            return D(CompileAction.KEEP_MUTABLE, "expected savings below compile cost")
+        return D(CompileAction.COMPILE, "expected savings exceed compile cost", n)
+
+
+def build_compile_policy(mode: str = "legacy_fixed_64", **kw) -> CompilePolicy:
+    return {"legacy_fixed_64": CompilePolicy, "compile_all_immutable": CompileAllImmutablePolicy,
+            "cost_benefit": CostBenefitCompilePolicy}[mode](**kw)
+
+
+# --------------------------------------------------------------------- gates
+class ReuseEligibility:
+    """Gate 1: only canonical, standalone-compiled state may be linked."""
+
+    def __init__(self, allow_foreign: bool = False):
+        self.allow_foreign = allow_foreign
+
+    def gate(self, v: SubContext, decision: CompileDecision) -> tuple[bool, str]:
+        if decision.action != CompileAction.COMPILE:
+            return False, "not compiled"
+        if v.metadata.get("foreign_state") and not self.allow_foreign:
+            return False, "foreign state (experimental) is off"
+        return True, "canonical standalone compile"
+
+
+@dataclass(frozen=True)
+class LayoutAdjustment:
+    sub_context_id: str
+    adjustment: str  # "none" | "promoted_for_prefix_closure" | "demoted_after_suffix"
+    reason: str = ""
+
+
+class LinkLayoutFeasibility:
+    """Gate 2: force ``[linked prefix][mutable suffix]``."""
+
+    def apply(self, ordered: Sequence[SubContext], link_ok: dict[str, bool],
+              promotable: dict[str, bool]) -> tuple[dict[str, bool], list[LayoutAdjustment]]:
+        eff = dict(link_ok)
+        adj = []
+        last_linked = max((i for i, v in enumerate(ordered) if link_ok.get(v.sub_context_id)), default=-1)
+        # promote reusable (immutable) blocks that sit before a linked block
+        for i, v in enumerate(ordered[: last_linked + 1]):
+            if not eff.get(v.sub_context_id):
+                if promotable.get(v.sub_context_id):
+                    eff[v.sub_context_id] = True
+                    adj.append(LayoutAdjustment(v.sub_context_id, "promoted_for_prefix_closure",
+                                                "reusable block inside the linked prefix"))
+                else:
+                    break
+        # everything after the first non-linked block is the mutable suffix
+        in_suffix = False
+        for v in ordered:
+            if not eff.get(v.sub_context_id):
+                in_suffix = True
+            elif in_suffix:
+                eff[v.sub_context_id] = False
+                adj.append(LayoutAdjustment(v.sub_context_id, "demoted_after_suffix",
+                                            "compiled block after the mutable suffix starts"))
+        return eff, adj
+
+
+@dataclass(frozen=True)
+class ReuseAccounting:
+    reused_tokens: int
+    compiled_tokens: int
+    recompute_tokens: int
+    repair_tokens: int
+    total_tokens: int
+    verdict: str  # observe-only profitability
+
+    def to_dict(self) -> dict:
+        return dict(self.__dict__)
+
+
+# ------------------------------------------------------------------ planner
+@dataclass(frozen=True)
+class BlockPlanningRecord:
+    sub_context_id: str
+    block_id: str
+    cache_key: str
+    token_count: int
+    policy_action: str
+    layout_adjustment: str
+    effective_action: str
+    planner_category: str  # linked | compile_on_miss | mutable | omitted
+    reason: str = ""
+
+    def to_dict(self) -> dict:
+        return dict(self.__dict__)
+
+
+@dataclass(frozen=True)
+class ExecutionPlan:
+    manifest: AgentContextManifest
+    included_contexts: tuple
+    linked_contexts: tuple
+    compile_on_miss_contexts: tuple
+    mutable_contexts: tuple
+    omitted_contexts: tuple
+    records: tuple
+    accounting: ReuseAccounting
+    text_separator: str = "\n\n"
+
+    @property
+    def expected_cache_keys(self) -> tuple:
+        return tuple(v.cache_key for v in self.linked_contexts)
+
+    @property
+    def baseline_selected_text(self) -> str:
+        parts = [v.raw_text for v in self.included_contexts]
+        if self.manifest.mutable_text:
+            parts.append(self.manifest.mutable_text)
+        return self.text_separator.join(parts)
+
+    def to_dict(self) -> dict:
+        return {"manifest": self.manifest.to_dict(), "linked": [v.sub_context_id for v in self.linked_contexts],
+                "compile_on_miss": [v.sub_context_id for v in self.compile_on_miss_contexts],
+                "mutable": [v.sub_context_id for v in self.mutable_contexts],
+                "omitted": [v.sub_context_id for v in self.omitted_contexts],
+                "block_planning": [r.to_dict() for r in self.records], "reuse_accounting": self.accounting.to_dict()}
+
+
+class Planner:
+    def __init__(self, policy: Optional[CompilePolicy] = None, catalog: Optional[CacheCatalog] = None,
+                 resolver: Optional[NamespaceResolver] = None, eligibility: Optional[ReuseEligibility] = None,
+                 feasibility: Optional[LinkLayoutFeasibility] = None, repair_window: int = 16,
+                 separator: str = "\n\n"):
+        self.policy = policy or CompilePolicy()
+        self.catalog = catalog or CacheCatalog()
+        self.resolver = resolver or NamespaceResolver()
+        self.eligibility = eligibility or ReuseEligibility()
+        self.feasibility = feasibility or LinkLayoutFeasibility()
+        self.repair_window = repair_window
+        self.separator = separator
+
+    def plan(self, manifest: AgentContextManifest, contexts: Iterable[SubContext], *, namespace: str = "default",
+             policy_context: PolicyContext = PolicyContext()) -> ExecutionPlan:
+        by_id = {v.sub_context_id: v for v in contexts}
+        ordered = [self.resolver.resolve(by_id[i], namespace) for i in manifest.selected_sub_context_ids
+                   if i in by_id]
+        decisions = {}
+        for v in ordered:
+            ctx = replace(policy_context, cache_present=self.catalog.is_compiled(v.cache_key))
+            decisions[v.sub_context_id] = self.policy.decide(v, ctx)
+        included = [v for v in ordered if decisions[v.sub_context_id].action != CompileAction.DO_NOT_INCLUDE]
+        omitted = [v for v in ordered if decisions[v.sub_context_id].action == CompileAction.DO_NOT_INCLUDE]
+        link_ok = {v.sub_context_id: self.eligibility.gate(v, decisions[v.sub_context_id])[0] for v in included}
+        promotable = {v.sub_context_id: (not v.is_mutable and v.reuse_candidate and not v.invalidated)
+                      for v in included}
+        eff, adj = self.feasibility.apply(included, link_ok, promotable)
+        adj_of = {a.sub_context_id: a.adjustment for a in adj}
+        linked = [v for v in included if eff.get(v.sub_context_id)]
+        mutable = [v for v in included if not eff.get(v.sub_context_id)]
+        com = [v for v in linked if not self.catalog.is_compiled(v.cache_key)]
+        records = []
+        for v in ordered:
+            d = decisions[v.sub_context_id]
+            if v in omitted:
+                cat, ea = "omitted", "do_not_include"
+            elif eff.get(v.sub_context_id):
+                cat = "compile_on_miss" if v in com else "linked"
+                ea = "link"
+            else:
+                cat, ea = "mutable", "recompute"
+            records.append(BlockPlanningRecord(v.sub_context_id, v.semantic_identity, v.cache_key, v.token_count,
+                                               d.action.value, adj_of.get(v.sub_context_id, "none"), ea, cat,
+                                               d.reason))
+        for v in linked:
+            self.resolver.record(v, namespace)
+        reused = sum(v.token_count for v in linked if v not in com)
+        compiled = sum(v.token_count for v in com)
+        recompute = sum(v.token_count for v in mutable)
+        repair = sum(min(self.repair_window, v.token_count) for v in linked)
+        total = sum(v.token_count for v in included)
+        verdict = "observe_only:" + ("profitable" if reused > repair else "not_profitable")
+        acc = ReuseAccounting(reused, compiled, recompute, repair, total, verdict)
+        return ExecutionPlan(manifest, tuple(included), tuple(linked), tuple(com), tuple(mutable), tuple(omitted),
+                             tuple(records), acc, self.separator)

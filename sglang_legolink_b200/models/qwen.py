@@ -243,7 +243,7 @@ class QwenModel:
                 ops.attention_decode(q, kv.k[li], kv.v[li], fb.page_table, fb.kv_lens, self.scale,
                                      nsplit=fb.decode_nsplit, out=attn)
             else:
-                ops.attention_prefill(q, kv.k[li], kv.v[li], fb.q_indptr, fb.positions, fb.page_table, fb.kv_lens,
+                ops.attention_prefill(q, kv.k, kv.v, li, fb.q_indptr, fb.positions, fb.page_table, fb.kv_lens,
                                       self.scale, tiles=tiles, out=attn)
             self._row_parallel(attn, lw.o_w, o)
             ops.fused_add_rmsnorm(o, residual, lw.post_norm, c.rms_norm_eps)

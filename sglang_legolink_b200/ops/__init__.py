@@ -192,37 +192,50 @@ def rope_qkv_write(qkv, positions, slots, cos_sin, q_out, k_pool_l, v_pool_l, nu
     return q_out
 
 
+PREFILL_ROWS_PER_TILE = 128  # packed (token, head) rows per CTA of the tcgen05 kernel
+
+
 def prefill_tiles(q_indptr_host: torch.Tensor, q_pos_host: torch.Tensor, num_heads: int, num_kv_heads: int,
-                  rows_per_tile: int = 64) -> torch.Tensor:
-    """Work list for the prefill/repair attention kernel: one int4
+                  rows_per_tile: int = PREFILL_ROWS_PER_TILE) -> torch.Tensor:
+    """Work list for the prefill/repair attention kernels: one int4
     ``(request, kv_head, first_packed_row, max_position_in_tile)`` per CTA,
-    longest (largest max position) first."""
+    longest (largest max position) first.  Packed row ``r`` of a request is
+    (token ``r // g``, q-head ``kv_head*g + r % g``), ``g = Hq / Hkv``."""
     g = num_heads // num_kv_heads
-    tiles = []
-    B = q_indptr_host.numel() - 1
-    qi = q_indptr_host.tolist()
-    qp = q_pos_host
+    qi = q_indptr_host.to(torch.int64)
+    qp = q_pos_host.to(torch.int64)
+    B = qi.numel() - 1
+    out = []
     for b in range(B):
-        s, e = qi[b], qi[b + 1]
+        s, e = int(qi[b]), int(qi[b + 1])
         nrows = (e - s) * g
-        for r0 in range(0, nrows, rows_per_tile):
-            t_last = s + min(nrows, r0 + rows_per_tile) // g - (1 if min(nrows, r0 + rows_per_tile) % g == 0 else 0)
-            t_first = s + r0 // g
-            mp = int(qp[t_first : t_last + 1].max())
-            for hk in range(num_kv_heads):
-                tiles.append((b, hk, r0, mp))
-    if not tiles:
+        if nrows <= 0:
+            continue
+        r0 = torch.arange(0, nrows, rows_per_tile, dtype=torch.int64)
+        last_tok = s + (torch.clamp(r0 + rows_per_tile, max=nrows) - 1) // g
+        # positions are ascending within a request, so the tile max is its last token's
+        mp = qp[last_tok]
+        n = r0.numel()
+        t = torch.empty(n * num_kv_heads, 4, dtype=torch.int64)
+        t[:, 0] = b
+        t[:, 1] = torch.arange(num_kv_heads).repeat(n)
+        t[:, 2] = r0.repeat_interleave(num_kv_heads)
+        t[:, 3] = mp.repeat_interleave(num_kv_heads)
+        out.append(t)
+    if not out:
         return torch.zeros(0, 4, dtype=torch.int32)
-    t = torch.tensor(tiles, dtype=torch.int32)
+    t = torch.cat(out)
     order = torch.argsort(t[:, 3], descending=True, stable=True)
-    return t[order].contiguous()
+    return t[order].to(torch.int32).contiguous()
 
 
-def attention_prefill(q, k_pool_l, v_pool_l, q_indptr, q_pos, page_table, kv_lens, scale, tiles=None,
+def attention_prefill(q, k_pool, v_pool, layer, q_indptr, q_pos, page_table, kv_lens, scale, tiles=None,
                       out=None) -> torch.Tensor:
-    """q [T, Hq, D] -> [T, Hq*D]; rows attend to positions [0, q_pos] of their request."""
+    """q [T, Hq, D] -> [T, Hq*D]; rows attend to positions [0, q_pos] of their
+    request (positions ascending within a request).  ``k_pool``/``v_pool`` are
+    the whole pools; ``layer`` selects one.  CUDA: tcgen05 kernel."""
     if not q.is_cuda:
-        y = ref.paged_attention(q, k_pool_l, v_pool_l, q_indptr, q_pos, page_table, kv_lens, scale)
+        y = ref.paged_attention(q, k_pool[layer], v_pool[layer], q_indptr, q_pos, page_table, kv_lens, scale)
         if out is not None:
             out.copy_(y)
             return out
@@ -231,15 +244,31 @@ def attention_prefill(q, k_pool_l, v_pool_l, q_indptr, q_pos, page_table, kv_len
     if out is None:
         out = torch.empty(T, Hq * D, dtype=q.dtype, device=q.device)
     if tiles is None:
-        tiles = prefill_tiles(q_indptr.cpu(), q_pos.cpu(), Hq, k_pool_l.shape[1]).to(q.device)
+        tiles = prefill_tiles(q_indptr.cpu(), q_pos.cpu(), Hq, k_pool.shape[2]).to(q.device)
+    _cuda().attn_prefill_tc(q, k_pool, v_pool, layer, q_indptr, q_pos, page_table, tiles, out, scale,
+                            workspace(q.device).err)
+    return out
+
+
+def attention_prefill_mma(q, k_pool_l, v_pool_l, q_indptr, q_pos, page_table, scale, tiles=None, out=None):
+    """Same op on the legacy mma.sync tensor-core path (64-row tiles): the
+    baseline the tcgen05 kernel is measured against."""
+    T, Hq, D = q.shape
+    if out is None:
+        out = torch.empty(T, Hq * D, dtype=q.dtype, device=q.device)
+    if tiles is None:
+        tiles = prefill_tiles(q_indptr.cpu(), q_pos.cpu(), Hq, k_pool_l.shape[1], rows_per_tile=64).to(q.device)
     _cuda().attn_prefill(q, k_pool_l, v_pool_l, q_indptr, q_pos, page_table, tiles, out, scale)
     return out
 
 
 def decode_splits(batch: int, num_kv_heads: int, max_kv_len: int, num_sms: int = 148) -> int:
-    target = 4 * num_sms
+    """Split count for decode attention: about 6 one-warp CTAs per SM (the
+    residency limit of the kernel's 36 KB of shared memory), each covering at
+    least 64 keys (two 32-key blocks), capped at 1024 splits."""
+    target = 6 * num_sms
     n = max(1, math.ceil(target / max(1, batch * num_kv_heads)))
-    return int(max(1, min(n, math.ceil(max_kv_len / 64))))
+    return int(max(1, min(n, math.ceil(max_kv_len / 64), 1024)))
 
 
 def attention_decode(q, k_pool_l, v_pool_l, page_table, kv_lens, scale, nsplit=None, out=None) -> torch.Tensor:

@@ -1,0 +1,220 @@
+"""Request scheduler: admission of Compile / Link / plain prefills and
+continuous batching of decode.
+
+The reference admits a Link only into an empty engine (a batch of one that
+waits for every running decode to finish; its own trace attributes 97.8 % of
+TTFT at concurrency 8 to that wait, reference ``pic_runtime.py:2023-2026``,
+``managers/scheduler.py:2597-2690``).  Here one loop thread alternates:
+
+1. admit: pop up to ``max_prefills_per_step`` queued requests and run each
+   prefill-type op (Compile prefill, Link = KV link + sparse repair, plain
+   prefill) -- a Link never waits for the running decodes to drain;
+2. decode: one batched greedy step for every running sequence (CUDA graph per
+   batch bucket on GPU), streaming each new token to its request.
+
+Arrival checks (reference ``managers/scheduler.py:1915-2057``): a request is a
+Compile (``sub_context``) XOR a Link (``pic_link``); in LegoLink-only mode
+plain generation is refused; a Link may not ask for input logprobs; an
+overlength Link is rejected, never truncated.  Two Compiles of one key never
+run concurrently (the loop is serial and the registry keeps the resident
+copy on a duplicate).  Every failure is request-scoped.
+"""
+
+from __future__ import annotations
+
+import queue
+import threading
+import time
+import traceback
+from dataclasses import dataclass, field
+from typing import Any, Callable, Optional
+
+from ..contract import ContractError
+from ..utils.trace import emit_trace
+from .engine import Engine, RuntimeErrorAbort, Sequence_
+
+
+class RequestRejected(ValueError):
+    pass
+
+
+@dataclass
+class Request:
+    kind: str  # "compile" | "link" | "plain"
+    rid: str
+    input_ids: list
+    max_new_tokens: int
+    stop_ids: tuple = ()
+    sub_context: Optional[dict] = None
+    pic_link: Optional[dict] = None
+    created: float = field(default_factory=time.perf_counter)
+    events: "queue.Queue" = field(default_factory=queue.Queue)  # ("token", id) | ("done", info) | ("error", msg)
+    seq: Optional[Sequence_] = None
+    ttft_s: Optional[float] = None
+
+
+class Scheduler:
+    def __init__(self, engine: Engine, *, legolink_only: bool = True, max_running: int = 64,
+                 max_prefills_per_step: int = 1, max_context: Optional[int] = None):
+        self.engine = engine
+        self.legolink_only = legolink_only
+        self.max_running = max_running
+        self.max_prefills_per_step = max_prefills_per_step
+        self.max_context = max_context or engine.max_context
+        self.waiting: "queue.Queue[Request]" = queue.Queue()
+        self.running: list[Request] = []
+        self._stop = threading.Event()
+        self._thread: Optional[threading.Thread] = None
+        self.stats = {"admitted": 0, "rejected": 0, "finished": 0, "decode_steps": 0}
+
+    # ------------------------------------------------------------ arrival
+    def check(self, req: Request) -> None:
+        if req.sub_context is not None and req.pic_link is not None:
+            raise RequestRejected("a request is either a Compile (sub_context) or a Link (pic_link), not both")
+        if req.kind == "plain" and self.legolink_only:
+            raise RequestRejected("LegoLink-only runtime: plain generation is refused; send a Compile or a Link")
+        if req.kind == "link" and not isinstance(req.pic_link, dict):
+            raise RequestRejected("pic_link must be an object.")
+        if len(req.input_ids) + req.max_new_tokens > self.max_context and req.kind != "link":
+            raise RequestRejected(f"request of {len(req.input_ids)} tokens exceeds the context window")
+
+    def submit(self, req: Request) -> Request:
+        try:
+            self.check(req)
+        except RequestRejected as e:
+            self.stats["rejected"] += 1
+            req.events.put(("error", str(e)))
+            return req
+        self.waiting.put(req)
+        return req
+
+    # ---------------------------------------------------------------- loop
+    def start(self) -> None:
+        if self._thread is None:
+            self._thread = threading.Thread(target=self._loop, name="legolink-scheduler", daemon=True)
+            self._thread.start()
+
+    def stop(self) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=30)
+
+    def _loop(self) -> None:
+        while not self._stop.is_set():
+            did = self.step()
+            if not did:
+                try:
+                    req = self.waiting.get(timeout=0.01)
+                    self.waiting.put(req)
+                except queue.Empty:
+                    pass
+
+    def step(self) -> bool:
+        """One scheduling iteration; returns False when idle."""
+        did = False
+        for _ in range(self.max_prefills_per_step):
+            if len(self.running) >= self.max_running:
+                break
+            try:
+                req = self.waiting.get_nowait()
+            except queue.Empty:
+                break
+            did = True
+            self._admit(req)
+        if self.running:
+            did = True
+            self._decode()
+        return did
+
+    def _admit(self, req: Request) -> None:
+        eng = self.engine
+        try:
+            if req.kind == "compile":
+                sc = req.sub_context or {}
+                key = sc.get("cache_key")
+                if not key:
+                    raise ContractError("sub_context.cache_key is required for a Compile")
+                r = eng.compile(req.input_ids, str(key), sub_context=sc)
+                req.ttft_s = time.perf_counter() - req.created
+                req.events.put(("token", r["first_token"]))
+                req.events.put(("done", {"compile": r, "finish_reason": "length"}))
+                self.stats["finished"] += 1
+                return
+            if req.kind == "link":
+                seq = eng.link(req.pic_link, req.input_ids, rid=req.rid)
+                if seq.length + req.max_new_tokens > self.max_context:
+                    eng.free(seq)
+                    raise RequestRejected("overlength Link (total tokens + max_tokens exceeds the context window)")
+            else:
+                seq = eng.prefill(req.input_ids, rid=req.rid)
+            req.seq = seq
+            req.ttft_s = time.perf_counter() - req.created
+            first = seq.output_ids[-1]
+            req.events.put(("token", first))
+            self.stats["admitted"] += 1
+            if req.max_new_tokens <= 1 or first in req.stop_ids:
+                self._finish(req, "stop" if first in req.stop_ids else "length")
+            else:
+                self.running.append(req)
+        except (ContractError, RuntimeErrorAbort, RequestRejected, ValueError, KeyError) as e:
+            emit_trace("legolink_request_failed_closed", rid=req.rid, kind=req.kind, reason=str(e)[:500])
+            req.events.put(("error", str(e)))
+        except Exception as e:  # keep the loop alive: this request fails, the runtime continues
+            emit_trace("legolink_request_failed_closed", rid=req.rid, kind=req.kind, reason=repr(e)[:500])
+            req.events.put(("error", f"internal error: {e!r}\n{traceback.format_exc(limit=3)}"))
+
+    def _decode(self) -> None:
+        seqs = [r.seq for r in self.running]
+        try:
+            toks = self.engine.decode_step(seqs)
+        except Exception as e:
+            for r in self.running:
+                r.events.put(("error", f"decode failed: {e!r}"))
+                self.engine.free(r.seq)
+            self.running = []
+            return
+        self.stats["decode_steps"] += 1
+        still = []
+        for r, t in zip(self.running, toks):
+            r.seq.output_ids.append(int(t))
+            r.events.put(("token", int(t)))
+            n = len(r.seq.output_ids)
+            if int(t) in r.stop_ids:
+                self._finish(r, "stop")
+            elif n >= r.max_new_tokens:
+                self._finish(r, "length")
+            else:
+                still.append(r)
+        self.running = still
+
+    def _finish(self, req: Request, reason: str) -> None:
+        info = {"finish_reason": reason, "completion_tokens": len(req.seq.output_ids) if req.seq else 0,
+                "prompt_tokens": req.seq.length - len(req.seq.output_ids) + 1 if req.seq else len(req.input_ids)}
+        if req.seq is not None:
+            if req.seq.link_plan is not None:
+                info["link"] = {"total_token_count": req.seq.link_plan.total_token_count,
+                                "recompute_rows": len(req.seq.link_plan.recompute_positions)}
+            self.engine.free(req.seq)
+        req.events.put(("done", info))
+        self.stats["finished"] += 1
+
+    # ------------------------------------------------------------ helpers
+    def run_sync(self, req: Request, timeout: float = 600.0) -> dict:
+        """Submits and drains one request (for in-process callers/tests)."""
+        self.submit(req)
+        toks = []
+        while True:
+            if self._thread is None:
+                self.step()
+                try:
+                    kind, val = req.events.get_nowait()
+                except queue.Empty:
+                    continue
+            else:
+                kind, val = req.events.get(timeout=timeout)
+            if kind == "token":
+                toks.append(val)
+            elif kind == "done":
+                return {"tokens": toks, **val, "ttft_s": req.ttft_s}
+            else:
+                raise RequestRejected(val)

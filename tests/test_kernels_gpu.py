@@ -13,7 +13,7 @@ DEV = "cuda"
 
 
 def _rel(a, b):
-    a, b = a.float(), b.float()
+    a, b = a.float().cpu(), b.float().cpu()
     return ((a - b).norm() / (b.norm() + 1e-6)).item()
 
 
@@ -154,9 +154,9 @@ def _paged_setup(B, lens, Hkv, D, ps, seed=0):
     return kp, vp, pt
 
 
-@pytest.mark.parametrize("Hq,Hkv", [(28, 4), (8, 8), (64, 8), (4, 2)])
-def test_attention_prefill_sparse_rows(Hq, Hkv):
-    D, ps = 128, 16
+@pytest.mark.parametrize("Hq,Hkv,ps", [(28, 4, 16), (8, 8, 16), (64, 8, 16), (4, 2, 16), (28, 4, 64), (7, 1, 32)])
+def test_attention_prefill_sparse_rows(Hq, Hkv, ps):
+    D = 128
     lens = [700, 130, 1500]
     kp, vp, pt = _paged_setup(3, lens, Hkv, D, ps)
     g = torch.Generator().manual_seed(1)
@@ -173,10 +173,15 @@ def test_attention_prefill_sparse_rows(Hq, Hkv):
     qi = torch.tensor(qptr, dtype=torch.int32)
     kvl = torch.tensor(lens, dtype=torch.int32)
     scale = 1 / math.sqrt(D)
-    out = ops.attention_prefill(q.to(DEV), kp.to(DEV), vp.to(DEV), qi.to(DEV), qpos.to(DEV), pt.to(DEV),
-                                kvl.to(DEV), scale)
+    kd, vd = kp[None].to(DEV), vp[None].to(DEV)
+    out = ops.attention_prefill(q.to(DEV), kd, vd, 0, qi.to(DEV), qpos.to(DEV), pt.to(DEV), kvl.to(DEV), scale)
+    torch.cuda.synchronize()
+    assert ops.check_errors(DEV) == 0
     exp = ref.paged_attention(q.float(), kp.float(), vp.float(), qi, qpos, pt, kvl, scale)
     assert _rel(out.cpu(), exp) < 1.5e-2
+    legacy = ops.attention_prefill_mma(q.to(DEV), kp.to(DEV), vp.to(DEV), qi.to(DEV), qpos.to(DEV), pt.to(DEV),
+                                       scale)
+    assert _rel(legacy.cpu(), exp) < 1.5e-2
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,n", [(1, 28, 4, 16000), (3, 28, 4, 1000), (16, 8, 1, 3000), (2, 64, 8, 77)])
@@ -191,6 +196,26 @@ def test_attention_decode(B, Hq, Hkv, n):
     out = ops.attention_decode(q.to(DEV), kp.to(DEV), vp.to(DEV), pt.to(DEV), kvl.to(DEV), scale)
     exp = ref.paged_attention(q.float(), kp.float(), vp.float(), torch.arange(B + 1, dtype=torch.int32),
                               kvl - 1, pt, kvl, scale)
+    assert _rel(out.cpu(), exp) < 1.5e-2
+
+
+def test_attention_prefill_multi_layer_pool_full_causal():
+    """Full causal prefill of two requests reading layer 1 of a 3-layer pool."""
+    D, ps, Hq, Hkv = 128, 16, 28, 4
+    lens = [300, 1000]
+    kp, vp, pt = _paged_setup(2, lens, Hkv, D, ps, seed=5)
+    g = torch.Generator().manual_seed(9)
+    K3 = torch.randn(3, *kp.shape, generator=g).to(torch.bfloat16)
+    V3 = torch.randn(3, *vp.shape, generator=g).to(torch.bfloat16)
+    rows = list(range(lens[0])) + list(range(lens[1]))
+    qptr = torch.tensor([0, lens[0], lens[0] + lens[1]], dtype=torch.int32)
+    q = torch.randn(len(rows), Hq, D, generator=g).to(torch.bfloat16)
+    qpos = torch.tensor(rows, dtype=torch.int32)
+    kvl = torch.tensor(lens, dtype=torch.int32)
+    scale = 1 / math.sqrt(D)
+    out = ops.attention_prefill(q.to(DEV), K3.to(DEV), V3.to(DEV), 1, qptr.to(DEV), qpos.to(DEV), pt.to(DEV),
+                                kvl.to(DEV), scale)
+    exp = ref.paged_attention(q.float(), K3[1].float(), V3[1].float(), qptr, qpos, pt, kvl, scale)
     assert _rel(out.cpu(), exp) < 1.5e-2
 
 
