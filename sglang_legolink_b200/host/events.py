@@ -172,6 +172,7 @@ class ExtractedSource:
     sequence_number: int
     source_path: str = ""
     metadata: dict = field(default_factory=dict)
+    revision: int = 0
 
 
 @dataclass(frozen=True)
@@ -233,7 +234,8 @@ class FieldExtractor:
             if cls is not None:
                 meta["field_classification"] = cls
             fields[f].append(ExtractedSource(f, ev.event_id, ev.source_id, ev.raw_text, ev.sequence_number,
-                                             str(meta.get("path") or meta.get("file_path") or ""), meta))
+                                             str(meta.get("path") or meta.get("file_path") or ""), meta,
+                                             ev.session_revision))
         return FieldExtraction(next(iter(tasks), ""), max((e.session_revision for e in ordered), default=0),
                                {k: tuple(v) for k, v in fields.items()}, tuple(filtered))
 

@@ -15,8 +15,9 @@
 
 Mutability rule: stable fields (task instruction, tool definitions, workspace
 evidence, task metadata) are immutable at once; conversation / tool-history
-sources are immutable once a newer history source exists (the newest entries
-stay in the mutable suffix); the user prompt is always mutable.
+sources are immutable once a later ingest added newer history (the entries of
+the newest batch stay in the mutable suffix); the user prompt is always
+mutable.
 """
 
 from __future__ import annotations
@@ -177,7 +178,7 @@ class ContextManager:
                 values.append(SubContext.create(
                     task_id=self.task_id, context_field=src.context_field, source_id=src.source_id, spans=[span],
                     raw_text=src.raw_text[sg.start:sg.end], tokenizer=self.tokenizer,
-                    sequence_number=src.sequence_number, source_revision=revision,
+                    sequence_number=src.sequence_number, source_revision=src.revision,
                     model_fingerprint=self.model_fingerprint, recompute_policy_version=self.recompute_policy_version,
                     capture_token_ids=self.capture_token_ids,
                     metadata={"segment_index": i, "segment_count": len(segs), "event_id": src.event_id}))
@@ -192,7 +193,7 @@ class ContextManager:
         ext = self.extractor.extract(self.collector.events())
         active = {s.source_id: s.event_id for s in ext.sources()}
         out = [v for v in self.store.all(self.task_id) if active.get(v.source_id) == v.metadata.get("event_id")]
-        newest_hist = max((v.sequence_number for v in out if v.context_field in HISTORY_FIELDS), default=-1)
+        newest_hist = max((v.source_revision for v in out if v.context_field in HISTORY_FIELDS), default=-1)
         res = []
         for v in out:
             if v.context_field == "user_prompt":
@@ -200,7 +201,7 @@ class ContextManager:
             elif v.context_field in STABLE_FIELDS:
                 mut = False
             else:
-                mut = v.sequence_number >= newest_hist
+                mut = v.source_revision >= newest_hist
             res.append(v if v.is_mutable == mut else _with(v, is_mutable=mut))
         return res
 

@@ -156,8 +156,13 @@ class PersistentCacheCatalog(CacheCatalog):
 
     def _append(self, rec: dict) -> None:
         line = (json.dumps(rec, separators=(",", ":")) + "\n").encode()
-        fd = os.open(self.path, os.O_WRONLY | os.O_CREAT | os.O_APPEND, 0o644)
+        fd = os.open(self.path, os.O_RDWR | os.O_CREAT | os.O_APPEND, 0o644)
         try:
+            # A torn last line (a writer died mid-record) would swallow this
+            # record; terminate it first so only the torn record is lost.
+            size = os.fstat(fd).st_size
+            if size and os.pread(fd, 1, size - 1) != b"\n":
+                line = b"\n" + line
             os.write(fd, line)
         finally:
             os.close(fd)

@@ -53,7 +53,11 @@ class RuntimeService:
         self._profiler = None
 
     def build_request(self, payload: dict) -> Request:
-        sc, link = payload.get("sub_context"), payload.get("pic_link")
+        import copy
+
+        # The runtime publishes its resolved plan into the pic_link dict; work
+        # on a copy so an in-process caller's payload is never modified.
+        sc, link = copy.deepcopy(payload.get("sub_context")), copy.deepcopy(payload.get("pic_link"))
         if sc is not None and link is not None:
             raise RequestRejected("a request is either a Compile (sub_context) or a Link (pic_link), not both")
         if link is not None and (payload.get("logprobs") and payload.get("echo") or payload.get("input_logprobs")):
