@@ -263,10 +263,23 @@ class QwenModel:
             self.comm.gemm_allreduce(x, w, out)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
-        out = ops.linear(hidden, self.lm_head)
+        """Logits of this rank's vocab shard (the full vocab when tp_size == 1)."""
+        return ops.linear(hidden, self.lm_head)
+
+    def full_logits(self, local: torch.Tensor) -> torch.Tensor:
         if self.tp_size > 1 and self.comm is not None:
-            out = self.comm.all_gather_vocab(out, self.cfg.vocab_size)
-        return out
+            return self.comm.all_gather_vocab(local, self.cfg.vocab_size)
+        return local
+
+    def greedy(self, local_logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Greedy token ids [R] int32 from (vocab-sharded) logits."""
+        if self.tp_size > 1 and self.comm is not None:
+            ids = self.comm.argmax_vocab(local_logits, self.vocab_range()[0])
+            if out is not None:
+                out.copy_(ids)
+                return out
+            return ids
+        return ops.argmax(local_logits, out=out)
 
 
 # ------------------------------------------------------------ safetensors IO

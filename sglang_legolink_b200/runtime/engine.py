@@ -222,7 +222,7 @@ class Engine:
         )
 
     def _sample(self, logits: torch.Tensor) -> torch.Tensor:
-        return ops.argmax(logits)
+        return self.model.greedy(logits)
 
     # --------------------------------------------------------------- compile
     def compile(self, token_ids: Sequence[int], cache_key: str, *, sub_context: Optional[dict] = None,
@@ -512,10 +512,10 @@ class Engine:
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
             for _ in range(2):
-                ops.argmax(self.model.forward(fb, self.kv), out=out)
+                self.model.greedy(self.model.forward(fb, self.kv), out=out)
         torch.cuda.current_stream(dev).wait_stream(s)
         graph = torch.cuda.CUDAGraph()
         with launch_count.Recorder() as rec, torch.cuda.graph(graph):
-            ops.argmax(self.model.forward(fb, self.kv), out=out)
+            self.model.greedy(self.model.forward(fb, self.kv), out=out)
         st.update(graph=graph, out=out, fb=fb, launches=rec.n)
         return st
