@@ -27,6 +27,7 @@ CUDA_SOURCES = [
     "elementwise.cu",
     "attention.cu",
     "attention_tc.cu",
+    "gemm_small_m_noalloc.cu",
 ]
 HOST_SOURCES = ["host_runtime.cpp"]
 
