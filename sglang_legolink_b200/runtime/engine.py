@@ -94,7 +94,8 @@ class Engine:
     def __init__(self, model: QwenModel, *, num_pages: Optional[int] = None, page_size: int = 16,
                  mem_fraction: float = 0.85, max_blocks: int = 256, max_context: int = 32768,
                  use_cuda_graphs: bool = True, residency: Optional[int] = None, legolink_only: bool = False,
-                 compat_overrides: Optional[dict] = None, kv_pool: Optional[KVPool] = None):
+                 compat_overrides: Optional[dict] = None, kv_pool: Optional[KVPool] = None,
+                 directory=None, replica_rank: int = 0, peer_pools: Optional[dict] = None):
         self.model = model
         self.cfg = model.cfg
         self.device = model.device
@@ -118,7 +119,14 @@ class Engine:
         self._graphs: dict = {}
         self._lock = threading.RLock()
         self._rid = 0
-        self.stats = {"compiles": 0, "links": 0, "prefills": 0, "decode_steps": 0}
+        self.stats = {"compiles": 0, "links": 0, "prefills": 0, "decode_steps": 0, "remote_blocks_linked": 0}
+        # DP replicas sharing compiled blocks: directory of blocks on any
+        # replica, and how to reach a peer replica's pool (GPU: base pointers
+        # from SharedKVPool.peer; CPU: the peer's (k, v) tensors).
+        self.directory = directory
+        self.replica_rank = replica_rank
+        self.peer_pools = peer_pools if peer_pools is not None else {}
+        self._remote: dict = {}
         if self.is_cuda:
             ws = ops.workspace(self.device)
             ws.reserve_decode(64 * model.hq, 592, self.cfg.head_dim)
@@ -250,11 +258,20 @@ class Engine:
             status = self.registry.register_block(str(cache_key), ckey, physical_token_ids_sha256(toks), toks, pages,
                                                   0, str(block_id or sc.get("semantic_block_id") or cache_key))
             self.stats["compiles"] += 1
+            if self.directory is not None and status == "registered":
+                from ..parallel.dp import RemoteBlock
+
+                self.registry.pin([str(cache_key)])  # a peer may link it at any time: never evict
+                self.directory.publish(RemoteBlock(self.replica_rank, str(cache_key), tuple(pages), 0, tuple(toks),
+                                                   ckey, physical_token_ids_sha256(toks), self.page_size))
             emit_trace("compile_registered", cache_key=str(cache_key), token_count=n, status=status)
             return {"cache_key": str(cache_key), "status": status, "token_count": n, "first_token": first}
 
     def block_tokens(self, cache_key: str):
-        return self.registry.tokens(cache_key)
+        t = self.registry.tokens(cache_key)
+        if t is None and cache_key in self._remote:
+            return list(self._remote[cache_key].token_ids)
+        return t
 
     # ------------------------------------------------------------------ link
     def resolve(self, pic_link: dict, mutable_input_ids: Sequence[int]) -> ResolvedLinkPlan:
@@ -267,6 +284,18 @@ class Engine:
         ckey = self.compat_key(pic_link.get("adapter_id"), pic_link.get("segmentation_policy_version"),
                                pic_link.get("legolink_policy_version"))
         res = self.registry.lookup(keys, ckey)
+        self._remote = {}
+        if not res["ok"] and self.directory is not None:
+            still = []
+            for k in res["missing"]:
+                rb = self.directory.lookup(k)
+                if rb is not None and rb.owner != self.replica_rank and rb.compat_key == ckey \
+                        and (rb.owner in self.peer_pools):
+                    self._remote[k] = rb
+                else:
+                    still.append(k)
+            res["missing"] = still
+            res["ok"] = not (still or res["stale"] or res["incompatible"])
         if not res["ok"]:
             emit_trace("legolink_request_failed_closed", reason="scheduler_source_preflight_failed",
                        missing=res["missing"], stale=res["stale"], incompatible=res["incompatible"])
@@ -276,7 +305,7 @@ class Engine:
 
     def reserve_link_sources(self, resolved: ResolvedLinkPlan, pic_link: dict) -> list[str]:
         """lookup -> pin -> capacity check (reference ``pic_runtime.py:2790-2961``)."""
-        keys = list(dict.fromkeys(resolved.cache_keys))
+        keys = [k for k in dict.fromkeys(resolved.cache_keys) if k not in self._remote]
         ckey = self.compat_key(pic_link.get("adapter_id"), pic_link.get("segmentation_policy_version"),
                                pic_link.get("legolink_policy_version"))
         res = self.registry.lookup(keys, ckey)
@@ -287,36 +316,44 @@ class Engine:
                 residency_recovery_message(res["missing"], res["stale"], res["incompatible"]),
                 res["missing"], res["stale"], res["incompatible"])
         self.registry.pin(keys)
+        for k in self._remote:
+            self.directory.pin(k, 1)
         need = pages_for(resolved.total_token_count, self.page_size)
         allocatable = self.alloc.num_free + self.radix.evictable_pages() + self.registry.capacity_evictable_pages()
         if need > allocatable:
             self.registry.unpin(keys)
+            for k in self._remote:
+                self.directory.pin(k, -1)
             raise CapacityError(
                 "LegoLink cannot allocate request-private destination KV without evicting its reserved source "
                 f"blocks: required={resolved.total_token_count}, allocatable={allocatable * self.page_size}.")
         pic_link["_scheduler_reserved_cache_keys"] = keys
         return keys
 
-    def _link_rows(self, resolved: ResolvedLinkPlan, dst_pages: list[int]):
-        """Flattened (src_slot, dst_slot, local_pos, global_pos) of every
-        linked token (recomputed rows are skipped: repair rewrites them)."""
+    def _link_rows(self, resolved: ResolvedLinkPlan, dst_pages: list[int]) -> dict:
+        """(src_slot, dst_slot, local_pos, global_pos) of every linked token
+        (recomputed rows are skipped: repair rewrites them), grouped by the
+        replica whose pool holds the source block (``None`` = this one)."""
         ps = self.page_size
-        src, dst, lp, gp = [], [], [], []
+        groups: dict = {}
         dpg = torch.as_tensor(dst_pages, dtype=torch.int64)
         for key, l0, g0, cnt in resolved.linked_rows():
-            h = self.registry.handle(key)
-            spg = torch.as_tensor(h["pages"], dtype=torch.int64)
+            rb = self._remote.get(key)
+            if rb is None:
+                h = self.registry.handle(key)
+                pages, off, sps, owner = h["pages"], int(h["first_page_offset"]), ps, None
+            else:
+                pages, off, sps, owner = rb.pages, rb.first_page_offset, rb.page_size, rb.owner
+            spg = torch.as_tensor(list(pages), dtype=torch.int64)
             loc = torch.arange(l0, l0 + cnt, dtype=torch.int64)
-            sl = loc + int(h["first_page_offset"])
-            src.append(spg[sl // ps] * ps + sl % ps)
+            sl = loc + off
             glob = torch.arange(g0, g0 + cnt, dtype=torch.int64)
-            dst.append(dpg[glob // ps] * ps + glob % ps)
-            lp.append(loc.to(torch.int32))
-            gp.append(glob.to(torch.int32))
-        if not src:
-            e64, e32 = torch.zeros(0, dtype=torch.int64), torch.zeros(0, dtype=torch.int32)
-            return e64, e64, e32, e32
-        return torch.cat(src), torch.cat(dst), torch.cat(lp), torch.cat(gp)
+            g = groups.setdefault(owner, ([], [], [], []))
+            g[0].append(spg[sl // sps] * sps + sl % sps)
+            g[1].append(dpg[glob // ps] * ps + glob % ps)
+            g[2].append(loc.to(torch.int32))
+            g[3].append(glob.to(torch.int32))
+        return {o: tuple(torch.cat(x) for x in g) for o, g in groups.items()}
 
     def link(self, pic_link: dict, mutable_input_ids: Sequence[int], *, rid: Optional[str] = None,
              timer: Optional["CudaTimer"] = None) -> Sequence_:
@@ -345,6 +382,10 @@ class Engine:
                 raise
             finally:
                 self.registry.unpin(keys)
+                for k in self._remote:
+                    self.directory.pin(k, -1)
+                self.stats["remote_blocks_linked"] += len(self._remote)
+                self._remote = {}
                 pic_link.pop("_scheduler_reserved_cache_keys", None)
             rec = set(resolved.recompute_positions)
             for b in resolved.block_ranges:
@@ -357,10 +398,20 @@ class Engine:
         dev = self.device
         timer = timer or CudaTimer(enabled=False)
         with timer.span("kv_link"):
-            src, dst, lp, gp = self._link_rows(resolved, pages)
-            if src.numel():
-                ops.kv_link_rope(self.kv.k, self.kv.v, src.to(dev), dst.to(dev), lp.to(dev), gp.to(dev),
-                                 self.model.cos_sin)
+            groups = self._link_rows(resolved, pages)
+            nlinked = 0
+            for owner, (src, dst, lp, gp) in groups.items():
+                nlinked += int(src.numel())
+                if not src.numel():
+                    continue
+                args = (self.kv.k, self.kv.v, src.to(dev), dst.to(dev), lp.to(dev), gp.to(dev), self.model.cos_sin)
+                if owner is None:
+                    ops.kv_link_rope(*args)
+                elif self.is_cuda:  # peer replica's pool, read over NVLink by the link kernel
+                    kp, vp, sps, sls = self.peer_pools[owner]
+                    ops.kv_link_rope(*args, src_k_ptr=kp, src_v_ptr=vp, src_page_size=sps, src_layer_stride=sls)
+                else:
+                    ops.kv_link_rope(*args, src_pools=self.peer_pools[owner])
         rows = list(resolved.recompute_positions)
         toks = [resolved.linked_token_ids[p] for p in rows]
         with timer.span("sparse_repair"):
@@ -369,7 +420,7 @@ class Engine:
             first = self._sample(logits)
         first_id = int(first[0].item())
         emit_trace("model_link_complete", rid=rid, total_token_count=resolved.total_token_count,
-                   recompute_rows=len(rows), linked_rows=int(src.numel()))
+                   recompute_rows=len(rows), linked_rows=nlinked)
         return Sequence_(rid=rid, token_ids=list(resolved.linked_token_ids), pages=pages,
                          length=resolved.total_token_count, output_ids=[first_id], kind="link", link_plan=resolved)
 
