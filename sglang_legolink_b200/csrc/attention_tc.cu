@@ -2,23 +2,29 @@
 //
 // Same contract as attn_prefill_kernel (attention.cu): query rows at arbitrary
 // positions, keys = the request's paged KV, causal by logical position, GQA
-// rows packed as (token, q-head-of-the-group) pairs.  One CTA owns 128 packed
-// rows of one (request, kv head) and walks 64-key blocks:
+// rows packed as (token, q-head-of-the-group) pairs.  One CTA owns TC_NT = 2
+// tiles of 128 packed rows of one (request, kv head) and walks 64-key blocks;
+// both tiles share every K/V block:
 //
 //   warp 0      TMA producer: K and V pages of each block (one box of
-//               page_size keys x 64 dims per page and half), 3-stage ring.
-//   warp 1      MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM
-//               S buffers (M=128, N=64, K=16 x 8), then O += P_{j-1} V_{j-1}
-//               (M=128, N=128, K=16 x 4; V is the MN-major B operand).
-//   warps 2..5  softmax, one query row per thread (TMEM lane = row): read S
-//               with tcgen05.ld, mask by position, online max/sum in fp32
-//               (log2 domain), write P (bf16) to shared memory in the 128-byte
-//               swizzled K-major layout the MMA reads.  O stays in TMEM; it is
-//               rescaled (tcgen05.ld/st) only when a row's running max grows
-//               by more than 2^8, so P <= 256 and most blocks skip the rescale.
+//               page_size keys x 64 dims per page and half), 2-stage ring.
+//   warp 1      MMA issuer (one thread), per block j: S(t, j) = Q_t K_j^T for
+//               both tiles into their TMEM S double buffers (M=128, N=64,
+//               K=16 x 8), then O_t += P(t, j-1) V_{j-1} (M=128, N=128,
+//               K=16 x 4; V is the MN-major B operand).
+//   warps 2..9  two softmax warpgroups, one per tile, one query row per
+//               thread (TMEM lane = row): read S with tcgen05.ld, mask by
+//               position, online max/sum in fp32 (log2 domain), write P (bf16)
+//               to shared memory in the 128-byte swizzled K-major layout the
+//               MMA reads.  O stays in TMEM; it is rescaled (tcgen05.ld/st)
+//               only when a row's running max grows by more than 2^8, so
+//               P <= 256 and most blocks skip the rescale.  While one
+//               warpgroup runs its softmax the tensor core works on the other
+//               tile.
 //
-// Barriers: kv_full/kv_empty per stage, s_full/s_empty and p_full/p_empty
-// per double buffer, q_full, o_full.  Every wait is bounded (common.cuh).
+// Barriers: kv_full/kv_empty per stage; s_full/s_empty and p_full/p_empty
+// per tile and double buffer; q_full, o_full.  Every wait is bounded
+// (common.cuh).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -26,17 +32,19 @@
 
 namespace ll {
 
-constexpr int TC_BM = 128;        // packed query rows per CTA
+constexpr int TC_BM = 128;        // packed query rows per tile
+constexpr int TC_NT = 2;          // tiles per CTA
 constexpr int TC_BN = 64;         // keys per block
 constexpr int TC_D = 128;
-constexpr int TC_STAGES = 3;
-constexpr int TC_Q_BYTES = TC_BM * TC_D * 2;         // 32 KB: [2 halves][128 rows][128 B]
+constexpr int TC_STAGES = 2;
+constexpr int TC_Q_BYTES = TC_BM * TC_D * 2;         // 32 KB per tile: [2 halves][128 rows][128 B]
 constexpr int TC_Q_HALF = TC_BM * 128;               // 16 KB
 constexpr int TC_KV_BYTES = TC_BN * TC_D * 2;        // 16 KB: [2 halves][64 rows][128 B]
 constexpr int TC_KV_HALF = TC_BN * 128;              // 8 KB
 constexpr int TC_P_BYTES = TC_BM * TC_BN * 2;        // 16 KB: [128 rows][128 B]
-constexpr int TC_SMEM = TC_Q_BYTES + 2 * TC_STAGES * TC_KV_BYTES + 2 * TC_P_BYTES + 1024 + 256;
-constexpr uint32_t TC_TMEM_COLS = 256;               // S0 [0,64) S1 [64,128) O [128,256)
+constexpr int TC_SMEM = TC_NT * TC_Q_BYTES + 2 * TC_STAGES * TC_KV_BYTES + TC_NT * 2 * TC_P_BYTES + 1024 + 512;
+constexpr uint32_t TC_TMEM_COLS = 512;               // per tile t: S0 [256t, +64) S1 [+64, +128) O [+128, +256)
+constexpr int TC_THREADS = 64 + 128 * TC_NT;
 constexpr float TC_RESCALE_THRESHOLD = 8.0f;         // log2 units
 
 __device__ __forceinline__ float ex2(float x) {
@@ -84,7 +92,7 @@ __device__ __forceinline__ void cp_async16_tc(uint32_t saddr, const void* g, boo
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr), "l"(g), "r"(n) : "memory");
 }
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(TC_THREADS, 1)
     attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                            const bf16* __restrict__ q, const int* __restrict__ q_indptr,
                            const int* __restrict__ q_pos, const int* __restrict__ page_table, int pt_stride,
@@ -92,18 +100,18 @@ __global__ void __launch_bounds__(192, 1)
                            int layer, float scale_log2, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + TC_Q_BYTES;
+  uint8_t* sQ = smem;                                   // [TC_NT][Q]
+  uint8_t* sK = sQ + TC_NT * TC_Q_BYTES;                // [STAGES][KV]
   uint8_t* sV = sK + TC_STAGES * TC_KV_BYTES;
-  uint8_t* sP = sV + TC_STAGES * TC_KV_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * TC_P_BYTES);
+  uint8_t* sP = sV + TC_STAGES * TC_KV_BYTES;           // [TC_NT][2][P]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + TC_NT * 2 * TC_P_BYTES);
   uint64_t* kv_full = bars;
   uint64_t* kv_empty = kv_full + TC_STAGES;
-  uint64_t* s_full = kv_empty + TC_STAGES;
-  uint64_t* s_empty = s_full + 2;
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* p_empty = p_full + 2;
-  uint64_t* q_full = p_empty + 2;
+  uint64_t* s_full = kv_empty + TC_STAGES;    // [TC_NT][2]
+  uint64_t* s_empty = s_full + 2 * TC_NT;
+  uint64_t* p_full = s_empty + 2 * TC_NT;
+  uint64_t* p_empty = p_full + 2 * TC_NT;
+  uint64_t* q_full = p_empty + 2 * TC_NT;
   uint64_t* o_full = q_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
 
@@ -121,13 +129,13 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 2 * TC_NT; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 4);
       mbar_init(&p_full[i], 4);
       mbar_init(&p_empty[i], 1);
     }
-    mbar_init(q_full, 4);
+    mbar_init(q_full, 4 * TC_NT);
     mbar_init(o_full, 1);
     fence_mbar_init();
   }
@@ -143,9 +151,10 @@ __global__ void __launch_bounds__(192, 1)
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
       const int pages_per_block = TC_BN / ps;
-      for (int j = 0; j < nb; ++j) {
+      bool ok = true;
+      for (int j = 0; j < nb && ok; ++j) {
         const int st = j % TC_STAGES, n = j / TC_STAGES;
-        if (!mbar_wait(&kv_empty[st], (n & 1) ^ 1, err, kErrSmemEmptyTimeout)) break;
+        if (!mbar_wait(&kv_empty[st], (n & 1) ^ 1, err, kErrSmemEmptyTimeout)) { ok = false; break; }
         mbar_arrive_expect_tx(&kv_full[st], 2 * TC_KV_BYTES);
         for (int p = 0; p < pages_per_block; ++p) {
           const int key0 = j * TC_BN + p * ps;
@@ -159,46 +168,58 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
+      if (!ok) {
+        unsigned long long t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 2000000ull) {
+        }
+      }
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16_f32(TC_BM, TC_BN);
       constexpr uint32_t idesc_pv = umma_idesc_bf16_f32(TC_BM, TC_D) | (1u << 16);  // B (V) MN-major
-      const uint32_t o_tmem = tmem + 128;
       bool ok = mbar_wait(q_full, 0, err, kErrTmaFullTimeout);
       tc_fence_after();
+      // O_t += P(t, i) V_i for both tiles, then release K_i/V_i.
       auto issue_pv = [&](int i) -> bool {
         const int pb = i & 1;
-        if (!mbar_wait(&p_full[pb], (i >> 1) & 1, err, kErrTmemFullTimeout)) return false;
-        tc_fence_after();
         const int st = i % TC_STAGES;
-        const uint32_t pbase = smem_u32(sP + pb * TC_P_BYTES);
         const uint32_t vbase = smem_u32(sV + st * TC_KV_BYTES);
 #pragma unroll
-        for (int k = 0; k < TC_BN / 16; ++k) {
-          const uint64_t ad = umma_desc_sw128_kmajor(pbase + 32 * k);
-          const uint64_t bd = umma_desc_sw128_mnmajor(vbase + k * 16 * 128, TC_KV_HALF, 1024);
-          umma_bf16(o_tmem, ad, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+        for (int t = 0; t < TC_NT; ++t) {
+          if (!mbar_wait(&p_full[2 * t + pb], (i >> 1) & 1, err, kErrTmemFullTimeout)) return false;
+          tc_fence_after();
+          const uint32_t pbase = smem_u32(sP + (2 * t + pb) * TC_P_BYTES);
+#pragma unroll
+          for (int k = 0; k < TC_BN / 16; ++k) {
+            const uint64_t ad = umma_desc_sw128_kmajor(pbase + 32 * k);
+            const uint64_t bd = umma_desc_sw128_mnmajor(vbase + k * 16 * 128, TC_KV_HALF, 1024);
+            umma_bf16(tmem + 256 * t + 128, ad, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&p_empty[2 * t + pb]);
         }
-        umma_commit(&p_empty[pb]);
         umma_commit(&kv_empty[st]);
         return true;
       };
       for (int j = 0; j < nb && ok; ++j) {
         const int st = j % TC_STAGES, sb = j & 1;
         if (!mbar_wait(&kv_full[st], (j / TC_STAGES) & 1, err, kErrTmaFullTimeout)) { ok = false; break; }
-        if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1, err, kErrTmemEmptyTimeout)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t qbase = smem_u32(sQ);
         const uint32_t kbase = smem_u32(sK + st * TC_KV_BYTES);
 #pragma unroll
-        for (int k = 0; k < TC_D / 16; ++k) {
-          const uint64_t ad = umma_desc_sw128_kmajor(qbase + (k >> 2) * TC_Q_HALF + (k & 3) * 32);
-          const uint64_t bd = umma_desc_sw128_kmajor(kbase + (k >> 2) * TC_KV_HALF + (k & 3) * 32);
-          umma_bf16(tmem + sb * TC_BN, ad, bd, idesc_s, k > 0 ? 1u : 0u);
+        for (int t = 0; t < TC_NT; ++t) {
+          if (!mbar_wait(&s_empty[2 * t + sb], ((j >> 1) & 1) ^ 1, err, kErrTmemEmptyTimeout)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t qbase = smem_u32(sQ + t * TC_Q_BYTES);
+#pragma unroll
+          for (int k = 0; k < TC_D / 16; ++k) {
+            const uint64_t ad = umma_desc_sw128_kmajor(qbase + (k >> 2) * TC_Q_HALF + (k & 3) * 32);
+            const uint64_t bd = umma_desc_sw128_kmajor(kbase + (k >> 2) * TC_KV_HALF + (k & 3) * 32);
+            umma_bf16(tmem + 256 * t + sb * TC_BN, ad, bd, idesc_s, k > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[2 * t + sb]);
         }
-        umma_commit(&s_full[sb]);
+        if (!ok) break;
         if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
       }
       if (ok) ok = issue_pv(nb - 1);
@@ -208,20 +229,22 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------- softmax
+    const int t = (warp - 2) >> 2;        // tile of this warpgroup
     const int qd = warp & 3;              // TMEM lane quarter of this warp
-    const int r = qd * 32 + lane;         // query row of this thread
-    const int pr = row0 + r;
+    const int r = qd * 32 + lane;         // query row of this thread within the tile
+    const int pr = row0 + t * TC_BM + r;
     const bool valid = pr < nrows;
     const int tok = s0 + pr / g;
     const int head = hk * g + pr % g;
     const int pos = valid ? q_pos[tok] : -1;
+    uint8_t* sQt = sQ + t * TC_Q_BYTES;
     // Q row -> shared memory (two 128-B halves, 128-B swizzle), then signal.
     {
       const bf16* src = q + ((size_t)tok * Hq + head) * TC_D;
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         const int h = c >> 3, cc = c & 7;
-        const uint32_t dst = smem_u32(sQ) + h * TC_Q_HALF + r * 128 + ((cc ^ (r & 7)) << 4);
+        const uint32_t dst = smem_u32(sQt) + h * TC_Q_HALF + r * 128 + ((cc ^ (r & 7)) << 4);
         cp_async16_tc(dst, valid ? (const void*)(src + c * 8) : (const void*)q, valid);
       }
       asm volatile("cp.async.wait_all;" ::: "memory");
@@ -229,12 +252,16 @@ __global__ void __launch_bounds__(192, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(q_full);
     }
-    const uint32_t lane_base = tmem + (uint32_t(qd * 32) << 16);
+    const uint32_t lane_base = tmem + (uint32_t(qd * 32) << 16) + 256 * t;
+    uint64_t* sf = s_full + 2 * t;
+    uint64_t* se = s_empty + 2 * t;
+    uint64_t* pf = p_full + 2 * t;
+    uint64_t* pe = p_empty + 2 * t;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nb; ++j) {
       const int sb = j & 1;
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, err, kErrTmemFullTimeout)) { ok = false; break; }
+      if (!mbar_wait(&sf[sb], (j >> 1) & 1, err, kErrTmemFullTimeout)) { ok = false; break; }
       tc_fence_after();
       uint32_t s[64];
       tmem_ld_32x32b_x32(lane_base + sb * TC_BN, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
@@ -242,7 +269,7 @@ __global__ void __launch_bounds__(192, 1)
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[sb]);
+      if (lane == 0) mbar_arrive(&se[sb]);
       const int kbase = j * TC_BN;
       float mx = -INFINITY;
 #pragma unroll
@@ -256,12 +283,12 @@ __global__ void __launch_bounds__(192, 1)
       const bool grow = m_new > m_run + TC_RESCALE_THRESHOLD;  // false while m_new == -inf
       const float m_use = grow ? m_new : m_run;
       const float o_scale = (grow && m_run != -INFINITY) ? ex2(m_run - m_new) : 1.f;
-      // P buffer sb is free once PV of block j-2 finished.
-      if (!mbar_wait(&p_empty[sb], ((j >> 1) & 1) ^ 1, err, kErrTmemEmptyTimeout)) { ok = false; break; }
+      // P buffer sb of this tile is free once PV of block j-2 finished.
+      if (!mbar_wait(&pe[sb], ((j >> 1) & 1) ^ 1, err, kErrTmemEmptyTimeout)) { ok = false; break; }
       if (j > 0 && __any_sync(0xffffffffu, o_scale != 1.f)) {
         // O must be stable: PV of block j-1 complete.
         const int pb = (j - 1) & 1;
-        if (!mbar_wait(&p_empty[pb], ((j - 1) >> 1) & 1, err, kErrTmemEmptyTimeout)) { ok = false; break; }
+        if (!mbar_wait(&pe[pb], ((j - 1) >> 1) & 1, err, kErrTmemEmptyTimeout)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < TC_D; c += 32) {
@@ -278,7 +305,7 @@ __global__ void __launch_bounds__(192, 1)
       m_run = m_use;
       // P = exp2(s - m) as bf16 into the swizzled K-major tile.
       float sum = 0.f;
-      const uint32_t prow = smem_u32(sP + sb * TC_P_BYTES) + r * 128;
+      const uint32_t prow = smem_u32(sP + (2 * t + sb) * TC_P_BYTES) + r * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint32_t pk[4];
@@ -298,7 +325,7 @@ __global__ void __launch_bounds__(192, 1)
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[sb]);
+      if (lane == 0) mbar_arrive(&pf[sb]);
     }
     // ----------------------------------------------------------- epilogue
     if (ok && mbar_wait(o_full, 0, err, kErrTmemFullTimeout)) {
@@ -381,7 +408,7 @@ extern "C" int ll_attn_prefill_tc(const bf16* q, const bf16* k_pool, const bf16*
     cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
     init = true;
   }
-  attn_prefill_tc_kernel<<<ntiles, 192, TC_SMEM, stream>>>(tk, tv, q, q_indptr, q_pos, page_table, pt_stride,
+  attn_prefill_tc_kernel<<<ntiles, TC_THREADS, TC_SMEM, stream>>>(tk, tv, q, q_indptr, q_pos, page_table, pt_stride,
                                                            reinterpret_cast<const int4*>(tiles), out, Hq, Hkv,
                                                            page_size, layer, scale * 1.4426950408889634f, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;

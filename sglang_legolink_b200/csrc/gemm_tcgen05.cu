@@ -407,6 +407,290 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---------------------------------------------------------------------------
+// 2-SM variant (cta_group::2): a cluster of two CTAs computes a 256 x BN
+// tile.  CTA r of the pair loads A rows [128r, 128r+128) and B rows
+// [BN/2 * r, BN/2 * (r+1)) of the tile into its own shared memory; the
+// leader (r = 0) issues tcgen05.mma.cta_group::2 (M=256, N=BN, K=16), which
+// reads both CTAs' operands and accumulates rows [128r, 128r+128) into CTA
+// r's TMEM.  Per SM this moves 32 KB of operands per 64-deep k-block instead
+// of 48 KB for the same FLOPs, so a 6-deep ring hides more load latency.
+// Both CTAs' TMA loads complete on the leader's `full` barrier; the leader's
+// commits arrive on both CTAs' `empty` / `tfull` barriers (commit multicast);
+// the epilogue warps of both CTAs release an accumulator on the leader's
+// `tempty` barrier.  No TMA load uses cluster multicast.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// shared::cluster address of the same variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_2sm(void* smem_dst, const void* tmap, uint32_t leader_bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(tmap), "r"(leader_bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_bf16_2sm(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n"
+      "}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrive on the barrier at this offset in both CTAs of the pair once every
+// MMA issued so far by this thread has completed.
+__device__ __forceinline__ void umma_commit_2sm_both(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)0x3)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit_2sm_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+template <int EPI>
+__device__ __forceinline__ void epi_store_chunk(const uint32_t (&r)[32], bf16* __restrict__ C,
+                                                const bf16* __restrict__ bias, int row, int col0, int M, int N,
+                                                int ldc) {
+  if (row >= M || col0 >= N) return;
+  if constexpr (EPI == kEpiSwiGLU) {
+    bf16* dst = C + (size_t)row * ldc + (col0 >> 1);
+    uint32_t packed[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float g0 = __uint_as_float(r[2 * i]), g1 = __uint_as_float(r[2 * i + 1]);
+      float u0 = __uint_as_float(r[16 + 2 * i]), u1 = __uint_as_float(r[16 + 2 * i + 1]);
+      if (bias != nullptr) {
+        g0 += __bfloat162float(bias[col0 + 2 * i]);
+        g1 += __bfloat162float(bias[col0 + 2 * i + 1]);
+        u0 += __bfloat162float(bias[col0 + 16 + 2 * i]);
+        u1 += __bfloat162float(bias[col0 + 16 + 2 * i + 1]);
+      }
+      packed[i] = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
+    }
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+    d4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    d4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+  } else {
+    bf16* dst = C + (size_t)row * ldc + col0;
+    if (col0 + 32 <= N) {
+      uint32_t packed[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float a0 = __uint_as_float(r[2 * i]), a1 = __uint_as_float(r[2 * i + 1]);
+        if (bias != nullptr) {
+          a0 += __bfloat162float(bias[col0 + 2 * i]);
+          a1 += __bfloat162float(bias[col0 + 2 * i + 1]);
+        }
+        packed[i] = pack_bf16x2(a0, a1);
+      }
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+    } else {
+      for (int i = 0; i < 32 && col0 + i < N; ++i) {
+        float a = __uint_as_float(r[i]);
+        if (bias != nullptr) a += __bfloat162float(bias[col0 + i]);
+        dst[i] = __float2bfloat16(a);
+      }
+    }
+  }
+}
+
+template <int BN>
+struct Gemm2Cfg {
+  static constexpr int STAGES = 6;
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;       // this CTA's 128 rows of A
+  static constexpr int B_BYTES = (BN / 2) * GEMM_BK * 2;      // this CTA's half of the B tile
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + 1024 + 256;
+};
+
+template <int BN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                            bf16* __restrict__ C, const bf16* __restrict__ bias, int M, int N, int K, int ldc,
+                            int* err) {
+  using Cfg = Gemm2Cfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int num_m = (M + 2 * GEMM_BM - 1) / (2 * GEMM_BM);
+  const int num_n = (N + BN - 1) / BN;
+  const int ntiles = num_m * num_n;
+  const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);  // 4 epilogue warps x 2 CTAs (used on the leader)
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"((uint32_t)Cfg::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmA);
+      prefetch_tmap(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < ntiles && ok; t += npairs) {
+        const int mb = t % num_m, nb = t / num_m;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrSmemEmptyTimeout)) {
+            ok = false;
+            break;
+          }
+          const uint32_t leader_full = mapa_shared(smem_u32(&full[stage]), 0);
+          if (crank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+          tma_load_2d_2sm(sA + stage * Cfg::A_BYTES, &tmA, leader_full, kb * GEMM_BK,
+                          mb * 2 * GEMM_BM + (int)crank * GEMM_BM);
+          tma_load_2d_2sm(sB + stage * Cfg::B_BYTES, &tmB, leader_full, kb * GEMM_BK,
+                          nb * BN + (int)crank * (BN / 2));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        unsigned long long t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 2000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && crank == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16_f32(2 * GEMM_BM, BN);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, aphase = 0;
+      bool ok = true;
+      for (int t = pair; t < ntiles && ok; t += npairs) {
+        if (!mbar_wait(&tempty[acc], aphase ^ 1, err, kErrTmemEmptyTimeout)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, err, kErrTmaFullTimeout)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = umma_desc_sw128_kmajor(smem_u32(sA + stage * Cfg::A_BYTES));
+          const uint64_t bd = umma_desc_sw128_kmajor(smem_u32(sB + stage * Cfg::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < GEMM_BK / 16; ++k)
+            umma_bf16_2sm(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit_2sm_both(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_2sm_both(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          aphase ^= 1;
+        }
+      }
+      umma_commit_2sm_local(drain);
+      mbar_wait(drain, 0, nullptr, 0);
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;
+    const uint32_t leader_tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    const uint32_t leader_tempty1 = mapa_shared(smem_u32(&tempty[1]), 0);
+    int acc = 0;
+    uint32_t aphase = 0;
+    for (int t = pair; t < ntiles; t += npairs) {
+      const int mb = t % num_m, nb = t / num_m;
+      if (!mbar_wait(&tfull[acc], aphase, err, kErrTmemFullTimeout)) break;
+      tc_fence_after();
+      const int row = mb * 2 * GEMM_BM + (int)crank * GEMM_BM + q * 32 + lane;
+      const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tbase + c, r);
+        tmem_ld_wait();
+        epi_store_chunk<EPI>(r, C, bias, row, nb * BN + c, M, N, ldc);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc == 0 ? leader_tempty0 : leader_tempty1);
+      if (++acc == 2) {
+        acc = 0;
+        aphase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"((uint32_t)Cfg::TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side.
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -477,6 +761,27 @@ extern "C" int ll_gemm_bf16(const bf16* A, int lda, const bf16* W, int ldw, bf16
   if (epilogue == kEpiSwiGLU && (N % 32)) return -4;
   CUtensorMap tA, tB;
   const int BN = (bn == 128) ? 128 : 256;
+  if (BN == 256 && M > 2 * GEMM_BM) {
+    // 2-SM tiles (256 x 256 per CTA pair).
+    if (make_tmap_2d(&tA, A, M, K, lda, GEMM_BM)) return -2;
+    if (make_tmap_2d(&tB, W, N, K, ldw, BN / 2)) return -2;
+    const int ntiles2 = ((M + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * ((N + BN - 1) / BN);
+    const int pairs = ntiles2 < num_sms() / 2 ? ntiles2 : num_sms() / 2;
+#define LL_LAUNCH2(EPI_)                                                                              \
+  do {                                                                                                \
+    auto kern = gemm_tcgen05_2sm_kernel<256, EPI_>;                                                   \
+    if (Gemm2Cfg<256>::SMEM > max_smem_optin()) return -7;                                            \
+    static bool init = false;                                                                         \
+    if (!init) {                                                                                      \
+      set_smem(kern, Gemm2Cfg<256>::SMEM);                                                            \
+      init = true;                                                                                    \
+    }                                                                                                 \
+    kern<<<2 * pairs, 192, Gemm2Cfg<256>::SMEM, stream>>>(tA, tB, C, bias, M, N, K, ldc, err);        \
+  } while (0)
+    if (epilogue == kEpiSwiGLU) LL_LAUNCH2(kEpiSwiGLU); else LL_LAUNCH2(kEpiPlain);
+#undef LL_LAUNCH2
+    return cudaGetLastError() == cudaSuccess ? 0 : -5;
+  }
   if (make_tmap_2d(&tA, A, M, K, lda, GEMM_BM)) return -2;
   if (make_tmap_2d(&tB, W, N, K, ldw, BN)) return -2;
   const int ntiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN);

@@ -192,7 +192,7 @@ def rope_qkv_write(qkv, positions, slots, cos_sin, q_out, k_pool_l, v_pool_l, nu
     return q_out
 
 
-PREFILL_ROWS_PER_TILE = 128  # packed (token, head) rows per CTA of the tcgen05 kernel
+PREFILL_ROWS_PER_TILE = 256  # packed (token, head) rows per CTA of the tcgen05 kernel (2 tiles of 128)
 
 
 def prefill_tiles(q_indptr_host: torch.Tensor, q_pos_host: torch.Tensor, num_heads: int, num_kv_heads: int,

@@ -18,6 +18,7 @@ def _rel(a, b):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 128), (256, 512, 1024), (1000, 4608, 3584), (77, 640, 512),
+                                   (600, 2200, 768), (1300, 2560, 1024), (257, 2048, 64),
                                    (384, 3584, 18944), (4096, 1024, 512)])
 def test_gemm_tcgen05(M, N, K):
     torch.manual_seed(0)
