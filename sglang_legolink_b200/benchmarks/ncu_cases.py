@@ -1,0 +1,54 @@
+"""Small single-kernel cases sized for `ncu --set full` captures (a few
+launches, a few hundred MB on the device), one per hot kernel:
+
+    python -m sglang_legolink_b200.benchmarks.ncu_cases {gemm,attn,gemv,decode,link}
+"""
+import sys, os, math
+
+import torch
+from sglang_legolink_b200 import ops
+from sglang_legolink_b200.ops import reference as ref
+case = sys.argv[1]
+torch.manual_seed(0)
+if case == "gemv":
+    for N, K in ((4608, 3584), (3584, 18944)):
+        a = torch.randn(1, K, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+        o = torch.empty(1, N, device="cuda", dtype=torch.bfloat16)
+        for _ in range(4): ops.linear(a, w, out=o)
+elif case == "gemm":
+    M, N, K = 2048, 37888, 3584
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    o = torch.empty(M, N // 2, device="cuda", dtype=torch.bfloat16)
+    for _ in range(4): ops.linear(a, w, out=o, swiglu_epilogue=True)
+elif case == "attn":
+    D, ps, Hq, Hkv, n, qrows = 128, 16, 28, 4, 8192, 2048
+    pages = n // ps
+    kp = torch.randn(1, pages, Hkv, ps, D, device="cuda", dtype=torch.bfloat16); vp = torch.randn_like(kp)
+    pt = torch.randperm(pages, device="cuda").to(torch.int32)[None]
+    pos = torch.sort(torch.randperm(n)[:qrows]).values.to(torch.int32)
+    qi = torch.tensor([0, qrows], dtype=torch.int32)
+    tiles = ops.prefill_tiles(qi, pos, Hq, Hkv).cuda()
+    q = torch.randn(qrows, Hq, D, device="cuda", dtype=torch.bfloat16)
+    kvl = torch.tensor([n], dtype=torch.int32, device="cuda")
+    for _ in range(4): ops.attention_prefill(q, kp, vp, 0, qi.cuda(), pos.cuda(), pt, kvl, 1/math.sqrt(D), tiles=tiles)
+elif case == "decode":
+    B, Hq, Hkv, n, D, ps = 1, 28, 4, 16640, 128, 16
+    pages = n // ps
+    kp = torch.randn(pages, Hkv, ps, D, device="cuda", dtype=torch.bfloat16); vp = torch.randn_like(kp)
+    pt = torch.randperm(pages, device="cuda").to(torch.int32)[None]
+    q = torch.randn(B, Hq, D, device="cuda", dtype=torch.bfloat16)
+    kvl = torch.full((B,), n, dtype=torch.int32, device="cuda")
+    for _ in range(4): ops.attention_decode(q, kp, vp, pt, kvl, 1/math.sqrt(D))
+elif case == "link":  # fused KV link + RoPE delta: 4096 tokens x 28 layers (Qwen2.5-7B KV layout)
+    L, Hkv, D, ps, n = 28, 4, 128, 16, 4096
+    pages = 2 * n // ps + 8
+    k = torch.randn(L, pages, Hkv, ps, D, device="cuda", dtype=torch.bfloat16); v = torch.randn_like(k)
+    src = torch.arange(n, device="cuda", dtype=torch.int64)
+    dst = src + (pages // 2) * ps
+    lp = torch.arange(n, device="cuda", dtype=torch.int32)
+    cs = ref.rope_cos_sin_table(32768, D, 1e6).cuda()
+    for _ in range(4): ops.kv_link_rope(k, v, src, dst, lp, lp + 3000, cs)
+torch.cuda.synchronize()
+print("ok", case, ops.check_errors("cuda"))
