@@ -96,6 +96,12 @@ def bench_small_m(pk, with_torch):
         gbs = (N * K * 2 + M * K * 2 + M * N * 2) / ms / 1e6
         r = {"op": f"gemm_small_m[{name}]", "M": M, "N": N, "K": K, "ms": round(ms, 4), "gbs": round(gbs, 1),
              "frac_of_hbm": round(gbs / pk["hbm_gbs"], 3)}
+        if N % 128 == 0 and K % 64 == 0:
+            wt = ops.tile_weight(w)
+            ext, wsp = ops._cuda(), ops.workspace("cuda")
+            mt = time_fn(lambda: ops._small_m(ext, wsp, a, wt, None, out))
+            r["tile_major_ms"] = round(mt, 4)
+            r["tile_major_frac_of_hbm"] = round((N * K * 2 + M * K * 2 + M * N * 2) / mt / 1e6 / pk["hbm_gbs"], 3)
         if with_torch:
             mt = time_fn(lambda: torch.matmul(a, w.t(), out=out))
             r["cublas_ms"] = round(mt, 4)

@@ -50,5 +50,15 @@ elif case == "link":  # fused KV link + RoPE delta: 4096 tokens x 28 layers (Qwe
     lp = torch.arange(n, device="cuda", dtype=torch.int32)
     cs = ref.rope_cos_sin_table(32768, D, 1e6).cuda()
     for _ in range(4): ops.kv_link_rope(k, v, src, dst, lp, lp + 3000, cs)
+elif case == "decode_step":  # Qwen2.5-7B, 16K context, eager decode steps (launch lists only: full size)
+    from sglang_legolink_b200.models.config import PRESETS
+    from sglang_legolink_b200.models.qwen import QwenModel
+    from sglang_legolink_b200.runtime.engine import Engine
+    cfg = PRESETS["qwen2.5-7b"]
+    m = QwenModel.random_init(cfg, seed=0, device="cuda", dtype=torch.bfloat16)
+    eng = Engine(m, page_size=16, max_context=17000, mem_fraction=0.5, use_cuda_graphs=False)
+    seq = eng.prefill(torch.randint(0, cfg.vocab_size, (16384,)).tolist())
+    torch.cuda.synchronize()
+    eng.decode([seq], int(os.environ.get("DECODE_STEPS", "3")))
 torch.cuda.synchronize()
 print("ok", case, ops.check_errors("cuda"))

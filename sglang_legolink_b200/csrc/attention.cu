@@ -292,6 +292,8 @@ __global__ void __launch_bounds__(32)
   const uint32_t sQ = smem_u32(smem);
   const uint32_t sK0 = sQ + 16 * AT_ROW_BYTES;
   const uint32_t sV0 = sK0 + 2 * DC_BN * AT_ROW_BYTES;
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x / Hkv, hk = blockIdx.x % Hkv;
   const int split = blockIdx.y, nsplit = gridDim.y;
   const int g = Hq / Hkv;
@@ -459,23 +461,36 @@ __global__ void __launch_bounds__(32)
 // grid (B*Hq), block 128 (one thread per head_dim element).  The split
 // maxima and weights are computed cooperatively in shared memory, then each
 // thread reduces its head_dim column over the splits (coalesced reads).
+// 256 threads: the split maxima and weights are computed cooperatively in
+// shared memory; then each of the 8 warps sums a strided subset of the
+// splits (lane l owns head_dim elements [4l, 4l+4) via float4 loads, 8 loads
+// in flight per lane) and the warps' partial vectors are added in shared
+// memory.  A thread-per-element loop over the splits is latency-bound.
 constexpr int CB_MAX_SPLITS = 1024;
-__global__ void __launch_bounds__(128) attn_combine_kernel(bf16* __restrict__ out, const float* __restrict__ ws_o,
-                                                           const float* __restrict__ ws_ml, int nsplit) {
+constexpr int CB_THREADS = 256;
+__global__ void __launch_bounds__(CB_THREADS) attn_combine_kernel(bf16* __restrict__ out,
+                                                                  const float* __restrict__ ws_o,
+                                                                  const float* __restrict__ ws_ml, int nsplit) {
   __shared__ float w[CB_MAX_SPLITS];
-  __shared__ float red[4];
+  __shared__ float red[CB_THREADS / 32];
+  __shared__ float4 part[CB_THREADS / 32][32];
+  pdl_trigger();
+  pdl_wait();
   const size_t row = blockIdx.x;
-  const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  constexpr int NW = CB_THREADS / 32;
   const float2* ml = reinterpret_cast<const float2*>(ws_ml) + row * nsplit;
   float M = -INFINITY;
-  for (int sp = d; sp < nsplit; sp += 128) M = fmaxf(M, ml[sp].x);
+  for (int sp = t; sp < nsplit; sp += CB_THREADS) M = fmaxf(M, ml[sp].x);
   M = warp_max(M);
   if (lane == 0) red[warp] = M;
   __syncthreads();
-  M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  M = red[0];
+#pragma unroll
+  for (int i = 1; i < NW; ++i) M = fmaxf(M, red[i]);
   __syncthreads();
   float den = 0.f;
-  for (int sp = d; sp < nsplit; sp += 128) {
+  for (int sp = t; sp < nsplit; sp += CB_THREADS) {
     const float2 v = ml[sp];
     const float wt = (v.x == -INFINITY || M == -INFINITY) ? 0.f : exp2f(v.x - M);
     w[sp] = wt;
@@ -484,12 +499,36 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(bf16* __restrict__ ou
   den = warp_sum(den);
   if (lane == 0) red[warp] = den;
   __syncthreads();
-  den = red[0] + red[1] + red[2] + red[3];
-  const float* o = ws_o + row * (size_t)nsplit * AT_D + d;
-  float num = 0.f;
-#pragma unroll 4
-  for (int sp = 0; sp < nsplit; ++sp) num += w[sp] * o[(size_t)sp * AT_D];
-  out[row * AT_D + d] = __float2bfloat16(den > 0.f ? num / den : 0.f);
+  den = 0.f;
+#pragma unroll
+  for (int i = 0; i < NW; ++i) den += red[i];
+  const float4* o = reinterpret_cast<const float4*>(ws_o + row * (size_t)nsplit * AT_D) + lane;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+  for (int sp = warp; sp < nsplit; sp += NW) {
+    const float4 v = __ldcg(o + (size_t)sp * (AT_D / 4));
+    const float wt = w[sp];
+    acc.x += wt * v.x;
+    acc.y += wt * v.y;
+    acc.z += wt * v.z;
+    acc.w += wt * v.w;
+  }
+  part[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0) {
+    float4 s = part[0][lane];
+#pragma unroll
+    for (int i = 1; i < NW; ++i) {
+      const float4 p = part[i][lane];
+      s.x += p.x;
+      s.y += p.y;
+      s.z += p.z;
+      s.w += p.w;
+    }
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    uint2 pk = make_uint2(pack_bf16x2(s.x * inv, s.y * inv), pack_bf16x2(s.z * inv, s.w * inv));
+    *reinterpret_cast<uint2*>(out + row * AT_D + 4 * lane) = pk;
+  }
 }
 
 }  // namespace ll
@@ -528,8 +567,9 @@ extern "C" int ll_attn_decode(const bf16* q, const bf16* kpool, const bf16* vpoo
   }
   dim3 grid(B * Hkv, nsplit);
   const float sl2 = scale * 1.4426950408889634f;
-  attn_decode_kernel<<<grid, 32, DC_SMEM, stream>>>(q, kpool, vpool, page_table, pt_stride, kv_lens, out, ws_o,
-                                                    ws_ml, Hq, Hkv, page_size, sl2);
-  if (nsplit > 1) attn_combine_kernel<<<B * Hq, AT_D, 0, stream>>>(out, ws_o, ws_ml, nsplit);
+  launch_pdl(attn_decode_kernel, grid, dim3(32), DC_SMEM, stream, q, kpool, vpool, page_table, pt_stride, kv_lens,
+             out, ws_o, ws_ml, Hq, Hkv, page_size, sl2);
+  if (nsplit > 1)
+    launch_pdl(attn_combine_kernel, dim3(B * Hq), dim3(CB_THREADS), 0, stream, out, ws_o, ws_ml, nsplit);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }

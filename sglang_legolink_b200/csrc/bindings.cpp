@@ -15,6 +15,9 @@ int ll_gemm_bf16_small_m(const bf16* A, int lda, const bf16* W, int ldw, bf16* C
                          int N, int K, int splits, float* ws, size_t ws_floats, int* tickets, int* err,
                          cudaStream_t stream);
 int ll_gemm_small_m_splits(int N, int K);
+int ll_gemm_bf16_small_m_ex(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc, const bf16* bias,
+                            int M, int N, int K, int splits, float* ws, size_t ws_floats, int* tickets, int* err,
+                            int w_tiled, cudaStream_t stream);
 int ll_rmsnorm(bf16* out, const bf16* x, bf16* residual, const bf16* w, int rows, int hidden, float eps,
                cudaStream_t stream);
 int ll_rope_qkv_write(const bf16* qkv, const int* positions, const int64_t* slots, const float* cos_sin, bf16* q_out,
@@ -79,12 +82,20 @@ void gemm_small_m(const at::Tensor& a, const at::Tensor& w, const c10::optional<
                   int64_t splits, at::Tensor& ws, at::Tensor& tickets, const at::Tensor& err) {
   CHECK_CUDA(a); CHECK_BF16(a); CHECK_BF16(w); CHECK_BF16(out); CHECK_CONTIG(w); CHECK_F32(ws); CHECK_I32(tickets);
   TORCH_CHECK(a.stride(1) == 1 && out.stride(1) == 1);
-  const int M = a.size(0), K = a.size(1), N = w.size(0);
-  TORCH_CHECK(w.size(1) == K && out.size(0) == M && out.size(1) == N);
+  // w: [N, K] row-major, or tile-major [N/128, K/64, 128, 64].
+  const bool tiled = w.dim() == 4;
+  const int M = a.size(0), K = a.size(1);
+  const int N = tiled ? (int)(w.size(0) * 128) : (int)w.size(0);
+  if (tiled) {
+    TORCH_CHECK(w.size(2) == 128 && w.size(3) == 64 && w.size(1) * 64 == K, "bad tile-major weight shape");
+  } else {
+    TORCH_CHECK(w.size(1) == K);
+  }
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N);
   c10::cuda::CUDAGuard g(a.device());
-  check_rc(ll_gemm_bf16_small_m(bp(a), a.stride(0), bp(w), w.stride(0), bp(out), out.stride(0), bp_opt(bias), M, N,
-                                K, (int)splits, ws.data_ptr<float>(), (size_t)ws.numel(), tickets.data_ptr<int>(),
-                                err.data_ptr<int>(), cur_stream()),
+  check_rc(ll_gemm_bf16_small_m_ex(bp(a), a.stride(0), bp(w), tiled ? K : (int)w.stride(0), bp(out), out.stride(0),
+                                   bp_opt(bias), M, N, K, (int)splits, ws.data_ptr<float>(), (size_t)ws.numel(),
+                                   tickets.data_ptr<int>(), err.data_ptr<int>(), tiled ? 1 : 0, cur_stream()),
            "ll_gemm_bf16_small_m");
 }
 

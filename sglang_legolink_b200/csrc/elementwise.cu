@@ -18,6 +18,8 @@ template <int VPT, bool ADD>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(bf16* __restrict__ out, const bf16* __restrict__ x,
                                                       bf16* __restrict__ residual, const bf16* __restrict__ w,
                                                       int hidden, float eps) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   const int nvec = hidden / 8;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * hidden);
@@ -96,6 +98,8 @@ __global__ void __launch_bounds__(256) rope_qkv_write_kernel(
     bf16* __restrict__ v_pool, const bf16* __restrict__ q_norm_w, const bf16* __restrict__ k_norm_w, int Hq,
     int Hkv, int page_size, int qkv_ld, float eps) {
   constexpr int D = 128;
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int pos = positions[t];
@@ -218,6 +222,8 @@ __global__ void __launch_bounds__(256) kv_link_rope_kernel(
 // are gate features [16j, 16j+16) and [32j+16, 32j+32) the matching up
 // features.  out[t, 16j+i] = silu(gate) * up.
 __global__ void swiglu_kernel(bf16* __restrict__ out, const bf16* __restrict__ gu, int T, int inter) {
+  pdl_trigger();
+  pdl_wait();
   const size_t nvec = (size_t)T * inter / 8;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < nvec; i += (size_t)gridDim.x * blockDim.x) {
     const size_t t = (i * 8) / inter, c = (i * 8) % inter;
@@ -239,6 +245,8 @@ __global__ void swiglu_kernel(bf16* __restrict__ out, const bf16* __restrict__ g
 // --------------------------------------------------------------- embedding
 __global__ void embedding_kernel(bf16* __restrict__ out, const int* __restrict__ ids, const bf16* __restrict__ table,
                                  int hidden, int vocab_start, int vocab_end) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   const int id = ids[t];
   uint4* o = reinterpret_cast<uint4*>(out + (size_t)t * hidden);
@@ -251,10 +259,28 @@ __global__ void embedding_kernel(bf16* __restrict__ out, const int* __restrict__
 // One CTA per row; ties resolve to the smallest index (torch.argmax order).
 __global__ void __launch_bounds__(1024) argmax_kernel(int* __restrict__ out, const bf16* __restrict__ logits,
                                                       int vocab, int ld) {
+  pdl_trigger();
+  pdl_wait();
   const bf16* row = logits + (size_t)blockIdx.x * ld;
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+  // 16-byte loads (8 logits) with several in flight per thread; each thread
+  // visits its indices in increasing order, so a strict '>' keeps the first.
+  const bool vec = ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
+  const int nvec = vec ? vocab / 8 : 0;
+  const uint4* rv = reinterpret_cast<const uint4*>(row);
+#pragma unroll 4
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+    const uint4 x = __ldg(rv + v);
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(&x);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(u[j]);
+      if (f.x > best) { best = f.x; bi = 8 * v + 2 * j; }
+      if (f.y > best) { best = f.y; bi = 8 * v + 2 * j + 1; }
+    }
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < vocab; i += blockDim.x) {
     const float v = __bfloat162float(row[i]);
     if (v > best || (v == best && i < bi)) {
       best = v;
@@ -308,9 +334,11 @@ extern "C" int ll_rmsnorm(bf16* out, const bf16* x, bf16* residual, const bf16* 
 #define LL_RMS(V)                                                                                           \
   do {                                                                                                      \
     if (residual)                                                                                           \
-      rmsnorm_kernel<V, true><<<rows, threads, 0, stream>>>(out, x, residual, w, hidden, eps);              \
+      launch_pdl(rmsnorm_kernel<V, true>, dim3(rows), dim3(threads), 0, stream, out, x, residual, w, hidden, \
+                 eps);                                                                                      \
     else                                                                                                    \
-      rmsnorm_kernel<V, false><<<rows, threads, 0, stream>>>(out, x, residual, w, hidden, eps);             \
+      launch_pdl(rmsnorm_kernel<V, false>, dim3(rows), dim3(threads), 0, stream, out, x, residual, w,       \
+                 hidden, eps);                                                                              \
   } while (0)
   if (vpt <= 1) LL_RMS(1);
   else if (vpt <= 2) LL_RMS(2);
@@ -327,8 +355,8 @@ extern "C" int ll_rope_qkv_write(const bf16* qkv, const int* positions, const in
                                  cudaStream_t stream) {
   if (T <= 0) return 0;
   if (head_dim != 128) return -3;
-  rope_qkv_write_kernel<<<T, 256, 0, stream>>>(qkv, positions, slots, cos_sin, q_out, k_pool, v_pool, q_norm_w,
-                                               k_norm_w, Hq, Hkv, page_size, qkv_ld, eps);
+  launch_pdl(rope_qkv_write_kernel, dim3(T), dim3(256), 0, stream, qkv, positions, slots, cos_sin, q_out, k_pool,
+             v_pool, q_norm_w, k_norm_w, Hq, Hkv, page_size, qkv_ld, eps);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
@@ -353,7 +381,7 @@ extern "C" int ll_swiglu(bf16* out, const bf16* gu, int T, int inter, cudaStream
   const size_t nvec = (size_t)T * inter / 8;
   int blocks = (int)((nvec + 255) / 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
-  swiglu_kernel<<<blocks, 256, 0, stream>>>(out, gu, T, inter);
+  launch_pdl(swiglu_kernel, dim3(blocks), dim3(256), 0, stream, out, gu, T, inter);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
@@ -361,12 +389,12 @@ extern "C" int ll_embedding(bf16* out, const int* ids, const bf16* table, int T,
                             int vocab_end, cudaStream_t stream) {
   if (T <= 0) return 0;
   if (hidden % 8) return -3;
-  embedding_kernel<<<T, 128, 0, stream>>>(out, ids, table, hidden, vocab_start, vocab_end);
+  launch_pdl(embedding_kernel, dim3(T), dim3(128), 0, stream, out, ids, table, hidden, vocab_start, vocab_end);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
 extern "C" int ll_argmax(int* out, const bf16* logits, int rows, int vocab, int ld, cudaStream_t stream) {
   if (rows <= 0) return 0;
-  argmax_kernel<<<rows, 1024, 0, stream>>>(out, logits, vocab, ld);
+  launch_pdl(argmax_kernel, dim3(rows), dim3(1024), 0, stream, out, logits, vocab, ld);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }

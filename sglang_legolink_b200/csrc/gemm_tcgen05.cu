@@ -250,17 +250,21 @@ template <int BNX>
 struct SwapCfg {
   static constexpr int W_BYTES = GEMM_BM * GEMM_BK * 2;  // 16 KB
   static constexpr int X_BYTES = BNX * GEMM_BK * 2;
-  // as deep a ring as fits in ~200 KB (8 stages for BNX <= 64, 6 for 128)
-  static constexpr int STAGES = (200 * 1024) / (W_BYTES + X_BYTES) > 8 ? 8 : (200 * 1024) / (W_BYTES + X_BYTES);
+  // A ring of <= 108 KB so that two CTAs share an SM: one CTA's tail then
+  // overlaps the next CTA's start, and two independent streams keep twice
+  // the weight bytes in flight (6 stages for BNX=16, 5 for 32, 4 for 64,
+  // 3 for 128).
+  static constexpr int STAGES = (108 * 1024) / (W_BYTES + X_BYTES);
   static constexpr int TMEM_COLS = BNX < 32 ? 32 : BNX;
   static constexpr int SMEM = STAGES * (W_BYTES + X_BYTES) + 1024 + 256;
 };
 
 template <int BNX>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, 2)
     gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                        bf16* __restrict__ C, const bf16* __restrict__ bias, int M, int N, int K, int ldc,
-                       int kb_per_split, float* __restrict__ ws, int* __restrict__ tickets, int* err) {
+                       int kb_per_split, float* __restrict__ ws, int* __restrict__ tickets, int* err,
+                       int w_tiled) {
   using Cfg = SwapCfg<BNX>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -279,6 +283,7 @@ __global__ void __launch_bounds__(192, 1)
   const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
   const int kb0 = split * kb_per_split;
   const int kb1 = min(num_kb, kb0 + kb_per_split);
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -301,13 +306,31 @@ __global__ void __launch_bounds__(192, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int kb = kb0; kb < kb1; ++kb) {
+      // The weights do not depend on the previous kernel: start streaming the
+      // first ring's worth of them before waiting for it, then add the
+      // activation tiles once its output is visible.
+      const int pre = (kb1 - kb0) < STAGES ? (kb1 - kb0) : STAGES;
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], Cfg::W_BYTES + Cfg::X_BYTES);
+        if (w_tiled)  // one contiguous 16 KB tile
+          tma_load_4d_(sW + i * Cfg::W_BYTES, &tmW, &full[i], 0, 0, kb0 + i, nb);
+        else
+          tma_load_2d(sW + i * Cfg::W_BYTES, &tmW, &full[i], (kb0 + i) * GEMM_BK, nb * GEMM_BM);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(sX + i * Cfg::X_BYTES, &tmX, &full[i], (kb0 + i) * GEMM_BK, 0);
+      if (pre == STAGES) phase = 1;  // stage wrapped around exactly once
+      for (int kb = kb0 + pre; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrSmemEmptyTimeout)) {
           ok = false;
           break;
         }
         mbar_arrive_expect_tx(&full[stage], Cfg::W_BYTES + Cfg::X_BYTES);
-        tma_load_2d(sW + stage * Cfg::W_BYTES, &tmW, &full[stage], kb * GEMM_BK, nb * GEMM_BM);
+        if (w_tiled)
+          tma_load_4d_(sW + stage * Cfg::W_BYTES, &tmW, &full[stage], 0, 0, kb, nb);
+        else
+          tma_load_2d(sW + stage * Cfg::W_BYTES, &tmW, &full[stage], kb * GEMM_BK, nb * GEMM_BM);
         tma_load_2d(sX + stage * Cfg::X_BYTES, &tmX, &full[stage], kb * GEMM_BK, 0);
         if (++stage == STAGES) {
           stage = 0;
@@ -345,6 +368,7 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     const int q = warp & 3;
     const int feat = nb * GEMM_BM + q * 32 + lane;  // output column of C
+    pdl_wait();  // outputs / workspace may still be in use by the previous kernel
     bool ok = mbar_wait(tfull, 0, err, kErrTmemFullTimeout);
     tc_fence_after();
     const bool empty_split = (kb1 <= kb0);
@@ -808,15 +832,44 @@ extern "C" int ll_gemm_bf16(const bf16* A, int lda, const bf16* W, int ldw, bf16
 
 extern "C" int ll_gemm_small_m_splits(int N, int K);
 
+// Tile-major weights: W stored as [N/128][K/64][128][64] so that every TMA
+// box of the small-M kernel is one contiguous 16 KB block (row-major W reads
+// 128 rows x 128 B scattered by the row pitch).
+static int make_tmap_w_tiled(CUtensorMap* tm, const void* ptr, int N, int K) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return -1;
+  cuuint64_t dims[4] = {64, 128, (cuuint64_t)(K / 64), (cuuint64_t)(N / 128)};
+  cuuint64_t strides[3] = {128, 16384, (cuuint64_t)16384 * (K / 64)};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+extern "C" int ll_gemm_bf16_small_m_ex(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc,
+                                       const bf16* bias, int M, int N, int K, int splits, float* ws,
+                                       size_t ws_floats, int* tickets, int* err, int w_tiled, cudaStream_t stream);
+
 // Small-M path.  ws must hold splits*M*N floats, tickets ceil(N/128) ints
 // (zero-initialised once; the kernel leaves them zero).  splits <= 0 picks a
 // split count that puts about one CTA on every SM.
 extern "C" int ll_gemm_bf16_small_m(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc,
                                     const bf16* bias, int M, int N, int K, int splits, float* ws, size_t ws_floats,
                                     int* tickets, int* err, cudaStream_t stream) {
+  return ll_gemm_bf16_small_m_ex(A, lda, W, ldw, C, ldc, bias, M, N, K, splits, ws, ws_floats, tickets, err, 0,
+                                 stream);
+}
+
+// Same, with `w_tiled` = 1 for tile-major W (N % 128 == 0, K % 64 == 0).
+extern "C" int ll_gemm_bf16_small_m_ex(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc,
+                                       const bf16* bias, int M, int N, int K, int splits, float* ws,
+                                       size_t ws_floats, int* tickets, int* err, int w_tiled, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if (M > 128) return -3;
   if ((K % 8) || (lda % 8) || (ldw % 8)) return -3;
+  if (w_tiled && ((N % 128) || (K % 64))) return -3;
   const int ntiles = (N + GEMM_BM - 1) / GEMM_BM;
   const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
   if (splits <= 0) splits = ll_gemm_small_m_splits(N, K);
@@ -825,7 +878,7 @@ extern "C" int ll_gemm_bf16_small_m(const bf16* A, int lda, const bf16* W, int l
   if (splits > 1 && (ws == nullptr || tickets == nullptr || ws_floats < (size_t)splits * M * N)) return -6;
   const int BNX = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
   CUtensorMap tW, tX;
-  if (make_tmap_2d(&tW, W, N, K, ldw, GEMM_BM)) return -2;
+  if (w_tiled ? make_tmap_w_tiled(&tW, W, N, K) : make_tmap_2d(&tW, W, N, K, ldw, GEMM_BM)) return -2;
   if (make_tmap_2d(&tX, A, M, K, lda, BNX)) return -2;
   dim3 grid(ntiles, splits);
 #define LL_LAUNCH_S(BNX_)                                                                                \
@@ -837,8 +890,8 @@ extern "C" int ll_gemm_bf16_small_m(const bf16* A, int lda, const bf16* W, int l
       set_smem(kern, SwapCfg<BNX_>::SMEM);                                                               \
       init = true;                                                                                       \
     }                                                                                                    \
-    kern<<<grid, 192, SwapCfg<BNX_>::SMEM, stream>>>(tW, tX, C, bias, M, N, K, ldc, kb_per, ws, tickets, \
-                                                     err);                                               \
+    launch_pdl(kern, grid, dim3(192), SwapCfg<BNX_>::SMEM, stream, tW, tX, C, bias, M, N, K, ldc, kb_per, ws, \
+               tickets, err, w_tiled);                                                                   \
   } while (0)
   switch (BNX) {
     case 16: LL_LAUNCH_S(16); break;
@@ -850,12 +903,12 @@ extern "C" int ll_gemm_bf16_small_m(const bf16* A, int lda, const bf16* W, int l
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
-// Split count that keeps the grid within one wave of CTAs (one per SM):
-// floor(SMs / tiles), so no SM runs a second CTA while others idle.
+// Split count that keeps the grid within one wave of resident CTAs (two per
+// SM): floor(2 * SMs / tiles), so no SM runs a third CTA while others idle.
 extern "C" int ll_gemm_small_m_splits(int N, int K) {
   const int ntiles = (N + GEMM_BM - 1) / GEMM_BM;
   const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
-  int splits = num_sms() / ntiles;
+  int splits = 2 * num_sms() / ntiles;
   if (splits > num_kb / 2) splits = num_kb / 2;
   if (splits < 1) splits = 1;
   int kb_per = (num_kb + splits - 1) / splits;

@@ -126,9 +126,22 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None
     return out
 
 
+def tile_weight(w: torch.Tensor) -> torch.Tensor:
+    """[N, K] -> tile-major [N/128, K/64, 128, 64]: each 128-row x 64-column
+    TMA box of the small-M GEMM becomes one contiguous 16 KB block."""
+    N, K = w.shape
+    assert N % 128 == 0 and K % 64 == 0, "tile-major weights need N % 128 == 0 and K % 64 == 0"
+    return w.reshape(N // 128, 128, K // 64, 64).permute(0, 2, 1, 3).contiguous()
+
+
+def untile_weight(wt: torch.Tensor) -> torch.Tensor:
+    a, b, c, d = wt.shape
+    return wt.permute(0, 2, 1, 3).reshape(a * c, b * d)
+
+
 def _small_m(ext, ws, x, w, bias, out):
     M, K = x.shape
-    N = w.shape[0]
+    N = w.shape[0] * 128 if w.dim() == 4 else w.shape[0]
     splits = ext.gemm_small_m_splits(N, K)
     if splits > 1:
         need = splits * M * N

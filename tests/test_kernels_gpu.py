@@ -229,3 +229,15 @@ def test_swiglu_embedding_argmax():
     assert torch.equal(ops.embedding(ids, table), table[ids.long()])
     logits = torch.randn(5, 152064, device=DEV, dtype=torch.bfloat16)
     assert torch.equal(ops.argmax(logits).cpu(), torch.argmax(logits.float(), -1).int().cpu())
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 4608, 3584), (16, 3584, 18944), (64, 1024, 512)])
+def test_gemm_small_m_tile_major_weights(M, N, K):
+    torch.manual_seed(8)
+    a = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    wt = ops.tile_weight(w)
+    assert torch.equal(ops.untile_weight(wt), w)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    ops._small_m(ops._cuda(), ops.workspace(DEV), a, wt, None, out)
+    assert _rel(out, a.float() @ w.float().t()) < 1e-2
