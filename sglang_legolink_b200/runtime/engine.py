@@ -36,6 +36,7 @@ from ..ops import _ext
 from ..utils import launch_count
 from ..utils.trace import emit_trace, CudaTimer
 from .link_plan import ResolvedLinkPlan, resolve_link_plan
+from .sampling import GREEDY, SamplingParams, make_generator, sample_rows
 
 
 class RuntimeErrorAbort(RuntimeError):
@@ -66,6 +67,8 @@ class Sequence_:
     link_plan: Optional[ResolvedLinkPlan] = None
     timings: dict = field(default_factory=dict)
     finished: bool = False
+    sampling: SamplingParams = GREEDY
+    generator: Optional[torch.Generator] = None
 
 
 class KVPool:
@@ -229,8 +232,23 @@ class Engine:
             tiles=tiles,
         )
 
-    def _sample(self, logits: torch.Tensor) -> torch.Tensor:
-        return self.model.greedy(logits)
+    def _sample(self, logits: torch.Tensor, params: Sequence[SamplingParams] = (),
+                gens: Sequence[Optional[torch.Generator]] = (), greedy: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Token ids for the rows of ``logits`` (this rank's vocab shard).
+        Greedy rows come from the argmax kernel; when any row samples, the
+        full-vocab logits are gathered (TP) and those rows are redrawn."""
+        ids = greedy if greedy is not None else self.model.greedy(logits)
+        if not any(not p.greedy for p in params):
+            return ids
+        full = self.model.full_logits(logits[: len(params)])
+        drawn = sample_rows(full, list(params), list(gens) or None)
+        ids = ids.clone()
+        ids[: len(params)] = drawn.to(ids.device)
+        return ids
+
+    def _new_sampling(self, sampling: Optional[SamplingParams]):
+        sp = sampling or GREEDY
+        return sp, make_generator(sp, self.device)
 
     # --------------------------------------------------------------- compile
     def compile(self, token_ids: Sequence[int], cache_key: str, *, sub_context: Optional[dict] = None,
@@ -356,7 +374,7 @@ class Engine:
         return {o: tuple(torch.cat(x) for x in g) for o, g in groups.items()}
 
     def link(self, pic_link: dict, mutable_input_ids: Sequence[int], *, rid: Optional[str] = None,
-             timer: Optional["CudaTimer"] = None) -> Sequence_:
+             timer: Optional["CudaTimer"] = None, sampling: Optional[SamplingParams] = None) -> Sequence_:
         """Executes one Link.  Returns a sequence whose KV holds the whole
         linked prompt and whose ``output_ids[0]`` is the first token."""
         with self._lock:
@@ -373,7 +391,7 @@ class Engine:
                 self.registry.acquire(keys)
                 try:
                     pages = self._alloc_pages(pages_for(resolved.total_token_count, self.page_size))
-                    seq = self._run_link(resolved, pages, rid, timer)
+                    seq = self._run_link(resolved, pages, rid, timer, sampling)
                 finally:
                     self.registry.release(keys)
             except Exception:
@@ -394,8 +412,10 @@ class Engine:
             self.stats["links"] += 1
             return seq
 
-    def _run_link(self, resolved: ResolvedLinkPlan, pages: list[int], rid: str, timer) -> Sequence_:
+    def _run_link(self, resolved: ResolvedLinkPlan, pages: list[int], rid: str, timer,
+                  sampling: Optional[SamplingParams] = None) -> Sequence_:
         dev = self.device
+        sp, gen = self._new_sampling(sampling)
         timer = timer or CudaTimer(enabled=False)
         with timer.span("kv_link"):
             groups = self._link_rows(resolved, pages)
@@ -417,16 +437,17 @@ class Engine:
         with timer.span("sparse_repair"):
             fb = self._extend_batch([(toks, rows, pages, resolved.total_token_count)])
             logits = self.model.forward(fb, self.kv)
-            first = self._sample(logits)
+            first = self._sample(logits, [sp], [gen])
         first_id = int(first[0].item())
         emit_trace("model_link_complete", rid=rid, total_token_count=resolved.total_token_count,
                    recompute_rows=len(rows), linked_rows=nlinked)
         return Sequence_(rid=rid, token_ids=list(resolved.linked_token_ids), pages=pages,
-                         length=resolved.total_token_count, output_ids=[first_id], kind="link", link_plan=resolved)
+                         length=resolved.total_token_count, output_ids=[first_id], kind="link", link_plan=resolved,
+                         sampling=sp, generator=gen)
 
     # --------------------------------------------------------------- prefill
     def prefill(self, token_ids: Sequence[int], *, rid: Optional[str] = None, namespace: Optional[str] = None,
-                use_prefix_cache: bool = False) -> Sequence_:
+                use_prefix_cache: bool = False, sampling: Optional[SamplingParams] = None) -> Sequence_:
         """Full prefill of a plain prompt (the baseline of a Link)."""
         with self._lock:
             toks = [int(t) for t in token_ids]
@@ -448,16 +469,18 @@ class Engine:
                     self.alloc.release(cached)
                 raise
             try:
+                sp, gen = self._new_sampling(sampling)
                 fb = self._extend_batch([(toks[start:], list(range(start, n)), pages, n)])
                 logits = self.model.forward(fb, self.kv)
-                first = int(self._sample(logits)[0].item())
+                first = int(self._sample(logits, [sp], [gen])[0].item())
             except Exception:
                 self.alloc.release(pages)
                 raise
             if use_prefix_cache:
                 self.radix.insert(namespace or "", toks, pages)
             self.stats["prefills"] += 1
-            return Sequence_(rid=rid, token_ids=toks, pages=pages, length=n, output_ids=[first], kind="plain")
+            return Sequence_(rid=rid, token_ids=toks, pages=pages, length=n, output_ids=[first], kind="plain",
+                             sampling=sp, generator=gen)
 
     # ---------------------------------------------------------------- decode
     def decode(self, seqs: list[Sequence_], steps: int, stop_ids: Sequence[int] = ()) -> None:
@@ -519,7 +542,7 @@ class Engine:
                           q_indptr=torch.arange(B + 1, dtype=torch.int32).to(dev), page_table=pt.to(dev),
                           kv_lens=kvl.to(dev), logit_rows=None)
         logits = self.model.forward(fb, self.kv)
-        return self._sample(logits).tolist()
+        return self._sample(logits, [s.sampling for s in seqs], [s.generator for s in seqs]).tolist()
 
     def _bucket(self, B: int) -> int:
         for b in (1, 2, 4, 8, 16, 32, 64):
@@ -543,6 +566,9 @@ class Engine:
         g["kvl"].copy_(kvl, non_blocking=True)
         g["graph"].replay()
         launch_count.add(g["launches"])
+        if any(not s.sampling.greedy for s in seqs):
+            return self._sample(g["logits"][:B], [s.sampling for s in seqs], [s.generator for s in seqs],
+                                greedy=g["out"][:B]).tolist()
         return g["out"][:B].tolist()
 
     def _capture(self, bucket: int, max_pages: int, seqs) -> dict:
@@ -567,6 +593,7 @@ class Engine:
         torch.cuda.current_stream(dev).wait_stream(s)
         graph = torch.cuda.CUDAGraph()
         with launch_count.Recorder() as rec, torch.cuda.graph(graph):
-            self.model.greedy(self.model.forward(fb, self.kv), out=out)
-        st.update(graph=graph, out=out, fb=fb, launches=rec.n)
+            logits = self.model.forward(fb, self.kv)
+            self.model.greedy(logits, out=out)
+        st.update(graph=graph, out=out, logits=logits, fb=fb, launches=rec.n)
         return st

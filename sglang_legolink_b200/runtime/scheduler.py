@@ -32,6 +32,7 @@ from typing import Any, Callable, Optional
 from ..contract import ContractError
 from ..utils.trace import emit_trace
 from .engine import Engine, RuntimeErrorAbort, Sequence_
+from .sampling import GREEDY, SamplingParams
 
 
 class RequestRejected(ValueError):
@@ -51,6 +52,7 @@ class Request:
     events: "queue.Queue" = field(default_factory=queue.Queue)  # ("token", id) | ("done", info) | ("error", msg)
     seq: Optional[Sequence_] = None
     ttft_s: Optional[float] = None
+    sampling: SamplingParams = GREEDY
 
 
 class Scheduler:
@@ -141,12 +143,12 @@ class Scheduler:
                 self.stats["finished"] += 1
                 return
             if req.kind == "link":
-                seq = eng.link(req.pic_link, req.input_ids, rid=req.rid)
+                seq = eng.link(req.pic_link, req.input_ids, rid=req.rid, sampling=req.sampling)
                 if seq.length + req.max_new_tokens > self.max_context:
                     eng.free(seq)
                     raise RequestRejected("overlength Link (total tokens + max_tokens exceeds the context window)")
             else:
-                seq = eng.prefill(req.input_ids, rid=req.rid)
+                seq = eng.prefill(req.input_ids, rid=req.rid, sampling=req.sampling)
             req.seq = seq
             req.ttft_s = time.perf_counter() - req.created
             first = seq.output_ids[-1]

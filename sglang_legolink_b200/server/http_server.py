@@ -33,6 +33,7 @@ from typing import Any, Optional
 
 from ..contract import ContractError, physical_token_ids_sha256, validate_physical_token_input
 from ..runtime.scheduler import Request, RequestRejected, Scheduler
+from ..runtime.sampling import SamplingParams
 
 
 def _prompt_ids(tokenizer, payload: dict) -> list[int]:
@@ -64,6 +65,8 @@ class RuntimeService:
             raise RequestRejected("a Link may not request input logprobs")
         max_new = int(payload.get("max_tokens") or payload.get("max_completion_tokens") or 16)
         stop = (self.eos,) if (self.eos is not None and not payload.get("ignore_eos")) else ()
+        stop = stop + tuple(int(t) for t in (payload.get("stop_token_ids") or ()))
+        sampling = SamplingParams.from_request(payload)
         rid = str(payload.get("rid") or (link or {}).get("request_id") or uuid.uuid4().hex[:16])
         if sc is not None:
             if not isinstance(sc, dict):
@@ -77,13 +80,13 @@ class RuntimeService:
                 ids = validate_physical_token_input(link, label="pic_link")
             else:
                 ids = _prompt_ids(self.tokenizer, payload)
-            return Request("link", rid, list(ids or []), max_new, stop, pic_link=link)
+            return Request("link", rid, list(ids or []), max_new, stop, pic_link=link, sampling=sampling)
         if "prompt" in payload:
             p = payload["prompt"]
             ids = list(p) if isinstance(p, list) else list(self.tokenizer.tokenize(str(p)))
         else:
             ids = _prompt_ids(self.tokenizer, payload)
-        return Request("plain", rid, ids, max_new, stop)
+        return Request("plain", rid, ids, max_new, stop, sampling=sampling)
 
     def complete(self, payload: dict) -> dict:
         req = self.build_request(payload)
