@@ -3,28 +3,33 @@
 // Same contract as attn_prefill_kernel (attention.cu): query rows at arbitrary
 // positions, keys = the request's paged KV, causal by logical position, GQA
 // rows packed as (token, q-head-of-the-group) pairs.  One CTA owns TC_NT = 2
-// tiles of 128 packed rows of one (request, kv head) and walks 64-key blocks;
-// both tiles share every K/V block:
+// tiles of 128 packed rows of one (request, kv head) and walks 128-key blocks;
+// both tiles share every K/V block.
 //
 //   warp 0      TMA producer: K and V pages of each block (one box of
-//               page_size keys x 64 dims per page and half), 2-stage ring.
-//   warp 1      MMA issuer (one thread), per block j: S(t, j) = Q_t K_j^T for
-//               both tiles into their TMEM S double buffers (M=128, N=64,
-//               K=16 x 8), then O_t += P(t, j-1) V_{j-1} (M=128, N=128,
-//               K=16 x 4; V is the MN-major B operand).
-//   warps 2..9  two softmax warpgroups, one per tile, one query row per
-//               thread (TMEM lane = row): read S with tcgen05.ld, mask by
-//               position, online max/sum in fp32 (log2 domain), write P (bf16)
-//               to shared memory in the 128-byte swizzled K-major layout the
-//               MMA reads.  O stays in TMEM; it is rescaled (tcgen05.ld/st)
-//               only when a row's running max grows by more than 2^8, so
-//               P <= 256 and most blocks skip the rescale.  While one
-//               warpgroup runs its softmax the tensor core works on the other
-//               tile.
+//               page_size keys x 64 dims per page and half) into separate
+//               K and V rings, so K of block j+1 streams while V of block j
+//               is still in use.
+//   warp 1      MMA issuer (one thread).  Per block j and tile t:
+//                 O_t += P_t(j-1) V_{j-1}   A = P from TMEM, B = V (MN-major)
+//                 S_t  = Q_t K_j^T          A = Q, B = K from shared memory
+//               P_t aliases the first 64 columns of S_t (bf16 pairs), so
+//               each tile needs 256 TMEM columns (S/P 128 + O 128).  The
+//               tensor pipe executes one thread's MMAs in issue order, so
+//               S_t(j) overwriting P_t(j-1) after the PV MMA that reads it
+//               is safe.  While softmax t works on S_t(j), the tensor core
+//               runs the other tile's PV and S MMAs (ping-pong).
+//   warps 2,3   idle (their registers go to the softmax warpgroups).
+//   warps 4..11 two softmax warpgroups, one per tile, one query row per
+//               thread (TMEM lane = row): tcgen05.ld S, causal mask, online
+//               max/sum in fp32 (log2 domain), P = exp2(S*scale - m) as bf16
+//               written back to TMEM with tcgen05.st.  O stays in TMEM; it
+//               is rescaled in place only when a row's running max grows by
+//               more than 2^8, so P <= 256 and most blocks skip the rescale.
+//               At the end: O / l -> global memory.
 //
-// Barriers: kv_full/kv_empty per stage; s_full/s_empty and p_full/p_empty
-// per tile and double buffer; q_full, o_full.  Every wait is bounded
-// (common.cuh).
+// Barriers: k_full/k_empty, v_full/v_empty per stage; s_full, p_full per
+// tile; q_full, o_full.  Every wait is bounded (common.cuh).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -34,17 +39,27 @@ namespace ll {
 
 constexpr int TC_BM = 128;        // packed query rows per tile
 constexpr int TC_NT = 2;          // tiles per CTA
-constexpr int TC_BN = 64;         // keys per block
+constexpr int TC_BN = 128;        // keys per block
 constexpr int TC_D = 128;
-constexpr int TC_STAGES = 2;
+constexpr int TC_KS = 2;          // K ring stages
+constexpr int TC_VS = 2;          // V ring stages
 constexpr int TC_Q_BYTES = TC_BM * TC_D * 2;         // 32 KB per tile: [2 halves][128 rows][128 B]
 constexpr int TC_Q_HALF = TC_BM * 128;               // 16 KB
-constexpr int TC_KV_BYTES = TC_BN * TC_D * 2;        // 16 KB: [2 halves][64 rows][128 B]
-constexpr int TC_KV_HALF = TC_BN * 128;              // 8 KB
-constexpr int TC_P_BYTES = TC_BM * TC_BN * 2;        // 16 KB: [128 rows][128 B]
-constexpr int TC_SMEM = TC_NT * TC_Q_BYTES + 2 * TC_STAGES * TC_KV_BYTES + TC_NT * 2 * TC_P_BYTES + 1024 + 512;
-constexpr uint32_t TC_TMEM_COLS = 512;               // per tile t: S0 [256t, +64) S1 [+64, +128) O [+128, +256)
-constexpr int TC_THREADS = 64 + 128 * TC_NT;
+constexpr int TC_KV_BYTES = TC_BN * TC_D * 2;        // 32 KB: [2 halves][128 keys][128 B]
+constexpr int TC_KV_HALF = TC_BN * 128;              // 16 KB
+constexpr int TC_SMEM = TC_NT * TC_Q_BYTES + (TC_KS + TC_VS) * TC_KV_BYTES + 1024 + 256;
+constexpr uint32_t TC_TMEM_COLS = 512;               // S_t/P_t at 128t, O_t at 256 + 128t
+constexpr int TC_THREADS = 128 + 128 * TC_NT;        // warpgroup 0: producer, MMA, 2 idle; then softmax
+// Register split (setmaxnreg): the CTA launches at 168 registers per thread
+// (384 x 168 = 64512; 3 warps per SM sub-partition x 32 x 168 <= 16384).
+// Warpgroup 0 gives registers back, the softmax warpgroups take them:
+// 4 x 32 x 80 + 8 x 32 x 208 = 63488 <= 64512, the launch total, and per
+// sub-partition 32 x (80 + 2 x 208) = 15872 <= 16384.
+constexpr int TC_REGS_LAUNCH = 168;
+constexpr int TC_REGS_CTRL = 80;
+constexpr int TC_REGS_SOFTMAX = 208;
+static_assert(4 * TC_REGS_CTRL + 4 * TC_NT * TC_REGS_SOFTMAX <= (TC_THREADS / 32) * TC_REGS_LAUNCH,
+              "register split exceeds the launch allocation");
 constexpr float TC_RESCALE_THRESHOLD = 8.0f;         // log2 units
 
 __device__ __forceinline__ float ex2(float x) {
@@ -66,6 +81,19 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mnmajor(uint32_t smem_addr, 
   return d;
 }
 
+// D(tmem) (+)= A(tmem) * B(smem): A is M x K with row m in TMEM lane m and
+// K elements packed two per 32-bit column.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
+      "}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -75,6 +103,14 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
       "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
       "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]));
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]));
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -101,17 +137,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                   // [TC_NT][Q]
-  uint8_t* sK = sQ + TC_NT * TC_Q_BYTES;                // [STAGES][KV]
-  uint8_t* sV = sK + TC_STAGES * TC_KV_BYTES;
-  uint8_t* sP = sV + TC_STAGES * TC_KV_BYTES;           // [TC_NT][2][P]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + TC_NT * 2 * TC_P_BYTES);
-  uint64_t* kv_full = bars;
-  uint64_t* kv_empty = kv_full + TC_STAGES;
-  uint64_t* s_full = kv_empty + TC_STAGES;    // [TC_NT][2]
-  uint64_t* s_empty = s_full + 2 * TC_NT;
-  uint64_t* p_full = s_empty + 2 * TC_NT;
-  uint64_t* p_empty = p_full + 2 * TC_NT;
-  uint64_t* q_full = p_empty + 2 * TC_NT;
+  uint8_t* sK = sQ + TC_NT * TC_Q_BYTES;                // [KS][KV]
+  uint8_t* sV = sK + TC_KS * TC_KV_BYTES;               // [VS][KV]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + TC_VS * TC_KV_BYTES);
+  uint64_t* k_full = bars;
+  uint64_t* k_empty = k_full + TC_KS;
+  uint64_t* v_full = k_empty + TC_KS;
+  uint64_t* v_empty = v_full + TC_VS;
+  uint64_t* s_full = v_empty + TC_VS;   // [TC_NT]
+  uint64_t* p_full = s_full + TC_NT;    // [TC_NT]
+  uint64_t* q_full = p_full + TC_NT;
   uint64_t* o_full = q_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
 
@@ -125,15 +160,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int* pt = page_table + (size_t)b * pt_stride;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < TC_STAGES; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+    for (int i = 0; i < TC_KS; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
     }
-    for (int i = 0; i < 2 * TC_NT; ++i) {
+    for (int i = 0; i < TC_VS; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < TC_NT; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
       mbar_init(&p_full[i], 4);
-      mbar_init(&p_empty[i], 1);
     }
     mbar_init(q_full, 4 * TC_NT);
     mbar_init(o_full, 1);
@@ -145,91 +182,104 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      prefetch_tmap(&tmK);
-      prefetch_tmap(&tmV);
-      const int pages_per_block = TC_BN / ps;
-      bool ok = true;
-      for (int j = 0; j < nb && ok; ++j) {
-        const int st = j % TC_STAGES, n = j / TC_STAGES;
-        if (!mbar_wait(&kv_empty[st], (n & 1) ^ 1, err, kErrSmemEmptyTimeout)) { ok = false; break; }
-        mbar_arrive_expect_tx(&kv_full[st], 2 * TC_KV_BYTES);
-        for (int p = 0; p < pages_per_block; ++p) {
-          const int key0 = j * TC_BN + p * ps;
-          const int ycoord = key0 <= max_pos ? pt[key0 / ps] * Hkv + hk : -1;  // -1: out of range, zero fill
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            uint8_t* dk = sK + st * TC_KV_BYTES + h * TC_KV_HALF + p * ps * 128;
-            uint8_t* dv = sV + st * TC_KV_BYTES + h * TC_KV_HALF + p * ps * 128;
-            tma_load_4d(dk, &tmK, &kv_full[st], 64 * h, 0, ycoord, layer);
-            tma_load_4d(dv, &tmV, &kv_full[st], 64 * h, 0, ycoord, layer);
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(TC_REGS_CTRL));
+    if (warp == 0) {
+      // ------------------------------------------------------------ producer
+      if (lane == 0) {
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmV);
+        const int pages_per_block = TC_BN / ps;
+        bool ok = true;
+        auto load_block = [&](const CUtensorMap* tm, uint8_t* dst, uint64_t* bar, int j) {
+          mbar_arrive_expect_tx(bar, TC_KV_BYTES);
+          for (int p = 0; p < pages_per_block; ++p) {
+            const int key0 = j * TC_BN + p * ps;
+            const int ycoord = key0 <= max_pos ? pt[key0 / ps] * Hkv + hk : -1;  // -1: out of range, zero fill
+  #pragma unroll
+            for (int h = 0; h < 2; ++h) tma_load_4d(dst + h * TC_KV_HALF + p * ps * 128, tm, bar, 64 * h, 0, ycoord, layer);
+          }
+        };
+        for (int j = 0; j < nb && ok; ++j) {
+          const int sk = j % TC_KS, sv = j % TC_VS;
+          if (!mbar_wait(&k_empty[sk], ((j / TC_KS) & 1) ^ 1, err, kErrSmemEmptyTimeout)) { ok = false; break; }
+          load_block(&tmK, sK + sk * TC_KV_BYTES, &k_full[sk], j);
+          if (!mbar_wait(&v_empty[sv], ((j / TC_VS) & 1) ^ 1, err, kErrSmemEmptyTimeout)) { ok = false; break; }
+          load_block(&tmV, sV + sv * TC_KV_BYTES, &v_full[sv], j);
+        }
+        if (!ok) {
+          unsigned long long t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 2000000ull) {
           }
         }
       }
-      if (!ok) {
-        unsigned long long t0 = globaltimer_ns();
-        while (globaltimer_ns() - t0 < 2000000ull) {
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ----------------------------------------------------------------- MMA
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = umma_idesc_bf16_f32(TC_BM, TC_BN);
-      constexpr uint32_t idesc_pv = umma_idesc_bf16_f32(TC_BM, TC_D) | (1u << 16);  // B (V) MN-major
-      bool ok = mbar_wait(q_full, 0, err, kErrTmaFullTimeout);
-      tc_fence_after();
-      // O_t += P(t, i) V_i for both tiles, then release K_i/V_i.
-      auto issue_pv = [&](int i) -> bool {
-        const int pb = i & 1;
-        const int st = i % TC_STAGES;
-        const uint32_t vbase = smem_u32(sV + st * TC_KV_BYTES);
-#pragma unroll
-        for (int t = 0; t < TC_NT; ++t) {
-          if (!mbar_wait(&p_full[2 * t + pb], (i >> 1) & 1, err, kErrTmemFullTimeout)) return false;
-          tc_fence_after();
-          const uint32_t pbase = smem_u32(sP + (2 * t + pb) * TC_P_BYTES);
-#pragma unroll
+    } else if (warp == 1) {
+      // ----------------------------------------------------------------- MMA
+      if (lane == 0) {
+        constexpr uint32_t idesc_s = umma_idesc_bf16_f32(TC_BM, TC_BN);
+        constexpr uint32_t idesc_pv = umma_idesc_bf16_f32(TC_BM, TC_D) | (1u << 16);  // B (V) MN-major
+        bool ok = mbar_wait(q_full, 0, err, kErrTmaFullTimeout);
+        tc_fence_after();
+        // O_t += P_t(i) V_i (P from TMEM columns [128t, 128t + 64)).
+        auto issue_pv = [&](int t, int i) {
+          const uint32_t vbase = smem_u32(sV + (i % TC_VS) * TC_KV_BYTES);
+  #pragma unroll
           for (int k = 0; k < TC_BN / 16; ++k) {
-            const uint64_t ad = umma_desc_sw128_kmajor(pbase + 32 * k);
             const uint64_t bd = umma_desc_sw128_mnmajor(vbase + k * 16 * 128, TC_KV_HALF, 1024);
-            umma_bf16(tmem + 256 * t + 128, ad, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+            umma_bf16_ts(tmem + 256 + 128 * t, tmem + 128 * t + 8 * k, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(&p_empty[2 * t + pb]);
-        }
-        umma_commit(&kv_empty[st]);
-        return true;
-      };
-      for (int j = 0; j < nb && ok; ++j) {
-        const int st = j % TC_STAGES, sb = j & 1;
-        if (!mbar_wait(&kv_full[st], (j / TC_STAGES) & 1, err, kErrTmaFullTimeout)) { ok = false; break; }
-        const uint32_t kbase = smem_u32(sK + st * TC_KV_BYTES);
-#pragma unroll
-        for (int t = 0; t < TC_NT; ++t) {
-          if (!mbar_wait(&s_empty[2 * t + sb], ((j >> 1) & 1) ^ 1, err, kErrTmemEmptyTimeout)) { ok = false; break; }
+        };
+        for (int j = 0; j < nb && ok; ++j) {
+          const int sk = j % TC_KS;
+          if (!mbar_wait(&k_full[sk], (j / TC_KS) & 1, err, kErrTmaFullTimeout)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t qbase = smem_u32(sQ + t * TC_Q_BYTES);
-#pragma unroll
-          for (int k = 0; k < TC_D / 16; ++k) {
-            const uint64_t ad = umma_desc_sw128_kmajor(qbase + (k >> 2) * TC_Q_HALF + (k & 3) * 32);
-            const uint64_t bd = umma_desc_sw128_kmajor(kbase + (k >> 2) * TC_KV_HALF + (k & 3) * 32);
-            umma_bf16(tmem + 256 * t + sb * TC_BN, ad, bd, idesc_s, k > 0 ? 1u : 0u);
+          const uint32_t kbase = smem_u32(sK + sk * TC_KV_BYTES);
+  #pragma unroll
+          for (int t = 0; t < TC_NT; ++t) {
+            if (j > 0) {
+              if (!mbar_wait(&p_full[t], (j - 1) & 1, err, kErrTmemFullTimeout)) { ok = false; break; }
+              if (t == 0 && !mbar_wait(&v_full[(j - 1) % TC_VS], ((j - 1) / TC_VS) & 1, err, kErrTmaFullTimeout)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_pv(t, j - 1);
+              if (t == TC_NT - 1) umma_commit(&v_empty[(j - 1) % TC_VS]);
+            }
+            const uint32_t qbase = smem_u32(sQ + t * TC_Q_BYTES);
+  #pragma unroll
+            for (int k = 0; k < TC_D / 16; ++k) {
+              const uint64_t ad = umma_desc_sw128_kmajor(qbase + (k >> 2) * TC_Q_HALF + (k & 3) * 32);
+              const uint64_t bd = umma_desc_sw128_kmajor(kbase + (k >> 2) * TC_KV_HALF + (k & 3) * 32);
+              umma_bf16(tmem + 128 * t, ad, bd, idesc_s, k > 0 ? 1u : 0u);
+            }
+            umma_commit(&s_full[t]);
           }
-          umma_commit(&s_full[2 * t + sb]);
+          if (!ok) break;
+          umma_commit(&k_empty[sk]);
         }
-        if (!ok) break;
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        if (ok) {
+          const int i = nb - 1;
+          for (int t = 0; t < TC_NT && ok; ++t) {
+            if (!mbar_wait(&p_full[t], i & 1, err, kErrTmemFullTimeout)) { ok = false; break; }
+            if (t == 0 && !mbar_wait(&v_full[i % TC_VS], (i / TC_VS) & 1, err, kErrTmaFullTimeout)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(t, i);
+          }
+          if (ok) umma_commit(&v_empty[i % TC_VS]);
+        }
+        umma_commit(o_full);  // also drains every MMA issued above
+        mbar_wait(o_full, 0, nullptr, 0);
       }
-      if (ok) ok = issue_pv(nb - 1);
-      umma_commit(o_full);  // also drains every MMA issued above
-      mbar_wait(o_full, 0, nullptr, 0);
+      __syncwarp();
     }
-    __syncwarp();
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(TC_REGS_SOFTMAX));
     // ------------------------------------------------------------- softmax
-    const int t = (warp - 2) >> 2;        // tile of this warpgroup
+    const int t = (warp - 4) >> 2;        // tile of this warpgroup
     const int qd = warp & 3;              // TMEM lane quarter of this warp
     const int r = qd * 32 + lane;         // query row of this thread within the tile
     const int pr = row0 + t * TC_BM + r;
@@ -252,80 +302,66 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(q_full);
     }
-    const uint32_t lane_base = tmem + (uint32_t(qd * 32) << 16) + 256 * t;
-    uint64_t* sf = s_full + 2 * t;
-    uint64_t* se = s_empty + 2 * t;
-    uint64_t* pf = p_full + 2 * t;
-    uint64_t* pe = p_empty + 2 * t;
+    const uint32_t lane_base = tmem + (uint32_t(qd * 32) << 16);
+    const uint32_t s_col = lane_base + 128 * t;
+    const uint32_t o_col = lane_base + 256 + 128 * t;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nb; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait(&sf[sb], (j >> 1) & 1, err, kErrTmemFullTimeout)) { ok = false; break; }
+      if (!mbar_wait(&s_full[t], j & 1, err, kErrTmemFullTimeout)) { ok = false; break; }
       tc_fence_after();
-      uint32_t s[64];
-      tmem_ld_32x32b_x32(lane_base + sb * TC_BN, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-      tmem_ld_32x32b_x32(lane_base + sb * TC_BN + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+      uint32_t s[TC_BN];
+#pragma unroll
+      for (int c = 0; c < TC_BN / 32; ++c)
+        tmem_ld_32x32b_x32(s_col + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&s[32 * c]));
       tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&se[sb]);
       const int kbase = j * TC_BN;
+      if (kbase + TC_BN - 1 > pos) {
+#pragma unroll
+        for (int i = 0; i < TC_BN; ++i)
+          if (kbase + i > pos) s[i] = __float_as_uint(-INFINITY);
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        float v = __uint_as_float(s[i]) * scale_log2;
-        if (kbase + i > pos) v = -INFINITY;
-        s[i] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
-      }
-      const float m_new = fmaxf(m_run, mx);
+      for (int i = 0; i < TC_BN; ++i) mx = fmaxf(mx, __uint_as_float(s[i]));
+      const float m_new = fmaxf(m_run, mx * scale_log2);
       const bool grow = m_new > m_run + TC_RESCALE_THRESHOLD;  // false while m_new == -inf
       const float m_use = grow ? m_new : m_run;
       const float o_scale = (grow && m_run != -INFINITY) ? ex2(m_run - m_new) : 1.f;
-      // P buffer sb of this tile is free once PV of block j-2 finished.
-      if (!mbar_wait(&pe[sb], ((j >> 1) & 1) ^ 1, err, kErrTmemEmptyTimeout)) { ok = false; break; }
-      if (j > 0 && __any_sync(0xffffffffu, o_scale != 1.f)) {
-        // O must be stable: PV of block j-1 complete.
-        const int pb = (j - 1) & 1;
-        if (!mbar_wait(&pe[pb], ((j - 1) >> 1) & 1, err, kErrTmemEmptyTimeout)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < TC_D; c += 32) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(lane_base + 128 + c, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * o_scale);
-          tmem_st_32x32b_x32(lane_base + 128 + c, o);
-        }
-        tmem_st_wait();
-      }
-      l_run *= o_scale;
-      m_run = m_use;
-      // P = exp2(s - m) as bf16 into the swizzled K-major tile.
+      const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
+      // P = exp2(S*scale - m) as bf16 pairs over the first 64 columns of S.
       float sum = 0.f;
-      const uint32_t prow = smem_u32(sP + (2 * t + sb) * TC_P_BYTES) + r * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t pk[4];
+      for (int c = 0; c < TC_BN / 32; ++c) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float a = __uint_as_float(s[8 * c + 2 * e]), bb = __uint_as_float(s[8 * c + 2 * e + 1]);
-          const float pa = (m_use == -INFINITY) ? 0.f : ex2(a - m_use);
-          const float pb = (m_use == -INFINITY) ? 0.f : ex2(bb - m_use);
+        for (int e = 0; e < 16; ++e) {
+          const float pa = ex2(fmaf(__uint_as_float(s[32 * c + 2 * e]), scale_log2, neg_m));
+          const float pb = ex2(fmaf(__uint_as_float(s[32 * c + 2 * e + 1]), scale_log2, neg_m));
           sum += pa + pb;
           pk[e] = pack_bf16x2(pa, pb);
         }
-        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(prow + ((c ^ (r & 7)) << 4)), "r"(pk[0]),
-                     "r"(pk[1]), "r"(pk[2]), "r"(pk[3])
-                     : "memory");
+        tmem_st_32x32b_x16(s_col + 16 * c, pk);
       }
-      l_run += sum;
-      fence_proxy_async();
+      // O is stable here: PV of block j-1 was issued before S(j) and the
+      // commit that signalled S(j) covers it.
+      if (__any_sync(0xffffffffu, o_scale != 1.f)) {
+#pragma unroll 1
+        for (int c = 0; c < TC_D; c += 32) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(o_col + c, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * o_scale);
+          tmem_st_32x32b_x32(o_col + c, o);
+        }
+      }
+      tmem_st_wait();
+      l_run = l_run * o_scale + sum;
+      m_run = m_use;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&pf[sb]);
+      if (lane == 0) mbar_arrive(&p_full[t]);
     }
     // ----------------------------------------------------------- epilogue
     if (ok && mbar_wait(o_full, 0, err, kErrTmemFullTimeout)) {
@@ -335,7 +371,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll 1
       for (int c = 0; c < TC_D; c += 32) {
         uint32_t o[32];
-        tmem_ld_32x32b_x32(lane_base + 128 + c, o);
+        tmem_ld_32x32b_x32(o_col + c, o);
         tmem_ld_wait();
         if (valid) {
           uint32_t pk[16];
@@ -403,11 +439,21 @@ extern "C" int ll_attn_prefill_tc(const bf16* q, const bf16* k_pool, const bf16*
   CUtensorMap tk, tv;
   if (make_pool_map(&tk, k_pool, L, pages, Hkv, page_size)) return -2;
   if (make_pool_map(&tv, v_pool, L, pages, Hkv, page_size)) return -2;
-  static bool init = false;
-  if (!init) {
-    cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
-    init = true;
+  // A launch whose registers or shared memory cannot fit one CTA on an SM is
+  // refused here: such launches crashed the host process inside the driver
+  // instead of returning an error.
+  static int fits = -1;
+  if (fits < 0) {
+    int n = 0;
+    fits = cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) ==
+                   cudaSuccess &&
+               cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_prefill_tc_kernel, TC_THREADS, TC_SMEM) ==
+                   cudaSuccess &&
+               n >= 1
+           ? 1
+           : 0;
   }
+  if (!fits) return -7;
   attn_prefill_tc_kernel<<<ntiles, TC_THREADS, TC_SMEM, stream>>>(tk, tv, q, q_indptr, q_pos, page_table, pt_stride,
                                                            reinterpret_cast<const int4*>(tiles), out, Hq, Hkv,
                                                            page_size, layer, scale * 1.4426950408889634f, err);
