@@ -154,6 +154,48 @@ def bench_attention(pk, with_torch):
     return rows
 
 
+def bench_attention_variants(pk, with_torch):
+    """Every exp2 / bf16-pack variant of the tcgen05 attention kernel on the
+    repair case, with its error against the fp32 reference on a small case."""
+    rows = []
+    ext = ops._cuda()
+    nvar = ext.attn_prefill_tc_set_variant(-1)
+    D, ps, Hq, Hkv, n, qrows = 128, 16, 28, 4, 16384, 5087
+    pages = n // ps
+    kp = torch.randn(1, pages, Hkv, ps, D, device="cuda", dtype=torch.bfloat16)
+    vp = torch.randn_like(kp)
+    pt = torch.randperm(pages, device="cuda").to(torch.int32)[None]
+    pos = torch.sort(torch.randperm(n)[:qrows]).values.to(torch.int32)
+    qi = torch.tensor([0, qrows], dtype=torch.int32)
+    tiles = ops.prefill_tiles(qi, pos, Hq, Hkv).cuda()
+    q = torch.randn(qrows, Hq, D, device="cuda", dtype=torch.bfloat16)
+    kvl = torch.tensor([n], dtype=torch.int32, device="cuda")
+    posd, qid = pos.cuda(), qi.cuda()
+    out = torch.empty(qrows, Hq * D, device="cuda", dtype=torch.bfloat16)
+    flops = 4 * D * Hq * float((pos.double() + 1).sum())
+    # small numerics case: 300 rows over 2000 keys
+    sn, sr = 2000, 300
+    skp, svp = kp[:, : sn // ps + 1], vp[:, : sn // ps + 1]
+    spt = torch.arange(sn // ps + 1, device="cuda", dtype=torch.int32)[None]
+    spos = torch.sort(torch.randperm(sn)[:sr]).values.to(torch.int32)
+    sqi = torch.tensor([0, sr], dtype=torch.int32)
+    sq = q[:sr]
+    skvl = torch.tensor([sn], dtype=torch.int32)
+    exp = ref.paged_attention(sq.float().cpu(), skp[0].float().cpu(), svp[0].float().cpu(), sqi, spos, spt.cpu(),
+                              skvl, 1 / math.sqrt(D))
+    for v in range(nvar):
+        ext.attn_prefill_tc_set_variant(v)
+        ms = time_fn(lambda: ops.attention_prefill(q, kp, vp, 0, qid, posd, pt, kvl, 1 / math.sqrt(D), tiles=tiles,
+                                                   out=out))
+        so = ops.attention_prefill(sq, skp, svp, 0, sqi.cuda(), spos.cuda(), spt, skvl.cuda(), 1 / math.sqrt(D))
+        err = float(((so.float().cpu() - exp).norm() / exp.norm()))
+        tf = flops / ms / 1e9
+        rows.append({"op": f"attn_prefill_tcgen05[repair5k,variant{v}]", "ms": round(ms, 4), "tflops": round(tf, 1),
+                     "frac_of_peak": round(tf / pk["bf16_tflops"], 3), "rel_err_vs_fp32": round(err, 5)})
+    ext.attn_prefill_tc_set_variant(-1)
+    return rows
+
+
 def bench_kv_link(pk, with_torch):
     rows = []
     L, Hkv, D, ps = 28, 4, 128, 16
@@ -180,7 +222,8 @@ def main():
     ap.add_argument("--torch", action="store_true")
     a = ap.parse_args()
     pk = peaks()
-    fns = {"gemm": bench_gemm, "small_m": bench_small_m, "attn": bench_attention, "kv_link": bench_kv_link}
+    fns = {"gemm": bench_gemm, "small_m": bench_small_m, "attn": bench_attention, "kv_link": bench_kv_link,
+           "attn_variants": bench_attention_variants}
     for name in a.only.split(","):
         for r in fns[name](pk, a.torch):
             r["peaks"] = pk["src"]

@@ -23,7 +23,7 @@ elif case == "gemm":
     o = torch.empty(M, N // 2, device="cuda", dtype=torch.bfloat16)
     for _ in range(4): ops.linear(a, w, out=o, swiglu_epilogue=True)
 elif case == "attn":
-    D, ps, Hq, Hkv, n, qrows = 128, 16, 28, 4, 8192, 2048
+    D, ps, Hq, Hkv, n, qrows = 128, 16, 28, 4, 8192, 4096
     pages = n // ps
     kp = torch.randn(1, pages, Hkv, ps, D, device="cuda", dtype=torch.bfloat16); vp = torch.randn_like(kp)
     pt = torch.randperm(pages, device="cuda").to(torch.int32)[None]

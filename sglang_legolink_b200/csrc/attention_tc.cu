@@ -30,6 +30,8 @@
 //
 // Barriers: k_full/k_empty, v_full/v_empty per stage; s_full, p_full per
 // tile; q_full, o_full.  Every wait is bounded (common.cuh).
+#include <cstdlib>
+
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -66,6 +68,37 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA pipe, for x <= 16: x = n + f with n = rint(x) (the
+// 1.5 * 2^23 add leaves n in the low mantissa bits of t) and f in
+// [-0.5, 0.5]; 2^f from a degree-3 polynomial whose coefficients are a
+// relative-error Lawson (iteratively reweighted least-squares) fit of 2^f on
+// Chebyshev nodes of [-0.5, 0.5] (max relative error 7.5e-5, below the bf16
+// half-ulp 2^-9 that P is rounded to); 2^n is added to the exponent field.
+// x is clamped at -126 so the exponent never wraps: masked (-inf) scores give
+// a denormal below 1e-38 instead of 0.
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = __fadd_rn(x, 12582912.f);
+  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.f));
+  float p = fmaf(f, 0.05517166f, 0.24261113f);
+  p = fmaf(p, f, 0.69326097f);
+  p = fmaf(p, f, 0.99992806f);
+  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
+}
+
+// Two non-negative finite floats -> bf16x2 (lo in the low half) on the ALU
+// pipe: add half an ulp of bf16 and keep the high halves (round half up; the
+// tie case differs from round-to-nearest-even only on exact ties).
+__device__ __forceinline__ uint32_t pack_bf16x2_alu(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 // Descriptor of an MN-major operand in the 128-byte swizzle: atoms of 8 K-rows
@@ -128,6 +161,21 @@ __device__ __forceinline__ void cp_async16_tc(uint32_t saddr, const void* g, boo
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr), "l"(g), "r"(n) : "memory");
 }
 
+// POLY8 of every 8 scores take exp2 on the FMA pipe (exp2_poly) instead of
+// the MUFU pipe; ALU_PACK rounds P to bf16 on the ALU pipe.  Both move work
+// off the MUFU/XU pipe, which bounds the softmax.
+// TRACE: CTA 0 records clock64() at the handoffs of each block into
+// g_attn_trace (diagnostic build only; read with ll_attn_prefill_tc_trace).
+constexpr int TC_TRACE_EV = 12;
+constexpr int TC_TRACE_BLOCKS = 256;
+__device__ unsigned long long g_attn_trace[TC_TRACE_BLOCKS * TC_TRACE_EV];
+#define TC_TR(j, e)                                                                   \
+  do {                                                                                \
+    if (TRACE && blockIdx.x == 0 && (j) < TC_TRACE_BLOCKS)                            \
+      g_attn_trace[(j) * TC_TRACE_EV + (e)] = clock64();                              \
+  } while (0)
+
+template <int POLY8, bool ALU_PACK, bool TRACE = false>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                            const bf16* __restrict__ q, const int* __restrict__ q_indptr,
@@ -186,33 +234,48 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(TC_REGS_CTRL));
     if (warp == 0) {
       // ------------------------------------------------------------ producer
+      // The whole warp: lane p owns page p of a block (page_size >= 4, so a
+      // block spans at most 32 pages).  Its page-table entry for block j+1 is
+      // loaded while block j streams, and each lane issues its own page's
+      // TMA boxes, so neither the page-table latency nor the TMA issue is
+      // serialised on one thread.
       if (lane == 0) {
         prefetch_tmap(&tmK);
         prefetch_tmap(&tmV);
-        const int pages_per_block = TC_BN / ps;
-        bool ok = true;
-        auto load_block = [&](const CUtensorMap* tm, uint8_t* dst, uint64_t* bar, int j) {
-          mbar_arrive_expect_tx(bar, TC_KV_BYTES);
-          for (int p = 0; p < pages_per_block; ++p) {
-            const int key0 = j * TC_BN + p * ps;
-            const int ycoord = key0 <= max_pos ? pt[key0 / ps] * Hkv + hk : -1;  // -1: out of range, zero fill
-  #pragma unroll
-            for (int h = 0; h < 2; ++h) tma_load_4d(dst + h * TC_KV_HALF + p * ps * 128, tm, bar, 64 * h, 0, ycoord, layer);
-          }
-        };
-        for (int j = 0; j < nb && ok; ++j) {
-          const int sk = j % TC_KS, sv = j % TC_VS;
-          if (!mbar_wait(&k_empty[sk], ((j / TC_KS) & 1) ^ 1, err, kErrSmemEmptyTimeout)) { ok = false; break; }
-          load_block(&tmK, sK + sk * TC_KV_BYTES, &k_full[sk], j);
-          if (!mbar_wait(&v_empty[sv], ((j / TC_VS) & 1) ^ 1, err, kErrSmemEmptyTimeout)) { ok = false; break; }
-          load_block(&tmV, sV + sv * TC_KV_BYTES, &v_full[sv], j);
+      }
+      const int ppb = TC_BN / ps;
+      auto page_of = [&](int j) -> int {
+        const int key0 = j * TC_BN + lane * ps;
+        return (lane < ppb && key0 <= max_pos) ? pt[key0 / ps] * Hkv + hk : -1;  // -1: out of range, zero fill
+      };
+      auto load_block = [&](const CUtensorMap* tm, uint8_t* dst, uint64_t* bar, int y) {
+        if (lane == 0) mbar_arrive_expect_tx(bar, TC_KV_BYTES);
+        __syncwarp();
+        if (lane < ppb) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) tma_load_4d(dst + h * TC_KV_HALF + lane * ps * 128, tm, bar, 64 * h, 0, y, layer);
         }
-        if (!ok) {
-          unsigned long long t0 = globaltimer_ns();
-          while (globaltimer_ns() - t0 < 2000000ull) {
-          }
+      };
+      bool ok = true;
+      int y_next = page_of(0);
+      for (int j = 0; j < nb; ++j) {
+        const int y = y_next;
+        if (j + 1 < nb) y_next = page_of(j + 1);
+        const int sk = j % TC_KS, sv = j % TC_VS;
+        bool w = true;
+        if (lane == 0) w = mbar_wait(&k_empty[sk], ((j / TC_KS) & 1) ^ 1, err, kErrSmemEmptyTimeout);
+        if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
+        load_block(&tmK, sK + sk * TC_KV_BYTES, &k_full[sk], y);
+        if (lane == 0) w = mbar_wait(&v_empty[sv], ((j / TC_VS) & 1) ^ 1, err, kErrSmemEmptyTimeout);
+        if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
+        load_block(&tmV, sV + sv * TC_KV_BYTES, &v_full[sv], y);
+      }
+      if (!ok && lane == 0) {
+        unsigned long long t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 2000000ull) {
         }
       }
+      __syncwarp();
     } else if (warp == 1) {
       // ----------------------------------------------------------------- MMA
       if (lane == 0) {
@@ -223,7 +286,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // O_t += P_t(i) V_i (P from TMEM columns [128t, 128t + 64)).
         auto issue_pv = [&](int t, int i) {
           const uint32_t vbase = smem_u32(sV + (i % TC_VS) * TC_KV_BYTES);
-  #pragma unroll
+#pragma unroll
           for (int k = 0; k < TC_BN / 16; ++k) {
             const uint64_t bd = umma_desc_sw128_mnmajor(vbase + k * 16 * 128, TC_KV_HALF, 1024);
             umma_bf16_ts(tmem + 256 + 128 * t, tmem + 128 * t + 8 * k, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
@@ -231,13 +294,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         };
         for (int j = 0; j < nb && ok; ++j) {
           const int sk = j % TC_KS;
-          if (!mbar_wait(&k_full[sk], (j / TC_KS) & 1, err, kErrTmaFullTimeout)) { ok = false; break; }
-          tc_fence_after();
           const uint32_t kbase = smem_u32(sK + sk * TC_KV_BYTES);
-  #pragma unroll
+#pragma unroll
           for (int t = 0; t < TC_NT; ++t) {
             if (j > 0) {
               if (!mbar_wait(&p_full[t], (j - 1) & 1, err, kErrTmemFullTimeout)) { ok = false; break; }
+              TC_TR(j, 7 + t);
               if (t == 0 && !mbar_wait(&v_full[(j - 1) % TC_VS], ((j - 1) / TC_VS) & 1, err, kErrTmaFullTimeout)) {
                 ok = false;
                 break;
@@ -246,14 +308,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               issue_pv(t, j - 1);
               if (t == TC_NT - 1) umma_commit(&v_empty[(j - 1) % TC_VS]);
             }
+            if (t == 0) {  // K_j is needed only from here: PV of block j-1 did not wait for it
+              if (!mbar_wait(&k_full[sk], (j / TC_KS) & 1, err, kErrTmaFullTimeout)) { ok = false; break; }
+              TC_TR(j, 6);
+              tc_fence_after();
+            }
             const uint32_t qbase = smem_u32(sQ + t * TC_Q_BYTES);
-  #pragma unroll
+#pragma unroll
             for (int k = 0; k < TC_D / 16; ++k) {
               const uint64_t ad = umma_desc_sw128_kmajor(qbase + (k >> 2) * TC_Q_HALF + (k & 3) * 32);
               const uint64_t bd = umma_desc_sw128_kmajor(kbase + (k >> 2) * TC_KV_HALF + (k & 3) * 32);
               umma_bf16(tmem + 128 * t, ad, bd, idesc_s, k > 0 ? 1u : 0u);
             }
             umma_commit(&s_full[t]);
+            TC_TR(j, 9 + t);
           }
           if (!ok) break;
           umma_commit(&k_empty[sk]);
@@ -309,40 +377,51 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     bool ok = true;
     for (int j = 0; j < nb; ++j) {
       if (!mbar_wait(&s_full[t], j & 1, err, kErrTmemFullTimeout)) { ok = false; break; }
+      if (r == 0) TC_TR(j, 3 * t);
       tc_fence_after();
       uint32_t s[TC_BN];
 #pragma unroll
       for (int c = 0; c < TC_BN / 32; ++c)
         tmem_ld_32x32b_x32(s_col + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&s[32 * c]));
       tmem_ld_wait();
+      if (r == 0) TC_TR(j, 3 * t + 1);
       const int kbase = j * TC_BN;
       if (kbase + TC_BN - 1 > pos) {
 #pragma unroll
         for (int i = 0; i < TC_BN; ++i)
           if (kbase + i > pos) s[i] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int i = 0; i < TC_BN; ++i) mx = fmaxf(mx, __uint_as_float(s[i]));
+      for (int i = 0; i < TC_BN; i += 8) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          m4[u] = fmax3(m4[u], __uint_as_float(s[i + 2 * u]), __uint_as_float(s[i + 2 * u + 1]));
+      }
+      const float mx = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
       const float m_new = fmaxf(m_run, mx * scale_log2);
       const bool grow = m_new > m_run + TC_RESCALE_THRESHOLD;  // false while m_new == -inf
       const float m_use = grow ? m_new : m_run;
       const float o_scale = (grow && m_run != -INFINITY) ? ex2(m_run - m_new) : 1.f;
       const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
       // P = exp2(S*scale - m) as bf16 pairs over the first 64 columns of S.
-      float sum = 0.f;
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < TC_BN / 32; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float pa = ex2(fmaf(__uint_as_float(s[32 * c + 2 * e]), scale_log2, neg_m));
-          const float pb = ex2(fmaf(__uint_as_float(s[32 * c + 2 * e + 1]), scale_log2, neg_m));
-          sum += pa + pb;
-          pk[e] = pack_bf16x2(pa, pb);
+          const int i0 = 32 * c + 2 * e;
+          const float xa = fmaf(__uint_as_float(s[i0]), scale_log2, neg_m);
+          const float xb = fmaf(__uint_as_float(s[i0 + 1]), scale_log2, neg_m);
+          const float pa = (i0 & 7) < POLY8 ? exp2_poly(xa) : ex2(xa);
+          const float pb = ((i0 + 1) & 7) < POLY8 ? exp2_poly(xb) : ex2(xb);
+          sum4[e & 3] += pa + pb;
+          pk[e] = ALU_PACK ? pack_bf16x2_alu(pa, pb) : pack_bf16x2(pa, pb);
         }
         tmem_st_32x32b_x16(s_col + 16 * c, pk);
       }
+      const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       // O is stable here: PV of block j-1 was issued before S(j) and the
       // commit that signalled S(j) covers it.
       if (__any_sync(0xffffffffu, o_scale != 1.f)) {
@@ -361,6 +440,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       m_run = m_use;
       tc_fence_before();
       __syncwarp();
+      if (r == 0) TC_TR(j, 3 * t + 2);
       if (lane == 0) mbar_arrive(&p_full[t]);
     }
     // ----------------------------------------------------------- epilogue
@@ -423,6 +503,27 @@ static int make_pool_map(CUtensorMap* tm, const void* base, int L, int pages, in
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
+typedef void (*Kern)(CUtensorMap, CUtensorMap, const bf16*, const int*, const int*, const int*, int, const int4*,
+                     bf16*, int, int, int, int, float, int*);
+// (POLY8, ALU_PACK) variants; LL_ATTN_VARIANT=<index> selects one.
+constexpr int kNumVariants = 7;
+static const Kern kVariants[kNumVariants] = {
+    attn_prefill_tc_kernel<0, false>, attn_prefill_tc_kernel<0, true>, attn_prefill_tc_kernel<2, true>,
+    attn_prefill_tc_kernel<3, true>,  attn_prefill_tc_kernel<4, true>, attn_prefill_tc_kernel<2, false>,
+    attn_prefill_tc_kernel<0, false, true>};
+constexpr int kDefaultVariant = 0;
+
+static int g_attn_variant = -1;
+
+static int attn_tc_variant() {
+  if (g_attn_variant < 0) {
+    const char* e = getenv("LL_ATTN_VARIANT");
+    g_attn_variant = e != nullptr ? atoi(e) : kDefaultVariant;
+    if (g_attn_variant < 0 || g_attn_variant >= kNumVariants) g_attn_variant = kDefaultVariant;
+  }
+  return g_attn_variant;
+}
+
 }  // namespace ll
 
 using namespace ll;
@@ -434,28 +535,43 @@ extern "C" int ll_attn_prefill_tc(const bf16* q, const bf16* k_pool, const bf16*
                                   int page_size, float scale, int* err, cudaStream_t stream) {
   if (ntiles <= 0) return 0;
   if (head_dim != TC_D || Hq % Hkv) return -3;
-  if (page_size <= 0 || page_size > TC_BN || TC_BN % page_size) return -3;
+  if (page_size < 4 || page_size > TC_BN || TC_BN % page_size) return -3;  // one producer lane per page
   if (Hq / Hkv > TC_BM) return -3;
   CUtensorMap tk, tv;
   if (make_pool_map(&tk, k_pool, L, pages, Hkv, page_size)) return -2;
   if (make_pool_map(&tv, v_pool, L, pages, Hkv, page_size)) return -2;
+  const int v = attn_tc_variant();
+  Kern kern = kVariants[v];
   // A launch whose registers or shared memory cannot fit one CTA on an SM is
   // refused here: such launches crashed the host process inside the driver
   // instead of returning an error.
-  static int fits = -1;
-  if (fits < 0) {
+  static int fits[kNumVariants] = {-1, -1, -1, -1, -1, -1, -1};
+  if (fits[v] < 0) {
     int n = 0;
-    fits = cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) ==
-                   cudaSuccess &&
-               cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_prefill_tc_kernel, TC_THREADS, TC_SMEM) ==
-                   cudaSuccess &&
-               n >= 1
-           ? 1
-           : 0;
+    fits[v] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) == cudaSuccess &&
+                      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, TC_THREADS, TC_SMEM) == cudaSuccess &&
+                      n >= 1
+                  ? 1
+                  : 0;
   }
-  if (!fits) return -7;
-  attn_prefill_tc_kernel<<<ntiles, TC_THREADS, TC_SMEM, stream>>>(tk, tv, q, q_indptr, q_pos, page_table, pt_stride,
-                                                           reinterpret_cast<const int4*>(tiles), out, Hq, Hkv,
-                                                           page_size, layer, scale * 1.4426950408889634f, err);
+  if (!fits[v]) return -7;
+  kern<<<ntiles, TC_THREADS, TC_SMEM, stream>>>(tk, tv, q, q_indptr, q_pos, page_table, pt_stride,
+                                                reinterpret_cast<const int4*>(tiles), out, Hq, Hkv, page_size, layer,
+                                                scale * 1.4426950408889634f, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+// Selects the (POLY8, ALU_PACK) variant for later launches; returns the
+// number of variants (a negative or out-of-range index only queries).
+extern "C" int ll_attn_prefill_tc_set_variant(int v) {
+  if (v >= 0 && v < kNumVariants) g_attn_variant = v;
+  return kNumVariants;
+}
+
+// Copies the clock64() trace of the last TRACE-variant launch (blocks x 12
+// events) to host memory; returns the number of values copied.
+extern "C" int ll_attn_prefill_tc_trace(unsigned long long* host, int n) {
+  n = n < TC_TRACE_BLOCKS * TC_TRACE_EV ? n : TC_TRACE_BLOCKS * TC_TRACE_EV;
+  if (cudaMemcpyFromSymbol(host, g_attn_trace, n * sizeof(unsigned long long)) != cudaSuccess) return -1;
+  return n;
 }

@@ -41,6 +41,8 @@ int ll_attn_prefill_tc(const bf16* q, const bf16* k_pool, const bf16* v_pool, in
                        const int* q_indptr, const int* q_pos, const int* page_table, int pt_stride, const int* tiles,
                        int ntiles, bf16* out, int Hq, int Hkv, int head_dim, int page_size, float scale, int* err,
                        cudaStream_t stream);
+int ll_attn_prefill_tc_set_variant(int v);
+int ll_attn_prefill_tc_trace(unsigned long long* host, int n);
 }
 
 namespace {
@@ -236,4 +238,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_prefill", &attn_prefill);
   m.def("attn_decode", &attn_decode);
   m.def("attn_prefill_tc", &attn_prefill_tc);
+  m.def("attn_prefill_tc_set_variant", [](int64_t v) { return ll_attn_prefill_tc_set_variant((int)v); });
+  m.def("attn_prefill_tc_trace", []() {
+    auto t = at::zeros({256 * 12}, at::kLong);
+    const int n = ll_attn_prefill_tc_trace(reinterpret_cast<unsigned long long*>(t.data_ptr<int64_t>()), 256 * 12);
+    TORCH_CHECK(n > 0, "trace copy failed");
+    return t.view({256, 12});
+  });
 }

@@ -47,7 +47,7 @@ class _Counted:
     """Proxy over the kernel module that credits each launch to
     :mod:`sglang_legolink_b200.utils.launch_count`."""
 
-    _KERNELS = {"gemm_small_m_splits": 0}
+    _KERNELS = {"gemm_small_m_splits": 0, "attn_prefill_tc_set_variant": 0, "attn_prefill_tc_trace": 0}
 
     def __init__(self, mod):
         self._mod = mod
