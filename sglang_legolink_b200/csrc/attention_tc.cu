@@ -31,6 +31,7 @@
 // Barriers: k_full/k_empty, v_full/v_empty per stage; s_full, p_full per
 // tile; q_full, o_full.  Every wait is bounded (common.cuh).
 #include <cstdlib>
+#include <type_traits>
 
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -166,7 +167,7 @@ __device__ __forceinline__ void cp_async16_tc(uint32_t saddr, const void* g, boo
 // off the MUFU/XU pipe, which bounds the softmax.
 // TRACE: CTA 0 records clock64() at the handoffs of each block into
 // g_attn_trace (diagnostic build only; read with ll_attn_prefill_tc_trace).
-constexpr int TC_TRACE_EV = 12;
+constexpr int TC_TRACE_EV = 20;
 constexpr int TC_TRACE_BLOCKS = 256;
 __device__ unsigned long long g_attn_trace[TC_TRACE_BLOCKS * TC_TRACE_EV];
 #define TC_TR(j, e)                                                                   \
@@ -374,9 +375,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t s_col = lane_base + 128 * t;
     const uint32_t o_col = lane_base + 256 + 128 * t;
     float m_run = -INFINITY, l_run = 0.f;
-    bool ok = true;
-    for (int j = 0; j < nb; ++j) {
-      if (!mbar_wait(&s_full[t], j & 1, err, kErrTmemFullTimeout)) { ok = false; break; }
+    // Blocks before jd are visible to every row of this tile (positions
+    // ascend, so the tile's first row has its smallest position) and skip
+    // the causal mask; the mask is compiled into a separate copy of the
+    // block step so unmasked blocks carry none of its per-score selects.
+    const int pr0 = row0 + t * TC_BM;
+    const int tile_min_pos = pr0 < nrows ? q_pos[s0 + pr0 / g] : -1;
+    const int jd = min((tile_min_pos + 1) / TC_BN, nb);
+    auto step = [&](int j, auto mask_c) -> bool {
+      constexpr bool MASK = decltype(mask_c)::value;
+      if (!mbar_wait(&s_full[t], j & 1, err, kErrTmemFullTimeout)) return false;
       if (r == 0) TC_TR(j, 3 * t);
       tc_fence_after();
       uint32_t s[TC_BN];
@@ -385,12 +393,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tmem_ld_32x32b_x32(s_col + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&s[32 * c]));
       tmem_ld_wait();
       if (r == 0) TC_TR(j, 3 * t + 1);
-      const int kbase = j * TC_BN;
-      if (kbase + TC_BN - 1 > pos) {
+      if (MASK) {
+        const int lim = pos - j * TC_BN;  // scores with index > lim are masked
 #pragma unroll
         for (int i = 0; i < TC_BN; ++i)
-          if (kbase + i > pos) s[i] = __float_as_uint(-INFINITY);
+          if (i > lim) s[i] = __float_as_uint(-INFINITY);
       }
+      if (r == 0 && t == 0) TC_TR(j, 17);
       float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int i = 0; i < TC_BN; i += 8) {
@@ -399,6 +408,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           m4[u] = fmax3(m4[u], __uint_as_float(s[i + 2 * u]), __uint_as_float(s[i + 2 * u + 1]));
       }
       const float mx = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+      if (r == 0 && t == 0) TC_TR(j, 11);
       const float m_new = fmaxf(m_run, mx * scale_log2);
       const bool grow = m_new > m_run + TC_RESCALE_THRESHOLD;  // false while m_new == -inf
       const float m_use = grow ? m_new : m_run;
@@ -420,6 +430,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           pk[e] = ALU_PACK ? pack_bf16x2_alu(pa, pb) : pack_bf16x2(pa, pb);
         }
         tmem_st_32x32b_x16(s_col + 16 * c, pk);
+        if (r == 0 && t == 0) TC_TR(j, 12 + c);
       }
       const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       // O is stable here: PV of block j-1 was issued before S(j) and the
@@ -436,13 +447,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
       }
       tmem_st_wait();
+      if (r == 0 && t == 0) TC_TR(j, 16);
       l_run = l_run * o_scale + sum;
       m_run = m_use;
       tc_fence_before();
       __syncwarp();
       if (r == 0) TC_TR(j, 3 * t + 2);
       if (lane == 0) mbar_arrive(&p_full[t]);
-    }
+      return true;
+    };
+    bool ok = true;
+    int j = 0;
+    for (; j < jd && ok; ++j) ok = step(j, std::false_type{});
+    for (; j < nb && ok; ++j) ok = step(j, std::true_type{});
     // ----------------------------------------------------------- epilogue
     if (ok && mbar_wait(o_full, 0, err, kErrTmemFullTimeout)) {
       tc_fence_after();

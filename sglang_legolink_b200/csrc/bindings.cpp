@@ -240,9 +240,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_prefill_tc", &attn_prefill_tc);
   m.def("attn_prefill_tc_set_variant", [](int64_t v) { return ll_attn_prefill_tc_set_variant((int)v); });
   m.def("attn_prefill_tc_trace", []() {
-    auto t = at::zeros({256 * 12}, at::kLong);
-    const int n = ll_attn_prefill_tc_trace(reinterpret_cast<unsigned long long*>(t.data_ptr<int64_t>()), 256 * 12);
+    auto t = at::zeros({256 * 20}, at::kLong);
+    const int n = ll_attn_prefill_tc_trace(reinterpret_cast<unsigned long long*>(t.data_ptr<int64_t>()), 256 * 20);
     TORCH_CHECK(n > 0, "trace copy failed");
-    return t.view({256, 12});
+    return t.view({256, 20});
   });
 }
