@@ -28,6 +28,7 @@ CUDA_SOURCES = [
     "attention.cu",
     "attention_tc.cu",
     "gemm_small_m_noalloc.cu",
+    "tp_fused.cu",
 ]
 HOST_SOURCES = ["host_runtime.cpp"]
 

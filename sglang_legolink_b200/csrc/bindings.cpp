@@ -8,6 +8,8 @@
 
 using bf16 = __nv_bfloat16;
 
+#include "tp_fused.h"
+
 extern "C" {
 int ll_gemm_bf16(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc, const bf16* bias, int M, int N,
                  int K, int epilogue, int bn, int* err, cudaStream_t stream);
@@ -78,6 +80,81 @@ void gemm(const at::Tensor& a, const at::Tensor& w, const c10::optional<at::Tens
   check_rc(ll_gemm_bf16(bp(a), a.stride(0), bp(w), w.stride(0), bp(out), out.stride(0), bp_opt(bias), M, N, K,
                         (int)epilogue, (int)bn, err.data_ptr<int>(), cur_stream()),
            "ll_gemm_bf16");
+}
+
+// Tensor-parallel GEMM (2-SM kernel): epilogue 0 plain, 1 SwiGLU, 2 scatter
+// into the owners' slot buffers.  Pointer lists are device addresses.
+void gemm_tp(const at::Tensor& a, const at::Tensor& w, const c10::optional<at::Tensor>& bias,
+             const c10::optional<at::Tensor>& out, int64_t epilogue, int64_t N_out_ld, std::vector<int64_t> slot_ptrs,
+             std::vector<int64_t> cnt_ptrs, int64_t wait_cnt, int64_t wait_target, int64_t rank, int64_t world,
+             int64_t rows_per_rank, const at::Tensor& err) {
+  CHECK_CUDA(a); CHECK_BF16(a); CHECK_BF16(w); CHECK_CONTIG(w);
+  TORCH_CHECK(a.dim() == 2 && w.dim() == 2 && a.stride(1) == 1);
+  const int M = a.size(0), K = a.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K);
+  TORCH_CHECK((int64_t)slot_ptrs.size() <= LL_MAX_TP_RANKS && (int64_t)cnt_ptrs.size() <= LL_MAX_TP_RANKS);
+  LLTpArgs tp{};
+  for (size_t i = 0; i < slot_ptrs.size(); ++i) tp.slot[i] = reinterpret_cast<void*>(slot_ptrs[i]);
+  for (size_t i = 0; i < cnt_ptrs.size(); ++i) tp.cnt[i] = reinterpret_cast<unsigned long long*>(cnt_ptrs[i]);
+  tp.wait_cnt = reinterpret_cast<const unsigned long long*>(wait_cnt);
+  tp.wait_target = (unsigned long long)wait_target;
+  tp.rank = (int)rank;
+  tp.world = (int)world;
+  tp.rows_per_rank = (int)rows_per_rank;
+  void* c = nullptr;
+  int ldc = (int)N_out_ld;
+  if (out.has_value()) {
+    CHECK_BF16(*out);
+    TORCH_CHECK(out->dim() == 2 && out->stride(1) == 1 && out->size(0) == M);
+    TORCH_CHECK(out->size(1) == (epilogue == 1 ? N / 2 : N));
+    c = out->data_ptr();
+    ldc = out->stride(0);
+  }
+  if (bias.has_value()) { CHECK_BF16(*bias); TORCH_CHECK(bias->numel() == N); }
+  c10::cuda::CUDAGuard g(a.device());
+  check_rc(ll_gemm_bf16_tp(a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), c, ldc,
+                           bias.has_value() ? bias->data_ptr() : nullptr, M, N, K, (int)epilogue, &tp,
+                           err.data_ptr<int>(), cur_stream()),
+           "ll_gemm_bf16_tp");
+}
+
+// Owner side of the fused TP boundary: sum slots (optional) + residual ->
+// residual, RMSNorm -> every rank's gather buffer.  Returns the grid (the
+// per-rank increment of every G counter is world x grid).
+int64_t tp_reduce_norm_gather(const c10::optional<at::Tensor>& slots, at::Tensor& residual, const at::Tensor& w,
+                              double eps, int64_t rows, std::vector<int64_t> g_ptrs, std::vector<int64_t> g_cnt_ptrs,
+                              int64_t slot_cnt, int64_t slot_target, int64_t rank, int64_t world,
+                              int64_t rows_per_rank, const at::Tensor& err) {
+  CHECK_CUDA(residual); CHECK_BF16(residual); CHECK_CONTIG(residual); CHECK_BF16(w);
+  TORCH_CHECK((int64_t)g_ptrs.size() == world && (int64_t)g_cnt_ptrs.size() == world && world <= LL_MAX_TP_RANKS);
+  const int H = residual.size(1);
+  TORCH_CHECK(residual.size(0) >= rows && w.numel() == H);
+  if (slots.has_value()) {
+    CHECK_BF16(*slots); CHECK_CONTIG(*slots);
+    TORCH_CHECK(slots->numel() >= world * rows_per_rank * H);
+  }
+  LLTpGather tg{};
+  for (int i = 0; i < world; ++i) {
+    tg.g[i] = reinterpret_cast<void*>(g_ptrs[i]);
+    tg.g_cnt[i] = reinterpret_cast<unsigned long long*>(g_cnt_ptrs[i]);
+  }
+  tg.slot_cnt = reinterpret_cast<const unsigned long long*>(slot_cnt);
+  tg.slot_target = (unsigned long long)slot_target;
+  tg.rank = (int)rank;
+  tg.world = (int)world;
+  tg.rows_per_rank = (int)rows_per_rank;
+  c10::cuda::CUDAGuard g(residual.device());
+  check_rc(ll_tp_reduce_norm_gather(slots.has_value() ? slots->data_ptr() : nullptr, residual.data_ptr(),
+                                    w.data_ptr(), (float)eps, H, (int)rows, &tg, err.data_ptr<int>(), cur_stream()),
+           "ll_tp_reduce_norm_gather");
+  return ll_tp_reduce_norm_gather_grid((int)rows);
+}
+
+void tp_wait(int64_t cnt, int64_t target, const at::Tensor& err) {
+  c10::cuda::CUDAGuard g(err.device());
+  check_rc(ll_tp_wait(reinterpret_cast<const void*>(cnt), (unsigned long long)target, err.data_ptr<int>(),
+                      cur_stream()),
+           "ll_tp_wait");
 }
 
 void gemm_small_m(const at::Tensor& a, const at::Tensor& w, const c10::optional<at::Tensor>& bias, at::Tensor& out,
@@ -238,6 +315,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_prefill", &attn_prefill);
   m.def("attn_decode", &attn_decode);
   m.def("attn_prefill_tc", &attn_prefill_tc);
+  m.def("gemm_tp", &gemm_tp);
+  m.def("tp_reduce_norm_gather", &tp_reduce_norm_gather);
+  m.def("tp_wait", &tp_wait);
   m.def("attn_prefill_tc_set_variant", [](int64_t v) { return ll_attn_prefill_tc_set_variant((int)v); });
   m.def("attn_prefill_tc_trace", []() {
     auto t = at::zeros({256 * 20}, at::kLong);

@@ -210,6 +210,45 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// ------------------------------------------------- cross-GPU signalling
+// Adds `v` to a counter that may live in another GPU's memory, with release
+// semantics at system scope: this thread's earlier writes (and, after a
+// fence + warp/CTA barrier, its peers') are visible before the add.
+__device__ __forceinline__ void red_release_sys_add(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Orders this thread's generic-proxy view of global memory before its later
+// async-proxy (TMA) accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Bounded wait until *p >= target (kWaitLimitNs); records kErrPeerFlagTimeout
+// and returns false when it runs out or another thread already failed.
+__device__ __forceinline__ bool wait_counter_geq(const unsigned long long* p, unsigned long long target, int* err) {
+  if (ld_acquire_sys(p) >= target) return true;
+  const unsigned long long start = globaltimer_ns();
+  uint32_t iter = 0;
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_sys(p) >= target) return true;
+    if ((++iter & 63u) == 0) {
+      if (err != nullptr && *((volatile int*)err) != 0) return false;
+      if (globaltimer_ns() - start > kWaitLimitNs) {
+        record_error(err, kErrPeerFlagTimeout);
+        return false;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- misc
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -30,13 +30,17 @@
 #include <unordered_map>
 
 #include "common.cuh"
+#include "tp_fused.h"
 
 namespace ll {
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
 
-enum Epilogue : int { kEpiPlain = 0, kEpiSwiGLU = 1 };
+enum Epilogue : int { kEpiPlain = 0, kEpiSwiGLU = 1, kEpiScatter = 2 };
+
+// Tensor-parallel hooks of the 2-SM kernel (tp_fused.h, tp_fused.cu).
+using TpArgs = LLTpArgs;
 
 template <int BN>
 struct GemmCfg {
@@ -560,7 +564,7 @@ template <int BN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     gemm_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             bf16* __restrict__ C, const bf16* __restrict__ bias, int M, int N, int K, int ldc,
-                            int* err) {
+                            int* err, const __grid_constant__ TpArgs tp) {
   using Cfg = Gemm2Cfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -612,6 +616,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      if (tp.wait_cnt != nullptr) {
+        ok = wait_counter_geq(tp.wait_cnt, tp.wait_target, err);
+        fence_proxy_async_global();  // peers' generic stores -> this CTA's TMA (async proxy) reads
+      }
       for (int t = pair; t < ntiles && ok; t += npairs) {
         const int mb = t % num_m, nb = t / num_m;
         for (int kb = 0; kb < num_kb; ++kb) {
@@ -685,14 +693,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       const int mb = t % num_m, nb = t / num_m;
       if (!mbar_wait(&tfull[acc], aphase, err, kErrTmemFullTimeout)) break;
       tc_fence_after();
-      const int row = mb * 2 * GEMM_BM + (int)crank * GEMM_BM + q * 32 + lane;
+      const int row0 = mb * 2 * GEMM_BM + (int)crank * GEMM_BM + q * 32;  // this warp's 32-row slice
+      const int row = row0 + lane;
       const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
+      if constexpr (EPI == kEpiScatter) {
+        // rows_per_rank is a multiple of 32, so the slice has one owner.
+        const int d = row0 / tp.rows_per_rank;
+        const int R = tp.rows_per_rank;
+        bf16* dst = row0 < M ? static_cast<bf16*>(tp.slot[d]) + (size_t)tp.rank * R * ldc : nullptr;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tbase + c, r);
-        tmem_ld_wait();
-        epi_store_chunk<EPI>(r, C, bias, row, nb * BN + c, M, N, ldc);
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c, r);
+          tmem_ld_wait();
+          if (dst != nullptr) epi_store_chunk<kEpiPlain>(r, dst, bias, row - d * R, nb * BN + c, R, N, ldc);
+        }
+        if (row0 < M) {
+          __threadfence_system();
+          __syncwarp();
+          if (lane == 0) red_release_sys_add(tp.cnt[d], 1ull);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c, r);
+          tmem_ld_wait();
+          epi_store_chunk<EPI>(r, C, bias, row, nb * BN + c, M, N, ldc);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -800,7 +828,7 @@ extern "C" int ll_gemm_bf16(const bf16* A, int lda, const bf16* W, int ldw, bf16
       set_smem(kern, Gemm2Cfg<256>::SMEM);                                                            \
       init = true;                                                                                    \
     }                                                                                                 \
-    kern<<<2 * pairs, 192, Gemm2Cfg<256>::SMEM, stream>>>(tA, tB, C, bias, M, N, K, ldc, err);        \
+    kern<<<2 * pairs, 192, Gemm2Cfg<256>::SMEM, stream>>>(tA, tB, C, bias, M, N, K, ldc, err, TpArgs{}); \
   } while (0)
     if (epilogue == kEpiSwiGLU) LL_LAUNCH2(kEpiSwiGLU); else LL_LAUNCH2(kEpiPlain);
 #undef LL_LAUNCH2
@@ -831,6 +859,46 @@ extern "C" int ll_gemm_bf16(const bf16* A, int lda, const bf16* W, int ldw, bf16
 }
 
 extern "C" int ll_gemm_small_m_splits(int N, int K);
+
+// Tensor-parallel GEMM on the 2-SM kernel: `tp` carries the optional wait on
+// the all-gathered A and, for epilogue kEpiScatter, the owners' slot buffers
+// and counters.  Requires M > 256; kEpiScatter also needs
+// M == world * rows_per_rank with rows_per_rank a multiple of 32.
+extern "C" int ll_gemm_bf16_tp(const void* A_, int lda, const void* W_, int ldw, void* C_, int ldc, const void* bias_,
+                               int M, int N, int K, int epilogue, const LLTpArgs* tp, int* err, void* stream_) {
+  const bf16* A = static_cast<const bf16*>(A_);
+  const bf16* W = static_cast<const bf16*>(W_);
+  bf16* C = static_cast<bf16*>(C_);
+  const bf16* bias = static_cast<const bf16*>(bias_);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (M <= 2 * GEMM_BM || N <= 0 || K <= 0) return -3;
+  if ((K % 8) || (lda % 8) || (ldw % 8) || (ldc % 8)) return -3;
+  if (epilogue == kEpiSwiGLU && (N % 32)) return -4;
+  if (epilogue == kEpiScatter &&
+      (tp->world < 1 || tp->world > LL_MAX_TP_RANKS || tp->rows_per_rank % 32 || M != tp->world * tp->rows_per_rank))
+    return -4;
+  CUtensorMap tA, tB;
+  if (make_tmap_2d(&tA, A, M, K, lda, GEMM_BM)) return -2;
+  if (make_tmap_2d(&tB, W, N, K, ldw, 128)) return -2;
+  const int ntiles2 = ((M + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * ((N + 255) / 256);
+  const int pairs = ntiles2 < num_sms() / 2 ? ntiles2 : num_sms() / 2;
+  if (Gemm2Cfg<256>::SMEM > max_smem_optin()) return -7;
+#define LL_LAUNCH_TP(EPI_)                                                                            \
+  do {                                                                                                \
+    auto kern = gemm_tcgen05_2sm_kernel<256, EPI_>;                                                   \
+    static bool init = false;                                                                         \
+    if (!init) {                                                                                      \
+      set_smem(kern, Gemm2Cfg<256>::SMEM);                                                            \
+      init = true;                                                                                    \
+    }                                                                                                 \
+    kern<<<2 * pairs, 192, Gemm2Cfg<256>::SMEM, stream>>>(tA, tB, C, bias, M, N, K, ldc, err, *tp);  \
+  } while (0)
+  if (epilogue == kEpiSwiGLU) LL_LAUNCH_TP(kEpiSwiGLU);
+  else if (epilogue == kEpiScatter) LL_LAUNCH_TP(kEpiScatter);
+  else LL_LAUNCH_TP(kEpiPlain);
+#undef LL_LAUNCH_TP
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
 
 // Tile-major weights: W stored as [N/128][K/64][128][64] so that every TMA
 // box of the small-M kernel is one contiguous 16 KB block (row-major W reads

@@ -1,0 +1,174 @@
+// Tensor-parallel layer boundary without a collective library call.
+//
+// Row-parallel GEMMs (o_proj, down_proj) of a TP layer produce partial sums
+// that the reference reduces with an NCCL all-reduce (reference
+// patched_sglang_files/python/sglang/srt/models/qwen2.py:80-86,162-168, the
+// RowParallelLinear path).  Here the sequence is split into `world` row
+// ranges of `rows_per_rank` rows (R, a multiple of 32) and:
+//
+//   1. the 2-SM GEMM's epilogue (kEpiScatter, gemm_tcgen05.cu) stores each
+//      output row straight into its owner's slot buffer over NVLink while
+//      the tensor cores work on the next tile, and bumps the owner's
+//      arrival counter per 32-row slice (reduce-scatter fused into the GEMM);
+//   2. tp_reduce_norm_gather_kernel (this file) runs on every owner: it waits
+//      for all slices, sums the world slots in fp32, adds the residual,
+//      stores the new residual, applies RMSNorm and writes the normalised
+//      row into EVERY rank's gather buffer G over NVLink (the all-gather,
+//      fused into the norm), then bumps every rank's G counter;
+//   3. the next column-parallel GEMM (QKV / gate-up) waits on its G counter
+//      in its producer warp and TMA-loads A from the local G.
+//
+// Counters only grow: the host keeps the cumulative target of each one, so
+// no counter is ever reset between layers.  Every wait is bounded
+// (wait_counter_geq in common.cuh) and reports kErrPeerFlagTimeout.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "tp_fused.h"
+
+namespace ll {
+
+using TpGather = LLTpGather;
+
+// One CTA of 256 threads per row (grid-strided); each thread keeps VPT
+// 16-byte vectors of the row in registers.
+template <int VPT>
+__global__ void __launch_bounds__(256)
+    tp_reduce_norm_gather_kernel(const bf16* __restrict__ slots, bf16* __restrict__ residual,
+                                 const bf16* __restrict__ w, float eps, int H, int rows,
+                                 const __grid_constant__ TpGather tg, int* err) {
+  __shared__ int s_ok;
+  __shared__ float red[8];
+  const int R = tg.rows_per_rank;
+  if (threadIdx.x == 0) s_ok = tg.slot_cnt == nullptr ? 1 : (wait_counter_geq(tg.slot_cnt, tg.slot_target, err) ? 1 : 0);
+  __syncthreads();
+  const int nvec = H / 8;
+  if (s_ok) {
+    for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+      uint4* rr = reinterpret_cast<uint4*>(residual + (size_t)row * H);
+      float v[VPT][8];
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int idx = threadIdx.x + i * 256;
+        if (idx < nvec) {
+          uint4 b = rr[idx];
+          const uint32_t* bu = reinterpret_cast<const uint32_t*>(&b);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = unpack_bf16x2(bu[j]);
+            v[i][2 * j] = f.x;
+            v[i][2 * j + 1] = f.y;
+          }
+          if (slots != nullptr) {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int s = 0; s < tg.world; ++s) {
+              // L2-only loads: the slots were written by other GPUs.
+              const uint4 a = __ldcg(reinterpret_cast<const uint4*>(slots + ((size_t)s * R + row) * H) + idx);
+              const uint32_t* au = reinterpret_cast<const uint32_t*>(&a);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 f = unpack_bf16x2(au[j]);
+                acc[2 * j] += f.x;
+                acc[2 * j + 1] += f.y;
+              }
+            }
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[i][j] += acc[j];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[j] = pack_bf16x2(v[i][2 * j], v[i][2 * j + 1]);
+            rr[idx] = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+        }
+      }
+      ss = warp_sum(ss);
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+      __syncthreads();
+      float tot = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) tot += red[i];
+      __syncthreads();
+      const float rstd = rsqrtf(tot / H + eps);
+      const size_t grow = (size_t)tg.rank * R + row;  // row index in every rank's G
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int idx = threadIdx.x + i * 256;
+        if (idx < nvec) {
+          const uint4 wv = reinterpret_cast<const uint4*>(w)[idx];
+          const uint32_t* wu = reinterpret_cast<const uint32_t*>(&wv);
+          uint32_t o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = unpack_bf16x2(wu[j]);
+            o[j] = pack_bf16x2(v[i][2 * j] * rstd * f.x, v[i][2 * j + 1] * rstd * f.y);
+          }
+          const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
+          for (int d = 0; d < tg.world; ++d) reinterpret_cast<uint4*>(static_cast<bf16*>(tg.g[d]) + grow * H)[idx] = ov;
+        }
+      }
+    }
+  }
+  // Publish: every thread's peer stores, then one release-add per rank.
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < tg.world) red_release_sys_add(tg.g_cnt[threadIdx.x], 1ull);
+}
+
+}  // namespace ll
+
+using namespace ll;
+
+// Grid used by ll_tp_reduce_norm_gather for `rows` rows: the same on every
+// rank (each rank's G counter grows by world x this per call).
+extern "C" int ll_tp_reduce_norm_gather_grid(int rows) {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  const int g = 2 * sms;
+  return rows < g ? rows : g;
+}
+
+// slots: this rank's [world][R][H] slot buffer, or nullptr for a plain
+// norm + all-gather (the first layer).  residual: this rank's [R][H] rows.
+extern "C" int ll_tp_reduce_norm_gather(const void* slots_, void* residual_, const void* w_, float eps, int H,
+                                        int rows, const LLTpGather* tg, int* err, void* stream_) {
+  const bf16* slots = static_cast<const bf16*>(slots_);
+  bf16* residual = static_cast<bf16*>(residual_);
+  const bf16* w = static_cast<const bf16*>(w_);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (H % 8 || H > 8 * 256 * 4 || rows <= 0 || rows > tg->rows_per_rank) return -3;
+  if (tg->world < 1 || tg->world > LL_MAX_TP_RANKS) return -3;
+  const int grid = ll_tp_reduce_norm_gather_grid(rows);
+  const int vpt = (H / 8 + 255) / 256;
+  switch (vpt) {
+    case 1: tp_reduce_norm_gather_kernel<1><<<grid, 256, 0, stream>>>(slots, residual, w, eps, H, rows, *tg, err); break;
+    case 2: tp_reduce_norm_gather_kernel<2><<<grid, 256, 0, stream>>>(slots, residual, w, eps, H, rows, *tg, err); break;
+    case 3: tp_reduce_norm_gather_kernel<3><<<grid, 256, 0, stream>>>(slots, residual, w, eps, H, rows, *tg, err); break;
+    default: tp_reduce_norm_gather_kernel<4><<<grid, 256, 0, stream>>>(slots, residual, w, eps, H, rows, *tg, err); break;
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+namespace ll {
+// One thread waits (bounded) for a gather counter so that later kernels on
+// the stream may read the gathered rows with ordinary loads.
+__global__ void tp_wait_kernel(const unsigned long long* cnt, unsigned long long target, int* err) {
+  if (threadIdx.x == 0) {
+    wait_counter_geq(cnt, target, err);
+    __threadfence();
+  }
+}
+}  // namespace ll
+
+extern "C" int ll_tp_wait(const void* cnt, unsigned long long target, int* err, void* stream) {
+  ll::tp_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const unsigned long long*>(cnt),
+                                                                       target, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}

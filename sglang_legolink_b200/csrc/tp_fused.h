@@ -1,0 +1,40 @@
+// Kernel arguments of the fused tensor-parallel path (gemm_tcgen05.cu,
+// tp_fused.cu), shared with the host bindings.  Plain C layout.
+#pragma once
+
+#define LL_MAX_TP_RANKS 8
+
+// 2-SM GEMM hooks.  wait_cnt != nullptr: the producer waits until
+// *wait_cnt >= wait_target before loading A.  Scatter epilogue: row r goes to
+// rank r / rows_per_rank's slot buffer `slot[d]`, and each 32-row x 256-column
+// slice adds 1 to `cnt[d]`.
+struct LLTpArgs {
+  void* slot[LL_MAX_TP_RANKS];
+  unsigned long long* cnt[LL_MAX_TP_RANKS];
+  const unsigned long long* wait_cnt;
+  unsigned long long wait_target;
+  int rank, world, rows_per_rank;
+};
+
+// Reduce + RMSNorm + all-gather: g[d] / g_cnt[d] are rank d's gather buffer
+// and counter; slot_cnt / slot_target gate the read of this rank's slots.
+struct LLTpGather {
+  void* g[LL_MAX_TP_RANKS];
+  unsigned long long* g_cnt[LL_MAX_TP_RANKS];
+  const unsigned long long* slot_cnt;
+  unsigned long long slot_target;
+  int rank, world, rows_per_rank;
+};
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+int ll_gemm_bf16_tp(const void* A, int lda, const void* W, int ldw, void* C, int ldc, const void* bias, int M, int N,
+                    int K, int epilogue, const struct LLTpArgs* tp, int* err, void* stream);
+int ll_tp_reduce_norm_gather(const void* slots, void* residual, const void* w, float eps, int H, int rows,
+                             const struct LLTpGather* tg, int* err, void* stream);
+int ll_tp_reduce_norm_gather_grid(int rows);
+int ll_tp_wait(const void* cnt, unsigned long long target, int* err, void* stream);
+#ifdef __cplusplus
+}
+#endif

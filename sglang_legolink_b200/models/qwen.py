@@ -218,6 +218,9 @@ class QwenModel:
         ``fb.logit_rows`` (all rows when None)."""
         c = self.cfg
         T = fb.num_rows
+        if (fb.mode == "extend" and getattr(self.comm, "name", "") == "fused" and fb.input_ids.is_cuda
+                and self.comm.use_fused(T)):
+            return self._forward_fused_tp(fb, kv, return_hidden)
         H, D = c.hidden_size, c.head_dim
         qkv_n = (self.hq + 2 * self.hkv) * D
         x = ops.embedding(fb.input_ids, self.embed, out=self._buf("x", (T, H)))
@@ -252,6 +255,55 @@ class QwenModel:
         # final: residual += h ; h = norm(residual)
         ops.fused_add_rmsnorm(h, residual, self.final_norm, c.rms_norm_eps)
         rows = h if fb.logit_rows is None else h.index_select(0, fb.logit_rows)
+        if return_hidden:
+            return rows
+        return self.logits(rows)
+
+    def _forward_fused_tp(self, fb: ForwardBatch, kv, return_hidden: bool = False) -> torch.Tensor:
+        """Extend forward with the TP reductions fused into the kernels
+        (:class:`~sglang_legolink_b200.parallel.tp_fused.FusedTPComm`): this
+        rank keeps the residual of its R rows only; every layer boundary is
+        GEMM-with-scatter -> reduce+norm+all-gather -> GEMM-from-gather."""
+        c, comm = self.cfg, self.comm
+        T = fb.num_rows
+        H, D = c.hidden_size, c.head_dim
+        W, rank = comm.size, comm.rank
+        R = comm.rows_per_rank(T)
+        Tp = W * R
+        qkv_n = (self.hq + 2 * self.hkv) * D
+        r0 = rank * R
+        nv = max(0, min(R, T - r0))
+        ids = self._buf("tp_ids", (R,), torch.int32)
+        ids.zero_()
+        if nv:
+            ids[:nv].copy_(fb.input_ids[r0 : r0 + nv])
+        res = ops.embedding(ids, self.embed, out=self._buf("tp_res", (R, H)))
+        comm.reduce_norm_gather(res, self.layers[0].in_norm, c.rms_norm_eps, T, with_slots=False)
+        q = self._buf("q", (T, self.hq, D))
+        attn = self._buf("tp_attn", (Tp, self.hq * D))
+        if Tp > T:
+            attn[T:].zero_()
+        qkv = self._buf("tp_qkv", (Tp, qkv_n))
+        mlp = self._buf("tp_mlp", (Tp, self.inter))
+        tiles = fb.tiles
+        if tiles is None:
+            tiles = ops.prefill_tiles(fb.q_indptr.cpu(), fb.positions.cpu(), self.hq, self.hkv).to(self.device)
+        nl = len(self.layers)
+        for li, lw in enumerate(self.layers):
+            comm.gemm_from_gather(lw.qkv_w, lw.qkv_b, qkv, T)
+            ops.rope_qkv_write(qkv[:T], fb.positions, fb.slots, self.cos_sin, q, kv.k[li], kv.v[li], self.hq,
+                               self.hkv, D, lw.q_norm, lw.k_norm, c.rms_norm_eps)
+            ops.attention_prefill(q, kv.k, kv.v, li, fb.q_indptr, fb.positions, fb.page_table, fb.kv_lens,
+                                  self.scale, tiles=tiles, out=attn[:T])
+            comm.gemm_scatter(attn, lw.o_w, T)
+            comm.reduce_norm_gather(res, lw.post_norm, c.rms_norm_eps, T)
+            comm.gemm_from_gather(lw.gu_w, None, mlp, T, swiglu=True)
+            comm.gemm_scatter(mlp, lw.down_w, T)
+            nxt = self.layers[li + 1].in_norm if li + 1 < nl else self.final_norm
+            comm.reduce_norm_gather(res, nxt, c.rms_norm_eps, T)
+        comm.wait_gather(self.device)
+        g = comm.gather_view(T)[:T]
+        rows = g if fb.logit_rows is None else g.index_select(0, fb.logit_rows)
         if return_hidden:
             return rows
         return self.logits(rows)

@@ -1,0 +1,129 @@
+"""Tensor parallelism with the reduction fused into the kernels (no collective
+library call on the prefill / Link path).
+
+The reference reduces the row-parallel o_proj / down_proj outputs with an
+NCCL all-reduce after each GEMM (reference
+``patched_sglang_files/python/sglang/srt/models/qwen2.py:80-86,162-168``).
+:class:`FusedTPComm` instead splits the T rows of a forward into ``world``
+ranges of ``R`` rows (R a multiple of 32) and drives three kernels per layer
+boundary (``csrc/tp_fused.cu``, ``csrc/gemm_tcgen05.cu``):
+
+* :meth:`gemm_scatter` -- the row-parallel GEMM whose epilogue stores every
+  output row over NVLink into its owner rank's slot buffer (one slot per
+  source rank) and bumps the owner's arrival counter (reduce-scatter fused
+  into the GEMM, overlapping the next tiles' MMAs);
+* :meth:`reduce_norm_gather` -- on each owner: wait for the slices, sum the
+  slots + residual, RMSNorm, and write the normalised rows into every rank's
+  gather buffer ``G`` over NVLink (the all-gather fused into the norm);
+* :meth:`gemm_from_gather` -- the next column-parallel GEMM, whose TMA
+  producer waits for the gather counter and reads ``G`` from local memory.
+
+The buffers live in symmetric memory (``torch.distributed._symmetric_memory``)
+so every rank holds the others' base addresses.  The counters only grow;
+this object keeps each counter's cumulative target, so every rank must run
+the same sequence of fused calls (as it does the same forward).
+
+Decode (a few rows) and short prefills keep the NCCL path inherited from
+:class:`~.tp.NcclTPComm`.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from .tp import NcclTPComm
+
+# below this many (padded) rows a forward takes the NCCL path
+MIN_FUSED_ROWS = 512
+
+
+def _round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+class FusedTPComm(NcclTPComm):
+    name = "fused"
+
+    def __init__(self, hidden: int, max_rows: int, device, group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        super().__init__(group)
+        W = self.size
+        self.hidden = hidden
+        self.r_max = _round_up(math.ceil(max_rows / W), 32)
+        n = W * self.r_max * hidden
+        group = group or dist.group.WORLD
+        gname = group.group_name
+        self.slots = symm_mem.empty((n,), dtype=torch.bfloat16, device=device)
+        self.gbuf = symm_mem.empty((n,), dtype=torch.bfloat16, device=device)
+        self.cnt = symm_mem.empty((2,), dtype=torch.int64, device=device)
+        self.gbuf.zero_()
+        self.cnt.zero_()
+        self._hs = symm_mem.rendezvous(self.slots, gname)
+        self._hg = symm_mem.rendezvous(self.gbuf, gname)
+        self._hc = symm_mem.rendezvous(self.cnt, gname)
+        self.slot_ptrs = [int(p) for p in self._hs.buffer_ptrs]
+        self.g_ptrs = [int(p) for p in self._hg.buffer_ptrs]
+        self.slot_cnt_ptrs = [int(p) for p in self._hc.buffer_ptrs]
+        self.g_cnt_ptrs = [p + 8 for p in self.slot_cnt_ptrs]
+        self.slot_target = 0
+        self.g_target = 0
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)  # every counter is zero before any peer adds to it
+        self.stats = {"fused_gemms": 0, "fused_reduces": 0}
+
+    # ------------------------------------------------------------ geometry
+    def rows_per_rank(self, T: int) -> int:
+        return _round_up(math.ceil(T / self.size), 32)
+
+    def use_fused(self, T: int) -> bool:
+        R = self.rows_per_rank(T)
+        return R <= self.r_max and self.size * R >= MIN_FUSED_ROWS
+
+    def gather_view(self, T: int) -> torch.Tensor:
+        R = self.rows_per_rank(T)
+        return self.gbuf[: self.size * R * self.hidden].view(self.size * R, self.hidden)
+
+    def slot_view(self, T: int) -> torch.Tensor:
+        R = self.rows_per_rank(T)
+        return self.slots[: self.size * R * self.hidden].view(self.size, R, self.hidden)
+
+    # ------------------------------------------------------------- kernels
+    def reduce_norm_gather(self, residual: torch.Tensor, w: torch.Tensor, eps: float, T: int,
+                           with_slots: bool = True) -> None:
+        """residual [R, H] (this rank's rows) += sum of slots (when
+        ``with_slots``); G[rank*R:(rank+1)*R] on every rank = RMSNorm(residual)."""
+        R = self.rows_per_rank(T)
+        err = ops.workspace(residual.device).err
+        grid = ops._cuda().tp_reduce_norm_gather(
+            self.slot_view(T) if with_slots else None, residual, w, float(eps), R, self.g_ptrs, self.g_cnt_ptrs,
+            self.slot_cnt_ptrs[self.rank] if with_slots else 0, self.slot_target, self.rank, self.size, R, err)
+        self.g_target += self.size * int(grid)
+        self.stats["fused_reduces"] += 1
+
+    def gemm_from_gather(self, w: torch.Tensor, bias, out: torch.Tensor, T: int, swiglu: bool = False) -> None:
+        """out[Tp, N] = G @ w^T (+ bias), after this rank's G is complete."""
+        R = self.rows_per_rank(T)
+        g = self.gather_view(T)
+        ops._cuda().gemm_tp(g, w, bias, out, 1 if swiglu else 0, 0, [], [], self.g_cnt_ptrs[self.rank],
+                            self.g_target, self.rank, self.size, R, ops.workspace(g.device).err)
+        self.stats["fused_gemms"] += 1
+
+    def gemm_scatter(self, a: torch.Tensor, w: torch.Tensor, T: int) -> None:
+        """Partial a @ w^T of all Tp rows, each row stored into its owner's
+        slot for this rank (reduce-scatter inside the GEMM epilogue)."""
+        R = self.rows_per_rank(T)
+        N = w.shape[0]
+        ops._cuda().gemm_tp(a, w, None, None, 2, N, self.slot_ptrs, self.slot_cnt_ptrs, 0, 0, self.rank,
+                            self.size, R, ops.workspace(a.device).err)
+        self.slot_target += self.size * (R // 32) * ((N + 255) // 256)
+        self.stats["fused_gemms"] += 1
+
+    def wait_gather(self, device) -> None:
+        """Makes the current stream wait until this rank's G is complete
+        (before torch ops read it)."""
+        ops._cuda().tp_wait(self.g_cnt_ptrs[self.rank], self.g_target, ops.workspace(device).err)

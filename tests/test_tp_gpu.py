@@ -19,3 +19,17 @@ def test_tp2_gpu():
     r = subprocess.run(cmd, capture_output=True, text=True, env={**os.environ, "NCCL_NVLS_ENABLE": "0"})
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "TP_OK" in r.stdout
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_tp2_fused_gpu():
+    """Fused TP path (reduce-scatter in the GEMM epilogue, all-gather in the
+    norm kernel, over NVLink peer stores) matches the NCCL path."""
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29538",
+           os.path.join(ROOT, "tests", "tp_fused_worker.py")]
+    env = {**os.environ, "NCCL_NVLS_ENABLE": "0", "TORCH_SYMM_MEM_DISABLE_MULTICAST": "1"}
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "TP_FUSED_OK" in r.stdout
