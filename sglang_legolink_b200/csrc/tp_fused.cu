@@ -30,15 +30,16 @@ namespace ll {
 
 using TpGather = LLTpGather;
 
-// One CTA of 256 threads per row (grid-strided); each thread keeps VPT
-// 16-byte vectors of the row in registers.
+// One CTA of TPB = 128 threads per row (grid-strided, several CTAs per SM
+// in flight); each thread keeps VPT 16-byte vectors of the row in registers.
+constexpr int TPB = 128;
 template <int VPT>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(TPB)
     tp_reduce_norm_gather_kernel(const bf16* __restrict__ slots, bf16* __restrict__ residual,
                                  const bf16* __restrict__ w, float eps, int H, int rows,
                                  const __grid_constant__ TpGather tg, int* err) {
   __shared__ int s_ok;
-  __shared__ float red[8];
+  __shared__ float red[TPB / 32];
   const int R = tg.rows_per_rank;
   if (threadIdx.x == 0) s_ok = tg.slot_cnt == nullptr ? 1 : (wait_counter_geq(tg.slot_cnt, tg.slot_target, err) ? 1 : 0);
   __syncthreads();
@@ -47,55 +48,70 @@ __global__ void __launch_bounds__(256)
     for (int row = blockIdx.x; row < rows; row += gridDim.x) {
       uint4* rr = reinterpret_cast<uint4*>(residual + (size_t)row * H);
       float v[VPT][8];
-      float ss = 0.f;
+      // residual, then each source rank's slot (all VPT loads of one slot are
+      // independent and issue back to back)
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
-        const int idx = threadIdx.x + i * 256;
-        if (idx < nvec) {
-          uint4 b = rr[idx];
-          const uint32_t* bu = reinterpret_cast<const uint32_t*>(&b);
+        const int idx = threadIdx.x + i * TPB;
+        uint4 b = idx < nvec ? rr[idx] : make_uint4(0, 0, 0, 0);
+        const uint32_t* bu = reinterpret_cast<const uint32_t*>(&b);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 f = unpack_bf16x2(bu[j]);
-            v[i][2 * j] = f.x;
-            v[i][2 * j + 1] = f.y;
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16x2(bu[j]);
+          v[i][2 * j] = f.x;
+          v[i][2 * j + 1] = f.y;
+        }
+      }
+      if (slots != nullptr) {
+#pragma unroll 2
+        for (int s = 0; s < tg.world; ++s) {
+          const uint4* sr = reinterpret_cast<const uint4*>(slots + ((size_t)s * R + row) * H);
+          uint4 a[VPT];
+#pragma unroll
+          for (int i = 0; i < VPT; ++i) {
+            const int idx = threadIdx.x + i * TPB;
+            // L2-only loads: the slots were written by other GPUs.
+            a[i] = idx < nvec ? __ldcg(sr + idx) : make_uint4(0, 0, 0, 0);
           }
-          if (slots != nullptr) {
-            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            for (int s = 0; s < tg.world; ++s) {
-              // L2-only loads: the slots were written by other GPUs.
-              const uint4 a = __ldcg(reinterpret_cast<const uint4*>(slots + ((size_t)s * R + row) * H) + idx);
-              const uint32_t* au = reinterpret_cast<const uint32_t*>(&a);
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float2 f = unpack_bf16x2(au[j]);
-                acc[2 * j] += f.x;
-                acc[2 * j + 1] += f.y;
-              }
+          for (int i = 0; i < VPT; ++i) {
+            const uint32_t* au = reinterpret_cast<const uint32_t*>(&a[i]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = unpack_bf16x2(au[j]);
+              v[i][2 * j] += f.x;
+              v[i][2 * j + 1] += f.y;
             }
-            uint32_t o[4];
+          }
+        }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[i][j] += acc[j];
+        for (int i = 0; i < VPT; ++i) {
+          const int idx = threadIdx.x + i * TPB;
+          if (idx < nvec) {
+            uint32_t o[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) o[j] = pack_bf16x2(v[i][2 * j], v[i][2 * j + 1]);
             rr[idx] = make_uint4(o[0], o[1], o[2], o[3]);
           }
-#pragma unroll
-          for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
         }
       }
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
       ss = warp_sum(ss);
       if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
       __syncthreads();
       float tot = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) tot += red[i];
+      for (int i = 0; i < TPB / 32; ++i) tot += red[i];
       __syncthreads();
       const float rstd = rsqrtf(tot / H + eps);
       const size_t grow = (size_t)tg.rank * R + row;  // row index in every rank's G
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
-        const int idx = threadIdx.x + i * 256;
+        const int idx = threadIdx.x + i * TPB;
         if (idx < nvec) {
           const uint4 wv = reinterpret_cast<const uint4*>(w)[idx];
           const uint32_t* wu = reinterpret_cast<const uint32_t*>(&wv);
@@ -131,7 +147,7 @@ extern "C" int ll_tp_reduce_norm_gather_grid(int rows) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (sms <= 0) sms = 148;
   }
-  const int g = 2 * sms;
+  const int g = 8 * sms;
   return rows < g ? rows : g;
 }
 
@@ -143,16 +159,21 @@ extern "C" int ll_tp_reduce_norm_gather(const void* slots_, void* residual_, con
   bf16* residual = static_cast<bf16*>(residual_);
   const bf16* w = static_cast<const bf16*>(w_);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  if (H % 8 || H > 8 * 256 * 4 || rows <= 0 || rows > tg->rows_per_rank) return -3;
+  if (H % 8 || H > 8 * TPB * 8 || rows <= 0 || rows > tg->rows_per_rank) return -3;
   if (tg->world < 1 || tg->world > LL_MAX_TP_RANKS) return -3;
   const int grid = ll_tp_reduce_norm_gather_grid(rows);
-  const int vpt = (H / 8 + 255) / 256;
+  const int vpt = (H / 8 + TPB - 1) / TPB;
+#define LL_RNG(V) tp_reduce_norm_gather_kernel<V><<<grid, TPB, 0, stream>>>(slots, residual, w, eps, H, rows, *tg, err)
   switch (vpt) {
-    case 1: tp_reduce_norm_gather_kernel<1><<<grid, 256, 0, stream>>>(slots, residual, w, eps, H, rows, *tg, err); break;
-    case 2: tp_reduce_norm_gather_kernel<2><<<grid, 256, 0, stream>>>(slots, residual, w, eps, H, rows, *tg, err); break;
-    case 3: tp_reduce_norm_gather_kernel<3><<<grid, 256, 0, stream>>>(slots, residual, w, eps, H, rows, *tg, err); break;
-    default: tp_reduce_norm_gather_kernel<4><<<grid, 256, 0, stream>>>(slots, residual, w, eps, H, rows, *tg, err); break;
+    case 1: LL_RNG(1); break;
+    case 2: LL_RNG(2); break;
+    case 3: LL_RNG(3); break;
+    case 4: LL_RNG(4); break;
+    case 5: LL_RNG(5); break;
+    case 6: LL_RNG(6); break;
+    default: LL_RNG(8); break;
   }
+#undef LL_RNG
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
