@@ -689,6 +689,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     const uint32_t leader_tempty1 = mapa_shared(smem_u32(&tempty[1]), 0);
     int acc = 0;
     uint32_t aphase = 0;
+    // kEpiScatter: slices stored per owner rank, published once at the end
+    // (one system fence per warp instead of one per tile).
+    uint32_t sent[LL_MAX_TP_RANKS] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int t = pair; t < ntiles; t += npairs) {
       const int mb = t % num_m, nb = t / num_m;
       if (!mbar_wait(&tfull[acc], aphase, err, kErrTmemFullTimeout)) break;
@@ -700,18 +703,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         // rows_per_rank is a multiple of 32, so the slice has one owner.
         const int d = row0 / tp.rows_per_rank;
         const int R = tp.rows_per_rank;
-        bf16* dst = row0 < M ? static_cast<bf16*>(tp.slot[d]) + (size_t)tp.rank * R * ldc : nullptr;
+        // This warp's 32 rows in the owner's slot for this rank.
+        bf16* dst = row0 < M ? static_cast<bf16*>(tp.slot[d]) + ((size_t)tp.rank * R + (row0 - d * R)) * ldc
+                             : nullptr;
+        const int q = lane & 3, grp = lane >> 2;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tbase + c, r);
           tmem_ld_wait();
-          if (dst != nullptr) epi_store_chunk<kEpiPlain>(r, dst, bias, row - d * R, nb * BN + c, R, N, ldc);
+          const int col0 = nb * BN + c;
+          if (dst == nullptr || col0 >= N) continue;  // warp-uniform
+          uint32_t p[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) p[i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+          // Remote stores are issued row-contiguous: in store k the four
+          // lanes of group g write the 4 x 16 B of row 4g + k (held by lane
+          // 4g + k), so each NVLink write carries 64 contiguous bytes instead
+          // of 16 bytes of 32 different rows.
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int src = 4 * grp + k;
+            uint32_t v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t w0 = __shfl_sync(0xffffffffu, p[j], src);
+              const uint32_t w1 = __shfl_sync(0xffffffffu, p[4 + j], src);
+              const uint32_t w2 = __shfl_sync(0xffffffffu, p[8 + j], src);
+              const uint32_t w3 = __shfl_sync(0xffffffffu, p[12 + j], src);
+              v[j] = q == 0 ? w0 : q == 1 ? w1 : q == 2 ? w2 : w3;
+            }
+            *reinterpret_cast<uint4*>(dst + (size_t)src * ldc + col0 + 8 * q) = make_uint4(v[0], v[1], v[2], v[3]);
+          }
         }
         if (row0 < M) {
-          __threadfence_system();
-          __syncwarp();
-          if (lane == 0) red_release_sys_add(tp.cnt[d], 1ull);
+#pragma unroll
+          for (int i = 0; i < LL_MAX_TP_RANKS; ++i) sent[i] += (i == d) ? 1u : 0u;
         }
       } else {
 #pragma unroll 1
@@ -728,6 +755,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       if (++acc == 2) {
         acc = 0;
         aphase ^= 1;
+      }
+    }
+    if constexpr (EPI == kEpiScatter) {
+      __threadfence_system();  // this lane's peer stores are visible system-wide
+      __syncwarp();
+      if (lane == 0) {
+#pragma unroll
+        for (int i = 0; i < LL_MAX_TP_RANKS; ++i)
+          if (i < tp.world && sent[i] != 0) red_release_sys_add(tp.cnt[i], (unsigned long long)sent[i]);
       }
     }
   }
@@ -875,7 +911,8 @@ extern "C" int ll_gemm_bf16_tp(const void* A_, int lda, const void* W_, int ldw,
   if ((K % 8) || (lda % 8) || (ldw % 8) || (ldc % 8)) return -3;
   if (epilogue == kEpiSwiGLU && (N % 32)) return -4;
   if (epilogue == kEpiScatter &&
-      (tp->world < 1 || tp->world > LL_MAX_TP_RANKS || tp->rows_per_rank % 32 || M != tp->world * tp->rows_per_rank))
+      (tp->world < 1 || tp->world > LL_MAX_TP_RANKS || tp->rows_per_rank % 32 || M != tp->world * tp->rows_per_rank ||
+       N % 32 || bias_ != nullptr))
     return -4;
   CUtensorMap tA, tB;
   if (make_tmap_2d(&tA, A, M, K, lda, GEMM_BM)) return -2;

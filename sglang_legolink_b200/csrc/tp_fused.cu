@@ -9,7 +9,8 @@
 //   1. the 2-SM GEMM's epilogue (kEpiScatter, gemm_tcgen05.cu) stores each
 //      output row straight into its owner's slot buffer over NVLink while
 //      the tensor cores work on the next tile, and bumps the owner's
-//      arrival counter per 32-row slice (reduce-scatter fused into the GEMM);
+//      arrival counter by the 32-row slices it stored, once at the end of the
+//      GEMM (reduce-scatter fused into the GEMM);
 //   2. tp_reduce_norm_gather_kernel (this file) runs on every owner: it waits
 //      for all slices, sums the world slots in fp32, adds the residual,
 //      stores the new residual, applies RMSNorm and writes the normalised
