@@ -1,0 +1,111 @@
+"""Per-op device time of one decode step (batch 1, Qwen2.5-7B, 16K context)
+measured the way the step runs: each op is captured into a CUDA graph as 28
+launches (one per layer, on that layer's own weights / KV, so every launch
+streams from HBM like the real step), replayed, and timed with CUDA events.
+
+    python -m sglang_legolink_b200.benchmarks.decode_breakdown [--context 16640]
+
+Prints one JSON line per op: microseconds per layer and the fraction of the
+measured HBM bandwidth its bytes would take.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+from .. import ops
+from ..models.config import PRESETS
+from ..models.qwen import QwenModel
+from .kernels import peaks
+
+
+def graph_time(fn, reps=10) -> float:
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="qwen2.5-7b")
+    ap.add_argument("--context", type=int, default=16640)
+    a = ap.parse_args()
+    cfg = PRESETS[a.model]
+    dev = torch.device("cuda")
+    m = QwenModel.random_init(cfg, seed=0, device=dev, dtype=torch.bfloat16)
+    L, H, D = cfg.num_layers, cfg.hidden_size, cfg.head_dim
+    hq, hkv, inter = m.hq, m.hkv, m.inter
+    n, ps = a.context, 16
+    pages = (n + ps - 1) // ps
+    kpool = torch.randn(L, pages, hkv, ps, D, device=dev, dtype=torch.bfloat16)
+    vpool = torch.randn_like(kpool)
+    pt = torch.arange(pages, device=dev, dtype=torch.int32)[None]
+    kvl = torch.tensor([n], device=dev, dtype=torch.int32)
+    pos = torch.tensor([n - 1], device=dev, dtype=torch.int32)
+    slot = torch.tensor([n - 1], device=dev, dtype=torch.int64)
+    x = torch.randn(1, H, device=dev, dtype=torch.bfloat16)
+    res = torch.randn(1, H, device=dev, dtype=torch.bfloat16)
+    qkv = torch.empty(1, (hq + 2 * hkv) * D, device=dev, dtype=torch.bfloat16)
+    q = torch.randn(1, hq, D, device=dev, dtype=torch.bfloat16)
+    attn = torch.empty(1, hq * D, device=dev, dtype=torch.bfloat16)
+    o = torch.empty(1, H, device=dev, dtype=torch.bfloat16)
+    gu = torch.empty(1, 2 * inter, device=dev, dtype=torch.bfloat16)
+    mlp = torch.randn(1, inter, device=dev, dtype=torch.bfloat16)
+    nsplit = ops.decode_splits(1, hkv, n)
+    ops.workspace(dev).reserve_decode(hq, nsplit, D)
+    for lw in m.layers[:1]:  # reserve GEMM workspaces outside capture
+        ops.linear(x, lw.gu_w, out=gu)
+    scale = 1.0 / math.sqrt(D)
+    pk = peaks()
+    kvb = n * hkv * D * 2 * 2
+    cases = {
+        "rmsnorm_add": (lambda: [ops.fused_add_rmsnorm(x, res, lw.in_norm, cfg.rms_norm_eps) for lw in m.layers],
+                        4 * H * 2),
+        "gemv_qkv": (lambda: [ops.linear(x, lw.qkv_w, lw.qkv_b, out=qkv) for lw in m.layers],
+                     m.layers[0].qkv_w.numel() * 2),
+        "rope_qkv_write": (lambda: [ops.rope_qkv_write(qkv, pos, slot, m.cos_sin, q, kpool[i], vpool[i], hq, hkv, D)
+                                    for i in range(L)], qkv.numel() * 4),
+        "attn_decode": (lambda: [ops.attention_decode(q, kpool[i], vpool[i], pt, kvl, scale, nsplit=nsplit, out=attn)
+                                 for i in range(L)], kvb),
+        "gemv_o_proj": (lambda: [ops.linear(attn, lw.o_w, out=o) for lw in m.layers], m.layers[0].o_w.numel() * 2),
+        "gemv_gate_up": (lambda: [ops.linear(x, lw.gu_w, out=gu) for lw in m.layers], m.layers[0].gu_w.numel() * 2),
+        "swiglu": (lambda: [ops.swiglu(gu, out=mlp) for _ in range(L)], gu.numel() * 3),
+        "gemv_down": (lambda: [ops.linear(mlp, lw.down_w, out=o) for lw in m.layers], m.layers[0].down_w.numel() * 2),
+    }
+    total = 0.0
+    for name, (fn, bytes_per_layer) in cases.items():
+        ms = graph_time(fn)
+        us = ms * 1e3 / L
+        total += us
+        roof_us = bytes_per_layer / (pk["hbm_gbs"] * 1e3)
+        print(json.dumps({"op": name, "us_per_layer": round(us, 2), "us_per_token": round(us * L, 1),
+                          "roofline_us_per_layer": round(roof_us, 2), "frac_of_hbm": round(roof_us / us, 3),
+                          "peaks": pk["src"]}), flush=True)
+    print(json.dumps({"op": "sum_of_layer_ops", "ms_per_token": round(total * L / 1e3, 3)}), flush=True)
+    lm = graph_time(lambda: ops.linear(x, m.lm_head))
+    print(json.dumps({"op": "gemv_lm_head", "us": round(lm * 1e3, 1),
+                      "frac_of_hbm": round(m.lm_head.numel() * 2 / (pk["hbm_gbs"] * 1e3) / (lm * 1e3), 3)}))
+
+
+if __name__ == "__main__":
+    main()

@@ -16,7 +16,11 @@
 //
 // attn_decode_kernel: one query token per request; split-KV over 1-warp CTAs
 //   (16 rows = the token's g heads), partials combined by attn_combine_kernel.
+//   The default decode path is the TMA-fed 4-warp kernel in attention_tc.cu;
+//   this one is the comparison point (LL_DECODE_V1=1).
 #include <cuda_runtime.h>
+
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -552,9 +556,27 @@ extern "C" int ll_attn_prefill(const bf16* q, const bf16* kpool, const bf16* vpo
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
-extern "C" int ll_attn_decode(const bf16* q, const bf16* kpool, const bf16* vpool, const int* page_table,
-                              int pt_stride, const int* kv_lens, bf16* out, float* ws_o, float* ws_ml, int B, int Hq,
-                              int Hkv, int head_dim, int page_size, int nsplit, float scale, cudaStream_t stream) {
+extern "C" int ll_attn_decode_tma(const bf16* q, const bf16* k_pool, const bf16* v_pool, int pages,
+                                  const int* page_table, int pt_stride, const int* kv_lens, bf16* out, float* ws_o,
+                                  float* ws_ml, int B, int Hq, int Hkv, int page_size, int nsplit, float scale_log2,
+                                  int* err, cudaStream_t stream);
+
+// Decode attention runs on the TMA-fed kernel (attention_tc.cu);
+// LL_DECODE_V1=1 selects the one-warp cp.async kernel above, kept as the
+// comparison point (and used for page sizes that do not divide 64).
+static bool decode_tma_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("LL_DECODE_V1");
+    v = (e != nullptr && e[0] == '1') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+extern "C" int ll_attn_decode(const bf16* q, const bf16* kpool, const bf16* vpool, int num_pages,
+                              const int* page_table, int pt_stride, const int* kv_lens, bf16* out, float* ws_o,
+                              float* ws_ml, int B, int Hq, int Hkv, int head_dim, int page_size, int nsplit,
+                              float scale, int* err, cudaStream_t stream) {
   if (B <= 0) return 0;
   if (head_dim != AT_D || Hq % Hkv || Hq / Hkv > 16) return -3;
   if (nsplit < 1) nsplit = 1;
@@ -567,8 +589,14 @@ extern "C" int ll_attn_decode(const bf16* q, const bf16* kpool, const bf16* vpoo
   }
   dim3 grid(B * Hkv, nsplit);
   const float sl2 = scale * 1.4426950408889634f;
-  launch_pdl(attn_decode_kernel, grid, dim3(32), DC_SMEM, stream, q, kpool, vpool, page_table, pt_stride, kv_lens,
-             out, ws_o, ws_ml, Hq, Hkv, page_size, sl2);
+  if (decode_tma_enabled() && page_size >= 4 && 64 % page_size == 0) {
+    const int rc = ll_attn_decode_tma(q, kpool, vpool, num_pages, page_table, pt_stride, kv_lens, out, ws_o, ws_ml,
+                                      B, Hq, Hkv, page_size, nsplit, sl2, err, stream);
+    if (rc != 0) return rc;
+  } else {
+    launch_pdl(attn_decode_kernel, grid, dim3(32), DC_SMEM, stream, q, kpool, vpool, page_table, pt_stride, kv_lens,
+               out, ws_o, ws_ml, Hq, Hkv, page_size, sl2);
+  }
   if (nsplit > 1)
     launch_pdl(attn_combine_kernel, dim3(B * Hq), dim3(CB_THREADS), 0, stream, out, ws_o, ws_ml, nsplit);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;

@@ -541,6 +541,300 @@ static int attn_tc_variant() {
   return g_attn_variant;
 }
 
+// ----------------------------------------------------------------- decode
+// One query token per request, split-KV.  grid (B*Hkv, nsplit), block 160:
+// warps 0-3 compute, warp 4 is the TMA producer.  A CTA owns one contiguous
+// key range of one (request, kv head); its page-table entries are copied to
+// shared memory once, then 64-key K/V blocks arrive by TMA (one box of
+// page_size keys x 64 dims per page and half, 128-byte swizzle) in a 3-stage
+// ring, 16 bulk copies per block instead of 2048 16-byte copies.  Warp w takes
+// keys [16w, 16w+16) of every block with its own online softmax on mma.sync
+// m16n8k16 (16 rows = the token's g query heads); the warps' (m, l, O) are
+// merged in shared memory.  Output: final rows (nsplit == 1) or unnormalised
+// partials [B*Hq, nsplit, D] + (max log2, sum) for attn_combine_kernel.
+constexpr int DT_BN = 64;
+constexpr int DT_STAGES = 3;
+constexpr int DT_THREADS = 160;
+constexpr int DT_MAXP = 1024;
+constexpr int DT_HALF = DT_BN * 128;                 // 8 KB: one 64-dim half of a 64-key block
+constexpr int DT_KV = 2 * DT_HALF;                   // 16 KB per K (or V) block
+constexpr int DT_SMEM = 1024 + 4096 + DT_STAGES * 2 * DT_KV + DT_MAXP * 4 + 128;
+
+__device__ __forceinline__ uint32_t dt_swz(int key, int c16) {  // TMA 128-byte swizzle, two 64-dim halves
+  return (uint32_t)((c16 >> 3) * DT_HALF + key * 128 + (((c16 & 7) ^ (key & 7)) << 4));
+}
+__device__ __forceinline__ uint32_t dt_qswz(int row, int c16) {  // Q: 256-byte rows, XOR swizzle
+  return (uint32_t)(row * 256 + ((c16 ^ (row & 7)) << 4));
+}
+__device__ __forceinline__ void dt_ldsm(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void dt_ldsm_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void dt_mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(DT_THREADS)
+    attn_decode_tma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                           const bf16* __restrict__ q, const int* __restrict__ page_table, int pt_stride,
+                           const int* __restrict__ kv_lens, bf16* __restrict__ out, float* __restrict__ ws_o,
+                           float* __restrict__ ws_ml, int Hq, int Hkv, int ps, float scale_log2, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sKV = smem;                                  // [stage][K|V][2 halves][64 keys][128 B]
+  uint8_t* sQb = sKV + DT_STAGES * 2 * DT_KV;           // 16 rows x 256 B
+  int* spage = reinterpret_cast<int*>(sQb + 4096);
+  uint64_t* full = reinterpret_cast<uint64_t*>(spage + DT_MAXP);
+  uint64_t* empty = full + DT_STAGES;
+  const uint32_t sQ = smem_u32(sQb);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    for (int i = 0; i < DT_STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 4);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 4 && lane == 0) {
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x / Hkv, hk = blockIdx.x % Hkv;
+  const int split = blockIdx.y, nsplit = gridDim.y;
+  const int g = Hq / Hkv;
+  const int kv_len = kv_lens[b];
+  int chunk = (kv_len + nsplit - 1) / nsplit;
+  chunk = (chunk + DT_BN - 1) / DT_BN * DT_BN;
+  const int kbeg = min(kv_len, split * chunk);
+  const int kend = min(kv_len, kbeg + chunk);
+  const int nblocks = (kend - kbeg + DT_BN - 1) / DT_BN;
+  const int* pt = page_table + (size_t)b * pt_stride;
+  const int p0 = kbeg / ps;
+  const int npages = kend > kbeg ? (kend - 1) / ps - p0 + 1 : 0;
+  for (int i = tid; i < npages && i < DT_MAXP; i += DT_THREADS) spage[i] = pt[p0 + i];
+  if (warp < 4) {
+    const int c = tid & 15;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int r = (tid >> 4) + 8 * i;
+      const bool ok = r < g;
+      const bf16* src = ok ? q + (((size_t)b * Hq + hk * g + r) * 128 + c * 8) : q;
+      const int n = ok ? 16 : 0;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sQ + dt_qswz(r, c)), "l"(src), "r"(n)
+                   : "memory");
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  }
+  __syncthreads();  // barriers initialised, page list and Q in shared memory
+
+  float O[16][4];
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  if (warp == 4) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      const int pages_per_block = DT_BN / ps;
+      for (int blk = 0; blk < nblocks; ++blk) {
+        const int st = blk % DT_STAGES;
+        if (!mbar_wait(&empty[st], ((blk / DT_STAGES) & 1) ^ 1, err, kErrSmemEmptyTimeout)) break;
+        mbar_arrive_expect_tx(&full[st], 2 * DT_KV);
+        uint8_t* dk = sKV + st * 2 * DT_KV;
+        uint8_t* dv = dk + DT_KV;
+        for (int p = 0; p < pages_per_block; ++p) {
+          const int key0 = kbeg + blk * DT_BN + p * ps;
+          const int lp = key0 / ps - p0;
+          const int y = key0 < kend ? (lp < DT_MAXP ? spage[lp] : pt[p0 + lp]) * Hkv + hk : -1;  // -1: zero fill
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            tma_load_4d(dk + h * DT_HALF + p * ps * 128, &tmK, &full[st], 64 * h, 0, y, 0);
+            tma_load_4d(dv + h * DT_HALF + p * ps * 128, &tmV, &full[st], 64 * h, 0, y, 0);
+          }
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- consumers
+#pragma unroll
+    for (int i = 0; i < 16; ++i) O[i][0] = O[i][1] = O[i][2] = O[i][3] = 0.f;
+    uint32_t qf[8][4];
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int r = (lane & 7) + 8 * ((lane >> 3) & 1);
+      dt_ldsm(sQ + dt_qswz(r, 2 * kk + (lane >> 4)), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+    }
+    for (int blk = 0; blk < nblocks; ++blk) {
+      const int st = blk % DT_STAGES;
+      if (!mbar_wait(&full[st], (blk / DT_STAGES) & 1, err, kErrTmaFullTimeout)) break;
+      const uint32_t sK = smem_u32(sKV + st * 2 * DT_KV);
+      const uint32_t sV = sK + DT_KV;
+      const int k0 = kbeg + blk * DT_BN + 16 * warp;  // this warp's 16 keys
+      if (k0 + 16 > kend) {
+        // Rows past the last key hold whatever the page held: zero this
+        // warp's V rows there so that P = 0 never meets a non-finite V.
+        const int r = lane >> 1;
+        if (k0 + r >= kend) {
+          uint4* vrow0 = reinterpret_cast<uint4*>(sKV + st * 2 * DT_KV + DT_KV + (lane & 1) * DT_HALF +
+                                                  (16 * warp + r) * 128);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) vrow0[i] = make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+      }
+      float S[2][4];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) S[i][0] = S[i][1] = S[i][2] = S[i][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t b0, b1, b2, b3;
+        const int key = 16 * warp + (lane & 7) + 8 * (lane >> 4);
+        dt_ldsm(sK + dt_swz(key, 2 * kk + ((lane >> 3) & 1)), b0, b1, b2, b3);
+        dt_mma(S[0], qf[kk], b0, b1);
+        dt_mma(S[1], qf[kk], b2, b3);
+      }
+      float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = k0 + nt * 8 + 2 * (lane & 3) + e;
+          float va = S[nt][e] * scale_log2, vb = S[nt][2 + e] * scale_log2;
+          if (key >= kend) va = vb = -INFINITY;
+          S[nt][e] = va;
+          S[nt][2 + e] = vb;
+          mx_a = fmaxf(mx_a, va);
+          mx_b = fmaxf(mx_b, vb);
+        }
+      }
+      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+      const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+      const float al_a = (mn_a == -INFINITY) ? 1.f : ex2(m_a - mn_a);
+      const float al_b = (mn_b == -INFINITY) ? 1.f : ex2(m_b - mn_b);
+      const float sub_a = (mn_a == -INFINITY) ? 0.f : mn_a;
+      const float sub_b = (mn_b == -INFINITY) ? 0.f : mn_b;
+      m_a = mn_a;
+      m_b = mn_b;
+      float rs_a = 0.f, rs_b = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        S[nt][0] = ex2(S[nt][0] - sub_a);
+        S[nt][1] = ex2(S[nt][1] - sub_a);
+        S[nt][2] = ex2(S[nt][2] - sub_b);
+        S[nt][3] = ex2(S[nt][3] - sub_b);
+        rs_a += S[nt][0] + S[nt][1];
+        rs_b += S[nt][2] + S[nt][3];
+      }
+      l_a = l_a * al_a + rs_a;
+      l_b = l_b * al_b + rs_b;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        O[i][0] *= al_a;
+        O[i][1] *= al_a;
+        O[i][2] *= al_b;
+        O[i][3] *= al_b;
+      }
+      uint32_t a[4];
+      a[0] = pack_bf16x2(S[0][0], S[0][1]);
+      a[1] = pack_bf16x2(S[0][2], S[0][3]);
+      a[2] = pack_bf16x2(S[1][0], S[1][1]);
+      a[3] = pack_bf16x2(S[1][2], S[1][3]);
+#pragma unroll
+      for (int dp = 0; dp < 8; ++dp) {
+        uint32_t b0, b1, b2, b3;
+        const int key = 16 * warp + (lane & 7) + 8 * ((lane >> 3) & 1);
+        dt_ldsm_t(sV + dt_swz(key, 2 * dp + (lane >> 4)), b0, b1, b2, b3);
+        dt_mma(O[2 * dp], a, b0, b1);
+        dt_mma(O[2 * dp + 1], a, b2, b3);
+      }
+      fence_proxy_async();  // generic accesses of the stage before the next TMA write
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+  }
+  // ---- merge the four compute warps (every issued block was consumed, so
+  // the ring is free)
+  __syncthreads();
+  float* sm = reinterpret_cast<float*>(sKV);  // [4 warps][16 rows] m, then l
+  float* so = sm + 2 * 4 * 16;                // [16 rows][128] fp32
+  const int ra = lane >> 2, rb = ra + 8;
+  if (warp < 4 && (lane & 3) == 0) {
+    sm[warp * 16 + ra] = m_a;
+    sm[warp * 16 + rb] = m_b;
+    sm[64 + warp * 16 + ra] = l_a;
+    sm[64 + warp * 16 + rb] = l_b;
+  }
+  for (int i = tid; i < 16 * 128; i += DT_THREADS) so[i] = 0.f;
+  __syncthreads();
+  if (warp < 4) {
+    float Ma = -INFINITY, Mb = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      Ma = fmaxf(Ma, sm[w * 16 + ra]);
+      Mb = fmaxf(Mb, sm[w * 16 + rb]);
+    }
+    const float fa = (m_a == -INFINITY) ? 0.f : ex2(m_a - Ma);
+    const float fb = (m_b == -INFINITY) ? 0.f : ex2(m_b - Mb);
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      const int d = nt * 8 + 2 * (lane & 3);
+      atomicAdd(&so[ra * 128 + d], O[nt][0] * fa);
+      atomicAdd(&so[ra * 128 + d + 1], O[nt][1] * fa);
+      atomicAdd(&so[rb * 128 + d], O[nt][2] * fb);
+      atomicAdd(&so[rb * 128 + d + 1], O[nt][3] * fb);
+    }
+  }
+  __syncthreads();
+  if (tid < 128) {
+    const int r = tid >> 3, d0 = (tid & 7) * 16;
+    float M = -INFINITY, Lsum = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm[w * 16 + r]);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float mw = sm[w * 16 + r];
+      Lsum += (mw == -INFINITY) ? 0.f : sm[64 + w * 16 + r] * ex2(mw - M);
+    }
+    if (r < g) {
+      const size_t row = (size_t)b * Hq + hk * g + r;
+      if (nsplit == 1) {
+        const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          pk[i] = pack_bf16x2(so[r * 128 + d0 + 2 * i] * inv, so[r * 128 + d0 + 2 * i + 1] * inv);
+        uint4* dst = reinterpret_cast<uint4*>(out + row * 128 + d0);
+        dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      } else {
+        const size_t idx = row * nsplit + split;
+        float4* dst = reinterpret_cast<float4*>(ws_o + idx * 128 + d0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          dst[i] = make_float4(so[r * 128 + d0 + 4 * i], so[r * 128 + d0 + 4 * i + 1], so[r * 128 + d0 + 4 * i + 2],
+                               so[r * 128 + d0 + 4 * i + 3]);
+        if ((tid & 7) == 0) *reinterpret_cast<float2*>(ws_ml + idx * 2) = make_float2(M, Lsum);
+      }
+    }
+  }
+}
+
 }  // namespace ll
 
 using namespace ll;
@@ -591,4 +885,32 @@ extern "C" int ll_attn_prefill_tc_trace(unsigned long long* host, int n) {
   n = n < TC_TRACE_BLOCKS * TC_TRACE_EV ? n : TC_TRACE_BLOCKS * TC_TRACE_EV;
   if (cudaMemcpyFromSymbol(host, g_attn_trace, n * sizeof(unsigned long long)) != cudaSuccess) return -1;
   return n;
+}
+
+// Decode attention (split-KV partials or final rows); the caller launches the
+// combine when nsplit > 1.  k_pool / v_pool: ONE layer's pool [pages, Hkv,
+// page_size, 128].  page_size must divide 64 and be >= 4.
+extern "C" int ll_attn_decode_tma(const bf16* q, const bf16* k_pool, const bf16* v_pool, int pages,
+                                  const int* page_table, int pt_stride, const int* kv_lens, bf16* out, float* ws_o,
+                                  float* ws_ml, int B, int Hq, int Hkv, int page_size, int nsplit, float scale_log2,
+                                  int* err, cudaStream_t stream) {
+  if (page_size < 4 || DT_BN % page_size || Hq / Hkv > 16) return -3;
+  CUtensorMap tk, tv;
+  if (make_pool_map(&tk, k_pool, 1, pages, Hkv, page_size)) return -2;
+  if (make_pool_map(&tv, v_pool, 1, pages, Hkv, page_size)) return -2;
+  static int fits = -1;
+  if (fits < 0) {
+    int n = 0;
+    fits = cudaFuncSetAttribute(attn_decode_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DT_SMEM) ==
+                   cudaSuccess &&
+               cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_decode_tma_kernel, DT_THREADS, DT_SMEM) ==
+                   cudaSuccess &&
+               n >= 1
+           ? 1
+           : 0;
+  }
+  if (!fits) return -7;
+  launch_pdl(attn_decode_tma_kernel, dim3(B * Hkv, nsplit), dim3(DT_THREADS), DT_SMEM, stream, tk, tv, q, page_table,
+             pt_stride, kv_lens, out, ws_o, ws_ml, Hq, Hkv, page_size, scale_log2, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }

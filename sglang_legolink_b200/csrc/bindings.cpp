@@ -36,9 +36,9 @@ int ll_argmax(int* out, const bf16* logits, int rows, int vocab, int ld, cudaStr
 int ll_attn_prefill(const bf16* q, const bf16* kpool, const bf16* vpool, const int* q_indptr, const int* q_pos,
                     const int* page_table, int pt_stride, const int* tiles, int ntiles, bf16* out, int Hq, int Hkv,
                     int head_dim, int page_size, float scale, cudaStream_t stream);
-int ll_attn_decode(const bf16* q, const bf16* kpool, const bf16* vpool, const int* page_table, int pt_stride,
-                   const int* kv_lens, bf16* out, float* ws_o, float* ws_ml, int B, int Hq, int Hkv, int head_dim,
-                   int page_size, int nsplit, float scale, cudaStream_t stream);
+int ll_attn_decode(const bf16* q, const bf16* kpool, const bf16* vpool, int num_pages, const int* page_table,
+                   int pt_stride, const int* kv_lens, bf16* out, float* ws_o, float* ws_ml, int B, int Hq, int Hkv,
+                   int head_dim, int page_size, int nsplit, float scale, int* err, cudaStream_t stream);
 int ll_attn_prefill_tc(const bf16* q, const bf16* k_pool, const bf16* v_pool, int L, int pages, int layer,
                        const int* q_indptr, const int* q_pos, const int* page_table, int pt_stride, const int* tiles,
                        int ntiles, bf16* out, int Hq, int Hkv, int head_dim, int page_size, float scale, int* err,
@@ -284,7 +284,7 @@ void attn_prefill_tc(const at::Tensor& q, const at::Tensor& k_pool, const at::Te
 
 void attn_decode(const at::Tensor& q, const at::Tensor& k_pool_l, const at::Tensor& v_pool_l,
                  const at::Tensor& page_table, const at::Tensor& kv_lens, at::Tensor& out, at::Tensor& ws_o,
-                 at::Tensor& ws_ml, int64_t nsplit, double scale) {
+                 at::Tensor& ws_ml, int64_t nsplit, double scale, const at::Tensor& err) {
   CHECK_CUDA(q); CHECK_BF16(q); CHECK_CONTIG(q); CHECK_I32(page_table); CHECK_I32(kv_lens); CHECK_CONTIG(out);
   const int B = q.size(0), Hq = q.size(1), D = q.size(2);
   const int Hkv = k_pool_l.size(1), ps = k_pool_l.size(2);
@@ -293,9 +293,11 @@ void attn_decode(const at::Tensor& q, const at::Tensor& k_pool_l, const at::Tens
                 "decode workspace too small");
   }
   c10::cuda::CUDAGuard g(q.device());
-  check_rc(ll_attn_decode(bp(q), bp(k_pool_l), bp(v_pool_l), page_table.data_ptr<int>(), page_table.stride(0),
-                          kv_lens.data_ptr<int>(), bp(out), ws_o.data_ptr<float>(), ws_ml.data_ptr<float>(), B, Hq,
-                          Hkv, D, ps, (int)nsplit, (float)scale, cur_stream()),
+  TORCH_CHECK(k_pool_l.is_contiguous() && v_pool_l.is_contiguous() && k_pool_l.sizes() == v_pool_l.sizes());
+  check_rc(ll_attn_decode(bp(q), bp(k_pool_l), bp(v_pool_l), (int)k_pool_l.size(0), page_table.data_ptr<int>(),
+                          page_table.stride(0), kv_lens.data_ptr<int>(), bp(out), ws_o.data_ptr<float>(),
+                          ws_ml.data_ptr<float>(), B, Hq, Hkv, D, ps, (int)nsplit, (float)scale,
+                          err.data_ptr<int>(), cur_stream()),
            "ll_attn_decode");
 }
 

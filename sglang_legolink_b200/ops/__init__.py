@@ -276,12 +276,12 @@ def attention_prefill_mma(q, k_pool_l, v_pool_l, q_indptr, q_pos, page_table, sc
 
 
 def decode_splits(batch: int, num_kv_heads: int, max_kv_len: int, num_sms: int = 148) -> int:
-    """Split count for decode attention: about 6 one-warp CTAs per SM (the
-    residency limit of the kernel's 36 KB of shared memory), each covering at
-    least 64 keys (two 32-key blocks), capped at 1024 splits."""
-    target = 6 * num_sms
+    """Split count for decode attention: about two 4-warp CTAs per SM (the
+    residency limit of the kernel's 104 KB of shared memory), each covering
+    at least 128 keys (two 64-key blocks), capped at 1024 splits."""
+    target = 2 * num_sms
     n = max(1, math.ceil(target / max(1, batch * num_kv_heads)))
-    return int(max(1, min(n, math.ceil(max_kv_len / 64), 1024)))
+    return int(max(1, min(n, math.ceil(max_kv_len / 128), 1024)))
 
 
 def attention_decode(q, k_pool_l, v_pool_l, page_table, kv_lens, scale, nsplit=None, out=None) -> torch.Tensor:
@@ -307,7 +307,7 @@ def attention_decode(q, k_pool_l, v_pool_l, page_table, kv_lens, scale, nsplit=N
                 raise RuntimeError("decode workspace too small during CUDA graph capture; reserve it first")
             ws.reserve_decode(B * Hq, nsplit, D)
     _cuda().attn_decode(q, k_pool_l, v_pool_l, page_table, kv_lens, out.view(B, Hq, D), ws.dec_o, ws.dec_ml,
-                        nsplit, scale)
+                        nsplit, scale, ws.err)
     return out
 
 
