@@ -125,12 +125,15 @@ class AgentContextManifest:
     mutable_text: str
     selection_order: tuple = ()
     selector: str = "rule-based-v1"
+    excluded_sub_context_ids: tuple = ()
+    token_budget: Optional[int] = None
 
     def to_dict(self) -> dict:
         return {"task_id": self.task_id, "session_revision": self.session_revision,
                 "selected_sub_context_ids": list(self.selected_sub_context_ids),
                 "mutable_sub_context_ids": list(self.mutable_sub_context_ids), "mutable_text": self.mutable_text,
-                "selection_order": list(self.selection_order), "selector": self.selector}
+                "selection_order": list(self.selection_order), "selector": self.selector,
+                "excluded_sub_context_ids": list(self.excluded_sub_context_ids), "token_budget": self.token_budget}
 
 
 FIELD_ORDER = {f: i for i, f in enumerate(("task_instruction", "tool_definitions", "task_metadata",
@@ -141,7 +144,7 @@ class ContextManager:
     def __init__(self, task_id: str, *, tokenizer=None, store: Optional[SubContextStore] = None,
                  segmenter: Optional[DeterministicSegmenter] = None, model_fingerprint: str = "runtime-local",
                  recompute_policy_version: str = DEFAULT_RECOMPUTE_POLICY_VERSION, classifier=None,
-                 capture_token_ids: bool = False):
+                 capture_token_ids: bool = False, selector=None):
         self.task_id = task_id
         self.tokenizer = tokenizer or RegexTokenizer()
         self.collector = EventCollector(task_id)
@@ -151,6 +154,7 @@ class ContextManager:
         self.model_fingerprint = model_fingerprint
         self.recompute_policy_version = recompute_policy_version
         self.capture_token_ids = capture_token_ids
+        self.selector = selector  # host.selection selector; None = keep every active sub-context
         self._stored_revision: dict[str, str] = {}
 
     def ingest(self, values: Iterable[tuple], *, fail_after_extract: bool = False) -> list[SessionEvent]:
@@ -206,6 +210,16 @@ class ContextManager:
         return res
 
     def select(self, query_text: str = "") -> AgentContextManifest:
+        if self.selector is not None:
+            return self.selector.select(self, query_text)
+        ctx = self.ordered_contexts()
+        sel = tuple(v.sub_context_id for v in ctx)
+        mut = tuple(v.sub_context_id for v in ctx if v.is_mutable)
+        return AgentContextManifest(self.task_id, self.collector.revision, sel, mut, query_text, sel)
+
+    def ordered_contexts(self) -> list[SubContext]:
+        """Active sub-contexts in prompt order: stable fields, then history by
+        sequence, then the user prompt."""
         ctx = self.contexts()
 
         def order(v: SubContext):
@@ -217,9 +231,7 @@ class ContextManager:
             return (1, 0, v.sequence_number, v.metadata.get("segment_index", 0))
 
         ctx.sort(key=order)
-        sel = tuple(v.sub_context_id for v in ctx)
-        mut = tuple(v.sub_context_id for v in ctx if v.is_mutable)
-        return AgentContextManifest(self.task_id, self.collector.revision, sel, mut, query_text, sel)
+        return ctx
 
 
 def _with(v: SubContext, **kw) -> SubContext:
