@@ -1,7 +1,7 @@
 """Small single-kernel cases sized for `ncu --set full` captures (a few
 launches, a few hundred MB on the device), one per hot kernel:
 
-    python -m sglang_legolink_b200.benchmarks.ncu_cases {gemm,attn,gemv,decode,link}
+    python -m sglang_legolink_b200.benchmarks.ncu_cases {gemm,attn,gemv,decode,link,tp_reduce,tp_scatter}
 """
 import sys, os, math
 
@@ -50,6 +50,24 @@ elif case == "link":  # fused KV link + RoPE delta: 4096 tokens x 28 layers (Qwe
     lp = torch.arange(n, device="cuda", dtype=torch.int32)
     cs = ref.rope_cos_sin_table(32768, D, 1e6).cuda()
     for _ in range(4): ops.kv_link_rope(k, v, src, dst, lp, lp + 3000, cs)
+elif case in ("tp_reduce", "tp_scatter"):  # fused-TP kernels on one GPU: both "ranks'" buffers are local
+    W, H, K, T = 2, 5120, 4096, 16384
+    R = T // W
+    err = ops.workspace("cuda").err
+    ext = ops._cuda()
+    slots = [torch.zeros(W, R, H, device="cuda", dtype=torch.bfloat16) for _ in range(W)]
+    G = [torch.zeros(W * R, H, device="cuda", dtype=torch.bfloat16) for _ in range(W)]
+    cnt = [torch.zeros(2, device="cuda", dtype=torch.int64) for _ in range(W)]
+    sp, cp = [x.data_ptr() for x in slots], [c.data_ptr() for c in cnt]
+    gp, gcp = [x.data_ptr() for x in G], [c.data_ptr() + 8 for c in cnt]
+    if case == "tp_reduce":
+        res = torch.randn(R, H, device="cuda").to(torch.bfloat16)
+        w = torch.ones(H, device="cuda", dtype=torch.bfloat16)
+        for _ in range(4): ext.tp_reduce_norm_gather(slots[0], res, w, 1e-6, R, gp, gcp, 0, 0, 0, W, R, err)
+    else:
+        a = (torch.randn(T, K, device="cuda") * 0.5).to(torch.bfloat16)
+        w = (torch.randn(H, K, device="cuda") / 64).to(torch.bfloat16)
+        for _ in range(4): ext.gemm_tp(a, w, None, None, 2, H, sp, cp, 0, 0, 0, W, R, err)
 elif case == "decode_step":  # Qwen2.5-7B, 16K context, eager decode steps (launch lists only: full size)
     from sglang_legolink_b200.models.config import PRESETS
     from sglang_legolink_b200.models.qwen import QwenModel

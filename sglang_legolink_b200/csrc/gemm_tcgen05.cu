@@ -53,6 +53,20 @@ struct GemmCfg {
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
+// Tile order: groups of GEMM_GROUP_M m-blocks, m fastest inside a group, so
+// the tiles in flight at once (one per SM or SM pair) share a few A row
+// blocks and a few W column blocks; plain m-fastest order re-streams all of
+// A from HBM once per W column block when A does not fit in L2.
+constexpr int GEMM_GROUP_M = 8;
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = GEMM_GROUP_M * num_n;
+  const int first_m = (t / per_group) * GEMM_GROUP_M;
+  const int gm = min(num_m - first_m, GEMM_GROUP_M);
+  const int r = t % per_group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -103,7 +117,8 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const int mb = t % num_m, nb = t / num_m;
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrSmemEmptyTimeout)) {
             ok = false;
@@ -172,7 +187,8 @@ __global__ void __launch_bounds__(192, 1)
     int acc = 0;
     uint32_t aphase = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-      const int mb = t % num_m, nb = t / num_m;
+      int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
       if (!mbar_wait(&tfull[acc], aphase, err, kErrTmemFullTimeout)) break;
       tc_fence_after();
       const int row = mb * GEMM_BM + q * 32 + lane;
@@ -621,7 +637,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         fence_proxy_async_global();  // peers' generic stores -> this CTA's TMA (async proxy) reads
       }
       for (int t = pair; t < ntiles && ok; t += npairs) {
-        const int mb = t % num_m, nb = t / num_m;
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrSmemEmptyTimeout)) {
             ok = false;
@@ -693,7 +710,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     // (one system fence per warp instead of one per tile).
     uint32_t sent[LL_MAX_TP_RANKS] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int t = pair; t < ntiles; t += npairs) {
-      const int mb = t % num_m, nb = t / num_m;
+      int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
       if (!mbar_wait(&tfull[acc], aphase, err, kErrTmemFullTimeout)) break;
       tc_fence_after();
       const int row0 = mb * 2 * GEMM_BM + (int)crank * GEMM_BM + q * 32;  // this warp's 32-row slice
