@@ -643,24 +643,25 @@ __global__ void __launch_bounds__(DT_THREADS)
   float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
   if (warp == 4) {
     // ---------------------------------------------------------- producer
-    if (lane == 0) {
-      const int pages_per_block = DT_BN / ps;
-      for (int blk = 0; blk < nblocks; ++blk) {
-        const int st = blk % DT_STAGES;
-        if (!mbar_wait(&empty[st], ((blk / DT_STAGES) & 1) ^ 1, err, kErrSmemEmptyTimeout)) break;
-        mbar_arrive_expect_tx(&full[st], 2 * DT_KV);
-        uint8_t* dk = sKV + st * 2 * DT_KV;
-        uint8_t* dv = dk + DT_KV;
-        for (int p = 0; p < pages_per_block; ++p) {
-          const int key0 = kbeg + blk * DT_BN + p * ps;
-          const int lp = key0 / ps - p0;
-          const int y = key0 < kend ? (lp < DT_MAXP ? spage[lp] : pt[p0 + lp]) * Hkv + hk : -1;  // -1: zero fill
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            tma_load_4d(dk + h * DT_HALF + p * ps * 128, &tmK, &full[st], 64 * h, 0, y, 0);
-            tma_load_4d(dv + h * DT_HALF + p * ps * 128, &tmV, &full[st], 64 * h, 0, y, 0);
-          }
-        }
+    // The whole warp issues: lane (p, h, kv) = (lane >> 2, (lane >> 1) & 1,
+    // lane & 1) owns one box of page p, so a block's 16 boxes (page_size 16)
+    // go out in one instruction instead of 16 serial ones from one thread.
+    const int pages_per_block = DT_BN / ps;
+    const int p = lane >> 2, h = (lane >> 1) & 1, isv = lane & 1;
+    for (int blk = 0; blk < nblocks; ++blk) {
+      const int st = blk % DT_STAGES;
+      bool w = true;
+      if (lane == 0) {
+        w = mbar_wait(&empty[st], ((blk / DT_STAGES) & 1) ^ 1, err, kErrSmemEmptyTimeout);
+        if (w) mbar_arrive_expect_tx(&full[st], 2 * DT_KV);
+      }
+      if (!__shfl_sync(0xffffffffu, w, 0)) break;
+      for (int pp = p; pp < pages_per_block; pp += 8) {
+        const int key0 = kbeg + blk * DT_BN + pp * ps;
+        const int lp = key0 / ps - p0;
+        const int y = key0 < kend ? (lp < DT_MAXP ? spage[lp] : pt[p0 + lp]) * Hkv + hk : -1;  // -1: zero fill
+        uint8_t* dst = sKV + st * 2 * DT_KV + isv * DT_KV + h * DT_HALF + pp * ps * 128;
+        tma_load_4d(dst, isv ? &tmV : &tmK, &full[st], 64 * h, 0, y, 0);
       }
     }
   } else {
@@ -772,7 +773,8 @@ __global__ void __launch_bounds__(DT_THREADS)
   // the ring is free)
   __syncthreads();
   float* sm = reinterpret_cast<float*>(sKV);  // [4 warps][16 rows] m, then l
-  float* so = sm + 2 * 4 * 16;                // [16 rows][128] fp32
+  float* sw = sm + 2 * 4 * 16;                // [4 warps][16 rows][128] fp32, scaled partial O
+  float* so = sw;                             // warp 0's slice receives the sum
   const int ra = lane >> 2, rb = ra + 8;
   if (warp < 4 && (lane & 3) == 0) {
     sm[warp * 16 + ra] = m_a;
@@ -780,7 +782,6 @@ __global__ void __launch_bounds__(DT_THREADS)
     sm[64 + warp * 16 + ra] = l_a;
     sm[64 + warp * 16 + rb] = l_b;
   }
-  for (int i = tid; i < 16 * 128; i += DT_THREADS) so[i] = 0.f;
   __syncthreads();
   if (warp < 4) {
     float Ma = -INFINITY, Mb = -INFINITY;
@@ -791,13 +792,30 @@ __global__ void __launch_bounds__(DT_THREADS)
     }
     const float fa = (m_a == -INFINITY) ? 0.f : ex2(m_a - Ma);
     const float fb = (m_b == -INFINITY) ? 0.f : ex2(m_b - Mb);
+    float* mine = sw + warp * 16 * 128;
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt) {
       const int d = nt * 8 + 2 * (lane & 3);
-      atomicAdd(&so[ra * 128 + d], O[nt][0] * fa);
-      atomicAdd(&so[ra * 128 + d + 1], O[nt][1] * fa);
-      atomicAdd(&so[rb * 128 + d], O[nt][2] * fb);
-      atomicAdd(&so[rb * 128 + d + 1], O[nt][3] * fb);
+      *reinterpret_cast<float2*>(&mine[ra * 128 + d]) = make_float2(O[nt][0] * fa, O[nt][1] * fa);
+      *reinterpret_cast<float2*>(&mine[rb * 128 + d]) = make_float2(O[nt][2] * fb, O[nt][3] * fb);
+    }
+  }
+  __syncthreads();
+  // sum the four slices: thread -> 16 consecutive values of the 16 x 128 tile
+  if (tid < 128) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = tid * 16 + 4 * i;
+      float4 acc = *reinterpret_cast<const float4*>(&sw[e]);
+#pragma unroll
+      for (int w = 1; w < 4; ++w) {
+        const float4 v = *reinterpret_cast<const float4*>(&sw[w * 16 * 128 + e]);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      *reinterpret_cast<float4*>(&so[e]) = acc;
     }
   }
   __syncthreads();
