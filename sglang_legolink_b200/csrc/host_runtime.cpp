@@ -71,7 +71,11 @@ class PageAllocator {
   // number of pages freed.
   int64_t release(const std::vector<int32_t>& pages) {
     int64_t freed = 0;
-    for (int32_t p : pages) {
+    // Pushed in reverse so that a later alloc (which pops from the back)
+    // hands the run out again in ascending order: ascending page runs let
+    // the attention kernels load several pages with one TMA box.
+    for (auto it = pages.rbegin(); it != pages.rend(); ++it) {
+      const int32_t p = *it;
       check(p);
       if (refs_[p] <= 0) throw std::runtime_error("release of a free page");
       if (--refs_[p] == 0) {
