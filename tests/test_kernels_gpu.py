@@ -139,10 +139,12 @@ def test_kv_link_rope_matches_fp32_within_one_ulp(ps):
     assert torch.equal(vd.cpu(), vr.to(torch.bfloat16))
 
 
-def _paged_setup(B, lens, Hkv, D, ps, seed=0):
+def _paged_setup(B, lens, Hkv, D, ps, seed=0, contiguous=False):
     g = torch.Generator().manual_seed(seed)
     npages = sum((n + ps - 1) // ps for n in lens) + 4
-    perm = torch.randperm(npages, generator=g)
+    perm = torch.arange(npages) if contiguous else torch.randperm(npages, generator=g)
+    if contiguous:  # ascending runs with one break, so both load paths of the kernels run
+        perm[npages // 3:] = torch.flip(perm[npages // 3:], [0])
     kp = torch.randn(npages, Hkv, ps, D, generator=g).to(torch.bfloat16)
     vp = torch.randn(npages, Hkv, ps, D, generator=g).to(torch.bfloat16)
     maxp = max((n + ps - 1) // ps for n in lens)
@@ -185,11 +187,13 @@ def test_attention_prefill_sparse_rows(Hq, Hkv, ps):
     assert _rel(legacy.cpu(), exp) < 1.5e-2
 
 
-@pytest.mark.parametrize("B,Hq,Hkv,n", [(1, 28, 4, 16000), (3, 28, 4, 1000), (16, 8, 1, 3000), (2, 64, 8, 77)])
-def test_attention_decode(B, Hq, Hkv, n):
+@pytest.mark.parametrize("B,Hq,Hkv,n,contiguous", [(1, 28, 4, 16000, False), (1, 28, 4, 16000, True),
+                                                   (3, 28, 4, 1000, True), (16, 8, 1, 3000, False),
+                                                   (2, 64, 8, 77, False)])
+def test_attention_decode(B, Hq, Hkv, n, contiguous):
     D, ps = 128, 16
     lens = [n - 3 * b for b in range(B)]
-    kp, vp, pt = _paged_setup(B, lens, Hkv, D, ps, seed=3)
+    kp, vp, pt = _paged_setup(B, lens, Hkv, D, ps, seed=3, contiguous=contiguous)
     g = torch.Generator().manual_seed(2)
     q = torch.randn(B, Hq, D, generator=g).to(torch.bfloat16)
     kvl = torch.tensor(lens, dtype=torch.int32)
@@ -200,11 +204,14 @@ def test_attention_decode(B, Hq, Hkv, n):
     assert _rel(out.cpu(), exp) < 1.5e-2
 
 
-def test_attention_prefill_multi_layer_pool_full_causal():
-    """Full causal prefill of two requests reading layer 1 of a 3-layer pool."""
+@pytest.mark.parametrize("contiguous", [False, True])
+def test_attention_prefill_multi_layer_pool_full_causal(contiguous):
+    """Full causal prefill of two requests reading layer 1 of a 3-layer pool
+    (random page tables, and ascending page runs that use the whole-block
+    TMA boxes)."""
     D, ps, Hq, Hkv = 128, 16, 28, 4
     lens = [300, 1000]
-    kp, vp, pt = _paged_setup(2, lens, Hkv, D, ps, seed=5)
+    kp, vp, pt = _paged_setup(2, lens, Hkv, D, ps, seed=5, contiguous=contiguous)
     g = torch.Generator().manual_seed(9)
     K3 = torch.randn(3, *kp.shape, generator=g).to(torch.bfloat16)
     V3 = torch.randn(3, *vp.shape, generator=g).to(torch.bfloat16)
