@@ -55,6 +55,8 @@ namespace {
 #define CHECK_I64(x) TORCH_CHECK((x).scalar_type() == at::kLong, #x " must be int64")
 #define CHECK_F32(x) TORCH_CHECK((x).scalar_type() == at::kFloat, #x " must be float32")
 #define CHECK_CONTIG(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
+#define CHECK_ALIGN16(x) \
+  TORCH_CHECK(reinterpret_cast<uintptr_t>((x).data_ptr()) % 16 == 0, #x " must start on a 16-byte boundary")
 
 inline bf16* bp(const at::Tensor& t) { return reinterpret_cast<bf16*>(t.data_ptr()); }
 inline bf16* bp_opt(const c10::optional<at::Tensor>& t) { return t.has_value() ? bp(*t) : nullptr; }
@@ -254,7 +256,7 @@ void attn_prefill(const at::Tensor& q, const at::Tensor& k_pool_l, const at::Ten
                   const at::Tensor& q_indptr, const at::Tensor& q_pos, const at::Tensor& page_table,
                   const at::Tensor& tiles, at::Tensor& out, double scale) {
   CHECK_CUDA(q); CHECK_BF16(q); CHECK_CONTIG(q); CHECK_I32(q_indptr); CHECK_I32(q_pos); CHECK_I32(page_table);
-  CHECK_I32(tiles); CHECK_CONTIG(tiles); CHECK_CONTIG(out);
+  CHECK_I32(tiles); CHECK_CONTIG(tiles); CHECK_ALIGN16(tiles); CHECK_CONTIG(out);
   const int Hq = q.size(1), D = q.size(2);
   const int Hkv = k_pool_l.size(1), ps = k_pool_l.size(2);
   c10::cuda::CUDAGuard g(q.device());
@@ -270,7 +272,7 @@ void attn_prefill_tc(const at::Tensor& q, const at::Tensor& k_pool, const at::Te
                      const at::Tensor& tiles, at::Tensor& out, double scale, const at::Tensor& err) {
   CHECK_CUDA(q); CHECK_BF16(q); CHECK_CONTIG(q); CHECK_BF16(k_pool); CHECK_BF16(v_pool); CHECK_CONTIG(k_pool);
   CHECK_CONTIG(v_pool); CHECK_I32(q_indptr); CHECK_I32(q_pos); CHECK_I32(page_table); CHECK_I32(tiles);
-  CHECK_CONTIG(tiles); CHECK_CONTIG(out);
+  CHECK_CONTIG(tiles); CHECK_ALIGN16(tiles); CHECK_CONTIG(out);
   TORCH_CHECK(k_pool.dim() == 5 && k_pool.sizes() == v_pool.sizes());
   TORCH_CHECK(layer >= 0 && layer < k_pool.size(0));
   const int Hq = q.size(1), D = q.size(2);

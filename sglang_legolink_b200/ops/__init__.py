@@ -242,6 +242,37 @@ def prefill_tiles(q_indptr_host: torch.Tensor, q_pos_host: torch.Tensor, num_hea
     return t[order].to(torch.int32).contiguous()
 
 
+def prefill_tiles_np(q_indptr, q_pos, num_heads: int, num_kv_heads: int,
+                     rows_per_tile: int = PREFILL_ROWS_PER_TILE):
+    """numpy form of :func:`prefill_tiles` (int32 [n, 4]) for the host-side
+    batch build."""
+    import numpy as np
+
+    g = num_heads // num_kv_heads
+    qi = np.asarray(q_indptr, dtype=np.int64)
+    qp = np.asarray(q_pos, dtype=np.int64)
+    out = []
+    for b in range(len(qi) - 1):
+        s, e = int(qi[b]), int(qi[b + 1])
+        nrows = (e - s) * g
+        if nrows <= 0:
+            continue
+        r0 = np.arange(0, nrows, rows_per_tile, dtype=np.int64)
+        mp = qp[s + (np.minimum(r0 + rows_per_tile, nrows) - 1) // g]
+        n = len(r0)
+        t = np.empty((n * num_kv_heads, 4), dtype=np.int64)
+        t[:, 0] = b
+        t[:, 1] = np.tile(np.arange(num_kv_heads), n)
+        t[:, 2] = np.repeat(r0, num_kv_heads)
+        t[:, 3] = np.repeat(mp, num_kv_heads)
+        out.append(t)
+    if not out:
+        return np.zeros((0, 4), dtype=np.int32)
+    t = np.concatenate(out)
+    order = np.argsort(-t[:, 3], kind="stable")
+    return t[order].astype(np.int32)
+
+
 def attention_prefill(q, k_pool, v_pool, layer, q_indptr, q_pos, page_table, kv_lens, scale, tiles=None,
                       out=None) -> torch.Tensor:
     """q [T, Hq, D] -> [T, Hq*D]; rows attend to positions [0, q_pos] of their

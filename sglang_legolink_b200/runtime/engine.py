@@ -26,6 +26,7 @@ import time
 from dataclasses import dataclass, field
 from typing import Any, Callable, Optional, Sequence
 
+import numpy as np
 import torch
 
 from .. import ops
@@ -69,6 +70,30 @@ class Sequence_:
     finished: bool = False
     sampling: SamplingParams = GREEDY
     generator: Optional[torch.Generator] = None
+
+
+def _pinned_copy(host: np.ndarray, dev) -> torch.Tensor:
+    """One pinned staging buffer per dtype and device (grown on demand);
+    the copy is asynchronous, and the staging buffer is reused only after the
+    previous copy from it has finished."""
+    key = (str(host.dtype), str(dev))
+    ent = _PINNED.get(key)
+    if ent is None or ent[0].numel() < host.size:
+        buf = torch.empty(max(host.size, 1 << 16), dtype=torch.from_numpy(host[:0]).dtype, pin_memory=True)
+        ent = [buf, None]
+        _PINNED[key] = ent
+    buf, ev = ent
+    if ev is not None:
+        ev.synchronize()
+    buf[: host.size].numpy()[:] = host
+    out = buf[: host.size].to(dev, non_blocking=True)
+    ev = torch.cuda.Event()
+    ev.record()
+    ent[1] = ev
+    return out
+
+
+_PINNED: dict = {}
 
 
 class KVPool:
@@ -197,39 +222,58 @@ class Engine:
     # ----------------------------------------------------------- batch build
     def _extend_batch(self, items: list[tuple[list[int], list[int], list[int], int]],
                       logits_last_only=True) -> ForwardBatch:
-        """items: (token_ids_of_rows, positions_of_rows, pages, kv_len)."""
+        """items: (token_ids_of_rows, positions_of_rows, pages, kv_len).
+        The batch's int32 arrays travel in one host->device copy and its
+        int64 arrays in another (numpy on the host, views on the device)."""
         ps = self.page_size
-        ids, pos, slots, qptr = [], [], [], [0]
-        max_pages = max(len(p) for _, _, p, _ in items)
-        pt = torch.zeros(len(items), max(1, max_pages), dtype=torch.int32)
-        kvl = []
-        last_rows = []
-        for b, (t, p, pages, kv_len) in enumerate(items):
-            ids.extend(t)
-            pos.extend(p)
-            pg = torch.as_tensor(pages, dtype=torch.int64)
-            pp = torch.as_tensor(p, dtype=torch.int64)
-            slots.append(pg[pp // ps] * ps + pp % ps)
-            qptr.append(qptr[-1] + len(t))
-            pt[b, : len(pages)] = torch.as_tensor(pages, dtype=torch.int32)
-            kvl.append(kv_len)
-            last_rows.append(qptr[-1] - 1)
-        dev = self.device
-        positions = torch.as_tensor(pos, dtype=torch.int32)
-        q_indptr = torch.as_tensor(qptr, dtype=torch.int32)
-        tiles = None
+        B = len(items)
+        max_pages = max(1, max(len(p) for _, _, p, _ in items))
+        ids = np.concatenate([np.asarray(t, dtype=np.int32) for t, _, _, _ in items])
+        pos = np.concatenate([np.asarray(p, dtype=np.int64) for _, p, _, _ in items])
+        counts = np.asarray([len(t) for t, _, _, _ in items], dtype=np.int64)
+        qptr = np.concatenate(([0], np.cumsum(counts))).astype(np.int32)
+        pt = np.zeros((B, max_pages), dtype=np.int32)
+        slots = np.empty(len(pos), dtype=np.int64)
+        for b, (_, p, pages, _) in enumerate(items):
+            pg = np.asarray(pages, dtype=np.int64)
+            pt[b, : len(pg)] = pg
+            pp = pos[qptr[b] : qptr[b + 1]]
+            slots[qptr[b] : qptr[b + 1]] = pg[pp // ps] * ps + pp % ps
+        kvl = np.asarray([kv for _, _, _, kv in items], dtype=np.int32)
+        last_rows = (qptr[1:] - 1).astype(np.int64)
+        pos32 = pos.astype(np.int32)
+        parts32 = [ids, pos32, qptr, pt.reshape(-1), kvl]
         if self.is_cuda:
-            tiles = ops.prefill_tiles(q_indptr, positions, self.model.hq, self.model.hkv).to(dev, non_blocking=True)
+            parts32.append(ops.prefill_tiles_np(qptr, pos32, self.model.hq, self.model.hkv).reshape(-1))
+        # every segment starts on a 256-byte boundary: kernels read some of
+        # them (the prefill tile list) with 16-byte vector loads
+        sizes32 = [a.size for a in parts32]
+        starts32 = np.concatenate(([0], np.cumsum([-(-n // 64) * 64 for n in sizes32]))).tolist()
+        host32 = np.zeros(starts32[-1], dtype=np.int32)
+        for st, a in zip(starts32, parts32):
+            host32[st:st + a.size] = a
+        n = len(pos)
+        off64 = -(-n // 32) * 32
+        host64 = np.zeros(off64 + B, dtype=np.int64)
+        host64[:n] = slots
+        host64[off64:] = last_rows
+        dev = self.device
+        if self.is_cuda:
+            d32 = _pinned_copy(host32, dev)
+            d64 = _pinned_copy(host64, dev)
+        else:
+            d32, d64 = torch.from_numpy(host32), torch.from_numpy(host64)
+        view = [d32[st:st + sz] for st, sz in zip(starts32, sizes32)]
         return ForwardBatch(
             mode="extend",
-            input_ids=torch.as_tensor(ids, dtype=torch.int32).to(dev, non_blocking=True),
-            positions=positions.to(dev, non_blocking=True),
-            slots=torch.cat(slots).to(dev, non_blocking=True),
-            q_indptr=q_indptr.to(dev, non_blocking=True),
-            page_table=pt.to(dev, non_blocking=True),
-            kv_lens=torch.as_tensor(kvl, dtype=torch.int32).to(dev, non_blocking=True),
-            logit_rows=torch.as_tensor(last_rows, dtype=torch.int64).to(dev, non_blocking=True),
-            tiles=tiles,
+            input_ids=view[0],
+            positions=view[1],
+            slots=d64[:n],
+            q_indptr=view[2],
+            page_table=view[3].view(B, max_pages),
+            kv_lens=view[4],
+            logit_rows=d64[off64:],
+            tiles=view[5].view(-1, 4) if self.is_cuda else None,
         )
 
     def _sample(self, logits: torch.Tensor, params: Sequence[SamplingParams] = (),
@@ -354,7 +398,7 @@ class Engine:
         replica whose pool holds the source block (``None`` = this one)."""
         ps = self.page_size
         groups: dict = {}
-        dpg = torch.as_tensor(dst_pages, dtype=torch.int64)
+        dpg = np.asarray(dst_pages, dtype=np.int64)
         for key, l0, g0, cnt in resolved.linked_rows():
             rb = self._remote.get(key)
             if rb is None:
@@ -362,16 +406,21 @@ class Engine:
                 pages, off, sps, owner = h["pages"], int(h["first_page_offset"]), ps, None
             else:
                 pages, off, sps, owner = rb.pages, rb.first_page_offset, rb.page_size, rb.owner
-            spg = torch.as_tensor(list(pages), dtype=torch.int64)
-            loc = torch.arange(l0, l0 + cnt, dtype=torch.int64)
+            spg = np.asarray(pages, dtype=np.int64)
+            loc = np.arange(l0, l0 + cnt, dtype=np.int64)
             sl = loc + off
-            glob = torch.arange(g0, g0 + cnt, dtype=torch.int64)
+            glob = np.arange(g0, g0 + cnt, dtype=np.int64)
             g = groups.setdefault(owner, ([], [], [], []))
             g[0].append(spg[sl // sps] * sps + sl % sps)
             g[1].append(dpg[glob // ps] * ps + glob % ps)
-            g[2].append(loc.to(torch.int32))
-            g[3].append(glob.to(torch.int32))
-        return {o: tuple(torch.cat(x) for x in g) for o, g in groups.items()}
+            g[2].append(loc)
+            g[3].append(glob)
+        out = {}
+        for o, g in groups.items():
+            src, dst, lp, gp = (np.concatenate(x) for x in g)
+            out[o] = (torch.from_numpy(src), torch.from_numpy(dst), torch.from_numpy(lp.astype(np.int32)),
+                      torch.from_numpy(gp.astype(np.int32)))
+        return out
 
     def link(self, pic_link: dict, mutable_input_ids: Sequence[int], *, rid: Optional[str] = None,
              timer: Optional["CudaTimer"] = None, sampling: Optional[SamplingParams] = None) -> Sequence_:

@@ -92,20 +92,19 @@ class ResolvedLinkPlan:
     def linked_rows(self) -> list[tuple[str, int, int]]:
         """(cache_key, local_start, global_start, count) runs of linked (not
         recomputed) tokens; used to build the KV link gather."""
-        rec = set(self.recompute_positions)
+        import numpy as np
+
+        rec = np.zeros(self.total_token_count + 1, dtype=np.bool_)
+        if self.recompute_positions:
+            rec[np.asarray(self.recompute_positions, dtype=np.int64)] = True
         runs = []
         for b in self.block_ranges:
-            i = 0
-            n = b.token_count
-            while i < n:
-                while i < n and (b.start_token + i) in rec:
-                    i += 1
-                j = i
-                while j < n and (b.start_token + j) not in rec:
-                    j += 1
-                if j > i:
-                    runs.append((b.cache_key, i, b.start_token + i, j - i))
-                i = j
+            linked = ~rec[b.start_token:b.end_token]
+            if not linked.any():
+                continue
+            edges = np.flatnonzero(np.diff(np.concatenate(([False], linked, [False])).astype(np.int8)))
+            for i, j in zip(edges[0::2].tolist(), edges[1::2].tolist()):
+                runs.append((b.cache_key, i, b.start_token + i, j - i))
         return runs
 
 
