@@ -88,8 +88,8 @@ def main():
         "attn_decode": (lambda: [ops.attention_decode(q, kpool[i], vpool[i], pt, kvl, scale, nsplit=nsplit, out=attn)
                                  for i in range(L)], kvb),
         "gemv_o_proj": (lambda: [ops.linear(attn, lw.o_w, out=o) for lw in m.layers], m.layers[0].o_w.numel() * 2),
-        "gemv_gate_up": (lambda: [ops.linear(x, lw.gu_w, out=gu) for lw in m.layers], m.layers[0].gu_w.numel() * 2),
-        "swiglu": (lambda: [ops.swiglu(gu, out=mlp) for _ in range(L)], gu.numel() * 3),
+        "gemv_gate_up_swiglu": (lambda: [ops.linear(x, lw.gu_w, out=mlp, swiglu_epilogue=True) for lw in m.layers],
+                                m.layers[0].gu_w.numel() * 2),
         "gemv_down": (lambda: [ops.linear(mlp, lw.down_w, out=o) for lw in m.layers], m.layers[0].down_w.numel() * 2),
     }
     total = 0.0

@@ -559,7 +559,7 @@ extern "C" int ll_attn_prefill(const bf16* q, const bf16* kpool, const bf16* vpo
 extern "C" int ll_attn_decode_tma(const bf16* q, const bf16* k_pool, const bf16* v_pool, int pages,
                                   const int* page_table, int pt_stride, const int* kv_lens, bf16* out, float* ws_o,
                                   float* ws_ml, int B, int Hq, int Hkv, int page_size, int nsplit, float scale_log2,
-                                  int* err, cudaStream_t stream);
+                                  int new_tokens, int* err, cudaStream_t stream);
 
 // Decode attention runs on the TMA-fed kernel (attention_tc.cu);
 // LL_DECODE_V1=1 selects the one-warp cp.async kernel above, kept as the
@@ -590,8 +590,13 @@ extern "C" int ll_attn_decode(const bf16* q, const bf16* kpool, const bf16* vpoo
   dim3 grid(B * Hkv, nsplit);
   const float sl2 = scale * 1.4426950408889634f;
   if (decode_tma_enabled() && page_size >= 4 && 64 % page_size == 0) {
+    // One query per request: only its own key (the last) may have been
+    // written by the previous kernel; the TMA kernel streams the older keys
+    // before waiting on it.  Every other K/V writer is separated from this
+    // launch by a stream-ordered copy (each decode step starts with its
+    // input copies), so it has completed.
     const int rc = ll_attn_decode_tma(q, kpool, vpool, num_pages, page_table, pt_stride, kv_lens, out, ws_o, ws_ml,
-                                      B, Hq, Hkv, page_size, nsplit, sl2, err, stream);
+                                      B, Hq, Hkv, page_size, nsplit, sl2, 1, err, stream);
     if (rc != 0) return rc;
   } else {
     launch_pdl(attn_decode_kernel, grid, dim3(32), DC_SMEM, stream, q, kpool, vpool, page_table, pt_stride, kv_lens,

@@ -615,7 +615,8 @@ __global__ void __launch_bounds__(DT_THREADS)
                            const __grid_constant__ CUtensorMap tmKr, const __grid_constant__ CUtensorMap tmVr,
                            const bf16* __restrict__ q, const int* __restrict__ page_table, int pt_stride,
                            const int* __restrict__ kv_lens, bf16* __restrict__ out, float* __restrict__ ws_o,
-                           float* __restrict__ ws_ml, int Hq, int Hkv, int ps, float scale_log2, int* err) {
+                           float* __restrict__ ws_ml, int Hq, int Hkv, int ps, float scale_log2, int new_tokens,
+                           int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sKV = smem;                                  // [stage][K|V][2 halves][64 keys][128 B]
@@ -639,11 +640,16 @@ __global__ void __launch_bounds__(DT_THREADS)
     prefetch_tmap(&tmVr);
   }
   pdl_trigger();
-  pdl_wait();
+  // Before the wait on the previous kernel: the kv lengths and page table
+  // (written before this step's first kernel) and the K/V of every key but
+  // the newest `new_tokens` of each request (written by earlier steps).  Only
+  // Q and those newest keys come from the previous kernel (rope + KV write),
+  // so the page list and the first blocks stream in while it finishes.
   const int b = blockIdx.x / Hkv, hk = blockIdx.x % Hkv;
   const int split = blockIdx.y, nsplit = gridDim.y;
   const int g = Hq / Hkv;
   const int kv_len = kv_lens[b];
+  const int fresh0 = kv_len - new_tokens;  // keys >= fresh0 are read only after the wait
   int chunk = (kv_len + nsplit - 1) / nsplit;
   chunk = (chunk + DT_BN - 1) / DT_BN * DT_BN;
   const int kbeg = min(kv_len, split * chunk);
@@ -653,20 +659,7 @@ __global__ void __launch_bounds__(DT_THREADS)
   const int p0 = kbeg / ps;
   const int npages = kend > kbeg ? (kend - 1) / ps - p0 + 1 : 0;
   for (int i = tid; i < npages && i < DT_MAXP; i += DT_THREADS) spage[i] = pt[p0 + i];
-  if (warp < 4) {
-    const int c = tid & 15;
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int r = (tid >> 4) + 8 * i;
-      const bool ok = r < g;
-      const bf16* src = ok ? q + (((size_t)b * Hq + hk * g + r) * 128 + c * 8) : q;
-      const int n = ok ? 16 : 0;
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sQ + dt_qswz(r, c)), "l"(src), "r"(n)
-                   : "memory");
-    }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-  }
-  __syncthreads();  // barriers initialised, page list and Q in shared memory
+  __syncthreads();  // barriers initialised, page list in shared memory
 
   float O[16][4];
   float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
@@ -677,8 +670,13 @@ __global__ void __launch_bounds__(DT_THREADS)
     // go out in one instruction instead of 16 serial ones from one thread.
     const int pages_per_block = DT_BN / ps;
     const int p = lane >> 2, h = (lane >> 1) & 1, isv = lane & 1;
+    bool waited = false;
     for (int blk = 0; blk < nblocks; ++blk) {
       const int st = blk % DT_STAGES;
+      if (!waited && kbeg + (blk + 1) * DT_BN > fresh0) {
+        pdl_wait();  // this block holds keys the previous kernel wrote
+        waited = true;
+      }
       bool w = true;
       if (lane == 0) {
         w = mbar_wait(&empty[st], ((blk / DT_STAGES) & 1) ^ 1, err, kErrSmemEmptyTimeout);
@@ -713,6 +711,21 @@ __global__ void __launch_bounds__(DT_THREADS)
     }
   } else {
     // ---------------------------------------------------------- consumers
+    pdl_wait();  // Q (and the outputs' previous readers) belong to earlier kernels
+    {
+      const int c = tid & 15;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int r = (tid >> 4) + 8 * i;
+        const bool ok = r < g;
+        const bf16* src = ok ? q + (((size_t)b * Hq + hk * g + r) * 128 + c * 8) : q;
+        const int n = ok ? 16 : 0;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sQ + dt_qswz(r, c)), "l"(src), "r"(n)
+                     : "memory");
+      }
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the four compute warps: Q in shared memory
+    }
 #pragma unroll
     for (int i = 0; i < 16; ++i) O[i][0] = O[i][1] = O[i][2] = O[i][3] = 0.f;
     uint32_t qf[8][4];
@@ -817,11 +830,12 @@ __global__ void __launch_bounds__(DT_THREADS)
     l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
   }
   // ---- merge the four compute warps (every issued block was consumed, so
-  // the ring is free)
+  // the ring is free).  Only the g real query rows are written; the slices
+  // use an XOR swizzle (column ^ 8 * row) so that a warp's float2 stores and
+  // the summing threads' float4 loads are free of bank conflicts.
   __syncthreads();
   float* sm = reinterpret_cast<float*>(sKV);  // [4 warps][16 rows] m, then l
   float* sw = sm + 2 * 4 * 16;                // [4 warps][16 rows][128] fp32, scaled partial O
-  float* so = sw;                             // warp 0's slice receives the sum
   const int ra = lane >> 2, rb = ra + 8;
   if (warp < 4 && (lane & 3) == 0) {
     sm[warp * 16 + ra] = m_a;
@@ -840,33 +854,25 @@ __global__ void __launch_bounds__(DT_THREADS)
     const float fa = (m_a == -INFINITY) ? 0.f : ex2(m_a - Ma);
     const float fb = (m_b == -INFINITY) ? 0.f : ex2(m_b - Mb);
     float* mine = sw + warp * 16 * 128;
+    if (ra < g) {
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
-      const int d = nt * 8 + 2 * (lane & 3);
-      *reinterpret_cast<float2*>(&mine[ra * 128 + d]) = make_float2(O[nt][0] * fa, O[nt][1] * fa);
-      *reinterpret_cast<float2*>(&mine[rb * 128 + d]) = make_float2(O[nt][2] * fb, O[nt][3] * fb);
-    }
-  }
-  __syncthreads();
-  // sum the four slices: thread -> 16 consecutive values of the 16 x 128 tile
-  if (tid < 128) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int e = tid * 16 + 4 * i;
-      float4 acc = *reinterpret_cast<const float4*>(&sw[e]);
-#pragma unroll
-      for (int w = 1; w < 4; ++w) {
-        const float4 v = *reinterpret_cast<const float4*>(&sw[w * 16 * 128 + e]);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+      for (int nt = 0; nt < 16; ++nt) {
+        const int d = (nt * 8 + 2 * (lane & 3)) ^ (ra << 3);
+        *reinterpret_cast<float2*>(&mine[ra * 128 + d]) = make_float2(O[nt][0] * fa, O[nt][1] * fa);
       }
-      *reinterpret_cast<float4*>(&so[e]) = acc;
+    }
+    if (rb < g) {
+#pragma unroll
+      for (int nt = 0; nt < 16; ++nt) {
+        const int d = (nt * 8 + 2 * (lane & 3)) ^ (rb << 3);
+        *reinterpret_cast<float2*>(&mine[rb * 128 + d]) = make_float2(O[nt][2] * fb, O[nt][3] * fb);
+      }
     }
   }
   __syncthreads();
-  if (tid < 128) {
+  // thread -> 16 consecutive columns of one row: sum the four slices and
+  // write the final row (nsplit == 1) or this split's partial
+  if (tid < 128 && (tid >> 3) < g) {
     const int r = tid >> 3, d0 = (tid & 7) * 16;
     float M = -INFINITY, Lsum = 0.f;
 #pragma unroll
@@ -876,26 +882,39 @@ __global__ void __launch_bounds__(DT_THREADS)
       const float mw = sm[w * 16 + r];
       Lsum += (mw == -INFINITY) ? 0.f : sm[64 + w * 16 + r] * ex2(mw - M);
     }
-    if (r < g) {
-      const size_t row = (size_t)b * Hq + hk * g + r;
-      if (nsplit == 1) {
-        const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
-        uint32_t pk[8];
+    float acc[16];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          pk[i] = pack_bf16x2(so[r * 128 + d0 + 2 * i] * inv, so[r * 128 + d0 + 2 * i + 1] * inv);
-        uint4* dst = reinterpret_cast<uint4*>(out + row * 128 + d0);
-        dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-      } else {
-        const size_t idx = row * nsplit + split;
-        float4* dst = reinterpret_cast<float4*>(ws_o + idx * 128 + d0);
+    for (int i = 0; i < 4; ++i) {
+      const int e = r * 128 + ((d0 + 4 * i) ^ (r << 3));
+      float4 a4 = *reinterpret_cast<const float4*>(&sw[e]);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          dst[i] = make_float4(so[r * 128 + d0 + 4 * i], so[r * 128 + d0 + 4 * i + 1], so[r * 128 + d0 + 4 * i + 2],
-                               so[r * 128 + d0 + 4 * i + 3]);
-        if ((tid & 7) == 0) *reinterpret_cast<float2*>(ws_ml + idx * 2) = make_float2(M, Lsum);
+      for (int w = 1; w < 4; ++w) {
+        const float4 v = *reinterpret_cast<const float4*>(&sw[w * 16 * 128 + e]);
+        a4.x += v.x;
+        a4.y += v.y;
+        a4.z += v.z;
+        a4.w += v.w;
       }
+      acc[4 * i] = a4.x;
+      acc[4 * i + 1] = a4.y;
+      acc[4 * i + 2] = a4.z;
+      acc[4 * i + 3] = a4.w;
+    }
+    const size_t row = (size_t)b * Hq + hk * g + r;
+    if (nsplit == 1) {
+      const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+      uint32_t pk[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pk[i] = pack_bf16x2(acc[2 * i] * inv, acc[2 * i + 1] * inv);
+      uint4* dst = reinterpret_cast<uint4*>(out + row * 128 + d0);
+      dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+    } else {
+      const size_t idx = row * nsplit + split;
+      float4* dst = reinterpret_cast<float4*>(ws_o + idx * 128 + d0);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) dst[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+      if ((tid & 7) == 0) *reinterpret_cast<float2*>(ws_ml + idx * 2) = make_float2(M, Lsum);
     }
   }
 }
@@ -958,7 +977,7 @@ extern "C" int ll_attn_prefill_tc_trace(unsigned long long* host, int n) {
 extern "C" int ll_attn_decode_tma(const bf16* q, const bf16* k_pool, const bf16* v_pool, int pages,
                                   const int* page_table, int pt_stride, const int* kv_lens, bf16* out, float* ws_o,
                                   float* ws_ml, int B, int Hq, int Hkv, int page_size, int nsplit, float scale_log2,
-                                  int* err, cudaStream_t stream) {
+                                  int new_tokens, int* err, cudaStream_t stream) {
   if (page_size < 4 || DT_BN % page_size || Hq / Hkv > 16) return -3;
   CUtensorMap tk, tv, tkr, tvr;
   if (make_pool_map(&tk, k_pool, 1, pages, Hkv, page_size)) return -2;
@@ -979,6 +998,6 @@ extern "C" int ll_attn_decode_tma(const bf16* q, const bf16* k_pool, const bf16*
   if (!fits) return -7;
   launch_pdl(attn_decode_tma_kernel, dim3(B * Hkv, nsplit), dim3(DT_THREADS), DT_SMEM, stream, tk, tv, tkr, tvr, q,
              page_table,
-             pt_stride, kv_lens, out, ws_o, ws_ml, Hq, Hkv, page_size, scale_log2, err);
+             pt_stride, kv_lens, out, ws_o, ws_ml, Hq, Hkv, page_size, scale_log2, new_tokens, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }

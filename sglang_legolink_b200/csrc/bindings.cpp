@@ -19,7 +19,7 @@ int ll_gemm_bf16_small_m(const bf16* A, int lda, const bf16* W, int ldw, bf16* C
 int ll_gemm_small_m_splits(int N, int K);
 int ll_gemm_bf16_small_m_ex(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc, const bf16* bias,
                             int M, int N, int K, int splits, float* ws, size_t ws_floats, int* tickets, int* err,
-                            int w_tiled, cudaStream_t stream);
+                            int flags, cudaStream_t stream);
 int ll_rmsnorm(bf16* out, const bf16* x, bf16* residual, const bf16* w, int rows, int hidden, float eps,
                cudaStream_t stream);
 int ll_rope_qkv_write(const bf16* qkv, const int* positions, const int64_t* slots, const float* cos_sin, bf16* q_out,
@@ -159,8 +159,10 @@ void tp_wait(int64_t cnt, int64_t target, const at::Tensor& err) {
            "ll_tp_wait");
 }
 
+// swiglu: w is the interleaved gate/up weight and out holds silu(gate) * up
+// (N / 2 columns).
 void gemm_small_m(const at::Tensor& a, const at::Tensor& w, const c10::optional<at::Tensor>& bias, at::Tensor& out,
-                  int64_t splits, at::Tensor& ws, at::Tensor& tickets, const at::Tensor& err) {
+                  int64_t splits, at::Tensor& ws, at::Tensor& tickets, const at::Tensor& err, bool swiglu) {
   CHECK_CUDA(a); CHECK_BF16(a); CHECK_BF16(w); CHECK_BF16(out); CHECK_CONTIG(w); CHECK_F32(ws); CHECK_I32(tickets);
   TORCH_CHECK(a.stride(1) == 1 && out.stride(1) == 1);
   // w: [N, K] row-major, or tile-major [N/128, K/64, 128, 64].
@@ -172,11 +174,12 @@ void gemm_small_m(const at::Tensor& a, const at::Tensor& w, const c10::optional<
   } else {
     TORCH_CHECK(w.size(1) == K);
   }
-  TORCH_CHECK(out.size(0) == M && out.size(1) == N);
+  TORCH_CHECK(out.size(0) == M && out.size(1) == (swiglu ? N / 2 : N));
   c10::cuda::CUDAGuard g(a.device());
   check_rc(ll_gemm_bf16_small_m_ex(bp(a), a.stride(0), bp(w), tiled ? K : (int)w.stride(0), bp(out), out.stride(0),
                                    bp_opt(bias), M, N, K, (int)splits, ws.data_ptr<float>(), (size_t)ws.numel(),
-                                   tickets.data_ptr<int>(), err.data_ptr<int>(), tiled ? 1 : 0, cur_stream()),
+                                   tickets.data_ptr<int>(), err.data_ptr<int>(), (tiled ? 1 : 0) | (swiglu ? 2 : 0),
+                                   cur_stream()),
            "ll_gemm_bf16_small_m");
 }
 

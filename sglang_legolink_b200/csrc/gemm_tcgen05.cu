@@ -36,6 +36,9 @@ namespace ll {
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
+// ll_gemm_bf16_small_m_ex flags
+constexpr int LL_SMALL_M_W_TILED = 1;
+constexpr int LL_SMALL_M_SWIGLU = 2;
 
 enum Epilogue : int { kEpiPlain = 0, kEpiSwiGLU = 1, kEpiScatter = 2 };
 
@@ -284,8 +287,14 @@ __global__ void __launch_bounds__(192, 2)
     gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                        bf16* __restrict__ C, const bf16* __restrict__ bias, int M, int N, int K, int ldc,
                        int kb_per_split, float* __restrict__ ws, int* __restrict__ tickets, int* err,
-                       int w_tiled) {
+                       int flags) {
   using Cfg = SwapCfg<BNX>;
+  const int w_tiled = flags & LL_SMALL_M_W_TILED;
+  // SwiGLU epilogue: features are gate/up interleaved in groups of 16 (lanes
+  // 0-15 of a warp hold gate features, lanes 16-31 the matching up
+  // features); C then has N / 2 columns.  N % 32 == 0, so a warp is wholly
+  // inside or outside N.
+  const bool swiglu = (flags & LL_SMALL_M_SWIGLU) != 0;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -404,7 +413,18 @@ __global__ void __launch_bounds__(192, 2)
       tmem_ld_wait();
       if (!ok) continue;
       const int ncols = BNX < 32 ? BNX : 32;
-      if (nsplit == 1) {
+      if (nsplit == 1 && swiglu) {
+        if (feat < N) {
+          const float b = bias != nullptr ? __bfloat162float(bias[feat]) : 0.f;
+          const int ocol = (feat >> 5) * 16 + (lane & 15);
+          for (int i = 0; i < ncols; ++i) {
+            const int m = c + i;
+            const float v = __uint_as_float(r[i]) + b;
+            const float u = __shfl_down_sync(0xffffffffu, v, 16);
+            if (lane < 16 && m < M) C[(size_t)m * ldc + ocol] = __float2bfloat16(silu_f(v) * u);
+          }
+        }
+      } else if (nsplit == 1) {
         if (feat < N) {
           const float b = bias != nullptr ? __bfloat162float(bias[feat]) : 0.f;
           for (int i = 0; i < ncols; ++i) {
@@ -433,10 +453,16 @@ __global__ void __launch_bounds__(192, 2)
         __threadfence();
         if (feat < N) {
           const float b = bias != nullptr ? __bfloat162float(bias[feat]) : 0.f;
+          const int ocol = (feat >> 5) * 16 + (lane & 15);
           for (int m = 0; m < M; ++m) {
             float s = b;
             for (int sp = 0; sp < nsplit; ++sp) s += __ldcg(ws + ((size_t)sp * M + m) * N + feat);
-            C[(size_t)m * ldc + feat] = __float2bfloat16(s);
+            if (swiglu) {
+              const float u = __shfl_down_sync(0xffffffffu, s, 16);
+              if (lane < 16) C[(size_t)m * ldc + ocol] = __float2bfloat16(silu_f(s) * u);
+            } else {
+              C[(size_t)m * ldc + feat] = __float2bfloat16(s);
+            }
           }
         }
         if (threadIdx.x == 64) tickets[nb] = 0;  // ready for the next launch / graph replay
@@ -973,7 +999,7 @@ static int make_tmap_w_tiled(CUtensorMap* tm, const void* ptr, int N, int K) {
 
 extern "C" int ll_gemm_bf16_small_m_ex(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc,
                                        const bf16* bias, int M, int N, int K, int splits, float* ws,
-                                       size_t ws_floats, int* tickets, int* err, int w_tiled, cudaStream_t stream);
+                                       size_t ws_floats, int* tickets, int* err, int flags, cudaStream_t stream);
 
 // Small-M path.  ws must hold splits*M*N floats, tickets ceil(N/128) ints
 // (zero-initialised once; the kernel leaves them zero).  splits <= 0 picks a
@@ -985,14 +1011,18 @@ extern "C" int ll_gemm_bf16_small_m(const bf16* A, int lda, const bf16* W, int l
                                  stream);
 }
 
-// Same, with `w_tiled` = 1 for tile-major W (N % 128 == 0, K % 64 == 0).
+// Same, with flags: LL_SMALL_M_W_TILED for tile-major W (N % 128 == 0,
+// K % 64 == 0); LL_SMALL_M_SWIGLU to write silu(gate) * up of the
+// interleaved gate/up product (C: M x N/2; N % 32 == 0).
 extern "C" int ll_gemm_bf16_small_m_ex(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc,
                                        const bf16* bias, int M, int N, int K, int splits, float* ws,
-                                       size_t ws_floats, int* tickets, int* err, int w_tiled, cudaStream_t stream) {
+                                       size_t ws_floats, int* tickets, int* err, int flags, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if (M > 128) return -3;
   if ((K % 8) || (lda % 8) || (ldw % 8)) return -3;
+  const int w_tiled = flags & LL_SMALL_M_W_TILED;
   if (w_tiled && ((N % 128) || (K % 64))) return -3;
+  if ((flags & LL_SMALL_M_SWIGLU) && (N % 32)) return -3;
   const int ntiles = (N + GEMM_BM - 1) / GEMM_BM;
   const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
   if (splits <= 0) splits = ll_gemm_small_m_splits(N, K);
@@ -1014,7 +1044,7 @@ extern "C" int ll_gemm_bf16_small_m_ex(const bf16* A, int lda, const bf16* W, in
       init = true;                                                                                       \
     }                                                                                                    \
     launch_pdl(kern, grid, dim3(192), SwapCfg<BNX_>::SMEM, stream, tW, tX, C, bias, M, N, K, ldc, kb_per, ws, \
-               tickets, err, w_tiled);                                                                   \
+               tickets, err, flags);                                                                     \
   } while (0)
   switch (BNX) {
     case 16: LL_LAUNCH_S(16); break;

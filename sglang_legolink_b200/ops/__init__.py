@@ -114,12 +114,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None
     if out is None:
         out = torch.empty(M, N // 2 if swiglu_epilogue else N, dtype=x.dtype, device=x.device)
     if M <= SMALL_M_MAX and not (M > 64 and N >= 148 * 256):
-        if swiglu_epilogue:
-            tmp = torch.empty(M, N, dtype=x.dtype, device=x.device)
-            _small_m(ext, ws, x, w, bias, tmp)
-            ext.swiglu(out, tmp)
-        else:
-            _small_m(ext, ws, x, w, bias, out)
+        _small_m(ext, ws, x, w, bias, out, swiglu_epilogue)
         return out
     bn = 256 if N >= 2048 else 128
     ext.gemm(x, w, bias, out, 1 if swiglu_epilogue else 0, bn, ws.err)
@@ -139,7 +134,7 @@ def untile_weight(wt: torch.Tensor) -> torch.Tensor:
     return wt.permute(0, 2, 1, 3).reshape(a * c, b * d)
 
 
-def _small_m(ext, ws, x, w, bias, out):
+def _small_m(ext, ws, x, w, bias, out, swiglu: bool = False):
     M, K = x.shape
     N = w.shape[0] * 128 if w.dim() == 4 else w.shape[0]
     splits = ext.gemm_small_m_splits(N, K)
@@ -149,7 +144,7 @@ def _small_m(ext, ws, x, w, bias, out):
             if torch.cuda.is_current_stream_capturing():
                 raise RuntimeError("GEMM workspace too small during CUDA graph capture; reserve it first")
             ws.reserve_gemm(need, (N + 127) // 128)
-    ext.gemm_small_m(x, w, bias, out, splits, ws.gemm_ws, ws.tickets, ws.err)
+    ext.gemm_small_m(x, w, bias, out, splits, ws.gemm_ws, ws.tickets, ws.err, swiglu)
 
 
 def ref_swiglu_interleaved(gu: torch.Tensor) -> torch.Tensor:

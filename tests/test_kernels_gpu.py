@@ -56,6 +56,28 @@ def test_gemm_swiglu_epilogue():
     assert _rel(out, exp) < 1e-2
 
 
+@pytest.mark.parametrize("M", [1, 7, 64])
+@pytest.mark.parametrize("splits", [1, 0])
+def test_gemm_small_m_swiglu_epilogue(M, splits):
+    """SwiGLU applied in the small-M GEMM's own epilogue (one split) and in
+    its split-K fix-up (auto splits) against fp32 silu(a.gate^T) * a.up^T."""
+    torch.manual_seed(4)
+    I, K = 1024, 1536
+    a = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    gate = torch.randn(I, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    up = torch.randn(I, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    gu = ops.interleave_gate_up(gate, up)
+    ws = ops.workspace(DEV)
+    ws.reserve_gemm(32 * M * 2 * I, 2 * I // 128)
+    out = torch.empty(M, I, device=DEV, dtype=torch.bfloat16)
+    ops._cuda().gemm_small_m(a, gu, None, out, splits, ws.gemm_ws, ws.tickets, ws.err, True)
+    torch.cuda.synchronize()
+    assert ops.check_errors(DEV) == 0
+    exp = torch.nn.functional.silu(a.float() @ gate.float().t()) * (a.float() @ up.float().t())
+    assert _rel(out, exp) < 1e-2
+    assert torch.equal(ops.linear(a, gu, swiglu_epilogue=True), out) or splits == 1
+
+
 @pytest.mark.parametrize("M", [1, 3, 16, 17, 64, 100, 128])
 @pytest.mark.parametrize("N,K", [(4608, 3584), (3584, 18944), (1000, 512)])
 def test_gemm_small_m(M, N, K):
