@@ -75,22 +75,27 @@ def main():
     ops.workspace(dev).reserve_decode(hq, nsplit, D)
     for lw in m.layers[:1]:  # reserve GEMM workspaces outside capture
         ops.linear(x, lw.gu_w, out=gu)
+        ops.linear(x, lw.qkv_w, out=qkv)
     scale = 1.0 / math.sqrt(D)
     pk = peaks()
     kvb = n * hkv * D * 2 * 2
+    # the five kernels of the fused decode layer (QwenModel._forward_decode_fused)
+    eps = cfg.rms_norm_eps
+    ss = torch.full((1,), float(H), device=dev)
+    sq = torch.zeros(1, device=dev)
+    hp = torch.empty(1, H, device=dev, dtype=torch.bfloat16)
     cases = {
-        "rmsnorm_add": (lambda: [ops.fused_add_rmsnorm(x, res, lw.in_norm, cfg.rms_norm_eps) for lw in m.layers],
-                        4 * H * 2),
-        "gemv_qkv": (lambda: [ops.linear(x, lw.qkv_w, lw.qkv_b, out=qkv) for lw in m.layers],
-                     m.layers[0].qkv_w.numel() * 2),
-        "rope_qkv_write": (lambda: [ops.rope_qkv_write(qkv, pos, slot, m.cos_sin, q, kpool[i], vpool[i], hq, hkv, D)
-                                    for i in range(L)], qkv.numel() * 4),
+        "gemv_qkv_rope": (lambda: [ops.gemv_qkv_rope(x, lw.qkv_w, lw.qkv_b, pos, slot, m.cos_sin, q, kpool[i],
+                                                     vpool[i], hq, hkv, lw.q_norm, lw.k_norm, eps, scale_sumsq=ss)
+                                   for i, lw in enumerate(m.layers)], m.layers[0].qkv_w.numel() * 2),
         "attn_decode": (lambda: [ops.attention_decode(q, kpool[i], vpool[i], pt, kvl, scale, nsplit=nsplit, out=attn)
                                  for i in range(L)], kvb),
-        "gemv_o_proj": (lambda: [ops.linear(attn, lw.o_w, out=o) for lw in m.layers], m.layers[0].o_w.numel() * 2),
-        "gemv_gate_up_swiglu": (lambda: [ops.linear(x, lw.gu_w, out=mlp, swiglu_epilogue=True) for lw in m.layers],
-                                m.layers[0].gu_w.numel() * 2),
-        "gemv_down": (lambda: [ops.linear(mlp, lw.down_w, out=o) for lw in m.layers], m.layers[0].down_w.numel() * 2),
+        "gemv_o_proj_residual": (lambda: [ops.gemv_residual(attn, lw.o_w, res, lw.post_norm, hp, sq, eps=eps)
+                                          for lw in m.layers], m.layers[0].o_w.numel() * 2),
+        "gemv_gate_up_swiglu": (lambda: [ops.gemv_rownorm(hp, lw.gu_w, None, ss, eps, out=mlp, swiglu=True)
+                                         for lw in m.layers], m.layers[0].gu_w.numel() * 2),
+        "gemv_down_residual": (lambda: [ops.gemv_residual(mlp, lw.down_w, res, lw.in_norm, x, sq, eps=eps)
+                                        for lw in m.layers], m.layers[0].down_w.numel() * 2),
     }
     total = 0.0
     for name, (fn, bytes_per_layer) in cases.items():

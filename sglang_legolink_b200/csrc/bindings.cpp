@@ -8,6 +8,7 @@
 
 using bf16 = __nv_bfloat16;
 
+#include "gemm_epi.h"
 #include "tp_fused.h"
 
 extern "C" {
@@ -185,6 +186,94 @@ void gemm_small_m(const at::Tensor& a, const at::Tensor& w, const c10::optional<
 
 int64_t gemm_small_m_splits(int64_t N, int64_t K) { return ll_gemm_small_m_splits((int)N, (int)K); }
 
+template <typename T>
+static T* opt_ptr(const c10::optional<at::Tensor>& t) {
+  return t.has_value() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+// Small-M GEMM with a decode-layer epilogue (gemm_epi.h): mode 0 store,
+// 1 SwiGLU, 2 residual + norm weight + row sum of squares, 3 qkv heads with
+// QK-norm, RoPE and the KV write.  scale_sumsq: rows' sums of squares of an
+// unnormalised input (RMSNorm applied after the product).
+void gemm_small_m_epi(const at::Tensor& a, const at::Tensor& w, const c10::optional<at::Tensor>& bias,
+                      const c10::optional<at::Tensor>& out, int64_t splits, at::Tensor& ws, at::Tensor& tickets,
+                      const at::Tensor& err, int64_t mode, const c10::optional<at::Tensor>& scale_sumsq,
+                      double scale_eps, const c10::optional<at::Tensor>& res, const c10::optional<at::Tensor>& norm_w,
+                      const c10::optional<at::Tensor>& h_out, const c10::optional<at::Tensor>& sumsq_out,
+                      const c10::optional<at::Tensor>& positions, const c10::optional<at::Tensor>& slots,
+                      const c10::optional<at::Tensor>& cos_sin, const c10::optional<at::Tensor>& q_out,
+                      const c10::optional<at::Tensor>& k_pool_l, const c10::optional<at::Tensor>& v_pool_l,
+                      const c10::optional<at::Tensor>& q_norm_w, const c10::optional<at::Tensor>& k_norm_w,
+                      int64_t Hq, int64_t Hkv, int64_t page_size, double eps) {
+  CHECK_CUDA(a); CHECK_BF16(a); CHECK_BF16(w); CHECK_CONTIG(w); CHECK_F32(ws); CHECK_I32(tickets);
+  TORCH_CHECK(a.stride(1) == 1);
+  const bool tiled = w.dim() == 4;
+  const int M = a.size(0), K = a.size(1);
+  const int N = tiled ? (int)(w.size(0) * 128) : (int)w.size(0);
+  if (tiled) {
+    TORCH_CHECK(w.size(2) == 128 && w.size(3) == 64 && w.size(1) * 64 == K, "bad tile-major weight shape");
+  } else {
+    TORCH_CHECK(w.size(1) == K);
+  }
+  LLSmallMEpi e{};
+  e.mode = (int)mode;
+  if (scale_sumsq.has_value()) {
+    CHECK_F32(*scale_sumsq);
+    TORCH_CHECK(scale_sumsq->numel() >= M);
+  }
+  e.scale_sumsq = opt_ptr<const float>(scale_sumsq);
+  e.scale_eps = (float)scale_eps;
+  int ldc = 0;
+  if (mode == LL_EPI_STORE || mode == LL_EPI_SWIGLU) {
+    TORCH_CHECK(out.has_value(), "this epilogue writes `out`");
+    CHECK_BF16(*out);
+    TORCH_CHECK(out->stride(1) == 1 && out->size(0) == M && out->size(1) == (mode == LL_EPI_SWIGLU ? N / 2 : N));
+    ldc = out->stride(0);
+  } else if (mode == LL_EPI_RESIDUAL) {
+    TORCH_CHECK(res.has_value() && norm_w.has_value() && h_out.has_value() && sumsq_out.has_value());
+    CHECK_BF16(*res); CHECK_BF16(*norm_w); CHECK_BF16(*h_out); CHECK_F32(*sumsq_out);
+    TORCH_CHECK(res->size(0) == M && res->size(1) == N && res->stride(1) == 1 && h_out->sizes() == res->sizes() &&
+                h_out->strides() == res->strides() && norm_w->numel() == N && sumsq_out->numel() >= M);
+    e.res = opt_ptr<ll_bf16_t>(res);
+    e.norm_w = opt_ptr<const ll_bf16_t>(norm_w);
+    e.h_out = opt_ptr<ll_bf16_t>(h_out);
+    e.sumsq_out = opt_ptr<float>(sumsq_out);
+    e.ld = res->stride(0);
+  } else if (mode == LL_EPI_QKV_ROPE) {
+    TORCH_CHECK(positions.has_value() && slots.has_value() && cos_sin.has_value() && q_out.has_value() &&
+                k_pool_l.has_value() && v_pool_l.has_value());
+    CHECK_I32(*positions); CHECK_I64(*slots); CHECK_F32(*cos_sin); CHECK_BF16(*q_out); CHECK_BF16(*k_pool_l);
+    CHECK_BF16(*v_pool_l); CHECK_CONTIG(*q_out); CHECK_CONTIG(*k_pool_l); CHECK_CONTIG(*v_pool_l);
+    CHECK_CONTIG(*cos_sin);
+    TORCH_CHECK(cos_sin->size(-1) == 128 && q_out->numel() >= (int64_t)M * Hq * 128 && positions->numel() >= M &&
+                slots->numel() >= M);
+    TORCH_CHECK(k_pool_l->size(-1) == 128 && k_pool_l->size(-3) == Hkv && k_pool_l->size(-2) == page_size);
+    if (q_norm_w.has_value()) CHECK_BF16(*q_norm_w);
+    if (k_norm_w.has_value()) CHECK_BF16(*k_norm_w);
+    e.positions = opt_ptr<const int>(positions);
+    e.slots = opt_ptr<const int64_t>(slots);
+    e.cos_sin = opt_ptr<const float>(cos_sin);
+    e.q_out = opt_ptr<ll_bf16_t>(q_out);
+    e.k_pool = opt_ptr<ll_bf16_t>(k_pool_l);
+    e.v_pool = opt_ptr<ll_bf16_t>(v_pool_l);
+    e.q_norm_w = opt_ptr<const ll_bf16_t>(q_norm_w);
+    e.k_norm_w = opt_ptr<const ll_bf16_t>(k_norm_w);
+    e.Hq = (int)Hq;
+    e.Hkv = (int)Hkv;
+    e.page_size = (int)page_size;
+    e.eps = (float)eps;
+  } else {
+    TORCH_CHECK(false, "unknown epilogue mode");
+  }
+  c10::cuda::CUDAGuard g(a.device());
+  check_rc(ll_gemm_bf16_small_m_epi(a.data_ptr(), a.stride(0), w.data_ptr(), tiled ? K : (int)w.stride(0),
+                                    out.has_value() ? out->data_ptr() : nullptr, ldc,
+                                    bias.has_value() ? bias->data_ptr() : nullptr, M, N, K, (int)splits,
+                                    ws.data_ptr<float>(), (size_t)ws.numel(), tickets.data_ptr<int>(),
+                                    err.data_ptr<int>(), tiled ? 1 : 0, &e, cur_stream()),
+           "ll_gemm_bf16_small_m_epi");
+}
+
 void rmsnorm(at::Tensor& out, const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w,
              double eps) {
   CHECK_CUDA(x); CHECK_BF16(x); CHECK_BF16(out); CHECK_BF16(w); CHECK_CONTIG(x); CHECK_CONTIG(out);
@@ -313,6 +402,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm);
   m.def("gemm_small_m", &gemm_small_m);
   m.def("gemm_small_m_splits", &gemm_small_m_splits);
+  m.def("gemm_small_m_epi", &gemm_small_m_epi);
   m.def("rmsnorm", &rmsnorm);
   m.def("rope_qkv_write", &rope_qkv_write);
   m.def("kv_link_rope", &kv_link_rope);

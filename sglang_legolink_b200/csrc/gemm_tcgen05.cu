@@ -30,6 +30,7 @@
 #include <unordered_map>
 
 #include "common.cuh"
+#include "gemm_epi.h"
 #include "tp_fused.h"
 
 namespace ll {
@@ -55,6 +56,20 @@ struct GemmCfg {
 };
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16(x)); }
+// Named barrier 1 over the 128 epilogue threads (warps 2-5).
+__device__ __forceinline__ void bar_sync_128() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Same barrier, returning whether `p` held in all 128 threads.
+__device__ __forceinline__ bool bar_and_128(bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred pi, po;\n setp.ne.u32 pi, %1, 0;\n bar.red.and.pred po, 1, 128, pi;\n"
+      " selp.u32 %0, 1, 0, po;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)p)
+      : "memory");
+  return r != 0;
+}
 
 // Tile order: groups of GEMM_GROUP_M m-blocks, m fastest inside a group, so
 // the tiles in flight at once (one per SM or SM pair) share a few A row
@@ -287,14 +302,8 @@ __global__ void __launch_bounds__(192, 2)
     gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                        bf16* __restrict__ C, const bf16* __restrict__ bias, int M, int N, int K, int ldc,
                        int kb_per_split, float* __restrict__ ws, int* __restrict__ tickets, int* err,
-                       int flags) {
+                       int w_tiled, const __grid_constant__ LLSmallMEpi epi) {
   using Cfg = SwapCfg<BNX>;
-  const int w_tiled = flags & LL_SMALL_M_W_TILED;
-  // SwiGLU epilogue: features are gate/up interleaved in groups of 16 (lanes
-  // 0-15 of a warp hold gate features, lanes 16-31 the matching up
-  // features); C then has N / 2 columns.  N % 32 == 0, so a warp is wholly
-  // inside or outside N.
-  const bool swiglu = (flags & LL_SMALL_M_SWIGLU) != 0;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -305,6 +314,8 @@ __global__ void __launch_bounds__(192, 2)
   uint64_t* tfull = empty + STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
   __shared__ int s_last;
+  __shared__ float s_head[GEMM_BM];  // LL_EPI_QKV_ROPE: one row of the head (rotate-half partner exchange)
+  __shared__ float s_red[4];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = blockIdx.x;  // feature tile
@@ -396,12 +407,100 @@ __global__ void __launch_bounds__(192, 2)
     __syncwarp();
   } else {
     const int q = warp & 3;
-    const int feat = nb * GEMM_BM + q * 32 + lane;  // output column of C
+    const int f = q * 32 + lane;             // feature within the tile
+    const int feat = nb * GEMM_BM + f;       // output column of C
     pdl_wait();  // outputs / workspace may still be in use by the previous kernel
-    bool ok = mbar_wait(tfull, 0, err, kErrTmemFullTimeout);
+    // Epilogue operands that do not depend on this product are loaded now,
+    // while the main loop runs: per-row scalars in lane `row` (rows < 32,
+    // read back with a shuffle), per-feature values and row 0's per-element
+    // values in registers.  Other rows load at use.
+    float pf_rstd = 1.f;
+    if (epi.scale_sumsq != nullptr && lane < M)
+      pf_rstd = rsqrtf(__ldcg(epi.scale_sumsq + lane) / (float)K + epi.scale_eps);
+    const float pf_bias = (bias != nullptr && feat < N) ? __bfloat162float(bias[feat]) : 0.f;
+    float pf_res0 = 0.f, pf_w = 0.f, pf_c0 = 0.f, pf_s0 = 0.f;
+    int pf_pos = 0;
+    int64_t pf_slot = 0;
+    if (epi.mode == LL_EPI_RESIDUAL && feat < N) {
+      pf_res0 = __bfloat162float(epi.res[feat]);
+      pf_w = __bfloat162float(epi.norm_w[feat]);
+    } else if (epi.mode == LL_EPI_QKV_ROPE) {
+      if (lane < M) {
+        pf_pos = epi.positions[lane];
+        pf_slot = epi.slots[lane];
+      }
+      const int p0 = __shfl_sync(0xffffffffu, pf_pos, 0);
+      pf_c0 = epi.cos_sin[(size_t)p0 * 128 + (f & 63)];
+      pf_s0 = epi.cos_sin[(size_t)p0 * 128 + 64 + (f & 63)];
+      const bf16* nw = nb < epi.Hq ? epi.q_norm_w : (nb < epi.Hq + epi.Hkv ? epi.k_norm_w : nullptr);
+      if (nw != nullptr) pf_w = __bfloat162float(nw[f]);
+    }
+    // The four epilogue warps agree on `ok`: the epilogues below use named
+    // barriers, which every one of the 128 threads must reach.
+    const bool ok = bar_and_128(mbar_wait(tfull, 0, err, kErrTmemFullTimeout));
     tc_fence_after();
     const bool empty_split = (kb1 <= kb0);
     const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16);
+    // Final value of (row m, feature feat), called by all 128 threads for
+    // the same m.  Features past N (N % 32 == 0: whole warps) store nothing.
+    auto emit = [&](int m, float v) {
+      if (epi.scale_sumsq != nullptr) {
+        const float rs = __shfl_sync(0xffffffffu, pf_rstd, m & 31);
+        v *= m < 32 ? rs : rsqrtf(__ldcg(epi.scale_sumsq + m) / (float)K + epi.scale_eps);
+      }
+      v += pf_bias;
+      if (epi.mode == LL_EPI_STORE) {
+        if (feat < N) C[(size_t)m * ldc + feat] = __float2bfloat16(v);
+      } else if (epi.mode == LL_EPI_SWIGLU) {
+        // gate/up interleaved in groups of 16: lanes 0-15 hold gate
+        // features, lanes 16-31 the matching up features
+        const float u = __shfl_down_sync(0xffffffffu, v, 16);
+        if (lane < 16 && feat < N) C[(size_t)m * ldc + (feat >> 5) * 16 + lane] = __float2bfloat16(silu_f(v) * u);
+      } else if (epi.mode == LL_EPI_RESIDUAL) {
+        float r = 0.f;
+        if (feat < N) {
+          const size_t i = (size_t)m * epi.ld + feat;
+          r = bf16_round(v) + (m == 0 ? pf_res0 : __bfloat162float(epi.res[i]));
+          epi.res[i] = __float2bfloat16(r);
+          epi.h_out[i] = __float2bfloat16(r * pf_w);
+        }
+        const float ss = warp_sum(r * r);
+        if (lane == 0) atomicAdd(epi.sumsq_out + m, ss);
+      } else {  // LL_EPI_QKV_ROPE: this tile is head nb of [Hq | Hkv keys | Hkv values]
+        float x = bf16_round(v);
+        const int64_t sl = __shfl_sync(0xffffffffu, pf_slot, m & 31);
+        const int64_t slot = m < 32 ? sl : epi.slots[m];
+        const int64_t page = slot / epi.page_size, off = slot % epi.page_size;
+        bf16* dst;
+        if (nb < epi.Hq + epi.Hkv) {
+          const bf16* nw = nb < epi.Hq ? epi.q_norm_w : epi.k_norm_w;
+          if (nw != nullptr) {
+            const float ss = warp_sum(x * x);
+            if (lane == 0) s_red[q] = ss;
+            bar_sync_128();
+            const float tot = (s_red[0] + s_red[1]) + (s_red[2] + s_red[3]);
+            x = x * rsqrtf(tot / 128.f + epi.eps) * pf_w;
+          }
+          s_head[f] = x;
+          bar_sync_128();
+          const int j = f & 63;
+          float c = pf_c0, sn = pf_s0;
+          if (m > 0) {
+            const int pm = __shfl_sync(0xffffffffu, pf_pos, m & 31);
+            const float* cs = epi.cos_sin + (size_t)(m < 32 ? pm : epi.positions[m]) * 128;
+            c = cs[j];
+            sn = cs[64 + j];
+          }
+          x = f < 64 ? x * c - s_head[f + 64] * sn : x * c + s_head[f - 64] * sn;
+          bar_sync_128();  // s_head / s_red are free for the next row
+          dst = nb < epi.Hq ? epi.q_out + ((size_t)m * epi.Hq + nb) * 128
+                            : epi.k_pool + (((size_t)page * epi.Hkv + (nb - epi.Hq)) * epi.page_size + off) * 128;
+        } else {
+          dst = epi.v_pool + (((size_t)page * epi.Hkv + (nb - epi.Hq - epi.Hkv)) * epi.page_size + off) * 128;
+        }
+        dst[f] = __float2bfloat16(x);
+      }
+    };
 #pragma unroll 1
     for (int c = 0; c < BNX; c += 32) {
       uint32_t r[32];
@@ -413,25 +512,8 @@ __global__ void __launch_bounds__(192, 2)
       tmem_ld_wait();
       if (!ok) continue;
       const int ncols = BNX < 32 ? BNX : 32;
-      if (nsplit == 1 && swiglu) {
-        if (feat < N) {
-          const float b = bias != nullptr ? __bfloat162float(bias[feat]) : 0.f;
-          const int ocol = (feat >> 5) * 16 + (lane & 15);
-          for (int i = 0; i < ncols; ++i) {
-            const int m = c + i;
-            const float v = __uint_as_float(r[i]) + b;
-            const float u = __shfl_down_sync(0xffffffffu, v, 16);
-            if (lane < 16 && m < M) C[(size_t)m * ldc + ocol] = __float2bfloat16(silu_f(v) * u);
-          }
-        }
-      } else if (nsplit == 1) {
-        if (feat < N) {
-          const float b = bias != nullptr ? __bfloat162float(bias[feat]) : 0.f;
-          for (int i = 0; i < ncols; ++i) {
-            const int m = c + i;
-            if (m < M) C[(size_t)m * ldc + feat] = __float2bfloat16(__uint_as_float(r[i]) + b);
-          }
-        }
+      if (nsplit == 1) {
+        for (int i = 0; i < ncols && c + i < M; ++i) emit(c + i, __uint_as_float(r[i]));
       } else if (feat < N) {
         float* w = ws + ((size_t)split * M) * N;
         for (int i = 0; i < ncols; ++i) {
@@ -443,27 +525,27 @@ __global__ void __launch_bounds__(192, 2)
     if (nsplit > 1) {
       // Split-K fix-up: the last CTA of this feature tile reduces all splits.
       __threadfence();
-      asm volatile("bar.sync 1, 128;");
+      bar_sync_128();
       if (threadIdx.x == 64) {
         const int prev = atomicAdd(&tickets[nb], 1);
         s_last = (prev == nsplit - 1);
       }
-      asm volatile("bar.sync 1, 128;");
+      bar_sync_128();
       if (s_last) {
         __threadfence();
-        if (feat < N) {
-          const float b = bias != nullptr ? __bfloat162float(bias[feat]) : 0.f;
-          const int ocol = (feat >> 5) * 16 + (lane & 15);
-          for (int m = 0; m < M; ++m) {
-            float s = b;
-            for (int sp = 0; sp < nsplit; ++sp) s += __ldcg(ws + ((size_t)sp * M + m) * N + feat);
-            if (swiglu) {
-              const float u = __shfl_down_sync(0xffffffffu, s, 16);
-              if (lane < 16) C[(size_t)m * ldc + ocol] = __float2bfloat16(silu_f(s) * u);
-            } else {
-              C[(size_t)m * ldc + feat] = __float2bfloat16(s);
-            }
-          }
+        for (int m = 0; m < M; ++m) {
+          // all partials in flight at once, then summed in split order
+          float part[16];
+          const float* src = ws + (size_t)m * N + feat;
+          const size_t sstride = (size_t)M * N;
+#pragma unroll
+          for (int sp = 0; sp < 16; ++sp) part[sp] = (sp < nsplit && feat < N) ? __ldcg(src + sp * sstride) : 0.f;
+          float sum = 0.f;
+#pragma unroll
+          for (int sp = 0; sp < 16; ++sp) sum += part[sp];
+          for (int sp = 16; sp < nsplit; ++sp)
+            if (feat < N) sum += __ldcg(src + sp * sstride);
+          if (ok) emit(m, sum);
         }
         if (threadIdx.x == 64) tickets[nb] = 0;  // ready for the next launch / graph replay
       }
@@ -1011,18 +1093,34 @@ extern "C" int ll_gemm_bf16_small_m(const bf16* A, int lda, const bf16* W, int l
                                  stream);
 }
 
-// Same, with flags: LL_SMALL_M_W_TILED for tile-major W (N % 128 == 0,
-// K % 64 == 0); LL_SMALL_M_SWIGLU to write silu(gate) * up of the
-// interleaved gate/up product (C: M x N/2; N % 32 == 0).
-extern "C" int ll_gemm_bf16_small_m_ex(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc,
-                                       const bf16* bias, int M, int N, int K, int splits, float* ws,
-                                       size_t ws_floats, int* tickets, int* err, int flags, cudaStream_t stream) {
+static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc, const bf16* bias, int M,
+                          int N, int K, int splits, float* ws, size_t ws_floats, int* tickets, int* err, int w_tiled,
+                          const LLSmallMEpi& epi, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   if (M > 128) return -3;
   if ((K % 8) || (lda % 8) || (ldw % 8)) return -3;
-  const int w_tiled = flags & LL_SMALL_M_W_TILED;
   if (w_tiled && ((N % 128) || (K % 64))) return -3;
-  if ((flags & LL_SMALL_M_SWIGLU) && (N % 32)) return -3;
+  switch (epi.mode) {
+    case LL_EPI_STORE:
+      if (C == nullptr) return -3;
+      break;
+    case LL_EPI_SWIGLU:
+      if (C == nullptr || (N % 32)) return -3;
+      break;
+    case LL_EPI_RESIDUAL:
+      if ((N % 32) || epi.res == nullptr || epi.norm_w == nullptr || epi.h_out == nullptr ||
+          epi.sumsq_out == nullptr || epi.ld < N)
+        return -3;
+      break;
+    case LL_EPI_QKV_ROPE:
+      if (N != (epi.Hq + 2 * epi.Hkv) * GEMM_BM || epi.Hq <= 0 || epi.Hkv <= 0 || epi.page_size <= 0 ||
+          epi.positions == nullptr || epi.slots == nullptr || epi.cos_sin == nullptr || epi.q_out == nullptr ||
+          epi.k_pool == nullptr || epi.v_pool == nullptr)
+        return -3;
+      break;
+    default:
+      return -3;
+  }
   const int ntiles = (N + GEMM_BM - 1) / GEMM_BM;
   const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
   if (splits <= 0) splits = ll_gemm_small_m_splits(N, K);
@@ -1044,7 +1142,7 @@ extern "C" int ll_gemm_bf16_small_m_ex(const bf16* A, int lda, const bf16* W, in
       init = true;                                                                                       \
     }                                                                                                    \
     launch_pdl(kern, grid, dim3(192), SwapCfg<BNX_>::SMEM, stream, tW, tX, C, bias, M, N, K, ldc, kb_per, ws, \
-               tickets, err, flags);                                                                     \
+               tickets, err, w_tiled, epi);                                                              \
   } while (0)
   switch (BNX) {
     case 16: LL_LAUNCH_S(16); break;
@@ -1054,6 +1152,28 @@ extern "C" int ll_gemm_bf16_small_m_ex(const bf16* A, int lda, const bf16* W, in
   }
 #undef LL_LAUNCH_S
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+// Same, with flags: LL_SMALL_M_W_TILED for tile-major W (N % 128 == 0,
+// K % 64 == 0); LL_SMALL_M_SWIGLU to write silu(gate) * up of the
+// interleaved gate/up product (C: M x N/2; N % 32 == 0).
+extern "C" int ll_gemm_bf16_small_m_ex(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc,
+                                       const bf16* bias, int M, int N, int K, int splits, float* ws,
+                                       size_t ws_floats, int* tickets, int* err, int flags, cudaStream_t stream) {
+  LLSmallMEpi epi{};
+  epi.mode = (flags & LL_SMALL_M_SWIGLU) ? LL_EPI_SWIGLU : LL_EPI_STORE;
+  return small_m_launch(A, lda, W, ldw, C, ldc, bias, M, N, K, splits, ws, ws_floats, tickets, err,
+                        flags & LL_SMALL_M_W_TILED, epi, stream);
+}
+
+extern "C" int ll_gemm_bf16_small_m_epi(const void* A, int lda, const void* W, int ldw, void* C, int ldc,
+                                        const void* bias, int M, int N, int K, int splits, float* ws,
+                                        size_t ws_floats, int* tickets, int* err, int w_tiled,
+                                        const LLSmallMEpi* epi, void* stream) {
+  if (epi == nullptr) return -3;
+  return small_m_launch(static_cast<const bf16*>(A), lda, static_cast<const bf16*>(W), ldw, static_cast<bf16*>(C),
+                        ldc, static_cast<const bf16*>(bias), M, N, K, splits, ws, ws_floats, tickets, err, w_tiled,
+                        *epi, static_cast<cudaStream_t>(stream));
 }
 
 // Split count that keeps the grid within one wave of resident CTAs (two per

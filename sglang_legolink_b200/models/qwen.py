@@ -221,6 +221,8 @@ class QwenModel:
         if (fb.mode == "extend" and getattr(self.comm, "name", "") == "fused" and fb.input_ids.is_cuda
                 and self.comm.use_fused(T)):
             return self._forward_fused_tp(fb, kv, return_hidden)
+        if fb.mode == "decode" and not return_hidden and self._decode_fusable(T):
+            return self._forward_decode_fused(fb, kv)
         H, D = c.hidden_size, c.head_dim
         qkv_n = (self.hq + 2 * self.hkv) * D
         x = ops.embedding(fb.input_ids, self.embed, out=self._buf("x", (T, H)))
@@ -258,6 +260,49 @@ class QwenModel:
         if return_hidden:
             return rows
         return self.logits(rows)
+
+    def _decode_fusable(self, T: int) -> bool:
+        return (self.embed.is_cuda and (self.tp_size == 1 or self.comm is None) and T <= ops.SMALL_M_MAX
+                and self.cfg.head_dim == 128 and self.cfg.rotary_dim == 128 and self.cfg.hidden_size % 32 == 0)
+
+    def _forward_decode_fused(self, fb: ForwardBatch, kv) -> torch.Tensor:
+        """Decode step as five kernels per layer: the qkv GEMV writes Q and
+        the new K/V (per-head norm and RoPE in its stores), attention, and
+        three GEMVs whose stores add the residual and produce the next
+        RMSNorm's input ``residual * norm_weight`` with the rows' sums of
+        squares; the GEMV that reads it applies the ``rsqrt`` row scale.
+        Same math as :meth:`forward` with the norm's scale moved after the
+        product (reference layer order:
+        patched_sglang_files/python/sglang/srt/models/qwen2.py:170-200)."""
+        c = self.cfg
+        T = fb.num_rows
+        H, D, L = c.hidden_size, c.head_dim, len(self.layers)
+        eps = c.rms_norm_eps
+        x = ops.embedding(fb.input_ids, self.embed, out=self._buf("x", (T, H)))
+        residual = self._buf("res", (T, H))
+        residual.copy_(x)
+        h = self._buf("h", (T, H))
+        ops.rmsnorm(residual, self.layers[0].in_norm, eps, out=h)
+        hp = self._buf("hp", (T, H))
+        q = self._buf("q", (T, self.hq, D))
+        attn = self._buf("attn", (T, self.hq * D))
+        mlp = self._buf("mlp", (T, self.inter))
+        ss = self._buf("rowsq", (2 * L, T), torch.float32)
+        ss.zero_()
+        for li, lw in enumerate(self.layers):
+            ops.gemv_qkv_rope(h, lw.qkv_w, lw.qkv_b, fb.positions, fb.slots, self.cos_sin, q, kv.k[li], kv.v[li],
+                              self.hq, self.hkv, lw.q_norm, lw.k_norm, eps,
+                              scale_sumsq=ss[2 * li - 1] if li > 0 else None)
+            ops.attention_decode(q, kv.k[li], kv.v[li], fb.page_table, fb.kv_lens, self.scale,
+                                 nsplit=fb.decode_nsplit, out=attn)
+            ops.gemv_residual(attn, lw.o_w, residual, lw.post_norm, hp, ss[2 * li], eps=eps)
+            ops.gemv_rownorm(hp, lw.gu_w, None, ss[2 * li], eps, out=mlp, swiglu=True)
+            nxt = self.layers[li + 1].in_norm if li + 1 < L else self.final_norm
+            ops.gemv_residual(mlp, lw.down_w, residual, nxt, h, ss[2 * li + 1], eps=eps)
+        rows, sq = h, ss[2 * L - 1]
+        if fb.logit_rows is not None:
+            rows, sq = h.index_select(0, fb.logit_rows), sq.index_select(0, fb.logit_rows)
+        return ops.gemv_rownorm(rows, self.lm_head, None, sq, eps)
 
     def _forward_fused_tp(self, fb: ForwardBatch, kv, return_hidden: bool = False) -> torch.Tensor:
         """Extend forward with the TP reductions fused into the kernels

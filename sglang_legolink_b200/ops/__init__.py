@@ -25,7 +25,8 @@ from ._ext import ExtensionMissing, cuda as _cuda  # noqa: F401
 __all__ = [
     "ExtensionMissing", "linear", "rmsnorm", "fused_add_rmsnorm", "rope_qkv_write", "attention_prefill",
     "attention_decode", "swiglu", "embedding", "argmax", "kv_link_rope", "interleave_gate_up",
-    "deinterleave_gate_up", "prefill_tiles", "workspace", "check_errors",
+    "deinterleave_gate_up", "prefill_tiles", "workspace", "check_errors", "gemv_rownorm", "gemv_residual",
+    "gemv_qkv_rope",
 ]
 
 SMALL_M_MAX = 128
@@ -137,14 +138,95 @@ def untile_weight(wt: torch.Tensor) -> torch.Tensor:
 def _small_m(ext, ws, x, w, bias, out, swiglu: bool = False):
     M, K = x.shape
     N = w.shape[0] * 128 if w.dim() == 4 else w.shape[0]
-    splits = ext.gemm_small_m_splits(N, K)
+    ext.gemm_small_m(x, w, bias, out, _small_m_splits(ws, M, N, K), ws.gemm_ws, ws.tickets, ws.err, swiglu)
+
+
+EPI_STORE, EPI_SWIGLU, EPI_RESIDUAL, EPI_QKV_ROPE = 0, 1, 2, 3
+
+
+def _small_m_splits(ws, M: int, N: int, K: int) -> int:
+    splits = _cuda().gemm_small_m_splits(N, K)
     if splits > 1:
         need = splits * M * N
         if ws.gemm_ws.numel() < need or ws.tickets.numel() < (N + 127) // 128:
             if torch.cuda.is_current_stream_capturing():
                 raise RuntimeError("GEMM workspace too small during CUDA graph capture; reserve it first")
             ws.reserve_gemm(need, (N + 127) // 128)
-    ext.gemm_small_m(x, w, bias, out, splits, ws.gemm_ws, ws.tickets, ws.err, swiglu)
+    return splits
+
+
+def _row_rstd(sumsq: torch.Tensor, K: int, eps: float) -> torch.Tensor:
+    return torch.rsqrt(sumsq.float() / K + eps)
+
+
+def gemv_rownorm(x, w, bias, sumsq, eps: float, out=None, swiglu: bool = False):
+    """``(x @ w.T) * rsqrt(sumsq / K + eps)[:, None] + bias`` (SwiGLU of the
+    interleaved gate/up product with ``swiglu``): the GEMV of an input whose
+    RMSNorm scale is applied after the product (the producer wrote
+    ``residual * norm_weight`` and the rows' sums of squares).  Decode sizes
+    (M <= 128) only."""
+    M, K = x.shape
+    N = w.shape[0] * 128 if w.dim() == 4 else w.shape[0]
+    if out is None:
+        out = torch.empty(M, N // 2 if swiglu else N, dtype=x.dtype, device=x.device)
+    if not x.is_cuda:
+        y = x.float() @ w.float().t() * _row_rstd(sumsq[:M], K, eps)[:, None]
+        if bias is not None:
+            y = y + bias.float()
+        out.copy_(ref_swiglu_interleaved(y) if swiglu else y)
+        return out
+    ws = workspace(x.device)
+    _cuda().gemm_small_m_epi(x, w, bias, out, _small_m_splits(ws, M, N, K), ws.gemm_ws, ws.tickets, ws.err,
+                             EPI_SWIGLU if swiglu else EPI_STORE, sumsq, eps, None, None, None, None, None, None,
+                             None, None, None, None, None, None, 0, 0, 0, eps)
+    return out
+
+
+def gemv_residual(x, w, residual, norm_w, h_out, sumsq_out, scale_sumsq=None, eps: float = 1e-6):
+    """``y = x @ w.T``; ``r = bf16(y) + residual``; ``residual = bf16(r)``;
+    ``h_out = bf16(r * norm_w)``; ``sumsq_out[m] += sum(r[m]^2)`` (fp32
+    ``r``) -- the residual add and the data half of the next RMSNorm, done in
+    the GEMV's stores.  ``sumsq_out`` must be zero beforehand."""
+    M, K = x.shape
+    N = w.shape[0] * 128 if w.dim() == 4 else w.shape[0]
+    if not x.is_cuda:
+        y = x.float() @ w.float().t()
+        if scale_sumsq is not None:
+            y = y * _row_rstd(scale_sumsq[:M], K, eps)[:, None]
+        r = y.to(x.dtype).float() + residual.float()
+        residual.copy_(r)
+        h_out.copy_(r * norm_w.float())
+        sumsq_out[:M] += (r * r).sum(-1)
+        return h_out
+    ws = workspace(x.device)
+    _cuda().gemm_small_m_epi(x, w, None, None, _small_m_splits(ws, M, N, K), ws.gemm_ws, ws.tickets, ws.err,
+                             EPI_RESIDUAL, scale_sumsq, eps, residual, norm_w, h_out, sumsq_out, None, None, None,
+                             None, None, None, None, None, 0, 0, 0, eps)
+    return h_out
+
+
+def gemv_qkv_rope(x, w, bias, positions, slots, cos_sin, q_out, k_pool_l, v_pool_l, num_heads: int,
+                  num_kv_heads: int, q_norm_w=None, k_norm_w=None, eps: float = 1e-6, scale_sumsq=None):
+    """The qkv GEMV with :func:`rope_qkv_write` in its stores: one 128-wide
+    output tile is one head, so the tile's last CTA applies the head's
+    RMSNorm (Qwen3), RoPE, and writes Q to ``q_out`` and K/V to the pool
+    slot.  The qkv product is rounded to bf16 first, as when it is stored."""
+    M, K = x.shape
+    N = w.shape[0] * 128 if w.dim() == 4 else w.shape[0]
+    if not x.is_cuda:
+        y = x.float() @ w.float().t()
+        if scale_sumsq is not None:
+            y = y * _row_rstd(scale_sumsq[:M], K, eps)[:, None]
+        if bias is not None:
+            y = y + bias.float()
+        return rope_qkv_write(y.to(x.dtype), positions, slots, cos_sin, q_out, k_pool_l, v_pool_l, num_heads,
+                              num_kv_heads, 128, q_norm_w, k_norm_w, eps)
+    ws = workspace(x.device)
+    _cuda().gemm_small_m_epi(x, w, bias, None, _small_m_splits(ws, M, N, K), ws.gemm_ws, ws.tickets, ws.err,
+                             EPI_QKV_ROPE, scale_sumsq, eps, None, None, None, None, positions, slots, cos_sin,
+                             q_out, k_pool_l, v_pool_l, q_norm_w, k_norm_w, num_heads, num_kv_heads,
+                             k_pool_l.shape[-2], eps)
+    return q_out
 
 
 def ref_swiglu_interleaved(gu: torch.Tensor) -> torch.Tensor:

@@ -104,6 +104,9 @@ class KVPool:
         self.k = torch.zeros(shape, dtype=dtype, device=device)
         self.v = torch.zeros(shape, dtype=dtype, device=device)
         self.alloc = _ext.host().PageAllocator(num_pages)
+        # Held for the pool's lifetime: padded rows of a decode bucket write
+        # their K/V here (never into a live sequence's slot).
+        self.scratch_page = int(self.alloc.alloc(1)[0])
 
     @property
     def bytes(self) -> int:
@@ -575,10 +578,11 @@ class Engine:
             slots[b] = s.pages[s.length // ps] * ps + s.length % ps
             pt[b, : len(s.pages)] = torch.as_tensor(s.pages, dtype=torch.int32)
             kvl[b] = s.length + 1
-        # padded rows write into a scratch slot of page 0 of row 0 and attend to 1 key
+        # padded rows write into the pool's scratch page and attend to 1 key
+        # there; no live sequence's slot is touched
         for b in range(B, bucket):
-            pt[b, 0] = seqs[0].pages[0]
-            slots[b] = int(slots[0])
+            pt[b, 0] = self.kv.scratch_page
+            slots[b] = self.kv.scratch_page * ps
             pos[b] = 0
         return ids, pos, slots, pt, kvl
 
@@ -632,8 +636,8 @@ class Engine:
                           kv_lens=st["kvl"], logit_rows=None, decode_nsplit=nsplit)
         out = torch.zeros(bucket, dtype=torch.int32, device=dev)
         # warm-up (allocates the model's scratch buffers outside the graph).
-        # The padded rows' writes land on the slot row 0 is about to fill, so
-        # the real step below overwrites them.
+        # Row 0's writes land on the slot it is about to fill, so the real
+        # step below overwrites them.
         s = torch.cuda.Stream(device=dev)
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):

@@ -4,6 +4,7 @@
 import pytest
 import torch
 
+from sglang_legolink_b200 import ops
 from sglang_legolink_b200.models.config import PRESETS
 from sglang_legolink_b200.models.qwen import QwenModel
 from sglang_legolink_b200.runtime.engine import Engine
@@ -52,6 +53,44 @@ def test_batched_decode_matches_single():
     seqs = [eng.prefill(subs[i] + suffix) for i in range(4)]
     eng.decode(seqs, 8)
     for i in range(4):
+        s = eng.prefill(subs[i] + suffix)
+        eng.decode([s], 8)
+        assert s.output_ids == seqs[i].output_ids
+
+
+@pytest.mark.parametrize("name", ["small-qwen2", "small-qwen3"])
+def test_fused_decode_step_matches_unfused(name, monkeypatch):
+    """The five-kernel decode layer (norms, RoPE and KV write in the GEMV
+    stores) gives the logits and the new K/V of the unfused layer."""
+    from sglang_legolink_b200.models.qwen import ForwardBatch
+
+    cfg, eng, subs, suffix = _setup(name, seed=3)
+    seqs = [eng.prefill(subs[i] + suffix) for i in (0, 1, 2)]
+    ids, pos, slots, pt, kvl = eng._decode_inputs(seqs, 4, max(len(s.pages) for s in seqs))
+    dev = eng.device
+    fb = ForwardBatch(mode="decode", input_ids=ids.to(dev), positions=pos.to(dev), slots=slots.to(dev),
+                      q_indptr=torch.arange(5, dtype=torch.int32, device=dev), page_table=pt.to(dev),
+                      kv_lens=kvl.to(dev), logit_rows=None,
+                      decode_nsplit=ops.decode_splits(4, eng.model.hkv, int(kvl.max())))
+    ops.workspace(dev).reserve_decode(4 * eng.model.hq, fb.decode_nsplit)
+    assert eng.model._decode_fusable(4)
+    fused = eng.model.forward(fb, eng.kv).float()
+    kf = eng.kv.k[:, slots[0] // 16].clone()
+    monkeypatch.setattr(type(eng.model), "_decode_fusable", lambda self, T: False)
+    plain = eng.model.forward(fb, eng.kv).float()
+    kp = eng.kv.k[:, slots[0] // 16].clone()
+    for r in range(3):
+        assert ((fused[r] - plain[r]).norm() / plain[r].norm()).item() < 2e-2
+    assert ((kf.float() - kp.float()).norm() / kp.float().norm()).item() < 1e-2
+
+
+def test_padded_decode_bucket_keeps_row0_kv():
+    """Three sequences in the bucket of four: the padded row writes the
+    pool's scratch page, so every sequence decodes as it does alone."""
+    cfg, eng, subs, suffix = _setup("small-qwen2", seed=4)
+    seqs = [eng.prefill(subs[i] + suffix) for i in range(3)]
+    eng.decode(seqs, 8)
+    for i in range(3):
         s = eng.prefill(subs[i] + suffix)
         eng.decode([s], 8)
         assert s.output_ids == seqs[i].output_ids

@@ -78,6 +78,68 @@ def test_gemm_small_m_swiglu_epilogue(M, splits):
     assert torch.equal(ops.linear(a, gu, swiglu_epilogue=True), out) or splits == 1
 
 
+@pytest.mark.parametrize("M", [1, 5])
+def test_gemv_rownorm_and_residual_epilogues(M):
+    """Row-scaled GEMV (plain and SwiGLU) and the residual epilogue against
+    fp32: y * rsqrt(sumsq / K + eps) + bias; r = bf16(y) + res, res = bf16(r),
+    h = bf16(r * w), sumsq += sum(r^2)."""
+    torch.manual_seed(6)
+    K, N, eps = 1536, 1024, 1e-6
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    bias = torch.randn(N, device=DEV, dtype=torch.bfloat16)
+    sumsq = torch.rand(M, device=DEV) * K * 3 + 1.0
+    rstd = torch.rsqrt(sumsq / K + eps)[:, None]
+    out = ops.gemv_rownorm(x, w, bias, sumsq, eps)
+    assert _rel(out, (x.float() @ w.float().t()) * rstd + bias.float()) < 1e-2
+    gate, up = w[: N // 2], torch.randn(N // 2, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    sw = ops.gemv_rownorm(x, ops.interleave_gate_up(gate, up), None, sumsq, eps, swiglu=True)
+    exp = torch.nn.functional.silu((x.float() @ gate.float().t()) * rstd) * ((x.float() @ up.float().t()) * rstd)
+    assert _rel(sw, exp) < 1e-2
+    res = torch.randn(M, N, device=DEV, dtype=torch.bfloat16)
+    res0 = res.clone()
+    nw = torch.rand(N, device=DEV, dtype=torch.bfloat16) + 0.5
+    h = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    sq = torch.zeros(M, device=DEV)
+    ops.gemv_residual(x, w, res, nw, h, sq)
+    torch.cuda.synchronize()
+    assert ops.check_errors(DEV) == 0
+    r = (x.float() @ w.float().t()).to(torch.bfloat16).float() + res0.float()
+    assert _rel(res, r) < 1e-2 and _rel(h, r * nw.float()) < 1e-2
+    assert _rel(sq, (r * r).sum(-1)) < 1e-3
+
+
+@pytest.mark.parametrize("qk_norm", [False, True])
+def test_gemv_qkv_rope_matches_unfused(qk_norm):
+    """qkv GEMV with per-head norm, RoPE and the KV write in its stores ==
+    GEMV then rope_qkv_write, and == the fp32 CPU definition."""
+    torch.manual_seed(7)
+    Hq, Hkv, D, K, M, ps, pages = 8, 2, 128, 1024, 3, 16, 8
+    N = (Hq + 2 * Hkv) * D
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    bias = torch.randn(N, device=DEV, dtype=torch.bfloat16)
+    pos = torch.tensor([5, 17, 100], device=DEV, dtype=torch.int32)
+    slots = torch.tensor([3, 40, 77], device=DEV, dtype=torch.int64)
+    cs = ref.rope_cos_sin_table(4096, 128, 1e6).to(DEV)
+    qn = (torch.rand(D, device=DEV, dtype=torch.bfloat16) + 0.5) if qk_norm else None
+    kn = (torch.rand(D, device=DEV, dtype=torch.bfloat16) + 0.5) if qk_norm else None
+    pools = [torch.zeros(pages, Hkv, ps, D, device=DEV, dtype=torch.bfloat16) for _ in range(4)]
+    q1 = torch.empty(M, Hq, D, device=DEV, dtype=torch.bfloat16)
+    q2 = torch.empty_like(q1)
+    ops.gemv_qkv_rope(x, w, bias, pos, slots, cs, q1, pools[0], pools[1], Hq, Hkv, qn, kn, 1e-6)
+    torch.cuda.synchronize()
+    assert ops.check_errors(DEV) == 0
+    ops.rope_qkv_write(ops.linear(x, w, bias), pos, slots, cs, q2, pools[2], pools[3], Hq, Hkv, D, qn, kn, 1e-6)
+    assert _rel(q1, q2) < 1e-2 and _rel(pools[0], pools[2]) < 1e-2 and _rel(pools[1], pools[3]) < 1e-2
+    kc = torch.zeros(pages, Hkv, ps, D)
+    vc = torch.zeros_like(kc)
+    qc = torch.empty(M, Hq, D)
+    c = lambda t: None if t is None else t.cpu().float()
+    ops.gemv_qkv_rope(c(x), c(w), c(bias), pos.cpu(), slots.cpu(), cs.cpu(), qc, kc, vc, Hq, Hkv, c(qn), c(kn), 1e-6)
+    assert _rel(q1, qc) < 1e-2 and _rel(pools[0], kc) < 1e-2 and _rel(pools[1], vc) < 1e-2
+
+
 @pytest.mark.parametrize("M", [1, 3, 16, 17, 64, 100, 128])
 @pytest.mark.parametrize("N,K", [(4608, 3584), (3584, 18944), (1000, 512)])
 def test_gemm_small_m(M, N, K):
