@@ -457,10 +457,10 @@ class Engine:
                 self.stats["remote_blocks_linked"] += len(self._remote)
                 self._remote = {}
                 pic_link.pop("_scheduler_reserved_cache_keys", None)
-            rec = set(resolved.recompute_positions)
+            rec = np.sort(np.asarray(resolved.recompute_positions, dtype=np.int64))
             for b in resolved.block_ranges:
-                reused = sum(1 for p in range(b.start_token, b.end_token) if p not in rec)
-                self.registry.record_execution(b.cache_key, reused, b.token_count - reused)
+                recomputed = int(np.searchsorted(rec, b.end_token) - np.searchsorted(rec, b.start_token))
+                self.registry.record_execution(b.cache_key, b.token_count - recomputed, recomputed)
             self.stats["links"] += 1
             return seq
 

@@ -148,7 +148,7 @@ def resolve_link_plan(plan: dict, mutable_input_ids: Sequence[int],
     keys = [str(k) for k in plan["cache_keys"]]
     normalized = plan.get("physical_token_layout_version") is not None
     validated = validate_physical_token_input(plan, label="pic_link")
-    ids = [int(t) for t in mutable_input_ids]
+    ids = list(map(int, mutable_input_ids))
     if normalized:
         if validated is None:
             raise LinkPlanError("normalized pic_link is missing physical_input_ids.")
@@ -199,7 +199,7 @@ def resolve_link_plan(plan: dict, mutable_input_ids: Sequence[int],
         toks = block_tokens(key)
         if toks is None:
             raise LinkPlanError(f"PIC block is not compiled in this scheduler: {key}")
-        toks = [int(t) for t in toks]
+        toks = list(map(int, toks))
         if normalized:
             seg = segs[i]
             if str(seg.get("cache_key")) != key:
