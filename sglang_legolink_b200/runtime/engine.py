@@ -70,6 +70,16 @@ class Sequence_:
     finished: bool = False
     sampling: SamplingParams = GREEDY
     generator: Optional[torch.Generator] = None
+    promotion: Optional[dict] = None  # record of an experimental group promotion
+
+
+def group_promotion_enabled() -> bool:
+    """EXPERIMENTAL, off by default.  A Link's reconstructed execution group
+    becomes a cache block only when the deployment sets this flag AND the
+    request sets ``promote_reconstructed_group`` (neither alone promotes)."""
+    from ..contract import env_flag
+
+    return env_flag("SGLANG_PIC_EXPERIMENTAL_GROUP_PROMOTION")
 
 
 def _pinned_copy(host: np.ndarray, dev) -> torch.Tensor:
@@ -147,6 +157,7 @@ class Engine:
         self.legolink_only = legolink_only
         self.compat = self._compat(compat_overrides or {})
         self.use_cuda_graphs = use_cuda_graphs and self.is_cuda
+        self.decode_chunk = 64  # greedy steps per chained decode chunk (one host read per chunk)
         self._graphs: dict = {}
         self._lock = threading.RLock()
         self._rid = 0
@@ -444,6 +455,10 @@ class Engine:
                 try:
                     pages = self._alloc_pages(pages_for(resolved.total_token_count, self.page_size))
                     seq = self._run_link(resolved, pages, rid, timer, sampling)
+                    # after repair, before decode: a failed promotion costs a
+                    # trace row, never the answer
+                    if group_promotion_enabled() and pic_link.get("promote_reconstructed_group"):
+                        seq.promotion = self._promote_group(resolved, pages, pic_link, rid)
                 finally:
                     self.registry.release(keys)
             except Exception:
@@ -497,6 +512,76 @@ class Engine:
                          length=resolved.total_token_count, output_ids=[first_id], kind="link", link_plan=resolved,
                          sampling=sp, generator=gen)
 
+    def _promote_group(self, resolved: ResolvedLinkPlan, pages: list[int], plan: dict, rid: str) -> Optional[dict]:
+        """EXPERIMENTAL.  Makes a fully reconstructed execution group durable:
+        the group's rows (first member's start to last member's end) are
+        copied from this request's pages into new cache-owned pages, rotated
+        from their global positions back to group-local ones (the inverse of
+        the link rotation, done by the same kernel with the two position
+        arrays swapped), and registered under ``execution_group_key`` like a
+        compiled block, so a later Link of the same members links one block.
+        A copy, not a hand-over: the request keeps its own rows and frame.
+        Only groups whose members after the first were recomputed in full
+        qualify (a partially repaired group is never persisted); an existing
+        key wins.  Every refusal or failure is a ``group_promotion_skipped``
+        trace row and the request is served regardless.
+        Reference: ``pic_runtime.py:5718-6023`` (gate ``:925``)."""
+
+        def skip(reason: str, **details) -> None:
+            self.stats["group_promotions_skipped"] = self.stats.get("group_promotions_skipped", 0) + 1
+            emit_trace("group_promotion_skipped", rid=rid, reason=reason, **details)
+            return None
+
+        key = plan.get("execution_group_key")
+        if not isinstance(key, str) or not key.strip():
+            return skip("no_execution_group_key")
+        key = key.strip()
+        ranges = resolved.block_ranges
+        if len(ranges) < 2:
+            return skip("singleton_group", member_count=len(ranges))
+        for i, (b, w) in enumerate(zip(ranges[1:], resolved.recompute_tokens_per_block[1:]), start=1):
+            if int(w) < b.token_count:
+                return skip("reconstruction_below_promotion_policy", member_index=i, recomputed=int(w),
+                            token_count=b.token_count)
+        if self.registry.contains(key):
+            return skip("already_registered", cache_key=key)
+        g0, g1 = ranges[0].start_token, ranges[-1].end_token
+        n = g1 - g0
+        toks = [int(t) for t in resolved.linked_token_ids[g0:g1]]
+        t0 = time.perf_counter()
+        try:
+            new_pages = self._alloc_pages(pages_for(n, self.page_size))
+        except CapacityError:
+            return skip("allocation_failed", token_count=n, free_pages=self.alloc.num_free)
+        registered = False
+        try:
+            ps = self.page_size
+            glob = np.arange(g0, g1, dtype=np.int64)
+            loc = np.arange(n, dtype=np.int64)
+            src = np.asarray(pages, dtype=np.int64)[glob // ps] * ps + glob % ps
+            dst = np.asarray(new_pages, dtype=np.int64)[loc // ps] * ps + loc % ps
+            dev = self.device
+            ops.kv_link_rope(self.kv.k, self.kv.v, torch.from_numpy(src).to(dev), torch.from_numpy(dst).to(dev),
+                             torch.from_numpy(glob.astype(np.int32)).to(dev),
+                             torch.from_numpy(loc.astype(np.int32)).to(dev), self.model.cos_sin)
+            ckey = self.compat_key(plan.get("adapter_id"), plan.get("segmentation_policy_version"),
+                                   plan.get("legolink_policy_version"))
+            status = self.registry.register_block(key, ckey, physical_token_ids_sha256(toks), toks, new_pages, 0,
+                                                  key)
+            registered = True  # from here the registry owns (or has released) the pages
+            if status != "registered":
+                return skip("already_registered", cache_key=key)
+            self.registry.record_execution(key, 0, n)
+        except Exception as e:  # noqa: BLE001 - never fail a served request
+            if not registered:
+                self.alloc.release(new_pages)
+            return skip("promotion_failed", error=str(e)[:300], registered=registered)
+        rec = {"cache_key": key, "member_cache_keys": [b.cache_key for b in ranges], "token_count": n,
+               "group_start_token": g0, "promotion_elapsed_s": round(time.perf_counter() - t0, 6)}
+        self.stats["group_promotions"] = self.stats.get("group_promotions", 0) + 1
+        emit_trace("group_promotion_completed", rid=rid, **rec)
+        return rec
+
     # --------------------------------------------------------------- prefill
     def prefill(self, token_ids: Sequence[int], *, rid: Optional[str] = None, namespace: Optional[str] = None,
                 use_prefix_cache: bool = False, sampling: Optional[SamplingParams] = None) -> Sequence_:
@@ -539,15 +624,87 @@ class Engine:
         """Greedy-decode ``steps`` tokens for every sequence (in place).  The
         last output token of each sequence is fed as the next input."""
         stop = set(int(s) for s in stop_ids)
-        for _ in range(steps):
+        done = 0
+        while done < steps:
             live = [s for s in seqs if not s.finished]
             if not live:
                 break
+            if self.use_cuda_graphs and steps - done > 1 and all(s.sampling.greedy for s in live):
+                n = min(steps - done, self.decode_chunk if not stop else min(self.decode_chunk, 16))
+                self.decode_chained(live, n, stop)
+                done += n
+                continue
             nxt = self.decode_step(live)
+            done += 1
             for s, t in zip(live, nxt):
                 s.output_ids.append(int(t))
                 if int(t) in stop:
                     s.finished = True
+
+    def decode_chained(self, seqs: list[Sequence_], steps: int, stop: set = frozenset()) -> None:
+        """``steps`` greedy decode steps with no host round trip between
+        them: capacity for all steps is reserved first, every step's
+        positions / slots / lengths are computed on the host and copied to
+        the device once, and each step's input ids are the previous step's
+        argmax, copied on the device before the graph replays.  The outputs
+        are read back once at the end; a sequence that produced a stop token
+        keeps the tokens up to it (the rows computed after it are dropped, as
+        the per-step loop would never have computed them).  A Compile or Link
+        runs only between such chunks: the host waits for the chunk's tokens
+        before it returns.  Greedy sequences, CUDA graphs only."""
+        with self._lock:
+            B = len(seqs)
+            ps = self.page_size
+            for s in seqs:
+                self._ensure_capacity(s, s.length + steps)
+            bucket = self._bucket(B)
+            max_pages = pages_for(self.max_context, ps)
+            g = self._graphs.get(bucket)
+            if g is None:
+                g = self._capture(bucket, max_pages, seqs)
+                self._graphs[bucket] = g
+            ids, _, _, pt, _ = self._decode_inputs(seqs, bucket, max_pages)
+            L0 = np.asarray([s.length for s in seqs], dtype=np.int64)
+            pos = np.zeros((steps, bucket), dtype=np.int64)
+            slots = np.full((steps, bucket), self.kv.scratch_page * ps, dtype=np.int64)
+            pos[:, :B] = L0[None, :] + np.arange(steps, dtype=np.int64)[:, None]
+            for b, s in enumerate(seqs):
+                pg = np.asarray(s.pages, dtype=np.int64)
+                pb = pos[:, b]
+                slots[:, b] = pg[pb // ps] * ps + pb % ps
+            kvl = np.where(np.arange(bucket)[None, :] < B, pos + 1, 1)
+            dev = self.device
+            d32 = _pinned_copy(np.concatenate([pos.astype(np.int32).reshape(-1), kvl.astype(np.int32).reshape(-1)]),
+                               dev)
+            d64 = _pinned_copy(slots.reshape(-1), dev)
+            dpos = d32[: steps * bucket].view(steps, bucket)
+            dkvl = d32[steps * bucket:].view(steps, bucket)
+            dslots = d64.view(steps, bucket)
+            g["ids"].copy_(ids, non_blocking=True)
+            g["pt"].copy_(pt, non_blocking=True)
+            hist = torch.empty(steps, bucket, dtype=torch.int32, device=dev)
+            for t in range(steps):
+                if t > 0:
+                    g["ids"].copy_(g["out"])
+                g["pos"].copy_(dpos[t])
+                g["kvl"].copy_(dkvl[t])
+                g["slots"].copy_(dslots[t])
+                g["graph"].replay()
+                hist[t].copy_(g["out"])
+                launch_count.add(g["launches"])
+            out = hist[:, :B].t().tolist()
+            for s, toks in zip(seqs, out):
+                n = steps
+                for j, t in enumerate(toks):
+                    if t in stop:
+                        n = j + 1
+                        s.finished = True
+                        break
+                inputs = [s.output_ids[-1]] + toks[: n - 1]
+                s.output_ids.extend(toks[:n])
+                s.token_ids.extend(inputs)
+                s.length += n
+            self.stats["decode_steps"] += steps
 
     def decode_step(self, seqs: list[Sequence_]) -> list[int]:
         with self._lock:

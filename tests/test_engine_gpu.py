@@ -94,3 +94,27 @@ def test_padded_decode_bucket_keeps_row0_kv():
         s = eng.prefill(subs[i] + suffix)
         eng.decode([s], 8)
         assert s.output_ids == seqs[i].output_ids
+
+
+def test_chained_decode_matches_per_step_with_stop_and_continue():
+    """Greedy chunks with no host round trip between steps give the eager
+    per-step tokens; a stop token ends a sequence at the same token and the
+    same length, and decoding it further continues the same stream."""
+    cfg, eng, subs, suffix = _setup("small-qwen2", seed=5)
+    a = eng.prefill(subs[1] + suffix)
+    eng.use_cuda_graphs = False
+    eng.decode([a], 12)
+    ref_ids, ref_len = list(a.output_ids), a.length
+    eng.use_cuda_graphs = True
+    b = eng.prefill(subs[1] + suffix)
+    eng.decode([b], 12)
+    assert b.output_ids == ref_ids and b.length == ref_len
+    c = eng.prefill(subs[1] + suffix)
+    gen = ref_ids[1:]  # output_ids[0] is the prefill's token
+    stop = gen[4]
+    j = gen.index(stop)  # decode steps up to and including the first stop
+    eng.decode([c], 12, stop_ids=[stop])
+    assert c.finished and c.output_ids == ref_ids[: 2 + j] and c.length == ref_len - (12 - (j + 1))
+    c.finished = False
+    eng.decode([c], 12 - (j + 1))
+    assert c.output_ids == ref_ids and c.length == ref_len

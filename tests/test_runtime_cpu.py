@@ -120,3 +120,32 @@ def test_normalized_layout_hashes_checked(world):
     bad["expected_complete_token_ids_sha256"] = "0" * 64
     with pytest.raises(ContractError):
         eng.link(bad, ids)
+
+
+def test_group_promotion_gated_exact_and_fail_closed(world, monkeypatch):
+    """EXPERIMENTAL promotion: off unless the deployment flag AND the request
+    ask; a fully reconstructed group becomes one block that links to the same
+    answer; partial repair and an existing key are refused."""
+    eng, subs, suffix = world
+    order = ["instruction", "turn", "tool_schema"]
+    plan = {"cache_keys": order, "recompute_tokens_per_block": [0] + [len(subs[k]) for k in order[1:]],
+            "promote_reconstructed_group": True, "execution_group_key": "grp-a"}
+    monkeypatch.delenv("SGLANG_PIC_EXPERIMENTAL_GROUP_PROMOTION", raising=False)
+    seq = eng.link(dict(plan), suffix)
+    assert seq.promotion is None and not eng.registry.contains("grp-a")
+    eng.free(seq)
+    monkeypatch.setenv("SGLANG_PIC_EXPERIMENTAL_GROUP_PROMOTION", "1")
+    seq = eng.link(dict(plan), suffix)
+    assert seq.promotion["cache_key"] == "grp-a" and eng.registry.contains("grp-a")
+    assert seq.promotion["token_count"] == sum(len(subs[k]) for k in order)
+    one = eng.link({"cache_keys": ["grp-a"], "recompute_tokens_per_block": [0]}, suffix)
+    eng.decode([seq], 8)
+    eng.decode([one], 8)
+    assert one.output_ids == seq.output_ids
+    part = dict(plan, execution_group_key="grp-b", recompute_tokens_per_block=[0, 8, 8])
+    s2 = eng.link(part, suffix)
+    assert s2.promotion is None and not eng.registry.contains("grp-b")
+    s3 = eng.link(dict(plan), suffix)  # the key exists: first registration wins
+    assert s3.promotion is None
+    for s in (seq, one, s2, s3):
+        eng.free(s)
