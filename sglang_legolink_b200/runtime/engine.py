@@ -312,36 +312,79 @@ class Engine:
     def compile(self, token_ids: Sequence[int], cache_key: str, *, sub_context: Optional[dict] = None,
                 block_id: Optional[str] = None) -> dict:
         """Prefill a block alone from position 0 and register it."""
-        with self._lock:
-            sc = dict(sub_context or {})
-            override = validate_physical_token_input(sc, label="sub_context")
-            toks = [int(t) for t in (override if override is not None else token_ids)]
-            if override is not None and token_ids and list(token_ids) != override:
-                raise ContractError("Compile request tokens differ from the validated physical_input_ids override.")
-            if not toks:
-                raise ContractError("Compile requires a non-empty sub-context.")
-            ckey = self.compat_key(sc.get("adapter_id"), sc.get("segmentation_policy_version"),
-                                   sc.get("legolink_policy_version"))
-            n = len(toks)
-            pages = self._alloc_pages(pages_for(n, self.page_size))
-            try:
-                fb = self._extend_batch([(toks, list(range(n)), pages, n)])
-                logits = self.model.forward(fb, self.kv)
-                first = int(self._sample(logits)[0].item())
-            except Exception:
-                self.alloc.release(pages)
-                raise
-            status = self.registry.register_block(str(cache_key), ckey, physical_token_ids_sha256(toks), toks, pages,
-                                                  0, str(block_id or sc.get("semantic_block_id") or cache_key))
-            self.stats["compiles"] += 1
-            if self.directory is not None and status == "registered":
-                from ..parallel.dp import RemoteBlock
+        r = self.compile_batch([(token_ids, cache_key, sub_context, block_id)])[0]
+        if isinstance(r, Exception):
+            raise r
+        return r
 
-                self.registry.pin([str(cache_key)])  # a peer may link it at any time: never evict
-                self.directory.publish(RemoteBlock(self.replica_rank, str(cache_key), tuple(pages), 0, tuple(toks),
-                                                   ckey, physical_token_ids_sha256(toks), self.page_size))
-            emit_trace("compile_registered", cache_key=str(cache_key), token_count=n, status=status)
-            return {"cache_key": str(cache_key), "status": status, "token_count": n, "first_token": first}
+    def compile_batch(self, items: Sequence[tuple]) -> list:
+        """Several Compiles in one extend forward (each block from position 0
+        in its own pages, one logits row per block).  ``items``: (token_ids,
+        cache_key, sub_context, block_id).  Returns one result dict or the
+        exception per item; an item that fails validation or allocation fails
+        alone.  Two Compiles of one key may not share a batch (the scheduler
+        defers the second to the next batch, where it takes the duplicate
+        path); here that is refused outright.
+        Reference: ``pic_compile_key_in_batch``, ``pic_runtime.py:1954-1975``."""
+        with self._lock:
+            out: list = [None] * len(items)
+            prepared = []
+            seen: set = set()
+            for i, it in enumerate(items):
+                token_ids, cache_key, sub_context, block_id = (tuple(it) + (None, None))[:4]
+                try:
+                    if str(cache_key) in seen:
+                        raise ContractError(f"two Compiles of '{cache_key}' in one batch")
+                    seen.add(str(cache_key))
+                    toks, ckey, bid = self._compile_prepare(token_ids, cache_key, sub_context, block_id)
+                    pages = self._alloc_pages(pages_for(len(toks), self.page_size))
+                    prepared.append((i, toks, ckey, bid, str(cache_key), pages))
+                except Exception as e:  # noqa: BLE001 - request-scoped
+                    out[i] = e
+            if not prepared:
+                return out
+            try:
+                fb = self._extend_batch([(toks, list(range(len(toks))), pages, len(toks))
+                                         for _, toks, _, _, _, pages in prepared])
+                logits = self.model.forward(fb, self.kv)
+                firsts = self._sample(logits).tolist()
+            except Exception as e:
+                for i, *_rest, pages in prepared:
+                    self.alloc.release(pages)
+                    out[i] = e
+                return out
+            for (i, toks, ckey, bid, key, pages), first in zip(prepared, firsts):
+                try:
+                    out[i] = self._compile_register(toks, key, ckey, bid, pages, int(first))
+                except Exception as e:  # noqa: BLE001
+                    out[i] = e
+            return out
+
+    def _compile_prepare(self, token_ids, cache_key, sub_context, block_id):
+        sc = dict(sub_context or {})
+        override = validate_physical_token_input(sc, label="sub_context")
+        toks = [int(t) for t in (override if override is not None else token_ids)]
+        if override is not None and token_ids and list(token_ids) != override:
+            raise ContractError("Compile request tokens differ from the validated physical_input_ids override.")
+        if not toks:
+            raise ContractError("Compile requires a non-empty sub-context.")
+        ckey = self.compat_key(sc.get("adapter_id"), sc.get("segmentation_policy_version"),
+                               sc.get("legolink_policy_version"))
+        return toks, ckey, str(block_id or sc.get("semantic_block_id") or cache_key)
+
+    def _compile_register(self, toks, cache_key: str, ckey, bid: str, pages, first: int) -> dict:
+        n = len(toks)
+        status = self.registry.register_block(str(cache_key), ckey, physical_token_ids_sha256(toks), toks, pages, 0,
+                                              bid)
+        self.stats["compiles"] += 1
+        if self.directory is not None and status == "registered":
+            from ..parallel.dp import RemoteBlock
+
+            self.registry.pin([str(cache_key)])  # a peer may link it at any time: never evict
+            self.directory.publish(RemoteBlock(self.replica_rank, str(cache_key), tuple(pages), 0, tuple(toks),
+                                               ckey, physical_token_ids_sha256(toks), self.page_size))
+        emit_trace("compile_registered", cache_key=str(cache_key), token_count=n, status=status)
+        return {"cache_key": str(cache_key), "status": status, "token_count": n, "first_token": first}
 
     def block_tokens(self, cache_key: str):
         t = self.registry.tokens(cache_key)
@@ -641,7 +684,7 @@ class Engine:
                 if int(t) in stop:
                     s.finished = True
 
-    def decode_chained(self, seqs: list[Sequence_], steps: int, stop: set = frozenset()) -> None:
+    def decode_chained(self, seqs: list[Sequence_], steps: int, stop=frozenset()) -> None:
         """``steps`` greedy decode steps with no host round trip between
         them: capacity for all steps is reserved first, every step's
         positions / slots / lengths are computed on the host and copied to
@@ -651,7 +694,8 @@ class Engine:
         keeps the tokens up to it (the rows computed after it are dropped, as
         the per-step loop would never have computed them).  A Compile or Link
         runs only between such chunks: the host waits for the chunk's tokens
-        before it returns.  Greedy sequences, CUDA graphs only."""
+        before it returns.  ``stop``: one set of stop ids for all sequences
+        or one set per sequence.  Greedy sequences, CUDA graphs only."""
         with self._lock:
             B = len(seqs)
             ps = self.page_size
@@ -693,10 +737,11 @@ class Engine:
                 hist[t].copy_(g["out"])
                 launch_count.add(g["launches"])
             out = hist[:, :B].t().tolist()
-            for s, toks in zip(seqs, out):
+            stops = stop if isinstance(stop, (list, tuple)) else [stop] * B
+            for s, toks, st in zip(seqs, out, stops):
                 n = steps
                 for j, t in enumerate(toks):
-                    if t in stop:
+                    if t in st:
                         n = j + 1
                         s.finished = True
                         break

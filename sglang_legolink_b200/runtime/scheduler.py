@@ -15,9 +15,13 @@ TTFT at concurrency 8 to that wait, reference ``pic_runtime.py:2023-2026``,
 Arrival checks (reference ``managers/scheduler.py:1915-2057``): a request is a
 Compile (``sub_context``) XOR a Link (``pic_link``); in LegoLink-only mode
 plain generation is refused; a Link may not ask for input logprobs; an
-overlength Link is rejected, never truncated.  Two Compiles of one key never
-run concurrently (the loop is serial and the registry keeps the resident
-copy on a duplicate).  Every failure is request-scoped.
+overlength Link is rejected, never truncated.  The Compiles admitted in one
+step share one extend forward; a second Compile of a key already in that
+batch is deferred to the next one (where the registry keeps the resident copy
+on the duplicate).  When nothing is waiting, greedy decode runs
+``decode_chunk`` steps back to back on the device (no host read between
+them); a Compile or Link is admitted only between chunks.  Every failure is
+request-scoped.
 """
 
 from __future__ import annotations
@@ -57,11 +61,13 @@ class Request:
 
 class Scheduler:
     def __init__(self, engine: Engine, *, legolink_only: bool = True, max_running: int = 64,
-                 max_prefills_per_step: int = 1, max_context: Optional[int] = None):
+                 max_prefills_per_step: int = 4, max_context: Optional[int] = None, decode_chunk: int = 8):
         self.engine = engine
         self.legolink_only = legolink_only
         self.max_running = max_running
         self.max_prefills_per_step = max_prefills_per_step
+        self.decode_chunk = decode_chunk
+        self._deferred: list = []  # Compiles pushed to the next batch (same key already in this one)
         self.max_context = max_context or engine.max_context
         self.waiting: "queue.Queue[Request]" = queue.Queue()
         self.running: list[Request] = []
@@ -111,22 +117,80 @@ class Scheduler:
                 except queue.Empty:
                     pass
 
+    def _next_waiting(self) -> Optional[Request]:
+        if self._deferred:
+            return self._deferred.pop(0)
+        try:
+            return self.waiting.get_nowait()
+        except queue.Empty:
+            return None
+
     def step(self) -> bool:
         """One scheduling iteration; returns False when idle."""
-        did = False
+        batch = []
         for _ in range(self.max_prefills_per_step):
-            if len(self.running) >= self.max_running:
+            if len(self.running) + len(batch) >= self.max_running:
                 break
-            try:
-                req = self.waiting.get_nowait()
-            except queue.Empty:
+            req = self._next_waiting()
+            if req is None:
                 break
-            did = True
-            self._admit(req)
+            batch.append(req)
+        did = bool(batch)
+        if batch:
+            self._admit_batch(batch)
         if self.running:
             did = True
             self._decode()
         return did
+
+    def _admit_batch(self, batch: list) -> None:
+        """Compiles of one step share one extend forward; a Compile whose key
+        is already in the batch waits for the next one (where it takes the
+        registry's duplicate path).  Links and plain prefills run one by one.
+        Reference: ``pic_compile_key_in_batch`` ``pic_runtime.py:1954-1975``,
+        ``managers/scheduler.py:2611-2617``."""
+        compiles, keys = [], set()
+        for req in batch:
+            if req.kind != "compile":
+                continue
+            key = (req.sub_context or {}).get("cache_key")
+            if key and str(key) in keys:
+                self._deferred.append(req)
+                emit_trace("compile_deferred_same_key_in_batch", rid=req.rid, cache_key=str(key))
+                continue
+            if key:
+                keys.add(str(key))
+            compiles.append(req)
+        if compiles:
+            self._admit_compiles(compiles)
+        for req in batch:
+            if req.kind != "compile":
+                self._admit(req)
+
+    def _admit_compiles(self, reqs: list) -> None:
+        items, live = [], []
+        for req in reqs:
+            key = (req.sub_context or {}).get("cache_key")
+            if not key:
+                req.events.put(("error", "sub_context.cache_key is required for a Compile"))
+                continue
+            items.append((req.input_ids, str(key), req.sub_context or {}, None))
+            live.append(req)
+        if not items:
+            return
+        try:
+            results = self.engine.compile_batch(items)
+        except Exception as e:  # the whole batch failed: each request fails alone
+            results = [e] * len(items)
+        for req, r in zip(live, results):
+            if isinstance(r, Exception):
+                emit_trace("legolink_request_failed_closed", rid=req.rid, kind="compile", reason=str(r)[:500])
+                req.events.put(("error", str(r)))
+                continue
+            req.ttft_s = time.perf_counter() - req.created
+            req.events.put(("token", r["first_token"]))
+            req.events.put(("done", {"compile": r, "finish_reason": "length"}))
+            self.stats["finished"] += 1
 
     def _admit(self, req: Request) -> None:
         eng = self.engine
@@ -167,6 +231,36 @@ class Scheduler:
 
     def _decode(self) -> None:
         seqs = [r.seq for r in self.running]
+        eng = self.engine
+        k = 1
+        if (self.decode_chunk > 1 and self.waiting.empty() and not self._deferred and eng.use_cuda_graphs
+                and all(r.sampling.greedy for r in self.running)):
+            k = min(self.decode_chunk, min(r.max_new_tokens - len(r.seq.output_ids) for r in self.running))
+        if k >= 2:
+            # nothing is waiting: k steps back to back on the device, tokens
+            # streamed when the chunk returns
+            before = [len(r.seq.output_ids) for r in self.running]
+            try:
+                eng.decode_chained(seqs, k, [set(int(t) for t in r.stop_ids) for r in self.running])
+            except Exception as e:
+                for r in self.running:
+                    r.events.put(("error", f"decode failed: {e!r}"))
+                    self.engine.free(r.seq)
+                self.running = []
+                return
+            self.stats["decode_steps"] += k
+            still = []
+            for r, b0 in zip(self.running, before):
+                for t in r.seq.output_ids[b0:]:
+                    r.events.put(("token", int(t)))
+                if r.seq.finished:
+                    self._finish(r, "stop")
+                elif len(r.seq.output_ids) >= r.max_new_tokens:
+                    self._finish(r, "length")
+                else:
+                    still.append(r)
+            self.running = still
+            return
         try:
             toks = self.engine.decode_step(seqs)
         except Exception as e:

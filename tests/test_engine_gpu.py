@@ -118,3 +118,36 @@ def test_chained_decode_matches_per_step_with_stop_and_continue():
     c.finished = False
     eng.decode([c], 12 - (j + 1))
     assert c.output_ids == ref_ids and c.length == ref_len
+
+
+def test_scheduler_chunked_decode_streams_the_per_step_tokens():
+    """With nothing waiting, the scheduler decodes in chained chunks; the
+    streamed tokens, stops and finish reasons are those of per-step decode."""
+    from sglang_legolink_b200.runtime.scheduler import Request, Scheduler
+
+    cfg, eng, subs, suffix = _setup("small-qwen2", seed=6)
+    prompts = [subs[0] + suffix, subs[2] + suffix]
+    eng.use_cuda_graphs = False
+    refs = []
+    for p in prompts:
+        s = eng.prefill(p)
+        eng.decode([s], 19)
+        refs.append(list(s.output_ids))
+        eng.free(s)
+    eng.use_cuda_graphs = True
+    stop = refs[1][7]
+    sch = Scheduler(eng, legolink_only=False, decode_chunk=8)
+    reqs = [Request("plain", "p0", prompts[0], 20), Request("plain", "p1", prompts[1], 20, stop_ids=(stop,))]
+    for r in reqs:
+        sch.submit(r)
+    while sch.step():
+        pass
+    got = []
+    for r in reqs:
+        ev = []
+        while not r.events.empty():
+            ev.append(r.events.get_nowait())
+        got.append(([v for k, v in ev if k == "token"], [v for k, v in ev if k == "done"][0]["finish_reason"]))
+    assert got[0] == (refs[0], "length")
+    j = refs[1].index(stop)
+    assert got[1] == (refs[1][: j + 1], "stop")

@@ -149,3 +149,41 @@ def test_group_promotion_gated_exact_and_fail_closed(world, monkeypatch):
     assert s3.promotion is None
     for s in (seq, one, s2, s3):
         eng.free(s)
+
+
+def test_scheduler_batches_compiles_and_defers_same_key(world, monkeypatch):
+    """Compiles admitted in one step share one forward; a second Compile of a
+    key already in that batch waits for the next batch and takes the
+    duplicate path; results match one-by-one Compiles."""
+    from sglang_legolink_b200.runtime.scheduler import Request, Scheduler
+
+    eng, subs, suffix = world
+    g = torch.Generator().manual_seed(11)
+    a = torch.randint(0, 1024, (96,), generator=g).tolist()
+    b = torch.randint(0, 1024, (40,), generator=g).tolist()
+    calls = []
+    orig = eng.compile_batch
+
+    def spy(items):
+        calls.append([str(it[1]) for it in items])
+        return orig(items)
+
+    monkeypatch.setattr(eng, "compile_batch", spy)
+    sch = Scheduler(eng, max_prefills_per_step=4)
+    reqs = [Request("compile", f"c{i}", toks, 1, sub_context={"cache_key": key})
+            for i, (key, toks) in enumerate([("sched-a", a), ("sched-a", a), ("sched-b", b)])]
+    for r in reqs:
+        sch.submit(r)
+    while sch.step():
+        pass
+    assert calls == [["sched-a", "sched-b"], ["sched-a"]]
+    done = []
+    for r in reqs:
+        ev = []
+        while not r.events.empty():
+            ev.append(r.events.get_nowait())
+        done.append([v for k, v in ev if k == "done"][0]["compile"])
+    assert [d["status"] for d in done] == ["registered", "duplicate", "registered"]
+    solo = Engine(QwenModel.random_init(PRESETS["tiny-qwen2"], seed=0), num_pages=256, page_size=16)
+    assert solo.compile(b, "solo-b")["first_token"] == done[2]["first_token"]
+    assert solo.compile(a, "solo-a")["first_token"] == done[0]["first_token"]
