@@ -45,6 +45,9 @@ class ForwardBatch:
     logit_rows: Optional[torch.Tensor] = None  # [R] int64 rows whose logits are returned
     tiles: Optional[torch.Tensor] = None  # prefill attention work list
     decode_nsplit: Optional[int] = None
+    # grouped execution rows of one extend forward (row-wise repair compute):
+    # {"batch_execution_unit_size": n, "repair_ranges": [{"start", "end"}], ...}
+    repair_meta: Optional[dict] = None
 
     @property
     def num_rows(self) -> int:
@@ -63,6 +66,7 @@ class QwenModel:
         self.dtype = dtype
         self.tp_rank, self.tp_size = tp_rank, tp_size
         self.comm = comm
+        self.capture = None  # optional RepairStateCapture (diagnostics; extend forwards only)
         assert cfg.num_heads % tp_size == 0, "num_heads must divide by tp_size"
         self.hq = cfg.num_heads // tp_size
         # KV heads are split when possible, else replicated (each rank keeps one).
@@ -238,22 +242,46 @@ class QwenModel:
         tiles = fb.tiles
         if fb.mode == "extend" and tiles is None and fb.input_ids.is_cuda:
             tiles = ops.prefill_tiles(fb.q_indptr.cpu(), fb.positions.cpu(), self.hq, self.hkv).to(self.device)
+        rw_o = rw_ffn = ()
+        if fb.mode == "extend" and fb.repair_meta is not None:
+            from ..runtime.repair_diagnostics import rowwise_slices
+
+            rw_o = rowwise_slices(fb.repair_meta, T, "output_projection")
+            rw_ffn = rowwise_slices(fb.repair_meta, T, "ffn")
+        cap = self.capture if fb.mode == "extend" else None
         for li, lw in enumerate(self.layers):
             if li > 0:
                 ops.fused_add_rmsnorm(h, residual, lw.in_norm, c.rms_norm_eps)
+            if cap is not None and cap.wants(li):
+                cap.on_component(li, "pre_attention_norm", hidden=h, residual=residual)
             ops.linear(h, lw.qkv_w, lw.qkv_b, out=qkv)
             ops.rope_qkv_write(qkv, fb.positions, fb.slots, self.cos_sin, q, kv.k[li], kv.v[li], self.hq, self.hkv,
                                D, lw.q_norm, lw.k_norm, c.rms_norm_eps)
+            if cap is not None and cap.wants(li):
+                cap.on_component(li, "qkv_projection", qkv=qkv)
+                cap.on_component(li, "rope", q=q)
             if fb.mode == "decode":
                 ops.attention_decode(q, kv.k[li], kv.v[li], fb.page_table, fb.kv_lens, self.scale,
                                      nsplit=fb.decode_nsplit, out=attn)
             else:
                 ops.attention_prefill(q, kv.k, kv.v, li, fb.q_indptr, fb.positions, fb.page_table, fb.kv_lens,
                                       self.scale, tiles=tiles, out=attn)
-            self._row_parallel(attn, lw.o_w, o)
+            # row-wise: each grouped row with the shapes it has alone
+            for sl in rw_o or (slice(None),):
+                self._row_parallel(attn[sl], lw.o_w, o[sl])
+            if cap is not None and cap.wants(li):
+                cap.on_component(li, "attention", attention_output=attn)
+                cap.on_component(li, "output_projection", projected_output=o)
             ops.fused_add_rmsnorm(o, residual, lw.post_norm, c.rms_norm_eps)
-            ops.linear(o, lw.gu_w, out=mlp, swiglu_epilogue=True)
-            self._row_parallel(mlp, lw.down_w, h)
+            if cap is not None and cap.wants(li):
+                cap.on_component(li, "post_attention_norm", hidden=o, residual=residual)
+            for sl in rw_ffn or (slice(None),):
+                ops.linear(o[sl], lw.gu_w, out=mlp[sl], swiglu_epilogue=True)
+                self._row_parallel(mlp[sl], lw.down_w, h[sl])
+            if cap is not None:
+                if cap.wants(li):
+                    cap.on_component(li, "mlp", mlp_output=h)
+                cap.on_layer(li, hidden=h, residual=residual)
         # final: residual += h ; h = norm(residual)
         ops.fused_add_rmsnorm(h, residual, self.final_norm, c.rms_norm_eps)
         rows = h if fb.logit_rows is None else h.index_select(0, fb.logit_rows)

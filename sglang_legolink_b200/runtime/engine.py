@@ -346,6 +346,12 @@ class Engine:
             try:
                 fb = self._extend_batch([(toks, list(range(len(toks))), pages, len(toks))
                                          for _, toks, _, _, _, pages in prepared])
+                if len(prepared) > 1:  # grouped execution rows (row-wise compute when enabled)
+                    o, ranges = 0, []
+                    for _, toks, *_ in prepared:
+                        ranges.append({"start": o, "end": o + len(toks)})
+                        o += len(toks)
+                    fb.repair_meta = {"batch_execution_unit_size": len(prepared), "repair_ranges": ranges}
                 logits = self.model.forward(fb, self.kv)
                 firsts = self._sample(logits).tolist()
             except Exception as e:

@@ -187,3 +187,60 @@ def test_scheduler_batches_compiles_and_defers_same_key(world, monkeypatch):
     solo = Engine(QwenModel.random_init(PRESETS["tiny-qwen2"], seed=0), num_pages=256, page_size=16)
     assert solo.compile(b, "solo-b")["first_token"] == done[2]["first_token"]
     assert solo.compile(a, "solo-a")["first_token"] == done[0]["first_token"]
+
+
+def test_rowwise_slices_and_state_capture(world, tmp_path, monkeypatch):
+    """Row-wise output projection / FFN over grouped Compile rows (validated
+    ranges, observation recorded) match the rows compiled alone; the state
+    capture writes every layer, the chosen layer's components and the repair
+    rows' K/V."""
+    from sglang_legolink_b200.runtime.repair_diagnostics import (RepairRowView, RepairStateCapture,
+                                                                 SparseRepairComputeError, rowwise_slices)
+
+    meta = {"batch_execution_unit_size": 2, "repair_ranges": [{"start": 0, "end": 5}, {"start": 5, "end": 9}]}
+    monkeypatch.delenv("SGLANG_PIC_SPARSE_REPAIR_ROWWISE_FFN", raising=False)
+    assert rowwise_slices(dict(meta), 9, "ffn") == ()
+    m = dict(meta, rowwise_ffn_enabled=True)
+    assert rowwise_slices(m, 9, "ffn") == (slice(0, 5), slice(5, 9))
+    assert m["rowwise_ffn_observed"] and m["rowwise_ffn_lengths"] == [5, 4]
+    with pytest.raises(SparseRepairComputeError):
+        rowwise_slices(dict(m), 10, "ffn")
+    with pytest.raises(SparseRepairComputeError):
+        rowwise_slices(dict(meta, rowwise_output_projection_enabled="yes"), 9, "output_projection")
+
+    eng, subs, suffix = world
+    g = torch.Generator().manual_seed(12)
+    a = torch.randint(0, 1024, (70,), generator=g).tolist()
+    b = torch.randint(0, 1024, (33,), generator=g).tolist()
+    monkeypatch.setenv("SGLANG_PIC_SPARSE_REPAIR_ROWWISE_FFN", "1")
+    monkeypatch.setenv("SGLANG_PIC_SPARSE_REPAIR_ROWWISE_OUTPUT_PROJECTION", "1")
+    res = eng.compile_batch([(a, "rw-a", None, None), (b, "rw-b", None, None)])
+    solo = Engine(QwenModel.random_init(PRESETS["tiny-qwen2"], seed=0), num_pages=256, page_size=16)
+    sb = solo.compile(b, "rw-b")
+    assert res[1]["first_token"] == sb["first_token"]
+    hb, hs = eng.registry.handle("rw-b"), solo.registry.handle("rw-b")
+    def block_k(e, h):  # [L, tokens, Hkv * D] of the block's own slots
+        k = e.kv.k[:, list(h["pages"])].permute(0, 1, 3, 2, 4)
+        return k.reshape(k.shape[0], -1, k.shape[-2] * k.shape[-1])[:, : len(b)]
+
+    assert torch.allclose(block_k(eng, hb), block_k(solo, hs), atol=1e-4, rtol=1e-4)
+
+    cap = RepairStateCapture(tmp_path / "sparse_repair_state.pt", component_layers=[0])
+    eng.model.capture = cap
+    try:
+        order = ["turn", "instruction"]
+        seq = eng.link({"cache_keys": order, "recompute_tokens_per_block": [0, 8]}, suffix)
+    finally:
+        eng.model.capture = None
+    rows = list(seq.link_plan.recompute_positions)
+    slots = eng.kv.slots(seq.pages, torch.tensor(rows))
+    path = cap.save(eng.kv, slots, rows, [rows], None)
+    state = torch.load(path)
+    L = eng.model.cfg.num_layers
+    assert state["diagnostic_only"] and sorted(state["layer_outputs"]) == list(range(L))
+    assert set(state["component_outputs"][0]) == {"pre_attention_norm", "qkv_projection", "rope", "attention",
+                                                   "output_projection", "post_attention_norm", "mlp"}
+    assert state["repaired_kv"][0]["key"].shape[0] == len(rows)
+    view = RepairRowView.of("r", slots.tolist(), rows)
+    assert view.token_count == len(rows) and len(view.slot_digest) == 64
+    eng.free(seq)
