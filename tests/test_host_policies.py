@@ -138,3 +138,92 @@ def test_equivalence_audit_on_a_real_layout():
     aud = audit_layout(layout, "req-1")
     assert aud.status == "exact" and aud.token_delta == 0
     assert aud.baseline.sha256 == aud.assembled.sha256
+
+
+def _profile(**over):
+    from sglang_legolink_b200.host.group_profile import GroupRepairProfile, SCHEMA_VERSION, ShapeBands
+
+    kw = dict(profile_id="p", profile_version="1", schema_version=SCHEMA_VERSION, method="prefix_absorb_refresh_1",
+              supported_ordering="in_order_only", context_token_buckets=((100, 5000),), semantic_block_count_min=2,
+              semantic_block_count_max=8, execution_group_member_min=2, execution_group_member_max=4,
+              reconstruction_policy="prefix_absorb", member0_prefix_refresh_tokens=16, later_member_refresh="full",
+              requires_all_members_resident=True, requires_group_absent_for_reconstruction=True,
+              promotion="execution_group", fallback_policy="FULL_GROUP_RECOMPILE",
+              supported_member_shapes=("balanced", "front_heavy"),
+              member_shape_classifier=ShapeBands(1.5, 2.0, 6.0, 1.5),
+              compatibility={"model_id": "m", "tokenizer_fingerprint": "t", "adapter_id": "base"})
+    kw.update(over)
+    return GroupRepairProfile(**kw)
+
+
+def _greq(**over):
+    from sglang_legolink_b200.host.group_profile import GroupRequest
+
+    kw = dict(context_tokens=900, token_unit="model", semantic_block_count=3, request_member_ids=("a", "b"),
+              group_member_ids=("a", "b"), member_token_counts=(200, 180), members_resident=(True, True),
+              group_present=False, reconstruction_policy="prefix_absorb", member0_prefix_refresh_tokens=16,
+              later_member_refresh="full", compatibility={"model_id": "m", "tokenizer_fingerprint": "t",
+                                                          "adapter_id": "base"})
+    kw.update(over)
+    return GroupRequest(**kw)
+
+
+def test_group_repair_profile_contract_checks_and_routes(tmp_path):
+    from sglang_legolink_b200.host import group_profile as gp
+
+    p = _profile()
+    with pytest.raises(ValueError):
+        _profile(compatibility={"model_id": "m", "logits": "x"})
+    with pytest.raises(ValueError):
+        _profile(later_member_refresh="partial")
+    (tmp_path / "p.json").write_text(__import__("json").dumps(p.to_dict()))
+    assert gp.load_profile(tmp_path / "p.json").digest == p.digest
+    bad = dict(p.to_dict(), contract_digest="grqp-0")
+    with pytest.raises(ValueError):
+        gp.GroupRepairProfile.from_dict(bad)
+    cases = [({}, "ELIGIBLE"), ({"group_present": True}, "GROUP_ALREADY_PRESENT"),
+             ({"requested_profile_version": "2"}, "PROFILE_VERSION_MISMATCH"),
+             ({"compatibility": {"model_id": "x", "tokenizer_fingerprint": "t"}}, "MODEL_MISMATCH"),
+             ({"compatibility": {"model_id": "m", "tokenizer_fingerprint": "t", "adapter_id": "lora"}},
+              "COMPATIBILITY_MISMATCH"),
+             ({"token_unit": "estimated"}, "TOKEN_UNIT_NOT_MODEL"), ({"request_member_ids": ("b", "a")}, "REORDERED"),
+             ({"semantic_block_count": 9}, "UNSUPPORTED_BLOCK_COUNT"), ({"context_tokens": 9000}, "OUT_OF_CONTEXT_RANGE"),
+             ({"member_token_counts": (100, 400)}, "UNSUPPORTED_LAYOUT"),
+             ({"member0_prefix_refresh_tokens": 32}, "WRONG_RECONSTRUCTION_POLICY"),
+             ({"members_resident": (False, False)}, "MEMBERS_NOT_RESIDENT"),
+             ({"members_resident": (True, False)}, "PARTIAL_MEMBER_RESIDENCY")]
+    for over, code in cases:
+        assert gp.evaluate(_greq(**over), p).reason_code == code, over
+    assert gp.ShapeBands(1.5, 2.0, 6.0, 1.5).classify([600, 150, 160]) == "front_heavy"
+    r = gp.route(_greq(), p, promotion_feature_enabled=False)
+    assert r.route == "FULL_GROUP_RECOMPILE" and r.reason_code == "PROMOTION_FEATURE_DISABLED"
+    r = gp.route(_greq(), p, promotion_feature_enabled=True)
+    assert r.route == "PREFIX_ABSORB_RECONSTRUCT_AND_PROMOTE" and r.reconstruction_windows == (16, 180)
+    assert gp.route(_greq(group_present=True), p, promotion_feature_enabled=True).route == "GROUP_CACHE_HIT"
+    rows = gp.trace_rows(r, request_id="q1")
+    assert [x["event"] for x in rows] == ["repair_profile_checked", "repair_profile_eligible"]
+    with pytest.raises(ValueError):
+        gp.trace_rows(r, logits=[1.0])
+    gp.append_trace(tmp_path / "t.jsonl", rows)
+    assert len((tmp_path / "t.jsonl").read_text().splitlines()) == 2
+    assert gp.link_fields(r, "grp")["promote_reconstructed_group"] is True
+
+
+def test_group_profile_route_drives_engine_promotion(monkeypatch):
+    """An eligible route's Link fields make the runtime promote the group."""
+    import torch
+
+    from sglang_legolink_b200.host import group_profile as gp
+    from sglang_legolink_b200.models.config import PRESETS
+    from sglang_legolink_b200.models.qwen import QwenModel
+    from sglang_legolink_b200.runtime.engine import Engine
+
+    eng = Engine(QwenModel.random_init(PRESETS["tiny-qwen2"], seed=0), num_pages=256, page_size=16)
+    g = torch.Generator().manual_seed(3)
+    a, b = (torch.randint(0, 1024, (n,), generator=g).tolist() for n in (200, 180))
+    eng.compile(a, "a")
+    eng.compile(b, "b")
+    r = gp.route(_greq(), _profile(), promotion_feature_enabled=True)
+    monkeypatch.setenv("SGLANG_PIC_EXPERIMENTAL_GROUP_PROMOTION", "1")
+    seq = eng.link({"cache_keys": ["a", "b"], **gp.link_fields(r, "grp-ab")}, [5, 6, 7])
+    assert seq.promotion is not None and eng.registry.contains("grp-ab")
