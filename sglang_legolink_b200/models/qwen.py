@@ -67,6 +67,9 @@ class QwenModel:
         self.tp_rank, self.tp_size = tp_rank, tp_size
         self.comm = comm
         self.capture = None  # optional RepairStateCapture (diagnostics; extend forwards only)
+        from ..utils.layer_markers import LayerMarkers
+
+        self.markers = LayerMarkers.from_env()  # profiler regions (off unless enabled)
         assert cfg.num_heads % tp_size == 0, "num_heads must divide by tp_size"
         self.hq = cfg.num_heads // tp_size
         # KV heads are split when possible, else replicated (each rank keeps one).
@@ -249,6 +252,7 @@ class QwenModel:
             rw_o = rowwise_slices(fb.repair_meta, T, "output_projection")
             rw_ffn = rowwise_slices(fb.repair_meta, T, "ffn")
         cap = self.capture if fb.mode == "extend" else None
+        mk = self.markers
         for li, lw in enumerate(self.layers):
             if li > 0:
                 ops.fused_add_rmsnorm(h, residual, lw.in_norm, c.rms_norm_eps)
@@ -260,12 +264,13 @@ class QwenModel:
             if cap is not None and cap.wants(li):
                 cap.on_component(li, "qkv_projection", qkv=qkv)
                 cap.on_component(li, "rope", q=q)
-            if fb.mode == "decode":
-                ops.attention_decode(q, kv.k[li], kv.v[li], fb.page_table, fb.kv_lens, self.scale,
-                                     nsplit=fb.decode_nsplit, out=attn)
-            else:
-                ops.attention_prefill(q, kv.k, kv.v, li, fb.q_indptr, fb.positions, fb.page_table, fb.kv_lens,
-                                      self.scale, tiles=tiles, out=attn)
+            with mk.region("Attention", li, q=q):
+                if fb.mode == "decode":
+                    ops.attention_decode(q, kv.k[li], kv.v[li], fb.page_table, fb.kv_lens, self.scale,
+                                         nsplit=fb.decode_nsplit, out=attn)
+                else:
+                    ops.attention_prefill(q, kv.k, kv.v, li, fb.q_indptr, fb.positions, fb.page_table, fb.kv_lens,
+                                          self.scale, tiles=tiles, out=attn)
             # row-wise: each grouped row with the shapes it has alone
             for sl in rw_o or (slice(None),):
                 self._row_parallel(attn[sl], lw.o_w, o[sl])
@@ -275,9 +280,10 @@ class QwenModel:
             ops.fused_add_rmsnorm(o, residual, lw.post_norm, c.rms_norm_eps)
             if cap is not None and cap.wants(li):
                 cap.on_component(li, "post_attention_norm", hidden=o, residual=residual)
-            for sl in rw_ffn or (slice(None),):
-                ops.linear(o[sl], lw.gu_w, out=mlp[sl], swiglu_epilogue=True)
-                self._row_parallel(mlp[sl], lw.down_w, h[sl])
+            with mk.region("FFN", li, hidden=o):
+                for sl in rw_ffn or (slice(None),):
+                    ops.linear(o[sl], lw.gu_w, out=mlp[sl], swiglu_epilogue=True)
+                    self._row_parallel(mlp[sl], lw.down_w, h[sl])
             if cap is not None:
                 if cap.wants(li):
                     cap.on_component(li, "mlp", mlp_output=h)
@@ -330,7 +336,8 @@ class QwenModel:
         rows, sq = h, ss[2 * L - 1]
         if fb.logit_rows is not None:
             rows, sq = h.index_select(0, fb.logit_rows), sq.index_select(0, fb.logit_rows)
-        return ops.gemv_rownorm(rows, self.lm_head, None, sq, eps)
+        with self.markers.region("LMHead", hidden=rows):
+            return ops.gemv_rownorm(rows, self.lm_head, None, sq, eps)
 
     def _forward_fused_tp(self, fb: ForwardBatch, kv, return_hidden: bool = False) -> torch.Tensor:
         """Extend forward with the TP reductions fused into the kernels
@@ -389,7 +396,8 @@ class QwenModel:
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """Logits of this rank's vocab shard (the full vocab when tp_size == 1)."""
-        return ops.linear(hidden, self.lm_head)
+        with self.markers.region("LMHead", hidden=hidden):
+            return ops.linear(hidden, self.lm_head)
 
     def full_logits(self, local: torch.Tensor) -> torch.Tensor:
         if self.tp_size > 1 and self.comm is not None:

@@ -295,6 +295,10 @@ class Engine:
         """Token ids for the rows of ``logits`` (this rank's vocab shard).
         Greedy rows come from the argmax kernel; when any row samples, the
         full-vocab logits are gathered (TP) and those rows are redrawn."""
+        with self.model.markers.region("Sampling", logits=logits):
+            return self._sample_rows(logits, params, gens, greedy)
+
+    def _sample_rows(self, logits, params, gens, greedy):
         ids = greedy if greedy is not None else self.model.greedy(logits)
         if not any(not p.greedy for p in params):
             return ids

@@ -248,7 +248,7 @@ def serve(svc: RuntimeService, host: str = "127.0.0.1", port: int = 30000) -> Th
 
 def build_service(model: str = "tiny-qwen2", *, device: str = "cpu", tokenizer: Optional[str] = None,
                   legolink_only: bool = True, page_size: int = 16, num_pages: Optional[int] = None,
-                  max_context: int = 32768, seed: int = 0) -> RuntimeService:
+                  max_context: int = 32768, seed: int = 0, layerwise_markers: bool = False) -> RuntimeService:
     import torch
 
     from ..host.tokenizer import HashTokenizer, HFTokenizer
@@ -261,6 +261,10 @@ def build_service(model: str = "tiny-qwen2", *, device: str = "cpu", tokenizer: 
         m = QwenModel.from_pretrained(model, device=device, dtype=dtype)
     else:
         m = QwenModel.random_init(get_config(model), seed=seed, device=device, dtype=dtype)
+    if layerwise_markers:
+        from ..utils.layer_markers import LayerMarkers
+
+        m.markers = LayerMarkers(True)
     tok = HFTokenizer(tokenizer) if tokenizer else HashTokenizer(m.cfg.vocab_size, name=m.cfg.name)
     eng = Engine(m, page_size=page_size, num_pages=num_pages, max_context=max_context)
     sch = Scheduler(eng, legolink_only=legolink_only)
@@ -279,10 +283,12 @@ def main(argv=None) -> None:
     ap.add_argument("--context-length", type=int, default=32768)
     ap.add_argument("--allow-plain-generation", action="store_true")
     ap.add_argument("--skip-warmup", action="store_true")
+    ap.add_argument("--enable-layerwise-nvtx-marker", action="store_true",
+                    help="LegoLink::Attention / FFN / LMHead / Sampling profiler regions and NVTX ranges")
     a = ap.parse_args(argv)
     svc = build_service(a.model, device=a.device, tokenizer=a.tokenizer,
                         legolink_only=not a.allow_plain_generation, page_size=a.page_size,
-                        max_context=a.context_length)
+                        max_context=a.context_length, layerwise_markers=a.enable_layerwise_nvtx_marker)
     if not a.skip_warmup and os.getenv("SGLANG_PIC_WARMUP", "1") != "0":
         print("warmup", svc.warmup(int(os.getenv("SGLANG_PIC_WARMUP_BLOCK_TOKENS", "256")),
                                    int(os.getenv("SGLANG_PIC_WARMUP_LEGOLINK_K", "16"))), flush=True)

@@ -244,3 +244,24 @@ def test_rowwise_slices_and_state_capture(world, tmp_path, monkeypatch):
     view = RepairRowView.of("r", slots.tolist(), rows)
     assert view.token_count == len(rows) and len(view.slot_digest) == 64
     eng.free(seq)
+
+
+def test_layerwise_markers_label_the_profile(world):
+    """With markers on, a Link's profiler trace holds the Attention, FFN,
+    LMHead and Sampling regions; off, nothing is pushed."""
+    from sglang_legolink_b200.utils.layer_markers import LayerMarkers
+
+    eng, subs, suffix = world
+    assert not eng.model.markers.enabled
+    eng.model.markers = LayerMarkers(True)
+    try:
+        with torch.profiler.profile() as prof:
+            seq = eng.link({"cache_keys": ["turn", "instruction"], "recompute_tokens_per_block": [0, 4]}, suffix)
+        names = {e.name for e in prof.events()}
+        pushed = eng.model.markers.pushed
+    finally:
+        eng.model.markers = LayerMarkers(False)
+    eng.free(seq)
+    L = eng.model.cfg.num_layers
+    assert {"LegoLink::Attention", "LegoLink::FFN", "LegoLink::LMHead", "LegoLink::Sampling"} <= names
+    assert pushed == 2 * L + 2
