@@ -253,6 +253,11 @@ class QwenModel:
             rw_ffn = rowwise_slices(fb.repair_meta, T, "ffn")
         cap = self.capture if fb.mode == "extend" else None
         mk = self.markers
+        cmp_attn = False
+        if fb.mode == "extend":
+            from ..runtime.repair_diagnostics import compare_enabled
+
+            cmp_attn = compare_enabled("attention")
         for li, lw in enumerate(self.layers):
             if li > 0:
                 ops.fused_add_rmsnorm(h, residual, lw.in_norm, c.rms_norm_eps)
@@ -271,6 +276,15 @@ class QwenModel:
                 else:
                     ops.attention_prefill(q, kv.k, kv.v, li, fb.q_indptr, fb.positions, fb.page_table, fb.kv_lens,
                                           self.scale, tiles=tiles, out=attn)
+                    if cmp_attn:  # diagnostic: native kernel vs the fp32 torch statement, sampled rows
+                        from ..runtime.repair_diagnostics import compare_attention
+                        from ..utils.trace import emit_trace
+
+                        row = compare_attention(li, q, attn, kv.k[li], kv.v[li], fb.q_indptr, fb.positions,
+                                                fb.page_table, fb.kv_lens, self.scale)
+                        if fb.repair_meta is not None:
+                            fb.repair_meta.setdefault("native_operator_comparisons", []).append(row)
+                        emit_trace("repair_attention_compare", **row)
             # row-wise: each grouped row with the shapes it has alone
             for sl in rw_o or (slice(None),):
                 self._row_parallel(attn[sl], lw.o_w, o[sl])

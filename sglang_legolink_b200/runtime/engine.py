@@ -37,6 +37,7 @@ from ..ops import _ext
 from ..utils import launch_count
 from ..utils.trace import emit_trace, CudaTimer
 from .link_plan import ResolvedLinkPlan, resolve_link_plan
+from .repair_diagnostics import compare_enabled, compare_kv_link
 from .sampling import GREEDY, SamplingParams, make_generator, sample_rows
 
 
@@ -365,13 +366,31 @@ class Engine:
                 return out
             for (i, toks, ckey, bid, key, pages), first in zip(prepared, firsts):
                 try:
+                    if self.storage_mode(items[i][2] if len(items[i]) > 2 else None) == "clone":
+                        pages = self._clone_pages(pages)
                     out[i] = self._compile_register(toks, key, ckey, bid, pages, int(first))
                 except Exception as e:  # noqa: BLE001
                     out[i] = e
             return out
 
+    @staticmethod
+    def storage_mode(sub_context: Optional[dict]) -> str:
+        """How a Compile's KV is kept: "reference" (default: the computed
+        pages move to the registry) or "clone" (the registry gets a copy in
+        fresh pages and the computed pages are released).  Per Compile
+        (``pic_storage_mode``) or per deployment (``SGLANG_PIC_STORAGE_MODE``).
+        Reference: ``pic_runtime.py:1982-1988`` (mode), ``:3519-3530`` (clone)."""
+        import os
+
+        raw = (sub_context or {}).get("pic_storage_mode") or os.getenv("SGLANG_PIC_STORAGE_MODE", "reference")
+        mode = str(raw).lower()
+        if mode not in ("clone", "reference"):
+            raise ContractError("PIC storage mode must be 'clone' or 'reference'.")
+        return mode
+
     def _compile_prepare(self, token_ids, cache_key, sub_context, block_id):
         sc = dict(sub_context or {})
+        self.storage_mode(sc)  # validated before any work
         override = validate_physical_token_input(sc, label="sub_context")
         toks = [int(t) for t in (override if override is not None else token_ids)]
         if override is not None and token_ids and list(token_ids) != override:
@@ -381,6 +400,17 @@ class Engine:
         ckey = self.compat_key(sc.get("adapter_id"), sc.get("segmentation_policy_version"),
                                sc.get("legolink_policy_version"))
         return toks, ckey, str(block_id or sc.get("semantic_block_id") or cache_key)
+
+    def _clone_pages(self, pages: list[int]) -> list[int]:
+        """Copy whole pages (all layers, K and V) into fresh pages and release
+        the originals (checklist K15)."""
+        new = self._alloc_pages(len(pages))
+        src = torch.as_tensor(pages, dtype=torch.long, device=self.kv.k.device)
+        dst = torch.as_tensor(new, dtype=torch.long, device=self.kv.k.device)
+        self.kv.k[:, dst] = self.kv.k[:, src]
+        self.kv.v[:, dst] = self.kv.v[:, src]
+        self.alloc.release(pages)
+        return new
 
     def _compile_register(self, toks, cache_key: str, ckey, bid: str, pages, first: int) -> dict:
         n = len(toks)
@@ -547,6 +577,8 @@ class Engine:
                 args = (self.kv.k, self.kv.v, src.to(dev), dst.to(dev), lp.to(dev), gp.to(dev), self.model.cos_sin)
                 if owner is None:
                     ops.kv_link_rope(*args)
+                    if compare_enabled("kv_link"):  # diagnostic: fused kernel vs the torch statement
+                        emit_trace("kv_link_compare", rid=rid, **compare_kv_link(*args))
                 elif self.is_cuda:  # peer replica's pool, read over NVLink by the link kernel
                     kp, vp, sps, sls = self.peer_pools[owner]
                     ops.kv_link_rope(*args, src_k_ptr=kp, src_v_ptr=vp, src_page_size=sps, src_layer_stride=sls)

@@ -184,3 +184,67 @@ class RepairStateCapture:
         self.output_path.parent.mkdir(parents=True, exist_ok=True)
         torch.save(payload, self.output_path)
         return self.output_path
+
+
+# ----------------------------------------------------------- debug compares
+def compare_enabled(kind: str) -> bool:
+    """``kv_link``: ``SGLANG_PIC_COMPARE_FUSED_TORCH_KV_LINK``;
+    ``attention``: ``SGLANG_PIC_COMPARE_NATIVE_REFERENCE_ATTENTION``."""
+    return _flag({"kv_link": "SGLANG_PIC_COMPARE_FUSED_TORCH_KV_LINK",
+                  "attention": "SGLANG_PIC_COMPARE_NATIVE_REFERENCE_ATTENTION"}[kind])
+
+
+def _stats(got: torch.Tensor, want: torch.Tensor) -> dict:
+    d = got.float() - want.float()
+    return {"max_abs_error": float(d.abs().max().item()) if d.numel() else 0.0,
+            "mean_abs_error": float(d.abs().mean().item()) if d.numel() else 0.0,
+            "exact": bool(torch.equal(got.to(want.dtype), want)),
+            "allclose_bf16": bool(torch.allclose(got.float(), want.float(), atol=2e-2, rtol=2e-2))}
+
+
+def compare_kv_link(k_pool, v_pool, src_slots, dst_slots, local_pos, global_pos, cos_sin) -> dict:
+    """Destination rows the fused link kernel wrote, against the torch fp32
+    statement recomputed from the (untouched) source rows, all layers."""
+    from ..ops import reference as ref
+
+    ps = k_pool.shape[3]
+    dev = k_pool.device
+    src, dst = src_slots.long().to(dev), dst_slots.long().to(dev)
+    lp, gp = local_pos.long().to(dev), global_pos.long().to(dev)
+    # the reference writes into scratch pools holding only these rows
+    n = src.numel()
+    npg = (n + ps - 1) // ps
+    sk = torch.zeros(k_pool.shape[0], npg, *k_pool.shape[2:], dtype=k_pool.dtype, device=dev)
+    sv = torch.zeros_like(sk)
+    scratch = torch.arange(n, device=dev)
+    ref.kv_link_rope(sk, sv, src, scratch, lp, gp, cos_sin.to(dev), src_k_pool=k_pool, src_v_pool=v_pool)
+    kf = k_pool[:, dst // ps, :, dst % ps]
+    vf = v_pool[:, dst // ps, :, dst % ps]
+    kr = sk[:, scratch // ps, :, scratch % ps]
+    vr = sv[:, scratch // ps, :, scratch % ps]
+    return {"rows": int(n), "layers": int(k_pool.shape[0]), "key": _stats(kf, kr), "value": _stats(vf, vr)}
+
+
+def compare_attention(layer: int, q: torch.Tensor, out: torch.Tensor, k_pool_l, v_pool_l, q_indptr, q_pos,
+                      page_table, kv_lens, scale: float, max_rows: int = 128) -> dict:
+    """The repair attention's output rows against the fp32 torch statement
+    on a sample of at most ``max_rows`` rows (evenly spaced; every row is
+    independent given its position)."""
+    from ..ops import reference as ref
+
+    T = q.shape[0]
+    take = torch.linspace(0, T - 1, steps=min(T, max_rows)).round().long().unique().to(q.device)
+    qi = q_indptr.long().cpu()
+    req = torch.bucketize(take.cpu(), qi[1:], right=True)  # request of each sampled row
+    rows, got = [], []
+    for b in req.unique().tolist():
+        sel = take[(req == b).to(take.device)]
+        ptr = torch.tensor([0, sel.numel()], dtype=torch.int32, device=q.device)
+        y = ref.paged_attention(q[sel], k_pool_l, v_pool_l, ptr, q_pos[sel], page_table[b:b + 1], kv_lens[b:b + 1],
+                                scale)
+        rows.append(y)
+        got.append(out[sel])
+    want, have = torch.cat(rows), torch.cat(got)
+    return {"layer_id": int(layer), "rows_compared": int(want.shape[0]), "shape": list(out.shape),
+            **_stats(have, want), "native_norm": float(have.float().norm().item()),
+            "reference_norm": float(want.float().norm().item())}

@@ -265,3 +265,42 @@ def test_layerwise_markers_label_the_profile(world):
     L = eng.model.cfg.num_layers
     assert {"LegoLink::Attention", "LegoLink::FFN", "LegoLink::LMHead", "LegoLink::Sampling"} <= names
     assert pushed == 2 * L + 2
+
+
+def test_debug_compares_kv_link_and_attention(world, monkeypatch, tmp_path):
+    """Diagnostic compares (off by default): the link kernel's rows and the
+    repair attention rows against the torch fp32 statements, as trace rows."""
+    import json
+
+    eng, subs, suffix = world
+    path = tmp_path / "trace.jsonl"
+    monkeypatch.setenv("SGLANG_PIC_TRACE_PATH", str(path))
+    monkeypatch.setenv("SGLANG_PIC_COMPARE_FUSED_TORCH_KV_LINK", "1")
+    monkeypatch.setenv("SGLANG_PIC_COMPARE_NATIVE_REFERENCE_ATTENTION", "1")
+    seq = eng.link({"cache_keys": ["tool_output", "turn"], "recompute_tokens_per_block": [0, 8]}, suffix)
+    eng.free(seq)
+    rows = [json.loads(x) for x in path.read_text().splitlines()]
+    kv = [r for r in rows if r.get("event") == "kv_link_compare"]
+    at = [r for r in rows if r.get("event") == "repair_attention_compare"]
+    assert kv and kv[0]["key"]["allclose_bf16"] and kv[0]["value"]["exact"]
+    assert len(at) == eng.model.cfg.num_layers and all(r["allclose_bf16"] for r in at)
+
+
+def test_compile_clone_storage_mode(world):
+    """A clone-mode Compile registers a copy in fresh pages; linking it gives
+    the reference-mode block's answer; unknown modes are refused."""
+    eng, subs, suffix = world
+    g = torch.Generator().manual_seed(13)
+    t = torch.randint(0, 1024, (50,), generator=g).tolist()
+    r1 = eng.compile(t, "clone-ref")
+    r2 = eng.compile(t, "clone-copy", sub_context={"pic_storage_mode": "clone"})
+    assert r1["first_token"] == r2["first_token"]
+    assert set(eng.registry.handle("clone-ref")["pages"]).isdisjoint(eng.registry.handle("clone-copy")["pages"])
+    a = eng.link({"cache_keys": ["clone-ref"], "recompute_tokens_per_block": [0]}, suffix)
+    b = eng.link({"cache_keys": ["clone-copy"], "recompute_tokens_per_block": [0]}, suffix)
+    eng.decode([a], 6)
+    eng.decode([b], 6)
+    assert a.output_ids == b.output_ids
+    with pytest.raises(ContractError):
+        eng.compile(t, "clone-bad", sub_context={"pic_storage_mode": "mirror"})
+    eng.free(a), eng.free(b)
