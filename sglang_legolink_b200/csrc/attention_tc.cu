@@ -257,7 +257,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int ppb = TC_BN / ps;
       auto page_of = [&](int j) -> int {
         const int key0 = j * TC_BN + lane * ps;
-        return (lane < ppb && key0 <= max_pos) ? pt[key0 / ps] * Hkv + hk : -1;  // -1: out of range, zero fill
+        if (lane >= ppb || key0 > max_pos) return -1;  // -1: out of range, zero fill
+        if (key0 / ps >= pt_stride) {  // past the page-table row: recorded, zero fill
+          record_error(err, kErrBadIndex);
+          return -1;
+        }
+        return pt[key0 / ps] * Hkv + hk;
       };
       auto load_block = [&](const CUtensorMap* tm, uint8_t* dst, uint64_t* bar, int y) {
         if (lane == 0) mbar_arrive_expect_tx(bar, TC_KV_BYTES);
@@ -648,7 +653,11 @@ __global__ void __launch_bounds__(DT_THREADS)
   const int b = blockIdx.x / Hkv, hk = blockIdx.x % Hkv;
   const int split = blockIdx.y, nsplit = gridDim.y;
   const int g = Hq / Hkv;
-  const int kv_len = kv_lens[b];
+  int kv_len = kv_lens[b];
+  if (kv_len < 0 || kv_len > pt_stride * ps) {  // more keys than the page-table row holds: recorded, clamped
+    if (threadIdx.x == 0) record_error(err, kErrBadIndex);
+    kv_len = kv_len < 0 ? 0 : pt_stride * ps;
+  }
   const int fresh0 = kv_len - new_tokens;  // keys >= fresh0 are read only after the wait
   int chunk = (kv_len + nsplit - 1) / nsplit;
   chunk = (chunk + DT_BN - 1) / DT_BN * DT_BN;

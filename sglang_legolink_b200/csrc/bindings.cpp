@@ -25,11 +25,13 @@ int ll_rmsnorm(bf16* out, const bf16* x, bf16* residual, const bf16* w, int rows
                cudaStream_t stream);
 int ll_rope_qkv_write(const bf16* qkv, const int* positions, const int64_t* slots, const float* cos_sin, bf16* q_out,
                       bf16* k_pool, bf16* v_pool, const bf16* q_norm_w, const bf16* k_norm_w, int T, int Hq, int Hkv,
-                      int head_dim, int page_size, int qkv_ld, float eps, cudaStream_t stream);
+                      int head_dim, int page_size, int qkv_ld, float eps, int64_t slot_limit, int max_pos, int* err,
+                      cudaStream_t stream);
 int ll_kv_link_rope(bf16* dst_k, bf16* dst_v, const bf16* src_k, const bf16* src_v, const int64_t* src_slots,
                     const int64_t* dst_slots, const int* local_pos, const int* global_pos, const float* cos_sin, int n,
                     int num_layers, int Hkv, int head_dim, int src_page_size, int dst_page_size,
-                    int64_t src_layer_stride, int64_t dst_layer_stride, cudaStream_t stream);
+                    int64_t src_layer_stride, int64_t dst_layer_stride, int64_t src_slot_limit,
+                    int64_t dst_slot_limit, int max_pos, int* err, cudaStream_t stream);
 int ll_swiglu(bf16* out, const bf16* gu, int T, int inter, cudaStream_t stream);
 int ll_embedding(bf16* out, const int* ids, const bf16* table, int T, int hidden, int vocab_start, int vocab_end,
                  cudaStream_t stream);
@@ -262,6 +264,8 @@ void gemm_small_m_epi(const at::Tensor& a, const at::Tensor& w, const c10::optio
     e.Hkv = (int)Hkv;
     e.page_size = (int)page_size;
     e.eps = (float)eps;
+    e.slot_limit = k_pool_l->size(0) * page_size;
+    e.max_pos = (int)cos_sin->size(0);
   } else {
     TORCH_CHECK(false, "unknown epilogue mode");
   }
@@ -288,16 +292,18 @@ void rmsnorm(at::Tensor& out, const at::Tensor& x, const c10::optional<at::Tenso
 void rope_qkv_write(const at::Tensor& qkv, const at::Tensor& positions, const at::Tensor& slots,
                     const at::Tensor& cos_sin, at::Tensor& q_out, at::Tensor& k_pool_l, at::Tensor& v_pool_l,
                     const c10::optional<at::Tensor>& q_norm_w, const c10::optional<at::Tensor>& k_norm_w,
-                    int64_t Hq, int64_t Hkv, int64_t head_dim, double eps) {
+                    int64_t Hq, int64_t Hkv, int64_t head_dim, double eps, const at::Tensor& err) {
   CHECK_CUDA(qkv); CHECK_BF16(qkv); CHECK_I32(positions); CHECK_I64(slots); CHECK_F32(cos_sin);
-  CHECK_BF16(q_out); CHECK_BF16(k_pool_l); CHECK_BF16(v_pool_l);
+  CHECK_BF16(q_out); CHECK_BF16(k_pool_l); CHECK_BF16(v_pool_l); CHECK_I32(err);
   TORCH_CHECK(qkv.stride(1) == 1);
   const int T = qkv.size(0);
   const int ps = k_pool_l.size(2);
+  const int64_t slot_limit = k_pool_l.size(0) * ps;  // this layer's pool: [pages, Hkv, ps, D]
   c10::cuda::CUDAGuard g(qkv.device());
   check_rc(ll_rope_qkv_write(bp(qkv), positions.data_ptr<int>(), slots.data_ptr<int64_t>(), cos_sin.data_ptr<float>(),
                              bp(q_out), bp(k_pool_l), bp(v_pool_l), bp_opt(q_norm_w), bp_opt(k_norm_w), T, Hq, Hkv,
-                             head_dim, ps, qkv.stride(0), (float)eps, cur_stream()),
+                             head_dim, ps, qkv.stride(0), (float)eps, slot_limit, (int)cos_sin.size(0),
+                             err.data_ptr<int>(), cur_stream()),
            "ll_rope_qkv_write");
 }
 
@@ -306,19 +312,23 @@ void rope_qkv_write(const at::Tensor& qkv, const at::Tensor& positions, const at
 void kv_link_rope(at::Tensor& k_pool, at::Tensor& v_pool, int64_t src_k_ptr, int64_t src_v_ptr,
                   int64_t src_page_size, int64_t src_layer_stride, const at::Tensor& src_slots,
                   const at::Tensor& dst_slots, const at::Tensor& local_pos, const at::Tensor& global_pos,
-                  const at::Tensor& cos_sin) {
+                  const at::Tensor& cos_sin, const at::Tensor& err) {
   CHECK_CUDA(k_pool); CHECK_BF16(k_pool); CHECK_BF16(v_pool); CHECK_I64(src_slots); CHECK_I64(dst_slots);
   CHECK_I32(local_pos); CHECK_I32(global_pos); CHECK_F32(cos_sin); CHECK_CONTIG(k_pool); CHECK_CONTIG(v_pool);
+  CHECK_I32(err);
   const int L = k_pool.size(0), Hkv = k_pool.size(2), ps = k_pool.size(3), D = k_pool.size(4);
   const int n = src_slots.numel();
   const bf16* sk = src_k_ptr ? reinterpret_cast<const bf16*>(src_k_ptr) : bp(k_pool);
   const bf16* sv = src_v_ptr ? reinterpret_cast<const bf16*>(src_v_ptr) : bp(v_pool);
   const int sps = src_k_ptr ? (int)src_page_size : ps;
   const int64_t sls = src_k_ptr ? src_layer_stride : k_pool.stride(0);
+  // slots in a pool: one layer's elements / (Hkv * D) = pages * page_size
+  const int64_t src_limit = sls / ((int64_t)Hkv * D), dst_limit = k_pool.stride(0) / ((int64_t)Hkv * D);
   c10::cuda::CUDAGuard g(k_pool.device());
   check_rc(ll_kv_link_rope(bp(k_pool), bp(v_pool), sk, sv, src_slots.data_ptr<int64_t>(), dst_slots.data_ptr<int64_t>(),
                            local_pos.data_ptr<int>(), global_pos.data_ptr<int>(), cos_sin.data_ptr<float>(), n, L, Hkv,
-                           D, sps, ps, sls, k_pool.stride(0), cur_stream()),
+                           D, sps, ps, sls, k_pool.stride(0), src_limit, dst_limit, (int)cos_sin.size(0),
+                           err.data_ptr<int>(), cur_stream()),
            "ll_kv_link_rope");
 }
 

@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(256) rope_qkv_write_kernel(
     const bf16* __restrict__ qkv, const int* __restrict__ positions, const int64_t* __restrict__ slots,
     const float* __restrict__ cos_sin, bf16* __restrict__ q_out, bf16* __restrict__ k_pool,
     bf16* __restrict__ v_pool, const bf16* __restrict__ q_norm_w, const bf16* __restrict__ k_norm_w, int Hq,
-    int Hkv, int page_size, int qkv_ld, float eps) {
+    int Hkv, int page_size, int qkv_ld, float eps, int64_t slot_limit, int max_pos, int* err) {
   constexpr int D = 128;
   pdl_trigger();
   pdl_wait();
@@ -104,6 +104,10 @@ __global__ void __launch_bounds__(256) rope_qkv_write_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int pos = positions[t];
   const int64_t slot = slots[t];
+  if (slot < 0 || slot >= slot_limit || pos < 0 || pos >= max_pos) {  // checked, recorded, skipped
+    if (threadIdx.x == 0) record_error(err, kErrBadIndex);
+    return;
+  }
   const int64_t page = slot / page_size, off = slot % page_size;
   const float* cs = cos_sin + (size_t)pos * D;
   const float c0 = cs[lane], c1 = cs[lane + 32];
@@ -157,7 +161,7 @@ __global__ void __launch_bounds__(256) kv_link_rope_kernel(
     const bf16* __restrict__ src_v, const int64_t* __restrict__ src_slots, const int64_t* __restrict__ dst_slots,
     const int* __restrict__ local_pos, const int* __restrict__ global_pos, const float* __restrict__ cos_sin,
     int n, int num_layers, int Hkv, int src_page_size, int dst_page_size, int64_t src_layer_stride,
-    int64_t dst_layer_stride) {
+    int64_t dst_layer_stride, int64_t src_slot_limit, int64_t dst_slot_limit, int max_pos, int* err) {
   constexpr int D = 128;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -165,6 +169,14 @@ __global__ void __launch_bounds__(256) kv_link_rope_kernel(
   const int j = lane & 7;         // chunk within the head
   const int hsub = lane >> 3;     // 0..3: head offset within this pass
   const int lp = local_pos[gw], gp = global_pos[gw];
+  {
+    const int64_t s0 = src_slots[gw], d0 = dst_slots[gw];
+    if (s0 < 0 || s0 >= src_slot_limit || d0 < 0 || d0 >= dst_slot_limit || lp < 0 || lp >= max_pos || gp < 0 ||
+        gp >= max_pos) {  // checked, recorded, skipped (the whole row, every layer)
+      if (lane == 0) record_error(err, kErrBadIndex);
+      return;
+    }
+  }
   const bool same = (lp == gp);
   float dc[8], ds[8];
   if (!same) {
@@ -352,11 +364,11 @@ extern "C" int ll_rmsnorm(bf16* out, const bf16* x, bf16* residual, const bf16* 
 extern "C" int ll_rope_qkv_write(const bf16* qkv, const int* positions, const int64_t* slots, const float* cos_sin,
                                  bf16* q_out, bf16* k_pool, bf16* v_pool, const bf16* q_norm_w, const bf16* k_norm_w,
                                  int T, int Hq, int Hkv, int head_dim, int page_size, int qkv_ld, float eps,
-                                 cudaStream_t stream) {
+                                 int64_t slot_limit, int max_pos, int* err, cudaStream_t stream) {
   if (T <= 0) return 0;
   if (head_dim != 128) return -3;
   launch_pdl(rope_qkv_write_kernel, dim3(T), dim3(256), 0, stream, qkv, positions, slots, cos_sin, q_out, k_pool,
-             v_pool, q_norm_w, k_norm_w, Hq, Hkv, page_size, qkv_ld, eps);
+             v_pool, q_norm_w, k_norm_w, Hq, Hkv, page_size, qkv_ld, eps, slot_limit, max_pos, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
@@ -364,14 +376,16 @@ extern "C" int ll_kv_link_rope(bf16* dst_k, bf16* dst_v, const bf16* src_k, cons
                                const int64_t* src_slots, const int64_t* dst_slots, const int* local_pos,
                                const int* global_pos, const float* cos_sin, int n, int num_layers, int Hkv,
                                int head_dim, int src_page_size, int dst_page_size, int64_t src_layer_stride,
-                               int64_t dst_layer_stride, cudaStream_t stream) {
+                               int64_t dst_layer_stride, int64_t src_slot_limit, int64_t dst_slot_limit,
+                               int max_pos, int* err, cudaStream_t stream) {
   if (n <= 0) return 0;
   if (head_dim != 128) return -3;
   const int threads = 256;
   const int blocks = (int)(((int64_t)n * 32 + threads - 1) / threads);
   kv_link_rope_kernel<<<blocks, threads, 0, stream>>>(dst_k, dst_v, src_k, src_v, src_slots, dst_slots, local_pos,
                                                       global_pos, cos_sin, n, num_layers, Hkv, src_page_size,
-                                                      dst_page_size, src_layer_stride, dst_layer_stride);
+                                                      dst_page_size, src_layer_stride, dst_layer_stride,
+                                                      src_slot_limit, dst_slot_limit, max_pos, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 

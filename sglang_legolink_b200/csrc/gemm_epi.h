@@ -56,6 +56,8 @@ struct LLSmallMEpi {
   const ll_bf16_t* k_norm_w;
   int Hq, Hkv, page_size;
   float eps;
+  int64_t slot_limit;  // slots in this layer's pool (pages * page_size): larger slots are refused
+  int max_pos;         // rows of cos_sin: larger positions are refused
 };
 
 #ifdef __cplusplus

@@ -430,8 +430,10 @@ __global__ void __launch_bounds__(192, 2)
         pf_slot = epi.slots[lane];
       }
       const int p0 = __shfl_sync(0xffffffffu, pf_pos, 0);
-      pf_c0 = epi.cos_sin[(size_t)p0 * 128 + (f & 63)];
-      pf_s0 = epi.cos_sin[(size_t)p0 * 128 + 64 + (f & 63)];
+      if (p0 >= 0 && p0 < epi.max_pos) {  // an out-of-range row 0 is refused in the epilogue
+        pf_c0 = epi.cos_sin[(size_t)p0 * 128 + (f & 63)];
+        pf_s0 = epi.cos_sin[(size_t)p0 * 128 + 64 + (f & 63)];
+      }
       const bf16* nw = nb < epi.Hq ? epi.q_norm_w : (nb < epi.Hq + epi.Hkv ? epi.k_norm_w : nullptr);
       if (nw != nullptr) pf_w = __bfloat162float(nw[f]);
     }
@@ -470,6 +472,14 @@ __global__ void __launch_bounds__(192, 2)
         float x = bf16_round(v);
         const int64_t sl = __shfl_sync(0xffffffffu, pf_slot, m & 31);
         const int64_t slot = m < 32 ? sl : epi.slots[m];
+        const int pm0 = __shfl_sync(0xffffffffu, pf_pos, m & 31);
+        const int pos_m = m < 32 ? pm0 : epi.positions[m];
+        // checked per row (the same for all 128 threads, so the barriers
+        // below stay uniform): a bad slot or position is recorded, not written
+        if (slot < 0 || slot >= epi.slot_limit || pos_m < 0 || pos_m >= epi.max_pos) {
+          if (threadIdx.x == 64) record_error(err, kErrBadIndex);
+          return;
+        }
         const int64_t page = slot / epi.page_size, off = slot % epi.page_size;
         bf16* dst;
         if (nb < epi.Hq + epi.Hkv) {
@@ -486,8 +496,7 @@ __global__ void __launch_bounds__(192, 2)
           const int j = f & 63;
           float c = pf_c0, sn = pf_s0;
           if (m > 0) {
-            const int pm = __shfl_sync(0xffffffffu, pf_pos, m & 31);
-            const float* cs = epi.cos_sin + (size_t)(m < 32 ? pm : epi.positions[m]) * 128;
+            const float* cs = epi.cos_sin + (size_t)pos_m * 128;
             c = cs[j];
             sn = cs[64 + j];
           }
@@ -1115,7 +1124,7 @@ static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* 
     case LL_EPI_QKV_ROPE:
       if (N != (epi.Hq + 2 * epi.Hkv) * GEMM_BM || epi.Hq <= 0 || epi.Hkv <= 0 || epi.page_size <= 0 ||
           epi.positions == nullptr || epi.slots == nullptr || epi.cos_sin == nullptr || epi.q_out == nullptr ||
-          epi.k_pool == nullptr || epi.v_pool == nullptr)
+          epi.k_pool == nullptr || epi.v_pool == nullptr || epi.slot_limit <= 0 || epi.max_pos <= 0)
         return -3;
       break;
     default:

@@ -278,7 +278,7 @@ def rope_qkv_write(qkv, positions, slots, cos_sin, q_out, k_pool_l, v_pool_l, nu
         q_out.copy_(q)
         return q_out
     _cuda().rope_qkv_write(qkv, positions, slots, cos_sin, q_out, k_pool_l, v_pool_l, q_norm_w, k_norm_w,
-                           num_heads, num_kv_heads, head_dim, eps)
+                           num_heads, num_kv_heads, head_dim, eps, workspace(qkv.device).err)
     return q_out
 
 
@@ -459,4 +459,5 @@ def kv_link_rope(k_pool, v_pool, src_slots, dst_slots, local_pos, global_pos, co
                          src_k_pool=sk, src_v_pool=sv)
         return
     _cuda().kv_link_rope(k_pool, v_pool, int(src_k_ptr), int(src_v_ptr), int(src_page_size),
-                         int(src_layer_stride), src_slots, dst_slots, local_pos, global_pos, cos_sin)
+                         int(src_layer_stride), src_slots, dst_slots, local_pos, global_pos, cos_sin,
+                         workspace(k_pool.device).err)
