@@ -140,6 +140,8 @@ class SharedKVPool:
         self._hk = symm_mem.rendezvous(self.k, gname)
         self._hv = symm_mem.rendezvous(self.v, gname)
         self.alloc = _ext.host().PageAllocator(num_pages)
+        # held for the pool's lifetime, as in KVPool: padded decode rows write here
+        self.scratch_page = int(self.alloc.alloc(1)[0])
         self.layer_stride = num_pages * num_kv_heads * page_size * head_dim
 
     @property
