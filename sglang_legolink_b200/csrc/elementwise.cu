@@ -161,11 +161,17 @@ __global__ void __launch_bounds__(256) kv_link_rope_kernel(
     const bf16* __restrict__ src_v, const int64_t* __restrict__ src_slots, const int64_t* __restrict__ dst_slots,
     const int* __restrict__ local_pos, const int* __restrict__ global_pos, const float* __restrict__ cos_sin,
     int n, int num_layers, int Hkv, int src_page_size, int dst_page_size, int64_t src_layer_stride,
-    int64_t dst_layer_stride, int64_t src_slot_limit, int64_t dst_slot_limit, int max_pos, int* err) {
+    int64_t dst_layer_stride, int64_t src_slot_limit, int64_t dst_slot_limit, int max_pos, int* err,
+    int layer_groups) {
   constexpr int D = 128;
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  // warp -> (token, group of layers): few tokens spread their layers over
+  // several warps so that the dependent per-layer round trips overlap
+  const int64_t gwl = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (gw >= n) return;
+  if (gwl >= (int64_t)n * layer_groups) return;
+  const int gw = (int)(gwl / layer_groups), lgrp = (int)(gwl % layer_groups);
+  const int lpg = (num_layers + layer_groups - 1) / layer_groups;
+  const int layer0 = lgrp * lpg, layer1 = min(num_layers, layer0 + lpg);
   const int j = lane & 7;         // chunk within the head
   const int hsub = lane >> 3;     // 0..3: head offset within this pass
   const int lp = local_pos[gw], gp = global_pos[gw];
@@ -173,7 +179,7 @@ __global__ void __launch_bounds__(256) kv_link_rope_kernel(
     const int64_t s0 = src_slots[gw], d0 = dst_slots[gw];
     if (s0 < 0 || s0 >= src_slot_limit || d0 < 0 || d0 >= dst_slot_limit || lp < 0 || lp >= max_pos || gp < 0 ||
         gp >= max_pos) {  // checked, recorded, skipped (the whole row, every layer)
-      if (lane == 0) record_error(err, kErrBadIndex);
+      if (lane == 0 && lgrp == 0) record_error(err, kErrBadIndex);
       return;
     }
   }
@@ -193,7 +199,7 @@ __global__ void __launch_bounds__(256) kv_link_rope_kernel(
   const int64_t ss = src_slots[gw], dsl = dst_slots[gw];
   const int64_t sp = ss / src_page_size, so = ss % src_page_size;
   const int64_t dp = dsl / dst_page_size, dof = dsl % dst_page_size;
-  for (int layer = 0; layer < num_layers; ++layer) {
+  for (int layer = layer0; layer < layer1; ++layer) {
     for (int h0 = 0; h0 < Hkv; h0 += 4) {
       const int h = h0 + hsub;
       if (h >= Hkv) continue;
@@ -381,11 +387,16 @@ extern "C" int ll_kv_link_rope(bf16* dst_k, bf16* dst_v, const bf16* src_k, cons
   if (n <= 0) return 0;
   if (head_dim != 128) return -3;
   const int threads = 256;
-  const int blocks = (int)(((int64_t)n * 32 + threads - 1) / threads);
+  // about one resident wave of warps (148 SMs x 64 warps): fewer tokens
+  // than that split their layers over several warps
+  constexpr int64_t kTargetWarps = 148 * 64;
+  int groups = (int)((kTargetWarps + n - 1) / n);
+  groups = groups < 1 ? 1 : (groups > num_layers ? num_layers : groups);
+  const int blocks = (int)(((int64_t)n * groups * 32 + threads - 1) / threads);
   kv_link_rope_kernel<<<blocks, threads, 0, stream>>>(dst_k, dst_v, src_k, src_v, src_slots, dst_slots, local_pos,
                                                       global_pos, cos_sin, n, num_layers, Hkv, src_page_size,
                                                       dst_page_size, src_layer_stride, dst_layer_stride,
-                                                      src_slot_limit, dst_slot_limit, max_pos, err);
+                                                      src_slot_limit, dst_slot_limit, max_pos, err, groups);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
