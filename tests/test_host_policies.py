@@ -227,3 +227,33 @@ def test_group_profile_route_drives_engine_promotion(monkeypatch):
     monkeypatch.setenv("SGLANG_PIC_EXPERIMENTAL_GROUP_PROMOTION", "1")
     seq = eng.link({"cache_keys": ["a", "b"], **gp.link_fields(r, "grp-ab")}, [5, 6, 7])
     assert seq.promotion is not None and eng.registry.contains("grp-ab")
+
+
+def test_legacy_plan_bridge_is_refused_then_replayed_with_runtime_layout(tmp_path, monkeypatch):
+    """A pre-contract plan carries host-estimated layout: refused by default;
+    replayed with the legacy flag, the runtime derives its own layout."""
+    import torch
+
+    from sglang_legolink_b200.contract import ContractError
+    from sglang_legolink_b200.host.legacy_bridge import (LegacyBlock, build_legacy_link_plan, read_plan_file,
+                                                         write_plan_file)
+    from sglang_legolink_b200.models.config import PRESETS
+    from sglang_legolink_b200.models.qwen import QwenModel
+    from sglang_legolink_b200.runtime.engine import Engine
+
+    eng = Engine(QwenModel.random_init(PRESETS["tiny-qwen2"], seed=0), num_pages=256, page_size=16)
+    g = torch.Generator().manual_seed(5)
+    a, b = (torch.randint(0, 1024, (n,), generator=g).tolist() for n in (100, 60))
+    eng.compile(a, "la")
+    eng.compile(b, "lb")
+    query = [3, 4, 5, 6, 7]
+    plan = build_legacy_link_plan([LegacyBlock("A", "la", 100), LegacyBlock("B", "lb", 60)], request_id="old",
+                                  recompute_initial_tokens=8, mutable_token_estimate=3)  # estimate is off by 2
+    plan = read_plan_file(write_plan_file(plan, tmp_path / "plan.json"))
+    assert plan["imp_indices"] == list(range(100, 108)) + [160, 161, 162]
+    monkeypatch.delenv("SGLANG_PIC_ALLOW_LEGACY_LINK_FIELDS", raising=False)
+    with pytest.raises(ContractError):
+        eng.link(dict(plan), query)
+    monkeypatch.setenv("SGLANG_PIC_ALLOW_LEGACY_LINK_FIELDS", "1")
+    seq = eng.link(dict(plan), query)
+    assert list(seq.link_plan.recompute_positions) == list(range(100, 108)) + list(range(160, 165))
