@@ -589,7 +589,9 @@ constexpr int DT_THREADS = 160;
 constexpr int DT_MAXP = 1024;
 constexpr int DT_HALF = DT_BN * 128;                 // 8 KB: one 64-dim half of a 64-key block
 constexpr int DT_KV = 2 * DT_HALF;                   // 16 KB per K (or V) block
-constexpr int DT_SMEM = 1024 + 4096 + DT_STAGES * 2 * DT_KV + DT_MAXP * 4 + 128;
+constexpr int dt_smem(int stages) { return 1024 + 4096 + stages * 2 * DT_KV + DT_MAXP * 4 + 128; }
+constexpr int DT_SMEM = dt_smem(DT_STAGES);  // 3 stages (default)
+constexpr int DT_SMEM2 = dt_smem(2);          // 2 stages (LL_DECODE_STAGES=2): fits beside two 72 KB GEMV CTAs
 
 __device__ __forceinline__ uint32_t dt_swz(int key, int c16) {  // TMA 128-byte swizzle, two 64-dim halves
   return (uint32_t)((c16 >> 3) * DT_HALF + key * 128 + (((c16 & 7) ^ (key & 7)) << 4));
@@ -615,6 +617,7 @@ __device__ __forceinline__ void dt_mma(float (&c)[4], const uint32_t (&a)[4], ui
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+template <int ST>
 __global__ void __launch_bounds__(DT_THREADS)
     attn_decode_tma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                            const __grid_constant__ CUtensorMap tmKr, const __grid_constant__ CUtensorMap tmVr,
@@ -625,14 +628,14 @@ __global__ void __launch_bounds__(DT_THREADS)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sKV = smem;                                  // [stage][K|V][2 halves][64 keys][128 B]
-  uint8_t* sQb = sKV + DT_STAGES * 2 * DT_KV;           // 16 rows x 256 B
+  uint8_t* sQb = sKV + ST * 2 * DT_KV;           // 16 rows x 256 B
   int* spage = reinterpret_cast<int*>(sQb + 4096);
   uint64_t* full = reinterpret_cast<uint64_t*>(spage + DT_MAXP);
-  uint64_t* empty = full + DT_STAGES;
+  uint64_t* empty = full + ST;
   const uint32_t sQ = smem_u32(sQb);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) {
-    for (int i = 0; i < DT_STAGES; ++i) {
+    for (int i = 0; i < ST; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 4);
     }
@@ -681,14 +684,14 @@ __global__ void __launch_bounds__(DT_THREADS)
     const int p = lane >> 2, h = (lane >> 1) & 1, isv = lane & 1;
     bool waited = false;
     for (int blk = 0; blk < nblocks; ++blk) {
-      const int st = blk % DT_STAGES;
+      const int st = blk % ST;
       if (!waited && kbeg + (blk + 1) * DT_BN > fresh0) {
         pdl_wait();  // this block holds keys the previous kernel wrote
         waited = true;
       }
       bool w = true;
       if (lane == 0) {
-        w = mbar_wait(&empty[st], ((blk / DT_STAGES) & 1) ^ 1, err, kErrSmemEmptyTimeout);
+        w = mbar_wait(&empty[st], ((blk / ST) & 1) ^ 1, err, kErrSmemEmptyTimeout);
         if (w) mbar_arrive_expect_tx(&full[st], 2 * DT_KV);
       }
       if (!__shfl_sync(0xffffffffu, w, 0)) break;
@@ -744,8 +747,8 @@ __global__ void __launch_bounds__(DT_THREADS)
       dt_ldsm(sQ + dt_qswz(r, 2 * kk + (lane >> 4)), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
     }
     for (int blk = 0; blk < nblocks; ++blk) {
-      const int st = blk % DT_STAGES;
-      if (!mbar_wait(&full[st], (blk / DT_STAGES) & 1, err, kErrTmaFullTimeout)) break;
+      const int st = blk % ST;
+      if (!mbar_wait(&full[st], (blk / ST) & 1, err, kErrTmaFullTimeout)) break;
       const uint32_t sK = smem_u32(sKV + st * 2 * DT_KV);
       const uint32_t sV = sK + DT_KV;
       const int k0 = kbeg + blk * DT_BN + 16 * warp;  // this warp's 16 keys
@@ -993,20 +996,23 @@ extern "C" int ll_attn_decode_tma(const bf16* q, const bf16* k_pool, const bf16*
   if (make_pool_map(&tv, v_pool, 1, pages, Hkv, page_size)) return -2;
   if (make_pool_run_map(&tkr, k_pool, 1, pages, Hkv, page_size, DT_BN / page_size)) return -2;
   if (make_pool_run_map(&tvr, v_pool, 1, pages, Hkv, page_size, DT_BN / page_size)) return -2;
+  static int stages = -1;
+  if (stages < 0) {
+    const char* e = getenv("LL_DECODE_STAGES");
+    stages = (e != nullptr && atoi(e) == 2) ? 2 : 3;
+  }
+  auto kern = stages == 2 ? attn_decode_tma_kernel<2> : attn_decode_tma_kernel<3>;
+  const int smem = stages == 2 ? DT_SMEM2 : DT_SMEM;
   static int fits = -1;
   if (fits < 0) {
     int n = 0;
-    fits = cudaFuncSetAttribute(attn_decode_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DT_SMEM) ==
-                   cudaSuccess &&
-               cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_decode_tma_kernel, DT_THREADS, DT_SMEM) ==
-                   cudaSuccess &&
-               n >= 1
-           ? 1
-           : 0;
+    fits = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess &&
+                   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, DT_THREADS, smem) == cudaSuccess && n >= 1
+               ? 1
+               : 0;
   }
   if (!fits) return -7;
-  launch_pdl(attn_decode_tma_kernel, dim3(B * Hkv, nsplit), dim3(DT_THREADS), DT_SMEM, stream, tk, tv, tkr, tvr, q,
-             page_table,
-             pt_stride, kv_lens, out, ws_o, ws_ml, Hq, Hkv, page_size, scale_log2, new_tokens, err);
+  launch_pdl(kern, dim3(B * Hkv, nsplit), dim3(DT_THREADS), smem, stream, tk, tv, tkr, tvr, q, page_table, pt_stride,
+             kv_lens, out, ws_o, ws_ml, Hq, Hkv, page_size, scale_log2, new_tokens, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }

@@ -26,6 +26,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -284,26 +285,27 @@ __global__ void __launch_bounds__(192, 1)
 // Small-M (swap-AB, split-K) kernel.
 //   D^T[128 features, BNX rows] = W_tile[128, K] . A[BNX, K]^T
 // grid = (feature tiles, splits); each CTA does k-blocks [kb0, kb1).
-template <int BNX>
+template <int BNX, int RING_KB>
 struct SwapCfg {
   static constexpr int W_BYTES = GEMM_BM * GEMM_BK * 2;  // 16 KB
   static constexpr int X_BYTES = BNX * GEMM_BK * 2;
-  // A ring of <= 108 KB so that two CTAs share an SM: one CTA's tail then
+  // A ring of RING_KB: 108 KB lets two CTAs share an SM (one CTA's tail then
   // overlaps the next CTA's start, and two independent streams keep twice
-  // the weight bytes in flight (6 stages for BNX=16, 5 for 32, 4 for 64,
-  // 3 for 128).
-  static constexpr int STAGES = (108 * 1024) / (W_BYTES + X_BYTES);
+  // the weight bytes in flight); 72 KB leaves room for a third CTA, so the
+  // next kernel's CTAs can become resident and start streaming their weights
+  // while this kernel's last CTAs finish.
+  static constexpr int STAGES = (RING_KB * 1024) / (W_BYTES + X_BYTES);
   static constexpr int TMEM_COLS = BNX < 32 ? 32 : BNX;
   static constexpr int SMEM = STAGES * (W_BYTES + X_BYTES) + 1024 + 256;
 };
 
-template <int BNX>
+template <int BNX, int RING_KB>
 __global__ void __launch_bounds__(192, 2)
     gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                        bf16* __restrict__ C, const bf16* __restrict__ bias, int M, int N, int K, int ldc,
                        int kb_per_split, float* __restrict__ ws, int* __restrict__ tickets, int* err,
                        int w_tiled, const __grid_constant__ LLSmallMEpi epi) {
-  using Cfg = SwapCfg<BNX>;
+  using Cfg = SwapCfg<BNX, RING_KB>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1102,6 +1104,17 @@ extern "C" int ll_gemm_bf16_small_m(const bf16* A, int lda, const bf16* W, int l
                                  stream);
 }
 
+// Shared-memory ring of the small-M kernel in KB: 108 (default) or 72
+// (LL_GEMV_RING_KB=72: three CTAs fit on an SM).
+static int small_m_ring_kb() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("LL_GEMV_RING_KB");
+    v = (e != nullptr && atoi(e) == 72) ? 72 : 108;
+  }
+  return v;
+}
+
 static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc, const bf16* bias, int M,
                           int N, int K, int splits, float* ws, size_t ws_floats, int* tickets, int* err, int w_tiled,
                           const LLSmallMEpi& epi, cudaStream_t stream) {
@@ -1141,23 +1154,33 @@ static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* 
   if (w_tiled ? make_tmap_w_tiled(&tW, W, N, K) : make_tmap_2d(&tW, W, N, K, ldw, GEMM_BM)) return -2;
   if (make_tmap_2d(&tX, A, M, K, lda, BNX)) return -2;
   dim3 grid(ntiles, splits);
-#define LL_LAUNCH_S(BNX_)                                                                                \
+#define LL_LAUNCH_S(BNX_, RING_)                                                                         \
   do {                                                                                                   \
-    auto kern = gemm_swapab_kernel<BNX_>;                                                                \
-    if (SwapCfg<BNX_>::SMEM > max_smem_optin()) return -7;                                               \
+    auto kern = gemm_swapab_kernel<BNX_, RING_>;                                                         \
+    using C_ = SwapCfg<BNX_, RING_>;                                                                     \
+    if (C_::SMEM > max_smem_optin()) return -7;                                                          \
     static bool init = false;                                                                            \
     if (!init) {                                                                                         \
-      set_smem(kern, SwapCfg<BNX_>::SMEM);                                                               \
+      set_smem(kern, C_::SMEM);                                                                          \
       init = true;                                                                                       \
     }                                                                                                    \
-    launch_pdl(kern, grid, dim3(192), SwapCfg<BNX_>::SMEM, stream, tW, tX, C, bias, M, N, K, ldc, kb_per, ws, \
-               tickets, err, w_tiled, epi);                                                              \
+    launch_pdl(kern, grid, dim3(192), C_::SMEM, stream, tW, tX, C, bias, M, N, K, ldc, kb_per, ws, tickets, \
+               err, w_tiled, epi);                                                                       \
   } while (0)
-  switch (BNX) {
-    case 16: LL_LAUNCH_S(16); break;
-    case 32: LL_LAUNCH_S(32); break;
-    case 64: LL_LAUNCH_S(64); break;
-    default: LL_LAUNCH_S(128); break;
+  if (small_m_ring_kb() == 72) {
+    switch (BNX) {
+      case 16: LL_LAUNCH_S(16, 72); break;
+      case 32: LL_LAUNCH_S(32, 72); break;
+      case 64: LL_LAUNCH_S(64, 72); break;
+      default: LL_LAUNCH_S(128, 72); break;
+    }
+  } else {
+    switch (BNX) {
+      case 16: LL_LAUNCH_S(16, 108); break;
+      case 32: LL_LAUNCH_S(32, 108); break;
+      case 64: LL_LAUNCH_S(64, 108); break;
+      default: LL_LAUNCH_S(128, 108); break;
+    }
   }
 #undef LL_LAUNCH_S
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
