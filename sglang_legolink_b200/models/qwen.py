@@ -142,6 +142,18 @@ class QwenModel:
         self.lm_head = self._place(head[v0:v1])
         self.cos_sin = ref.rope_cos_sin_table(c.max_position_embeddings, c.rotary_dim, c.rope_theta).to(self.device)
 
+    def ensure_rope_positions(self, n: int) -> None:
+        """Makes the RoPE table cover positions [0, n) (it starts at
+        ``max_position_embeddings`` rows).  Called by the engine at
+        construction, before any CUDA graph captures the table's address.
+        Reference: the cos/sin cache extended on demand, ``pic_runtime.py:5051-5053``."""
+        if self.cos_sin is not None and self.cos_sin.shape[0] >= n:
+            return
+        c = self.cfg
+        rows = max(n, c.max_position_embeddings)
+        rows = (rows + 4095) // 4096 * 4096
+        self.cos_sin = ref.rope_cos_sin_table(rows, c.rotary_dim, c.rope_theta).to(self.device)
+
     def vocab_range(self) -> tuple[int, int]:
         v = self.cfg.vocab_size
         per = (v + self.tp_size - 1) // self.tp_size

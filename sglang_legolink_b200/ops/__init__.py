@@ -71,6 +71,11 @@ def workspace(device) -> _Workspace:
     return ws
 
 
+ERROR_NAMES = {1: "TMA full-barrier wait timed out", 2: "shared-memory empty-barrier wait timed out",
+               3: "TMEM full wait timed out", 4: "TMEM empty wait timed out", 5: "peer flag wait timed out",
+               6: "index past its bound (slot, position or page-table entry) refused"}
+
+
 def check_errors(device) -> int:
     """Read (and clear) the device error word set by bounded waits."""
     ws = workspace(device)

@@ -45,6 +45,12 @@ class RuntimeErrorAbort(RuntimeError):
     """A request-scoped failure: the request is aborted, the engine lives on."""
 
 
+class KernelFault(RuntimeErrorAbort):
+    """A kernel recorded an error in the device error word (a bounded wait
+    gave up, or an index past its bound was refused): the request that ran
+    it fails; the word is cleared, so later requests start clean."""
+
+
 class LinkSourceUnavailable(RuntimeErrorAbort):
     """A Link source is missing / stale / incompatible; the message carries
     the structured residency-recovery JSON."""
@@ -144,6 +150,7 @@ class Engine:
         self.page_size = page_size
         self.max_context = max_context
         self.is_cuda = self.device.type == "cuda"
+        model.ensure_rope_positions(max_context + 64)
         if kv_pool is None:
             if num_pages is None:
                 num_pages = self._auto_pages(mem_fraction)
@@ -291,6 +298,17 @@ class Engine:
             tiles=view[5].view(-1, 4) if self.is_cuda else None,
         )
 
+    def _kernel_check(self, what: str) -> None:
+        """Reads (and clears) the device error word after a synchronising
+        step; a recorded error aborts the request instead of passing silently.
+        Kernels that see the word set abandon their work, so an error left
+        uncleared would also slow every later kernel down."""
+        if not self.is_cuda:
+            return
+        code = ops.check_errors(self.device)
+        if code:
+            raise KernelFault(f"{what}: kernel error {code} ({ops.ERROR_NAMES.get(code, 'unknown')})")
+
     def _sample(self, logits: torch.Tensor, params: Sequence[SamplingParams] = (),
                 gens: Sequence[Optional[torch.Generator]] = (), greedy: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Token ids for the rows of ``logits`` (this rank's vocab shard).
@@ -359,6 +377,7 @@ class Engine:
                     fb.repair_meta = {"batch_execution_unit_size": len(prepared), "repair_ranges": ranges}
                 logits = self.model.forward(fb, self.kv)
                 firsts = self._sample(logits).tolist()
+                self._kernel_check("compile")
             except Exception as e:
                 for i, *_rest, pages in prepared:
                     self.alloc.release(pages)
@@ -591,6 +610,7 @@ class Engine:
             logits = self.model.forward(fb, self.kv)
             first = self._sample(logits, [sp], [gen])
         first_id = int(first[0].item())
+        self._kernel_check("link")
         emit_trace("model_link_complete", rid=rid, total_token_count=resolved.total_token_count,
                    recompute_rows=len(rows), linked_rows=nlinked)
         return Sequence_(rid=rid, token_ids=list(resolved.linked_token_ids), pages=pages,
@@ -695,6 +715,7 @@ class Engine:
                 fb = self._extend_batch([(toks[start:], list(range(start, n)), pages, n)])
                 logits = self.model.forward(fb, self.kv)
                 first = int(self._sample(logits, [sp], [gen])[0].item())
+                self._kernel_check("prefill")
             except Exception:
                 self.alloc.release(pages)
                 raise
@@ -779,6 +800,7 @@ class Engine:
                 hist[t].copy_(g["out"])
                 launch_count.add(g["launches"])
             out = hist[:, :B].t().tolist()
+            self._kernel_check("decode")
             stops = stop if isinstance(stop, (list, tuple)) else [stop] * B
             for s, toks, st in zip(seqs, out, stops):
                 n = steps
@@ -839,7 +861,9 @@ class Engine:
                           q_indptr=torch.arange(B + 1, dtype=torch.int32).to(dev), page_table=pt.to(dev),
                           kv_lens=kvl.to(dev), logit_rows=None)
         logits = self.model.forward(fb, self.kv)
-        return self._sample(logits, [s.sampling for s in seqs], [s.generator for s in seqs]).tolist()
+        out = self._sample(logits, [s.sampling for s in seqs], [s.generator for s in seqs]).tolist()
+        self._kernel_check("decode")
+        return out
 
     def _bucket(self, B: int) -> int:
         for b in (1, 2, 4, 8, 16, 32, 64):
@@ -864,9 +888,12 @@ class Engine:
         g["graph"].replay()
         launch_count.add(g["launches"])
         if any(not s.sampling.greedy for s in seqs):
-            return self._sample(g["logits"][:B], [s.sampling for s in seqs], [s.generator for s in seqs],
-                                greedy=g["out"][:B]).tolist()
-        return g["out"][:B].tolist()
+            out = self._sample(g["logits"][:B], [s.sampling for s in seqs], [s.generator for s in seqs],
+                               greedy=g["out"][:B]).tolist()
+        else:
+            out = g["out"][:B].tolist()
+        self._kernel_check("decode")
+        return out
 
     def _capture(self, bucket: int, max_pages: int, seqs) -> dict:
         dev = self.device

@@ -151,3 +151,30 @@ def test_scheduler_chunked_decode_streams_the_per_step_tokens():
     assert got[0] == (refs[0], "length")
     j = refs[1].index(stop)
     assert got[1] == (refs[1][: j + 1], "stop")
+
+
+def test_rope_table_covers_the_engine_context_and_kernel_errors_fail_the_request():
+    """Positions past the checkpoint's max_position_embeddings stay inside
+    the RoPE table (the engine extends it to its context); an error a kernel
+    records fails the request that ran it, and the word is cleared."""
+    import dataclasses
+
+    from sglang_legolink_b200.runtime.engine import KernelFault
+
+    cfg = dataclasses.replace(PRESETS["small-qwen2"], max_position_embeddings=512)
+    model = QwenModel.random_init(cfg, seed=0, device="cuda", dtype=torch.bfloat16)
+    eng = Engine(model, num_pages=512, page_size=16, max_context=2048)
+    assert model.cos_sin.shape[0] >= 2048
+    g = torch.Generator().manual_seed(9)
+    prompt = torch.randint(0, cfg.vocab_size, (600,), generator=g).tolist()
+    s = eng.prefill(prompt)
+    eng.decode([s], 8)  # positions 600..607, past the checkpoint's 512
+    assert ops.check_errors(torch.device("cuda")) == 0 and len(s.output_ids) == 9
+    # a recorded error fails the step that saw it (a decode step: its
+    # kernels are the split-K GEMVs and decode attention, whose early exits
+    # on a set error word are bounded waits and a bounded drain)
+    ops.workspace(torch.device("cuda")).err.fill_(6)
+    with pytest.raises(KernelFault):
+        eng.decode_step([s])
+    assert ops.check_errors(torch.device("cuda")) == 0
+    eng.free(s)
