@@ -1,7 +1,7 @@
 """Small single-kernel cases sized for `ncu --set full` captures (a few
 launches, a few hundred MB on the device), one per hot kernel:
 
-    python -m sglang_legolink_b200.benchmarks.ncu_cases {gemm,attn,gemv,decode,link,tp_reduce,tp_scatter}
+    python -m sglang_legolink_b200.benchmarks.ncu_cases {gemm,gemm_link,gemm_link_cublas,attn,gemv,decode,link,tp_reduce,tp_scatter}
 """
 import sys, os, math
 
@@ -22,6 +22,17 @@ elif case == "gemm":
     w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
     o = torch.empty(M, N // 2, device="cuda", dtype=torch.bfloat16)
     for _ in range(4): ops.linear(a, w, out=o, swiglu_epilogue=True)
+elif case in ("gemm_link", "gemm_link_cublas"):  # the Link's gate_up shape: ours vs cuBLAS (torch.matmul)
+    M, N, K = 5087, 37888, 3584
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) / math.sqrt(K)
+    o = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    for _ in range(3):
+        if case == "gemm_link":
+            ops.linear(a, w, out=o)
+        else:
+            torch.matmul(a, w.t(), out=o)
+    torch.cuda.synchronize()
 elif case == "attn":
     D, ps, Hq, Hkv, n, qrows = 128, 16, 28, 4, 8192, 4096
     pages = n // ps

@@ -23,6 +23,7 @@ would be refused by a LegoLink-only server), reference
 from __future__ import annotations
 
 import argparse
+import itertools
 import json
 import os
 import threading
@@ -31,7 +32,8 @@ import uuid
 from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
 from typing import Any, Optional
 
-from ..contract import ContractError, physical_token_ids_sha256, validate_physical_token_input
+from ..contract import (ContractError, physical_token_ids_sha256, validate_physical_token_input,
+                        validate_pic_link_request)
 from ..runtime.scheduler import Request, RequestRejected, Scheduler
 from ..runtime.sampling import SamplingParams
 
@@ -76,6 +78,9 @@ class RuntimeService:
                 ids = _prompt_ids(self.tokenizer, payload)
             return Request("compile", rid, ids, 1, stop, sub_context=sc)
         if link is not None:
+            # the request contract is checked on arrival (a copy: the engine
+            # checks it again against its own state)
+            validate_pic_link_request(copy.deepcopy(link))
             if isinstance(link, dict) and link.get("physical_token_layout_version") is not None:
                 ids = validate_physical_token_input(link, label="pic_link")
             else:
@@ -105,8 +110,11 @@ class RuntimeService:
                               **({"link": out["link"]} if "link" in out else {})}}
 
     def stream(self, payload: dict):
-        """Yields SSE chunk dicts; raises RequestRejected before the first chunk."""
+        """Yields SSE chunk dicts.  Arrival refusals (the request contract,
+        the scheduler's arrival checks) raise RequestRejected / ContractError
+        when the generator first runs, before any chunk."""
         req = self.build_request(payload)
+        self.scheduler.check(req)
         self.scheduler.submit(req)
         cid = f"chatcmpl-{req.rid}"
         while True:
@@ -225,12 +233,15 @@ def make_handler(svc: RuntimeService):
 
         def _stream(self, body: dict):
             gen = svc.stream(body)
+            # the request is validated when the generator first runs: take the
+            # first chunk before any header, so a refused request is a 400
+            first = next(gen)
             self.send_response(200)
             self.send_header("Content-Type", "text/event-stream")
             self.send_header("Cache-Control", "no-cache")
             self.send_header("Connection", "close")
             self.end_headers()
-            for chunk in gen:
+            for chunk in itertools.chain((first,), gen):
                 self.wfile.write(b"data: " + json.dumps(chunk).encode() + b"\n\n")
                 self.wfile.flush()
             self.wfile.write(b"data: [DONE]\n\n")
