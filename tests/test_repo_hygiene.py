@@ -1,0 +1,59 @@
+"""Source rules of this repository, checked on every run (CPU):
+
+* nothing committed imports, reads or runs the scratch directory;
+* no TMA or bulk load uses cluster multicast (this code runs on 1-8 GPUs;
+  ``tcgen05.commit`` with multicast is a different instruction and allowed);
+* none of the batched-copy runtime/driver calls that are closed on this GPU
+  pool appears anywhere (their names are assembled here, not spelled);
+* comments and docstrings name no build notes file and no machine path.
+"""
+
+import re
+import subprocess
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent.parent
+SELF = Path(__file__).resolve()
+
+
+def _sources(*suffixes):
+    out = subprocess.run(["git", "ls-files"], cwd=ROOT, capture_output=True, text=True).stdout.split()
+    files = [ROOT / f for f in out if f.endswith(suffixes)]
+    if not files:  # not a git checkout (an exported snapshot): walk the package and tests
+        files = [p for d in ("sglang_legolink_b200", "tests") for p in (ROOT / d).rglob("*") if p.suffix in suffixes]
+        files += [ROOT / "bench.py", ROOT / "__graft_entry__.py"]
+    return [f for f in files if f.exists() and f.resolve() != SELF]
+
+
+def test_no_committed_code_uses_the_scratch_directory():
+    pat = re.compile(r"""(['"/]_work[/'"]|import\s+_work|from\s+_work)""")
+    bad = [str(f.relative_to(ROOT)) for f in _sources(".py", ".sh", ".cu", ".cpp") if pat.search(f.read_text())]
+    assert not bad, bad
+
+
+def test_no_tma_or_bulk_load_uses_cluster_multicast():
+    mc = "multi" + "cast::" + "cluster"
+    bad = []
+    for f in _sources(".cu", ".cuh", ".h", ".cpp", ".py"):
+        for i, line in enumerate(f.read_text().splitlines(), 1):
+            if mc in line and "cp.async.bulk" in line:
+                bad.append(f"{f.relative_to(ROOT)}:{i}")
+    assert not bad, bad
+
+
+def test_closed_batched_copy_calls_are_absent():
+    names = [p + "Memcpy" + d + "Batch" + "Async" for p in ("cuda", "cu") for d in ("", "3D")]
+    bad = [f"{f.relative_to(ROOT)}: {n}" for f in _sources(".py", ".cu", ".cuh", ".h", ".cpp", ".sh")
+           for n in names if n in f.read_text()]
+    assert not bad, bad
+
+
+def test_sources_name_no_notes_file_or_machine_path():
+    notes = ["SUR" + "VEY", "DES" + "IGN.md", "VER" + "DICT", "ADV" + "ICE.md", "BASE" + "LINE.md"]
+    bad = []
+    for f in _sources(".py", ".cu", ".cuh", ".h", ".cpp"):
+        text = f.read_text()
+        for n in notes + ["/ro" + "ot/"]:
+            if n in text:
+                bad.append(f"{f.relative_to(ROOT)}: {n}")
+    assert not bad, bad
