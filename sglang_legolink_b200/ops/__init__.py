@@ -389,12 +389,31 @@ def attention_prefill_mma(q, k_pool_l, v_pool_l, q_indptr, q_pos, page_table, sc
 
 
 def decode_splits(batch: int, num_kv_heads: int, max_kv_len: int, num_sms: int = 148) -> int:
-    """Split count for decode attention: about two 4-warp CTAs per SM (the
-    residency limit of the kernel's 104 KB of shared memory), each covering
-    at least 128 keys (two 64-key blocks), capped at 1024 splits."""
-    target = 2 * num_sms
-    n = max(1, math.ceil(target / max(1, batch * num_kv_heads)))
-    return int(max(1, min(n, math.ceil(max_kv_len / 128), 1024)))
+    """Split count for decode attention, from a timing model of the kernel
+    fitted on B200: two 4-warp CTAs fit on an SM (``2 * num_sms`` per wave);
+    a CTA costs ~3 us of start-up + merge and streams at most ~80 keys/us
+    (its 3-stage TMA ring), and a wave cannot beat HBM (512 B of K+V per key
+    and KV head at ~6.5 TB/s); each split adds a little combine work.  The
+    fastest split count under that model is taken (at least 128 keys per
+    split, at most 1024 splits).  Split counts just past a wave boundary are
+    what the model avoids: at batch 16 / 4 KV heads / 32K keys, 5 splits
+    (320 CTAs: a second, nearly empty wave) ran 1.3x slower than 4."""
+    slots = 2 * num_sms
+    units = max(1, batch * num_kv_heads)
+    top = int(max(1, min(math.ceil(max_kv_len / 128), 1024)))
+    c0_us, keys_per_us, hbm_bytes_per_us = 3.0, 80.0, 6.5e6
+
+    def wave(active: int, keys: int) -> float:
+        return max(c0_us + keys / keys_per_us, active * keys * 512 / hbm_bytes_per_us)
+
+    best, best_t = 1, None
+    for s in range(1, top + 1):
+        keys = math.ceil(math.ceil(max_kv_len / s) / 64) * 64
+        full, rem = divmod(units * s, slots)
+        t = full * wave(slots, keys) + (wave(rem, keys) if rem else 0.0) + 0.02 * s
+        if best_t is None or t < best_t - 1e-9:
+            best, best_t = s, t
+    return best
 
 
 def attention_decode(q, k_pool_l, v_pool_l, page_table, kv_lens, scale, nsplit=None, out=None) -> torch.Tensor:
