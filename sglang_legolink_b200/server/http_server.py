@@ -15,6 +15,8 @@ http_server.py``, ``openai/protocol.py:696-709``, ``serving_chat.py:397-423``):
 * ``GET /v1/models``, ``GET /model_info``, ``GET /health``,
   ``POST /start_profile`` / ``/stop_profile`` (torch profiler window).
 
+``--tp-size`` / ``--dp-size`` start one process per GPU (``server/launch.py``).
+
 Startup warmup sends one Compile and one Link (a plain-generation warmup
 would be refused by a LegoLink-only server), reference
 ``pic_runtime.py:1381-1508``.
@@ -296,7 +298,20 @@ def main(argv=None) -> None:
     ap.add_argument("--skip-warmup", action="store_true")
     ap.add_argument("--enable-layerwise-nvtx-marker", action="store_true",
                     help="LegoLink::Attention / FFN / LMHead / Sampling profiler regions and NVTX ranges")
+    ap.add_argument("--tp-size", type=int, default=1, help="shard the model over this many GPUs (one process each)")
+    ap.add_argument("--dp-size", type=int, default=1, help="replicas sharing one block directory (one GPU each)")
+    ap.add_argument("--pp-size", type=int, default=1, help="pipeline parallelism: refused unless 1")
+    ap.add_argument("--tp-comm", choices=("fused", "nccl"), default="fused",
+                    help="TP boundary: fused NVLink kernels, or the collective library")
+    ap.add_argument("--dp-base-port", type=int, default=0, help="replica r > 0 listens on this + r (default --port)")
+    ap.add_argument("--dist-timeout", type=int, default=600, help="process-group timeout, seconds")
+    ap.add_argument("--seed", type=int, default=0)
     a = ap.parse_args(argv)
+    if a.tp_size > 1 or a.dp_size > 1 or a.pp_size != 1:
+        from .launch import launch
+
+        launch(a)
+        return
     svc = build_service(a.model, device=a.device, tokenizer=a.tokenizer,
                         legolink_only=not a.allow_plain_generation, page_size=a.page_size,
                         max_context=a.context_length, layerwise_markers=a.enable_layerwise_nvtx_marker)
