@@ -32,6 +32,7 @@ from __future__ import annotations
 import http.client
 import json
 import os
+import signal
 import socket
 import threading
 from collections import OrderedDict
@@ -130,12 +131,16 @@ class RouterService:
             self._owners.popitem(last=False)
         return hit
 
-    def pick(self, payload: dict) -> int:
+    def pick(self, payload: dict, reserve: bool = False) -> int:
+        """The replica for ``payload``; with ``reserve`` the choice is counted
+        in flight under the same lock, so concurrent requests spread out."""
         n = len(self.replicas)
         sc, link = payload.get("sub_context"), payload.get("pic_link")
         if isinstance(sc, dict) and sc.get("cache_key") is not None:
             o = self._owner(str(sc["cache_key"]))
             if o is not None and 0 <= o[0] < n:
+                if reserve:
+                    self._enter(o[0])
                 return o[0]
         local = [0] * n
         if isinstance(link, dict):
@@ -144,7 +149,11 @@ class RouterService:
                 if o is not None and 0 <= o[0] < n:
                     local[o[0]] += o[1]
         with self._lock:
-            return min(range(n), key=lambda r: (self.inflight[r], -local[r], self.routed[r], r))
+            r = min(range(n), key=lambda r: (self.inflight[r], -local[r], self.routed[r], r))
+            if reserve:
+                self.inflight[r] += 1
+                self.routed[r] += 1
+            return r
 
     def _enter(self, r: int) -> None:
         with self._lock:
@@ -157,8 +166,7 @@ class RouterService:
 
     # ------------------------------------------------------------ API calls
     def complete(self, payload: dict) -> dict:
-        r = self.pick(payload)
-        self._enter(r)
+        r = self.pick(payload, reserve=True)
         try:
             out = self.replicas[r].complete(payload)
         finally:
@@ -167,8 +175,7 @@ class RouterService:
         return out
 
     def stream(self, payload: dict):
-        r = self.pick(payload)
-        self._enter(r)
+        r = self.pick(payload, reserve=True)
         try:
             for chunk in self.replicas[r].stream(payload):
                 yield chunk
@@ -276,6 +283,11 @@ def rank_main(a, rank: int, world: int, local: int, ready=None) -> None:
     ctrl = control_group()
     eng, tok, name, directory = _build_rank(a, rank, world, local)
     stop = getattr(a, "stop_event", None) or threading.Event()
+    if threading.current_thread() is threading.main_thread():
+        # rank 0 turns SIGINT / SIGTERM into an orderly shutdown of every
+        # rank; the others leave only on rank 0's message, between steps
+        for sig in (signal.SIGINT, signal.SIGTERM):
+            signal.signal(sig, (lambda *_: stop.set()) if rank == 0 else signal.SIG_IGN)
     try:
         if a.tp_size > 1:
             if rank != 0:
@@ -292,7 +304,7 @@ def rank_main(a, rank: int, world: int, local: int, ready=None) -> None:
                 print(f"serving TP={world} on http://{a.host}:{a.port}", flush=True)
                 if ready is not None:
                     ready.put(a.port)
-                stop.wait()
+                _wait(stop)
                 srv.shutdown()
             finally:
                 sch.stop()
@@ -315,7 +327,7 @@ def rank_main(a, rank: int, world: int, local: int, ready=None) -> None:
             if ready is not None:
                 ready.put(a.port)
         if rank == 0:
-            stop.wait()
+            _wait(stop)
             dist.broadcast_object_list(["stop"], src=0, group=ctrl)
         else:
             box = [None]
@@ -325,6 +337,11 @@ def rank_main(a, rank: int, world: int, local: int, ready=None) -> None:
     finally:
         dist.barrier(group=ctrl)
         dist.destroy_process_group()
+
+
+def _wait(stop) -> None:
+    while not stop.wait(0.5):
+        pass
 
 
 def _spawn_entry(rank: int, world: int, port: int, a) -> None:
@@ -345,5 +362,9 @@ def launch(a) -> None:
         return
     import torch.multiprocessing as mp
 
+    # the children inherit the ignored signals; rank 0 installs its own
+    # handlers, and this process waits for every child to finish
+    for sig in (signal.SIGINT, signal.SIGTERM):
+        signal.signal(sig, signal.SIG_IGN)
     mp.start_processes(_spawn_entry, args=(world, _free_port(), a), nprocs=world, join=True,
                        start_method="spawn")
