@@ -184,6 +184,13 @@ class Engine:
             widest = max(2 * model.inter, (model.hq + 2 * model.hkv) * self.cfg.head_dim, self.cfg.hidden_size)
             ws.reserve_gemm(8 * 128 * max(widest, model.lm_head.shape[0]) // 2, 4096)
 
+    def release_graphs(self) -> None:
+        """Drops the captured decode graphs.  A TP model's graphs hold NCCL
+        calls, which must be released before the process group is destroyed."""
+        if self.is_cuda:
+            torch.cuda.synchronize(self.device)
+        self._graphs.clear()
+
     # ---------------------------------------------------------------- setup
     def _auto_pages(self, frac: float) -> int:
         c, m = self.cfg, self.model

@@ -335,6 +335,7 @@ def rank_main(a, rank: int, world: int, local: int, ready=None) -> None:
         srv.shutdown()
         sch.stop()
     finally:
+        eng.release_graphs()
         dist.barrier(group=ctrl)
         dist.destroy_process_group()
 
