@@ -211,7 +211,7 @@ def check_parallel_args(tp: int, dp: int, pp: int) -> None:
         raise ContractError("--tp-size and --dp-size cannot both exceed 1")
 
 
-def _build_rank(a, rank: int, world: int, local: int):
+def _build_rank(a, rank: int, world: int, local: int, ctrl=None):
     """(engine, tokenizer, model name, directory) of this rank."""
     import torch
     import torch.distributed as dist
@@ -255,7 +255,9 @@ def _build_rank(a, rank: int, world: int, local: int):
 
             per_page = 2 * m.cfg.num_layers * m.hkv * a.page_size * m.cfg.head_dim * 2
             free, _ = torch.cuda.mem_get_info(dev)
-            pages = max(64, int(free * 0.85 - (2 << 30)) // per_page)
+            pages = torch.tensor([max(64, int(free * 0.85 - (2 << 30)) // per_page)])
+            dist.all_reduce(pages, op=dist.ReduceOp.MIN, group=ctrl)  # symmetric memory: one size on all ranks
+            pages = int(pages)
             pool = SharedKVPool(m.cfg.num_layers, pages, m.hkv, a.page_size, m.cfg.head_dim, dtype, dev)
             kw.update(kv_pool=pool, peer_pools={r: pool.peer(r) for r in range(world) if r != rank})
     eng = Engine(m, page_size=a.page_size, max_context=a.context_length,
@@ -281,7 +283,7 @@ def rank_main(a, rank: int, world: int, local: int, ready=None) -> None:
         kw = {"device_id": torch.device("cuda", local)} if cuda else {}
         dist.init_process_group("nccl" if cuda else "gloo", timeout=timedelta(seconds=a.dist_timeout), **kw)
     ctrl = control_group()
-    eng, tok, name, directory = _build_rank(a, rank, world, local)
+    eng, tok, name, directory = _build_rank(a, rank, world, local, ctrl)
     stop = getattr(a, "stop_event", None) or threading.Event()
     if threading.current_thread() is threading.main_thread():
         # rank 0 turns SIGINT / SIGTERM into an orderly shutdown of every
