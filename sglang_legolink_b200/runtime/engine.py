@@ -923,7 +923,8 @@ class Engine:
                 self.model.greedy(self.model.forward(fb, self.kv), out=out)
         torch.cuda.current_stream(dev).wait_stream(s)
         graph = torch.cuda.CUDAGraph()
-        with launch_count.Recorder() as rec, torch.cuda.graph(graph):
+        # the capture stream belongs to the current device: make it the pool's
+        with torch.cuda.device(dev), launch_count.Recorder() as rec, torch.cuda.graph(graph):
             logits = self.model.forward(fb, self.kv)
             self.model.greedy(logits, out=out)
         st.update(graph=graph, out=out, logits=logits, fb=fb, launches=rec.n)

@@ -108,6 +108,13 @@ class Scheduler:
             self._thread.join(timeout=30)
 
     def _loop(self) -> None:
+        # the current CUDA device is per thread: this one drives the engine's
+        # GPU (graph capture, streams and events use the current device)
+        dev = getattr(self.engine, "device", None)
+        if dev is not None and dev.type == "cuda":
+            import torch
+
+            torch.cuda.set_device(dev)
         while not self._stop.is_set():
             did = self.step()
             if not did:
