@@ -162,6 +162,32 @@ void tp_wait(int64_t cnt, int64_t target, const at::Tensor& err) {
            "ll_tp_wait");
 }
 
+// Decode TP boundary: residual [rows, H] += sum over ranks of part[d] rows;
+// out = RMSNorm(residual) * w.  epoch: this rank's int64 [2] (zeroed once).
+void tp_decode_allreduce_norm(at::Tensor& residual, const at::Tensor& w, at::Tensor& out, double eps, int64_t rows,
+                              std::vector<int64_t> part_ptrs, std::vector<int64_t> cnt_ptrs, at::Tensor& epoch,
+                              int64_t rank, int64_t world, const at::Tensor& err) {
+  CHECK_CUDA(residual); CHECK_BF16(residual); CHECK_CONTIG(residual); CHECK_BF16(w); CHECK_BF16(out);
+  CHECK_CONTIG(out); CHECK_ALIGN16(residual); CHECK_ALIGN16(out); CHECK_ALIGN16(w);
+  TORCH_CHECK(epoch.scalar_type() == at::kLong && epoch.numel() >= 2 && epoch.is_cuda());
+  TORCH_CHECK((int64_t)part_ptrs.size() == world && (int64_t)cnt_ptrs.size() == world && world <= LL_MAX_TP_RANKS);
+  const int H = residual.size(1);
+  TORCH_CHECK(residual.size(0) >= rows && out.size(0) >= rows && out.size(1) == H && w.numel() == H);
+  LLTpDecode td{};
+  for (int i = 0; i < world; ++i) {
+    TORCH_CHECK(part_ptrs[i] % 16 == 0, "partial buffer must be 16-byte aligned");
+    td.part[i] = reinterpret_cast<const void*>(part_ptrs[i]);
+    td.cnt[i] = reinterpret_cast<unsigned long long*>(cnt_ptrs[i]);
+  }
+  td.epoch = reinterpret_cast<unsigned long long*>(epoch.data_ptr<int64_t>());
+  td.rank = (int)rank;
+  td.world = (int)world;
+  c10::cuda::CUDAGuard g(residual.device());
+  check_rc(ll_tp_decode_allreduce_norm(residual.data_ptr(), w.data_ptr(), out.data_ptr(), (float)eps, H, (int)rows,
+                                       &td, err.data_ptr<int>(), cur_stream()),
+           "ll_tp_decode_allreduce_norm");
+}
+
 // swiglu: w is the interleaved gate/up weight and out holds silu(gate) * up
 // (N / 2 columns).
 void gemm_small_m(const at::Tensor& a, const at::Tensor& w, const c10::optional<at::Tensor>& bias, at::Tensor& out,
@@ -425,6 +451,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tp", &gemm_tp);
   m.def("tp_reduce_norm_gather", &tp_reduce_norm_gather);
   m.def("tp_wait", &tp_wait);
+  m.def("tp_decode_allreduce_norm", &tp_decode_allreduce_norm);
   m.def("attn_prefill_tc_set_variant", [](int64_t v) { return ll_attn_prefill_tc_set_variant((int)v); });
   m.def("attn_prefill_tc_trace", []() {
     auto t = at::zeros({256 * 20}, at::kLong);

@@ -194,3 +194,149 @@ extern "C" int ll_tp_wait(const void* cnt, unsigned long long target, int* err, 
                                                                        target, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
+
+// ---------------------------------------------------------------- decode
+// Decode boundary of a TP layer: each rank's row-parallel GEMV wrote its
+// partial rows [rows][H] into its own symmetric buffer; this kernel, on every
+// rank, is a one-shot all-reduce fused with the residual add and RMSNorm:
+//
+//   * CTA 0 announces "my partial is complete" by a release-add of 1 to every
+//     rank's arrival counter (the GEMV before it on the stream has finished);
+//   * each CTA waits (bounded) until its own counter reaches world x epoch;
+//   * one CTA per row loads the row from every rank's buffer over NVLink (all
+//     loads of a rank issued back to back), sums residual + partials in fp32
+//     in rank order (so every rank computes the same bits), stores the new
+//     residual and writes RMSNorm(residual) * w;
+//   * the last CTA advances this rank's epoch.
+//
+// The caller alternates two partial buffers between consecutive calls.  A
+// rank rewrites buffer b only in call i + 2, after passing call i + 1's wait,
+// which every peer joins only after finishing its call-i reads of b, so no
+// end-of-call barrier is needed.
+namespace ll {
+constexpr int TPD = 256;
+template <int VPT>
+__global__ void __launch_bounds__(TPD)
+    tp_decode_allreduce_norm_kernel(bf16* __restrict__ residual, const bf16* __restrict__ w, bf16* __restrict__ out,
+                                    float eps, int H, int rows, const __grid_constant__ LLTpDecode td, int* err) {
+  __shared__ int s_ok;
+  __shared__ unsigned long long s_e;
+  __shared__ float red[TPD / 32];
+  if (threadIdx.x == 0) {
+    const unsigned long long e = *reinterpret_cast<volatile unsigned long long*>(td.epoch) + 1ull;
+    s_e = e;
+    if (blockIdx.x == 0) {
+      __threadfence_system();
+      for (int d = 0; d < td.world; ++d) red_release_sys_add(td.cnt[d], 1ull);
+    }
+    s_ok = wait_counter_geq(td.cnt[td.rank], e * (unsigned long long)td.world, err) ? 1 : 0;
+  }
+  __syncthreads();
+  const int nvec = H / 8;
+  const int row = blockIdx.x;
+  if (s_ok && row < rows) {
+    uint4* rr = reinterpret_cast<uint4*>(residual + (size_t)row * H);
+    float v[VPT][8];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int idx = threadIdx.x + i * TPD;
+      uint4 b = idx < nvec ? rr[idx] : make_uint4(0, 0, 0, 0);
+      const uint32_t* bu = reinterpret_cast<const uint32_t*>(&b);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(bu[j]);
+        v[i][2 * j] = f.x;
+        v[i][2 * j + 1] = f.y;
+      }
+    }
+#pragma unroll 2
+    for (int d = 0; d < td.world; ++d) {
+      const uint4* pr = reinterpret_cast<const uint4*>(static_cast<const bf16*>(td.part[d]) + (size_t)row * H);
+      uint4 a[VPT];
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int idx = threadIdx.x + i * TPD;
+        a[i] = idx < nvec ? __ldcg(pr + idx) : make_uint4(0, 0, 0, 0);  // not through L1: peer data
+      }
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const uint32_t* au = reinterpret_cast<const uint32_t*>(&a[i]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16x2(au[j]);
+          v[i][2 * j] += f.x;
+          v[i][2 * j + 1] += f.y;
+        }
+      }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int idx = threadIdx.x + i * TPD;
+      if (idx < nvec) {
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          // the norm reads the fp32 sum, as the unfused add + RMSNorm does
+          o[j] = pack_bf16x2(v[i][2 * j], v[i][2 * j + 1]);
+          ss += v[i][2 * j] * v[i][2 * j] + v[i][2 * j + 1] * v[i][2 * j + 1];
+        }
+        rr[idx] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < TPD / 32; ++i) tot += red[i];
+    const float rstd = rsqrtf(tot / H + eps);
+    uint4* orow = reinterpret_cast<uint4*>(out + (size_t)row * H);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int idx = threadIdx.x + i * TPD;
+      if (idx < nvec) {
+        const uint4 wv = reinterpret_cast<const uint4*>(w)[idx];
+        const uint32_t* wu = reinterpret_cast<const uint32_t*>(&wv);
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16x2(wu[j]);
+          o[j] = pack_bf16x2(v[i][2 * j] * rstd * f.x, v[i][2 * j + 1] * rstd * f.y);
+        }
+        orow[idx] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned int* ticket = reinterpret_cast<unsigned int*>(td.epoch + 1);
+    if (atomicAdd(ticket, 1u) == gridDim.x - 1) {
+      *reinterpret_cast<volatile unsigned int*>(ticket) = 0u;
+      __threadfence();
+      *reinterpret_cast<volatile unsigned long long*>(td.epoch) = s_e;
+    }
+  }
+}
+}  // namespace ll
+
+// One CTA per row; every rank must make the same sequence of calls.
+extern "C" int ll_tp_decode_allreduce_norm(void* residual, const void* w, void* out, float eps, int H, int rows,
+                                           const LLTpDecode* td, int* err, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (H % 8 || H > 8 * TPD * 4 || rows <= 0 || rows > 1024) return -3;
+  if (td->world < 1 || td->world > LL_MAX_TP_RANKS || td->rank < 0 || td->rank >= td->world) return -3;
+  const int vpt = (H / 8 + TPD - 1) / TPD;
+  bf16* r = static_cast<bf16*>(residual);
+  const bf16* wp = static_cast<const bf16*>(w);
+  bf16* o = static_cast<bf16*>(out);
+#define LL_TPD(V) ll::tp_decode_allreduce_norm_kernel<V><<<rows, ll::TPD, 0, stream>>>(r, wp, o, eps, H, rows, *td, err)
+  switch (vpt) {
+    case 1: LL_TPD(1); break;
+    case 2: LL_TPD(2); break;
+    case 3: LL_TPD(3); break;
+    default: LL_TPD(4); break;
+  }
+#undef LL_TPD
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}

@@ -26,6 +26,17 @@ struct LLTpGather {
   int rank, world, rows_per_rank;
 };
 
+// Decode boundary (one-shot all-reduce + residual + RMSNorm): part[d] is
+// rank d's partial rows of this call, cnt[d] rank d's arrival counter, epoch
+// this rank's [calls completed, CTA ticket] (device memory, so a CUDA graph
+// replays the boundary unchanged).
+struct LLTpDecode {
+  const void* part[LL_MAX_TP_RANKS];
+  unsigned long long* cnt[LL_MAX_TP_RANKS];
+  unsigned long long* epoch;
+  int rank, world;
+};
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -35,6 +46,8 @@ int ll_tp_reduce_norm_gather(const void* slots, void* residual, const void* w, f
                              const struct LLTpGather* tg, int* err, void* stream);
 int ll_tp_reduce_norm_gather_grid(int rows);
 int ll_tp_wait(const void* cnt, unsigned long long target, int* err, void* stream);
+int ll_tp_decode_allreduce_norm(void* residual, const void* w, void* out, float eps, int H, int rows,
+                                const struct LLTpDecode* td, int* err, void* stream);
 #ifdef __cplusplus
 }
 #endif

@@ -242,6 +242,9 @@ class QwenModel:
             return self._forward_fused_tp(fb, kv, return_hidden)
         if fb.mode == "decode" and not return_hidden and self._decode_fusable(T):
             return self._forward_decode_fused(fb, kv)
+        if (fb.mode == "decode" and not return_hidden and getattr(self.comm, "name", "") == "fused"
+                and fb.input_ids.is_cuda and self.comm.decode_fusable(T)):
+            return self._forward_decode_tp(fb, kv)
         H, D = c.hidden_size, c.head_dim
         qkv_n = (self.hq + 2 * self.hkv) * D
         x = ops.embedding(fb.input_ids, self.embed, out=self._buf("x", (T, H)))
@@ -319,6 +322,44 @@ class QwenModel:
         rows = h if fb.logit_rows is None else h.index_select(0, fb.logit_rows)
         if return_hidden:
             return rows
+        return self.logits(rows)
+
+    def _forward_decode_tp(self, fb: ForwardBatch, kv) -> torch.Tensor:
+        """TP decode step whose row-parallel reductions are fused kernels:
+        each o_proj / down GEMV writes its partial rows into this rank's
+        symmetric buffer, and one kernel per boundary sums every rank's rows
+        over NVLink, adds the residual and applies the next RMSNorm (the
+        reference's NCCL all-reduce + fused add-norm, ``models/qwen2.py:80-86,
+        162-168``)."""
+        c, comm, mk = self.cfg, self.comm, self.markers
+        T = fb.num_rows
+        H, D, eps = c.hidden_size, c.head_dim, c.rms_norm_eps
+        x = ops.embedding(fb.input_ids, self.embed, out=self._buf("x", (T, H)))
+        residual = self._buf("res", (T, H))
+        residual.copy_(x)
+        h = self._buf("h", (T, H))
+        ops.rmsnorm(residual, self.layers[0].in_norm, eps, out=h)
+        q = self._buf("q", (T, self.hq, D))
+        attn = self._buf("attn", (T, self.hq * D))
+        qkv = self._buf("qkv", (T, (self.hq + 2 * self.hkv) * D))
+        mlp = self._buf("mlp", (T, self.inter))
+        o = self._buf("o", (T, H))
+        n = len(self.layers)
+        for li, lw in enumerate(self.layers):
+            ops.linear(h, lw.qkv_w, lw.qkv_b, out=qkv)
+            ops.rope_qkv_write(qkv, fb.positions, fb.slots, self.cos_sin, q, kv.k[li], kv.v[li], self.hq, self.hkv,
+                               D, lw.q_norm, lw.k_norm, eps)
+            with mk.region("Attention", li, q=q):
+                ops.attention_decode(q, kv.k[li], kv.v[li], fb.page_table, fb.kv_lens, self.scale,
+                                     nsplit=fb.decode_nsplit, out=attn)
+            ops.linear(attn, lw.o_w, out=comm.decode_part(T))
+            comm.decode_allreduce_norm(T, residual, lw.post_norm, eps, o)
+            with mk.region("FFN", li, hidden=o):
+                ops.linear(o, lw.gu_w, out=mlp, swiglu_epilogue=True)
+                ops.linear(mlp, lw.down_w, out=comm.decode_part(T))
+                nxt = self.layers[li + 1].in_norm if li + 1 < n else self.final_norm
+                comm.decode_allreduce_norm(T, residual, nxt, eps, h)
+        rows = h if fb.logit_rows is None else h.index_select(0, fb.logit_rows)
         return self.logits(rows)
 
     def _decode_fusable(self, T: int) -> bool:

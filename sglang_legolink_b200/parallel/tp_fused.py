@@ -23,8 +23,13 @@ so every rank holds the others' base addresses.  The counters only grow;
 this object keeps each counter's cumulative target, so every rank must run
 the same sequence of fused calls (as it does the same forward).
 
-Decode (a few rows) and short prefills keep the NCCL path inherited from
-:class:`~.tp.NcclTPComm`.
+Decode steps (up to ``MAX_DECODE_ROWS`` rows) use a fourth kernel after
+each row-parallel GEMV, :meth:`decode_allreduce_norm`: the GEMV writes its
+partial rows into this rank's symmetric buffer (two buffers, alternating
+call by call), and the kernel sums every rank's rows over NVLink (one-shot
+all-reduce), adds the residual and applies the next RMSNorm.  Its epoch lives
+in device memory, so the decode CUDA graphs replay it unchanged.  Short
+prefills keep the NCCL path inherited from :class:`~.tp.NcclTPComm`.
 """
 
 from __future__ import annotations
@@ -39,6 +44,8 @@ from .tp import NcclTPComm
 
 # below this many (padded) rows a forward takes the NCCL path
 MIN_FUSED_ROWS = 512
+# decode steps with at most this many rows use the fused decode boundary
+MAX_DECODE_ROWS = 64
 
 
 def _round_up(x: int, m: int) -> int:
@@ -72,9 +79,20 @@ class FusedTPComm(NcclTPComm):
         self.g_cnt_ptrs = [p + 8 for p in self.slot_cnt_ptrs]
         self.slot_target = 0
         self.g_target = 0
+        # decode boundary: two partial buffers, one arrival counter per rank,
+        # this rank's [epoch, ticket]
+        self.dpart = symm_mem.empty((2 * MAX_DECODE_ROWS * hidden,), dtype=torch.bfloat16, device=device)
+        self.dcnt = symm_mem.empty((2,), dtype=torch.int64, device=device)
+        self.dcnt.zero_()
+        self.depoch = torch.zeros(2, dtype=torch.int64, device=device)
+        self._hdp = symm_mem.rendezvous(self.dpart, gname)
+        self._hdc = symm_mem.rendezvous(self.dcnt, gname)
+        self.dpart_ptrs = [int(p) for p in self._hdp.buffer_ptrs]
+        self.dcnt_ptrs = [int(p) for p in self._hdc.buffer_ptrs]
+        self._dparity = 0
         torch.cuda.synchronize(device)
         dist.barrier(group=self.group)  # every counter is zero before any peer adds to it
-        self.stats = {"fused_gemms": 0, "fused_reduces": 0}
+        self.stats = {"fused_gemms": 0, "fused_reduces": 0, "fused_decode_reduces": 0}
 
     # ------------------------------------------------------------ geometry
     def rows_per_rank(self, T: int) -> int:
@@ -91,6 +109,25 @@ class FusedTPComm(NcclTPComm):
     def slot_view(self, T: int) -> torch.Tensor:
         R = self.rows_per_rank(T)
         return self.slots[: self.size * R * self.hidden].view(self.size, R, self.hidden)
+
+    def decode_fusable(self, T: int) -> bool:
+        return T <= MAX_DECODE_ROWS
+
+    def decode_part(self, T: int) -> torch.Tensor:
+        """This rank's buffer for the next row-parallel GEMV's partial rows."""
+        n = MAX_DECODE_ROWS * self.hidden
+        return self.dpart[self._dparity * n: self._dparity * n + T * self.hidden].view(T, self.hidden)
+
+    def decode_allreduce_norm(self, T: int, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                              out: torch.Tensor) -> None:
+        """residual[:T] += the sum over ranks of their :meth:`decode_part`
+        rows; out[:T] = RMSNorm(residual) * w.  Flips the partial buffer."""
+        off = self._dparity * MAX_DECODE_ROWS * self.hidden * 2
+        ops._cuda().tp_decode_allreduce_norm(residual, w, out, float(eps), T, [p + off for p in self.dpart_ptrs],
+                                             self.dcnt_ptrs, self.depoch, self.rank, self.size,
+                                             ops.workspace(residual.device).err)
+        self._dparity ^= 1
+        self.stats["fused_decode_reduces"] += 1
 
     # ------------------------------------------------------------- kernels
     def reduce_norm_gather(self, residual: torch.Tensor, w: torch.Tensor, eps: float, T: int,

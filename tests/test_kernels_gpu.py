@@ -332,3 +332,53 @@ def test_gemm_small_m_tile_major_weights(M, N, K):
     out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
     ops._small_m(ops._cuda(), ops.workspace(DEV), a, wt, None, out)
     assert _rel(out, a.float() @ w.float().t()) < 1e-2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows,H", [(1, 5120), (16, 5120), (64, 3584), (7, 1024)])
+def test_tp_decode_allreduce_norm_single_rank(rows, H):
+    """The decode TP boundary with one rank: residual += partial; out =
+    RMSNorm(residual) * w, against fp32 torch; consecutive calls alternate
+    buffers and advance the device epoch, also when replayed from a CUDA
+    graph."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(rows * 7 + H)
+    w = (torch.rand(H, device=dev, generator=g) + 0.5).to(torch.bfloat16)
+    res = torch.randn(rows, H, device=dev, generator=g).to(torch.bfloat16)
+    parts = [torch.randn(rows, H, device=dev, generator=g).to(torch.bfloat16) for _ in range(2)]
+    out = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
+    cnt = torch.zeros(2, dtype=torch.int64, device=dev)
+    epoch = torch.zeros(2, dtype=torch.int64, device=dev)
+    err = ops.workspace(dev).err
+    k = ops._cuda()
+
+    def call(i):
+        k.tp_decode_allreduce_norm(res, w, out, 1e-6, rows, [parts[i % 2].data_ptr()], [cnt.data_ptr()], epoch, 0, 1,
+                                   err)
+
+    def expect(r, p):
+        s = r.float() + p.float()
+        return s.to(torch.bfloat16), (s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float())
+
+    for i in range(3):
+        r_exp, o_exp = expect(res, parts[i % 2])
+        call(i)
+        torch.cuda.synchronize()
+        assert torch.equal(res, r_exp)
+        assert _rel(out.float(), o_exp) < 1e-2
+    assert int(epoch[0]) == 3 and int(cnt[0]) == 3 and ops.check_errors(dev) == 0
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s), torch.cuda.graph(graph, stream=s):
+        call(0)
+        call(1)
+    torch.cuda.current_stream().wait_stream(s)
+    for rep in range(3):
+        r_exp, _ = expect(res, parts[0])
+        r_exp, o_exp = expect(r_exp, parts[1])
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(res, r_exp)
+        assert _rel(out.float(), o_exp) < 1e-2
+    assert int(epoch[0]) == 9 and int(epoch[1]) == 0 and ops.check_errors(dev) == 0

@@ -62,8 +62,30 @@ def main():
         outs = [None, None]
         dist.all_gather_object(outs, s.output_ids)
         ok = ok and outs[0] == outs[1] and fused.stats["fused_gemms"] > 0
+        ok = ok and fused.stats["fused_decode_reduces"] > 0
         if rank == 0:
             print(name, "link tokens", outs[0], "fused stats", fused.stats, flush=True)
+        # one eager decode step: the fused decode boundary (one-shot all-reduce
+        # + add + RMSNorm over NVLink) against NCCL all-reduce + add-norm
+        from sglang_legolink_b200.runtime.engine import ForwardBatch
+
+        for B in (1, 4):
+            seqs = [s] * B
+            ids, pos, slots, pt, kvl = eng._decode_inputs(seqs, B, len(s.pages))
+            fb = ForwardBatch(mode="decode", input_ids=ids.to(dev), positions=pos.to(dev), slots=slots.to(dev),
+                              q_indptr=torch.arange(B + 1, dtype=torch.int32).to(dev), page_table=pt.to(dev),
+                              kv_lens=kvl.to(dev), logit_rows=None)
+            m.comm = fused
+            a = m.forward(fb, eng.kv).float()
+            m.comm = nccl
+            b = m.forward(fb, eng.kv).float()
+            m.comm = fused
+            torch.cuda.synchronize()
+            e = ops.check_errors(dev)
+            rel = ((a - b).norm() / b.norm()).item()
+            if rank == 0:
+                print(name, "decode B", B, "fused vs nccl rel", rel, "err", e, flush=True)
+            ok = ok and rel < 2e-2 and e == 0
         eng._graphs.clear()
     if rank == 0 and ok:
         print("TP_FUSED_OK", flush=True)
