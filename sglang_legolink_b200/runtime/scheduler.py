@@ -57,6 +57,7 @@ class Request:
     seq: Optional[Sequence_] = None
     ttft_s: Optional[float] = None
     sampling: SamplingParams = GREEDY
+    resume: Optional[list] = None  # tokens generated before a retraction (plain requests)
 
 
 class Scheduler:
@@ -141,6 +142,9 @@ class Scheduler:
             req = self._next_waiting()
             if req is None:
                 break
+            if req.resume is not None and self.running and not self._fits(req):
+                self._deferred.insert(0, req)  # a retracted request waits for pages
+                break
             batch.append(req)
         did = bool(batch)
         if batch:
@@ -218,14 +222,18 @@ class Scheduler:
                 if seq.length + req.max_new_tokens > self.max_context:
                     eng.free(seq)
                     raise RequestRejected("overlength Link (total tokens + max_tokens exceeds the context window)")
+            elif req.resume is not None:  # re-admitted after a retraction
+                seq = eng.prefill(list(req.input_ids) + list(req.resume), rid=req.rid, sampling=req.sampling)
+                seq.output_ids[:0] = req.resume
             else:
                 seq = eng.prefill(req.input_ids, rid=req.rid, sampling=req.sampling)
             req.seq = seq
-            req.ttft_s = time.perf_counter() - req.created
+            if req.ttft_s is None:
+                req.ttft_s = time.perf_counter() - req.created
             first = seq.output_ids[-1]
             req.events.put(("token", first))
             self.stats["admitted"] += 1
-            if req.max_new_tokens <= 1 or first in req.stop_ids:
+            if len(seq.output_ids) >= req.max_new_tokens or first in req.stop_ids:
                 self._finish(req, "stop" if first in req.stop_ids else "length")
             else:
                 self.running.append(req)
@@ -236,13 +244,49 @@ class Scheduler:
             emit_trace("legolink_request_failed_closed", rid=req.rid, kind=req.kind, reason=repr(e)[:500])
             req.events.put(("error", f"internal error: {e!r}\n{traceback.format_exc(limit=3)}"))
 
+    LINK_RETRACTED = ("LegoLink request was retracted under KV pressure; its linked KV layout cannot be "
+                      "replayed, so it fails closed instead of being re-queued.")
+
+    def _pages_free(self) -> int:
+        eng = self.engine
+        return (eng.alloc.num_free + eng.radix.evictable_pages() + eng.registry.capacity_evictable_pages())
+
+    def _retract_for(self, steps: int) -> None:
+        """Before a decode of ``steps`` tokens: while the running sequences
+        need more new pages than the pool can give, retract the most recently
+        admitted one.  A Link fails closed (its re-prefill could not rebuild
+        the linked layout); a plain request is re-queued and resumes from its
+        prompt + generated tokens (reference ``pic_runtime.py:2978-3007``)."""
+        ps = self.engine.page_size
+
+        def need():
+            return sum(max(0, -(-(r.seq.length + steps) // ps) - len(r.seq.pages)) for r in self.running)
+
+        while len(self.running) > 1 and need() > self._pages_free():
+            r = self.running.pop()
+            out = list(r.seq.output_ids)
+            self.engine.free(r.seq)
+            self.stats["retracted"] = self.stats.get("retracted", 0) + 1
+            if r.kind == "link":
+                emit_trace("legolink_request_failed_closed", rid=r.rid, kind="link", reason="link_request_retracted")
+                r.events.put(("error", self.LINK_RETRACTED))
+            else:
+                emit_trace("request_retracted", rid=r.rid, generated=len(out))
+                r.resume, r.seq = out, None
+                self._deferred.insert(0, r)
+
+    def _fits(self, req: Request) -> bool:
+        n = len(req.input_ids) + len(req.resume or ()) + 1
+        return -(-n // self.engine.page_size) <= self._pages_free()
+
     def _decode(self) -> None:
-        seqs = [r.seq for r in self.running]
         eng = self.engine
         k = 1
         if (self.decode_chunk > 1 and self.waiting.empty() and not self._deferred and eng.use_cuda_graphs
                 and all(r.sampling.greedy for r in self.running)):
             k = min(self.decode_chunk, min(r.max_new_tokens - len(r.seq.output_ids) for r in self.running))
+        self._retract_for(max(1, k))
+        seqs = [r.seq for r in self.running]
         if k >= 2:
             # nothing is waiting: k steps back to back on the device, tokens
             # streamed when the chunk returns
