@@ -35,11 +35,13 @@ SMALL_M_MAX = 128
 # ----------------------------------------------------------------- workspace
 class _Workspace:
     """Per-device scratch: error word, split-K partials + tickets, decode
-    partials.  Sized up front by the engine so CUDA-graph replays never see a
-    reallocated buffer."""
+    partials.  Sized up front by the engine; a buffer that has to grow later
+    is replaced, and the old one is kept alive, because a captured CUDA graph
+    may still point at it."""
 
     def __init__(self, device: torch.device):
         self.device = device
+        self._retired: list = []
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         self.gemm_ws = torch.empty(0, dtype=torch.float32, device=device)
         self.tickets = torch.zeros(4096, dtype=torch.int32, device=device)
@@ -48,13 +50,16 @@ class _Workspace:
 
     def reserve_gemm(self, floats: int, tiles: int = 0) -> None:
         if self.gemm_ws.numel() < floats:
+            self._retired.append(self.gemm_ws)
             self.gemm_ws = torch.empty(floats, dtype=torch.float32, device=self.device)
         if self.tickets.numel() < tiles:
+            self._retired.append(self.tickets)
             self.tickets = torch.zeros(tiles, dtype=torch.int32, device=self.device)
 
     def reserve_decode(self, rows: int, nsplit: int, head_dim: int = 128) -> None:
         need = rows * nsplit
         if self.dec_o.numel() < need * head_dim:
+            self._retired += [self.dec_o, self.dec_ml]
             self.dec_o = torch.empty(need * head_dim, dtype=torch.float32, device=self.device)
             self.dec_ml = torch.empty(need * 2, dtype=torch.float32, device=self.device)
 
