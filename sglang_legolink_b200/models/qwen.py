@@ -83,6 +83,7 @@ class QwenModel:
         self.cos_sin: Optional[torch.Tensor] = None
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
         self._bufs: dict = {}
+        self.buf_generation = 0  # bumped whenever a scratch buffer is replaced by a larger one
 
     # ------------------------------------------------------------ weights
     def _kv_head_range(self) -> tuple[int, int]:
@@ -227,6 +228,10 @@ class QwenModel:
         for s in shape:
             n *= s
         if b is None or b.numel() < n or b.dtype != dtype:
+            if b is not None:
+                # the old memory is freed: captured decode graphs that point
+                # into it must be dropped before they replay (Engine._graph)
+                self.buf_generation += 1
             b = torch.empty(max(n, 1), dtype=dtype, device=self.device)
             self._bufs[name] = b
         return b[:n].view(*shape)

@@ -167,6 +167,7 @@ class Engine:
         self.use_cuda_graphs = use_cuda_graphs and self.is_cuda
         self.decode_chunk = 64  # greedy steps per chained decode chunk (one host read per chunk)
         self._graphs: dict = {}
+        self._graphs_gen = model.buf_generation
         self._lock = threading.RLock()
         self._rid = 0
         self.stats = {"compiles": 0, "links": 0, "prefills": 0, "decode_steps": 0, "remote_blocks_linked": 0}
@@ -773,10 +774,7 @@ class Engine:
                 self._ensure_capacity(s, s.length + steps)
             bucket = self._bucket(B)
             max_pages = pages_for(self.max_context, ps)
-            g = self._graphs.get(bucket)
-            if g is None:
-                g = self._capture(bucket, max_pages, seqs)
-                self._graphs[bucket] = g
+            g = self._graph(bucket, max_pages, seqs)
             ids, _, _, pt, _ = self._decode_inputs(seqs, bucket, max_pages)
             L0 = np.asarray([s.length for s in seqs], dtype=np.int64)
             pos = np.zeros((steps, bucket), dtype=np.int64)
@@ -882,10 +880,7 @@ class Engine:
         B = len(seqs)
         bucket = self._bucket(B)
         max_pages = pages_for(self.max_context, self.page_size)
-        g = self._graphs.get(bucket)
-        if g is None:
-            g = self._capture(bucket, max_pages, seqs)
-            self._graphs[bucket] = g
+        g = self._graph(bucket, max_pages, seqs)
         ids, pos, slots, pt, kvl = self._decode_inputs(seqs, bucket, max_pages)
         g["ids"].copy_(ids, non_blocking=True)
         g["pos"].copy_(pos, non_blocking=True)
@@ -901,6 +896,24 @@ class Engine:
             out = g["out"][:B].tolist()
         self._kernel_check("decode")
         return out
+
+    def _graph(self, bucket: int, max_pages: int, seqs) -> dict:
+        """The decode graph of ``bucket`` rows, captured on first use.  The
+        graphs point into the model's scratch buffers; when a larger forward
+        has since regrown one of them (the old memory is freed), every graph
+        is dropped and captured again before it could replay."""
+        gen = self.model.buf_generation
+        if gen != self._graphs_gen:
+            self._graphs.clear()
+            self._graphs_gen = gen
+        g = self._graphs.get(bucket)
+        if g is None:
+            g = self._capture(bucket, max_pages, seqs)
+            if self.model.buf_generation != gen:  # the capture's warm-up regrew a buffer
+                self._graphs.clear()
+            self._graphs[bucket] = g
+            self._graphs_gen = self.model.buf_generation
+        return g
 
     def _capture(self, bucket: int, max_pages: int, seqs) -> dict:
         dev = self.device

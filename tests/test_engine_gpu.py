@@ -178,3 +178,31 @@ def test_rope_table_covers_the_engine_context_and_kernel_errors_fail_the_request
         eng.decode_step([s])
     assert ops.check_errors(torch.device("cuda")) == 0
     eng.free(s)
+
+
+def test_decode_graphs_recaptured_after_scratch_buffers_grow():
+    """A decode graph points into the model's scratch buffers.  A later,
+    larger prefill replaces them (freeing the old memory); the engine must
+    drop and recapture its graphs, so decode after the growth still matches
+    eager decode."""
+    cfg = PRESETS["small-qwen2"]
+    model = QwenModel.random_init(cfg, seed=4, device="cuda", dtype=torch.bfloat16)
+    eng = Engine(model, num_pages=4096, page_size=16, max_context=8192)
+    g = torch.Generator().manual_seed(4)
+    short = torch.randint(0, cfg.vocab_size, (40,), generator=g).tolist()
+    long = torch.randint(0, cfg.vocab_size, (3000,), generator=g).tolist()
+    s0 = eng.prefill(short)
+    eng.decode([s0], 8)  # captures bucket 1 with the short prefill's buffers
+    gen0 = model.buf_generation
+    eng.free(s0)
+    big = eng.prefill(long)  # regrows the scratch buffers
+    assert model.buf_generation > gen0
+    churn = [torch.full((1 << 20,), 7.0, device="cuda") for _ in range(8)]  # reuse the freed memory
+    a = eng.prefill(short)
+    eng.decode([a], 12)
+    eng.use_cuda_graphs = False
+    b = eng.prefill(short)
+    eng.decode([b], 12)
+    assert a.output_ids == b.output_ids
+    assert all(bool((c == 7.0).all()) for c in churn)  # no stale graph wrote into them
+    eng.free(big)
