@@ -445,13 +445,42 @@ __global__ void __launch_bounds__(192, 2)
     tc_fence_after();
     const bool empty_split = (kb1 <= kb0);
     const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16);
-    // Final value of (row m, feature feat), called by all 128 threads for
-    // the same m.  Features past N (N % 32 == 0: whole warps) store nothing.
-    auto emit = [&](int m, float v) {
+    // Per-row operands of the epilogue (row scale, residual, position, slot,
+    // RoPE cos/sin).  They are loaded for a chunk of kRowChunk rows before
+    // any of those rows is emitted, so a batch of M rows waits on M /
+    // kRowChunk L2 round trips instead of one per row.  Called by all 128
+    // threads for the same m (the shuffles need whole warps).
+    struct RowPf {
+      float rs, res, c, s;
+      int pos;
+      int64_t slot;
+    };
+    auto row_pf = [&](int m) -> RowPf {
+      RowPf p{1.f, 0.f, pf_c0, pf_s0, 0, 0};
       if (epi.scale_sumsq != nullptr) {
         const float rs = __shfl_sync(0xffffffffu, pf_rstd, m & 31);
-        v *= m < 32 ? rs : rsqrtf(__ldcg(epi.scale_sumsq + m) / (float)K + epi.scale_eps);
+        p.rs = m < 32 ? rs : (m < M ? rsqrtf(__ldcg(epi.scale_sumsq + m) / (float)K + epi.scale_eps) : 1.f);
       }
+      if (epi.mode == LL_EPI_RESIDUAL) {
+        if (m < M && feat < N) p.res = m == 0 ? pf_res0 : __bfloat162float(epi.res[(size_t)m * epi.ld + feat]);
+      } else if (epi.mode == LL_EPI_QKV_ROPE) {
+        const int pm0 = __shfl_sync(0xffffffffu, pf_pos, m & 31);
+        const int64_t sl = __shfl_sync(0xffffffffu, pf_slot, m & 31);
+        p.pos = m < 32 ? pm0 : (m < M ? epi.positions[m] : 0);
+        p.slot = m < 32 ? sl : (m < M ? epi.slots[m] : 0);
+        if (m > 0 && m < M && nb < epi.Hq + epi.Hkv && p.pos >= 0 && p.pos < epi.max_pos) {
+          const float* cs = epi.cos_sin + (size_t)p.pos * 128;
+          p.c = cs[f & 63];
+          p.s = cs[64 + (f & 63)];
+        }
+      }
+      return p;
+    };
+    constexpr int kRowChunk = 4;
+    // Final value of (row m, feature feat), called by all 128 threads for
+    // the same m.  Features past N (N % 32 == 0: whole warps) store nothing.
+    auto emit = [&](int m, float v, const RowPf& p) {
+      if (epi.scale_sumsq != nullptr) v *= p.rs;
       v += pf_bias;
       if (epi.mode == LL_EPI_STORE) {
         if (feat < N) C[(size_t)m * ldc + feat] = __float2bfloat16(v);
@@ -464,7 +493,7 @@ __global__ void __launch_bounds__(192, 2)
         float r = 0.f;
         if (feat < N) {
           const size_t i = (size_t)m * epi.ld + feat;
-          r = bf16_round(v) + (m == 0 ? pf_res0 : __bfloat162float(epi.res[i]));
+          r = bf16_round(v) + p.res;
           epi.res[i] = __float2bfloat16(r);
           epi.h_out[i] = __float2bfloat16(r * pf_w);
         }
@@ -472,10 +501,8 @@ __global__ void __launch_bounds__(192, 2)
         if (lane == 0) atomicAdd(epi.sumsq_out + m, ss);
       } else {  // LL_EPI_QKV_ROPE: this tile is head nb of [Hq | Hkv keys | Hkv values]
         float x = bf16_round(v);
-        const int64_t sl = __shfl_sync(0xffffffffu, pf_slot, m & 31);
-        const int64_t slot = m < 32 ? sl : epi.slots[m];
-        const int pm0 = __shfl_sync(0xffffffffu, pf_pos, m & 31);
-        const int pos_m = m < 32 ? pm0 : epi.positions[m];
+        const int64_t slot = p.slot;
+        const int pos_m = p.pos;
         // checked per row (the same for all 128 threads, so the barriers
         // below stay uniform): a bad slot or position is recorded, not written
         if (slot < 0 || slot >= epi.slot_limit || pos_m < 0 || pos_m >= epi.max_pos) {
@@ -495,13 +522,7 @@ __global__ void __launch_bounds__(192, 2)
           }
           s_head[f] = x;
           bar_sync_128();
-          const int j = f & 63;
-          float c = pf_c0, sn = pf_s0;
-          if (m > 0) {
-            const float* cs = epi.cos_sin + (size_t)pos_m * 128;
-            c = cs[j];
-            sn = cs[64 + j];
-          }
+          const float c = p.c, sn = p.s;
           x = f < 64 ? x * c - s_head[f + 64] * sn : x * c + s_head[f - 64] * sn;
           bar_sync_128();  // s_head / s_red are free for the next row
           dst = nb < epi.Hq ? epi.q_out + ((size_t)m * epi.Hq + nb) * 128
@@ -524,7 +545,16 @@ __global__ void __launch_bounds__(192, 2)
       if (!ok) continue;
       const int ncols = BNX < 32 ? BNX : 32;
       if (nsplit == 1) {
-        for (int i = 0; i < ncols && c + i < M; ++i) emit(c + i, __uint_as_float(r[i]));
+#pragma unroll
+        for (int i0 = 0; i0 < ncols; i0 += kRowChunk) {
+          if (c + i0 >= M) break;
+          RowPf pf[kRowChunk];
+#pragma unroll
+          for (int j = 0; j < kRowChunk; ++j) pf[j] = row_pf(c + i0 + j);
+#pragma unroll
+          for (int j = 0; j < kRowChunk; ++j)
+            if (i0 + j < ncols && c + i0 + j < M) emit(c + i0 + j, __uint_as_float(r[i0 + j]), pf[j]);
+        }
       } else if (feat < N) {
         float* w = ws + ((size_t)split * M) * N;
         for (int i = 0; i < ncols; ++i) {
@@ -544,19 +574,34 @@ __global__ void __launch_bounds__(192, 2)
       bar_sync_128();
       if (s_last) {
         __threadfence();
-        for (int m = 0; m < M; ++m) {
-          // all partials in flight at once, then summed in split order
-          float part[16];
-          const float* src = ws + (size_t)m * N + feat;
-          const size_t sstride = (size_t)M * N;
+        const size_t sstride = (size_t)M * N;
+#pragma unroll 1
+        for (int m0 = 0; m0 < M; m0 += kRowChunk) {
+          // the partials of kRowChunk rows and their epilogue operands are
+          // all in flight at once; each row is then summed in split order
+          float part[kRowChunk][16];
 #pragma unroll
-          for (int sp = 0; sp < 16; ++sp) part[sp] = (sp < nsplit && feat < N) ? __ldcg(src + sp * sstride) : 0.f;
-          float sum = 0.f;
+          for (int j = 0; j < kRowChunk; ++j) {
+            const float* src = ws + (size_t)(m0 + j) * N + feat;
 #pragma unroll
-          for (int sp = 0; sp < 16; ++sp) sum += part[sp];
-          for (int sp = 16; sp < nsplit; ++sp)
-            if (feat < N) sum += __ldcg(src + sp * sstride);
-          if (ok) emit(m, sum);
+            for (int sp = 0; sp < 16; ++sp)
+              part[j][sp] = (m0 + j < M && sp < nsplit && feat < N) ? __ldcg(src + sp * sstride) : 0.f;
+          }
+          RowPf pf[kRowChunk];
+#pragma unroll
+          for (int j = 0; j < kRowChunk; ++j) pf[j] = row_pf(m0 + j);
+#pragma unroll
+          for (int j = 0; j < kRowChunk; ++j) {
+            const int m = m0 + j;
+            if (m >= M) break;
+            const float* src = ws + (size_t)m * N + feat;
+            float sum = 0.f;
+#pragma unroll
+            for (int sp = 0; sp < 16; ++sp) sum += part[j][sp];
+            for (int sp = 16; sp < nsplit; ++sp)
+              if (feat < N) sum += __ldcg(src + sp * sstride);
+            if (ok) emit(m, sum, pf[j]);
+          }
         }
         if (threadIdx.x == 64) tickets[nb] = 0;  // ready for the next launch / graph replay
       }
