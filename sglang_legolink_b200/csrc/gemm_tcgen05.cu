@@ -299,7 +299,11 @@ struct SwapCfg {
   static constexpr int SMEM = STAGES * (W_BYTES + X_BYTES) + 1024 + 256;
 };
 
-template <int BNX, int RING_KB>
+// kRowPrefetch (M > 1): the epilogue loads the per-row operands and split-K
+// partials of kRowChunk rows before emitting any of them.  M == 1 launches
+// the plain epilogue, a separate instantiation, so the batch-1 decode kernel
+// keeps its smaller code and register count.
+template <int BNX, int RING_KB, bool kRowPrefetch>
 __global__ void __launch_bounds__(192, 2)
     gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                        bf16* __restrict__ C, const bf16* __restrict__ bias, int M, int N, int K, int ldc,
@@ -545,15 +549,19 @@ __global__ void __launch_bounds__(192, 2)
       if (!ok) continue;
       const int ncols = BNX < 32 ? BNX : 32;
       if (nsplit == 1) {
+        if constexpr (kRowPrefetch) {
 #pragma unroll
-        for (int i0 = 0; i0 < ncols; i0 += kRowChunk) {
-          if (c + i0 >= M) break;
-          RowPf pf[kRowChunk];
+          for (int i0 = 0; i0 < ncols; i0 += kRowChunk) {
+            if (c + i0 >= M) break;
+            RowPf pf[kRowChunk];
 #pragma unroll
-          for (int j = 0; j < kRowChunk; ++j) pf[j] = row_pf(c + i0 + j);
+            for (int j = 0; j < kRowChunk; ++j) pf[j] = row_pf(c + i0 + j);
 #pragma unroll
-          for (int j = 0; j < kRowChunk; ++j)
-            if (i0 + j < ncols && c + i0 + j < M) emit(c + i0 + j, __uint_as_float(r[i0 + j]), pf[j]);
+            for (int j = 0; j < kRowChunk; ++j)
+              if (i0 + j < ncols && c + i0 + j < M) emit(c + i0 + j, __uint_as_float(r[i0 + j]), pf[j]);
+          }
+        } else {
+          for (int i = 0; i < ncols && c + i < M; ++i) emit(c + i, __uint_as_float(r[i]), row_pf(c + i));
         }
       } else if (feat < N) {
         float* w = ws + ((size_t)split * M) * N;
@@ -575,6 +583,21 @@ __global__ void __launch_bounds__(192, 2)
       if (s_last) {
         __threadfence();
         const size_t sstride = (size_t)M * N;
+        if constexpr (!kRowPrefetch) {
+          for (int m = 0; m < M; ++m) {
+            // all partials in flight at once, then summed in split order
+            float part[16];
+            const float* src = ws + (size_t)m * N + feat;
+#pragma unroll
+            for (int sp = 0; sp < 16; ++sp) part[sp] = (sp < nsplit && feat < N) ? __ldcg(src + sp * sstride) : 0.f;
+            float sum = 0.f;
+#pragma unroll
+            for (int sp = 0; sp < 16; ++sp) sum += part[sp];
+            for (int sp = 16; sp < nsplit; ++sp)
+              if (feat < N) sum += __ldcg(src + sp * sstride);
+            if (ok) emit(m, sum, row_pf(m));
+          }
+        } else {
 #pragma unroll 1
         for (int m0 = 0; m0 < M; m0 += kRowChunk) {
           // the partials of kRowChunk rows and their epilogue operands are
@@ -602,6 +625,7 @@ __global__ void __launch_bounds__(192, 2)
               if (feat < N) sum += __ldcg(src + sp * sstride);
             if (ok) emit(m, sum, pf[j]);
           }
+        }
         }
         if (threadIdx.x == 64) tickets[nb] = 0;  // ready for the next launch / graph replay
       }
@@ -1199,9 +1223,9 @@ static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* 
   if (w_tiled ? make_tmap_w_tiled(&tW, W, N, K) : make_tmap_2d(&tW, W, N, K, ldw, GEMM_BM)) return -2;
   if (make_tmap_2d(&tX, A, M, K, lda, BNX)) return -2;
   dim3 grid(ntiles, splits);
-#define LL_LAUNCH_S(BNX_, RING_)                                                                         \
+#define LL_LAUNCH_S(BNX_, RING_, PF_)                                                                    \
   do {                                                                                                   \
-    auto kern = gemm_swapab_kernel<BNX_, RING_>;                                                         \
+    auto kern = gemm_swapab_kernel<BNX_, RING_, PF_>;                                                    \
     using C_ = SwapCfg<BNX_, RING_>;                                                                     \
     if (C_::SMEM > max_smem_optin()) return -7;                                                          \
     static bool init = false;                                                                            \
@@ -1214,17 +1238,23 @@ static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* 
   } while (0)
   if (small_m_ring_kb() == 72) {
     switch (BNX) {
-      case 16: LL_LAUNCH_S(16, 72); break;
-      case 32: LL_LAUNCH_S(32, 72); break;
-      case 64: LL_LAUNCH_S(64, 72); break;
-      default: LL_LAUNCH_S(128, 72); break;
+      case 16:
+        if (M == 1) LL_LAUNCH_S(16, 72, false);
+        else LL_LAUNCH_S(16, 72, true);
+        break;
+      case 32: LL_LAUNCH_S(32, 72, true); break;
+      case 64: LL_LAUNCH_S(64, 72, true); break;
+      default: LL_LAUNCH_S(128, 72, true); break;
     }
   } else {
     switch (BNX) {
-      case 16: LL_LAUNCH_S(16, 108); break;
-      case 32: LL_LAUNCH_S(32, 108); break;
-      case 64: LL_LAUNCH_S(64, 108); break;
-      default: LL_LAUNCH_S(128, 108); break;
+      case 16:
+        if (M == 1) LL_LAUNCH_S(16, 108, false);
+        else LL_LAUNCH_S(16, 108, true);
+        break;
+      case 32: LL_LAUNCH_S(32, 108, true); break;
+      case 64: LL_LAUNCH_S(64, 108, true); break;
+      default: LL_LAUNCH_S(128, 108, true); break;
     }
   }
 #undef LL_LAUNCH_S

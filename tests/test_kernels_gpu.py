@@ -78,7 +78,7 @@ def test_gemm_small_m_swiglu_epilogue(M, splits):
     assert torch.equal(ops.linear(a, gu, swiglu_epilogue=True), out) or splits == 1
 
 
-@pytest.mark.parametrize("M", [1, 5])
+@pytest.mark.parametrize("M", [1, 5, 40])
 def test_gemv_rownorm_and_residual_epilogues(M):
     """Row-scaled GEMV (plain and SwiGLU) and the residual epilogue against
     fp32: y * rsqrt(sumsq / K + eps) + bias; r = bf16(y) + res, res = bf16(r),
@@ -109,18 +109,23 @@ def test_gemv_rownorm_and_residual_epilogues(M):
     assert _rel(sq, (r * r).sum(-1)) < 1e-3
 
 
-@pytest.mark.parametrize("qk_norm", [False, True])
-def test_gemv_qkv_rope_matches_unfused(qk_norm):
+@pytest.mark.parametrize("qk_norm,M", [(False, 3), (True, 3), (True, 37)])
+def test_gemv_qkv_rope_matches_unfused(qk_norm, M):
     """qkv GEMV with per-head norm, RoPE and the KV write in its stores ==
-    GEMV then rope_qkv_write, and == the fp32 CPU definition."""
+    GEMV then rope_qkv_write, and == the fp32 CPU definition.  M = 37 puts
+    rows past 32, whose positions and slots the epilogue reads from memory."""
     torch.manual_seed(7)
-    Hq, Hkv, D, K, M, ps, pages = 8, 2, 128, 1024, 3, 16, 8
+    Hq, Hkv, D, K, ps, pages = 8, 2, 128, 1024, 16, 8
     N = (Hq + 2 * Hkv) * D
     x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
     w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
     bias = torch.randn(N, device=DEV, dtype=torch.bfloat16)
-    pos = torch.tensor([5, 17, 100], device=DEV, dtype=torch.int32)
-    slots = torch.tensor([3, 40, 77], device=DEV, dtype=torch.int64)
+    if M == 3:
+        pos = torch.tensor([5, 17, 100], device=DEV, dtype=torch.int32)
+        slots = torch.tensor([3, 40, 77], device=DEV, dtype=torch.int64)
+    else:
+        pos = torch.randperm(4096, generator=torch.Generator().manual_seed(M))[:M].to(DEV, torch.int32)
+        slots = torch.randperm(pages * ps, generator=torch.Generator().manual_seed(M + 1))[:M].to(DEV)
     cs = ref.rope_cos_sin_table(4096, 128, 1e6).to(DEV)
     qn = (torch.rand(D, device=DEV, dtype=torch.bfloat16) + 0.5) if qk_norm else None
     kn = (torch.rand(D, device=DEV, dtype=torch.bfloat16) + 0.5) if qk_norm else None
