@@ -1,7 +1,7 @@
 """Small single-kernel cases sized for `ncu --set full` captures (a few
 launches, a few hundred MB on the device), one per hot kernel:
 
-    python -m sglang_legolink_b200.benchmarks.ncu_cases {gemm,gemm_link,gemm_link_cublas,attn,gemv,decode,link,tp_reduce,tp_scatter}
+    python -m sglang_legolink_b200.benchmarks.ncu_cases {gemm,gemm_link,gemm_link_cublas,attn,gemv,gemv_residual,decode,link,tp_reduce,tp_scatter}
 """
 import sys, os, math
 
@@ -16,6 +16,17 @@ if case == "gemv":
         w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
         o = torch.empty(1, N, device="cuda", dtype=torch.bfloat16)
         for _ in range(4): ops.linear(a, w, out=o)
+elif case == "gemv_residual":  # o_proj GEMV + residual epilogue: 4 launches at M = 16, then 4 at M = 1
+    H = 3584
+    w = ops.tile_weight((torch.randn(H, H, device="cuda") * 0.02).to(torch.bfloat16))
+    nw = torch.ones(H, device="cuda", dtype=torch.bfloat16)
+    for M in (16, 1):
+        x = torch.randn(M, H, device="cuda", dtype=torch.bfloat16)
+        res = torch.randn(M, H, device="cuda", dtype=torch.bfloat16)
+        h = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
+        sq = torch.zeros(M, device="cuda")
+        for _ in range(4): ops.gemv_residual(x, w, res, nw, h, sq)
+    torch.cuda.synchronize()
 elif case == "gemm":
     M, N, K = 2048, 37888, 3584
     a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
