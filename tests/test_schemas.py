@@ -144,3 +144,16 @@ def test_schema_field_sets_follow_the_code():
     m = cm.select("go")
     assert props("agent_context_manifest") == set(m.to_dict())
     assert props("execution_plan") == set(Planner().plan(m, cm.contexts()).to_dict())
+
+
+def test_command_line_validator(tmp_path, capsys, session):
+    from sglang_legolink_b200.schemas.__main__ import main
+
+    _, rows = session
+    good = tmp_path / "m.jsonl"
+    good.write_text("".join(json.dumps(r) + "\n" for r in rows) + "\n")
+    assert main(["metric_row", str(good)]) == 0 and capsys.readouterr().out.strip() == f"ok {len(rows)}"
+    bad = tmp_path / "link.json"
+    bad.write_text(json.dumps(dict(_good_link(), imp_indices=[3])))
+    assert main(["pic_link", str(bad)]) == 1 and "imp_indices" in capsys.readouterr().out
+    assert main(["no_such_schema", str(bad)]) == 2
