@@ -122,174 +122,298 @@ def physical_token_ids_sha256(token_ids) -> str:
 
 
 # ---------------------------------------------------------------- type rules
-def _err(name: str, problem: str) -> ContractError:
-    return ContractError(f"pic_link.{name} {problem}.")
+# Every host-sendable value has one entry in ``_VALUE_RULES``: the field name,
+# the shape it must have, and whether an explicit ``null`` is accepted.  The
+# shapes are small predicate objects, so the accepted set of a field reads off
+# the table (the refusal set is the reference's, ``pic_runtime.py:845-922``).
 
 
-def _int_field(plan: Mapping, name: str, *, nullable=False, minimum=0, maximum=PIC_LINK_MAX_INTEGER):
-    if name not in plan:
+def _is_int(v) -> bool:
+    return isinstance(v, int) and not isinstance(v, bool)
+
+
+def _in_range(v) -> bool:
+    return _is_int(v) and 0 <= v <= PIC_LINK_MAX_INTEGER
+
+
+class _Shape:
+    """A value shape: ``check(value, keys)`` returns None or a refusal."""
+
+    def check(self, value, keys: list) -> Optional[str]:
+        raise NotImplementedError
+
+
+class _OfType(_Shape):
+    def __init__(self, what: str, test):
+        self.what, self.test = what, test
+
+    def check(self, value, keys):
+        return None if self.test(value) else f"is not {self.what}"
+
+
+class _Count(_Shape):
+    def check(self, value, keys):
+        if not _is_int(value):
+            return "is not an integer"
+        return None if _in_range(value) else f"is outside [0, {PIC_LINK_MAX_INTEGER}]"
+
+
+class _Names(_Shape):
+    """A list of strings, optionally non-empty and bounded by the key count."""
+
+    def __init__(self, nonempty: bool = False, per_key_bound: bool = False):
+        self.nonempty, self.per_key_bound = nonempty, per_key_bound
+
+    def check(self, value, keys):
+        if not isinstance(value, list):
+            return "is not a list of strings"
+        if self.nonempty and not value:
+            return "is empty"
+        if not all(isinstance(x, str) for x in value):
+            return "holds a non-string entry"
+        if self.per_key_bound and len(value) > len(keys):
+            return f"names more entries than the {len(keys)} cache keys"
         return None
-    v = plan[name]
-    if v is None:
-        if nullable:
-            return None
-        raise _err(name, "must not be null")
-    if isinstance(v, bool) or not isinstance(v, int):
-        raise _err(name, "must be an integer")
-    if v < minimum or v > maximum:
-        raise _err(name, f"must be between {minimum} and {maximum}")
-    return v
 
 
-def _opt_str(plan: Mapping, name: str) -> None:
-    v = plan.get(name)
-    if v is not None and not isinstance(v, str):
-        raise _err(name, "must be a string when present")
+class _PerKeyCounts(_Shape):
+    def check(self, value, keys):
+        if not isinstance(value, list):
+            return "is not a list of integers"
+        if len(value) != len(keys):
+            return f"has {len(value)} entries for {len(keys)} cache keys"
+        return None if all(_in_range(x) for x in value) else "holds a value that is not a count"
 
 
-def _opt_bool(plan: Mapping, name: str) -> None:
-    v = plan.get(name)
-    if v is not None and not isinstance(v, bool):
-        raise _err(name, "must be a boolean when present")
+class _Mode(_Shape):
+    def check(self, value, keys):
+        if not isinstance(value, str):
+            return "is not a string"
+        return None if value.lower() in PIC_LINK_RECOMPUTE_MODES else \
+            "is not one of " + "/".join(sorted(PIC_LINK_RECOMPUTE_MODES))
 
 
-def _label(plan: Mapping, name: str) -> None:
-    v = plan.get(name)
-    if v is None or isinstance(v, str):
-        return
-    if isinstance(v, bool) or not isinstance(v, int):
-        raise _err(name, "must be a string or an integer when present")
+_TEXT = _OfType("a string", lambda v: isinstance(v, str))
+_FLAG = _OfType("a boolean", lambda v: isinstance(v, bool))
+_LABEL = _OfType("a string or an integer", lambda v: isinstance(v, str) or _is_int(v))
 
-
-def _str_list(plan: Mapping, name: str, *, required=False, at_most: Optional[int] = None):
-    if name not in plan:
-        if required:
-            raise _err(name, "must be non-empty")
-        return None
-    v = plan[name]
-    if v is None:
-        if required:
-            raise _err(name, "must not be null")
-        return None
-    if not isinstance(v, list):
-        raise _err(name, "must be a list of strings")
-    if required and not v:
-        raise _err(name, "must be non-empty")
-    if any(not isinstance(x, str) for x in v):
-        raise _err(name, "must contain only strings")
-    if at_most is not None and len(v) > at_most:
-        raise _err(name, f"may hold at most {at_most} entries")
-    return v
+# (field, shape, null accepted).  ``cache_keys`` is handled first: it is
+# required, and other shapes are judged against its length.
+_VALUE_RULES: tuple = (
+    ("request_id", _LABEL, True),
+    ("task_id", _LABEL, True),
+    ("variant", _TEXT, True),
+    ("profiling_warmup", _FLAG, True),
+    ("concurrency", _Count(), True),
+    ("block_ids", _Names(per_key_bound=True), True),
+    ("adapter_id", _TEXT, True),
+    ("segmentation_policy_version", _TEXT, True),
+    ("legolink_policy_version", _TEXT, True),
+    ("execution_group_key", _TEXT, True),
+    ("promote_reconstructed_group", _FLAG, True),
+    ("recompute_mode", _Mode(), False),
+    ("recompute_initial_tokens", _Count(), False),
+    ("legolink_k", _Count(), False),
+    ("recompute_first_block", _FLAG, True),
+    ("recompute_first_block_tokens", _Count(), True),
+    ("recompute_tokens_per_block", _PerKeyCounts(), True),
+)
 
 
 def validate_pic_link_field_types(plan: Mapping) -> None:
-    """Type/range checks for every host-sendable value (reference
-    ``pic_runtime.py:845-922``)."""
-    keys = _str_list(plan, "cache_keys", required=True) or []
-    for n in ("request_id", "task_id"):
-        _label(plan, n)
-    _opt_str(plan, "variant")
-    _opt_bool(plan, "profiling_warmup")
-    _int_field(plan, "concurrency", nullable=True)
-    _str_list(plan, "block_ids", at_most=len(keys))
-    for n in ("adapter_id", "segmentation_policy_version", "legolink_policy_version", "execution_group_key"):
-        _opt_str(plan, n)
-    _opt_bool(plan, "promote_reconstructed_group")
-    if "recompute_mode" in plan:
-        mode = plan["recompute_mode"]
-        if not isinstance(mode, str):
-            raise _err("recompute_mode", "must be a string")
-        if mode.lower() not in PIC_LINK_RECOMPUTE_MODES:
-            raise _err("recompute_mode", "must be one of " + ", ".join(sorted(PIC_LINK_RECOMPUTE_MODES)))
-    _int_field(plan, "recompute_initial_tokens")
-    _int_field(plan, "legolink_k")
-    _opt_bool(plan, "recompute_first_block")
-    _int_field(plan, "recompute_first_block_tokens", nullable=True)
-    if plan.get("recompute_tokens_per_block") is not None:
-        w = plan["recompute_tokens_per_block"]
-        if not isinstance(w, list):
-            raise _err("recompute_tokens_per_block", "must be a list of integers")
-        if len(w) != len(keys):
-            raise _err("recompute_tokens_per_block", "must contain one value per cache key")
-        for x in w:
-            if isinstance(x, bool) or not isinstance(x, int) or x < 0 or x > PIC_LINK_MAX_INTEGER:
-                raise _err("recompute_tokens_per_block", "must contain only non-negative integers within range")
+    """Checks the type and range of every host-sendable value in ``plan``
+    against ``_VALUE_RULES`` (absent fields pass; ``cache_keys`` is required
+    and must be a non-empty list of strings).  Reference refusal set:
+    ``pic_runtime.py:845-922``."""
+    keys = plan.get("cache_keys")
+    problem = "is missing" if "cache_keys" not in plan else \
+        ("is null" if keys is None else _Names(nonempty=True).check(keys, []))
+    if problem:
+        raise ContractError(f"pic_link.cache_keys {problem}.")
+    for name, shape, nullable in _VALUE_RULES:
+        if name not in plan:
+            continue
+        value = plan[name]
+        if value is None:
+            if nullable:
+                continue
+            problem = "is null"
+        else:
+            problem = shape.check(value, keys)
+        if problem:
+            raise ContractError(f"pic_link.{name} {problem}.")
+
+
+# ---------------------------------------------------------- governance rules
+# Execution governance (reference ``pic_runtime.py:1060-1148``, host twin
+# ``execution_governance.py:66``) as four ordered tables of named checks over
+# one view of the request.  Each table may assume the ones before it passed;
+# the request is refused with the first failing check's text.
+#
+#   framing   -- the FramingSpec is complete and names the supported layout;
+#   decision  -- the RepairDecision is complete and well formed;
+#   binding   -- the request's repair fields are exactly the decision's;
+#   evidence  -- (formal, or a quality-guarded decision) the deployment
+#                profile holds a passing, matching quality measurement.
+
+_HEX = frozenset("0123456789abcdef")
+_REPAIR_POLICIES = ("quality_guarded", "fixed_unvalidated_debug")
+
+
+def _nonblank(v) -> bool:
+    return isinstance(v, str) and bool(v.strip())
+
+
+def _exact_int(v) -> bool:
+    return type(v) is int
+
+
+def _finite_number(v) -> bool:
+    return type(v) in (int, float) and math.isfinite(v)
+
+
+class _Intent:
+    """Read-only view of one request's governance inputs."""
+
+    def __init__(self, wire: Mapping, profile):
+        self.wire = wire
+        self.profile = profile
+        self.spec = wire.get("framing_spec")
+        self.decision = wire.get("repair_decision")
+
+    # framing
+    @property
+    def layout(self):
+        return self.spec["framing_layout_version"]
+
+    # decision
+    @property
+    def k(self):
+        return self.decision["selected_k"]
+
+    @property
+    def windows(self):
+        return self.decision["windows"]
+
+    # evidence
+    def measurement(self):
+        table = self.profile.get("repair_quality_profiles", {})
+        return table.get(self.decision["quality_profile_id"]) if isinstance(table, Mapping) else None
+
+    def reviewed_inputs(self):
+        hashes = self.profile.get("canonical_input_hashes", [])
+        return hashes if isinstance(hashes, (list, tuple, set, frozenset)) else ()
+
+
+def _windows_ok(x: _Intent) -> bool:
+    w, k = x.windows, x.k
+    return (isinstance(w, list) and bool(w) and len(w) == len(x.wire.get("cache_keys", []))
+            and all(_exact_int(v) and 0 <= v <= k for v in w))
+
+
+def _measurement_matches(x: _Intent) -> bool:
+    m = x.measurement()
+    return all(m.get(f) == x.decision[f] for f in ("selected_k", "windows", "workload_class", "evidence_id"))
+
+
+def _measurement_passed(x: _Intent) -> bool:
+    m = x.measurement()
+    return (m.get("framing_spec") == x.spec and m.get("status") == "PASS"
+            and m.get("profile_id") == x.decision["quality_profile_id"]
+            and bool(x.decision["evidence_id"]) and bool(m.get("metric")))
+
+
+def _measurement_meets_threshold(x: _Intent) -> bool:
+    m = x.measurement()
+    got, need = m.get("measured_value"), m.get("required_threshold")
+    return _finite_number(got) and _finite_number(need) and got >= need
+
+
+_FRAMING_RULES = (
+    ("FramingSpec is absent or does not carry exactly its five fields",
+     lambda x: isinstance(x.spec, dict) and set(x.spec) == FRAMING_SPEC_FIELDS),
+    ("FramingSpec has a blank or non-string identity field",
+     lambda x: all(_nonblank(v) for v in x.spec.values())),
+    ("FramingSpec names a framing layout this runtime does not implement",
+     lambda x: x.layout == PHYSICAL_TOKEN_LAYOUT_VERSION),
+    ("FramingSpec.chat_template_sha256 is not 64 lowercase hex digits",
+     lambda x: len(x.spec["chat_template_sha256"]) == 64 and set(x.spec["chat_template_sha256"]) <= _HEX),
+    ("physical_token_layout_version differs from the FramingSpec layout",
+     lambda x: x.wire.get("physical_token_layout_version") == x.layout),
+)
+
+_DECISION_RULES = (
+    ("RepairDecision is absent or does not carry exactly its nine fields",
+     lambda x: isinstance(x.decision, dict) and set(x.decision) == REPAIR_DECISION_FIELDS),
+    ("RepairDecision.selected_k is not a non-negative integer",
+     lambda x: _exact_int(x.k) and x.k >= 0),
+    ("RepairDecision.windows is not one window in [0, selected_k] per cache key", _windows_ok),
+    ("RepairDecision.policy_version is not supported",
+     lambda x: x.decision["policy_version"] == REPAIR_DECISION_POLICY_VERSION),
+    ("RepairDecision was made for another framing layout",
+     lambda x: x.decision["framing_layout_version"] == x.layout),
+    ("RepairDecision.policy is not a known repair policy",
+     lambda x: x.decision["policy"] in _REPAIR_POLICIES),
+    ("RepairDecision.quality_profile_id is neither a string nor null",
+     lambda x: x.decision["quality_profile_id"] is None or isinstance(x.decision["quality_profile_id"], str)),
+    ("RepairDecision lacks its reason or workload class",
+     lambda x: _nonblank(x.decision["reason"]) and _nonblank(x.decision["workload_class"])),
+)
+
+_BINDING_RULES = (
+    ("recompute_initial_tokens is not the decision's selected_k",
+     lambda x: _exact_int(x.wire.get("recompute_initial_tokens")) and x.wire["recompute_initial_tokens"] == x.k),
+    ("recompute_tokens_per_block is not the decision's windows",
+     lambda x: x.wire.get("recompute_tokens_per_block") == x.windows),
+    ("first-block repair fields disagree with the decision's first window",
+     lambda x: x.wire.get("recompute_first_block_tokens") == x.windows[0]
+     and x.wire.get("recompute_first_block") is bool(x.windows[0])),
+    ("legacy legolink_k disagrees with the decision's selected_k",
+     lambda x: "legolink_k" not in x.wire or x.wire["legolink_k"] == x.k),
+)
+
+_EVIDENCE_RULES = (
+    ("formal execution needs a quality_guarded repair decision",
+     lambda x: x.decision["policy"] == "quality_guarded"),
+    ("the deployment profile is absent or was made for another FramingSpec",
+     lambda x: isinstance(x.profile, dict) and x.profile.get("framing_spec") == x.spec),
+    ("the complete input has no reviewed canonical framing in the deployment profile",
+     lambda x: x.wire.get("expected_complete_token_ids_sha256") in x.reviewed_inputs()),
+    ("the deployment profile has no repair quality measurement under quality_profile_id",
+     lambda x: isinstance(x.measurement(), dict)),
+    ("the repair quality measurement was made for another decision", _measurement_matches),
+    ("the repair quality measurement did not pass or lacks its provenance", _measurement_passed),
+    ("the measured repair quality is below its required threshold", _measurement_meets_threshold),
+)
+
+
+def _enforce(rules, x: _Intent) -> None:
+    for why, ok in rules:
+        if not ok(x):
+            raise ContractError(f"execution governance: {why}.")
 
 
 def validate_execution_intent(wire: Mapping, profile: Optional[Mapping] = None, *, require_formal=False) -> None:
-    """Formal vs legacy_debug governance (reference ``pic_runtime.py:1060-1148``
-    and host twin ``execution_governance.py:66``): FramingSpec and
-    RepairDecision shape, consistency with the repair fields, and -- for formal
-    or quality-guarded execution -- agreement with the deployment profile."""
+    """Refuses a request whose declared execution intent is not honoured.
+
+    ``legacy_debug`` requests that carry neither a FramingSpec nor a
+    RepairDecision are accepted as they are; anything else must pass the
+    framing, decision and binding tables, and formal execution (by request or
+    by deployment) or a quality-guarded decision must also pass the evidence
+    table against ``profile``."""
     mode = wire.get("execution_mode", "legacy_debug")
     if mode not in ("formal", "legacy_debug"):
-        raise ContractError("unknown execution_mode")
+        raise ContractError(f"execution governance: execution_mode {mode!r} is neither formal nor legacy_debug.")
     if require_formal and mode != "formal":
-        raise ContractError("formal deployment rejects legacy_debug execution")
-    formal = require_formal or mode == "formal"
-    framing, repair = wire.get("framing_spec"), wire.get("repair_decision")
-    if not formal and framing is None and repair is None:
+        raise ContractError("execution governance: this deployment serves formal execution only.")
+    formal = mode == "formal"
+    x = _Intent(wire, profile)
+    if not formal and x.spec is None and x.decision is None:
         return
-    if not isinstance(framing, dict) or set(framing) != FRAMING_SPEC_FIELDS:
-        raise ContractError("missing or malformed framing_spec")
-    if any(not isinstance(v, str) or not v.strip() for v in framing.values()):
-        raise ContractError("framing identity must be nonempty")
-    version = framing["framing_layout_version"]
-    if version != PHYSICAL_TOKEN_LAYOUT_VERSION:
-        raise ContractError("unsupported/legacy framing version")
-    th = framing["chat_template_sha256"]
-    if len(th) != 64 or any(ch not in "0123456789abcdef" for ch in th):
-        raise ContractError("invalid chat template hash")
-    if wire.get("physical_token_layout_version") != version:
-        raise ContractError("framing and physical layout version disagree")
-    if not isinstance(repair, dict) or set(repair) != REPAIR_DECISION_FIELDS:
-        raise ContractError("missing or malformed RepairDecision")
-    k, windows = repair["selected_k"], repair["windows"]
-    if type(k) is not int or k < 0:
-        raise ContractError("selected_k must be a nonnegative integer")
-    if (not isinstance(windows, list) or len(windows) != len(wire.get("cache_keys", [])) or not windows
-            or any(type(v) is not int or v < 0 or v > k for v in windows)):
-        raise ContractError("invalid repair window vector")
-    if repair["policy_version"] != REPAIR_DECISION_POLICY_VERSION:
-        raise ContractError("unsupported repair policy version")
-    if repair["framing_layout_version"] != version:
-        raise ContractError("repair/framing incompatibility")
-    if repair["policy"] not in ("quality_guarded", "fixed_unvalidated_debug"):
-        raise ContractError("unknown repair policy")
-    if repair["quality_profile_id"] is not None and not isinstance(repair["quality_profile_id"], str):
-        raise ContractError("quality_profile_id must be a string or null")
-    if not all(isinstance(repair[x], str) and repair[x].strip() for x in ("reason", "workload_class")):
-        raise ContractError("missing repair provenance")
-    if type(wire.get("recompute_initial_tokens")) is not int or wire["recompute_initial_tokens"] != k:
-        raise ContractError("repair K was replaced or defaulted")
-    if wire.get("recompute_tokens_per_block") != windows:
-        raise ContractError("repair windows were replaced or defaulted")
-    if (wire.get("recompute_first_block_tokens") != windows[0]
-            or wire.get("recompute_first_block") is not bool(windows[0])):
-        raise ContractError("first-block repair disagrees with decision")
-    if "legolink_k" in wire and wire["legolink_k"] != k:
-        raise ContractError("legacy K alias disagrees with decision")
-    if formal or repair["policy"] == "quality_guarded":
-        if repair["policy"] != "quality_guarded":
-            raise ContractError("formal execution requires measured repair quality")
-        if not isinstance(profile, dict) or profile.get("framing_spec") != framing:
-            raise ContractError("missing/incompatible deployment framing profile")
-        if wire.get("expected_complete_token_ids_sha256") not in profile.get("canonical_input_hashes", []):
-            raise ContractError("input has no reviewed canonical framing evidence")
-        quality = profile.get("repair_quality_profiles", {}).get(repair["quality_profile_id"])
-        if not isinstance(quality, dict):
-            raise ContractError("missing repair quality profile")
-        for name in ("selected_k", "windows", "workload_class", "evidence_id"):
-            if quality.get(name) != repair[name]:
-                raise ContractError("incompatible repair quality " + name)
-        if (quality.get("framing_spec") != framing or quality.get("status") != "PASS"
-                or quality.get("profile_id") != repair["quality_profile_id"]
-                or not repair["evidence_id"] or not quality.get("metric")):
-            raise ContractError("unvalidated repair quality provenance")
-        measured, threshold = quality.get("measured_value"), quality.get("required_threshold")
-        if (type(measured) not in (float, int) or type(threshold) not in (float, int)
-                or not math.isfinite(measured) or not math.isfinite(threshold) or measured < threshold):
-            raise ContractError("repair quality threshold not satisfied")
+    for table in (_FRAMING_RULES, _DECISION_RULES, _BINDING_RULES):
+        _enforce(table, x)
+    if formal or x.decision["policy"] == "quality_guarded":
+        _enforce(_EVIDENCE_RULES, x)
 
 
 def runtime_execution_profile() -> Optional[dict]:
