@@ -70,7 +70,7 @@ def main():
 
         pool = SharedKVPool(cfg.num_layers, pages, model.hkv, ps, cfg.head_dim, torch.bfloat16, dev)
         kw = dict(kv_pool=pool, directory=BlockDirectory(dist.distributed_c10d._get_default_store(),
-                                                         prefix="dp-sessions/"),
+                                                         prefix="dp-sessions/", world=world),
                   replica_rank=rank, peer_pools={r: pool.peer(r) for r in range(world) if r != rank})
     else:
         kw = dict(num_pages=pages)
@@ -132,9 +132,7 @@ def main():
             eng.free(seq)
         for s in mine:  # keep one turn of tool history resident
             if prev[s]:
-                if world > 1:  # published blocks are pinned (a peer may link them)
-                    eng.registry.unpin([prev[s]])
-                eng.registry.unregister(prev[s])
+                eng.unregister_block(prev[s])  # published: withdrawn from the directory first
             prev[s] = keys[s]
     total_ms = sum(links) + decode_ms
     stats = torch.tensor([statistics.median(links), sorted(links)[int(0.95 * (len(links) - 1))], decode_ms,

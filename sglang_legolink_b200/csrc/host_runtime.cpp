@@ -309,6 +309,26 @@ class BlockRegistry {
     return freed;
   }
 
+  // Unreferenced blocks with at most `max_pins` pins, lowest keep-value
+  // first, as (cache_key, owned pages).  A DP owner walks this list for
+  // published blocks (pinned once by publication) it may withdraw.
+  std::vector<std::pair<std::string, int64_t>> eviction_candidates(int64_t max_pins) const {
+    std::vector<std::pair<double, const BlockEntry*>> v;
+    const double t = now_s();
+    for (const auto& kv : blocks_) {
+      const BlockEntry& e = kv.second;
+      if (e.active_refs > 0 || e.pin_count > max_pins) continue;
+      v.emplace_back(score(e, t), &e);
+    }
+    std::sort(v.begin(), v.end(), [](const auto& a, const auto& b) {
+      return a.first < b.first || (a.first == b.first && a.second->cache_key < b.second->cache_key);
+    });
+    std::vector<std::pair<std::string, int64_t>> out;
+    out.reserve(v.size());
+    for (const auto& p : v) out.emplace_back(p.second->cache_key, owned_pages(*p.second));
+    return out;
+  }
+
   // Keep-value of a block: (reuse x recomputation saved) / (residency x (age+1)).
   static double score(const BlockEntry& e, double t) {
     const double reuse = 1.0 + (double)e.reuse_count;
@@ -573,6 +593,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("clear", &BlockRegistry::clear)
       .def("capacity_evictable_pages", &BlockRegistry::capacity_evictable_pages)
       .def("evict_for_capacity", &BlockRegistry::evict_for_capacity)
+      .def("eviction_candidates", &BlockRegistry::eviction_candidates)
       .def("handle", &BlockRegistry::handle)
       .def("tokens", &BlockRegistry::tokens)
       .def("contains", &BlockRegistry::contains)

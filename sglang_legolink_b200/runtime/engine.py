@@ -178,6 +178,12 @@ class Engine:
         self.replica_rank = replica_rank
         self.peer_pools = peer_pools if peer_pools is not None else {}
         self._remote: dict = {}
+        self._dir = None
+        self._published: dict = {}  # cache_key -> RemoteBlock this replica serves to its peers
+        if directory is not None:
+            from ..parallel.dp import DirectoryClient
+
+            self._dir = DirectoryClient(directory, replica_rank)
         if self.is_cuda:
             ws = ops.workspace(self.device)
             ws.reserve_decode(64 * model.hq, 592, self.cfg.head_dim)
@@ -235,9 +241,51 @@ class Engine:
             self.radix.evict(n - self.alloc.num_free)
         if self.alloc.num_free < n:
             self.registry.evict_for_capacity(n)
+        if self.alloc.num_free < n and self._published:
+            self._withdraw_published(n)
         if self.alloc.num_free < n:
             raise CapacityError(f"KV pool exhausted: need {n} pages, {self.alloc.num_free} free")
         return list(self.alloc.alloc(n))
+
+    def _published_evictable_pages(self) -> int:
+        """Pages of published blocks that only their publication pins."""
+        if not self._published:
+            return 0
+        return sum(p for k, p in self.registry.eviction_candidates(1) if k in self._published)
+
+    def _withdraw_published(self, n: int) -> None:
+        """Frees published blocks (lowest keep-value first) until ``n`` pages
+        are free: each is withdrawn from the directory and freed only after
+        every peer Link that may have found it has ended."""
+        for key, _pages in self.registry.eviction_candidates(1):
+            if self.alloc.num_free >= n:
+                return
+            rb = self._published.get(key)
+            if rb is None:
+                continue
+            h = self.registry.handle(key)
+            if h["pin_count"] != 1 or h["active_refs"]:
+                continue
+            if not self._dir.withdraw(rb):
+                emit_trace("published_block_withdraw_timeout", cache_key=key)
+                continue
+            del self._published[key]
+            self.registry.unpin([key])
+            self.registry.evict_for_capacity(n)
+            self.stats["published_blocks_withdrawn"] = self.stats.get("published_blocks_withdrawn", 0) + 1
+
+    def unregister_block(self, cache_key: str) -> bool:
+        """Drops a registered block.  A block this replica publishes is first
+        withdrawn from the directory (grace period for peer readers); returns
+        False when that did not close in time (the block stays)."""
+        with self._lock:
+            rb = self._published.get(cache_key)
+            if rb is not None:
+                if not self._dir.withdraw(rb):
+                    return False
+                del self._published[cache_key]
+                self.registry.unpin([cache_key])
+            return bool(self.registry.unregister(cache_key))
 
     def free(self, seq: Sequence_) -> None:
         if seq.pages:
@@ -444,12 +492,15 @@ class Engine:
         status = self.registry.register_block(str(cache_key), ckey, physical_token_ids_sha256(toks), toks, pages, 0,
                                               bid)
         self.stats["compiles"] += 1
-        if self.directory is not None and status == "registered":
+        if self._dir is not None and status == "registered":
             from ..parallel.dp import RemoteBlock
 
-            self.registry.pin([str(cache_key)])  # a peer may link it at any time: never evict
-            self.directory.publish(RemoteBlock(self.replica_rank, str(cache_key), tuple(pages), 0, tuple(toks),
-                                               ckey, physical_token_ids_sha256(toks), self.page_size))
+            rb = RemoteBlock(self.replica_rank, str(cache_key), tuple(int(p) for p in pages), 0,
+                             tuple(int(t) for t in toks), ckey, physical_token_ids_sha256(toks), self.page_size)
+            if self._dir.publish(rb):
+                # a peer may link it at any time: only a withdrawal frees it
+                self.registry.pin([str(cache_key)])
+                self._published[str(cache_key)] = rb
         emit_trace("compile_registered", cache_key=str(cache_key), token_count=n, status=status)
         return {"cache_key": str(cache_key), "status": status, "token_count": n, "first_token": first}
 
@@ -471,10 +522,10 @@ class Engine:
                                pic_link.get("legolink_policy_version"))
         res = self.registry.lookup(keys, ckey)
         self._remote = {}
-        if not res["ok"] and self.directory is not None:
+        if not res["ok"] and self._dir is not None:
             still = []
             for k in res["missing"]:
-                rb = self.directory.lookup(k)
+                rb = self._dir.find(k)
                 if rb is not None and rb.owner != self.replica_rank and rb.compat_key == ckey \
                         and (rb.owner in self.peer_pools):
                     self._remote[k] = rb
@@ -502,14 +553,25 @@ class Engine:
                 residency_recovery_message(res["missing"], res["stale"], res["incompatible"]),
                 res["missing"], res["stale"], res["incompatible"])
         self.registry.pin(keys)
-        for k in self._remote:
-            self.directory.pin(k, 1)
+        if self._remote:
+            # one grace-period ticket for this Link; entries of owners whose
+            # generation moved are re-read (a withdrawn block is missing now)
+            valid, missing, stale = self._dir.begin(self._remote)
+            if missing or stale:
+                self.registry.unpin(keys)
+                self._remote = {}
+                emit_trace("legolink_request_failed_closed", reason="scheduler_source_preflight_failed",
+                           missing=missing, stale=stale, incompatible=[])
+                raise LinkSourceUnavailable(residency_recovery_message(missing, stale, []), missing, stale, ())
+            self._remote = valid
         need = pages_for(resolved.total_token_count, self.page_size)
-        allocatable = self.alloc.num_free + self.radix.evictable_pages() + self.registry.capacity_evictable_pages()
+        allocatable = self.alloc.num_free + self.radix.evictable_pages() + self.registry.capacity_evictable_pages() \
+            + self._published_evictable_pages()
         if need > allocatable:
             self.registry.unpin(keys)
-            for k in self._remote:
-                self.directory.pin(k, -1)
+            if self._remote:
+                self._dir.end()
+                self._remote = {}
             raise CapacityError(
                 "LegoLink cannot allocate request-private destination KV without evicting its reserved source "
                 f"blocks: required={resolved.total_token_count}, allocatable={allocatable * self.page_size}.")
@@ -577,8 +639,8 @@ class Engine:
                 raise
             finally:
                 self.registry.unpin(keys)
-                for k in self._remote:
-                    self.directory.pin(k, -1)
+                if self._remote:
+                    self._dir.end()  # the link kernel finished reading (first token is on the host)
                 self.stats["remote_blocks_linked"] += len(self._remote)
                 self._remote = {}
                 pic_link.pop("_scheduler_reserved_cache_keys", None)
@@ -603,14 +665,19 @@ class Engine:
                     continue
                 args = (self.kv.k, self.kv.v, src.to(dev), dst.to(dev), lp.to(dev), gp.to(dev), self.model.cos_sin)
                 if owner is None:
-                    ops.kv_link_rope(*args)
+                    with timer.span("kv_link_local"):
+                        ops.kv_link_rope(*args)
                     if compare_enabled("kv_link"):  # diagnostic: fused kernel vs the torch statement
                         emit_trace("kv_link_compare", rid=rid, **compare_kv_link(*args))
                 elif self.is_cuda:  # peer replica's pool, read over NVLink by the link kernel
                     kp, vp, sps, sls = self.peer_pools[owner]
-                    ops.kv_link_rope(*args, src_k_ptr=kp, src_v_ptr=vp, src_page_size=sps, src_layer_stride=sls)
+                    with timer.span("kv_link_peer"):
+                        ops.kv_link_rope(*args, src_k_ptr=kp, src_v_ptr=vp, src_page_size=sps,
+                                         src_layer_stride=sls)
+                    self.stats["peer_tokens_linked"] = self.stats.get("peer_tokens_linked", 0) + int(src.numel())
                 else:
                     ops.kv_link_rope(*args, src_pools=self.peer_pools[owner])
+                    self.stats["peer_tokens_linked"] = self.stats.get("peer_tokens_linked", 0) + int(src.numel())
         rows = list(resolved.recompute_positions)
         toks = [resolved.linked_token_ids[p] for p in rows]
         with timer.span("sparse_repair"):

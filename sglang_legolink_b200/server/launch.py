@@ -248,7 +248,7 @@ def _build_rank(a, rank: int, world: int, local: int, ctrl=None):
     if a.dp_size > 1:
         from ..parallel.dp import BlockDirectory
 
-        directory = BlockDirectory(dist.distributed_c10d._get_default_store(), prefix="legolink-dp/")
+        directory = BlockDirectory(dist.distributed_c10d._get_default_store(), prefix="legolink-dp/", world=world)
         kw = dict(directory=directory, replica_rank=rank)
         if cuda:
             from ..parallel.dp import SharedKVPool

@@ -28,7 +28,7 @@ def main():
     model = QwenModel.random_init(cfg, seed=0, device=dev, dtype=torch.bfloat16)
     pool = SharedKVPool(cfg.num_layers, 2048, model.hkv, 16, cfg.head_dim, torch.bfloat16, dev)
     store = dist.distributed_c10d._get_default_store()
-    directory = BlockDirectory(store, prefix="peer-link-test/")
+    directory = BlockDirectory(store, prefix="peer-link-test/", world=2)
     other = 1 - rank
     eng = Engine(model, kv_pool=pool, max_context=4096, directory=directory, replica_rank=rank,
                  peer_pools={other: pool.peer(other)})

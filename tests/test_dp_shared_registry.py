@@ -45,7 +45,8 @@ def test_cross_replica_link_matches_local_link():
     assert b.stats["remote_blocks_linked"] == 2
     # the owner keeps published blocks pinned; the pins taken by the link are released
     assert a.registry.handle("blk0")["pin_count"] == 1
-    assert d.pins("blk0") == 0
+    # every Link that read a peer block closed its grace-period ticket
+    assert d.add("rcu/begun/1", 0) == d.add("rcu/ended/1", 0) == 1
 
 
 def test_incompatible_remote_block_is_refused():
