@@ -7,15 +7,26 @@ before timing and linked in a new shuffled order every step, 2 are fresh
 (they form the mutable suffix with the user turn).  Repair window 32 tokens
 per block boundary; then 256 greedy decode tokens at batch 1.
 
-One step = one Link request (TTFT) + 256 decode tokens + one full prefill of
-the same 16K prompt (the baseline the Link is compared to).  With N GPUs
-every rank serves its own replica (weak scaling); each per-step time is the
-max over ranks.
+One step = one full prefill of the 16K prompt + its 256-token decode (the
+baseline the Link is compared to), then one Link request (TTFT) + its
+256-token decode.
 
-Reported ``value`` = p50 device-timed Link TTFT in ms (lower is better).
-``e2e`` repeats the Link TTFT through the public engine API (plan
-resolution, H2D of the step's inputs from pinned host memory, first-token
-D2H), host wall clock.
+With N GPUs (one process per GPU, ``torchrun``) the ranks are DP replicas
+that share ONE block directory and map each other's KV pools (symmetric
+memory): every rank compiles its own 10 blocks once, and every Link reads a
+token-balanced half of its blocks from the next rank's pool over NVLink
+inside the fused link kernel (gather + RoPE delta + scatter in one pass),
+the other half from its own pool.  Per-GPU work is fixed (weak scaling);
+each per-step time is the max over ranks.
+
+Reported ``value`` = p50 over steps of the device-timed Link TTFT in ms
+(lower is better), max over ranks.  ``e2e`` is the same Link through the
+public engine API timed by the host (plan resolution, directory grace-period
+ticket, H2D of the step's inputs from pinned host memory, first-token D2H).
+``repair_agreement`` compares each Link's 256 greedy tokens with the full
+prefill's (sparse windows are an approximation: reported, not claimed);
+``exact_repair_match`` is one Link with full windows checked token for token
+against the full prefill during warm-up.
 
 ``--impl reference`` runs the unmodified reference.  Its runtime is a patch
 series over upstream SGLang that is not vendored and cannot be built offline,
@@ -59,8 +70,9 @@ def parse():
     return p.parse_args()
 
 
-def synthetic_context(n_sub: int, total: int, vocab: int, seed: int):
-    """Sub-context lengths log-uniform in [64, 4096], rescaled to ``total``."""
+def context_lengths(n_sub: int, total: int, seed: int) -> list[int]:
+    """Sub-context lengths log-uniform in [64, 4096], rescaled to ``total``
+    (the same on every rank, so per-GPU work is identical)."""
     rng = random.Random(seed)
     raw = [math.exp(rng.uniform(math.log(64), math.log(4096))) for _ in range(n_sub)]
     scale = total / sum(raw)
@@ -74,8 +86,28 @@ def synthetic_context(n_sub: int, total: int, vocab: int, seed: int):
         elif sum(lens) > total and lens[j] > 64:
             lens[j] -= 1
         i += 1
-    subs = [[rng.randrange(vocab) for _ in range(n)] for n in lens]
-    return subs
+    return lens
+
+
+def context_tokens(lens: list[int], vocab: int, seed: int, owner: int) -> list[list[int]]:
+    """The token ids of the sub-contexts compiled by replica ``owner``."""
+    rng = random.Random(seed * 7919 + 1 + owner)
+    return [[rng.randrange(vocab) for _ in range(n)] for n in lens]
+
+
+def peer_half(lens: list[int]) -> set[int]:
+    """Indices of the blocks a Link reads from a peer: a greedy split of the
+    linked blocks into two halves of about equal token count."""
+    order = sorted(range(len(lens)), key=lambda i: -lens[i])
+    a, b, sa, sb = [], [], 0, 0
+    for i in order:
+        if sa <= sb:
+            a.append(i)
+            sa += lens[i]
+        else:
+            b.append(i)
+            sb += lens[i]
+    return set(b)
 
 
 class ClockSampler:
@@ -137,14 +169,16 @@ def main():
         if int(os.environ.get("RANK", "0")) == 0:
             reference_arm(args)
         return
+    # the KV pools are mapped peer to peer; no NVLink multicast object is needed
+    os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
     import torch
     import torch.distributed as dist
 
-    from sglang_legolink_b200 import ops
     from sglang_legolink_b200.models.config import PRESETS
     from sglang_legolink_b200.models.qwen import QwenModel
-    from sglang_legolink_b200.runtime.engine import Engine
+    from sglang_legolink_b200.runtime.engine import Engine, pages_for
     from sglang_legolink_b200.utils.launch_count import LaunchCounter
+    from sglang_legolink_b200.utils.trace import CudaTimer
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -160,26 +194,52 @@ def main():
     t0 = time.time()
     model = QwenModel.random_init(cfg, seed=args.seed, device=dev, dtype=torch.bfloat16)
     torch.cuda.synchronize()
-    eng = Engine(model, page_size=args.page_size, max_context=args.context + args.decode + 1024,
-                 mem_fraction=0.6)
+    n_tot = args.context + 32
+    seq_pages = pages_for(n_tot + args.decode + 64, args.page_size)
+    # own compiled blocks + the Link's and the full prefill's sequences (+ the
+    # exact-repair check's) + slack; one size on every rank (symmetric memory)
+    num_pages = pages_for(args.context, args.page_size) + 3 * seq_pages + 1024
+    max_ctx = args.context + args.decode + 1024
+    peer = (rank + 1) % world
+    if world > 1:
+        from sglang_legolink_b200.parallel.dp import BlockDirectory, SharedKVPool
+
+        pool = SharedKVPool(cfg.num_layers, num_pages, model.hkv, args.page_size, cfg.head_dim, torch.bfloat16, dev)
+        directory = BlockDirectory(dist.distributed_c10d._get_default_store(), prefix="bench/", world=world)
+        eng = Engine(model, page_size=args.page_size, max_context=max_ctx, kv_pool=pool, directory=directory,
+                     replica_rank=rank, peer_pools={r: pool.peer(r) for r in range(world) if r != rank})
+    else:
+        eng = Engine(model, page_size=args.page_size, max_context=max_ctx, num_pages=num_pages)
     init_s = time.time() - t0
 
-    subs = synthetic_context(args.subcontexts, args.context, cfg.vocab_size, args.seed)
     n_link = args.subcontexts - args.fresh
-    prefix = [151644, 8948, 198]  # chat-template header tokens (system turn start)
+    lens = context_lengths(args.subcontexts, args.context, args.seed)
+    own = context_tokens(lens, cfg.vocab_size, args.seed, rank)
+    # every block is compiled once on the node: by its owner
     for i in range(n_link):
-        eng.compile(subs[i], f"sub-{i}")
-    fresh = sum(subs[n_link:], [])
+        eng.compile(own[i], f"sub-{rank}-{i}")
+    remote_idx = peer_half(lens[:n_link]) if world > 1 else set()
+    nxt = context_tokens(lens, cfg.vocab_size, args.seed, peer) if world > 1 else own
+    src_owner = {i: (peer if i in remote_idx else rank) for i in range(n_link)}
+    block_toks = {i: (nxt[i] if i in remote_idx else own[i]) for i in range(n_link)}
+    fresh = sum(own[n_link:], [])
+    peer_tokens = sum(lens[i] for i in remote_idx)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()  # every rank's blocks are published before any Link
     rng = random.Random(args.seed + 1 + rank)
 
-    def make_request(step):
+    def make_request(step, exact=False):
         order = list(range(n_link))
         rng.shuffle(order)
         user = [rng.randrange(cfg.vocab_size) for _ in range(32)]
         suffix = fresh + user
-        plan = {"cache_keys": [f"sub-{i}" for i in order], "recompute_initial_tokens": args.repair,
-                "recompute_first_block": True, "request_id": f"bench-{rank}-{step}"}
-        full = sum((subs[i] for i in order), []) + suffix
+        plan = {"cache_keys": [f"sub-{src_owner[i]}-{i}" for i in order], "request_id": f"bench-{rank}-{step}"}
+        if exact:
+            plan["recompute_tokens_per_block"] = [lens[i] for i in order]
+        else:
+            plan.update(recompute_initial_tokens=args.repair, recompute_first_block=True)
+        full = sum((block_toks[i] for i in order), []) + suffix
         return plan, suffix, full
 
     def barrier():
@@ -187,61 +247,67 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    def max_over_ranks(vals):
+    def reduce(vals, op):
         t = torch.tensor(vals, dtype=torch.float64, device=dev)
         if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return t.tolist()
-
-    def sum_over_ranks(vals):
-        t = torch.tensor(vals, dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.SUM)
+            dist.all_reduce(t, op=op)
         return t.tolist()
 
     counter = LaunchCounter()
 
-    def one_step(step, timed):
+    def one_step(step, exact=False):
         """Full prefill + its decode (the baseline), then Link + its decode.
         Both timed prefills start from the same GPU state -- the end of a
         decode -- so neither inherits the other's power-capped clocks (a
         Link issued right after a 16K-token dense prefill starts at
         ~1.3-1.4 GHz under sw_power_cap instead of 1.97 GHz)."""
-        plan, suffix, full = make_request(step)
+        plan, suffix, full = make_request(step, exact)
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
-        fp_ms = float("nan")
+        fp_ms, base_out = float("nan"), None
         if not args.no_full_prefill:
-            # --- full prefill baseline, decoded like the Link
             ev[4].record()
             base = eng.prefill(full)
             ev[5].record()
             eng.decode([base], args.decode - 1)
             ev[6].record()
+            base_out = list(base.output_ids)
             eng.free(base)
-        # --- Link (device-timed TTFT; e2e measured by the host around the API call)
+        timer = CudaTimer(enabled=True)
         torch.cuda.synchronize()
         h0 = time.perf_counter()
         ev[0].record()
-        seq = eng.link(plan, suffix)  # returns after the first token reached the host
+        seq = eng.link(plan, suffix, timer=timer)  # returns after the first token reached the host
         ev[1].record()
         h1 = time.perf_counter()
-        # --- decode
         ev[2].record()
         eng.decode([seq], args.decode - 1)
         ev[3].record()
+        link_out = list(seq.output_ids)
         eng.free(seq)
         torch.cuda.synchronize()
-        link_ms = ev[0].elapsed_time(ev[1])
-        dec_ms = ev[2].elapsed_time(ev[3])
-        if not args.no_full_prefill:
-            fp_ms = ev[4].elapsed_time(ev[5])
-        return link_ms, dec_ms, fp_ms, (h1 - h0) * 1e3, len(plan["imp_indices"])
+        spans = timer.finalize()
+        r = {"link": ev[0].elapsed_time(ev[1]), "dec": ev[2].elapsed_time(ev[3]), "e2e": (h1 - h0) * 1e3,
+             "rows": len(plan["imp_indices"]), "peer_ms": spans.get("kv_link_peer", 0.0),
+             "local_ms": spans.get("kv_link_local", 0.0), "fp": float("nan"), "first": float("nan"),
+             "prefix": float("nan")}
+        if base_out is not None:
+            r["fp"] = ev[4].elapsed_time(ev[5])
+            r["first"] = float(link_out[0] == base_out[0])
+            n = 0
+            while n < min(len(link_out), len(base_out)) and link_out[n] == base_out[n]:
+                n += 1
+            r["prefix"] = float(n)
+        return r
 
+    exact_prefix = None
     for w in range(args.warmup):
-        one_step(-1 - w, False)
+        r = one_step(-1 - w, exact=(w == 0 and not args.no_full_prefill))
+        if w == 0 and not args.no_full_prefill:
+            exact_prefix = r["prefix"]
+    exact_all = reduce([exact_prefix], dist.ReduceOp.MIN if world > 1 else None)[0] \
+        if exact_prefix is not None else None
     barrier()
-    links, decs, fps, e2es = [], [], [], []
-    rows = 0
+    res = []
     with ClockSampler(local) as clocks:
         counter.start()
         barrier()
@@ -249,29 +315,42 @@ def main():
         t_end = torch.cuda.Event(enable_timing=True)
         t_start.record()
         for s in range(args.steps):
-            l, d, f, e, rows = one_step(s, True)
-            links.append(l), decs.append(d), fps.append(f), e2es.append(e)
+            res.append(one_step(s))
         t_end.record()
         barrier()
         launches = counter.stop()
     total_ms = t_start.elapsed_time(t_end)
-    links = max_over_ranks(links)
-    decs = max_over_ranks(decs)
-    fps = max_over_ranks(fps)
-    e2es = max_over_ranks(e2es)
-    total_ms = max_over_ranks([total_ms])[0]
-    dec_tok_s_rank = (args.decode - 1) / (statistics.median(decs) / 1e3)
-    dec_tok_s = sum_over_ranks([dec_tok_s_rank])[0]
+    MAX = dist.ReduceOp.MAX if world > 1 else None
+    SUM = dist.ReduceOp.SUM if world > 1 else None
+    col = lambda k: [r[k] for r in res]  # noqa: E731
+    links, decs, fps, e2es = (reduce(col(k), MAX) for k in ("link", "dec", "fp", "e2e"))
+    peer_ms = reduce(col("peer_ms"), MAX)
+    total_ms = reduce([total_ms], MAX)[0]
+    firsts = reduce(col("first"), SUM)
+    prefixes = reduce(col("prefix"), SUM)
+    launches = int(reduce([launches], SUM)[0])
+    rows = res[-1]["rows"]
+    dec_tok_s_rank = (args.decode - 1) / (statistics.median(col("dec")) / 1e3)
+    dec_tok_s = reduce([dec_tok_s_rank], SUM)[0]
     link_p50 = statistics.median(links)
     fp_p50 = statistics.median(fps) if not args.no_full_prefill else None
     clk = clocks.summary()
     # bytes per step moved by the public API around the Link: token ids of the
     # recomputed rows + positions + slots + page table + link gather lists in,
     # the first token id out (the decode adds 4 B per generated token out).
-    n_tot = args.context + 32 + 0
     pages = (n_tot + args.page_size - 1) // args.page_size
     linked = n_tot - rows
     h2d = rows * (4 + 4 + 8) + pages * 4 + linked * (8 + 8 + 4 + 4)
+    kv_bytes_per_token = 2 * cfg.num_layers * model.hkv * cfg.head_dim * 2
+    peer_link = None
+    if world > 1:
+        pm = statistics.median(peer_ms)
+        gbs = peer_tokens * kv_bytes_per_token / (pm * 1e-3) / 1e9 if pm > 0 else None
+        peer_link = {"tokens_per_link": peer_tokens, "bytes_per_link": peer_tokens * kv_bytes_per_token,
+                     "kernel_ms_p50": round(pm, 4), "gbs": round(gbs, 1) if gbs else None,
+                     "roofline": "NVLink peer read, measured 770 GB/s per direction",
+                     "frac_of_measured_nvlink": round(gbs / 770.0, 3) if gbs else None}
+    nsteps = args.steps * world
     if rank == 0:
         out = {
             "metric": "Link-request p50 TTFT and decode tok/s vs full prefill, 1/2/4/8 B200",
@@ -290,7 +369,7 @@ def main():
                 "model": f"{args.model} (random init)",
                 "global_batch": world,
                 "seq_len": args.context,
-                "parallelism": f"dp{world}" if world > 1 else "single",
+                "parallelism": f"dp{world} sharing one block directory" if world > 1 else "single",
                 "subcontexts": args.subcontexts,
                 "linked": n_link,
                 "fresh": args.fresh,
@@ -298,6 +377,8 @@ def main():
                 "recompute_rows": rows,
                 "decode_tokens": args.decode,
                 "page_size": args.page_size,
+                "peer_blocks_per_link": len(remote_idx),
+                "peer_token_fraction": round(peer_tokens / max(1, sum(lens[:n_link])), 3),
                 "l2": "inputs larger than L2: 15.2 GB weights and 0.9 GB of KV per request are streamed each step",
                 "step": "full prefill + 255-token decode (baseline), then Link + 255-token decode; each timed "
                         "prefill starts after a decode",
@@ -308,14 +389,22 @@ def main():
             "decode_tok_s": round(dec_tok_s, 2),
             "decode_tok_s_per_gpu": round(dec_tok_s_rank, 2),
             "decode_ms_per_token": round(statistics.median(decs) / (args.decode - 1), 4),
+            "repair_agreement": None if args.no_full_prefill else {
+                "first_token_match_frac": round(sum(firsts) / nsteps, 3),
+                "greedy_prefix_match_mean": round(sum(prefixes) / nsteps, 2),
+                "of_tokens": args.decode, "links": nsteps},
+            "exact_repair_match": None if exact_all is None else bool(exact_all >= args.decode),
+            "exact_repair_prefix_match": None if exact_all is None else int(exact_all),
+            "peer_link": peer_link,
             "e2e": {"value": round(statistics.median(e2es), 3), "unit": "ms",
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4 * args.decode},
             "gpu_launches": launches,
             "clocks": clk,
             "init_s": round(init_s, 1),
         }
-        print(json.dumps(out))
+        print(json.dumps(out), flush=True)
     if world > 1:
+        eng.release_graphs()
         dist.barrier()
         dist.destroy_process_group()
 

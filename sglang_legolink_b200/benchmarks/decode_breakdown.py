@@ -81,8 +81,8 @@ def main():
     kvb = n * hkv * D * 2 * 2
     # the five kernels of the fused decode layer (QwenModel._forward_decode_fused)
     eps = cfg.rms_norm_eps
-    ss = torch.full((1,), float(H), device=dev)
-    sq = torch.zeros(1, device=dev)
+    ss = ops.sumsq_from_values(torch.full((1,), float(H), device=dev))
+    sq = ops.sumsq_buffer(1, dev)
     hp = torch.empty(1, H, device=dev, dtype=torch.bfloat16)
     cases = {
         "gemv_qkv_rope": (lambda: [ops.gemv_qkv_rope(x, lw.qkv_w, lw.qkv_b, pos, slot, m.cos_sin, q, kpool[i],

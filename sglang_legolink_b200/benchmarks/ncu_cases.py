@@ -24,7 +24,7 @@ elif case == "gemv_residual":  # o_proj GEMV + residual epilogue: 4 launches at 
         x = torch.randn(M, H, device="cuda", dtype=torch.bfloat16)
         res = torch.randn(M, H, device="cuda", dtype=torch.bfloat16)
         h = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
-        sq = torch.zeros(M, device="cuda")
+        sq = ops.sumsq_buffer(M, "cuda")
         for _ in range(4): ops.gemv_residual(x, w, res, nw, h, sq)
     torch.cuda.synchronize()
 elif case == "gemm":

@@ -246,10 +246,11 @@ void gemm_small_m_epi(const at::Tensor& a, const at::Tensor& w, const c10::optio
   LLSmallMEpi e{};
   e.mode = (int)mode;
   if (scale_sumsq.has_value()) {
-    CHECK_F32(*scale_sumsq);
+    TORCH_CHECK(scale_sumsq->scalar_type() == at::kLong && scale_sumsq->is_contiguous(),
+                "scale_sumsq: int64 fixed-point sums of squares");
     TORCH_CHECK(scale_sumsq->numel() >= M);
   }
-  e.scale_sumsq = opt_ptr<const float>(scale_sumsq);
+  e.scale_sumsq = opt_ptr<const unsigned long long>(scale_sumsq);
   e.scale_eps = (float)scale_eps;
   int ldc = 0;
   if (mode == LL_EPI_STORE || mode == LL_EPI_SWIGLU) {
@@ -259,13 +260,15 @@ void gemm_small_m_epi(const at::Tensor& a, const at::Tensor& w, const c10::optio
     ldc = out->stride(0);
   } else if (mode == LL_EPI_RESIDUAL) {
     TORCH_CHECK(res.has_value() && norm_w.has_value() && h_out.has_value() && sumsq_out.has_value());
-    CHECK_BF16(*res); CHECK_BF16(*norm_w); CHECK_BF16(*h_out); CHECK_F32(*sumsq_out);
+    CHECK_BF16(*res); CHECK_BF16(*norm_w); CHECK_BF16(*h_out);
+    TORCH_CHECK(sumsq_out->scalar_type() == at::kLong && sumsq_out->is_contiguous(),
+                "sumsq_out: int64 fixed-point sums of squares");
     TORCH_CHECK(res->size(0) == M && res->size(1) == N && res->stride(1) == 1 && h_out->sizes() == res->sizes() &&
                 h_out->strides() == res->strides() && norm_w->numel() == N && sumsq_out->numel() >= M);
     e.res = opt_ptr<ll_bf16_t>(res);
     e.norm_w = opt_ptr<const ll_bf16_t>(norm_w);
     e.h_out = opt_ptr<ll_bf16_t>(h_out);
-    e.sumsq_out = opt_ptr<float>(sumsq_out);
+    e.sumsq_out = opt_ptr<unsigned long long>(sumsq_out);
     e.ld = res->stride(0);
   } else if (mode == LL_EPI_QKV_ROPE) {
     TORCH_CHECK(positions.has_value() && slots.has_value() && cos_sin.has_value() && q_out.has_value() &&

@@ -11,6 +11,12 @@
 //                    of the qkv product is exactly one head (head_dim 128).
 //   o_proj / down -> LL_EPI_RESIDUAL: r = bf16(y) + res; res = bf16(r);
 //                    h = bf16(r * norm_w); sumsq_out[m] += sum(r^2).
+//
+// Row sums of squares are 64-bit fixed point in units of 2^-24
+// (LL_SUMSQ_ONE): each output tile adds its part with an integer atomic, and
+// integer addition does not depend on the order in which the tiles finish,
+// so a decode step gives the same bits every time it runs (a float atomic
+// add would not, and greedy decoding of near-tied logits then drifts).
 //   gate_up / qkv / lm_head read such an h: with scale_sumsq set, the
 //                    accumulator of row m is multiplied by
 //                    rsqrt(scale_sumsq[m] / K + scale_eps) before the bias,
@@ -27,6 +33,8 @@ typedef __nv_bfloat16 ll_bf16_t;
 typedef uint16_t ll_bf16_t;
 #endif
 
+#define LL_SUMSQ_ONE 16777216.0f
+
 enum {
   LL_EPI_STORE = 0,
   LL_EPI_SWIGLU = 1,    // interleaved gate/up (groups of 16) -> silu(gate) * up, N / 2 columns
@@ -36,14 +44,15 @@ enum {
 
 struct LLSmallMEpi {
   int mode;
-  // row scale (an RMSNorm folded after the product); null: none
-  const float* scale_sumsq;
+  // row scale (an RMSNorm folded after the product); null: none.
+  // Fixed-point sums of squares (units of 1 / LL_SUMSQ_ONE).
+  const unsigned long long* scale_sumsq;
   float scale_eps;
   // LL_EPI_RESIDUAL: [M, ld] rows; res is read and written in place
   ll_bf16_t* res;
   const ll_bf16_t* norm_w;
   ll_bf16_t* h_out;
-  float* sumsq_out;  // [M], zeroed before the GEMV
+  unsigned long long* sumsq_out;  // [M] fixed point, zeroed before the GEMV
   int ld;
   // LL_EPI_QKV_ROPE
   const int* positions;        // [M]

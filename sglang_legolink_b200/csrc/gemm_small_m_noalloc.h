@@ -14,14 +14,18 @@
 //
 // Scratch: a file-scope device array of LL_NOALLOC_WS_FLOATS floats (4 MiB)
 // for split-K partial sums and LL_NOALLOC_TICKETS ints for the split-K tickets.
-// Every GPU that loads the library holds these until the process exits.
 // A call whose split-K partials (splits * M * N floats) or tile count
 // (ceil(N / 128)) exceed them is rejected with LL_NOALLOC_E_TOO_LARGE before
 // anything is launched; ll_gemm_small_m_noalloc_error_string() names it.
 //
-// The first call on a device looks up the device address of the scratch
-// (cudaGetSymbolAddress, with that device current) and caches it; make that
-// first call before any stream capture.  The call allocates nothing: no
+// The first call on each device does a one-time set-up: it looks up the device
+// address of the scratch (cudaGetSymbolAddress, with that device current) and
+// caches it.  Under CUDA's default lazy module loading that lookup is also what
+// loads this file's module onto the device, and with it the static scratch: a
+// one-time allocation made by the driver, not by this code.  A caller that may
+// not enter the allocator at all should therefore make one call per device
+// during its initialisation, before any stream capture; the device then holds
+// the scratch until the process exits.  Every later call allocates nothing: no
 // cudaMalloc, cudaFree or allocating library routine; the tickets it uses are
 // cleared with cudaMemsetAsync on the caller's stream before the launch.
 //

@@ -282,6 +282,11 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Fixed-point row sum of squares -> float (see gemm_epi.h).
+__device__ __forceinline__ float sumsq_value(unsigned long long x) {
+  return __ull2float_rn(x) * (1.f / LL_SUMSQ_ONE);
+}
+
 // Small-M (swap-AB, split-K) kernel.
 //   D^T[128 features, BNX rows] = W_tile[128, K] . A[BNX, K]^T
 // grid = (feature tiles, splits); each CTA does k-blocks [kb0, kb1).
@@ -422,7 +427,7 @@ __global__ void __launch_bounds__(192, 2)
     // values in registers.  Other rows load at use.
     float pf_rstd = 1.f;
     if (epi.scale_sumsq != nullptr && lane < M)
-      pf_rstd = rsqrtf(__ldcg(epi.scale_sumsq + lane) / (float)K + epi.scale_eps);
+      pf_rstd = rsqrtf(sumsq_value(__ldcg(epi.scale_sumsq + lane)) / (float)K + epi.scale_eps);
     const float pf_bias = (bias != nullptr && feat < N) ? __bfloat162float(bias[feat]) : 0.f;
     float pf_res0 = 0.f, pf_w = 0.f, pf_c0 = 0.f, pf_s0 = 0.f;
     int pf_pos = 0;
@@ -463,7 +468,7 @@ __global__ void __launch_bounds__(192, 2)
       RowPf p{1.f, 0.f, pf_c0, pf_s0, 0, 0};
       if (epi.scale_sumsq != nullptr) {
         const float rs = __shfl_sync(0xffffffffu, pf_rstd, m & 31);
-        p.rs = m < 32 ? rs : (m < M ? rsqrtf(__ldcg(epi.scale_sumsq + m) / (float)K + epi.scale_eps) : 1.f);
+        p.rs = m < 32 ? rs : (m < M ? rsqrtf(sumsq_value(__ldcg(epi.scale_sumsq + m)) / (float)K + epi.scale_eps) : 1.f);
       }
       if (epi.mode == LL_EPI_RESIDUAL) {
         if (m < M && feat < N) p.res = m == 0 ? pf_res0 : __bfloat162float(epi.res[(size_t)m * epi.ld + feat]);
@@ -502,7 +507,7 @@ __global__ void __launch_bounds__(192, 2)
           epi.h_out[i] = __float2bfloat16(r * pf_w);
         }
         const float ss = warp_sum(r * r);
-        if (lane == 0) atomicAdd(epi.sumsq_out + m, ss);
+        if (lane == 0) atomicAdd(epi.sumsq_out + m, __float2ull_rn(ss * LL_SUMSQ_ONE));
       } else {  // LL_EPI_QKV_ROPE: this tile is head nb of [Hq | Hkv keys | Hkv values]
         float x = bf16_round(v);
         const int64_t slot = p.slot;

@@ -393,7 +393,7 @@ class QwenModel:
         q = self._buf("q", (T, self.hq, D))
         attn = self._buf("attn", (T, self.hq * D))
         mlp = self._buf("mlp", (T, self.inter))
-        ss = self._buf("rowsq", (2 * L, T), torch.float32)
+        ss = self._buf("rowsq", (2 * L, T), torch.int64)  # fixed-point sums of squares
         ss.zero_()
         for li, lw in enumerate(self.layers):
             ops.gemv_qkv_rope(h, lw.qkv_w, lw.qkv_b, fb.positions, fb.slots, self.cos_sin, q, kv.k[li], kv.v[li],

@@ -165,8 +165,29 @@ def _small_m_splits(ws, M: int, N: int, K: int) -> int:
     return splits
 
 
+SUMSQ_ONE = float(1 << 24)
+
+
+def sumsq_buffer(shape, device) -> torch.Tensor:
+    """Zeroed row sums of squares for the decode GEMV epilogues: int64 fixed
+    point (units of 2^-24) on CUDA, whose atomic accumulation does not depend
+    on tile completion order; fp32 on CPU."""
+    dtype = torch.int64 if torch.device(device).type == "cuda" else torch.float32
+    return torch.zeros(shape, dtype=dtype, device=device)
+
+
+def sumsq_values(sumsq: torch.Tensor) -> torch.Tensor:
+    """fp32 values of a sums-of-squares buffer (either representation)."""
+    return sumsq.double().div(SUMSQ_ONE).float() if sumsq.dtype == torch.int64 else sumsq.float()
+
+
+def sumsq_from_values(vals: torch.Tensor) -> torch.Tensor:
+    """The CUDA (fixed-point) representation of fp32 sums of squares."""
+    return torch.round(vals.double() * SUMSQ_ONE).to(torch.int64)
+
+
 def _row_rstd(sumsq: torch.Tensor, K: int, eps: float) -> torch.Tensor:
-    return torch.rsqrt(sumsq.float() / K + eps)
+    return torch.rsqrt(sumsq_values(sumsq) / K + eps)
 
 
 def gemv_rownorm(x, w, bias, sumsq, eps: float, out=None, swiglu: bool = False):
@@ -196,7 +217,8 @@ def gemv_residual(x, w, residual, norm_w, h_out, sumsq_out, scale_sumsq=None, ep
     """``y = x @ w.T``; ``r = bf16(y) + residual``; ``residual = bf16(r)``;
     ``h_out = bf16(r * norm_w)``; ``sumsq_out[m] += sum(r[m]^2)`` (fp32
     ``r``) -- the residual add and the data half of the next RMSNorm, done in
-    the GEMV's stores.  ``sumsq_out`` must be zero beforehand."""
+    the GEMV's stores.  ``sumsq_out`` must be zero beforehand; on CUDA it is
+    int64 fixed point (:func:`sumsq_buffer`)."""
     M, K = x.shape
     N = w.shape[0] * 128 if w.dim() == 4 else w.shape[0]
     if not x.is_cuda:

@@ -66,6 +66,20 @@ def _agree(ok: bool, group) -> tuple[bool, bool]:
     return bool(t[0]), bool(t[1])
 
 
+def _agree_items(oks: list, group) -> bool:
+    """True when every rank has the same per-item outcomes."""
+    t = torch.tensor([1 if ok else 0 for ok in oks] or [1], dtype=torch.int32)
+    lo, hi = t.clone(), t.clone()
+    dist.all_reduce(lo, op=dist.ReduceOp.MIN, group=group)
+    dist.all_reduce(hi, op=dist.ReduceOp.MAX, group=group)
+    return bool(torch.equal(lo, hi))
+
+
+def _step_oks(out) -> list:
+    c_out, l_out = out
+    return [not isinstance(r, Exception) for r in list(c_out) + list(l_out)]
+
+
 def _validate_tp() -> bool:
     return os.getenv("SGLANG_PIC_VALIDATE_TP", "0") == "1"
 
@@ -141,6 +155,43 @@ class SPMDEngine:
     def compile_batch(self, items):
         return self._call("compile_batch", (list(items),), {})
 
+    def extend_step(self, compiles=(), links=(), timer=None):
+        """One batched Compile + Link step on every rank.  Items fail alone,
+        so the ranks agree item by item; a Link that succeeded everywhere
+        gets a handle the workers know it by."""
+        with self._lock:
+            if self.broken:
+                raise TPDivergence(self.broken)
+            compiles = [tuple(c) for c in compiles]
+            items, handles = [], []
+            for it in links:
+                pic_link, ids, rid, sampling = (tuple(it) + (None, None))[:4]
+                self._next += 1
+                handles.append(self._next)
+                items.append((pic_link, list(ids), rid, _pin_seed(sampling)))
+            wire = (compiles, [(dict(p), i, r, sp) for p, i, r, sp in items])
+            dist.broadcast_object_list([("extend_step", wire, {"_handles": handles})], src=0, group=self._group)
+            try:
+                out = self._engine.extend_step(compiles=compiles, links=items)
+            except Exception as e:  # noqa: BLE001 - the whole step failed alone on this rank
+                out = ([e] * len(compiles), [e] * len(items))
+            if not _agree_items(_step_oks(out), self._group):
+                self.broken = "TP ranks diverged on extend_step"
+                raise TPDivergence(self.broken)
+            for h, seq in zip(handles, out[1]):
+                if not isinstance(seq, Exception):
+                    seq._spmd_handle = h
+        if _validate_tp():
+            for i, seq in enumerate(out[1]):
+                if isinstance(seq, Exception):
+                    continue
+                try:
+                    self._call("check_manifest", (seq,), {}, wire_args=(seq._spmd_handle,))
+                except Exception as e:  # noqa: BLE001
+                    self.free(seq)
+                    out[1][i] = e
+        return out
+
     def free(self, seq):
         return self._call("free", (seq,), {}, wire_args=(seq._spmd_handle,))
 
@@ -173,6 +224,17 @@ def worker_loop(engine, group) -> int:
         if op == "shutdown":
             return n
         n += 1
+        if op == "extend_step":
+            compiles, links = args
+            try:
+                out = engine.extend_step(compiles=compiles, links=links)
+            except Exception as e:  # noqa: BLE001
+                out = ([e] * len(compiles), [e] * len(links))
+            for h, seq in zip(kw.get("_handles", ()), out[1]):
+                if not isinstance(seq, Exception):
+                    live[h] = seq
+            _agree_items(_step_oks(out), group)
+            continue
         handle = kw.pop("_handle", None)
         ok = True
         try:

@@ -80,6 +80,20 @@ class Sequence_:
     promotion: Optional[dict] = None  # record of an experimental group promotion
 
 
+@dataclass
+class _LinkWork:
+    """One Link between its reservation and its first token."""
+    plan: dict
+    resolved: ResolvedLinkPlan
+    keys: list
+    remote: dict
+    pages: list
+    rid: str
+    sampling: SamplingParams
+    generator: Optional[torch.Generator]
+    linked_rows: int = 0
+
+
 def group_promotion_enabled() -> bool:
     """EXPERIMENTAL, off by default.  A Link's reconstructed execution group
     becomes a cache block only when the deployment sets this flag AND the
@@ -177,7 +191,6 @@ class Engine:
         self.directory = directory
         self.replica_rank = replica_rank
         self.peer_pools = peer_pools if peer_pools is not None else {}
-        self._remote: dict = {}
         self._dir = None
         self._published: dict = {}  # cache_key -> RemoteBlock this replica serves to its peers
         if directory is not None:
@@ -405,48 +418,7 @@ class Engine:
         defers the second to the next batch, where it takes the duplicate
         path); here that is refused outright.
         Reference: ``pic_compile_key_in_batch``, ``pic_runtime.py:1954-1975``."""
-        with self._lock:
-            out: list = [None] * len(items)
-            prepared = []
-            seen: set = set()
-            for i, it in enumerate(items):
-                token_ids, cache_key, sub_context, block_id = (tuple(it) + (None, None))[:4]
-                try:
-                    if str(cache_key) in seen:
-                        raise ContractError(f"two Compiles of '{cache_key}' in one batch")
-                    seen.add(str(cache_key))
-                    toks, ckey, bid = self._compile_prepare(token_ids, cache_key, sub_context, block_id)
-                    pages = self._alloc_pages(pages_for(len(toks), self.page_size))
-                    prepared.append((i, toks, ckey, bid, str(cache_key), pages))
-                except Exception as e:  # noqa: BLE001 - request-scoped
-                    out[i] = e
-            if not prepared:
-                return out
-            try:
-                fb = self._extend_batch([(toks, list(range(len(toks))), pages, len(toks))
-                                         for _, toks, _, _, _, pages in prepared])
-                if len(prepared) > 1:  # grouped execution rows (row-wise compute when enabled)
-                    o, ranges = 0, []
-                    for _, toks, *_ in prepared:
-                        ranges.append({"start": o, "end": o + len(toks)})
-                        o += len(toks)
-                    fb.repair_meta = {"batch_execution_unit_size": len(prepared), "repair_ranges": ranges}
-                logits = self.model.forward(fb, self.kv)
-                firsts = self._sample(logits).tolist()
-                self._kernel_check("compile")
-            except Exception as e:
-                for i, *_rest, pages in prepared:
-                    self.alloc.release(pages)
-                    out[i] = e
-                return out
-            for (i, toks, ckey, bid, key, pages), first in zip(prepared, firsts):
-                try:
-                    if self.storage_mode(items[i][2] if len(items[i]) > 2 else None) == "clone":
-                        pages = self._clone_pages(pages)
-                    out[i] = self._compile_register(toks, key, ckey, bid, pages, int(first))
-                except Exception as e:  # noqa: BLE001
-                    out[i] = e
-            return out
+        return self.extend_step(compiles=items)[0]
 
     @staticmethod
     def storage_mode(sub_context: Optional[dict]) -> str:
@@ -504,31 +476,32 @@ class Engine:
         emit_trace("compile_registered", cache_key=str(cache_key), token_count=n, status=status)
         return {"cache_key": str(cache_key), "status": status, "token_count": n, "first_token": first}
 
-    def block_tokens(self, cache_key: str):
+    def block_tokens(self, cache_key: str, remote: Optional[dict] = None):
         t = self.registry.tokens(cache_key)
-        if t is None and cache_key in self._remote:
-            return list(self._remote[cache_key].token_ids)
+        if t is None and remote and cache_key in remote:
+            return list(remote[cache_key].token_ids)
         return t
 
     # ------------------------------------------------------------------ link
     def resolve(self, pic_link: dict, mutable_input_ids: Sequence[int]) -> ResolvedLinkPlan:
         return resolve_link_plan(pic_link, mutable_input_ids, self.block_tokens)
 
-    def _preflight(self, pic_link: dict) -> None:
-        """Classify every source before anything is derived from it, so a
-        missing / stale / incompatible block aborts with the recovery JSON."""
+    def _preflight(self, pic_link: dict) -> dict:
+        """Classifies every source before anything is derived from it, so a
+        missing / stale / incompatible block aborts with the recovery JSON.
+        Returns the sources found on peer replicas (key -> RemoteBlock)."""
         keys = list(dict.fromkeys(str(k) for k in pic_link["cache_keys"]))
         ckey = self.compat_key(pic_link.get("adapter_id"), pic_link.get("segmentation_policy_version"),
                                pic_link.get("legolink_policy_version"))
         res = self.registry.lookup(keys, ckey)
-        self._remote = {}
+        remote: dict = {}
         if not res["ok"] and self._dir is not None:
             still = []
             for k in res["missing"]:
                 rb = self._dir.find(k)
                 if rb is not None and rb.owner != self.replica_rank and rb.compat_key == ckey \
                         and (rb.owner in self.peer_pools):
-                    self._remote[k] = rb
+                    remote[k] = rb
                 else:
                     still.append(k)
             res["missing"] = still
@@ -539,10 +512,16 @@ class Engine:
             raise LinkSourceUnavailable(
                 residency_recovery_message(res["missing"], res["stale"], res["incompatible"]),
                 res["missing"], res["stale"], res["incompatible"])
+        return remote
 
-    def reserve_link_sources(self, resolved: ResolvedLinkPlan, pic_link: dict) -> list[str]:
-        """lookup -> pin -> capacity check (reference ``pic_runtime.py:2790-2961``)."""
-        keys = [k for k in dict.fromkeys(resolved.cache_keys) if k not in self._remote]
+    def reserve_link_sources(self, resolved: ResolvedLinkPlan, pic_link: dict,
+                             remote: Optional[dict] = None, extra_pages: int = 0) -> tuple[list[str], dict]:
+        """lookup -> pin -> capacity check (reference ``pic_runtime.py:2790-2961``).
+        Returns the pinned local keys and the validated peer sources (with a
+        grace-period ticket open for them); ``extra_pages`` are pages the same
+        batch needs before this Link's own."""
+        remote = dict(remote or {})
+        keys = [k for k in dict.fromkeys(resolved.cache_keys) if k not in remote]
         ckey = self.compat_key(pic_link.get("adapter_id"), pic_link.get("segmentation_policy_version"),
                                pic_link.get("legolink_policy_version"))
         res = self.registry.lookup(keys, ckey)
@@ -553,32 +532,29 @@ class Engine:
                 residency_recovery_message(res["missing"], res["stale"], res["incompatible"]),
                 res["missing"], res["stale"], res["incompatible"])
         self.registry.pin(keys)
-        if self._remote:
+        if remote:
             # one grace-period ticket for this Link; entries of owners whose
             # generation moved are re-read (a withdrawn block is missing now)
-            valid, missing, stale = self._dir.begin(self._remote)
+            valid, missing, stale = self._dir.begin(remote)
             if missing or stale:
                 self.registry.unpin(keys)
-                self._remote = {}
                 emit_trace("legolink_request_failed_closed", reason="scheduler_source_preflight_failed",
                            missing=missing, stale=stale, incompatible=[])
                 raise LinkSourceUnavailable(residency_recovery_message(missing, stale, []), missing, stale, ())
-            self._remote = valid
-        need = pages_for(resolved.total_token_count, self.page_size)
+            remote = valid
+        need = pages_for(resolved.total_token_count, self.page_size) + extra_pages
         allocatable = self.alloc.num_free + self.radix.evictable_pages() + self.registry.capacity_evictable_pages() \
             + self._published_evictable_pages()
         if need > allocatable:
             self.registry.unpin(keys)
-            if self._remote:
+            if remote:
                 self._dir.end()
-                self._remote = {}
             raise CapacityError(
                 "LegoLink cannot allocate request-private destination KV without evicting its reserved source "
                 f"blocks: required={resolved.total_token_count}, allocatable={allocatable * self.page_size}.")
-        pic_link["_scheduler_reserved_cache_keys"] = keys
-        return keys
+        return keys, remote
 
-    def _link_rows(self, resolved: ResolvedLinkPlan, dst_pages: list[int]) -> dict:
+    def _link_rows(self, resolved: ResolvedLinkPlan, dst_pages: list[int], remote: dict) -> dict:
         """(src_slot, dst_slot, local_pos, global_pos) of every linked token
         (recomputed rows are skipped: repair rewrites them), grouped by the
         replica whose pool holds the source block (``None`` = this one)."""
@@ -586,7 +562,7 @@ class Engine:
         groups: dict = {}
         dpg = np.asarray(dst_pages, dtype=np.int64)
         for key, l0, g0, cnt in resolved.linked_rows():
-            rb = self._remote.get(key)
+            rb = remote.get(key)
             if rb is None:
                 h = self.registry.handle(key)
                 pages, off, sps, owner = h["pages"], int(h["first_page_offset"]), ps, None
@@ -601,96 +577,196 @@ class Engine:
             g[1].append(dpg[glob // ps] * ps + glob % ps)
             g[2].append(loc)
             g[3].append(glob)
-        out = {}
-        for o, g in groups.items():
-            src, dst, lp, gp = (np.concatenate(x) for x in g)
-            out[o] = (torch.from_numpy(src), torch.from_numpy(dst), torch.from_numpy(lp.astype(np.int32)),
-                      torch.from_numpy(gp.astype(np.int32)))
-        return out
+        return {o: tuple(np.concatenate(x) for x in g) for o, g in groups.items()}
+
+    def _link_prepare(self, pic_link: dict, mutable_input_ids: Sequence[int], rid: str,
+                      sampling: Optional[SamplingParams], extra_pages: int = 0) -> "_LinkWork":
+        """Validates, resolves and reserves one Link, then allocates its
+        request-private pages.  On failure nothing stays pinned or allocated."""
+        from ..contract import validate_pic_link_request
+
+        validate_pic_link_request(pic_link)
+        remote = self._preflight(pic_link)
+        resolved = resolve_link_plan(pic_link, mutable_input_ids, lambda k: self.block_tokens(k, remote),
+                                     validate=False)
+        resolved.apply_to(pic_link)
+        keys, remote = self.reserve_link_sources(resolved, pic_link, remote, extra_pages)
+        try:
+            self.registry.acquire(keys)
+            try:
+                pages = self._alloc_pages(pages_for(resolved.total_token_count, self.page_size))
+            except Exception:
+                self.registry.release(keys)
+                raise
+        except Exception:
+            self.registry.unpin(keys)
+            if remote:
+                self._dir.end()
+            raise
+        sp, gen = self._new_sampling(sampling)
+        return _LinkWork(pic_link, resolved, keys, remote, pages, rid, sp, gen)
+
+    def _link_close(self, w: "_LinkWork", ok: bool) -> None:
+        """Releases one Link's reservations (after its kernels finished)."""
+        self.registry.release(w.keys)
+        self.registry.unpin(w.keys)
+        if w.remote:
+            self._dir.end()  # the link kernel finished reading (the first token is on the host)
+            self.stats["remote_blocks_linked"] += len(w.remote)
+        if not ok and w.pages:
+            self.alloc.release(w.pages)
+            w.pages = []
+
+    def _link_account(self, w: "_LinkWork") -> None:
+        rec = np.sort(np.asarray(w.resolved.recompute_positions, dtype=np.int64))
+        for b in w.resolved.block_ranges:
+            recomputed = int(np.searchsorted(rec, b.end_token) - np.searchsorted(rec, b.start_token))
+            self.registry.record_execution(b.cache_key, b.token_count - recomputed, recomputed)
+        self.stats["links"] += 1
 
     def link(self, pic_link: dict, mutable_input_ids: Sequence[int], *, rid: Optional[str] = None,
              timer: Optional["CudaTimer"] = None, sampling: Optional[SamplingParams] = None) -> Sequence_:
         """Executes one Link.  Returns a sequence whose KV holds the whole
         linked prompt and whose ``output_ids[0]`` is the first token."""
+        out = self.extend_step(links=[(pic_link, mutable_input_ids, rid, sampling)], timer=timer)[1][0]
+        if isinstance(out, Exception):
+            raise out
+        return out
+
+    def link_batch(self, items: Sequence[tuple], timer: Optional["CudaTimer"] = None) -> list:
+        """Several Links in one step: every linked token of every Link moves
+        in one fused KV-link launch per source pool, and every Link's repair
+        rows go through ONE extend forward (per-request pages, positions and
+        causal-by-position attention).  ``items``: (pic_link, mutable ids[,
+        rid[, sampling]]).  Returns a Sequence_ or the exception per item;
+        an item that fails validation, reservation or allocation fails alone."""
+        return self.extend_step(links=items, timer=timer)[1]
+
+    def extend_step(self, compiles: Sequence[tuple] = (), links: Sequence[tuple] = (),
+                    timer: Optional["CudaTimer"] = None) -> tuple[list, list]:
+        """One prefill-type step: the given Compiles and Links share one
+        extend forward (one logits row each).  Returns (compile results,
+        link results), each a result or the exception per item."""
         with self._lock:
-            rid = rid or self.next_rid("link")
-            from ..contract import validate_pic_link_request
-
-            validate_pic_link_request(pic_link)
-            self._preflight(pic_link)
-            resolved = resolve_link_plan(pic_link, mutable_input_ids, self.block_tokens, validate=False)
-            resolved.apply_to(pic_link)
-            keys = self.reserve_link_sources(resolved, pic_link)
-            pages: list[int] = []
-            try:
-                self.registry.acquire(keys)
+            timer = timer or CudaTimer(enabled=False)
+            c_out: list = [None] * len(compiles)
+            l_out: list = [None] * len(links)
+            # ---- Compiles: validate + allocate
+            prepared, seen = [], set()
+            for i, it in enumerate(compiles):
+                token_ids, cache_key, sub_context, block_id = (tuple(it) + (None, None))[:4]
                 try:
-                    pages = self._alloc_pages(pages_for(resolved.total_token_count, self.page_size))
-                    seq = self._run_link(resolved, pages, rid, timer, sampling)
-                    # after repair, before decode: a failed promotion costs a
-                    # trace row, never the answer
-                    if group_promotion_enabled() and pic_link.get("promote_reconstructed_group"):
-                        seq.promotion = self._promote_group(resolved, pages, pic_link, rid)
-                finally:
-                    self.registry.release(keys)
-            except Exception:
-                if pages:
+                    if str(cache_key) in seen:
+                        raise ContractError(f"two Compiles of '{cache_key}' in one batch")
+                    seen.add(str(cache_key))
+                    toks, ckey, bid = self._compile_prepare(token_ids, cache_key, sub_context, block_id)
+                    pages = self._alloc_pages(pages_for(len(toks), self.page_size))
+                    prepared.append((i, toks, ckey, bid, str(cache_key), pages))
+                except Exception as e:  # noqa: BLE001 - request-scoped
+                    c_out[i] = e
+            # ---- Links: validate + resolve + reserve + allocate
+            works: list = []
+            for i, it in enumerate(links):
+                pic_link, ids, rid, sampling = (tuple(it) + (None, None))[:4]
+                rid = rid or self.next_rid("link")
+                try:
+                    works.append((i, self._link_prepare(pic_link, ids, rid, sampling)))
+                except Exception as e:  # noqa: BLE001 - request-scoped
+                    l_out[i] = e
+            if not prepared and not works:
+                return c_out, l_out
+            # ---- device work: fused KV link, then one forward
+            try:
+                if works:
+                    with timer.span("kv_link"):
+                        self._run_kv_links([w for _, w in works], timer)
+                items, params, gens = [], [], []
+                for _, toks, _, _, _, pages in prepared:
+                    items.append((toks, list(range(len(toks))), pages, len(toks)))
+                    params.append(GREEDY)
+                    gens.append(None)
+                for _, w in works:
+                    rows = list(w.resolved.recompute_positions)
+                    items.append(([w.resolved.linked_token_ids[p] for p in rows], rows, w.pages,
+                                  w.resolved.total_token_count))
+                    params.append(w.sampling)
+                    gens.append(w.generator)
+                with timer.span("sparse_repair"):
+                    fb = self._extend_batch(items)
+                    if len(prepared) > 1 and not works:  # grouped execution rows (row-wise compute when enabled)
+                        o, ranges = 0, []
+                        for _, toks, *_ in prepared:
+                            ranges.append({"start": o, "end": o + len(toks)})
+                            o += len(toks)
+                        fb.repair_meta = {"batch_execution_unit_size": len(prepared), "repair_ranges": ranges}
+                    logits = self.model.forward(fb, self.kv)
+                    firsts = self._sample(logits, params, gens).tolist()
+                self._kernel_check("link" if works else "compile")
+            except Exception as e:
+                for i, *_rest, pages in prepared:
                     self.alloc.release(pages)
-                raise
-            finally:
-                self.registry.unpin(keys)
-                if self._remote:
-                    self._dir.end()  # the link kernel finished reading (first token is on the host)
-                self.stats["remote_blocks_linked"] += len(self._remote)
-                self._remote = {}
-                pic_link.pop("_scheduler_reserved_cache_keys", None)
-            rec = np.sort(np.asarray(resolved.recompute_positions, dtype=np.int64))
-            for b in resolved.block_ranges:
-                recomputed = int(np.searchsorted(rec, b.end_token) - np.searchsorted(rec, b.start_token))
-                self.registry.record_execution(b.cache_key, b.token_count - recomputed, recomputed)
-            self.stats["links"] += 1
-            return seq
+                    c_out[i] = e
+                for i, w in works:
+                    self._link_close(w, ok=False)
+                    l_out[i] = e
+                return c_out, l_out
+            # ---- Compiles: register
+            for (i, toks, ckey, bid, key, pages), first in zip(prepared, firsts):
+                try:
+                    if self.storage_mode(compiles[i][2] if len(compiles[i]) > 2 else None) == "clone":
+                        pages = self._clone_pages(pages)
+                    c_out[i] = self._compile_register(toks, key, ckey, bid, pages, int(first))
+                except Exception as e:  # noqa: BLE001
+                    c_out[i] = e
+            # ---- Links: close reservations, account, build sequences
+            for (i, w), first in zip(works, firsts[len(prepared):]):
+                self._link_close(w, ok=True)
+                seq = Sequence_(rid=w.rid, token_ids=list(w.resolved.linked_token_ids), pages=w.pages,
+                                length=w.resolved.total_token_count, output_ids=[int(first)], kind="link",
+                                link_plan=w.resolved, sampling=w.sampling, generator=w.generator)
+                emit_trace("model_link_complete", rid=w.rid, total_token_count=w.resolved.total_token_count,
+                           recompute_rows=len(w.resolved.recompute_positions), linked_rows=w.linked_rows,
+                           batch_links=len(works))
+                # after repair, before decode: a failed promotion costs a
+                # trace row, never the answer
+                if group_promotion_enabled() and w.plan.get("promote_reconstructed_group"):
+                    seq.promotion = self._promote_group(w.resolved, w.pages, w.plan, w.rid)
+                w.plan.pop("_scheduler_reserved_cache_keys", None)
+                self._link_account(w)
+                l_out[i] = seq
+            return c_out, l_out
 
-    def _run_link(self, resolved: ResolvedLinkPlan, pages: list[int], rid: str, timer,
-                  sampling: Optional[SamplingParams] = None) -> Sequence_:
+    def _run_kv_links(self, works: list, timer) -> None:
+        """One fused KV-link launch per source pool for all ``works``."""
         dev = self.device
-        sp, gen = self._new_sampling(sampling)
-        timer = timer or CudaTimer(enabled=False)
-        with timer.span("kv_link"):
-            groups = self._link_rows(resolved, pages)
-            nlinked = 0
-            for owner, (src, dst, lp, gp) in groups.items():
-                nlinked += int(src.numel())
-                if not src.numel():
-                    continue
-                args = (self.kv.k, self.kv.v, src.to(dev), dst.to(dev), lp.to(dev), gp.to(dev), self.model.cos_sin)
-                if owner is None:
-                    with timer.span("kv_link_local"):
-                        ops.kv_link_rope(*args)
-                    if compare_enabled("kv_link"):  # diagnostic: fused kernel vs the torch statement
-                        emit_trace("kv_link_compare", rid=rid, **compare_kv_link(*args))
-                elif self.is_cuda:  # peer replica's pool, read over NVLink by the link kernel
-                    kp, vp, sps, sls = self.peer_pools[owner]
-                    with timer.span("kv_link_peer"):
-                        ops.kv_link_rope(*args, src_k_ptr=kp, src_v_ptr=vp, src_page_size=sps,
-                                         src_layer_stride=sls)
-                    self.stats["peer_tokens_linked"] = self.stats.get("peer_tokens_linked", 0) + int(src.numel())
-                else:
-                    ops.kv_link_rope(*args, src_pools=self.peer_pools[owner])
-                    self.stats["peer_tokens_linked"] = self.stats.get("peer_tokens_linked", 0) + int(src.numel())
-        rows = list(resolved.recompute_positions)
-        toks = [resolved.linked_token_ids[p] for p in rows]
-        with timer.span("sparse_repair"):
-            fb = self._extend_batch([(toks, rows, pages, resolved.total_token_count)])
-            logits = self.model.forward(fb, self.kv)
-            first = self._sample(logits, [sp], [gen])
-        first_id = int(first[0].item())
-        self._kernel_check("link")
-        emit_trace("model_link_complete", rid=rid, total_token_count=resolved.total_token_count,
-                   recompute_rows=len(rows), linked_rows=nlinked)
-        return Sequence_(rid=rid, token_ids=list(resolved.linked_token_ids), pages=pages,
-                         length=resolved.total_token_count, output_ids=[first_id], kind="link", link_plan=resolved,
-                         sampling=sp, generator=gen)
+        per_owner: dict = {}
+        for w in works:
+            rows = self._link_rows(w.resolved, w.pages, w.remote)
+            w.linked_rows = int(sum(len(g[0]) for g in rows.values()))
+            for owner, g in rows.items():
+                per_owner.setdefault(owner, []).append(g)
+        for owner, gs in per_owner.items():
+            src, dst, lp, gp = (np.concatenate([g[j] for g in gs]) for j in range(4))
+            if not src.size:
+                continue
+            t = [torch.from_numpy(src), torch.from_numpy(dst), torch.from_numpy(lp.astype(np.int32)),
+                 torch.from_numpy(gp.astype(np.int32))]
+            if self.is_cuda:
+                t = [_pinned_copy(x.numpy(), dev) for x in t]
+            args = (self.kv.k, self.kv.v, *t, self.model.cos_sin)
+            if owner is None:
+                with timer.span("kv_link_local"):
+                    ops.kv_link_rope(*args)
+                if compare_enabled("kv_link"):  # diagnostic: fused kernel vs the torch statement
+                    emit_trace("kv_link_compare", **compare_kv_link(*args))
+            elif self.is_cuda:  # peer replica's pool, read over NVLink by the link kernel
+                kp, vp, sps, sls = self.peer_pools[owner]
+                with timer.span("kv_link_peer"):
+                    ops.kv_link_rope(*args, src_k_ptr=kp, src_v_ptr=vp, src_page_size=sps, src_layer_stride=sls)
+                self.stats["peer_tokens_linked"] = self.stats.get("peer_tokens_linked", 0) + int(src.size)
+            else:
+                ops.kv_link_rope(*args, src_pools=self.peer_pools[owner])
+                self.stats["peer_tokens_linked"] = self.stats.get("peer_tokens_linked", 0) + int(src.size)
 
     def _promote_group(self, resolved: ResolvedLinkPlan, pages: list[int], plan: dict, rid: str) -> Optional[dict]:
         """EXPERIMENTAL.  Makes a fully reconstructed execution group durable:

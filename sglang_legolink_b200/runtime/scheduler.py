@@ -6,9 +6,11 @@ waits for every running decode to finish; its own trace attributes 97.8 % of
 TTFT at concurrency 8 to that wait, reference ``pic_runtime.py:2023-2026``,
 ``managers/scheduler.py:2597-2690``).  Here one loop thread alternates:
 
-1. admit: pop up to ``max_prefills_per_step`` queued requests and run each
-   prefill-type op (Compile prefill, Link = KV link + sparse repair, plain
-   prefill) -- a Link never waits for the running decodes to drain;
+1. admit: pop up to ``max_prefills_per_step`` queued requests; their
+   Compiles and Links run as ONE extend forward (every Link's KV link in one
+   fused launch per source pool, every repair row and Compile row in one
+   pass), plain prefills one by one -- a Link never waits for the running
+   decodes to drain;
 2. decode: one batched greedy step for every running sequence (CUDA graph per
    batch bucket on GPU), streaming each new token to its request.
 
@@ -62,7 +64,7 @@ class Request:
 
 class Scheduler:
     def __init__(self, engine: Engine, *, legolink_only: bool = True, max_running: int = 64,
-                 max_prefills_per_step: int = 4, max_context: Optional[int] = None, decode_chunk: int = 8):
+                 max_prefills_per_step: int = 8, max_context: Optional[int] = None, decode_chunk: int = 8):
         self.engine = engine
         self.legolink_only = legolink_only
         self.max_running = max_running
@@ -155,13 +157,20 @@ class Scheduler:
         return did
 
     def _admit_batch(self, batch: list) -> None:
-        """Compiles of one step share one extend forward; a Compile whose key
-        is already in the batch waits for the next one (where it takes the
-        registry's duplicate path).  Links and plain prefills run one by one.
-        Reference: ``pic_compile_key_in_batch`` ``pic_runtime.py:1954-1975``,
-        ``managers/scheduler.py:2611-2617``."""
-        compiles, keys = [], set()
+        """The Compiles and Links admitted in one step share ONE extend
+        forward (and the Links one fused KV-link launch per source pool); a
+        Compile whose key is already in the batch waits for the next one
+        (where it takes the registry's duplicate path).  Plain prefills run
+        one by one.  The reference admits a Link alone into an empty engine
+        (``managers/scheduler.py:2597-2690``; its trace attributes 97.8 % of
+        TTFT at concurrency 8 to that wait, ``pic_runtime.py:2023-2026``).
+        Compile race guard: ``pic_compile_key_in_batch``
+        ``pic_runtime.py:1954-1975``, ``managers/scheduler.py:2611-2617``."""
+        compiles, links, keys = [], [], set()
         for req in batch:
+            if req.kind == "link":
+                links.append(req)
+                continue
             if req.kind != "compile":
                 continue
             key = (req.sub_context or {}).get("cache_key")
@@ -172,28 +181,29 @@ class Scheduler:
             if key:
                 keys.add(str(key))
             compiles.append(req)
-        if compiles:
-            self._admit_compiles(compiles)
+        if compiles or links:
+            self._admit_extend(compiles, links)
         for req in batch:
-            if req.kind != "compile":
+            if req.kind == "plain":
                 self._admit(req)
 
-    def _admit_compiles(self, reqs: list) -> None:
+    def _admit_extend(self, compiles: list, links: list) -> None:
         items, live = [], []
-        for req in reqs:
+        for req in compiles:
             key = (req.sub_context or {}).get("cache_key")
             if not key:
                 req.events.put(("error", "sub_context.cache_key is required for a Compile"))
                 continue
             items.append((req.input_ids, str(key), req.sub_context or {}, None))
             live.append(req)
-        if not items:
-            return
+        link_items = [(r.pic_link, r.input_ids, r.rid, r.sampling) for r in links]
         try:
-            results = self.engine.compile_batch(items)
-        except Exception as e:  # the whole batch failed: each request fails alone
-            results = [e] * len(items)
-        for req, r in zip(live, results):
+            c_res, l_res = self.engine.extend_step(compiles=items, links=link_items)
+        except Exception as e:  # the whole step failed: each request fails alone
+            c_res, l_res = [e] * len(items), [e] * len(link_items)
+        if len(links) > 1:
+            self.stats["batched_links"] = self.stats.get("batched_links", 0) + len(links)
+        for req, r in zip(live, c_res):
             if isinstance(r, Exception):
                 emit_trace("legolink_request_failed_closed", rid=req.rid, kind="compile", reason=str(r)[:500])
                 req.events.put(("error", str(r)))
@@ -202,6 +212,31 @@ class Scheduler:
             req.events.put(("token", r["first_token"]))
             req.events.put(("done", {"compile": r, "finish_reason": "length"}))
             self.stats["finished"] += 1
+        for req, r in zip(links, l_res):
+            if isinstance(r, Exception):
+                emit_trace("legolink_request_failed_closed", rid=req.rid, kind="link", reason=str(r)[:500])
+                req.events.put(("error", str(r)))
+                continue
+            if r.length + req.max_new_tokens > self.max_context:
+                self.engine.free(r)
+                msg = "overlength Link (total tokens + max_tokens exceeds the context window)"
+                emit_trace("legolink_request_failed_closed", rid=req.rid, kind="link", reason=msg)
+                req.events.put(("error", msg))
+                continue
+            self._start(req, r)
+
+    def _start(self, req: Request, seq: Sequence_) -> None:
+        """A prefilled request emits its first token and joins the decode."""
+        req.seq = seq
+        if req.ttft_s is None:
+            req.ttft_s = time.perf_counter() - req.created
+        first = seq.output_ids[-1]
+        req.events.put(("token", first))
+        self.stats["admitted"] += 1
+        if len(seq.output_ids) >= req.max_new_tokens or first in req.stop_ids:
+            self._finish(req, "stop" if first in req.stop_ids else "length")
+        else:
+            self.running.append(req)
 
     def _admit(self, req: Request) -> None:
         eng = self.engine
@@ -227,16 +262,7 @@ class Scheduler:
                 seq.output_ids[:0] = req.resume
             else:
                 seq = eng.prefill(req.input_ids, rid=req.rid, sampling=req.sampling)
-            req.seq = seq
-            if req.ttft_s is None:
-                req.ttft_s = time.perf_counter() - req.created
-            first = seq.output_ids[-1]
-            req.events.put(("token", first))
-            self.stats["admitted"] += 1
-            if len(seq.output_ids) >= req.max_new_tokens or first in req.stop_ids:
-                self._finish(req, "stop" if first in req.stop_ids else "length")
-            else:
-                self.running.append(req)
+            self._start(req, seq)
         except (ContractError, RuntimeErrorAbort, RequestRejected, ValueError, KeyError) as e:
             emit_trace("legolink_request_failed_closed", rid=req.rid, kind=req.kind, reason=str(e)[:500])
             req.events.put(("error", str(e)))

@@ -31,6 +31,7 @@ from __future__ import annotations
 
 import http.client
 import json
+import faulthandler
 import os
 import signal
 import socket
@@ -337,9 +338,15 @@ def rank_main(a, rank: int, world: int, local: int, ready=None) -> None:
         srv.shutdown()
         sch.stop()
     finally:
+        # a shutdown that stalls prints every thread's stack after a minute
+        faulthandler.dump_traceback_later(60, repeat=False)
+        print(f"rank {rank}: shutting down", flush=True)
         eng.release_graphs()
         dist.barrier(group=ctrl)
+        print(f"rank {rank}: control barrier passed", flush=True)
         dist.destroy_process_group()
+        faulthandler.cancel_dump_traceback_later()
+        print(f"rank {rank}: stopped", flush=True)
 
 
 def _wait(stop) -> None:

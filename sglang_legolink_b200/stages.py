@@ -54,10 +54,10 @@ STAGES: tuple[Stage, ...] = (
     Stage(9, "Link contract", HOST, "contract.py", "validate_pic_link_request", ("host/framing.py:frame_link",)),
     Stage(10, "Adapter + residency recovery", HOST, "host/adapter.py", "RuntimeAdapter.link",
           ("host/adapter.py:ResidencyRecoveryCoordinator",)),
-    Stage(11, "Runtime admission", RUNTIME, "runtime/scheduler.py", "Scheduler._admit",
+    Stage(11, "Runtime admission", RUNTIME, "runtime/scheduler.py", "Scheduler._admit_batch",
           ("server/http_server.py:RuntimeService.build_request",)),
     Stage(12, "Link plan resolution", RUNTIME, "runtime/link_plan.py", "resolve_link_plan"),
-    Stage(13, "KV link + RoPE delta remap", RUNTIME, "runtime/engine.py", "Engine._run_link",
+    Stage(13, "KV link + RoPE delta remap", RUNTIME, "runtime/engine.py", "Engine._run_kv_links",
           ("ops/__init__.py:kv_link_rope",)),
     Stage(14, "Sparse boundary repair forward", RUNTIME, "models/qwen.py", "QwenModel.forward",
           ("ops/__init__.py:attention_prefill",)),
@@ -81,9 +81,9 @@ CALL_EDGES: tuple[CallEdge, ...] = (
     CallEdge(6, 7, "host/adapter.py", "RequestPipeline.execute", "build_layout"),
     CallEdge(7, 10, "host/adapter.py", "RequestPipeline.execute", "link"),
     CallEdge(10, 11, "server/http_server.py", "RuntimeService.complete", "build_request"),
-    CallEdge(11, 12, "runtime/engine.py", "Engine.link", "resolve_link_plan"),
-    CallEdge(12, 13, "runtime/engine.py", "Engine.link", "_run_link"),
-    CallEdge(13, 14, "runtime/engine.py", "Engine._run_link", "forward"),
+    CallEdge(11, 12, "runtime/engine.py", "Engine._link_prepare", "resolve_link_plan"),
+    CallEdge(12, 13, "runtime/engine.py", "Engine.extend_step", "_run_kv_links"),
+    CallEdge(13, 14, "runtime/engine.py", "Engine.extend_step", "forward"),
     CallEdge(13, 16, "ops/__init__.py", "kv_link_rope", "kv_link_rope"),
     CallEdge(14, 17, "ops/__init__.py", "attention_prefill", "attn_prefill_tc"),
     CallEdge(15, 18, "ops/__init__.py", "attention_decode", "attn_decode"),

@@ -88,8 +88,8 @@ def test_gemv_rownorm_and_residual_epilogues(M):
     x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
     w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
     bias = torch.randn(N, device=DEV, dtype=torch.bfloat16)
-    sumsq = torch.rand(M, device=DEV) * K * 3 + 1.0
-    rstd = torch.rsqrt(sumsq / K + eps)[:, None]
+    sumsq = ops.sumsq_from_values(torch.rand(M, device=DEV) * K * 3 + 1.0)  # int64 fixed point on CUDA
+    rstd = torch.rsqrt(ops.sumsq_values(sumsq) / K + eps)[:, None]
     out = ops.gemv_rownorm(x, w, bias, sumsq, eps)
     assert _rel(out, (x.float() @ w.float().t()) * rstd + bias.float()) < 1e-2
     gate, up = w[: N // 2], torch.randn(N // 2, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
@@ -100,13 +100,19 @@ def test_gemv_rownorm_and_residual_epilogues(M):
     res0 = res.clone()
     nw = torch.rand(N, device=DEV, dtype=torch.bfloat16) + 0.5
     h = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
-    sq = torch.zeros(M, device=DEV)
+    sq = ops.sumsq_buffer(M, DEV)
     ops.gemv_residual(x, w, res, nw, h, sq)
     torch.cuda.synchronize()
     assert ops.check_errors(DEV) == 0
     r = (x.float() @ w.float().t()).to(torch.bfloat16).float() + res0.float()
     assert _rel(res, r) < 1e-2 and _rel(h, r * nw.float()) < 1e-2
-    assert _rel(sq, (r * r).sum(-1)) < 1e-3
+    assert _rel(ops.sumsq_values(sq), (r * r).sum(-1)) < 1e-3
+    # the fixed-point sums are bit-identical however the tiles finish
+    for _ in range(3):
+        res.copy_(res0)
+        sq2 = ops.sumsq_buffer(M, DEV)
+        ops.gemv_residual(x, w, res, nw, h, sq2)
+        assert torch.equal(sq2, sq)
 
 
 @pytest.mark.parametrize("qk_norm,M", [(False, 3), (True, 3), (True, 37)])

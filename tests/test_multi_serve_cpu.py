@@ -185,3 +185,33 @@ def test_parallel_flags_are_checked():
     for tp, dp, pp in ((1, 1, 2), (2, 2, 1), (0, 1, 1)):
         with pytest.raises(ContractError):
             check_parallel_args(tp, dp, pp)
+
+
+def test_dp2_server_serves_and_shuts_down_cleanly():
+    """Two gloo ranks as DP replicas behind rank 0's router: Compile + Link
+    through the router, then an orderly shutdown of both ranks."""
+    ctx = mp.get_context("spawn")
+    q, stop = ctx.Queue(), ctx.Event()
+    a = argparse.Namespace(model="tiny-qwen2", device="cpu", tokenizer=None, host="127.0.0.1", port=_free_port(),
+                           page_size=16, context_length=4096, allow_plain_generation=False, skip_warmup=True,
+                           tp_size=1, dp_size=2, pp_size=1, tp_comm="nccl", dp_base_port=_free_port(),
+                           dist_timeout=120, seed=0, stop_event=stop)
+    dport = _free_port()
+    procs = [ctx.Process(target=_tp_rank, args=(r, 2, dport, a, q)) for r in range(2)]
+    [p.start() for p in procs]
+    try:
+        port = q.get(timeout=300)
+        base = f"http://127.0.0.1:{port}"
+        code, r = _post(base, {"messages": _msgs("tool output " * 60), "max_tokens": 1,
+                               "sub_context": {"cache_key": "dp-a"}})
+        assert code == 200, r
+        code, r = _post(base, {"messages": _msgs("next?"), "max_tokens": 4, "ignore_eos": True,
+                               "pic_link": {"cache_keys": ["dp-a"], "recompute_initial_tokens": 8}})
+        assert code == 200 and len(r["meta_info"]["output_ids"]) == 4, r
+    finally:
+        stop.set()
+        [p.join(timeout=120) for p in procs]
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]

@@ -162,13 +162,13 @@ def test_scheduler_batches_compiles_and_defers_same_key(world, monkeypatch):
     a = torch.randint(0, 1024, (96,), generator=g).tolist()
     b = torch.randint(0, 1024, (40,), generator=g).tolist()
     calls = []
-    orig = eng.compile_batch
+    orig = eng.extend_step
 
-    def spy(items):
-        calls.append([str(it[1]) for it in items])
-        return orig(items)
+    def spy(compiles=(), links=(), timer=None):
+        calls.append([str(it[1]) for it in compiles])
+        return orig(compiles=compiles, links=links, timer=timer)
 
-    monkeypatch.setattr(eng, "compile_batch", spy)
+    monkeypatch.setattr(eng, "extend_step", spy)
     sch = Scheduler(eng, max_prefills_per_step=4)
     reqs = [Request("compile", f"c{i}", toks, 1, sub_context={"cache_key": key})
             for i, (key, toks) in enumerate([("sched-a", a), ("sched-a", a), ("sched-b", b)])]

@@ -65,6 +65,28 @@ def test_no_alloc_matches_regular_entry_point_twice(M, N, K):
         assert _rel(got, a.float() @ w.float().t() + bias.float()) < 1e-2, call
 
 
+def test_warm_call_takes_no_device_memory():
+    """After the one-time set-up call on a device, a call leaves the
+    device's free memory unchanged (cudaMemGetInfo before and after)."""
+    fn, msg = _lib()
+    M, N, K = 16, 3584, 18944
+    torch.manual_seed(3)
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) / math.sqrt(K)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert _call(fn, a, w, None, out, err) == 0  # set-up call
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        rc = _call(fn, a, w, None, out, err)
+        assert rc == 0, msg(rc).decode()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert int(err.item()) == 0
+
+
 def test_no_alloc_rejects_problems_beyond_its_scratch():
     fn, msg = _lib()
     M, N, K = 128, 3584, 18944  # split-K partials far above the static scratch
