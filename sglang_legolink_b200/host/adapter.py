@@ -352,6 +352,9 @@ class PipelineExecution:
             d = self.plan.to_dict()
             row["block_planning"] = d["block_planning"]
             row["reuse_accounting"] = d["reuse_accounting"]
+            row.update(self.plan.namespace_config)
+            rec = (self.result.recovery or {}).get("recovered_cache_keys", [])
+            row["namespace"] = self.plan.namespace_summary(recovered_cache_keys=rec)
         if self.layout is not None:
             row["framing"] = self.layout.diagnostics()
         return row
@@ -375,7 +378,7 @@ class RequestPipeline:
         t = time.perf_counter()
         manifest = self.manager.select(query)
         contexts = self.manager.contexts()
-        plan = self.planner.plan(manifest, contexts, namespace=self.namespace)
+        plan = self.planner.plan(manifest, contexts)
         tm["plan"] = (time.perf_counter() - t) * 1e3
         if route == PipelineRoute.FULL_CONTEXT_ORIGINAL or route == PipelineRoute.SELECTED_CONTEXT_ORIGINAL:
             text = self.stitcher.baseline_text(plan)
@@ -391,9 +394,11 @@ class RequestPipeline:
         tm["frame"] = (time.perf_counter() - t) * 1e3
         t = time.perf_counter()
         nc, cdt = self.adapter.compile_plan(layout)
+        self.planner.after_compile(plan)
         tm["compile"] = (time.perf_counter() - t) * 1e3
         t = time.perf_counter()
         res = self.adapter.link(stitched, layout, task_id=self.manager.task_id)
+        self.planner.after_link(plan)
         tm["link"] = (time.perf_counter() - t) * 1e3
         return PipelineExecution(route, res, plan, stitched, layout, nc + res.compile_requests,
                                  cdt + res.compile_latency_s, tm)

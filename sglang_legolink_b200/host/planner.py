@@ -37,60 +37,11 @@ NO_EXPECTED_REUSE = "no expected future reuse"
 
 
 # ---------------------------------------------------------------- namespaces
-class NamespaceMode(str, Enum):
-    GLOBAL = "global"
-    HARD = "hard_namespace"
-    LOGICAL = "logical_namespace"
-
-
-def physical_kv_identity(v: SubContext) -> str:
-    """The compiled KV a sub-context denotes (content + compatibility)."""
-    return v.cache_key
-
-
-class SemanticCacheIndex:
-    """Logical namespace index: (namespace, semantic identity) -> physical key,
-    with aliases; removing a physical key invalidates every alias to it."""
-
-    def __init__(self):
-        self._alias: dict[tuple[str, str], str] = {}
-        self._lock = threading.Lock()
-
-    def lookup(self, namespace: str, identity: str) -> Optional[str]:
-        return self._alias.get((namespace, identity))
-
-    def record_alias(self, namespace: str, identity: str, physical_key: str) -> None:
-        with self._lock:
-            self._alias[(namespace, identity)] = physical_key
-
-    def on_physical_removed(self, physical_key: str) -> int:
-        with self._lock:
-            dead = [k for k, v in self._alias.items() if v == physical_key]
-            for k in dead:
-                del self._alias[k]
-            return len(dead)
-
-    def snapshot(self) -> dict:
-        return {f"{ns}|{ident}": key for (ns, ident), key in self._alias.items()}
-
-
-class NamespaceResolver:
-    def __init__(self, mode: NamespaceMode = NamespaceMode.LOGICAL, index: Optional[SemanticCacheIndex] = None):
-        self.mode = NamespaceMode(mode)
-        self.index = index or SemanticCacheIndex()
-
-    def resolve(self, v: SubContext, namespace: str) -> SubContext:
-        if self.mode == NamespaceMode.GLOBAL:
-            return v
-        if self.mode == NamespaceMode.HARD:
-            key = hashlib.sha256(f"{namespace}\0{v.cache_key}".encode()).hexdigest()
-            return replace(v, cache_key=key)
-        phys = self.index.lookup(namespace, v.semantic_identity) or physical_kv_identity(v)
-        return replace(v, cache_key=phys)
-
-    def record(self, v: SubContext, namespace: str) -> None:
-        if self.mode == NamespaceMode.LOGICAL:
-            self.index.record_alias(namespace, v.semantic_identity, v.cache_key)
+# The namespace taxonomy, logical roots and the resolver live in
+# ``host/namespaces.py``; the planner applies them first (stage 1 above).
+from .namespaces import (CacheNamespace, LogicalRootIndex, NamespaceLookup, NamespaceMode,  # noqa: E402,F401
+                         NamespacePolicy, NamespaceResolver, index_of, physical_kv_identity,
+                         summarize_namespace_request)
 
 
 # ------------------------------------------------------------------ catalog
@@ -103,6 +54,7 @@ class CacheCatalog:
         self._entries: dict[str, dict] = {}
         self._locks: dict[str, threading.Lock] = {}
         self._guard = threading.Lock()
+        self.logical_index = LogicalRootIndex()  # names per namespace root over the compiled blocks
 
     def lock(self, key: str) -> threading.Lock:
         with self._guard:
@@ -118,6 +70,7 @@ class CacheCatalog:
     def invalidate(self, key: str) -> None:
         if key in self._entries:
             self._entries[key]["stale"] = True
+        self.logical_index.drop_physical(key)  # its primary name and every alias miss from now on
 
     def entries(self) -> dict:
         return dict(self._entries)
@@ -361,6 +314,8 @@ class ExecutionPlan:
     records: tuple
     accounting: ReuseAccounting
     text_separator: str = "\n\n"
+    namespace_lookups: tuple = ()
+    namespace_config: dict = field(default_factory=dict)
 
     @property
     def expected_cache_keys(self) -> tuple:
@@ -378,7 +333,15 @@ class ExecutionPlan:
                 "compile_on_miss": [v.sub_context_id for v in self.compile_on_miss_contexts],
                 "mutable": [v.sub_context_id for v in self.mutable_contexts],
                 "omitted": [v.sub_context_id for v in self.omitted_contexts],
-                "block_planning": [r.to_dict() for r in self.records], "reuse_accounting": self.accounting.to_dict()}
+                "block_planning": [r.to_dict() for r in self.records], "reuse_accounting": self.accounting.to_dict(),
+                "namespace_lookups": [r.to_dict() for r in self.namespace_lookups],
+                "namespace_config": dict(self.namespace_config)}
+
+    def namespace_summary(self, recovered_cache_keys=(), repair_tokens_by_cache_key=None) -> dict:
+        return summarize_namespace_request(
+            self.namespace_lookups, linked_block_ids=[v.sub_context_id for v in self.linked_contexts],
+            link_cache_key_by_block={v.sub_context_id: v.cache_key for v in self.linked_contexts},
+            repair_tokens_by_cache_key=repair_tokens_by_cache_key, recovered_cache_keys=recovered_cache_keys)
 
 
 class Planner:
@@ -394,20 +357,26 @@ class Planner:
         self.repair_window = repair_window
         self.separator = separator
 
-    def plan(self, manifest: AgentContextManifest, contexts: Iterable[SubContext], *, namespace: str = "default",
-             policy_context: PolicyContext = PolicyContext()) -> ExecutionPlan:
+    def plan(self, manifest: AgentContextManifest, contexts: Iterable[SubContext], *,
+             policy_context: PolicyContext = PolicyContext(), namespace: Optional[str] = None) -> ExecutionPlan:
+        """``namespace`` is accepted for older callers and ignored: a block's
+        namespace follows from its field (``host/namespaces.py``)."""
         by_id = {v.sub_context_id: v for v in contexts}
-        ordered = [self.resolver.resolve(by_id[i], namespace) for i in manifest.selected_sub_context_ids
-                   if i in by_id]
-        decisions = {}
-        for v in ordered:
-            ctx = replace(policy_context, cache_present=self.catalog.is_compiled(v.cache_key))
-            decisions[v.sub_context_id] = self.policy.decide(v, ctx)
+        selected = [by_id[i] for i in manifest.selected_sub_context_ids if i in by_id]
+        ordered, lookups = self.resolver.apply(selected, self.catalog)
+        provisional = []
+        for v, r in zip(ordered, lookups):
+            ctx = replace(policy_context, cache_present=r.resident or self.catalog.is_compiled(v.cache_key))
+            provisional.append(self.policy.decide(v, ctx))
+        decisions = dict(zip((v.sub_context_id for v in ordered),
+                             self.resolver.enforce_persistence(lookups, provisional)))
+        perms = self.resolver.layout_permissions(lookups)
+        may_link = {v.sub_context_id: (True if perms is None else perms[i]) for i, v in enumerate(ordered)}
         included = [v for v in ordered if decisions[v.sub_context_id].action != CompileAction.DO_NOT_INCLUDE]
         omitted = [v for v in ordered if decisions[v.sub_context_id].action == CompileAction.DO_NOT_INCLUDE]
         link_ok = {v.sub_context_id: self.eligibility.gate(v, decisions[v.sub_context_id])[0] for v in included}
-        promotable = {v.sub_context_id: (not v.is_mutable and v.reuse_candidate and not v.invalidated)
-                      for v in included}
+        promotable = {v.sub_context_id: (not v.is_mutable and v.reuse_candidate and not v.invalidated
+                                         and may_link[v.sub_context_id]) for v in included}
         eff, adj = self.feasibility.apply(included, link_ok, promotable)
         adj_of = {a.sub_context_id: a.adjustment for a in adj}
         linked = [v for v in included if eff.get(v.sub_context_id)]
@@ -426,8 +395,6 @@ class Planner:
             records.append(BlockPlanningRecord(v.sub_context_id, v.semantic_identity, v.cache_key, v.token_count,
                                                d.action.value, adj_of.get(v.sub_context_id, "none"), ea, cat,
                                                d.reason))
-        for v in linked:
-            self.resolver.record(v, namespace)
         reused = sum(v.token_count for v in linked if v not in com)
         compiled = sum(v.token_count for v in com)
         recompute = sum(v.token_count for v in mutable)
@@ -436,4 +403,28 @@ class Planner:
         verdict = "observe_only:" + ("profitable" if reused > repair else "not_profitable")
         acc = ReuseAccounting(reused, compiled, recompute, repair, total, verdict)
         return ExecutionPlan(manifest, tuple(included), tuple(linked), tuple(com), tuple(mutable), tuple(omitted),
-                             tuple(records), acc, self.separator)
+                             tuple(records), acc, self.separator, tuple(lookups), self.resolver.describe())
+
+    def after_compile(self, plan: ExecutionPlan) -> int:
+        """The blocks a plan's Compiles made resident become primary names in
+        their roots."""
+        keys = [v.cache_key for v in plan.linked_contexts if self.catalog.is_compiled(v.cache_key)]
+        idx = index_of(self.catalog)
+        fresh = [k for v, k in zip(plan.linked_contexts, keys)
+                 if idx.lookup(self._root_of(plan, v), k) is None]
+        by_id = {r.sub_context_id: r for r in plan.namespace_lookups}
+        views = [v for v in plan.linked_contexts if v.sub_context_id in by_id]
+        return self.resolver.register_compiled(views, [by_id[v.sub_context_id] for v in views], self.catalog, fresh)
+
+    @staticmethod
+    def _root_of(plan: ExecutionPlan, v) -> str:
+        owner = (v.metadata or {}).get("physical_entry") or {}
+        for r in plan.namespace_lookups:
+            if r.sub_context_id == v.sub_context_id:
+                return owner.get("namespace") or r.logical_root or r.namespace
+        return ""
+
+    def after_link(self, plan: ExecutionPlan) -> int:
+        """A successful Link: record the names it served through other blocks."""
+        return self.resolver.record_aliases(plan.namespace_lookups, self.catalog,
+                                            linked_block_ids=[v.sub_context_id for v in plan.linked_contexts])

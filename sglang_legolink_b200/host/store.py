@@ -106,10 +106,16 @@ class SubContext:
                                  model_fingerprint=model_fingerprint, tokenizer_fingerprint=tokenizer.fingerprint,
                                  segmentation_policy_version=segmentation_policy_version,
                                  recompute_policy_version=recompute_policy_version)
+        md = dict(metadata or {})
+        # what the compiled KV depends on besides its tokens (physical KV identity)
+        md.setdefault("model_fingerprint", model_fingerprint)
+        md.setdefault("tokenizer_fingerprint", tokenizer.fingerprint)
+        md.setdefault("segmentation_policy_version", segmentation_policy_version)
+        md.setdefault("recompute_policy_version", recompute_policy_version)
         return cls(semantic_block_id(task_id=task_id, context_field=context_field, source_spans=spans), task_id,
                    context_field, source_id, tuple(spans), raw_text, len(toks),
                    getattr(tokenizer, "token_unit", "estimated"), ident, key, sequence_number, source_revision,
-                   is_mutable, True, False, ids, dict(metadata or {}))
+                   is_mutable, True, False, ids, md)
 
 
 class SubContextStore:
