@@ -138,6 +138,12 @@ class CompileAction(str, Enum):
     COMPILE = "compile"
     KEEP_MUTABLE = "keep_mutable"
     DO_NOT_INCLUDE = "do_not_include"
+    SUMMARIZE_THEN_COMPILE = "summarize_then_compile"
+
+
+# actions that place the block's state through a Link (Gate 1 input)
+LINK_ACTIONS = frozenset({CompileAction.COMPILE, CompileAction.SUMMARIZE_THEN_COMPILE})
+SUMMARIZE_EXEMPT_FIELDS = frozenset({"workspace_evidence", "tool_definitions"})  # verbatim by nature
 
 
 @dataclass(frozen=True)
@@ -148,6 +154,15 @@ class CompileDecision:
     reason: str
     token_count: int = 0
     policy: str = "legacy_fixed_64"
+    # why: policy + version, and for an economic decision the profile id,
+    # hardware, model, compatibility verdict and the full cost breakdown
+    provenance: dict = field(default_factory=dict)
+    cost: Optional[dict] = None
+
+    def to_dict(self) -> dict:
+        d = dict(self.__dict__)
+        d["action"] = self.action.value
+        return d
 
 
 @dataclass(frozen=True)
@@ -157,17 +172,22 @@ class PolicyContext:
     cache_present: bool = False
     min_compile_model_tokens: int = 64
     summarize_threshold_tokens: int = 8192
+    preceding_model_tokens: int = 0
+    planned_repair_model_tokens: Optional[int] = None
+    repair_window_source: str = "unspecified"
 
 
 class CompilePolicy:
     """Legacy fixed floor: compile an immutable reuse candidate iff it has at
-    least ``min_compile_model_tokens`` tokens (reference
-    ``compile_policy.py:234-350``)."""
+    least ``min_compile_model_tokens`` tokens; a very large compressible block
+    (``summarize_threshold_tokens``, not workspace evidence or tool schemas)
+    is summarized first (reference ``compile_policy.py:234-350``)."""
 
     name = "legacy_fixed_64"
+    version = LEGACY_COMPILE_POLICY_VERSION
 
     def decide(self, v: SubContext, ctx: PolicyContext = PolicyContext()) -> CompileDecision:
-        D = lambda a, r, n=0: CompileDecision(v.sub_context_id, v.cache_key, a, r, n, self.name)  # noqa: E731
+        D = self._maker(v)
         if v.invalidated:
             return D(CompileAction.DO_NOT_INCLUDE, "invalidated version")
         if v.is_mutable:
@@ -178,6 +198,11 @@ class CompilePolicy:
             return D(CompileAction.COMPILE, "already compiled; reuse catalog entry", v.token_count)
         return self._decide(v, ctx, D)
 
+    def _maker(self, v: SubContext, **extra):
+        prov = {"compile_policy": self.name, "compile_policy_version": self.version, **extra.pop("provenance", {})}
+        return lambda a, r, n=0, **kw: CompileDecision(v.sub_context_id, v.cache_key, a, r, n, self.name,
+                                                       {**prov, **kw.pop("provenance", {})}, kw.get("cost"))
+
     def _decide(self, v, ctx, D):
         if v.token_count < ctx.min_compile_model_tokens:
             return D(CompileAction.KEEP_MUTABLE, BELOW_COMPILE_FLOOR)
@@ -185,41 +210,130 @@ class CompilePolicy:
             return D(CompileAction.KEEP_MUTABLE, NO_EXPECTED_REUSE)
         if ctx.memory_pressure >= 0.9:
             return D(CompileAction.KEEP_MUTABLE, "high KV memory pressure")
-        return D(CompileAction.COMPILE, "immutable reuse candidate above the floor", v.token_count)
+        if v.token_count >= ctx.summarize_threshold_tokens and v.context_field not in SUMMARIZE_EXEMPT_FIELDS:
+            return D(CompileAction.SUMMARIZE_THEN_COMPILE, "large compressible stable context")
+        return D(CompileAction.COMPILE, "immutable reuse candidate above the floor",
+                 v.token_count * ctx.expected_future_reuse)
 
 
 class CompileAllImmutablePolicy(CompilePolicy):
     name = "compile_all_immutable"
+    version = "compile-all-immutable-v1"
 
     def _decide(self, v, ctx, D):
         return D(CompileAction.COMPILE, "ablation: every immutable block", v.token_count)
 
 
 class CostBenefitCompilePolicy(CompilePolicy):
-    """Compile when expected reuse savings exceed the one-time Compile cost.
-    ``profile`` holds measured per-token costs (ms): prefill, link, repair."""
+    """Compile iff the expected reuse savings exceed the Compile cost, from a
+    measured :class:`~.compile_cost.CompileCostProfile` of this deployment
+    and a :class:`~.compile_cost.ReuseExpectation` (required: assuming one
+    reuse is exactly the hidden guess this policy replaces).  The eligibility
+    checks before the floor are the legacy policy's; the floor itself is
+    replaced by the arithmetic.  Without a usable profile there is no
+    decision -- unless the caller named ``fallback="legacy_fixed_64"``, which
+    every decision it produces records.  Memory pressure >= 0.9 stays a hard
+    stop (residency cost is unmeasured, see ``DisabledResidencyCost``).
+    Reference: ``compile_policy.py:386-560``."""
 
     name = "cost_benefit"
+    memory_pressure_stop = 0.9
 
-    def __init__(self, profile: Optional[dict] = None, repair_window: int = 16):
-        self.profile = profile or {"prefill_ms_per_token": 0.02, "link_ms_per_token": 0.001,
-                                   "repair_ms_per_token": 0.02}
-        self.repair_window = repair_window
+    def __init__(self, *, reuse_expectation=None, profile=None, residency_cost_model=None, deployment=None,
+                 strict_profile_compatibility: bool = True, fallback: Optional[str] = None):
+        from . import compile_cost as cc
+
+        if reuse_expectation is None:
+            raise cc.CompileCostError("a cost-benefit policy needs a ReuseExpectation; there is no safe default")
+        if fallback not in (None, "legacy_fixed_64"):
+            raise cc.CompileCostError("the only supported fallback is legacy_fixed_64")
+        self.version = cc.COMPILE_COST_POLICY_VERSION
+        self.reuse = reuse_expectation
+        self.profile = profile
+        self.residency = residency_cost_model or cc.DisabledResidencyCost()
+        self.deployment = deployment
+        self.strict = strict_profile_compatibility
+        self.fallback = fallback
+        self._legacy = CompilePolicy()
 
     def _decide(self, v, ctx, D):
-        p = self.profile
-        n = v.token_count
-        saved_per_use = n * p["prefill_ms_per_token"] - (n * p["link_ms_per_token"]
-                                                          + min(n, self.repair_window) * p["repair_ms_per_token"])
-        cost = n * p["prefill_ms_per_token"]
-        if saved_per_use <= 0 or saved_per_use * max(0, ctx.expected_future_reuse) < cost:
-            return D(CompileAction.KEEP_MUTABLE, "expected savings below compile cost")
-        return D(CompileAction.COMPILE, "expected savings exceed compile cost", n)
+        from . import compile_cost as cc
+
+        if ctx.memory_pressure >= self.memory_pressure_stop:
+            return D(CompileAction.KEEP_MUTABLE, "high KV memory pressure")
+        try:
+            if self.profile is None:
+                raise cc.CompileCostUnavailable("no CompileCostProfile was supplied")
+            compat = self.profile.check_compatibility(self.deployment, strict=self.strict)
+            cand = cc.CompileCandidate(v.sub_context_id, v.cache_key, v.context_field, v.token_count,
+                                       not v.is_mutable, v.reuse_candidate, v.invalidated,
+                                       ctx.preceding_model_tokens, ctx.planned_repair_model_tokens,
+                                       ctx.repair_window_source, ctx.cache_present)
+            b = cc.evaluate_compile_economics(cand, profile=self.profile, reuse=self.reuse, residency=self.residency,
+                                              planned_future_reuse=ctx.expected_future_reuse,
+                                              memory_pressure=ctx.memory_pressure)
+        except cc.CompileCostUnavailable as e:
+            if self.fallback is None:
+                raise
+            d = self._legacy.decide(v, ctx)
+            return replace(d, policy=self.name, provenance={**d.provenance, "compile_policy": self.name,
+                                                            "fallback_policy": self.fallback,
+                                                            "fallback_reason": str(e)})
+        prov = {"profile_id": self.profile.profile_id, "profile_hardware": self.profile.provenance.hardware_id,
+                "profile_model": self.profile.provenance.model_id, "profile_compatibility": compat,
+                "reuse_expectation": self.reuse.name}
+        if not b.is_profitable:
+            return D(CompileAction.KEEP_MUTABLE, "expected reuse savings do not exceed the compile cost",
+                     provenance=prov, cost=b.to_dict())
+        return D(CompileAction.COMPILE, "expected reuse savings exceed the compile cost", v.token_count,
+                 provenance=prov, cost=b.to_dict())
 
 
 def build_compile_policy(mode: str = "legacy_fixed_64", **kw) -> CompilePolicy:
     return {"legacy_fixed_64": CompilePolicy, "compile_all_immutable": CompileAllImmutablePolicy,
             "cost_benefit": CostBenefitCompilePolicy}[mode](**kw)
+
+
+class ContextSummarizer:
+    """Turns a SUMMARIZE_THEN_COMPILE block into a derived summary block
+    (same field and spans, ``derived_from`` provenance, its own identity and
+    cache key) through a caller's ``summarize(text, target_tokens)``.  The
+    original is kept when there is no summarizer, when the text must stay
+    verbatim (code fences, JSON, tracebacks, shell prompts, error lines), or
+    when the summary does not reduce the token count.  Counting uses the
+    same tokenizer as the original.  Reference: ``pruning.py:22-80``."""
+
+    VERBATIM = __import__("re").compile(r"```|\{\s*[\"']|Traceback|(?:^|\n)\s*[$>]\s|(?:error|exception):",
+                                        __import__("re").IGNORECASE)
+
+    def __init__(self, summarize=None, *, tokenizer=None, target_ratio: float = 0.25):
+        self.summarize, self.tokenizer, self.target_ratio = summarize, tokenizer, target_ratio
+
+    def apply(self, v: SubContext) -> tuple[SubContext, str]:
+        if self.summarize is None or self.tokenizer is None:
+            return v, "summarizer unavailable"
+        if self.VERBATIM.search(v.raw_text):
+            return v, "verbatim content"
+        target = max(1, int(v.token_count * self.target_ratio))
+        try:
+            text = str(self.summarize(v.raw_text, target) or "").strip()
+        except Exception as e:  # noqa: BLE001 - a failed summary keeps the original
+            return v, f"summarizer failed: {e}"[:200]
+        n = self.tokenizer.count(text) if hasattr(self.tokenizer, "count") else len(self.tokenizer.tokenize(text))
+        if not text or n >= v.token_count:
+            return v, "summary did not reduce the context"
+        md = dict(v.metadata or {})
+        derived = SubContext.create(task_id=v.task_id, context_field=v.context_field, source_id=v.source_id,
+                                    spans=list(v.source_spans), raw_text=text, tokenizer=self.tokenizer,
+                                    sequence_number=v.sequence_number, source_revision=v.source_revision,
+                                    model_fingerprint=md.get("model_fingerprint", "runtime-local"),
+                                    segmentation_policy_version=str(md.get("segmentation_policy_version",
+                                                                           "field-first-v1")) + "+summary-v1",
+                                    capture_token_ids=bool(v.token_ids),
+                                    metadata={**md, "derived_from": [v.sub_context_id],
+                                              "semantic_independence_reason":
+                                                  "derived compression of a source-backed block"})
+        return derived, "summarized"
 
 
 # --------------------------------------------------------------------- gates
@@ -230,7 +344,7 @@ class ReuseEligibility:
         self.allow_foreign = allow_foreign
 
     def gate(self, v: SubContext, decision: CompileDecision) -> tuple[bool, str]:
-        if decision.action != CompileAction.COMPILE:
+        if decision.action not in LINK_ACTIONS:
             return False, "not compiled"
         if v.metadata.get("foreign_state") and not self.allow_foreign:
             return False, "foreign state (experimental) is off"
@@ -348,7 +462,8 @@ class Planner:
     def __init__(self, policy: Optional[CompilePolicy] = None, catalog: Optional[CacheCatalog] = None,
                  resolver: Optional[NamespaceResolver] = None, eligibility: Optional[ReuseEligibility] = None,
                  feasibility: Optional[LinkLayoutFeasibility] = None, repair_window: int = 16,
-                 separator: str = "\n\n"):
+                 separator: str = "\n\n", summarizer: Optional[ContextSummarizer] = None):
+        self.summarizer = summarizer or ContextSummarizer()
         self.policy = policy or CompilePolicy()
         self.catalog = catalog or CacheCatalog()
         self.resolver = resolver or NamespaceResolver()
@@ -364,12 +479,25 @@ class Planner:
         by_id = {v.sub_context_id: v for v in contexts}
         selected = [by_id[i] for i in manifest.selected_sub_context_ids if i in by_id]
         ordered, lookups = self.resolver.apply(selected, self.catalog)
+        ordered = list(ordered)
         provisional = []
         for v, r in zip(ordered, lookups):
             ctx = replace(policy_context, cache_present=r.resident or self.catalog.is_compiled(v.cache_key))
             provisional.append(self.policy.decide(v, ctx))
         decisions = dict(zip((v.sub_context_id for v in ordered),
                              self.resolver.enforce_persistence(lookups, provisional)))
+        # SUMMARIZE_THEN_COMPILE: the derived summary block takes the place
+        # of the original (same position, id kept so the manifest still names it)
+        for i, v in enumerate(ordered):
+            d = decisions[v.sub_context_id]
+            if d.action is not CompileAction.SUMMARIZE_THEN_COMPILE:
+                continue
+            derived, why = self.summarizer.apply(v)
+            if derived is not v:
+                ordered[i] = replace(derived, sub_context_id=v.sub_context_id)
+            decisions[v.sub_context_id] = replace(d, cache_key=ordered[i].cache_key,
+                                                  token_count=ordered[i].token_count,
+                                                  provenance={**d.provenance, "summary": why})
         perms = self.resolver.layout_permissions(lookups)
         may_link = {v.sub_context_id: (True if perms is None else perms[i]) for i, v in enumerate(ordered)}
         included = [v for v in ordered if decisions[v.sub_context_id].action != CompileAction.DO_NOT_INCLUDE]
