@@ -117,6 +117,51 @@ class DeterministicSegmenter:
 
 
 @dataclass(frozen=True)
+class FrozenSourcePrefix:
+    """The finalized leading blocks of a source's stored revision, whose
+    boundaries must not move when the source grows.
+
+    When the new revision of a source starts with exactly the text these
+    blocks cover (it was appended to, not edited), they are replayed as they
+    were stored -- same spans, same text, hence the same identity, id and
+    cache key -- and only the appended remainder is segmented.  A later
+    segmentation (possibly a model, nondeterministic across a context change)
+    therefore never re-cuts a block a Link may already depend on.  Blocks are
+    frozen from offset 0 while each is a reuse candidate, not invalidated,
+    owns exactly one span of this source and starts where the previous one
+    ended.  Reference: ``segmentation_validation.py:316-395``,
+    ``manager.py:309-341``."""
+
+    source_id: str
+    end: int
+    text: str
+    spans: tuple  # (start, end) of each frozen block, in order
+
+    @classmethod
+    def from_blocks(cls, source_id: str, blocks: Sequence[SubContext]) -> Optional["FrozenSourcePrefix"]:
+        owned = []
+        for b in blocks:
+            spans = list(b.source_spans)
+            if len(spans) != 1 or spans[0].source_id != source_id:
+                return None
+            owned.append((spans[0].start, spans[0].end, b))
+        owned.sort(key=lambda t: (t[0], t[1], t[2].sub_context_id))
+        cur, spans, text = 0, [], []
+        for start, end, b in owned:
+            if start != cur or b.invalidated or not b.reuse_candidate or b.context_field == "user_prompt":
+                break
+            spans.append((start, end))
+            text.append(b.raw_text)
+            cur = end
+        if not spans:
+            return None
+        return cls(source_id, cur, "".join(text), tuple(spans))
+
+    def applies_to(self, new_text: str) -> bool:
+        return len(new_text) > self.end and new_text.startswith(self.text)
+
+
+@dataclass(frozen=True)
 class AgentContextManifest:
     task_id: str
     session_revision: int
@@ -144,7 +189,7 @@ class ContextManager:
     def __init__(self, task_id: str, *, tokenizer=None, store: Optional[SubContextStore] = None,
                  segmenter: Optional[DeterministicSegmenter] = None, model_fingerprint: str = "runtime-local",
                  recompute_policy_version: str = DEFAULT_RECOMPUTE_POLICY_VERSION, classifier=None,
-                 capture_token_ids: bool = False, selector=None):
+                 capture_token_ids: bool = False, selector=None, boundary_locking: bool = True):
         self.task_id = task_id
         self.tokenizer = tokenizer or RegexTokenizer()
         self.collector = EventCollector(task_id)
@@ -156,6 +201,8 @@ class ContextManager:
         self.capture_token_ids = capture_token_ids
         self.selector = selector  # host.selection selector; None = keep every active sub-context
         self._stored_revision: dict[str, str] = {}
+        self.boundary_locking = boundary_locking
+        self.frozen_log: list[dict] = []  # one record per source revision segmented after a frozen prefix
 
     def ingest(self, values: Iterable[tuple], *, fail_after_extract: bool = False) -> list[SessionEvent]:
         cp = self.collector.checkpoint()
@@ -175,7 +222,7 @@ class ContextManager:
         for src in sources:
             if self._stored_revision.get(src.source_id) == src.event_id:
                 continue
-            segs = self.segmenter.segment(src)
+            segs = self._segment_with_frozen_prefix(src)
             values = []
             for i, sg in enumerate(segs):
                 span = SourceSpan(src.source_id, sg.start, sg.end, src.source_path)
@@ -192,6 +239,25 @@ class ContextManager:
             for src in sources:
                 if src.source_id in changed:
                     self._stored_revision[src.source_id] = src.event_id
+
+    def _segment_with_frozen_prefix(self, src: ExtractedSource) -> list:
+        """Segments of ``src``; a source that only grew keeps its stored
+        finalized leading blocks (:class:`FrozenSourcePrefix`)."""
+        prefix = None
+        if self.boundary_locking and src.source_id in self._stored_revision:
+            prev = [v for v in self.store.all(self.task_id) if v.source_id == src.source_id]
+            prefix = FrozenSourcePrefix.from_blocks(src.source_id, prev) if prev else None
+        if prefix is None or not prefix.applies_to(src.raw_text):
+            return self.segmenter.segment(src)
+        from dataclasses import replace as _replace
+
+        tail = self.segmenter.segment(_replace(src, raw_text=src.raw_text[prefix.end:]))
+        segs = [Segment(a, b) for a, b in prefix.spans] + [Segment(prefix.end + t.start, prefix.end + t.end)
+                                                            for t in tail]
+        validate_segments(src.raw_text, segs)
+        self.frozen_log.append({"source_id": src.source_id, "frozen_blocks": len(prefix.spans),
+                                "frozen_chars": prefix.end, "appended_chars": len(src.raw_text) - prefix.end})
+        return segs
 
     def contexts(self) -> list[SubContext]:
         ext = self.extractor.extract(self.collector.events())
