@@ -45,6 +45,81 @@ class RequestRejected(ValueError):
     pass
 
 
+COMPILE_STATE_ABSENT = "absent"
+COMPILE_STATE_COMPILING = "compiling"
+COMPILE_STATE_RESIDENT = "resident"
+
+
+class CompileStates:
+    """Per cache key: ``absent`` -> ``compiling`` (one or more admitted
+    Compiles not yet finished) -> ``resident`` (registered in the engine).
+
+    All in-flight Compiles of a key carry the same tokens and storage mode:
+    one that disagrees is refused at arrival instead of racing the first; one
+    that agrees is attached as its own record (duplicate work stays harmless:
+    the registry keeps the first block and releases the second).  A Compile
+    that ends without registering drops its record; a request that vanishes
+    without finishing (collected while queued) is dropped by a weak-reference
+    finalizer.  Nothing is written for a key before its Compile succeeds, so
+    a failure needs no rollback here.
+    Reference: ``pic_runtime.py:2270-2361`` (token registry states)."""
+
+    def __init__(self, resident: Callable[[str], bool]):
+        self._resident = resident
+        self._records: dict = {}  # owner id -> (key, tokens hash, storage mode)
+        self._owners: dict = {}   # key -> [owner ids]
+        self._lock = threading.Lock()
+
+    def state(self, key: str) -> str:
+        with self._lock:
+            if self._owners.get(key):
+                return COMPILE_STATE_COMPILING
+        return COMPILE_STATE_RESIDENT if self._resident(key) else COMPILE_STATE_ABSENT
+
+    def admit(self, owner, key: str, tokens, storage_mode: str) -> None:
+        import hashlib
+        import weakref
+
+        digest = hashlib.sha256(",".join(str(int(t)) for t in tokens).encode()).hexdigest()
+        with self._lock:
+            owners = self._owners.get(key)
+            if owners:
+                _, first_digest, first_mode = self._records[owners[0]]
+                if (first_digest, first_mode) != (digest, storage_mode):
+                    raise RequestRejected(
+                        f"a Compile of cache_key {key} with other tokens or storage mode is already in flight; a "
+                        "cache key names one block: wait for the first Compile or use another key")
+            oid = id(owner)
+            if oid in self._records:
+                self._drop_locked(oid)
+            self._owners.setdefault(key, []).append(oid)
+            self._records[oid] = (key, digest, storage_mode)
+        try:
+            fin = weakref.finalize(owner, self.finish, oid)
+            fin.atexit = False
+        except TypeError:
+            pass
+
+    def finish(self, owner) -> None:
+        """The Compile ended (registered or failed); idempotent."""
+        with self._lock:
+            self._drop_locked(owner if isinstance(owner, int) else id(owner))
+
+    def _drop_locked(self, oid: int) -> None:
+        rec = self._records.pop(oid, None)
+        if rec is None:
+            return
+        owners = self._owners.get(rec[0], [])
+        if oid in owners:
+            owners.remove(oid)
+        if not owners:
+            self._owners.pop(rec[0], None)
+
+    def inflight(self) -> dict:
+        with self._lock:
+            return {k: len(v) for k, v in self._owners.items()}
+
+
 @dataclass
 class Request:
     kind: str  # "compile" | "link" | "plain"
@@ -71,12 +146,15 @@ class Scheduler:
         self.max_prefills_per_step = max_prefills_per_step
         self.decode_chunk = decode_chunk
         self._deferred: list = []  # Compiles pushed to the next batch (same key already in this one)
+        self._parked: list = []  # Links waiting for an in-flight Compile of one of their keys
         self.max_context = max_context or engine.max_context
         self.waiting: "queue.Queue[Request]" = queue.Queue()
         self.running: list[Request] = []
         self._stop = threading.Event()
         self._thread: Optional[threading.Thread] = None
         self.stats = {"admitted": 0, "rejected": 0, "finished": 0, "decode_steps": 0}
+        self.compile_states = CompileStates(lambda k: bool(engine.registry.contains(k)))
+        self.max_link_waits = 64  # scheduler steps a Link waits for a Compile of one of its keys
 
     # ------------------------------------------------------------ arrival
     def check(self, req: Request) -> None:
@@ -92,12 +170,33 @@ class Scheduler:
     def submit(self, req: Request) -> Request:
         try:
             self.check(req)
-        except RequestRejected as e:
+            if req.kind == "compile":
+                sc = req.sub_context or {}
+                key = sc.get("cache_key")
+                if key:
+                    from .engine import Engine as _E
+
+                    self.compile_states.admit(req, str(key), req.input_ids, _E.storage_mode(sc))
+        except (RequestRejected, ContractError) as e:
             self.stats["rejected"] += 1
             req.events.put(("error", str(e)))
             return req
         self.waiting.put(req)
         return req
+
+    def _link_waits_for_compile(self, req: Request) -> bool:
+        """A Link naming a key whose Compile is still in flight waits (up to
+        ``max_link_waits`` steps) instead of failing with a missing source."""
+        keys = (req.pic_link or {}).get("cache_keys") if isinstance(req.pic_link, dict) else None
+        if not isinstance(keys, list):
+            return False
+        waits = getattr(req, "_compile_waits", 0)
+        if waits >= self.max_link_waits:
+            return False
+        if any(isinstance(k, str) and self.compile_states.state(k) == COMPILE_STATE_COMPILING for k in keys):
+            req._compile_waits = waits + 1
+            return True
+        return False
 
     # ---------------------------------------------------------------- loop
     def start(self) -> None:
@@ -128,16 +227,19 @@ class Scheduler:
                     pass
 
     def _next_waiting(self) -> Optional[Request]:
+        """Deferred requests first (retracted, same-key Compiles), then the
+        queue, then Links parked behind an in-flight Compile of their keys."""
         if self._deferred:
             return self._deferred.pop(0)
         try:
             return self.waiting.get_nowait()
         except queue.Empty:
-            return None
+            pass
+        return self._parked.pop(0) if self._parked else None
 
     def step(self) -> bool:
         """One scheduling iteration; returns False when idle."""
-        batch = []
+        batch, later = [], []
         for _ in range(self.max_prefills_per_step):
             if len(self.running) + len(batch) >= self.max_running:
                 break
@@ -147,8 +249,15 @@ class Scheduler:
             if req.resume is not None and self.running and not self._fits(req):
                 self._deferred.insert(0, req)  # a retracted request waits for pages
                 break
+            if req.kind == "link" and self._link_waits_for_compile(req) and (
+                    batch or not self.waiting.empty() or self._deferred):
+                # its source is compiling in this or a queued step
+                later.append(req)
+                emit_trace("link_deferred_compile_in_flight", rid=req.rid)
+                continue
             batch.append(req)
-        did = bool(batch)
+        self._parked.extend(later)
+        did = bool(batch) or bool(later)
         if batch:
             self._admit_batch(batch)
         if self.running:
@@ -203,6 +312,8 @@ class Scheduler:
             c_res, l_res = [e] * len(items), [e] * len(link_items)
         if len(links) > 1:
             self.stats["batched_links"] = self.stats.get("batched_links", 0) + len(links)
+        for req in compiles:
+            self.compile_states.finish(req)
         for req, r in zip(live, c_res):
             if isinstance(r, Exception):
                 emit_trace("legolink_request_failed_closed", rid=req.rid, kind="compile", reason=str(r)[:500])
@@ -308,7 +419,8 @@ class Scheduler:
     def _decode(self) -> None:
         eng = self.engine
         k = 1
-        if (self.decode_chunk > 1 and self.waiting.empty() and not self._deferred and eng.use_cuda_graphs
+        if (self.decode_chunk > 1 and self.waiting.empty() and not self._deferred and not self._parked
+                and eng.use_cuda_graphs
                 and all(r.sampling.greedy for r in self.running)):
             k = min(self.decode_chunk, min(r.max_new_tokens - len(r.seq.output_ids) for r in self.running))
         self._retract_for(max(1, k))

@@ -200,3 +200,42 @@ def test_batched_links_on_gpu_match_serial_kv():
         agree += int(s.output_ids[0] == first)
         e.free(s)
     assert agree >= 3
+
+
+def test_compile_states_refuse_conflicts_and_links_wait_for_compiles(eng):
+    """absent -> compiling -> resident; a conflicting Compile of an in-flight
+    key is refused at arrival, an agreeing one attaches; a Link queued behind
+    the Compile of its key waits for it instead of failing."""
+    import gc
+
+    from sglang_legolink_b200.runtime.scheduler import (COMPILE_STATE_ABSENT, COMPILE_STATE_COMPILING,
+                                                        COMPILE_STATE_RESIDENT, Request, Scheduler)
+
+    sch = Scheduler(eng, max_prefills_per_step=1)
+    toks = _toks(70, 501)
+    c1 = Request("compile", "c1", toks, 1, sub_context={"cache_key": "state-k"})
+    link = Request("link", "l1", [1, 2, 3], 2, pic_link={"cache_keys": ["state-k"], "recompute_initial_tokens": 4})
+    assert sch.compile_states.state("state-k") == COMPILE_STATE_ABSENT
+    sch.submit(c1)
+    assert sch.compile_states.state("state-k") == COMPILE_STATE_COMPILING
+    bad = sch.submit(Request("compile", "c2", _toks(70, 502), 1, sub_context={"cache_key": "state-k"}))
+    assert bad.events.get_nowait()[0] == "error"
+    same = sch.submit(Request("compile", "c3", list(toks), 1, sub_context={"cache_key": "state-k"}))
+    assert sch.compile_states.inflight() == {"state-k": 2}
+    sch.waiting.queue.appendleft(link)  # the Link arrives first, its Compile is still queued
+    while sch.step():
+        pass
+    assert sch.compile_states.state("state-k") == COMPILE_STATE_RESIDENT
+    kinds = []
+    while not link.events.empty():
+        kinds.append(link.events.get_nowait()[0])
+    assert "error" not in kinds and kinds[-1] == "done"
+    assert same.events.get_nowait()[0] == "token"  # the duplicate took the registry's duplicate path
+    # a queued Compile whose request vanishes is dropped from the in-flight set
+    sch2 = Scheduler(eng)
+    r = Request("compile", "c4", _toks(70, 503), 1, sub_context={"cache_key": "ghost"})
+    sch2.compile_states.admit(r, "ghost", r.input_ids, "reference")
+    assert sch2.compile_states.state("ghost") == COMPILE_STATE_COMPILING
+    del r
+    gc.collect()
+    assert sch2.compile_states.state("ghost") == COMPILE_STATE_ABSENT
