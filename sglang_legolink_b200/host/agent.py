@@ -24,7 +24,7 @@ from dataclasses import dataclass, field
 from typing import Callable, Iterable, Optional, Sequence
 
 from .adapter import PipelineExecution, PipelineRoute, RequestPipeline
-from .events import openai_request_events
+from .ingress import SourceLedger, openai_request_events
 from .metrics import AgentMetric, MetricsRecorder
 
 
@@ -52,7 +52,13 @@ class AgentLLM:
     def call(self, messages: Sequence[dict], tools: Optional[list] = None, *, objective: str = "",
              loop_stage: str = "act", events: Optional[list] = None, warmup: bool = False) -> TurnResult:
         self.turns += 1
-        evs = list(events) if events is not None else openai_request_events(list(messages), tools)
+        if events is None:
+            # what this call adds to the session: sources it already holds with
+            # the same text are skipped, an earlier request becomes history
+            held = self.pipeline.manager.collector.events()
+            events = openai_request_events(list(messages), tools=tools, ledger=SourceLedger.from_events(held),
+                                           first_turn=not held)
+        evs = list(events)
         query = objective or next((m.get("content") or "" for m in reversed(list(messages))
                                    if m.get("role") == "user" and isinstance(m.get("content"), str)), "")
         t0 = time.perf_counter()

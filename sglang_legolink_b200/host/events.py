@@ -257,10 +257,12 @@ def _content_text(content: Any) -> str:
 
 
 def openai_request_events(messages: list[dict], tools: Optional[list[dict]] = None) -> list[EventTuple]:
-    """OpenAI chat messages (+tools) -> event tuples with stable source ids:
-    system -> task instruction, user -> user request (the last user message)
-    or conversation, assistant -> conversation (+ tool calls), tool -> tool
-    output, each tool definition -> tool definition."""
+    """Stateless, position-keyed variant: OpenAI chat messages (+tools) ->
+    event tuples (system -> task instruction, the last user message -> user
+    request, other user / assistant -> conversation, tool -> tool output,
+    each tool definition -> tool definition).  Agents that resend their whole
+    conversation use the session-aware ``host.ingress.openai_request_events``
+    (content-derived ids and a source ledger)."""
     out: list[EventTuple] = []
     for i, tool in enumerate(tools or []):
         name = ((tool.get("function") or {}).get("name")) or tool.get("name") or f"tool-{i}"
