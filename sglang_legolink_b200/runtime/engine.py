@@ -154,7 +154,7 @@ def pages_for(n: int, ps: int) -> int:
 
 class Engine:
     def __init__(self, model: QwenModel, *, num_pages: Optional[int] = None, page_size: int = 16,
-                 mem_fraction: float = 0.85, max_blocks: int = 256, max_context: int = 32768,
+                 mem_fraction: float = 0.85, max_blocks: Optional[int] = None, max_context: int = 32768,
                  use_cuda_graphs: bool = True, residency: Optional[int] = None, legolink_only: bool = False,
                  compat_overrides: Optional[dict] = None, kv_pool: Optional[KVPool] = None,
                  directory=None, replica_rank: int = 0, peer_pools: Optional[dict] = None):
@@ -174,7 +174,12 @@ class Engine:
         self.alloc = kv_pool.alloc
         h = _ext.host()
         self.residency = residency if residency is not None else (self.device.index or 0)
-        self.registry = h.BlockRegistry(self.alloc, max_blocks, self.residency)
+        if max_blocks is None:  # deployment cap on registered blocks (LRU beyond it)
+            import os
+
+            max_blocks = int(os.getenv("SGLANG_PIC_MAX_BLOCKS", "256"))
+        self.max_blocks = int(max_blocks)
+        self.registry = h.BlockRegistry(self.alloc, self.max_blocks, self.residency)
         self.radix = h.RadixIndex(self.alloc, page_size)
         self.legolink_only = legolink_only
         self.compat = self._compat(compat_overrides or {})

@@ -17,7 +17,10 @@ from __future__ import annotations
 from dataclasses import dataclass
 from typing import Any, Callable, Optional, Sequence
 
+import os
+
 from ..contract import (
+    PIC_LINK_RECOMPUTE_MODES,
     ContractError,
     env_flag,
     physical_token_ids_sha256,
@@ -237,7 +240,12 @@ def resolve_link_plan(plan: dict, mutable_input_ids: Sequence[int],
         ah = physical_token_ids_sha256(full)
         if not isinstance(eh, str) or eh != ah:
             raise LinkPlanError(f"normalized Link complete token hash mismatch: expected={eh!r}, actual={ah}")
-    mode = str(plan.get("recompute_mode", "batched")).lower()
+    mode = str(plan.get("recompute_mode") or os.getenv("SGLANG_PIC_RECOMPUTE_MODE", "batched")).strip().lower()
+    if mode not in PIC_LINK_RECOMPUTE_MODES:
+        raise LinkPlanError(f"recompute mode {mode!r} (SGLANG_PIC_RECOMPUTE_MODE) is not one of "
+                            + ", ".join(sorted(PIC_LINK_RECOMPUTE_MODES)))
+    # batched and tokenwise recompute the same rows: one layer-outer pass over
+    # them is equal to the row-by-row order; full_causal recomputes every row
     if mode == "full_causal":
         recompute = list(range(len(full)))
     return ResolvedLinkPlan(

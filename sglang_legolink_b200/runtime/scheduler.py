@@ -138,10 +138,10 @@ class Request:
 
 
 class Scheduler:
-    def __init__(self, engine: Engine, *, legolink_only: bool = True, max_running: int = 64,
+    def __init__(self, engine: Engine, *, legolink_only: Optional[bool] = None, max_running: int = 64,
                  max_prefills_per_step: int = 8, max_context: Optional[int] = None, decode_chunk: int = 8):
         self.engine = engine
-        self.legolink_only = legolink_only
+        self._legolink_only = legolink_only  # None: SGLANG_PIC_LEGOLINK_ONLY (default on), read per request
         self.max_running = max_running
         self.max_prefills_per_step = max_prefills_per_step
         self.decode_chunk = decode_chunk
@@ -155,6 +155,21 @@ class Scheduler:
         self.stats = {"admitted": 0, "rejected": 0, "finished": 0, "decode_steps": 0}
         self.compile_states = CompileStates(lambda k: bool(engine.registry.contains(k)))
         self.max_link_waits = 64  # scheduler steps a Link waits for a Compile of one of its keys
+
+    @property
+    def legolink_only(self) -> bool:
+        """Plain generation is refused unless the deployment allows it: an
+        explicit setting wins, else ``SGLANG_PIC_LEGOLINK_ONLY`` (default on)
+        at the time of each request (reference ``pic_runtime.py:1326``)."""
+        if self._legolink_only is not None:
+            return bool(self._legolink_only)
+        from ..contract import env_flag
+
+        return env_flag("SGLANG_PIC_LEGOLINK_ONLY", "1")
+
+    @legolink_only.setter
+    def legolink_only(self, value: Optional[bool]) -> None:
+        self._legolink_only = value
 
     # ------------------------------------------------------------ arrival
     def check(self, req: Request) -> None:

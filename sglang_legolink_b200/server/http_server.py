@@ -260,7 +260,7 @@ def serve(svc: RuntimeService, host: str = "127.0.0.1", port: int = 30000) -> Th
 
 
 def build_service(model: str = "tiny-qwen2", *, device: str = "cpu", tokenizer: Optional[str] = None,
-                  legolink_only: bool = True, page_size: int = 16, num_pages: Optional[int] = None,
+                  legolink_only: Optional[bool] = True, page_size: int = 16, num_pages: Optional[int] = None,
                   max_context: int = 32768, seed: int = 0, layerwise_markers: bool = False) -> RuntimeService:
     import torch
 
@@ -294,7 +294,8 @@ def main(argv=None) -> None:
     ap.add_argument("--port", type=int, default=30000)
     ap.add_argument("--page-size", type=int, default=16)
     ap.add_argument("--context-length", type=int, default=32768)
-    ap.add_argument("--allow-plain-generation", action="store_true")
+    ap.add_argument("--allow-plain-generation", action="store_true",
+                    help="serve plain generation too (default: SGLANG_PIC_LEGOLINK_ONLY, on unless set to 0)")
     ap.add_argument("--skip-warmup", action="store_true")
     ap.add_argument("--enable-layerwise-nvtx-marker", action="store_true",
                     help="LegoLink::Attention / FFN / LMHead / Sampling profiler regions and NVTX ranges")
@@ -313,7 +314,7 @@ def main(argv=None) -> None:
         launch(a)
         return
     svc = build_service(a.model, device=a.device, tokenizer=a.tokenizer,
-                        legolink_only=not a.allow_plain_generation, page_size=a.page_size,
+                        legolink_only=False if a.allow_plain_generation else None, page_size=a.page_size,
                         max_context=a.context_length, layerwise_markers=a.enable_layerwise_nvtx_marker)
     if not a.skip_warmup and os.getenv("SGLANG_PIC_WARMUP", "1") != "0":
         print("warmup", svc.warmup(int(os.getenv("SGLANG_PIC_WARMUP_BLOCK_TOKENS", "256")),

@@ -297,7 +297,7 @@ def rank_main(a, rank: int, world: int, local: int, ready=None) -> None:
                 worker_loop(eng, ctrl)
                 return
             spmd = SPMDEngine(eng, ctrl)
-            sch = Scheduler(spmd, legolink_only=not a.allow_plain_generation)
+            sch = Scheduler(spmd, legolink_only=False if a.allow_plain_generation else None)
             sch.start()
             svc = RuntimeService(sch, tok, model_name=name)
             try:
@@ -314,7 +314,7 @@ def rank_main(a, rank: int, world: int, local: int, ready=None) -> None:
                 spmd.shutdown()
             return
         # DP: every rank is a replica
-        sch = Scheduler(eng, legolink_only=not a.allow_plain_generation)
+        sch = Scheduler(eng, legolink_only=False if a.allow_plain_generation else None)
         sch.start()
         svc = RuntimeService(sch, tok, model_name=name)
         if not a.skip_warmup:

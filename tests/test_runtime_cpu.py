@@ -304,3 +304,38 @@ def test_compile_clone_storage_mode(world):
     with pytest.raises(ContractError):
         eng.compile(t, "clone-bad", sub_context={"pic_storage_mode": "mirror"})
     eng.free(a), eng.free(b)
+
+
+def test_deployment_flags_are_read_at_call_time(monkeypatch):
+    """SGLANG_PIC_LEGOLINK_ONLY (default on) decides per request whether plain
+    generation is refused unless the server was given an explicit setting;
+    SGLANG_PIC_RECOMPUTE_MODE is the mode of a Link that names none;
+    SGLANG_PIC_MAX_BLOCKS caps the registry."""
+    from sglang_legolink_b200.runtime.scheduler import Request, RequestRejected, Scheduler
+
+    monkeypatch.setenv("SGLANG_PIC_MAX_BLOCKS", "3")
+    e = Engine(QwenModel.random_init(PRESETS["tiny-qwen2"], seed=0), num_pages=256, page_size=16)
+    assert e.max_blocks == 3
+    for i in range(5):
+        e.compile(list(range(10 + i, 40 + i)), f"cap-{i}")
+    assert len(e.registry.keys()) == 3  # least recently used beyond the cap are dropped
+    sch = Scheduler(e)
+    plain = Request("plain", "p", [1, 2, 3], 2)
+    monkeypatch.delenv("SGLANG_PIC_LEGOLINK_ONLY", raising=False)
+    with pytest.raises(RequestRejected):
+        sch.check(plain)
+    monkeypatch.setenv("SGLANG_PIC_LEGOLINK_ONLY", "0")
+    sch.check(plain)
+    with pytest.raises(RequestRejected):
+        Scheduler(e, legolink_only=True).check(plain)  # an explicit setting wins
+    e.compile(list(range(100, 180)), "rm")
+    monkeypatch.setenv("SGLANG_PIC_RECOMPUTE_MODE", "full_causal")
+    s = e.link({"cache_keys": ["rm"], "recompute_initial_tokens": 4}, [5, 6])
+    assert s.link_plan.recompute_mode == "full_causal" and len(s.link_plan.recompute_positions) == s.length
+    e.free(s)
+    s = e.link({"cache_keys": ["rm"], "recompute_initial_tokens": 4, "recompute_mode": "batched"}, [5, 6])
+    assert s.link_plan.recompute_mode == "batched" and len(s.link_plan.recompute_positions) < s.length
+    e.free(s)
+    monkeypatch.setenv("SGLANG_PIC_RECOMPUTE_MODE", "sideways")
+    with pytest.raises(ContractError):
+        e.link({"cache_keys": ["rm"]}, [5, 6])
