@@ -33,6 +33,7 @@ from ..contract import PIC_LINK_RUNTIME_OWNED_FIELDS, parse_residency_recovery
 from .framing import (ChatTokenLayout, RepairDecision, RepairWindowPlanner, Stitcher, StitchedContext, build_layout,
                       compile_payload, frame_link, framing_spec_for)
 from .manager import ContextManager
+from .token_reuse import RequestTokenSource, SharedTokenCache, host_token_reuse_enabled
 from .planner import CacheCatalog, ExecutionPlan, Planner
 
 
@@ -368,6 +369,7 @@ class RequestPipeline:
         self.planner = planner or Planner(catalog=adapter.catalog)
         self.stitcher = stitcher or Stitcher(tokenizer=None)
         self.namespace = namespace
+        self.shared_tokens = SharedTokenCache()  # immutable texts' ids across requests (host token reuse)
 
     def execute(self, events, route: PipelineRoute = PipelineRoute.SELECTED_CONTEXT_LEGOLINK, query: str = "",
                 tools=None) -> PipelineExecution:
@@ -390,8 +392,20 @@ class RequestPipeline:
             return PipelineExecution(route, res, plan, timings_ms=tm)
         t = time.perf_counter()
         stitched = self.stitcher.stitch(plan)
-        layout = build_layout(stitched, self.adapter.tokenizer, tools=tools)
+        tok = self.adapter.tokenizer
+        source = None
+        if host_token_reuse_enabled():
+            # framing reads the ids the stored sub-contexts already hold
+            source = RequestTokenSource(tok, shared=self.shared_tokens)
+            for v in plan.linked_contexts:
+                source.adopt(v)
+            for v in stitched.linked_views:  # block + separator: immutable, shared across turns
+                source.mark_immutable(v.raw_text)
+            tok = source
+        layout = build_layout(stitched, tok, tools=tools)
         tm["frame"] = (time.perf_counter() - t) * 1e3
+        if source is not None:
+            tm["token_reuse"] = source.counts()
         t = time.perf_counter()
         nc, cdt = self.adapter.compile_plan(layout)
         self.planner.after_compile(plan)
