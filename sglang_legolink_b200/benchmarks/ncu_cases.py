@@ -1,7 +1,7 @@
 """Small single-kernel cases sized for `ncu --set full` captures (a few
 launches, a few hundred MB on the device), one per hot kernel:
 
-    python -m sglang_legolink_b200.benchmarks.ncu_cases {gemm,gemm_link,gemm_link_cublas,attn,gemv,gemv_residual,decode,link,tp_reduce,tp_scatter}
+    python -m sglang_legolink_b200.benchmarks.ncu_cases {gemm,gemm_link,gemm_link_cublas,attn,gemv,gemv_residual,decode,link,rmsnorm,rope_qkv,tp_reduce,tp_scatter}
 """
 import sys, os, math
 
@@ -72,6 +72,22 @@ elif case == "link":  # fused KV link + RoPE delta: 4096 tokens x 28 layers (Qwe
     lp = torch.arange(n, device="cuda", dtype=torch.int32)
     cs = ref.rope_cos_sin_table(32768, D, 1e6).cuda()
     for _ in range(4): ops.kv_link_rope(k, v, src, dst, lp, lp + 3000, cs)
+elif case == "rmsnorm":  # fused residual add + RMSNorm over a Link's rows (8192 x 3584)
+    T, H = 8192, 3584
+    x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    r = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    w = torch.rand(H, device="cuda", dtype=torch.bfloat16) + 0.5
+    for _ in range(4): ops.fused_add_rmsnorm(x, r, w, 1e-6)
+elif case == "rope_qkv":  # RoPE of q/k + KV write of 8192 rows (Qwen2.5-7B heads) into a paged pool
+    T, Hq, Hkv, D, ps = 8192, 28, 4, 128, 16
+    pages = T // ps + 8
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device="cuda", dtype=torch.bfloat16)
+    kp = torch.zeros(pages, Hkv, ps, D, device="cuda", dtype=torch.bfloat16); vp = torch.zeros_like(kp)
+    pos = torch.arange(T, device="cuda", dtype=torch.int32)
+    slots = torch.arange(T, device="cuda", dtype=torch.int64)
+    cs = ref.rope_cos_sin_table(32768, D, 1e6).cuda()
+    q = torch.empty(T, Hq, D, device="cuda", dtype=torch.bfloat16)
+    for _ in range(4): ops.rope_qkv_write(qkv, pos, slots, cs, q, kp, vp, Hq, Hkv, D)
 elif case in ("tp_reduce", "tp_scatter"):  # fused-TP kernels on one GPU: both "ranks'" buffers are local
     W, H, K, T = 2, 5120, 4096, 16384
     R = T // W
