@@ -192,7 +192,7 @@ def bench_attention_variants(pk, with_torch):
         tf = flops / ms / 1e9
         rows.append({"op": f"attn_prefill_tcgen05[repair5k,variant{v}]", "ms": round(ms, 4), "tflops": round(tf, 1),
                      "frac_of_peak": round(tf / pk["bf16_tflops"], 3), "rel_err_vs_fp32": round(err, 5)})
-    ext.attn_prefill_tc_set_variant(-1)
+    ext.attn_prefill_tc_set_variant(-2)
     return rows
 
 

@@ -61,6 +61,7 @@ constexpr int TC_THREADS = 128 + 128 * TC_NT;        // warpgroup 0: producer, M
 constexpr int TC_REGS_LAUNCH = 168;
 constexpr int TC_REGS_CTRL = 80;
 constexpr int TC_REGS_SOFTMAX = 208;
+static_assert(TC_Q_HALF == TC_KV_HALF, "Q and K halves share descriptor offsets");
 static_assert(4 * TC_REGS_CTRL + 4 * TC_NT * TC_REGS_SOFTMAX <= (TC_THREADS / 32) * TC_REGS_LAUNCH,
               "register split exceeds the launch allocation");
 constexpr float TC_RESCALE_THRESHOLD = 8.0f;         // log2 units
@@ -68,6 +69,13 @@ constexpr float TC_RESCALE_THRESHOLD = 8.0f;         // log2 units
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 2^x of both bf16 halves in one MUFU op (+0 for -inf, subnormals flushed).
+__device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
   return y;
 }
 
@@ -174,9 +182,16 @@ __device__ __forceinline__ void cp_async16_tc(uint32_t saddr, const void* g, boo
 
 // POLY8 of every 8 scores take exp2 on the FMA pipe (exp2_poly) instead of
 // the MUFU pipe; ALU_PACK rounds P to bf16 on the ALU pipe.  Both move work
-// off the MUFU/XU pipe, which bounds the softmax.
+// off the MUFU/XU pipe, which bounds the softmax.  POLY8 == TC_EXP_BF16X2
+// instead rounds the exponent pairs to bf16 and takes both exp2 values in
+// one packed MUFU op (ex2.approx.ftz.bf16x2), whose result is already the
+// bf16 pair the PV MMA reads: half the MUFU ops and no pack after the exp.
+// The input rounding costs at most |x| * 2^-9 of the exponent, i.e. a
+// relative error of 0.14 % on P for |x| <= 1 (where the weight sits) and
+// about 1 % on weights below 2^-7 of the row maximum.
 // TRACE: CTA 0 records clock64() at the handoffs of each block into
 // g_attn_trace (diagnostic build only; read with ll_attn_prefill_tc_trace).
+constexpr int TC_EXP_BF16X2 = -1;
 constexpr int TC_TRACE_EV = 20;
 constexpr int TC_TRACE_BLOCKS = 256;
 __device__ unsigned long long g_attn_trace[TC_TRACE_BLOCKS * TC_TRACE_EV];
@@ -186,7 +201,7 @@ __device__ unsigned long long g_attn_trace[TC_TRACE_BLOCKS * TC_TRACE_EV];
       g_attn_trace[(j) * TC_TRACE_EV + (e)] = clock64();                              \
   } while (0)
 
-template <int POLY8, bool ALU_PACK, bool TRACE = false>
+template <int POLY8, bool ALU_PACK, bool TRACE = false, bool PIPE = false>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                            const bf16* __restrict__ q, const int* __restrict__ q_indptr,
@@ -207,7 +222,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* p_full = s_full + TC_NT;    // [TC_NT]
   uint64_t* q_full = p_full + TC_NT;
   uint64_t* o_full = q_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
+  uint64_t* s_free = o_full + 1;        // [TC_NT] PIPE: S_t read into registers
+  uint64_t* p_half = s_free + TC_NT;    // [TC_NT] PIPE: P_t of the first 64 keys stored
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p_half + TC_NT);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int4 tile = tiles[blockIdx.x];
@@ -230,6 +247,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     for (int i = 0; i < TC_NT; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_half[i], 4);
     }
     mbar_init(q_full, 4 * TC_NT);
     mbar_init(o_full, 1);
@@ -308,7 +327,73 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             umma_bf16_ts(tmem + 256 + 128 * t, tmem + 128 * t + 8 * k, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
           }
         };
-        for (int j = 0; j < nb && ok; ++j) {
+        // PIPE: S_t(j) = Q_t K_j^T in two N = 64 halves.  P_t(j-1) occupies
+        // only TMEM columns [128t, 128t + 64), so the upper half (keys
+        // 64..127 -> columns [128t + 64, 128t + 128)) is issued as soon as the
+        // softmax has read S_t(j-1) into registers (s_free), and runs while
+        // that softmax computes.  PV_t(j-1) goes in two K halves: keys 0..63
+        // after p_half, 64..127 after p_full; then the lower half of S_t(j).
+        constexpr uint32_t idesc_s64 = umma_idesc_bf16_f32(TC_BM, 64);
+        // Descriptors advance by adding byte offsets / 16 to their address
+        // field (shared addresses stay below 256 KB, so it never carries).
+        const uint64_t q_desc0 = umma_desc_sw128_kmajor(smem_u32(sQ));
+        const uint64_t k_desc0 = umma_desc_sw128_kmajor(smem_u32(sK));
+        const uint64_t v_desc0 = umma_desc_sw128_mnmajor(smem_u32(sV), TC_KV_HALF, 1024);
+        auto issue_s_half = [&](int t, int sk, int hi) {
+          const uint64_t qd = q_desc0 + (uint64_t)((t * TC_Q_BYTES) >> 4);
+          const uint64_t kd = k_desc0 + (uint64_t)((sk * TC_KV_BYTES + hi * 64 * 128) >> 4);
+#pragma unroll
+          for (int k = 0; k < TC_D / 16; ++k) {
+            const uint32_t off = ((k >> 2) * TC_Q_HALF + (k & 3) * 32) >> 4;  // TC_Q_HALF == TC_KV_HALF
+            umma_bf16(tmem + 128 * t + 64 * hi, qd + off, kd + off, idesc_s64, k > 0 ? 1u : 0u);
+          }
+        };
+        auto issue_pv_half = [&](int t, int i, int h) {
+          const uint64_t vd = v_desc0 + (uint64_t)(((i % TC_VS) * TC_KV_BYTES) >> 4);
+#pragma unroll
+          for (int k = 4 * h; k < 4 * h + 4; ++k)
+            umma_bf16_ts(tmem + 256 + 128 * t, tmem + 128 * t + 8 * k, vd + (uint64_t)((k * 16 * 128) >> 4), idesc_pv,
+                         (i > 0 || k > 0) ? 1u : 0u);
+        };
+        // PV_t(i) of block i in its two halves (waits: p_half, V_i, p_full)
+        auto pv_pipe = [&](int t, int i) -> bool {
+          if (!mbar_wait(&p_half[t], i & 1, err, kErrTmemFullTimeout)) return false;
+          if (t == 0 && !mbar_wait(&v_full[i % TC_VS], (i / TC_VS) & 1, err, kErrTmaFullTimeout)) return false;
+          tc_fence_after();
+          issue_pv_half(t, i, 0);
+          if (!mbar_wait(&p_full[t], i & 1, err, kErrTmemFullTimeout)) return false;
+          TC_TR(i + 1, 7 + t);
+          tc_fence_after();
+          issue_pv_half(t, i, 1);
+          return true;
+        };
+        for (int j = 0; PIPE && j < nb && ok; ++j) {
+          const int sk = j % TC_KS;
+#pragma unroll
+          for (int t = 0; t < TC_NT; ++t) {
+            if (j > 0 && !mbar_wait(&s_free[t], (j - 1) & 1, err, kErrTmemFullTimeout)) { ok = false; break; }
+            if (t == 0) {
+              if (!mbar_wait(&k_full[sk], (j / TC_KS) & 1, err, kErrTmaFullTimeout)) { ok = false; break; }
+              TC_TR(j, 6);
+            }
+            tc_fence_after();
+            issue_s_half(t, sk, 1);
+            if (j > 0) {
+              if (!pv_pipe(t, j - 1)) { ok = false; break; }
+              if (t == TC_NT - 1) umma_commit(&v_empty[(j - 1) % TC_VS]);
+            }
+            issue_s_half(t, sk, 0);
+            umma_commit(&s_full[t]);
+            TC_TR(j, 9 + t);
+          }
+          if (!ok) break;
+          umma_commit(&k_empty[sk]);
+        }
+        if (PIPE && ok) {
+          for (int t = 0; t < TC_NT && ok; ++t) ok = pv_pipe(t, nb - 1);
+          if (ok) umma_commit(&v_empty[(nb - 1) % TC_VS]);
+        }
+        for (int j = 0; !PIPE && j < nb && ok; ++j) {
           const int sk = j % TC_KS;
           const uint32_t kbase = smem_u32(sK + sk * TC_KV_BYTES);
 #pragma unroll
@@ -342,7 +427,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           if (!ok) break;
           umma_commit(&k_empty[sk]);
         }
-        if (ok) {
+        if (!PIPE && ok) {
           const int i = nb - 1;
           for (int t = 0; t < TC_NT && ok; ++t) {
             if (!mbar_wait(&p_full[t], i & 1, err, kErrTmemFullTimeout)) { ok = false; break; }
@@ -408,6 +493,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tmem_ld_32x32b_x32(s_col + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&s[32 * c]));
       tmem_ld_wait();
       if (r == 0) TC_TR(j, 3 * t + 1);
+      if constexpr (PIPE) {  // S_t is in registers: the MMA may overwrite its upper half
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[t]);
+      }
       if (MASK) {
         const int lim = pos - j * TC_BN;  // scores with index > lim are masked
 #pragma unroll
@@ -429,20 +519,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const float m_use = grow ? m_new : m_run;
       const float o_scale = (grow && m_run != -INFINITY) ? ex2(m_run - m_new) : 1.f;
       const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
+      // A warp that rescales O this block signals p_half only after the
+      // rescale (the MMA must not add P V into O before it).
+      const bool rescale = __any_sync(0xffffffffu, o_scale != 1.f);
       // P = exp2(S*scale - m) as bf16 pairs over the first 64 columns of S.
       float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < TC_BN / 32; ++c) {
+        if (PIPE && c == 2 && !rescale) {  // keys 0..63 of P stored: PV may start on them
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_half[t]);
+        }
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int i0 = 32 * c + 2 * e;
           const float xa = fmaf(__uint_as_float(s[i0]), scale_log2, neg_m);
           const float xb = fmaf(__uint_as_float(s[i0 + 1]), scale_log2, neg_m);
-          const float pa = (i0 & 7) < POLY8 ? exp2_poly(xa) : ex2(xa);
-          const float pb = ((i0 + 1) & 7) < POLY8 ? exp2_poly(xb) : ex2(xb);
-          sum4[e & 3] += pa + pb;
-          pk[e] = ALU_PACK ? pack_bf16x2_alu(pa, pb) : pack_bf16x2(pa, pb);
+          if constexpr (POLY8 == TC_EXP_BF16X2) {
+            const uint32_t pp = ex2_bf16x2(pack_bf16x2(xa, xb));
+            // the row sum adds the bf16 weights the MMA uses
+            sum4[e & 3] += __uint_as_float(pp << 16) + __uint_as_float(pp & 0xffff0000u);
+            pk[e] = pp;
+          } else {
+            const float pa = (i0 & 7) < POLY8 ? exp2_poly(xa) : ex2(xa);
+            const float pb = ((i0 + 1) & 7) < POLY8 ? exp2_poly(xb) : ex2(xb);
+            sum4[e & 3] += pa + pb;
+            pk[e] = ALU_PACK ? pack_bf16x2_alu(pa, pb) : pack_bf16x2(pa, pb);
+          }
         }
         tmem_st_32x32b_x16(s_col + 16 * c, pk);
         if (r == 0 && t == 0) TC_TR(j, 12 + c);
@@ -450,7 +556,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       // O is stable here: PV of block j-1 was issued before S(j) and the
       // commit that signalled S(j) covers it.
-      if (__any_sync(0xffffffffu, o_scale != 1.f)) {
+      if (rescale) {
 #pragma unroll 1
         for (int c = 0; c < TC_D; c += 32) {
           uint32_t o[32];
@@ -468,7 +574,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (r == 0) TC_TR(j, 3 * t + 2);
-      if (lane == 0) mbar_arrive(&p_full[t]);
+      if (lane == 0) {
+        if (PIPE && rescale) mbar_arrive(&p_half[t]);
+        mbar_arrive(&p_full[t]);
+      }
       return true;
     };
     bool ok = true;
@@ -554,11 +663,23 @@ static int make_pool_run_map(CUtensorMap* tm, const void* base, int L, int pages
 typedef void (*Kern)(CUtensorMap, CUtensorMap, const bf16*, const int*, const int*, const int*, int, const int4*,
                      bf16*, int, int, int, int, float, int*);
 // (POLY8, ALU_PACK) variants; LL_ATTN_VARIANT=<index> selects one.
-constexpr int kNumVariants = 7;
+// 7: packed bf16x2 exp2; 9, 10: the S/PV pipeline (PIPE) with fp32 and
+// packed exp2; 6, 8, 11, 12: the clock64() trace builds of 0, 7, 9, 10.
+constexpr int kNumVariants = 13;
 static const Kern kVariants[kNumVariants] = {
-    attn_prefill_tc_kernel<0, false>, attn_prefill_tc_kernel<0, true>, attn_prefill_tc_kernel<2, true>,
-    attn_prefill_tc_kernel<3, true>,  attn_prefill_tc_kernel<4, true>, attn_prefill_tc_kernel<2, false>,
-    attn_prefill_tc_kernel<0, false, true>};
+    attn_prefill_tc_kernel<0, false>,
+    attn_prefill_tc_kernel<0, true>,
+    attn_prefill_tc_kernel<2, true>,
+    attn_prefill_tc_kernel<3, true>,
+    attn_prefill_tc_kernel<4, true>,
+    attn_prefill_tc_kernel<2, false>,
+    attn_prefill_tc_kernel<0, false, true>,
+    attn_prefill_tc_kernel<TC_EXP_BF16X2, false>,
+    attn_prefill_tc_kernel<TC_EXP_BF16X2, false, true>,
+    attn_prefill_tc_kernel<0, false, false, true>,
+    attn_prefill_tc_kernel<TC_EXP_BF16X2, false, false, true>,
+    attn_prefill_tc_kernel<0, false, true, true>,
+    attn_prefill_tc_kernel<TC_EXP_BF16X2, false, true, true>};
 constexpr int kDefaultVariant = 0;
 
 static int g_attn_variant = -1;
@@ -952,26 +1073,28 @@ extern "C" int ll_attn_prefill_tc(const bf16* q, const bf16* k_pool, const bf16*
   // A launch whose registers or shared memory cannot fit one CTA on an SM is
   // refused here: such launches crashed the host process inside the driver
   // instead of returning an error.
-  static int fits[kNumVariants] = {-1, -1, -1, -1, -1, -1, -1};
-  if (fits[v] < 0) {
+  static int fits[kNumVariants] = {};  // 0: not checked yet, 1: fits, 2: refused
+  if (fits[v] == 0) {
     int n = 0;
     fits[v] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) == cudaSuccess &&
                       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, TC_THREADS, TC_SMEM) == cudaSuccess &&
                       n >= 1
                   ? 1
-                  : 0;
+                  : 2;
   }
-  if (!fits[v]) return -7;
+  if (fits[v] != 1) return -7;
   kern<<<ntiles, TC_THREADS, TC_SMEM, stream>>>(tk, tv, q, q_indptr, q_pos, page_table, pt_stride,
                                                 reinterpret_cast<const int4*>(tiles), out, Hq, Hkv, page_size, layer,
                                                 scale * 1.4426950408889634f, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
-// Selects the (POLY8, ALU_PACK) variant for later launches; returns the
-// number of variants (a negative or out-of-range index only queries).
+// Selects the build (kVariants index) for later launches; -2 goes back to
+// the default (LL_ATTN_VARIANT, else kDefaultVariant); any other negative or
+// out-of-range index only queries.  Returns the number of builds.
 extern "C" int ll_attn_prefill_tc_set_variant(int v) {
   if (v >= 0 && v < kNumVariants) g_attn_variant = v;
+  if (v == -2) g_attn_variant = -1;
   return kNumVariants;
 }
 

@@ -282,6 +282,39 @@ def test_attention_prefill_sparse_rows(Hq, Hkv, ps):
     assert _rel(legacy.cpu(), exp) < 1.5e-2
 
 
+@pytest.mark.parametrize("variant", [0, 7, 9, 10])
+def test_attention_prefill_builds_match_fp32(variant):
+    """The exp2 / pipeline builds of the tcgen05 kernel (0: fp32 exp2, 7:
+    packed bf16x2 exp2, 9 and 10: the split-S / half-PV pipeline with each)
+    on sparse and full causal rows; the second request's queries are scaled
+    up so that running maxima grow mid-row and O is rescaled in TMEM."""
+    ext = ops._cuda()
+    D, Hq, Hkv, ps = 128, 28, 4, 16
+    lens = [3000, 900]
+    kp, vp, pt = _paged_setup(2, lens, Hkv, D, ps, seed=11)
+    g = torch.Generator().manual_seed(12)
+    rows = sorted(set(range(0, 40)) | set(range(1000, 1100)) | set(range(2950, 3000)))
+    qptr = [0, len(rows), len(rows) + lens[1]]
+    rows = rows + list(range(lens[1]))
+    q = torch.randn(len(rows), Hq, D, generator=g)
+    q[qptr[1]:] *= 4.0
+    q = q.to(torch.bfloat16)
+    qpos = torch.tensor(rows, dtype=torch.int32)
+    qi = torch.tensor(qptr, dtype=torch.int32)
+    kvl = torch.tensor(lens, dtype=torch.int32)
+    scale = 1 / math.sqrt(D)
+    exp = ref.paged_attention(q.float(), kp.float(), vp.float(), qi, qpos, pt, kvl, scale)
+    try:
+        ext.attn_prefill_tc_set_variant(variant)
+        out = ops.attention_prefill(q.to(DEV), kp[None].to(DEV), vp[None].to(DEV), 0, qi.to(DEV), qpos.to(DEV),
+                                    pt.to(DEV), kvl.to(DEV), scale)
+        torch.cuda.synchronize()
+    finally:
+        ext.attn_prefill_tc_set_variant(-2)
+    assert ops.check_errors(DEV) == 0
+    assert _rel(out.cpu(), exp) < 1.5e-2
+
+
 @pytest.mark.parametrize("B,Hq,Hkv,n,contiguous", [(1, 28, 4, 16000, False), (1, 28, 4, 16000, True),
                                                    (3, 28, 4, 1000, True), (16, 8, 1, 3000, False),
                                                    (2, 64, 8, 77, False)])
