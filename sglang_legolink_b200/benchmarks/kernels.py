@@ -216,6 +216,32 @@ def bench_kv_link(pk, with_torch):
     return rows
 
 
+def bench_tp_reduce(pk, with_torch):
+    """The fused TP boundary reduction (sum of `world` partial slots +
+    residual -> residual, RMSNorm -> every rank's gather buffer) on one GPU
+    with all ranks' buffers local: Qwen3-32B hidden 5120, 8192 owned rows.
+    Bytes: reads (world slots + residual), writes (residual + world G rows)."""
+    rows = []
+    ext = ops._cuda()
+    err = ops.workspace("cuda").err
+    H, R = 5120, 8192
+    for W in (2, 4, 8):
+        slots = torch.randn(W, R, H, device="cuda").to(torch.bfloat16)
+        G = [torch.empty(W * R, H, device="cuda", dtype=torch.bfloat16) for _ in range(W)]
+        cnt = torch.zeros(W, 2, device="cuda", dtype=torch.int64)
+        res = torch.randn(R, H, device="cuda").to(torch.bfloat16)
+        w = torch.ones(H, device="cuda", dtype=torch.bfloat16)
+        gp = [x.data_ptr() for x in G]
+        gcp = [cnt[i].data_ptr() + 8 for i in range(W)]
+        ms = time_fn(lambda: ext.tp_reduce_norm_gather(slots, res, w, 1e-6, R, gp, gcp, 0, 0, 0, W, R, err))
+        byts = (W + 1) * R * H * 2 + (1 + W) * R * H * 2
+        gbs = byts / ms / 1e6
+        rows.append({"op": f"tp_reduce_norm_gather[world{W},rows{R},h{H},1gpu]", "ms": round(ms, 4),
+                     "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / pk["hbm_gbs"], 3)})
+        del slots, G
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,small_m,attn,kv_link")
@@ -223,7 +249,7 @@ def main():
     a = ap.parse_args()
     pk = peaks()
     fns = {"gemm": bench_gemm, "small_m": bench_small_m, "attn": bench_attention, "kv_link": bench_kv_link,
-           "attn_variants": bench_attention_variants}
+           "attn_variants": bench_attention_variants, "tp_reduce": bench_tp_reduce}
     for name in a.only.split(","):
         for r in fns[name](pk, a.torch):
             r["peaks"] = pk["src"]

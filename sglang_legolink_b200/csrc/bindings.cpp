@@ -152,7 +152,7 @@ int64_t tp_reduce_norm_gather(const c10::optional<at::Tensor>& slots, at::Tensor
   check_rc(ll_tp_reduce_norm_gather(slots.has_value() ? slots->data_ptr() : nullptr, residual.data_ptr(),
                                     w.data_ptr(), (float)eps, H, (int)rows, &tg, err.data_ptr<int>(), cur_stream()),
            "ll_tp_reduce_norm_gather");
-  return ll_tp_reduce_norm_gather_grid((int)rows);
+  return ll_tp_reduce_norm_gather_grid((int)rows, H);
 }
 
 void tp_wait(int64_t cnt, int64_t target, const at::Tensor& err) {

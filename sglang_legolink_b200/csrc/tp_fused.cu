@@ -31,8 +31,11 @@ namespace ll {
 
 using TpGather = LLTpGather;
 
-// One CTA of TPB = 128 threads per row (grid-strided, several CTAs per SM
-// in flight); each thread keeps VPT 16-byte vectors of the row in registers.
+// One CTA of TPB = 128 threads per row (grid-strided over as many CTAs as
+// are resident at once, so there is no partial second wave); each thread
+// keeps VPT 16-byte vectors of the row in registers, and its VPT vectors of
+// the norm weight for the whole loop (one load per CTA instead of an L2
+// round trip per row after the reduction).
 constexpr int TPB = 128;
 template <int VPT>
 __global__ void __launch_bounds__(TPB)
@@ -45,6 +48,12 @@ __global__ void __launch_bounds__(TPB)
   if (threadIdx.x == 0) s_ok = tg.slot_cnt == nullptr ? 1 : (wait_counter_geq(tg.slot_cnt, tg.slot_target, err) ? 1 : 0);
   __syncthreads();
   const int nvec = H / 8;
+  uint4 wv[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * TPB;
+    wv[i] = idx < nvec ? reinterpret_cast<const uint4*>(w)[idx] : make_uint4(0, 0, 0, 0);
+  }
   if (s_ok) {
     for (int row = blockIdx.x; row < rows; row += gridDim.x) {
       uint4* rr = reinterpret_cast<uint4*>(residual + (size_t)row * H);
@@ -114,8 +123,7 @@ __global__ void __launch_bounds__(TPB)
       for (int i = 0; i < VPT; ++i) {
         const int idx = threadIdx.x + i * TPB;
         if (idx < nvec) {
-          const uint4 wv = reinterpret_cast<const uint4*>(w)[idx];
-          const uint32_t* wu = reinterpret_cast<const uint32_t*>(&wv);
+          const uint32_t* wu = reinterpret_cast<const uint32_t*>(&wv[i]);
           uint32_t o[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -138,17 +146,39 @@ __global__ void __launch_bounds__(TPB)
 
 using namespace ll;
 
-// Grid used by ll_tp_reduce_norm_gather for `rows` rows: the same on every
-// rank (each rank's G counter grows by world x this per call).
-extern "C" int ll_tp_reduce_norm_gather_grid(int rows) {
-  static int sms = 0;
+typedef void (*TpRngKern)(const bf16*, bf16*, const bf16*, float, int, int, const TpGather, int*);
+
+static TpRngKern tp_rng_kernel(int H) {
+  switch ((H / 8 + TPB - 1) / TPB) {
+    case 1: return tp_reduce_norm_gather_kernel<1>;
+    case 2: return tp_reduce_norm_gather_kernel<2>;
+    case 3: return tp_reduce_norm_gather_kernel<3>;
+    case 4: return tp_reduce_norm_gather_kernel<4>;
+    case 5: return tp_reduce_norm_gather_kernel<5>;
+    case 6: return tp_reduce_norm_gather_kernel<6>;
+    default: return tp_reduce_norm_gather_kernel<8>;
+  }
+}
+
+// Grid used by ll_tp_reduce_norm_gather for `rows` rows of width H: the CTAs
+// that are resident at once (the same on every rank of one GPU type, so each
+// rank's G counter grows by world x this per call).
+extern "C" int ll_tp_reduce_norm_gather_grid(int rows, int H) {
+  static int sms = 0, per_sm[9] = {};
+  const int vpt = (H / 8 + TPB - 1) / TPB;
+  const int slot = vpt > 6 ? 8 : vpt;
   if (sms == 0) {
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (sms <= 0) sms = 148;
   }
-  const int g = 8 * sms;
+  if (per_sm[slot] == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, tp_rng_kernel(H), TPB, 0) != cudaSuccess || n <= 0) n = 4;
+    per_sm[slot] = n;
+  }
+  const int g = per_sm[slot] * sms;
   return rows < g ? rows : g;
 }
 
@@ -162,19 +192,8 @@ extern "C" int ll_tp_reduce_norm_gather(const void* slots_, void* residual_, con
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (H % 8 || H > 8 * TPB * 8 || rows <= 0 || rows > tg->rows_per_rank) return -3;
   if (tg->world < 1 || tg->world > LL_MAX_TP_RANKS) return -3;
-  const int grid = ll_tp_reduce_norm_gather_grid(rows);
-  const int vpt = (H / 8 + TPB - 1) / TPB;
-#define LL_RNG(V) tp_reduce_norm_gather_kernel<V><<<grid, TPB, 0, stream>>>(slots, residual, w, eps, H, rows, *tg, err)
-  switch (vpt) {
-    case 1: LL_RNG(1); break;
-    case 2: LL_RNG(2); break;
-    case 3: LL_RNG(3); break;
-    case 4: LL_RNG(4); break;
-    case 5: LL_RNG(5); break;
-    case 6: LL_RNG(6); break;
-    default: LL_RNG(8); break;
-  }
-#undef LL_RNG
+  const int grid = ll_tp_reduce_norm_gather_grid(rows, H);
+  tp_rng_kernel(H)<<<grid, TPB, 0, stream>>>(slots, residual, w, eps, H, rows, *tg, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 

@@ -44,7 +44,7 @@ int ll_gemm_bf16_tp(const void* A, int lda, const void* W, int ldw, void* C, int
                     int K, int epilogue, const struct LLTpArgs* tp, int* err, void* stream);
 int ll_tp_reduce_norm_gather(const void* slots, void* residual, const void* w, float eps, int H, int rows,
                              const struct LLTpGather* tg, int* err, void* stream);
-int ll_tp_reduce_norm_gather_grid(int rows);
+int ll_tp_reduce_norm_gather_grid(int rows, int H);
 int ll_tp_wait(const void* cnt, unsigned long long target, int* err, void* stream);
 int ll_tp_decode_allreduce_norm(void* residual, const void* w, void* out, float eps, int H, int rows,
                                 const struct LLTpDecode* td, int* err, void* stream);
