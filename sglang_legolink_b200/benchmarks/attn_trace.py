@@ -11,10 +11,10 @@ each hand-off over the steady-state blocks:
   softmax sees S (the tensor pipe's PV + S of that tile plus any queue);
 * the block period and how long the two tiles' softmax intervals overlap.
 
-    python -m sglang_legolink_b200.benchmarks.attn_trace [--variants 6,8,11,12]
+    python -m sglang_legolink_b200.benchmarks.attn_trace [--variants 5,6]
 
-Variants are indices of the kernel's build table (trace builds: 6 fp32 MUFU exp2,
-8 packed bf16x2 exp2, 11 and 12 the same with the split-S / half-PV pipeline).
+Variants are indices of the kernel's build table (trace builds: 5 with one
+softmax warpgroup per tile, 6 with two warpgroups of 64 key columns each).
 """
 
 from __future__ import annotations
@@ -88,7 +88,7 @@ def summarize(tr: torch.Tensor, nb: int) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--variants", default="6,8,11,12")
+    ap.add_argument("--variants", default="5,6")
     a = ap.parse_args()
     ext = ops._cuda()
     fn, nb = _case()

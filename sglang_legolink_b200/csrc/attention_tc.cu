@@ -20,16 +20,24 @@
 //               is safe.  While softmax t works on S_t(j), the tensor core
 //               runs the other tile's PV and S MMAs (ping-pong).
 //   warps 2,3   idle (their registers go to the softmax warpgroups).
-//   warps 4..11 two softmax warpgroups, one per tile, one query row per
-//               thread (TMEM lane = row): tcgen05.ld S, causal mask, online
-//               max/sum in fp32 (log2 domain), P = exp2(S*scale - m) as bf16
-//               written back to TMEM with tcgen05.st.  O stays in TMEM; it
-//               is rescaled in place only when a row's running max grows by
-//               more than 2^8, so P <= 256 and most blocks skip the rescale.
-//               At the end: O / l -> global memory.
+//   softmax     CS warpgroups per tile (CS = 1: warps 4..11; CS = 2: warps
+//               4..19), one query row per thread (TMEM lane = row); with
+//               CS = 2 each of the two warpgroups of a tile takes 64 of the
+//               128 key columns of every row, so each warp's dependent chain
+//               (TMEM load, max, exp2, pack, TMEM store) is half as long and
+//               twice as many warps hide each other's latency.  The two
+//               halves of a row exchange their maxima through shared memory
+//               behind a bounded mbarrier wait.  Per row: tcgen05.ld S,
+//               causal mask, online max/sum in fp32 (log2 domain), P =
+//               exp2(S*scale - m) as bf16 written back to TMEM with
+//               tcgen05.st.  O stays in TMEM; it is rescaled in place only
+//               when a row's running max grows by more than 2^8, so P <= 256
+//               and most blocks skip the rescale.  At the end: O / l ->
+//               global memory (each half writes its 64 of the 128 columns).
 //
 // Barriers: k_full/k_empty, v_full/v_empty per stage; s_full, p_full per
-// tile; q_full, o_full.  Every wait is bounded (common.cuh).
+// tile; q_full, o_full; with CS = 2, one max-exchange barrier per (tile,
+// TMEM lane quarter).  Every wait is bounded (common.cuh).
 #include <cstdlib>
 #include <type_traits>
 
@@ -50,32 +58,39 @@ constexpr int TC_Q_BYTES = TC_BM * TC_D * 2;         // 32 KB per tile: [2 halve
 constexpr int TC_Q_HALF = TC_BM * 128;               // 16 KB
 constexpr int TC_KV_BYTES = TC_BN * TC_D * 2;        // 32 KB: [2 halves][128 keys][128 B]
 constexpr int TC_KV_HALF = TC_BN * 128;              // 16 KB
-constexpr int TC_SMEM = TC_NT * TC_Q_BYTES + (TC_KS + TC_VS) * TC_KV_BYTES + 1024 + 256;
+constexpr int TC_SMEM_BASE = TC_NT * TC_Q_BYTES + (TC_KS + TC_VS) * TC_KV_BYTES + 1024 + 256;
 constexpr uint32_t TC_TMEM_COLS = 512;               // S_t/P_t at 128t, O_t at 256 + 128t
-constexpr int TC_THREADS = 128 + 128 * TC_NT;        // warpgroup 0: producer, MMA, 2 idle; then softmax
-// Register split (setmaxnreg): the CTA launches at 168 registers per thread
-// (384 x 168 = 64512; 3 warps per SM sub-partition x 32 x 168 <= 16384).
-// Warpgroup 0 gives registers back, the softmax warpgroups take them:
-// 4 x 32 x 80 + 8 x 32 x 208 = 63488 <= 64512, the launch total, and per
-// sub-partition 32 x (80 + 2 x 208) = 15872 <= 16384.
-constexpr int TC_REGS_LAUNCH = 168;
-constexpr int TC_REGS_CTRL = 80;
-constexpr int TC_REGS_SOFTMAX = 208;
+// Per softmax column split CS: threads, shared memory and the register split
+// (setmaxnreg).  Warpgroup 0 (producer, MMA, 2 idle warps) gives registers
+// back and the softmax warpgroups take them; the sum stays within the launch
+// allocation (threads x launch registers) and, per SM sub-partition (one
+// warp of every warpgroup), within 16384.
+//   CS = 1: 384 threads at 168: 4 x 32 x 80 + 8 x 32 x 208 = 63488 <= 64512;
+//           per sub-partition 32 x (80 + 2 x 208) = 15872.
+//   CS = 2: 640 threads at 96:  4 x 32 x 88 + 16 x 32 x 96 = 60416 <= 61440;
+//           per sub-partition 32 x (88 + 4 x 96) = 15104.  (With 64 for
+//           warpgroup 0 its MMA loop spills.)  Shared memory adds the max /
+//           sum exchange buffer [tile][parity][half][128].
+template <int CS>
+struct TcCfg {
+  static constexpr int THREADS = 128 + 128 * TC_NT * CS;
+  static constexpr int REGS_LAUNCH = CS == 1 ? 168 : 96;
+  static constexpr int REGS_CTRL = CS == 1 ? 80 : 88;
+  static constexpr int REGS_SOFTMAX = CS == 1 ? 208 : 96;
+  static constexpr int NC = TC_BN / CS;              // key columns per softmax thread
+  static constexpr int XBUF_BYTES = CS == 1 ? 0 : TC_NT * 2 * CS * TC_BM * 4;
+  static constexpr int SMEM = TC_SMEM_BASE + XBUF_BYTES;
+  static_assert(4 * REGS_CTRL + 4 * TC_NT * CS * REGS_SOFTMAX <= (THREADS / 32) * REGS_LAUNCH,
+                "register split exceeds the launch allocation");
+  static_assert(32 * (REGS_CTRL + TC_NT * CS * REGS_SOFTMAX) <= 16384, "register split exceeds a sub-partition");
+  static_assert(THREADS * REGS_LAUNCH <= 65536, "launch registers exceed the SM");
+};
 static_assert(TC_Q_HALF == TC_KV_HALF, "Q and K halves share descriptor offsets");
-static_assert(4 * TC_REGS_CTRL + 4 * TC_NT * TC_REGS_SOFTMAX <= (TC_THREADS / 32) * TC_REGS_LAUNCH,
-              "register split exceeds the launch allocation");
 constexpr float TC_RESCALE_THRESHOLD = 8.0f;         // log2 units
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// 2^x of both bf16 halves in one MUFU op (+0 for -inf, subnormals flushed).
-__device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
   return y;
 }
 
@@ -182,16 +197,9 @@ __device__ __forceinline__ void cp_async16_tc(uint32_t saddr, const void* g, boo
 
 // POLY8 of every 8 scores take exp2 on the FMA pipe (exp2_poly) instead of
 // the MUFU pipe; ALU_PACK rounds P to bf16 on the ALU pipe.  Both move work
-// off the MUFU/XU pipe, which bounds the softmax.  POLY8 == TC_EXP_BF16X2
-// instead rounds the exponent pairs to bf16 and takes both exp2 values in
-// one packed MUFU op (ex2.approx.ftz.bf16x2), whose result is already the
-// bf16 pair the PV MMA reads: half the MUFU ops and no pack after the exp.
-// The input rounding costs at most |x| * 2^-9 of the exponent, i.e. a
-// relative error of 0.14 % on P for |x| <= 1 (where the weight sits) and
-// about 1 % on weights below 2^-7 of the row maximum.
+// off the MUFU/XU pipe.
 // TRACE: CTA 0 records clock64() at the handoffs of each block into
 // g_attn_trace (diagnostic build only; read with ll_attn_prefill_tc_trace).
-constexpr int TC_EXP_BF16X2 = -1;
 constexpr int TC_TRACE_EV = 20;
 constexpr int TC_TRACE_BLOCKS = 256;
 __device__ unsigned long long g_attn_trace[TC_TRACE_BLOCKS * TC_TRACE_EV];
@@ -201,13 +209,15 @@ __device__ unsigned long long g_attn_trace[TC_TRACE_BLOCKS * TC_TRACE_EV];
       g_attn_trace[(j) * TC_TRACE_EV + (e)] = clock64();                              \
   } while (0)
 
-template <int POLY8, bool ALU_PACK, bool TRACE = false, bool PIPE = false>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+template <int CS, int POLY8, bool ALU_PACK, bool TRACE = false>
+__global__ void __launch_bounds__(TcCfg<CS>::THREADS, 1)
     attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                            const bf16* __restrict__ q, const int* __restrict__ q_indptr,
                            const int* __restrict__ q_pos, const int* __restrict__ page_table, int pt_stride,
                            const int4* __restrict__ tiles, bf16* __restrict__ out, int Hq, int Hkv, int ps,
                            int layer, float scale_log2, int* err) {
+  using Cfg = TcCfg<CS>;
+  constexpr int NC = Cfg::NC;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                   // [TC_NT][Q]
@@ -222,9 +232,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* p_full = s_full + TC_NT;    // [TC_NT]
   uint64_t* q_full = p_full + TC_NT;
   uint64_t* o_full = q_full + 1;
-  uint64_t* s_free = o_full + 1;        // [TC_NT] PIPE: S_t read into registers
-  uint64_t* p_half = s_free + TC_NT;    // [TC_NT] PIPE: P_t of the first 64 keys stored
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p_half + TC_NT);
+  uint64_t* x_bar = o_full + 1;         // [TC_NT][4] CS == 2: max / sum exchange per lane quarter
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_bar + 4 * TC_NT);
+  float* xbuf = reinterpret_cast<float*>(smem + TC_SMEM_BASE - 1024);  // [TC_NT][2][CS][TC_BM]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int4 tile = tiles[blockIdx.x];
@@ -246,11 +256,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int i = 0; i < TC_NT; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
-      mbar_init(&s_free[i], 4);
-      mbar_init(&p_half[i], 4);
+      mbar_init(&p_full[i], 4 * CS);
     }
-    mbar_init(q_full, 4 * TC_NT);
+    for (int i = 0; i < 4 * TC_NT; ++i) mbar_init(&x_bar[i], 64);  // both halves' 32 threads
+    mbar_init(q_full, 4 * TC_NT * CS);
     mbar_init(o_full, 1);
     fence_mbar_init();
   }
@@ -261,7 +270,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(TC_REGS_CTRL));
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Cfg::REGS_CTRL));
     if (warp == 0) {
       // ------------------------------------------------------------ producer
       // The whole warp: lane p owns page p of a block (page_size >= 4, so a
@@ -318,84 +327,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         constexpr uint32_t idesc_pv = umma_idesc_bf16_f32(TC_BM, TC_D) | (1u << 16);  // B (V) MN-major
         bool ok = mbar_wait(q_full, 0, err, kErrTmaFullTimeout);
         tc_fence_after();
-        // O_t += P_t(i) V_i (P from TMEM columns [128t, 128t + 64)).
-        auto issue_pv = [&](int t, int i) {
-          const uint32_t vbase = smem_u32(sV + (i % TC_VS) * TC_KV_BYTES);
-#pragma unroll
-          for (int k = 0; k < TC_BN / 16; ++k) {
-            const uint64_t bd = umma_desc_sw128_mnmajor(vbase + k * 16 * 128, TC_KV_HALF, 1024);
-            umma_bf16_ts(tmem + 256 + 128 * t, tmem + 128 * t + 8 * k, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
-          }
-        };
-        // PIPE: S_t(j) = Q_t K_j^T in two N = 64 halves.  P_t(j-1) occupies
-        // only TMEM columns [128t, 128t + 64), so the upper half (keys
-        // 64..127 -> columns [128t + 64, 128t + 128)) is issued as soon as the
-        // softmax has read S_t(j-1) into registers (s_free), and runs while
-        // that softmax computes.  PV_t(j-1) goes in two K halves: keys 0..63
-        // after p_half, 64..127 after p_full; then the lower half of S_t(j).
-        constexpr uint32_t idesc_s64 = umma_idesc_bf16_f32(TC_BM, 64);
         // Descriptors advance by adding byte offsets / 16 to their address
         // field (shared addresses stay below 256 KB, so it never carries).
         const uint64_t q_desc0 = umma_desc_sw128_kmajor(smem_u32(sQ));
         const uint64_t k_desc0 = umma_desc_sw128_kmajor(smem_u32(sK));
         const uint64_t v_desc0 = umma_desc_sw128_mnmajor(smem_u32(sV), TC_KV_HALF, 1024);
-        auto issue_s_half = [&](int t, int sk, int hi) {
-          const uint64_t qd = q_desc0 + (uint64_t)((t * TC_Q_BYTES) >> 4);
-          const uint64_t kd = k_desc0 + (uint64_t)((sk * TC_KV_BYTES + hi * 64 * 128) >> 4);
-#pragma unroll
-          for (int k = 0; k < TC_D / 16; ++k) {
-            const uint32_t off = ((k >> 2) * TC_Q_HALF + (k & 3) * 32) >> 4;  // TC_Q_HALF == TC_KV_HALF
-            umma_bf16(tmem + 128 * t + 64 * hi, qd + off, kd + off, idesc_s64, k > 0 ? 1u : 0u);
-          }
-        };
-        auto issue_pv_half = [&](int t, int i, int h) {
+        // O_t += P_t(i) V_i (P from TMEM columns [128t, 128t + 64)).
+        auto issue_pv = [&](int t, int i) {
           const uint64_t vd = v_desc0 + (uint64_t)(((i % TC_VS) * TC_KV_BYTES) >> 4);
 #pragma unroll
-          for (int k = 4 * h; k < 4 * h + 4; ++k)
+          for (int k = 0; k < TC_BN / 16; ++k)
             umma_bf16_ts(tmem + 256 + 128 * t, tmem + 128 * t + 8 * k, vd + (uint64_t)((k * 16 * 128) >> 4), idesc_pv,
                          (i > 0 || k > 0) ? 1u : 0u);
         };
-        // PV_t(i) of block i in its two halves (waits: p_half, V_i, p_full)
-        auto pv_pipe = [&](int t, int i) -> bool {
-          if (!mbar_wait(&p_half[t], i & 1, err, kErrTmemFullTimeout)) return false;
-          if (t == 0 && !mbar_wait(&v_full[i % TC_VS], (i / TC_VS) & 1, err, kErrTmaFullTimeout)) return false;
-          tc_fence_after();
-          issue_pv_half(t, i, 0);
-          if (!mbar_wait(&p_full[t], i & 1, err, kErrTmemFullTimeout)) return false;
-          TC_TR(i + 1, 7 + t);
-          tc_fence_after();
-          issue_pv_half(t, i, 1);
-          return true;
-        };
-        for (int j = 0; PIPE && j < nb && ok; ++j) {
+        for (int j = 0; j < nb && ok; ++j) {
           const int sk = j % TC_KS;
-#pragma unroll
-          for (int t = 0; t < TC_NT; ++t) {
-            if (j > 0 && !mbar_wait(&s_free[t], (j - 1) & 1, err, kErrTmemFullTimeout)) { ok = false; break; }
-            if (t == 0) {
-              if (!mbar_wait(&k_full[sk], (j / TC_KS) & 1, err, kErrTmaFullTimeout)) { ok = false; break; }
-              TC_TR(j, 6);
-            }
-            tc_fence_after();
-            issue_s_half(t, sk, 1);
-            if (j > 0) {
-              if (!pv_pipe(t, j - 1)) { ok = false; break; }
-              if (t == TC_NT - 1) umma_commit(&v_empty[(j - 1) % TC_VS]);
-            }
-            issue_s_half(t, sk, 0);
-            umma_commit(&s_full[t]);
-            TC_TR(j, 9 + t);
-          }
-          if (!ok) break;
-          umma_commit(&k_empty[sk]);
-        }
-        if (PIPE && ok) {
-          for (int t = 0; t < TC_NT && ok; ++t) ok = pv_pipe(t, nb - 1);
-          if (ok) umma_commit(&v_empty[(nb - 1) % TC_VS]);
-        }
-        for (int j = 0; !PIPE && j < nb && ok; ++j) {
-          const int sk = j % TC_KS;
-          const uint32_t kbase = smem_u32(sK + sk * TC_KV_BYTES);
+          const uint64_t kd = k_desc0 + (uint64_t)((sk * TC_KV_BYTES) >> 4);
 #pragma unroll
           for (int t = 0; t < TC_NT; ++t) {
             if (j > 0) {
@@ -414,12 +361,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               TC_TR(j, 6);
               tc_fence_after();
             }
-            const uint32_t qbase = smem_u32(sQ + t * TC_Q_BYTES);
+            const uint64_t qd = q_desc0 + (uint64_t)((t * TC_Q_BYTES) >> 4);
 #pragma unroll
             for (int k = 0; k < TC_D / 16; ++k) {
-              const uint64_t ad = umma_desc_sw128_kmajor(qbase + (k >> 2) * TC_Q_HALF + (k & 3) * 32);
-              const uint64_t bd = umma_desc_sw128_kmajor(kbase + (k >> 2) * TC_KV_HALF + (k & 3) * 32);
-              umma_bf16(tmem + 128 * t, ad, bd, idesc_s, k > 0 ? 1u : 0u);
+              const uint32_t off = ((k >> 2) * TC_Q_HALF + (k & 3) * 32) >> 4;  // TC_Q_HALF == TC_KV_HALF
+              umma_bf16(tmem + 128 * t, qd + off, kd + off, idesc_s, k > 0 ? 1u : 0u);
             }
             umma_commit(&s_full[t]);
             TC_TR(j, 9 + t);
@@ -427,7 +373,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           if (!ok) break;
           umma_commit(&k_empty[sk]);
         }
-        if (!PIPE && ok) {
+        if (ok) {
           const int i = nb - 1;
           for (int t = 0; t < TC_NT && ok; ++t) {
             if (!mbar_wait(&p_full[t], i & 1, err, kErrTmemFullTimeout)) { ok = false; break; }
@@ -446,9 +392,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       __syncwarp();
     }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(TC_REGS_SOFTMAX));
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Cfg::REGS_SOFTMAX));
     // ------------------------------------------------------------- softmax
-    const int t = (warp - 4) >> 2;        // tile of this warpgroup
+    const int sg = (warp - 4) >> 2;       // softmax warpgroup
+    const int t = sg / CS;                // tile of this warpgroup
+    const int h = sg % CS;                // its share of the key columns: [h * NC, (h + 1) * NC)
     const int qd = warp & 3;              // TMEM lane quarter of this warp
     const int r = qd * 32 + lane;         // query row of this thread within the tile
     const int pr = row0 + t * TC_BM + r;
@@ -457,13 +405,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int head = hk * g + pr % g;
     const int pos = valid ? q_pos[tok] : -1;
     uint8_t* sQt = sQ + t * TC_Q_BYTES;
-    // Q row -> shared memory (two 128-B halves, 128-B swizzle), then signal.
+    // Q row -> shared memory (two 128-B halves, 128-B swizzle; with CS = 2
+    // each half-thread copies 8 of the row's 16 chunks), then signal.
     {
       const bf16* src = q + ((size_t)tok * Hq + head) * TC_D;
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const int h = c >> 3, cc = c & 7;
-        const uint32_t dst = smem_u32(sQt) + h * TC_Q_HALF + r * 128 + ((cc ^ (r & 7)) << 4);
+      for (int i = 0; i < 16 / CS; ++i) {
+        const int c = h * (16 / CS) + i;
+        const int hh = c >> 3, cc = c & 7;
+        const uint32_t dst = smem_u32(sQt) + hh * TC_Q_HALF + r * 128 + ((cc ^ (r & 7)) << 4);
         cp_async16_tc(dst, valid ? (const void*)(src + c * 8) : (const void*)q, valid);
       }
       asm volatile("cp.async.wait_all;" ::: "memory");
@@ -472,8 +422,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (lane == 0) mbar_arrive(q_full);
     }
     const uint32_t lane_base = tmem + (uint32_t(qd * 32) << 16);
-    const uint32_t s_col = lane_base + 128 * t;
-    const uint32_t o_col = lane_base + 256 + 128 * t;
+    const uint32_t s_col = lane_base + 128 * t + h * NC;        // this thread's S columns
+    const uint32_t p_col = lane_base + 128 * t + h * (NC / 2);  // its P (bf16 pairs)
+    const uint32_t o_col = lane_base + 256 + 128 * t + h * (TC_D / CS);
+    uint64_t* xb = &x_bar[t * 4 + qd];
+    // exchange slot of (tile, parity, half) for this row
+    auto xslot = [&](int par, int hh) -> float* { return xbuf + ((t * 2 + par) * CS + hh) * TC_BM + r; };
+    // Both halves of a row publish a value and read the other's; false when
+    // the (bounded) wait gave up, which it records.
+    auto exchange = [&](int phase, float v, float& other) -> bool {
+      *xslot(phase & 1, h) = v;
+      mbar_arrive(xb);
+      if (!mbar_wait(xb, phase & 1, err, kErrTmemFullTimeout)) return false;
+      other = *xslot(phase & 1, h ^ 1);
+      return true;
+    };
     float m_run = -INFINITY, l_run = 0.f;
     // Blocks before jd are visible to every row of this tile (positions
     // ascend, so the tile's first row has its smallest position) and skip
@@ -485,80 +448,66 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     auto step = [&](int j, auto mask_c) -> bool {
       constexpr bool MASK = decltype(mask_c)::value;
       if (!mbar_wait(&s_full[t], j & 1, err, kErrTmemFullTimeout)) return false;
-      if (r == 0) TC_TR(j, 3 * t);
+      if (r == 0 && h == 0) TC_TR(j, 3 * t);
       tc_fence_after();
-      uint32_t s[TC_BN];
+      uint32_t s[NC];
 #pragma unroll
-      for (int c = 0; c < TC_BN / 32; ++c)
+      for (int c = 0; c < NC / 32; ++c)
         tmem_ld_32x32b_x32(s_col + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&s[32 * c]));
       tmem_ld_wait();
-      if (r == 0) TC_TR(j, 3 * t + 1);
-      if constexpr (PIPE) {  // S_t is in registers: the MMA may overwrite its upper half
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[t]);
-      }
+      if (r == 0 && h == 0) TC_TR(j, 3 * t + 1);
       if (MASK) {
-        const int lim = pos - j * TC_BN;  // scores with index > lim are masked
+        const int lim = pos - j * TC_BN - h * NC;  // scores with index > lim are masked
 #pragma unroll
-        for (int i = 0; i < TC_BN; ++i)
+        for (int i = 0; i < NC; ++i)
           if (i > lim) s[i] = __float_as_uint(-INFINITY);
       }
-      if (r == 0 && t == 0) TC_TR(j, 17);
+      if (r == 0 && t == 0 && h == 0) TC_TR(j, 17);
       float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int i = 0; i < TC_BN; i += 8) {
+      for (int i = 0; i < NC; i += 8) {
 #pragma unroll
         for (int u = 0; u < 4; ++u)
           m4[u] = fmax3(m4[u], __uint_as_float(s[i + 2 * u]), __uint_as_float(s[i + 2 * u + 1]));
       }
-      const float mx = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
-      if (r == 0 && t == 0) TC_TR(j, 11);
+      float mx = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+      if constexpr (CS == 2) {
+        float other;
+        if (!exchange(j, mx, other)) return false;
+        mx = fmaxf(mx, other);
+      }
+      if (r == 0 && t == 0 && h == 0) TC_TR(j, 11);
       const float m_new = fmaxf(m_run, mx * scale_log2);
       const bool grow = m_new > m_run + TC_RESCALE_THRESHOLD;  // false while m_new == -inf
       const float m_use = grow ? m_new : m_run;
       const float o_scale = (grow && m_run != -INFINITY) ? ex2(m_run - m_new) : 1.f;
       const float neg_m = m_use == -INFINITY ? 0.f : -m_use;
-      // A warp that rescales O this block signals p_half only after the
-      // rescale (the MMA must not add P V into O before it).
-      const bool rescale = __any_sync(0xffffffffu, o_scale != 1.f);
-      // P = exp2(S*scale - m) as bf16 pairs over the first 64 columns of S.
+      // P = exp2(S*scale - m) as bf16 pairs over this thread's share of the
+      // first 64 columns of S.
       float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < TC_BN / 32; ++c) {
-        if (PIPE && c == 2 && !rescale) {  // keys 0..63 of P stored: PV may start on them
-          tmem_st_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&p_half[t]);
-        }
+      for (int c = 0; c < NC / 32; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int i0 = 32 * c + 2 * e;
           const float xa = fmaf(__uint_as_float(s[i0]), scale_log2, neg_m);
-          const float xb = fmaf(__uint_as_float(s[i0 + 1]), scale_log2, neg_m);
-          if constexpr (POLY8 == TC_EXP_BF16X2) {
-            const uint32_t pp = ex2_bf16x2(pack_bf16x2(xa, xb));
-            // the row sum adds the bf16 weights the MMA uses
-            sum4[e & 3] += __uint_as_float(pp << 16) + __uint_as_float(pp & 0xffff0000u);
-            pk[e] = pp;
-          } else {
-            const float pa = (i0 & 7) < POLY8 ? exp2_poly(xa) : ex2(xa);
-            const float pb = ((i0 + 1) & 7) < POLY8 ? exp2_poly(xb) : ex2(xb);
-            sum4[e & 3] += pa + pb;
-            pk[e] = ALU_PACK ? pack_bf16x2_alu(pa, pb) : pack_bf16x2(pa, pb);
-          }
+          const float xb2 = fmaf(__uint_as_float(s[i0 + 1]), scale_log2, neg_m);
+          const float pa = (i0 & 7) < POLY8 ? exp2_poly(xa) : ex2(xa);
+          const float pb = ((i0 + 1) & 7) < POLY8 ? exp2_poly(xb2) : ex2(xb2);
+          sum4[e & 3] += pa + pb;
+          pk[e] = ALU_PACK ? pack_bf16x2_alu(pa, pb) : pack_bf16x2(pa, pb);
         }
-        tmem_st_32x32b_x16(s_col + 16 * c, pk);
-        if (r == 0 && t == 0) TC_TR(j, 12 + c);
+        tmem_st_32x32b_x16(p_col + 16 * c, pk);
+        if (r == 0 && t == 0 && h == 0) TC_TR(j, 12 + c);
       }
       const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       // O is stable here: PV of block j-1 was issued before S(j) and the
-      // commit that signalled S(j) covers it.
-      if (rescale) {
+      // commit that signalled S(j) covers it.  Each half rescales its
+      // share of O's columns (both halves see the same row maxima).
+      if (__any_sync(0xffffffffu, o_scale != 1.f)) {
 #pragma unroll 1
-        for (int c = 0; c < TC_D; c += 32) {
+        for (int c = 0; c < TC_D / CS; c += 32) {
           uint32_t o[32];
           tmem_ld_32x32b_x32(o_col + c, o);
           tmem_ld_wait();
@@ -568,16 +517,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
       }
       tmem_st_wait();
-      if (r == 0 && t == 0) TC_TR(j, 16);
+      if (r == 0 && t == 0 && h == 0) TC_TR(j, 16);
       l_run = l_run * o_scale + sum;
       m_run = m_use;
       tc_fence_before();
       __syncwarp();
-      if (r == 0) TC_TR(j, 3 * t + 2);
-      if (lane == 0) {
-        if (PIPE && rescale) mbar_arrive(&p_half[t]);
-        mbar_arrive(&p_full[t]);
-      }
+      if (r == 0 && h == 0) TC_TR(j, 3 * t + 2);
+      if (lane == 0) mbar_arrive(&p_full[t]);
       return true;
     };
     bool ok = true;
@@ -586,11 +532,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     for (; j < nb && ok; ++j) ok = step(j, std::true_type{});
     // ----------------------------------------------------------- epilogue
     if (ok && mbar_wait(o_full, 0, err, kErrTmemFullTimeout)) {
+      float l_tot = l_run;
+      if constexpr (CS == 2) {
+        float other = 0.f;
+        ok = exchange(nb, l_run, other);  // the row sum is the two halves' sums
+        l_tot += other;
+      }
       tc_fence_after();
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      bf16* dst = out + ((size_t)tok * Hq + head) * TC_D;
+      const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+      bf16* dst = out + ((size_t)tok * Hq + head) * TC_D + h * (TC_D / CS);
 #pragma unroll 1
-      for (int c = 0; c < TC_D; c += 32) {
+      for (int c = 0; c < TC_D / CS && ok; c += 32) {
         uint32_t o[32];
         tmem_ld_32x32b_x32(o_col + c, o);
         tmem_ld_wait();
@@ -662,24 +614,22 @@ static int make_pool_run_map(CUtensorMap* tm, const void* base, int L, int pages
 
 typedef void (*Kern)(CUtensorMap, CUtensorMap, const bf16*, const int*, const int*, const int*, int, const int4*,
                      bf16*, int, int, int, int, float, int*);
-// (POLY8, ALU_PACK) variants; LL_ATTN_VARIANT=<index> selects one.
-// 7: packed bf16x2 exp2; 9, 10: the S/PV pipeline (PIPE) with fp32 and
-// packed exp2; 6, 8, 11, 12: the clock64() trace builds of 0, 7, 9, 10.
-constexpr int kNumVariants = 13;
-static const Kern kVariants[kNumVariants] = {
-    attn_prefill_tc_kernel<0, false>,
-    attn_prefill_tc_kernel<0, true>,
-    attn_prefill_tc_kernel<2, true>,
-    attn_prefill_tc_kernel<3, true>,
-    attn_prefill_tc_kernel<4, true>,
-    attn_prefill_tc_kernel<2, false>,
-    attn_prefill_tc_kernel<0, false, true>,
-    attn_prefill_tc_kernel<TC_EXP_BF16X2, false>,
-    attn_prefill_tc_kernel<TC_EXP_BF16X2, false, true>,
-    attn_prefill_tc_kernel<0, false, false, true>,
-    attn_prefill_tc_kernel<TC_EXP_BF16X2, false, false, true>,
-    attn_prefill_tc_kernel<0, false, true, true>,
-    attn_prefill_tc_kernel<TC_EXP_BF16X2, false, true, true>};
+// Builds of the kernel, LL_ATTN_VARIANT=<index> selects one:
+//   0  CS = 1, exp2 on MUFU        3  CS = 2, exp2 on MUFU
+//   1  CS = 1, bf16 pack on ALU    4  CS = 2, 2 of 8 exp2 on the FMA pipe
+//   2  CS = 1, 2 of 8 exp2 on FMA  5, 6  clock64() trace builds of 0 and 3
+struct TcBuild {
+  Kern kern;
+  int threads, smem;
+};
+template <int CS, int POLY8, bool ALU_PACK, bool TRACE = false>
+constexpr TcBuild tc_build() {
+  return {attn_prefill_tc_kernel<CS, POLY8, ALU_PACK, TRACE>, TcCfg<CS>::THREADS, TcCfg<CS>::SMEM};
+}
+constexpr int kNumVariants = 7;
+static const TcBuild kVariants[kNumVariants] = {
+    tc_build<1, 0, false>(),       tc_build<1, 0, true>(),  tc_build<1, 2, true>(), tc_build<2, 0, false>(),
+    tc_build<2, 2, true>(),        tc_build<1, 0, false, true>(), tc_build<2, 0, false, true>()};
 constexpr int kDefaultVariant = 0;
 
 static int g_attn_variant = -1;
@@ -1069,21 +1019,22 @@ extern "C" int ll_attn_prefill_tc(const bf16* q, const bf16* k_pool, const bf16*
   if (make_pool_map(&tk, k_pool, L, pages, Hkv, page_size)) return -2;
   if (make_pool_map(&tv, v_pool, L, pages, Hkv, page_size)) return -2;
   const int v = attn_tc_variant();
-  Kern kern = kVariants[v];
+  const TcBuild& bd = kVariants[v];
+  Kern kern = bd.kern;
   // A launch whose registers or shared memory cannot fit one CTA on an SM is
   // refused here: such launches crashed the host process inside the driver
   // instead of returning an error.
   static int fits[kNumVariants] = {};  // 0: not checked yet, 1: fits, 2: refused
   if (fits[v] == 0) {
     int n = 0;
-    fits[v] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) == cudaSuccess &&
-                      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, TC_THREADS, TC_SMEM) == cudaSuccess &&
+    fits[v] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bd.smem) == cudaSuccess &&
+                      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, bd.threads, bd.smem) == cudaSuccess &&
                       n >= 1
                   ? 1
                   : 2;
   }
   if (fits[v] != 1) return -7;
-  kern<<<ntiles, TC_THREADS, TC_SMEM, stream>>>(tk, tv, q, q_indptr, q_pos, page_table, pt_stride,
+  kern<<<ntiles, bd.threads, bd.smem, stream>>>(tk, tv, q, q_indptr, q_pos, page_table, pt_stride,
                                                 reinterpret_cast<const int4*>(tiles), out, Hq, Hkv, page_size, layer,
                                                 scale * 1.4426950408889634f, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;

@@ -457,17 +457,27 @@ class Engine:
         """Copy whole pages (all layers, K and V) into fresh pages and release
         the originals (checklist K15)."""
         new = self._alloc_pages(len(pages))
-        src = torch.as_tensor(pages, dtype=torch.long, device=self.kv.k.device)
-        dst = torch.as_tensor(new, dtype=torch.long, device=self.kv.k.device)
-        self.kv.k[:, dst] = self.kv.k[:, src]
-        self.kv.v[:, dst] = self.kv.v[:, src]
+        try:
+            src = torch.as_tensor(pages, dtype=torch.long, device=self.kv.k.device)
+            dst = torch.as_tensor(new, dtype=torch.long, device=self.kv.k.device)
+            self.kv.k[:, dst] = self.kv.k[:, src]
+            self.kv.v[:, dst] = self.kv.v[:, src]
+        except Exception:
+            self.alloc.release(new)
+            raise
         self.alloc.release(pages)
         return new
 
     def _compile_register(self, toks, cache_key: str, ckey, bid: str, pages, first: int) -> dict:
         n = len(toks)
-        status = self.registry.register_block(str(cache_key), ckey, physical_token_ids_sha256(toks), toks, pages, 0,
-                                              bid)
+        try:
+            status = self.registry.register_block(str(cache_key), ckey, physical_token_ids_sha256(toks), toks, pages,
+                                                  0, bid)
+        except Exception:
+            # refused (the key names a block with other content): the
+            # registry took nothing, the computed pages go back
+            self.alloc.release(pages)
+            raise
         self.stats["compiles"] += 1
         if self._dir is not None and status == "registered":
             from ..parallel.dp import RemoteBlock
@@ -719,7 +729,11 @@ class Engine:
             for (i, toks, ckey, bid, key, pages), first in zip(prepared, firsts):
                 try:
                     if self.storage_mode(compiles[i][2] if len(compiles[i]) > 2 else None) == "clone":
-                        pages = self._clone_pages(pages)
+                        try:
+                            pages = self._clone_pages(pages)
+                        except Exception:
+                            self.alloc.release(pages)  # no copy: the computed pages go back
+                            raise
                     c_out[i] = self._compile_register(toks, key, ckey, bid, pages, int(first))
                 except Exception as e:  # noqa: BLE001
                     c_out[i] = e

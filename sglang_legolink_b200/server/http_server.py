@@ -40,6 +40,26 @@ from ..runtime.scheduler import Request, RequestRejected, Scheduler
 from ..runtime.sampling import SamplingParams
 
 
+def asks_input_logprobs(payload: dict) -> bool:
+    """Whether a request asks for log-probabilities of its INPUT tokens: the
+    OpenAI completions form (``echo`` with ``logprobs``), an explicit
+    ``input_logprobs``, or the native form (``return_logprob`` with a
+    ``logprob_start_len`` >= 0; -1, the default, asks for output tokens
+    only).  A Link's input rows are linked, not computed, so it has none
+    (reference ``tests/test_security_l1_link_input_logprobs.py``)."""
+    if payload.get("input_logprobs"):
+        return True
+    if payload.get("echo") and payload.get("logprobs"):
+        return True
+    start = payload.get("logprob_start_len")
+    if payload.get("return_logprob") and start is not None:
+        try:
+            return int(start) >= 0
+        except (TypeError, ValueError):
+            return True  # unreadable: treated as asking
+    return False
+
+
 def _prompt_ids(tokenizer, payload: dict) -> list[int]:
     msgs = payload.get("messages") or []
     return list(tokenizer.tokenize_messages(msgs, tools=payload.get("tools"),
@@ -65,8 +85,8 @@ class RuntimeService:
         sc, link = copy.deepcopy(payload.get("sub_context")), copy.deepcopy(payload.get("pic_link"))
         if sc is not None and link is not None:
             raise RequestRejected("a request is either a Compile (sub_context) or a Link (pic_link), not both")
-        if link is not None and (payload.get("logprobs") and payload.get("echo") or payload.get("input_logprobs")):
-            raise RequestRejected("a Link may not request input logprobs")
+        if link is not None and asks_input_logprobs(payload):
+            raise RequestRejected("a Link may not request input logprobs: its input rows are linked, not computed")
         max_new = int(payload.get("max_tokens") or payload.get("max_completion_tokens") or 16)
         stop = (self.eos,) if (self.eos is not None and not payload.get("ignore_eos")) else ()
         stop = stop + tuple(int(t) for t in (payload.get("stop_token_ids") or ()))

@@ -34,7 +34,7 @@ def _norm(x, w, eps=1e-6):
 def test_prefill_boundary_emulated_world(W):
     torch.manual_seed(W)
     ext, err = ops._cuda(), ops.workspace(DEV).err
-    R, H, K, N2 = 64, 1024, 512, 768
+    R, H, K, N2 = 128, 1024, 512, 768  # T = W x R >= 512, the fused path's minimum
     T = W * R
     a = [(torch.randn(T, K, device=DEV) * 0.5).to(torch.bfloat16) for _ in range(W)]   # rank r's activations
     wo = [(torch.randn(H, K, device=DEV) / 16).to(torch.bfloat16) for _ in range(W)]   # rank r's K-slice of o_proj
