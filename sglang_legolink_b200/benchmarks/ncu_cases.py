@@ -1,7 +1,7 @@
 """Small single-kernel cases sized for `ncu --set full` captures (a few
 launches, a few hundred MB on the device), one per hot kernel:
 
-    python -m sglang_legolink_b200.benchmarks.ncu_cases {gemm,gemm_link,gemm_link_cublas,attn,gemv,gemv_residual,decode,link,rmsnorm,rope_qkv,tp_reduce,tp_scatter}
+    python -m sglang_legolink_b200.benchmarks.ncu_cases {gemm,gemm_link,gemm_link_cublas,attn,gemv,gemv_residual,decode,link,rmsnorm,rope_qkv,tp_reduce,tp_scatter,tp_decode}
 """
 import sys, os, math
 
@@ -106,6 +106,24 @@ elif case in ("tp_reduce", "tp_scatter"):  # fused-TP kernels on one GPU: both "
         a = (torch.randn(T, K, device="cuda") * 0.5).to(torch.bfloat16)
         w = (torch.randn(H, K, device="cuda") / 64).to(torch.bfloat16)
         for _ in range(4): ext.gemm_tp(a, w, None, None, 2, H, sp, cp, 0, 0, 0, W, R, err)
+elif case == "tp_decode":  # decode TP boundary (one-shot all-reduce + residual + RMSNorm), world 2 on one GPU
+    # Both "ranks'" partial rows are local.  This process plays rank 0; before
+    # each call the host adds 1 to rank 0's arrival counter for the other
+    # rank, so the kernel's own arrival completes its wait (nothing waits on
+    # another launch).
+    W, rows, H = 2, 16, 5120
+    err = ops.workspace("cuda").err
+    ext = ops._cuda()
+    parts = [torch.randn(rows, H, device="cuda").to(torch.bfloat16) for _ in range(W)]
+    res = torch.randn(rows, H, device="cuda").to(torch.bfloat16)
+    w = torch.ones(H, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(rows, H, device="cuda", dtype=torch.bfloat16)
+    cnt = [torch.zeros(2, device="cuda", dtype=torch.int64) for _ in range(W)]
+    epoch = torch.zeros(2, device="cuda", dtype=torch.int64)
+    for _ in range(4):
+        cnt[0][0] += W - 1
+        ext.tp_decode_allreduce_norm(res, w, out, 1e-6, rows, [p.data_ptr() for p in parts],
+                                     [c.data_ptr() for c in cnt], epoch, 0, W, err)
 elif case == "decode_step":  # Qwen2.5-7B, 16K context, eager decode steps (launch lists only: full size)
     from sglang_legolink_b200.models.config import PRESETS
     from sglang_legolink_b200.models.qwen import QwenModel

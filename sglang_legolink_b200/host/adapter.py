@@ -30,8 +30,8 @@ from enum import Enum
 from typing import Any, Callable, Hashable, Optional
 
 from ..contract import PIC_LINK_RUNTIME_OWNED_FIELDS, parse_residency_recovery
-from .framing import (ChatTokenLayout, RepairDecision, RepairWindowPlanner, Stitcher, StitchedContext, build_layout,
-                      compile_payload, frame_link, framing_spec_for)
+from .framing import (ChatTokenLayout, RepairDecision, RepairWindowPlanner, Stitcher, StitchedContext,
+                      UniformRepairWindow, build_layout, compile_payload, frame_link, framing_spec_for)
 from .manager import ContextManager
 from .token_reuse import RequestTokenSource, SharedTokenCache, host_token_reuse_enabled
 from .planner import CacheCatalog, ExecutionPlan, Planner
@@ -416,3 +416,25 @@ class RequestPipeline:
         tm["link"] = (time.perf_counter() - t) * 1e3
         return PipelineExecution(route, res, plan, stitched, layout, nc + res.compile_requests,
                                  cdt + res.compile_latency_s, tm)
+
+
+def make_pipeline(transport: Callable[[dict], dict], *, task_id: str, model: str = "legolink", tokenizer=None,
+                  catalog: Optional[CacheCatalog] = None, coordinator: Optional[ResidencyRecoveryCoordinator] = None,
+                  namespace_mode="global", cross_namespace_pairs=(), resolver=None, repair_tokens: int = 16,
+                  generation: Optional[dict] = None) -> RequestPipeline:
+    """One agent session's pipeline.  Sessions that talk to one runtime
+    should share ``catalog`` (one host view of the runtime's blocks, which
+    the namespace resolver reads across tasks) and ``coordinator``.
+    ``namespace_mode`` / ``cross_namespace_pairs`` are validated here, at
+    construction (reference ``cache_namespace.py:502``); a ``resolver``
+    built once may be passed instead."""
+    from .namespaces import NamespacePolicy, NamespaceResolver
+
+    if resolver is None:
+        resolver = NamespaceResolver(namespace_mode, NamespacePolicy(cross_namespace_pairs=list(cross_namespace_pairs)))
+    cm = ContextManager(task_id, tokenizer=tokenizer) if tokenizer is not None else ContextManager(task_id)
+    catalog = catalog if catalog is not None else CacheCatalog()
+    ad = RuntimeAdapter(transport, model=model, tokenizer=cm.tokenizer, catalog=catalog, coordinator=coordinator,
+                        repair_planner=RepairWindowPlanner(UniformRepairWindow(repair_tokens)), generation=generation)
+    return RequestPipeline(cm, ad, planner=Planner(catalog=catalog, resolver=resolver))
+

@@ -33,11 +33,11 @@ import uuid
 from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
 from typing import Callable, Optional
 
-from ..host.adapter import RequestPipeline, RuntimeAdapter
+from ..host.adapter import ResidencyRecoveryCoordinator, make_pipeline
 from ..host.agent import AgentLLM
-from ..host.framing import RepairWindowPlanner, UniformRepairWindow
-from ..host.manager import ContextManager
 from ..host.metrics import MetricsRecorder
+from ..host.namespaces import NamespacePolicy, NamespaceResolver
+from ..host.planner import CacheCatalog
 
 
 def conversation_key(messages: list) -> str:
@@ -110,11 +110,17 @@ JSON_REPAIR_INSTRUCTION = ("Your previous reply was not valid JSON. Reply again 
 class LegoLinkProxy:
     def __init__(self, transport, *, model: str = "legolink", tokenizer=None, repair_tokens: int = 16,
                  metrics_path: Optional[str] = None, passthrough: bool = False, json_retries: int = 2,
-                 session_ttl_s: float = 3600.0):
+                 session_ttl_s: float = 3600.0, namespace_mode: str = "global", cross_namespace_pairs=()):
         self.transport = transport
         self.model = model
         self.tokenizer = tokenizer
         self.repair_tokens = repair_tokens
+        # one view of the runtime's blocks for every session (the namespace
+        # resolver reads it across tasks); the mode is checked here
+        self.resolver = NamespaceResolver(namespace_mode,
+                                          NamespacePolicy(cross_namespace_pairs=list(cross_namespace_pairs)))
+        self.catalog = CacheCatalog()
+        self.coordinator = ResidencyRecoveryCoordinator()
         self.recorder = MetricsRecorder(metrics_path) if metrics_path else None
         self.passthrough = passthrough
         self.json_retries = json_retries
@@ -122,10 +128,10 @@ class LegoLinkProxy:
         self.stats = {"requests": 0, "json_retries": 0, "passthrough": 0}
 
     def _new_session(self, key: str) -> AgentLLM:
-        cm = ContextManager(key, tokenizer=self.tokenizer) if self.tokenizer is not None else ContextManager(key)
-        ad = RuntimeAdapter(self.transport, model=self.model, tokenizer=cm.tokenizer,
-                            repair_planner=RepairWindowPlanner(UniformRepairWindow(self.repair_tokens)))
-        return AgentLLM(RequestPipeline(cm, ad), task_id=key, recorder=self.recorder)
+        pipe = make_pipeline(self.transport, task_id=key, model=self.model, tokenizer=self.tokenizer,
+                             catalog=self.catalog, coordinator=self.coordinator, resolver=self.resolver,
+                             repair_tokens=self.repair_tokens)
+        return AgentLLM(pipe, task_id=key, recorder=self.recorder)
 
     def session_key(self, payload: dict, headers: Optional[dict] = None) -> str:
         explicit = payload.get("session_id") or (headers or {}).get("X-Session-Id")
@@ -224,12 +230,18 @@ def main():
     ap.add_argument("--metrics", default=None, help="metrics JSONL path")
     ap.add_argument("--passthrough", action="store_true", help="control arm: forward requests unchanged")
     ap.add_argument("--json-retries", type=int, default=2)
+    ap.add_argument("--semantic-cache-namespace-mode", default="global",
+                    choices=["global", "hard_namespace", "logical_namespace"])
+    ap.add_argument("--cross-namespace-pairs", default="",
+                    help="logical mode: comma-separated requester->serving root pairs, e.g. workspace<->tool_output")
     a = ap.parse_args()
     from ..host.tokenizer import RuntimeTokenizer
 
     transport = JSONHTTPTransport(a.runtime)
     proxy = LegoLinkProxy(transport, tokenizer=RuntimeTokenizer(a.runtime), repair_tokens=a.repair_tokens,
-                          metrics_path=a.metrics, passthrough=a.passthrough, json_retries=a.json_retries)
+                          metrics_path=a.metrics, passthrough=a.passthrough, json_retries=a.json_retries,
+                          namespace_mode=a.semantic_cache_namespace_mode,
+                          cross_namespace_pairs=[x for x in a.cross_namespace_pairs.split(",") if x.strip()])
     srv = ThreadingHTTPServer((a.host, a.port), make_handler(proxy))
     print(f"LegoLink proxy on http://{a.host}:{a.port} -> {a.runtime}", flush=True)
     srv.serve_forever()

@@ -166,3 +166,40 @@ def test_the_host_keeps_one_physical_cache_and_the_index_is_a_view_over_it():
     assert primaries <= set(rig.compiles())  # every primary name is a compiled block, none is a copy
     assert len(names) >= len(primaries)
     assert snap["aliases_recorded"] >= 1
+
+
+def test_the_proxy_forwards_the_namespace_mode_and_shares_one_catalog():
+    from sglang_legolink_b200.server.proxy import LegoLinkProxy
+
+    with pytest.raises(ValueError):
+        LegoLinkProxy(StrictFakeRuntime(), tokenizer=TOK, namespace_mode="hard")
+    rt = StrictFakeRuntime()
+    proxy = LegoLinkProxy(rt, tokenizer=TOK, namespace_mode="hard_namespace")
+    a, _ = proxy.sessions.get("s-a")
+    b, _ = proxy.sessions.get("s-b")
+    for agent in (a, b):
+        planner = agent.pipeline.planner
+        assert planner.resolver is proxy.resolver and planner.catalog is proxy.catalog
+        assert agent.pipeline.adapter.catalog is proxy.catalog
+    msgs = [{"role": "system", "content": SYS}, {"role": "user", "content": "why does charge double-bill?"}]
+    r = proxy.chat_completion({"messages": msgs, "session_id": "s-a"})
+    assert r["legolink"]["session"] == "s-a"
+    row = a.pipeline.planner.resolver.describe()
+    assert row["semantic_cache_namespace_mode"] == "hard_namespace"
+    n = len([q for q in rt.requests if q.get("sub_context")])
+    proxy.chat_completion({"messages": msgs, "session_id": "s-b"})  # the shared instruction is not compiled again
+    assert len([q for q in rt.requests if q.get("sub_context")]) == n
+
+
+def test_make_pipeline_validates_the_mode_and_pairs():
+    from sglang_legolink_b200.host.adapter import make_pipeline
+
+    with pytest.raises(ValueError):
+        make_pipeline(StrictFakeRuntime(), task_id="t", tokenizer=TOK, namespace_mode="logical")
+    with pytest.raises(ValueError):
+        make_pipeline(StrictFakeRuntime(), task_id="t", tokenizer=TOK, namespace_mode="logical_namespace",
+                      cross_namespace_pairs=["workspace->nowhere"])
+    p = make_pipeline(StrictFakeRuntime(), task_id="t", tokenizer=TOK, namespace_mode="logical_namespace",
+                      cross_namespace_pairs=["workspace<->tool_output"])
+    assert p.planner.resolver.describe()["cross_namespace_pairs"] == ["tool_output->workspace",
+                                                                      "workspace->tool_output"]
