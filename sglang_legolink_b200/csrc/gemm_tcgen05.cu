@@ -710,6 +710,31 @@ __device__ __forceinline__ void umma_commit_2sm_local(uint64_t* bar) {
                : "memory");
 }
 
+// Bulk tensor store of a shared-memory box to global memory (bulk-group
+// completion), and the waits on this thread's outstanding groups.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_group_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// One warp's 32-row x 64-byte box of C (32 bf16 columns per row) staged for
+// a bulk tensor store: lane = row, `v` its 16 packed bf16 pairs; 16-byte chunk
+// k of row r lands at chunk k ^ ((r >> 1) & 3) (the 64-byte swizzle the
+// store's tensor map names), so the four st.shared.v4 of a quarter-warp hit
+// distinct banks.
+__device__ __forceinline__ void epi_stage_row64(uint8_t* box, int lane, const uint32_t (&v)[16]) {
+  uint4* row = reinterpret_cast<uint4*>(box + lane * 64);
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    row[k ^ ((lane >> 1) & 3)] = make_uint4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+}
+
 template <int EPI>
 __device__ __forceinline__ void epi_store_chunk(const uint32_t (&r)[32], bf16* __restrict__ C,
                                                 const bf16* __restrict__ bias, int row, int col0, int M, int N,
@@ -766,21 +791,25 @@ struct Gemm2Cfg {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;       // this CTA's 128 rows of A
   static constexpr int B_BYTES = (BN / 2) * GEMM_BK * 2;      // this CTA's half of the B tile
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + 1024 + 256;
+  // epilogue staging: 4 warps x 2 buffers x one 32-row x 64-byte box
+  static constexpr int EPI_BYTES = 4 * 2 * 32 * 64;
+  static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + EPI_BYTES + 1024 + 256;
 };
 
 template <int BN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     gemm_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                            bf16* __restrict__ C, const bf16* __restrict__ bias, int M, int N, int K, int ldc,
-                            int* err, const __grid_constant__ TpArgs tp) {
+                            const __grid_constant__ CUtensorMap tmC, int c_bulk, bf16* __restrict__ C,
+                            const bf16* __restrict__ bias, int M, int N, int K, int ldc, int* err,
+                            const __grid_constant__ TpArgs tp) {
   using Cfg = Gemm2Cfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint8_t* sEpi = sB + STAGES * Cfg::B_BYTES;  // [4 warps][2][32 rows x 64 B], 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + Cfg::EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -902,6 +931,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     // kEpiScatter: slices stored per owner rank, published once at the end
     // (one system fence per warp instead of one per tile).
     uint32_t sent[LL_MAX_TP_RANKS] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int nbox = 0;  // bulk-stored boxes of this warp (c_bulk)
     for (int t = pair; t < ntiles; t += npairs) {
       int mb, nb;
         tile_coords(t, num_m, num_n, mb, nb);
@@ -951,6 +981,67 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
 #pragma unroll
           for (int i = 0; i < LL_MAX_TP_RANKS; ++i) sent[i] += (i == d) ? 1u : 0u;
         }
+      } else if (c_bulk) {
+        // TMEM -> registers (bias, SwiGLU, bf16) -> a swizzled 32 x 64-byte
+        // box in shared memory -> one bulk tensor store per box, issued by
+        // lane 0: every global write is a whole 64-byte row segment instead
+        // of 16 bytes of 32 different rows.  The warp alternates two boxes
+        // and reuses one once the store before last has read it.  Rows past
+        // M and columns past N are clipped by the store.
+        uint8_t* boxes = sEpi + q * 2 * 2048;
+        const int row0w = mb * 2 * GEMM_BM + (int)crank * GEMM_BM + q * 32;
+        constexpr int STEP = EPI == kEpiSwiGLU ? 64 : 32;  // accumulator columns per box
+#pragma unroll 1
+        for (int c = 0; c < BN; c += STEP) {
+          const int col0 = nb * BN + c;
+          uint32_t v[16];
+          if constexpr (EPI == kEpiSwiGLU) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              uint32_t r[32];
+              tmem_ld_32x32b_x32(tbase + c + 32 * hh, r);
+              tmem_ld_wait();
+              const int cb = col0 + 32 * hh;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                float g0 = __uint_as_float(r[2 * i]), g1 = __uint_as_float(r[2 * i + 1]);
+                float u0 = __uint_as_float(r[16 + 2 * i]), u1 = __uint_as_float(r[16 + 2 * i + 1]);
+                if (bias != nullptr && cb < N) {  // N % 32 == 0: a 32-column group is wholly in or out
+                  g0 += __bfloat162float(bias[cb + 2 * i]);
+                  g1 += __bfloat162float(bias[cb + 2 * i + 1]);
+                  u0 += __bfloat162float(bias[cb + 16 + 2 * i]);
+                  u1 += __bfloat162float(bias[cb + 16 + 2 * i + 1]);
+                }
+                v[8 * hh + i] = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
+              }
+            }
+          } else {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tbase + c, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float a0 = __uint_as_float(r[2 * i]), a1 = __uint_as_float(r[2 * i + 1]);
+              if (bias != nullptr) {
+                if (col0 + 2 * i < N) a0 += __bfloat162float(bias[col0 + 2 * i]);
+                if (col0 + 2 * i + 1 < N) a1 += __bfloat162float(bias[col0 + 2 * i + 1]);
+              }
+              v[i] = pack_bf16x2(a0, a1);
+            }
+          }
+          if (col0 >= N || row0w >= M) continue;  // warp-uniform: the box is wholly outside C
+          uint8_t* box = boxes + (nbox & 1) * 2048;
+          if (nbox >= 2 && lane == 0) bulk_wait_group_read1();
+          __syncwarp();
+          epi_stage_row64(box, lane, v);
+          fence_proxy_async();  // this lane's shared writes -> the bulk copy (async proxy)
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, box, EPI == kEpiSwiGLU ? col0 / 2 : col0, row0w);
+            bulk_commit_group();
+          }
+          ++nbox;
+        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
@@ -968,6 +1059,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         aphase ^= 1;
       }
     }
+    if (lane == 0 && nbox > 0) bulk_wait_group0();  // this warp's bulk stores are complete
     if constexpr (EPI == kEpiScatter) {
       __threadfence_system();  // this lane's peer stores are visible system-wide
       __syncwarp();
@@ -1023,6 +1115,35 @@ static int make_tmap_2d(CUtensorMap* tm, const void* ptr, int rows, int cols, in
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
+// Store map of C for the bulk-store epilogue: box of 32 rows x 32 bf16
+// columns (64 bytes) with the 64-byte swizzle.  Returns 0 when C qualifies
+// (16-byte aligned base and row pitch).
+static int make_tmap_c(CUtensorMap* tm, const void* ptr, int rows, int cols, int ld) {
+  if (ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & 15) || (ld % 8)) return -3;
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return -1;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+// Bulk-store epilogue: LL_GEMM_BULK_STORE=1 selects it, 0 the per-thread
+// stores; unset: kGemmBulkStoreDefault.
+constexpr int kGemmBulkStoreDefault = 0;
+static bool gemm_bulk_store_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("LL_GEMM_BULK_STORE");
+    v = e != nullptr && e[0] != '\0' ? (e[0] == '0' ? 0 : 1) : kGemmBulkStoreDefault;
+  }
+  return v == 1;
+}
+
 static int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -1066,6 +1187,10 @@ extern "C" int ll_gemm_bf16(const bf16* A, int lda, const bf16* W, int ldw, bf16
     if (make_tmap_2d(&tB, W, N, K, ldw, BN / 2)) return -2;
     const int ntiles2 = ((M + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * ((N + BN - 1) / BN);
     const int pairs = ntiles2 < num_sms() / 2 ? ntiles2 : num_sms() / 2;
+    CUtensorMap tC;
+    const int c_bulk = gemm_bulk_store_enabled() &&
+                       make_tmap_c(&tC, C, M, epilogue == kEpiSwiGLU ? N / 2 : N, ldc) == 0;
+    if (!c_bulk) tC = tA;  // not read
 #define LL_LAUNCH2(EPI_)                                                                              \
   do {                                                                                                \
     auto kern = gemm_tcgen05_2sm_kernel<256, EPI_>;                                                   \
@@ -1075,7 +1200,8 @@ extern "C" int ll_gemm_bf16(const bf16* A, int lda, const bf16* W, int ldw, bf16
       set_smem(kern, Gemm2Cfg<256>::SMEM);                                                            \
       init = true;                                                                                    \
     }                                                                                                 \
-    kern<<<2 * pairs, 192, Gemm2Cfg<256>::SMEM, stream>>>(tA, tB, C, bias, M, N, K, ldc, err, TpArgs{}); \
+    kern<<<2 * pairs, 192, Gemm2Cfg<256>::SMEM, stream>>>(tA, tB, tC, c_bulk, C, bias, M, N, K, ldc, err, \
+                                                           TpArgs{});                                \
   } while (0)
     if (epilogue == kEpiSwiGLU) LL_LAUNCH2(kEpiSwiGLU); else LL_LAUNCH2(kEpiPlain);
 #undef LL_LAUNCH2
@@ -1131,6 +1257,12 @@ extern "C" int ll_gemm_bf16_tp(const void* A_, int lda, const void* W_, int ldw,
   const int ntiles2 = ((M + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * ((N + 255) / 256);
   const int pairs = ntiles2 < num_sms() / 2 ? ntiles2 : num_sms() / 2;
   if (Gemm2Cfg<256>::SMEM > max_smem_optin()) return -7;
+  // The scatter epilogue stores into peers' slot buffers with per-thread
+  // stores; the local outputs take the bulk-store epilogue.
+  CUtensorMap tC;
+  const int c_bulk = epilogue != kEpiScatter && gemm_bulk_store_enabled() &&
+                     make_tmap_c(&tC, C, M, epilogue == kEpiSwiGLU ? N / 2 : N, ldc) == 0;
+  if (!c_bulk) tC = tA;  // not read
 #define LL_LAUNCH_TP(EPI_)                                                                            \
   do {                                                                                                \
     auto kern = gemm_tcgen05_2sm_kernel<256, EPI_>;                                                   \
@@ -1139,7 +1271,8 @@ extern "C" int ll_gemm_bf16_tp(const void* A_, int lda, const void* W_, int ldw,
       set_smem(kern, Gemm2Cfg<256>::SMEM);                                                            \
       init = true;                                                                                    \
     }                                                                                                 \
-    kern<<<2 * pairs, 192, Gemm2Cfg<256>::SMEM, stream>>>(tA, tB, C, bias, M, N, K, ldc, err, *tp);  \
+    kern<<<2 * pairs, 192, Gemm2Cfg<256>::SMEM, stream>>>(tA, tB, tC, c_bulk, C, bias, M, N, K, ldc, err, \
+                                                           *tp);                                     \
   } while (0)
   if (epilogue == kEpiSwiGLU) LL_LAUNCH_TP(kEpiSwiGLU);
   else if (epilogue == kEpiScatter) LL_LAUNCH_TP(kEpiScatter);
