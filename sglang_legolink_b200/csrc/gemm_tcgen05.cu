@@ -942,39 +942,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(acc * BN);
       if constexpr (EPI == kEpiScatter) {
         // rows_per_rank is a multiple of 32, so the slice has one owner.
+        // The owner's slot for this rank is tiled: [R/32][N/32] tiles of 32
+        // rows x 32 columns, each tile 2 KB contiguous, so the warp's chunk
+        // (its 32 rows x 32 columns) is one contiguous 2 KB run.  The chunk
+        // goes through the warp's shared-memory box (lane = row, 64-byte
+        // swizzle) and is read back so that in store k the warp writes rows
+        // 8k..8k+7 -- 512 contiguous bytes per NVLink store instruction.
         const int d = row0 / tp.rows_per_rank;
         const int R = tp.rows_per_rank;
-        // This warp's 32 rows in the owner's slot for this rank.
-        bf16* dst = row0 < M ? static_cast<bf16*>(tp.slot[d]) + ((size_t)tp.rank * R + (row0 - d * R)) * ldc
-                             : nullptr;
-        const int q = lane & 3, grp = lane >> 2;
+        bf16* slot_rows = row0 < M ? static_cast<bf16*>(tp.slot[d]) + (size_t)tp.rank * R * N +
+                                         (size_t)((row0 - d * R) >> 5) * (size_t)(N >> 5) * 1024
+                                   : nullptr;
+        uint8_t* box = sEpi + q * 2 * 2048;
+        const int q4 = lane & 3, rw = lane >> 2;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tbase + c, r);
           tmem_ld_wait();
           const int col0 = nb * BN + c;
-          if (dst == nullptr || col0 >= N) continue;  // warp-uniform
+          if (slot_rows == nullptr || col0 >= N) continue;  // warp-uniform
           uint32_t p[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) p[i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-          // Remote stores are issued row-contiguous: in store k the four
-          // lanes of group g write the 4 x 16 B of row 4g + k (held by lane
-          // 4g + k), so each NVLink write carries 64 contiguous bytes instead
-          // of 16 bytes of 32 different rows.
+          __syncwarp();  // the previous chunk's reads of the box are done
+          epi_stage_row64(box, lane, p);
+          __syncwarp();
+          bf16* tile = slot_rows + (size_t)(col0 >> 5) * 1024;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const int src = 4 * grp + k;
-            uint32_t v[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint32_t w0 = __shfl_sync(0xffffffffu, p[j], src);
-              const uint32_t w1 = __shfl_sync(0xffffffffu, p[4 + j], src);
-              const uint32_t w2 = __shfl_sync(0xffffffffu, p[8 + j], src);
-              const uint32_t w3 = __shfl_sync(0xffffffffu, p[12 + j], src);
-              v[j] = q == 0 ? w0 : q == 1 ? w1 : q == 2 ? w2 : w3;
-            }
-            *reinterpret_cast<uint4*>(dst + (size_t)src * ldc + col0 + 8 * q) = make_uint4(v[0], v[1], v[2], v[3]);
+            const int row = 8 * k + rw;
+            const uint4 v = *reinterpret_cast<const uint4*>(box + row * 64 + ((q4 ^ ((row >> 1) & 3)) << 4));
+            *reinterpret_cast<uint4*>(tile + row * 32 + 8 * q4) = v;
           }
         }
         if (row0 < M) {

@@ -7,7 +7,8 @@
 // ranges of `rows_per_rank` rows (R, a multiple of 32) and:
 //
 //   1. the 2-SM GEMM's epilogue (kEpiScatter, gemm_tcgen05.cu) stores each
-//      output row straight into its owner's slot buffer over NVLink while
+//      output row straight into its owner's slot buffer over NVLink (tiled
+//      32 x 32, so each warp store instruction writes 512 contiguous bytes) while
 //      the tensor cores work on the next tile, and bumps the owner's
 //      arrival counter by the 32-row slices it stored, once at the end of the
 //      GEMM (reduce-scatter fused into the GEMM);
@@ -75,13 +76,16 @@ __global__ void __launch_bounds__(TPB)
       if (slots != nullptr) {
 #pragma unroll 2
         for (int s = 0; s < tg.world; ++s) {
-          const uint4* sr = reinterpret_cast<const uint4*>(slots + ((size_t)s * R + row) * H);
+          // source s's slot is tiled: [R/32][H/32] tiles of 32 x 32 (2 KB
+          // each); 16-byte vector idx of the row is in tile column idx / 4
+          const uint4* sr = reinterpret_cast<const uint4*>(slots + (size_t)s * R * H) +
+                            (size_t)(row >> 5) * (size_t)(H >> 5) * 128 + (row & 31) * 4;
           uint4 a[VPT];
 #pragma unroll
           for (int i = 0; i < VPT; ++i) {
             const int idx = threadIdx.x + i * TPB;
             // L2-only loads: the slots were written by other GPUs.
-            a[i] = idx < nvec ? __ldcg(sr + idx) : make_uint4(0, 0, 0, 0);
+            a[i] = idx < nvec ? __ldcg(sr + (idx >> 2) * 128 + (idx & 3)) : make_uint4(0, 0, 0, 0);
           }
 #pragma unroll
           for (int i = 0; i < VPT; ++i) {
@@ -190,7 +194,7 @@ extern "C" int ll_tp_reduce_norm_gather(const void* slots_, void* residual_, con
   bf16* residual = static_cast<bf16*>(residual_);
   const bf16* w = static_cast<const bf16*>(w_);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  if (H % 8 || H > 8 * TPB * 8 || rows <= 0 || rows > tg->rows_per_rank) return -3;
+  if (H % 32 || H > 8 * TPB * 8 || rows <= 0 || rows > tg->rows_per_rank || tg->rows_per_rank % 32) return -3;
   if (tg->world < 1 || tg->world > LL_MAX_TP_RANKS) return -3;
   const int grid = ll_tp_reduce_norm_gather_grid(rows, H);
   tp_rng_kernel(H)<<<grid, TPB, 0, stream>>>(slots, residual, w, eps, H, rows, *tg, err);
@@ -234,13 +238,29 @@ extern "C" int ll_tp_wait(const void* cnt, unsigned long long target, int* err, 
 // end-of-call barrier is needed.
 namespace ll {
 constexpr int TPD = 256;
-template <int VPT>
+// WMAX: compile-time bound on the world size, so that the loads of every
+// rank's partial row are issued together after the wait (one NVLink round
+// trip instead of one per pair of ranks).  The residual row and the norm
+// weights do not depend on the other ranks and are loaded before the wait.
+template <int VPT, int WMAX>
 __global__ void __launch_bounds__(TPD)
     tp_decode_allreduce_norm_kernel(bf16* __restrict__ residual, const bf16* __restrict__ w, bf16* __restrict__ out,
                                     float eps, int H, int rows, const __grid_constant__ LLTpDecode td, int* err) {
   __shared__ int s_ok;
   __shared__ unsigned long long s_e;
   __shared__ float red[TPD / 32];
+  const int nvec = H / 8;
+  const int row = blockIdx.x;
+  const bool live = row < rows;
+  uint4* rr = reinterpret_cast<uint4*>(residual + (size_t)row * H);
+  uint4 res_v[VPT], w_v[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * TPD;
+    const bool in = live && idx < nvec;
+    res_v[i] = in ? rr[idx] : make_uint4(0, 0, 0, 0);
+    w_v[i] = in ? reinterpret_cast<const uint4*>(w)[idx] : make_uint4(0, 0, 0, 0);
+  }
   if (threadIdx.x == 0) {
     const unsigned long long e = *reinterpret_cast<volatile unsigned long long*>(td.epoch) + 1ull;
     s_e = e;
@@ -251,16 +271,23 @@ __global__ void __launch_bounds__(TPD)
     s_ok = wait_counter_geq(td.cnt[td.rank], e * (unsigned long long)td.world, err) ? 1 : 0;
   }
   __syncthreads();
-  const int nvec = H / 8;
-  const int row = blockIdx.x;
-  if (s_ok && row < rows) {
-    uint4* rr = reinterpret_cast<uint4*>(residual + (size_t)row * H);
+  if (s_ok && live) {
+    uint4 a[WMAX][VPT];
+#pragma unroll
+    for (int d = 0; d < WMAX; ++d) {
+      if (d < td.world) {
+        const uint4* pr = reinterpret_cast<const uint4*>(static_cast<const bf16*>(td.part[d]) + (size_t)row * H);
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+          const int idx = threadIdx.x + i * TPD;
+          a[d][i] = idx < nvec ? __ldcg(pr + idx) : make_uint4(0, 0, 0, 0);  // not through L1: peer data
+        }
+      }
+    }
     float v[VPT][8];
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
-      const int idx = threadIdx.x + i * TPD;
-      uint4 b = idx < nvec ? rr[idx] : make_uint4(0, 0, 0, 0);
-      const uint32_t* bu = reinterpret_cast<const uint32_t*>(&b);
+      const uint32_t* bu = reinterpret_cast<const uint32_t*>(&res_v[i]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 f = unpack_bf16x2(bu[j]);
@@ -268,23 +295,19 @@ __global__ void __launch_bounds__(TPD)
         v[i][2 * j + 1] = f.y;
       }
     }
-#pragma unroll 2
-    for (int d = 0; d < td.world; ++d) {
-      const uint4* pr = reinterpret_cast<const uint4*>(static_cast<const bf16*>(td.part[d]) + (size_t)row * H);
-      uint4 a[VPT];
+    // residual + partials in rank order: every rank computes the same bits
 #pragma unroll
-      for (int i = 0; i < VPT; ++i) {
-        const int idx = threadIdx.x + i * TPD;
-        a[i] = idx < nvec ? __ldcg(pr + idx) : make_uint4(0, 0, 0, 0);  // not through L1: peer data
-      }
+    for (int d = 0; d < WMAX; ++d) {
+      if (d < td.world) {
 #pragma unroll
-      for (int i = 0; i < VPT; ++i) {
-        const uint32_t* au = reinterpret_cast<const uint32_t*>(&a[i]);
+        for (int i = 0; i < VPT; ++i) {
+          const uint32_t* au = reinterpret_cast<const uint32_t*>(&a[d][i]);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = unpack_bf16x2(au[j]);
-          v[i][2 * j] += f.x;
-          v[i][2 * j + 1] += f.y;
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = unpack_bf16x2(au[j]);
+            v[i][2 * j] += f.x;
+            v[i][2 * j + 1] += f.y;
+          }
         }
       }
     }
@@ -315,8 +338,7 @@ __global__ void __launch_bounds__(TPD)
     for (int i = 0; i < VPT; ++i) {
       const int idx = threadIdx.x + i * TPD;
       if (idx < nvec) {
-        const uint4 wv = reinterpret_cast<const uint4*>(w)[idx];
-        const uint32_t* wu = reinterpret_cast<const uint32_t*>(&wv);
+        const uint32_t* wu = reinterpret_cast<const uint32_t*>(&w_v[i]);
         uint32_t o[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -349,13 +371,20 @@ extern "C" int ll_tp_decode_allreduce_norm(void* residual, const void* w, void* 
   bf16* r = static_cast<bf16*>(residual);
   const bf16* wp = static_cast<const bf16*>(w);
   bf16* o = static_cast<bf16*>(out);
-#define LL_TPD(V) ll::tp_decode_allreduce_norm_kernel<V><<<rows, ll::TPD, 0, stream>>>(r, wp, o, eps, H, rows, *td, err)
+#define LL_TPD(V, W) ll::tp_decode_allreduce_norm_kernel<V, W><<<rows, ll::TPD, 0, stream>>>(r, wp, o, eps, H, rows, *td, err)
+#define LL_TPD_W(V)                    \
+  do {                                 \
+    if (td->world <= 2) LL_TPD(V, 2);  \
+    else if (td->world <= 4) LL_TPD(V, 4); \
+    else LL_TPD(V, 8);                 \
+  } while (0)
   switch (vpt) {
-    case 1: LL_TPD(1); break;
-    case 2: LL_TPD(2); break;
-    case 3: LL_TPD(3); break;
-    default: LL_TPD(4); break;
+    case 1: LL_TPD_W(1); break;
+    case 2: LL_TPD_W(2); break;
+    case 3: LL_TPD_W(3); break;
+    default: LL_TPD_W(4); break;
   }
+#undef LL_TPD_W
 #undef LL_TPD
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }

@@ -6,8 +6,10 @@
 
 // 2-SM GEMM hooks.  wait_cnt != nullptr: the producer waits until
 // *wait_cnt >= wait_target before loading A.  Scatter epilogue: row r goes to
-// rank r / rows_per_rank's slot buffer `slot[d]`, and each 32-row x 256-column
-// slice it stored adds 1 to `cnt[d]` (published at the end of the GEMM).
+// rank d = r / rows_per_rank's slot buffer `slot[d]`, into the region of the
+// storing rank, which is tiled as [R/32][N/32] tiles of 32 rows x 32 columns
+// (2 KB each, row-major inside); each 32-row x 256-column slice it stored
+// adds 1 to `cnt[d]` (published at the end of the GEMM).
 struct LLTpArgs {
   void* slot[LL_MAX_TP_RANKS];
   unsigned long long* cnt[LL_MAX_TP_RANKS];

@@ -49,11 +49,15 @@ def test_prefill_boundary_emulated_world(W):
     torch.cuda.synchronize()
     assert ops.check_errors(DEV) == 0
     per_rank_slices = (R // 32) * ((H + 255) // 256)
+
+    def untile(x):  # a source rank's slot region: [R/32][H/32][32][32] -> [R, H]
+        return x.reshape(R // 32, H // 32, 32, 32).permute(0, 2, 1, 3).reshape(R, H)
+
     for d in range(W):
         assert int(cnt[d][0]) == W * per_rank_slices
         for r in range(W):
             exp = a[r][d * R:(d + 1) * R].float() @ wo[r].float().t()
-            assert _rel(slots[d][r], exp) < 1e-2
+            assert _rel(untile(slots[d][r]), exp) < 1e-2
     # 2. every owner's reduce + residual + RMSNorm + all-gather
     res0 = [torch.randn(R, H, device=DEV).to(torch.bfloat16) for _ in range(W)]
     res = [x.clone() for x in res0]
@@ -66,7 +70,7 @@ def test_prefill_boundary_emulated_world(W):
     assert ops.check_errors(DEV) == 0
     assert len(set(grids)) == 1
     for d in range(W):
-        s = res0[d].float() + slots[d].float().sum(0)
+        s = res0[d].float() + sum(untile(slots[d][r]).float() for r in range(W))
         assert _rel(res[d], s) < 1e-2
         for e in range(W):
             assert _rel(G[e][d * R:(d + 1) * R], _norm(s, nw)) < 1e-2
