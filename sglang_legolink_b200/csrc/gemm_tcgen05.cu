@@ -1133,7 +1133,7 @@ static int make_tmap_c(CUtensorMap* tm, const void* ptr, int rows, int cols, int
 
 // Bulk-store epilogue: LL_GEMM_BULK_STORE=1 selects it, 0 the per-thread
 // stores; unset: kGemmBulkStoreDefault.
-constexpr int kGemmBulkStoreDefault = 0;
+constexpr int kGemmBulkStoreDefault = 1;
 static bool gemm_bulk_store_enabled() {
   static int v = -1;
   if (v < 0) {
