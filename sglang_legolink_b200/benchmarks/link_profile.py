@@ -42,6 +42,27 @@ def summarize(prof, label):
         print(f"  {us / 1e3:8.3f} ms {100 * us / max(tot, 1e-9):5.1f}%  x{n:<5d} {k}")
 
 
+def timeline(prof, marker: str) -> dict:
+    """Where the wall time of the ``marker`` CPU range went: host work before
+    the first kernel, device idle gaps between kernels, kernel time, and the
+    tail after the last kernel (microseconds, one clock: the profiler's)."""
+    mk = [e for e in prof.events() if e.name == marker and e.device_type == torch.autograd.DeviceType.CPU]
+    ks = sorted((e.time_range.start, e.time_range.end) for e in prof.events()
+                if e.device_type == torch.autograd.DeviceType.CUDA and e.time_range.end > e.time_range.start)
+    if not mk or not ks:
+        return {}
+    t0, t1 = mk[0].time_range.start, mk[0].time_range.end
+    busy, gaps, end = 0.0, 0.0, ks[0][0]
+    for a, b in ks:
+        if a > end:
+            gaps += a - end
+        busy += max(0.0, b - max(a, end))
+        end = max(end, b)
+    return {"wall_us": round(t1 - t0, 1), "host_before_first_kernel_us": round(ks[0][0] - t0, 1),
+            "device_busy_us": round(busy, 1), "device_idle_gaps_us": round(gaps, 1),
+            "after_last_kernel_us": round(t1 - end, 1)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="qwen2.5-7b")
@@ -64,10 +85,13 @@ def main():
     eng.free(s)
     torch.cuda.synchronize()
     acts = [torch.profiler.ProfilerActivity.CUDA]
-    with torch.profiler.profile(activities=acts) as p:
-        s = eng.link(dict(plan), suffix)
-        torch.cuda.synchronize()
+    acts_cpu = acts + [torch.profiler.ProfilerActivity.CPU]
+    with torch.profiler.profile(activities=acts_cpu) as p:
+        with torch.profiler.record_function("link_call"):
+            s = eng.link(dict(plan), suffix)
+            torch.cuda.synchronize()
     summarize(p, "link")
+    print("   timeline:", timeline(p, "link_call"))
     with torch.profiler.profile(activities=acts) as p:
         eng.decode([s], a.decode)
         torch.cuda.synchronize()
