@@ -188,6 +188,30 @@ void tp_decode_allreduce_norm(at::Tensor& residual, const at::Tensor& w, at::Ten
            "ll_tp_decode_allreduce_norm");
 }
 
+// Greedy token ids [rows] over vocab-sharded logits [rows, vocab_local]
+// (this rank's shard starting at vocab_start): records pushed to every
+// rank's slot array (device addresses), epoch this rank's int64 [2].
+void tp_argmax(const at::Tensor& logits, int64_t vocab_start, at::Tensor& out, std::vector<int64_t> slot_ptrs,
+               at::Tensor& epoch, int64_t rank, int64_t world, int64_t rmax, const at::Tensor& err) {
+  CHECK_CUDA(logits); CHECK_BF16(logits); CHECK_I32(out);
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1 && out.is_contiguous() && out.numel() >= logits.size(0));
+  TORCH_CHECK(epoch.scalar_type() == at::kLong && epoch.numel() >= 2 && epoch.is_cuda());
+  TORCH_CHECK((int64_t)slot_ptrs.size() == world && world <= LL_MAX_TP_RANKS);
+  LLTpArgmax ta{};
+  for (int i = 0; i < world; ++i) {
+    TORCH_CHECK(slot_ptrs[i] % 16 == 0, "argmax slot array must be 16-byte aligned");
+    ta.slot[i] = reinterpret_cast<void*>(slot_ptrs[i]);
+  }
+  ta.epoch = reinterpret_cast<unsigned long long*>(epoch.data_ptr<int64_t>());
+  ta.rank = (int)rank;
+  ta.world = (int)world;
+  ta.rmax = (int)rmax;
+  c10::cuda::CUDAGuard g(logits.device());
+  check_rc(ll_tp_argmax(logits.data_ptr(), (int)logits.size(1), (int)logits.stride(0), (int)vocab_start,
+                        (int)logits.size(0), out.data_ptr<int>(), &ta, err.data_ptr<int>(), cur_stream()),
+           "ll_tp_argmax");
+}
+
 // swiglu: w is the interleaved gate/up weight and out holds silu(gate) * up
 // (N / 2 columns).
 void gemm_small_m(const at::Tensor& a, const at::Tensor& w, const c10::optional<at::Tensor>& bias, at::Tensor& out,
@@ -455,6 +479,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_reduce_norm_gather", &tp_reduce_norm_gather);
   m.def("tp_wait", &tp_wait);
   m.def("tp_decode_allreduce_norm", &tp_decode_allreduce_norm);
+  m.def("tp_argmax", &tp_argmax);
   m.def("attn_prefill_tc_set_variant", [](int64_t v) { return ll_attn_prefill_tc_set_variant((int)v); });
   m.def("attn_prefill_tc_trace", []() {
     auto t = at::zeros({256 * 20}, at::kLong);

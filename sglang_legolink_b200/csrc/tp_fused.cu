@@ -388,3 +388,153 @@ extern "C" int ll_tp_decode_allreduce_norm(void* residual, const void* w, void* 
 #undef LL_TPD
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
+
+// ------------------------------------------------------- vocab-sharded argmax
+// Greedy sampling when the LM head is split over the vocabulary (reference:
+// the logits all-gather of the tensor-parallel LM head, replaced there by a
+// gather of per-rank (max, index) pairs): one kernel per call on every rank.
+//   * CTA i takes row i: block argmax of this rank's logits shard (ties: the
+//     smallest index, as torch.argmax);
+//   * it stores (max, vocab_start + index) into row i's record for this rank
+//     in EVERY rank's slot array (peer stores over NVLink), then the record's
+//     tag = epoch with release semantics;
+//   * it waits (bounded) until the W records of row i in its own slot carry
+//     this epoch, and writes the index of the largest max (ties: the lowest
+//     rank, whose vocabulary range comes first -> the smallest token id).
+// Records alternate between two parities by epoch: a rank writes parity p
+// again only in call e + 2, after passing call e + 1's wait, which every
+// peer joins only after finishing its call-e reads.  The epoch lives in
+// device memory (advanced by the last CTA), so a CUDA graph replays the
+// call unchanged.
+namespace ll {
+constexpr int TPA = 512;
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(TPA)
+    tp_argmax_kernel(const bf16* __restrict__ logits, int vocab, int ld, int vocab_start, int rows,
+                     int* __restrict__ out, const __grid_constant__ LLTpArgmax ta, int* err) {
+  __shared__ float sv[TPA / 32];
+  __shared__ int si[TPA / 32];
+  __shared__ unsigned long long s_e;
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x == 0) s_e = *reinterpret_cast<volatile unsigned long long*>(ta.epoch) + 1ull;
+  const int i = blockIdx.x;
+  const bf16* row = logits + (size_t)i * ld;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int v = threadIdx.x; v < vocab; v += TPA) {  // increasing per thread: '>' keeps the first
+    const float x = __bfloat162float(row[v]);
+    if (x > best) {
+      best = x;
+      bi = v;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = best;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    best = threadIdx.x < TPA / 32 ? sv[threadIdx.x] : -INFINITY;
+    bi = threadIdx.x < TPA / 32 ? si[threadIdx.x] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+  }
+  const unsigned long long e = s_e;
+  const int par = (int)(e & 1ull);
+  // lanes 0..world-1 of warp 0: push this rank's pair to every rank
+  if (threadIdx.x < 32) {
+    const int gidx = bi == 0x7fffffff ? vocab_start : vocab_start + bi;
+    const unsigned long long pair =
+        ((unsigned long long)__float_as_uint(__shfl_sync(0xffffffffu, best, 0)) << 32) |
+        (unsigned int)__shfl_sync(0xffffffffu, gidx, 0);
+    const int d = threadIdx.x;
+    if (d < ta.world) {
+      LLTpArgmaxRec* rec = static_cast<LLTpArgmaxRec*>(ta.slot[d]) +
+                           ((size_t)par * ta.rmax + i) * LL_MAX_TP_RANKS + ta.rank;
+      rec->pair = pair;
+      st_release_sys_u64(&rec->tag, e);
+    }
+    // wait for every rank's record of this row in this rank's slot
+    bool ok = true;
+    float rv = -INFINITY;
+    int ri = 0x7fffffff;
+    if (d < ta.world) {
+      LLTpArgmaxRec* own = static_cast<LLTpArgmaxRec*>(ta.slot[ta.rank]) +
+                           ((size_t)par * ta.rmax + i) * LL_MAX_TP_RANKS + d;
+      if (ld_acquire_sys(&own->tag) != e) {
+        const unsigned long long start = globaltimer_ns();
+        uint32_t iter = 0;
+        while (true) {
+          __nanosleep(32);
+          if (ld_acquire_sys(&own->tag) == e) break;
+          if ((++iter & 63u) == 0 && globaltimer_ns() - start > kWaitLimitNs) {
+            record_error(err, kErrPeerFlagTimeout);
+            ok = false;
+            break;
+          }
+        }
+      }
+      if (ok) {
+        const unsigned long long pv = *reinterpret_cast<volatile unsigned long long*>(&own->pair);
+        rv = __uint_as_float((unsigned int)(pv >> 32));
+        ri = (int)(unsigned int)(pv & 0xffffffffull);
+      }
+    }
+    // largest max; ties to the lowest rank (the smallest token id)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, rv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, ri, o);
+      if (ov > rv || (ov == rv && oi < ri)) {
+        rv = ov;
+        ri = oi;
+      }
+    }
+    const bool all_ok = __all_sync(0xffffffffu, ok);
+    if (threadIdx.x == 0 && i < rows) out[i] = all_ok ? ri : -1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned int* ticket = reinterpret_cast<unsigned int*>(ta.epoch + 1);
+    if (atomicAdd(ticket, 1u) == gridDim.x - 1) {
+      *reinterpret_cast<volatile unsigned int*>(ticket) = 0u;
+      __threadfence();
+      *reinterpret_cast<volatile unsigned long long*>(ta.epoch) = e;
+    }
+  }
+}
+}  // namespace ll
+
+// One CTA per row (rows <= rmax); every rank must make the same sequence of
+// calls with the same row count.
+extern "C" int ll_tp_argmax(const void* logits, int vocab_local, int ld, int vocab_start, int rows, int* out,
+                            const LLTpArgmax* ta, int* err, void* stream_) {
+  if (rows <= 0) return 0;
+  if (rows > ta->rmax || ta->world < 1 || ta->world > LL_MAX_TP_RANKS || ta->rank < 0 || ta->rank >= ta->world ||
+      vocab_local <= 0)
+    return -3;
+  launch_pdl(ll::tp_argmax_kernel, dim3(rows), dim3(ll::TPA), 0, static_cast<cudaStream_t>(stream_),
+             static_cast<const ll::bf16*>(logits), vocab_local, ld, vocab_start, rows, out, *ta, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+

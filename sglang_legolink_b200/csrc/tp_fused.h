@@ -39,9 +39,27 @@ struct LLTpDecode {
   int rank, world;
 };
 
+// Greedy token over vocab-sharded logits: slot[d] is rank d's record array
+// [2 parities][rmax rows][LL_MAX_TP_RANKS source ranks] of LLTpArgmaxRec;
+// epoch this rank's [calls completed, CTA ticket] (device memory).
+struct LLTpArgmax {
+  void* slot[LL_MAX_TP_RANKS];
+  unsigned long long* epoch;
+  int rank, world, rmax;
+};
+
+// One source rank's (max, global index) for one row, tagged with the call's
+// epoch; the tag is stored after the pair with release semantics.
+struct LLTpArgmaxRec {
+  unsigned long long pair;  // float bits of the max << 32 | global index
+  unsigned long long tag;
+};
+
 #ifdef __cplusplus
 extern "C" {
 #endif
+int ll_tp_argmax(const void* logits, int vocab_local, int ld, int vocab_start, int rows, int* out,
+                 const struct LLTpArgmax* ta, int* err, void* stream);
 int ll_gemm_bf16_tp(const void* A, int lda, const void* W, int ldw, void* C, int ldc, const void* bias, int M, int N,
                     int K, int epilogue, const struct LLTpArgs* tp, int* err, void* stream);
 int ll_tp_reduce_norm_gather(const void* slots, void* residual, const void* w, float eps, int H, int rows,

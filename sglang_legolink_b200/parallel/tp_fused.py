@@ -28,8 +28,10 @@ each row-parallel GEMV, :meth:`decode_allreduce_norm`: the GEMV writes its
 partial rows into this rank's symmetric buffer (two buffers, alternating
 call by call), and the kernel sums every rank's rows over NVLink (one-shot
 all-reduce), adds the residual and applies the next RMSNorm.  Its epoch lives
-in device memory, so the decode CUDA graphs replay it unchanged.  Short
-prefills keep the NCCL path inherited from :class:`~.tp.NcclTPComm`.
+in device memory, so the decode CUDA graphs replay it unchanged.  Greedy
+sampling over the vocab-sharded LM head is one kernel as well
+(:meth:`argmax_vocab`).  Short prefills keep the NCCL path inherited from
+:class:`~.tp.NcclTPComm`.
 """
 
 from __future__ import annotations
@@ -90,9 +92,16 @@ class FusedTPComm(NcclTPComm):
         self.dpart_ptrs = [int(p) for p in self._hdp.buffer_ptrs]
         self.dcnt_ptrs = [int(p) for p in self._hdc.buffer_ptrs]
         self._dparity = 0
+        # greedy over the vocab shards: per-row (max, index) records pushed
+        # to every rank ([2 parities][MAX_DECODE_ROWS][8 ranks][pair, tag])
+        self.arec = symm_mem.empty((2 * MAX_DECODE_ROWS * 8 * 2,), dtype=torch.int64, device=device)
+        self.arec.zero_()
+        self.aepoch = torch.zeros(2, dtype=torch.int64, device=device)
+        self._hak = symm_mem.rendezvous(self.arec, gname)
+        self.arec_ptrs = [int(p) for p in self._hak.buffer_ptrs]
         torch.cuda.synchronize(device)
         dist.barrier(group=self.group)  # every counter is zero before any peer adds to it
-        self.stats = {"fused_gemms": 0, "fused_reduces": 0, "fused_decode_reduces": 0}
+        self.stats = {"fused_gemms": 0, "fused_reduces": 0, "fused_decode_reduces": 0, "fused_argmax": 0}
 
     # ------------------------------------------------------------ geometry
     def rows_per_rank(self, T: int) -> int:
@@ -128,6 +137,20 @@ class FusedTPComm(NcclTPComm):
                                              ops.workspace(residual.device).err)
         self._dparity ^= 1
         self.stats["fused_decode_reduces"] += 1
+
+    def argmax_vocab(self, local: torch.Tensor, vocab_start: int) -> torch.Tensor:
+        """Greedy token ids over vocab-sharded logits in one kernel: every
+        rank pushes its rows' (max, index) to every rank over NVLink and
+        picks the winner (ties: the smallest token id).  Replaces the pair
+        all-gather of :class:`~.tp.NcclTPComm` for up to MAX_DECODE_ROWS rows."""
+        R = local.shape[0]
+        if not local.is_cuda or R > MAX_DECODE_ROWS or local.stride(-1) != 1:
+            return super().argmax_vocab(local, vocab_start)
+        out = torch.empty(R, dtype=torch.int32, device=local.device)
+        ops._cuda().tp_argmax(local, int(vocab_start), out, self.arec_ptrs, self.aepoch, self.rank, self.size,
+                              MAX_DECODE_ROWS, ops.workspace(local.device).err)
+        self.stats["fused_argmax"] += 1
+        return out
 
     # ------------------------------------------------------------- kernels
     def reduce_norm_gather(self, residual: torch.Tensor, w: torch.Tensor, eps: float, T: int,

@@ -112,3 +112,56 @@ def test_decode_boundary_emulated_world(W, rows, H):
         assert _rel(out, _norm(s, w)) < 1e-2
     for c in cnt:  # W - 1 pre-added + one arrival from each rank
         assert int(c[0]) == 2 * W - 1
+
+
+def _pair_word(val: float, gidx: int) -> int:
+    import struct
+
+    bits = struct.unpack("<I", struct.pack("<f", val))[0]
+    x = (bits << 32) | (gidx & 0xFFFFFFFF)
+    return x - (1 << 64) if x >= (1 << 63) else x
+
+
+@pytest.mark.parametrize("W", [2, 4, 8])
+def test_vocab_sharded_argmax_emulated_world(W):
+    """Greedy over vocab shards in one kernel, rank 0 of an emulated world:
+    the host writes the other ranks' (max, index) records for each call's
+    epoch into rank 0's slot array before the launch, so the kernel's wait is
+    already satisfied; the winner is the largest max, ties to the lowest rank
+    (the smallest token id), over three calls (both record parities)."""
+    torch.manual_seed(W)
+    ext, err = ops._cuda(), ops.workspace(DEV).err
+    R, V, RMAX = 16, 1000, 64
+    recs = [torch.zeros(2 * RMAX * 8 * 2, device=DEV, dtype=torch.int64) for _ in range(W)]
+    ptrs = [r.data_ptr() for r in recs]
+    epoch = torch.zeros(2, device=DEV, dtype=torch.int64)
+    for call in (1, 2, 3):
+        logits = torch.randn(R, V, device=DEV).to(torch.bfloat16)
+        lf = logits.float()
+        mine_v, mine_i = lf.max(-1)
+        par = call & 1
+        cands = [[(float(mine_v[i]), int(mine_i[i]))] for i in range(R)]
+        for r in range(1, W):
+            for i in range(R):
+                if i == 0:
+                    val = float(mine_v[i])  # a tie with rank 0: rank 0 (the smaller id) wins
+                elif i == 1 and r >= 2:
+                    val = 50.0  # a tie between the other ranks: the lowest of them wins
+                else:
+                    val = float(torch.randn(()).item() * 2)
+                gidx = r * V + int(torch.randint(0, V, ()).item())
+                cands[i].append((val, gidx))
+                base = ((par * RMAX + i) * 8 + r) * 2
+                recs[0][base] = _pair_word(val, gidx)
+                recs[0][base + 1] = call
+        out = torch.empty(R, device=DEV, dtype=torch.int32)
+        ext.tp_argmax(logits, 0, out, ptrs, epoch, 0, W, RMAX, err)
+        torch.cuda.synchronize()
+        assert ops.check_errors(DEV) == 0
+        exp = [max(c, key=lambda t: (t[0], -t[1]))[1] for c in cands]
+        assert out.tolist() == exp
+        assert int(epoch[0]) == call
+        # rank 0 pushed its own record, tagged with this call's epoch, to every rank
+        for d in range(W):
+            base = ((par * RMAX + 3) * 8 + 0) * 2
+            assert int(recs[d][base + 1]) == call
