@@ -11,10 +11,11 @@ each hand-off over the steady-state blocks:
   softmax sees S (the tensor pipe's PV + S of that tile plus any queue);
 * the block period and how long the two tiles' softmax intervals overlap.
 
-    python -m sglang_legolink_b200.benchmarks.attn_trace [--variants 5,6]
+    python -m sglang_legolink_b200.benchmarks.attn_trace [--variants 5,9]
 
 Variants are indices of the kernel's build table (trace builds: 5 with one
-softmax warpgroup per tile, 6 with two warpgroups of 64 key columns each).
+softmax warpgroup per tile, 6 with two warpgroups of 64 key columns each, 9
+with the 8-chain max and P stored after the whole row).
 """
 
 from __future__ import annotations
@@ -88,7 +89,7 @@ def summarize(tr: torch.Tensor, nb: int) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--variants", default="5,6")
+    ap.add_argument("--variants", default="5,9")
     a = ap.parse_args()
     ext = ops._cuda()
     fn, nb = _case()

@@ -209,7 +209,10 @@ __device__ unsigned long long g_attn_trace[TC_TRACE_BLOCKS * TC_TRACE_EV];
       g_attn_trace[(j) * TC_TRACE_EV + (e)] = clock64();                              \
   } while (0)
 
-template <int CS, int POLY8, bool ALU_PACK, bool TRACE = false>
+// SCHED 1: the row max over 8 independent chains, and the block's P values
+// all computed before any TMEM store (one stream of exp2s, four stores at
+// the end) instead of a store after every 32 columns.
+template <int CS, int POLY8, bool ALU_PACK, bool TRACE = false, int SCHED = 0>
 __global__ void __launch_bounds__(TcCfg<CS>::THREADS, 1)
     attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                            const bf16* __restrict__ q, const int* __restrict__ q_indptr,
@@ -463,14 +466,28 @@ __global__ void __launch_bounds__(TcCfg<CS>::THREADS, 1)
           if (i > lim) s[i] = __float_as_uint(-INFINITY);
       }
       if (r == 0 && t == 0 && h == 0) TC_TR(j, 17);
-      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      float mx;
+      if constexpr (SCHED == 1) {
+        float m8[8];
 #pragma unroll
-      for (int i = 0; i < NC; i += 8) {
+        for (int u = 0; u < 8; ++u) m8[u] = fmaxf(__uint_as_float(s[2 * u]), __uint_as_float(s[2 * u + 1]));
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          m4[u] = fmax3(m4[u], __uint_as_float(s[i + 2 * u]), __uint_as_float(s[i + 2 * u + 1]));
+        for (int i = 16; i < NC; i += 16) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            m8[u] = fmax3(m8[u], __uint_as_float(s[i + 2 * u]), __uint_as_float(s[i + 2 * u + 1]));
+        }
+        mx = fmaxf(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], fmax3(m8[5], m8[6], m8[7])));
+      } else {
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int i = 0; i < NC; i += 8) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            m4[u] = fmax3(m4[u], __uint_as_float(s[i + 2 * u]), __uint_as_float(s[i + 2 * u + 1]));
+        }
+        mx = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
       }
-      float mx = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
       if constexpr (CS == 2) {
         float other;
         if (!exchange(j, mx, other)) return false;
@@ -486,20 +503,38 @@ __global__ void __launch_bounds__(TcCfg<CS>::THREADS, 1)
       // first 64 columns of S.
       float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < NC / 32; ++c) {
-        uint32_t pk[16];
+      if constexpr (SCHED == 1) {
+        // the P values overwrite the scores they come from (s[e] holds pair
+        // e once s[2e], s[2e+1] are consumed), then four stores
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int i0 = 32 * c + 2 * e;
-          const float xa = fmaf(__uint_as_float(s[i0]), scale_log2, neg_m);
-          const float xb2 = fmaf(__uint_as_float(s[i0 + 1]), scale_log2, neg_m);
-          const float pa = (i0 & 7) < POLY8 ? exp2_poly(xa) : ex2(xa);
-          const float pb = ((i0 + 1) & 7) < POLY8 ? exp2_poly(xb2) : ex2(xb2);
+        for (int e = 0; e < NC / 2; ++e) {
+          const float xa = fmaf(__uint_as_float(s[2 * e]), scale_log2, neg_m);
+          const float xb2 = fmaf(__uint_as_float(s[2 * e + 1]), scale_log2, neg_m);
+          const float pa = ((2 * e) & 7) < POLY8 ? exp2_poly(xa) : ex2(xa);
+          const float pb = ((2 * e + 1) & 7) < POLY8 ? exp2_poly(xb2) : ex2(xb2);
           sum4[e & 3] += pa + pb;
-          pk[e] = ALU_PACK ? pack_bf16x2_alu(pa, pb) : pack_bf16x2(pa, pb);
+          s[e] = ALU_PACK ? pack_bf16x2_alu(pa, pb) : pack_bf16x2(pa, pb);
         }
-        tmem_st_32x32b_x16(p_col + 16 * c, pk);
-        if (r == 0 && t == 0 && h == 0) TC_TR(j, 12 + c);
+#pragma unroll
+        for (int c = 0; c < NC / 32; ++c)
+          tmem_st_32x32b_x16(p_col + 16 * c, *reinterpret_cast<const uint32_t(*)[16]>(&s[16 * c]));
+        if (r == 0 && t == 0 && h == 0) TC_TR(j, 15);
+      } else {
+        for (int c = 0; c < NC / 32; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int i0 = 32 * c + 2 * e;
+            const float xa = fmaf(__uint_as_float(s[i0]), scale_log2, neg_m);
+            const float xb2 = fmaf(__uint_as_float(s[i0 + 1]), scale_log2, neg_m);
+            const float pa = (i0 & 7) < POLY8 ? exp2_poly(xa) : ex2(xa);
+            const float pb = ((i0 + 1) & 7) < POLY8 ? exp2_poly(xb2) : ex2(xb2);
+            sum4[e & 3] += pa + pb;
+            pk[e] = ALU_PACK ? pack_bf16x2_alu(pa, pb) : pack_bf16x2(pa, pb);
+          }
+          tmem_st_32x32b_x16(p_col + 16 * c, pk);
+          if (r == 0 && t == 0 && h == 0) TC_TR(j, 12 + c);
+        }
       }
       const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       // O is stable here: PV of block j-1 was issued before S(j) and the
@@ -622,14 +657,17 @@ struct TcBuild {
   Kern kern;
   int threads, smem;
 };
-template <int CS, int POLY8, bool ALU_PACK, bool TRACE = false>
+template <int CS, int POLY8, bool ALU_PACK, bool TRACE = false, int SCHED = 0>
 constexpr TcBuild tc_build() {
-  return {attn_prefill_tc_kernel<CS, POLY8, ALU_PACK, TRACE>, TcCfg<CS>::THREADS, TcCfg<CS>::SMEM};
+  return {attn_prefill_tc_kernel<CS, POLY8, ALU_PACK, TRACE, SCHED>, TcCfg<CS>::THREADS, TcCfg<CS>::SMEM};
 }
-constexpr int kNumVariants = 7;
+//   7  CS = 1, SCHED 1 (8-chain max, P stored after the whole row)
+//   8  CS = 1, SCHED 1, 2 of 8 exp2 on FMA   9  trace build of 7
+constexpr int kNumVariants = 10;
 static const TcBuild kVariants[kNumVariants] = {
     tc_build<1, 0, false>(),       tc_build<1, 0, true>(),  tc_build<1, 2, true>(), tc_build<2, 0, false>(),
-    tc_build<2, 2, true>(),        tc_build<1, 0, false, true>(), tc_build<2, 0, false, true>()};
+    tc_build<2, 2, true>(),        tc_build<1, 0, false, true>(), tc_build<2, 0, false, true>(),
+    tc_build<1, 0, false, false, 1>(), tc_build<1, 2, false, false, 1>(), tc_build<1, 0, false, true, 1>()};
 constexpr int kDefaultVariant = 0;
 
 static int g_attn_variant = -1;
