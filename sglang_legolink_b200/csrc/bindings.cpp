@@ -164,9 +164,10 @@ void tp_wait(int64_t cnt, int64_t target, const at::Tensor& err) {
 
 // Decode TP boundary: residual [rows, H] += sum over ranks of part[d] rows;
 // out = RMSNorm(residual) * w.  epoch: this rank's int64 [2] (zeroed once).
-void tp_decode_allreduce_norm(at::Tensor& residual, const at::Tensor& w, at::Tensor& out, double eps, int64_t rows,
-                              std::vector<int64_t> part_ptrs, std::vector<int64_t> cnt_ptrs, at::Tensor& epoch,
-                              int64_t rank, int64_t world, const at::Tensor& err) {
+void tp_decode_allreduce_norm_nvls(at::Tensor& residual, const at::Tensor& w, at::Tensor& out, double eps,
+                                   int64_t rows, std::vector<int64_t> part_ptrs, std::vector<int64_t> cnt_ptrs,
+                                   at::Tensor& epoch, int64_t rank, int64_t world, const at::Tensor& err,
+                                   int64_t mc_ptr) {
   CHECK_CUDA(residual); CHECK_BF16(residual); CHECK_CONTIG(residual); CHECK_BF16(w); CHECK_BF16(out);
   CHECK_CONTIG(out); CHECK_ALIGN16(residual); CHECK_ALIGN16(out); CHECK_ALIGN16(w);
   TORCH_CHECK(epoch.scalar_type() == at::kLong && epoch.numel() >= 2 && epoch.is_cuda());
@@ -180,12 +181,21 @@ void tp_decode_allreduce_norm(at::Tensor& residual, const at::Tensor& w, at::Ten
     td.cnt[i] = reinterpret_cast<unsigned long long*>(cnt_ptrs[i]);
   }
   td.epoch = reinterpret_cast<unsigned long long*>(epoch.data_ptr<int64_t>());
+  TORCH_CHECK(mc_ptr % 16 == 0, "multicast address must be 16-byte aligned");
+  td.mc = reinterpret_cast<const void*>(mc_ptr);
   td.rank = (int)rank;
   td.world = (int)world;
   c10::cuda::CUDAGuard g(residual.device());
   check_rc(ll_tp_decode_allreduce_norm(residual.data_ptr(), w.data_ptr(), out.data_ptr(), (float)eps, H, (int)rows,
                                        &td, err.data_ptr<int>(), cur_stream()),
            "ll_tp_decode_allreduce_norm");
+}
+
+void tp_decode_allreduce_norm(at::Tensor& residual, const at::Tensor& w, at::Tensor& out, double eps, int64_t rows,
+                              std::vector<int64_t> part_ptrs, std::vector<int64_t> cnt_ptrs, at::Tensor& epoch,
+                              int64_t rank, int64_t world, const at::Tensor& err) {
+  tp_decode_allreduce_norm_nvls(residual, w, out, eps, rows, std::move(part_ptrs), std::move(cnt_ptrs), epoch, rank,
+                                world, err, 0);
 }
 
 // Greedy token ids [rows] over vocab-sharded logits [rows, vocab_local]
@@ -480,6 +490,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_wait", &tp_wait);
   m.def("tp_decode_allreduce_norm", &tp_decode_allreduce_norm);
   m.def("tp_argmax", &tp_argmax);
+  m.def("tp_decode_allreduce_norm_nvls", &tp_decode_allreduce_norm_nvls);
   m.def("attn_prefill_tc_set_variant", [](int64_t v) { return ll_attn_prefill_tc_set_variant((int)v); });
   m.def("attn_prefill_tc_trace", []() {
     auto t = at::zeros({256 * 20}, at::kLong);

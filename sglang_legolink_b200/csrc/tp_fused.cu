@@ -238,6 +238,59 @@ extern "C" int ll_tp_wait(const void* cnt, unsigned long long target, int* err, 
 // end-of-call barrier is needed.
 namespace ll {
 constexpr int TPD = 256;
+// residual (bf16) + sum (bf16, already reduced over the ranks) in fp32 ->
+// residual; RMSNorm(residual) * w -> out (one CTA per row, TPD threads).
+template <int VPT>
+__device__ __forceinline__ void res_add_norm_store(const uint4 (&res_v)[VPT], const uint4 (&sum_v)[VPT],
+                                                   const uint4 (&w_v)[VPT], uint4* rr, bf16* out, int row, int H,
+                                                   int nvec, float eps, float* red) {
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const uint32_t* bu = reinterpret_cast<const uint32_t*>(&res_v[i]);
+    const uint32_t* su = reinterpret_cast<const uint32_t*>(&sum_v[i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(bu[j]), g = unpack_bf16x2(su[j]);
+      v[i][2 * j] = f.x + g.x;
+      v[i][2 * j + 1] = f.y + g.y;
+    }
+    const int idx = threadIdx.x + i * TPD;
+    if (idx < nvec) {
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        o[j] = pack_bf16x2(v[i][2 * j], v[i][2 * j + 1]);
+        ss += v[i][2 * j] * v[i][2 * j] + v[i][2 * j + 1] * v[i][2 * j + 1];
+      }
+      rr[idx] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < TPD / 32; ++i) tot += red[i];
+  const float rstd = rsqrtf(tot / H + eps);
+  uint4* orow = reinterpret_cast<uint4*>(out + (size_t)row * H);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * TPD;
+    if (idx < nvec) {
+      const uint32_t* wu = reinterpret_cast<const uint32_t*>(&w_v[i]);
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(wu[j]);
+        o[j] = pack_bf16x2(v[i][2 * j] * rstd * f.x, v[i][2 * j + 1] * rstd * f.y);
+      }
+      orow[idx] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 // WMAX: compile-time bound on the world size, so that the loads of every
 // rank's partial row are issued together after the wait (one NVLink round
 // trip instead of one per pair of ranks).  The residual row and the norm
@@ -271,7 +324,27 @@ __global__ void __launch_bounds__(TPD)
     s_ok = wait_counter_geq(td.cnt[td.rank], e * (unsigned long long)td.world, err) ? 1 : 0;
   }
   __syncthreads();
-  if (s_ok && live) {
+  if (s_ok && live && td.mc != nullptr) {
+    // NVLS: every element's sum over the ranks comes from the switch in one
+    // multimem load (bf16 result, fp32 accumulation), then residual + norm
+    const uint4* mr = reinterpret_cast<const uint4*>(static_cast<const bf16*>(td.mc) + (size_t)row * H);
+    uint4 sm[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int idx = threadIdx.x + i * TPD;
+      if (idx < nvec) {
+        uint32_t r0, r1, r2, r3;
+        asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                     : "l"(mr + idx)
+                     : "memory");
+        sm[i] = make_uint4(r0, r1, r2, r3);
+      } else {
+        sm[i] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    res_add_norm_store<VPT>(res_v, sm, w_v, rr, out, row, H, nvec, eps, red);
+  } else if (s_ok && live) {
     uint4 a[WMAX][VPT];
 #pragma unroll
     for (int d = 0; d < WMAX; ++d) {

@@ -32,10 +32,14 @@ struct LLTpGather {
 // rank d's partial rows of this call, cnt[d] rank d's arrival counter, epoch
 // this rank's [calls completed, CTA ticket] (device memory, so a CUDA graph
 // replays the boundary unchanged).
+// mc != nullptr: the multicast (NVLS) address of this call's partial rows
+// in every rank's buffer; each element's sum over the ranks is then one
+// multimem load reduced in the NVLink switch instead of `world` peer loads.
 struct LLTpDecode {
   const void* part[LL_MAX_TP_RANKS];
   unsigned long long* cnt[LL_MAX_TP_RANKS];
   unsigned long long* epoch;
+  const void* mc;
   int rank, world;
 };
 

@@ -91,6 +91,13 @@ class FusedTPComm(NcclTPComm):
         self._hdc = symm_mem.rendezvous(self.dcnt, gname)
         self.dpart_ptrs = [int(p) for p in self._hdp.buffer_ptrs]
         self.dcnt_ptrs = [int(p) for p in self._hdc.buffer_ptrs]
+        # NVLS (SGLANG_PIC_TP_NVLS=1, where the switch supports it): the
+        # decode boundary sums the ranks' partial rows with one multimem load
+        # through the multicast address of the partial buffers
+        import os
+
+        mc = int(getattr(self._hdp, "multicast_ptr", 0) or 0)
+        self.dpart_mc = mc if (os.getenv("SGLANG_PIC_TP_NVLS", "0") == "1" and mc) else 0
         self._dparity = 0
         # greedy over the vocab shards: per-row (max, index) records pushed
         # to every rank ([2 parities][MAX_DECODE_ROWS][8 ranks][pair, tag])
@@ -101,7 +108,8 @@ class FusedTPComm(NcclTPComm):
         self.arec_ptrs = [int(p) for p in self._hak.buffer_ptrs]
         torch.cuda.synchronize(device)
         dist.barrier(group=self.group)  # every counter is zero before any peer adds to it
-        self.stats = {"fused_gemms": 0, "fused_reduces": 0, "fused_decode_reduces": 0, "fused_argmax": 0}
+        self.stats = {"fused_gemms": 0, "fused_reduces": 0, "fused_decode_reduces": 0, "fused_argmax": 0,
+                      "nvls_decode": bool(self.dpart_mc)}
 
     # ------------------------------------------------------------ geometry
     def rows_per_rank(self, T: int) -> int:
@@ -132,9 +140,10 @@ class FusedTPComm(NcclTPComm):
         """residual[:T] += the sum over ranks of their :meth:`decode_part`
         rows; out[:T] = RMSNorm(residual) * w.  Flips the partial buffer."""
         off = self._dparity * MAX_DECODE_ROWS * self.hidden * 2
-        ops._cuda().tp_decode_allreduce_norm(residual, w, out, float(eps), T, [p + off for p in self.dpart_ptrs],
-                                             self.dcnt_ptrs, self.depoch, self.rank, self.size,
-                                             ops.workspace(residual.device).err)
+        ops._cuda().tp_decode_allreduce_norm_nvls(residual, w, out, float(eps), T,
+                                                  [p + off for p in self.dpart_ptrs], self.dcnt_ptrs, self.depoch,
+                                                  self.rank, self.size, ops.workspace(residual.device).err,
+                                                  self.dpart_mc + off if self.dpart_mc else 0)
         self._dparity ^= 1
         self.stats["fused_decode_reduces"] += 1
 
