@@ -282,11 +282,12 @@ def test_attention_prefill_sparse_rows(Hq, Hkv, ps):
     assert _rel(legacy.cpu(), exp) < 1.5e-2
 
 
-@pytest.mark.parametrize("variant", [0, 2, 3, 4])
+@pytest.mark.parametrize("variant", [0, 2, 3, 4, 7, 8])
 def test_attention_prefill_builds_match_fp32(variant):
     """Builds of the tcgen05 kernel (0: one softmax warpgroup per tile, 2:
     with 2 of 8 exp2 on the FMA pipe, 3 and 4: two warpgroups per tile, 64
-    key columns each) on sparse and full causal rows; the second request's
+    key columns each, 7 and 8: 8-chain max and P stored after the whole row)
+    on sparse and full causal rows; the second request's
     queries are scaled up so that running maxima grow mid-row and O is
     rescaled in TMEM."""
     ext = ops._cuda()
