@@ -364,6 +364,14 @@ class BlockRegistry {
     return it->second.token_ids;
   }
 
+  // Content hash of a registered block (None when absent): equal hashes mean
+  // equal token ids, so a caller may keep a converted copy keyed by it.
+  std::optional<std::string> token_hash(const std::string& k) const {
+    auto it = blocks_.find(k);
+    if (it == blocks_.end()) return std::nullopt;
+    return it->second.token_hash;
+  }
+
   bool contains(const std::string& k) const { return blocks_.count(k) != 0; }
   int64_t size() const { return (int64_t)blocks_.size(); }
   int64_t generation() const { return generation_; }
@@ -596,6 +604,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("eviction_candidates", &BlockRegistry::eviction_candidates)
       .def("handle", &BlockRegistry::handle)
       .def("tokens", &BlockRegistry::tokens)
+      .def("token_hash", &BlockRegistry::token_hash)
       .def("contains", &BlockRegistry::contains)
       .def("keys", &BlockRegistry::keys)
       .def("stats", &BlockRegistry::stats)

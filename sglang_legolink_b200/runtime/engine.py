@@ -180,6 +180,7 @@ class Engine:
             max_blocks = int(os.getenv("SGLANG_PIC_MAX_BLOCKS", "256"))
         self.max_blocks = int(max_blocks)
         self.registry = h.BlockRegistry(self.alloc, self.max_blocks, self.residency)
+        self._token_cache: dict = {}  # cache_key -> (content hash, tuple of token ids)
         self.radix = h.RadixIndex(self.alloc, page_size)
         self.legolink_only = legolink_only
         self.compat = self._compat(compat_overrides or {})
@@ -492,9 +493,22 @@ class Engine:
         return {"cache_key": str(cache_key), "status": status, "token_count": n, "first_token": first}
 
     def block_tokens(self, cache_key: str, remote: Optional[dict] = None):
-        t = self.registry.tokens(cache_key)
-        if t is None and remote and cache_key in remote:
-            return list(remote[cache_key].token_ids)
+        """A registered block's token ids as a tuple of ints.  The converted
+        tuple is kept per key with the block's content hash, so a Link over
+        blocks it has seen converts no ids (a re-registered key with other
+        content has another hash and is fetched again)."""
+        h = self.registry.token_hash(cache_key)
+        if h is None:
+            if remote and cache_key in remote:
+                return tuple(remote[cache_key].token_ids)
+            return None
+        hit = self._token_cache.get(cache_key)
+        if hit is not None and hit[0] == h:
+            return hit[1]
+        t = tuple(int(x) for x in self.registry.tokens(cache_key))
+        if len(self._token_cache) >= 4 * max(1, self.max_blocks):
+            self._token_cache.pop(next(iter(self._token_cache)))
+        self._token_cache[cache_key] = (h, t)
         return t
 
     # ------------------------------------------------------------------ link

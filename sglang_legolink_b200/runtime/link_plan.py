@@ -202,7 +202,8 @@ def resolve_link_plan(plan: dict, mutable_input_ids: Sequence[int],
         toks = block_tokens(key)
         if toks is None:
             raise LinkPlanError(f"PIC block is not compiled in this scheduler: {key}")
-        toks = list(map(int, toks))
+        if not isinstance(toks, tuple):  # the engine hands out tuples of ints already
+            toks = tuple(map(int, toks))
         if normalized:
             seg = segs[i]
             if str(seg.get("cache_key")) != key:
