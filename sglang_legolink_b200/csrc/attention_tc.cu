@@ -668,7 +668,7 @@ static const TcBuild kVariants[kNumVariants] = {
     tc_build<1, 0, false>(),       tc_build<1, 0, true>(),  tc_build<1, 2, true>(), tc_build<2, 0, false>(),
     tc_build<2, 2, true>(),        tc_build<1, 0, false, true>(), tc_build<2, 0, false, true>(),
     tc_build<1, 0, false, false, 1>(), tc_build<1, 2, false, false, 1>(), tc_build<1, 0, false, true, 1>()};
-constexpr int kDefaultVariant = 0;
+constexpr int kDefaultVariant = 7;  // SCHED 1: 0.521 vs 0.533 ms on the Link repair case
 
 static int g_attn_variant = -1;
 
