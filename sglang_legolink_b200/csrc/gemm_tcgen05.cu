@@ -72,15 +72,17 @@ __device__ __forceinline__ bool bar_and_128(bool p) {
   return r != 0;
 }
 
-// Tile order: groups of GEMM_GROUP_M m-blocks, m fastest inside a group, so
+// Tile order: groups of `group_m` m-blocks, m fastest inside a group, so
 // the tiles in flight at once (one per SM or SM pair) share a few A row
 // blocks and a few W column blocks; plain m-fastest order re-streams all of
-// A from HBM once per W column block when A does not fit in L2.
+// A from HBM once per W column block when A does not fit in L2.  W is read
+// from HBM once per group, so the host makes a group as large as keeps its
+// A rows L2-resident (gemm_group_m).
 constexpr int GEMM_GROUP_M = 8;
-__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
-  const int per_group = GEMM_GROUP_M * num_n;
-  const int first_m = (t / per_group) * GEMM_GROUP_M;
-  const int gm = min(num_m - first_m, GEMM_GROUP_M);
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group_m, int& mb, int& nb) {
+  const int per_group = group_m * num_n;
+  const int first_m = (t / per_group) * group_m;
+  const int gm = min(num_m - first_m, group_m);
   const int r = t % per_group;
   mb = first_m + r % gm;
   nb = r / gm;
@@ -90,7 +92,7 @@ template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         bf16* __restrict__ C, const bf16* __restrict__ bias, int M, int N, int K, int ldc,
-                        int* err) {
+                        int* err, int group_m) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -137,7 +139,7 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
         int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
+        tile_coords(t, num_m, num_n, group_m, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrSmemEmptyTimeout)) {
             ok = false;
@@ -207,7 +209,7 @@ __global__ void __launch_bounds__(192, 1)
     uint32_t aphase = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
+        tile_coords(t, num_m, num_n, group_m, mb, nb);
       if (!mbar_wait(&tfull[acc], aphase, err, kErrTmemFullTimeout)) break;
       tc_fence_after();
       const int row = mb * GEMM_BM + q * 32 + lane;
@@ -801,7 +803,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     gemm_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmC, int c_bulk, bf16* __restrict__ C,
                             const bf16* __restrict__ bias, int M, int N, int K, int ldc, int* err,
-                            const __grid_constant__ TpArgs tp) {
+                            const __grid_constant__ TpArgs tp, int group_m) {
   using Cfg = Gemm2Cfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -860,7 +862,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       }
       for (int t = pair; t < ntiles && ok; t += npairs) {
         int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
+        tile_coords(t, num_m, num_n, group_m, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrSmemEmptyTimeout)) {
             ok = false;
@@ -934,7 +936,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     int nbox = 0;  // bulk-stored boxes of this warp (c_bulk)
     for (int t = pair; t < ntiles; t += npairs) {
       int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
+        tile_coords(t, num_m, num_n, group_m, mb, nb);
       if (!mbar_wait(&tfull[acc], aphase, err, kErrTmemFullTimeout)) break;
       tc_fence_after();
       const int row0 = mb * 2 * GEMM_BM + (int)crank * GEMM_BM + q * 32;  // this warp's 32-row slice
@@ -1143,6 +1145,26 @@ static bool gemm_bulk_store_enabled() {
   return v == 1;
 }
 
+// m-blocks per tile group: as many as keep the group's A rows (block_rows x
+// K bf16 each) within ~40 MB of L2, at least 8; LL_GEMM_GROUP_M=<n> fixes it.
+static int gemm_group_m(int M, int K, int block_rows) {
+  static int fixed = -1;
+  if (fixed < 0) {
+    const char* e = getenv("LL_GEMM_GROUP_M");
+    fixed = e != nullptr ? atoi(e) : 0;
+    if (fixed < 0) fixed = 0;
+  }
+  const int num_m = (M + block_rows - 1) / block_rows;
+  int g = fixed;
+  if (g == 0) {
+    const double per_block = (double)block_rows * (double)K * 2.0;
+    g = (int)((40.0 * 1024 * 1024) / per_block);
+    if (g < GEMM_GROUP_M) g = GEMM_GROUP_M;
+  }
+  if (g > num_m) g = num_m;
+  return g < 1 ? 1 : g;
+}
+
 static int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -1200,7 +1222,7 @@ extern "C" int ll_gemm_bf16(const bf16* A, int lda, const bf16* W, int ldw, bf16
       init = true;                                                                                    \
     }                                                                                                 \
     kern<<<2 * pairs, 192, Gemm2Cfg<256>::SMEM, stream>>>(tA, tB, tC, c_bulk, C, bias, M, N, K, ldc, err, \
-                                                           TpArgs{});                                \
+                                                           TpArgs{}, gemm_group_m(M, K, 2 * GEMM_BM)); \
   } while (0)
     if (epilogue == kEpiSwiGLU) LL_LAUNCH2(kEpiSwiGLU); else LL_LAUNCH2(kEpiPlain);
 #undef LL_LAUNCH2
@@ -1219,7 +1241,8 @@ extern "C" int ll_gemm_bf16(const bf16* A, int lda, const bf16* W, int ldw, bf16
       set_smem(kern, GemmCfg<BN_>::SMEM);                                                             \
       init = true;                                                                                    \
     }                                                                                                 \
-    kern<<<grid, 192, GemmCfg<BN_>::SMEM, stream>>>(tA, tB, C, bias, M, N, K, ldc, err);              \
+    kern<<<grid, 192, GemmCfg<BN_>::SMEM, stream>>>(tA, tB, C, bias, M, N, K, ldc, err,               \
+                                                    gemm_group_m(M, K, GEMM_BM));                   \
   } while (0)
   if (BN == 256) {
     if (epilogue == kEpiSwiGLU) LL_LAUNCH(256, kEpiSwiGLU); else LL_LAUNCH(256, kEpiPlain);
@@ -1271,7 +1294,7 @@ extern "C" int ll_gemm_bf16_tp(const void* A_, int lda, const void* W_, int ldw,
       init = true;                                                                                    \
     }                                                                                                 \
     kern<<<2 * pairs, 192, Gemm2Cfg<256>::SMEM, stream>>>(tA, tB, tC, c_bulk, C, bias, M, N, K, ldc, err, \
-                                                           *tp);                                     \
+                                                           *tp, gemm_group_m(M, K, 2 * GEMM_BM));    \
   } while (0)
   if (epilogue == kEpiSwiGLU) LL_LAUNCH_TP(kEpiSwiGLU);
   else if (epilogue == kEpiScatter) LL_LAUNCH_TP(kEpiScatter);
