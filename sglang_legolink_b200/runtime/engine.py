@@ -181,6 +181,7 @@ class Engine:
         self.max_blocks = int(max_blocks)
         self.registry = h.BlockRegistry(self.alloc, self.max_blocks, self.residency)
         self._token_cache: dict = {}  # cache_key -> (content hash, tuple of token ids)
+        self._link_side_stream = None  # peer-pool KV links overlap the local one on it
         self.radix = h.RadixIndex(self.alloc, page_size)
         self.legolink_only = legolink_only
         self.compat = self._compat(compat_overrides or {})
@@ -778,28 +779,49 @@ class Engine:
             w.linked_rows = int(sum(len(g[0]) for g in rows.values()))
             for owner, g in rows.items():
                 per_owner.setdefault(owner, []).append(g)
+        # Peer pools are read over NVLink and the local pool from HBM: the
+        # peer launches go on a side stream so that they overlap the local one
+        # (the repair forward after this waits for both).
+        side = None
+        if self.is_cuda and len(per_owner) > 1:
+            if self._link_side_stream is None:
+                self._link_side_stream = torch.cuda.Stream(device=dev)
+            side = self._link_side_stream
+            side.wait_stream(torch.cuda.current_stream(dev))
         for owner, gs in per_owner.items():
             src, dst, lp, gp = (np.concatenate([g[j] for g in gs]) for j in range(4))
             if not src.size:
                 continue
-            t = [torch.from_numpy(src), torch.from_numpy(dst), torch.from_numpy(lp.astype(np.int32)),
-                 torch.from_numpy(gp.astype(np.int32))]
-            if self.is_cuda:
-                t = [_pinned_copy(x.numpy(), dev) for x in t]
-            args = (self.kv.k, self.kv.v, *t, self.model.cos_sin)
-            if owner is None:
-                with timer.span("kv_link_local"):
-                    ops.kv_link_rope(*args)
-                if compare_enabled("kv_link"):  # diagnostic: fused kernel vs the torch statement
-                    emit_trace("kv_link_compare", **compare_kv_link(*args))
-            elif self.is_cuda:  # peer replica's pool, read over NVLink by the link kernel
-                kp, vp, sps, sls = self.peer_pools[owner]
-                with timer.span("kv_link_peer"):
-                    ops.kv_link_rope(*args, src_k_ptr=kp, src_v_ptr=vp, src_page_size=sps, src_layer_stride=sls)
-                self.stats["peer_tokens_linked"] = self.stats.get("peer_tokens_linked", 0) + int(src.size)
-            else:
-                ops.kv_link_rope(*args, src_pools=self.peer_pools[owner])
-                self.stats["peer_tokens_linked"] = self.stats.get("peer_tokens_linked", 0) + int(src.size)
+            if side is not None and owner is not None:
+                with torch.cuda.stream(side):
+                    self._launch_kv_link(owner, src, dst, lp, gp, timer)
+                continue
+            self._launch_kv_link(owner, src, dst, lp, gp, timer)
+        if side is not None:
+            torch.cuda.current_stream(dev).wait_stream(side)
+
+    def _launch_kv_link(self, owner, src, dst, lp, gp, timer) -> None:
+        """One fused KV-link launch for the linked tokens whose source pool
+        is ``owner``'s (None: this replica's) on the current stream."""
+        dev = self.device
+        t = [torch.from_numpy(src), torch.from_numpy(dst), torch.from_numpy(lp.astype(np.int32)),
+             torch.from_numpy(gp.astype(np.int32))]
+        if self.is_cuda:
+            t = [_pinned_copy(x.numpy(), dev) for x in t]
+        args = (self.kv.k, self.kv.v, *t, self.model.cos_sin)
+        if owner is None:
+            with timer.span("kv_link_local"):
+                ops.kv_link_rope(*args)
+            if compare_enabled("kv_link"):  # diagnostic: fused kernel vs the torch statement
+                emit_trace("kv_link_compare", **compare_kv_link(*args))
+        elif self.is_cuda:  # peer replica's pool, read over NVLink by the link kernel
+            kp, vp, sps, sls = self.peer_pools[owner]
+            with timer.span("kv_link_peer"):
+                ops.kv_link_rope(*args, src_k_ptr=kp, src_v_ptr=vp, src_page_size=sps, src_layer_stride=sls)
+            self.stats["peer_tokens_linked"] = self.stats.get("peer_tokens_linked", 0) + int(src.size)
+        else:
+            ops.kv_link_rope(*args, src_pools=self.peer_pools[owner])
+            self.stats["peer_tokens_linked"] = self.stats.get("peer_tokens_linked", 0) + int(src.size)
 
     def _promote_group(self, resolved: ResolvedLinkPlan, pages: list[int], plan: dict, rid: str) -> Optional[dict]:
         """EXPERIMENTAL.  Makes a fully reconstructed execution group durable:
