@@ -14,9 +14,17 @@ sessions link the copies of the next replica, so their reused blocks are read
 from a peer GPU's pool over NVLink by the link kernel.  (One turn of tool
 history keeps 20 turns inside the context window.)
 
-Timed on the device per replica (CUDA events around each Link and each
+Two arms for the Links of a round (``--arm``): ``batched`` -- a replica's
+Links of the round go through one step (one fused KV-link launch per source
+pool, one extend forward for every repair row), each Link's TTFT is that
+step; ``serial`` -- one Link per forward, all arriving together, so the k-th
+Link's TTFT includes the k - 1 before it (the reference admits a Link alone,
+``managers/scheduler.py:2597-2690``).  ``both`` (default) runs both each
+round and decodes the batched arm's sequences.
+
+Timed on the device per replica (CUDA events around each Link step and each
 decode batch, after a warm-up round), reported as the max over replicas:
-Link TTFT p50 / p95, decode tok/s summed over replicas, and turns/s.
+Link TTFT p50 / p95 per arm, decode tok/s summed over replicas, and turns/s.
 
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m sglang_legolink_b200.benchmarks.dp_sessions
 """
@@ -41,6 +49,9 @@ def main():
     ap.add_argument("--instruction", type=int, default=2048)
     ap.add_argument("--schema", type=int, default=4096)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--arm", default="both", choices=["batched", "serial", "both"],
+                    help="batched: a round's Links of a replica go through one extend forward; serial: one Link "
+                         "per forward (a Link waits for the ones before it); both: each round runs both")
     a = ap.parse_args()
 
     import torch
@@ -92,7 +103,7 @@ def main():
     peer = (rank + 1) % world
     owner = {s: (peer if (world > 1 and (s // world) % 2 == 1 and a.peer_frac > 0) else rank) for s in mine}
     prev = {s: None for s in mine}
-    links, decode_ms, turns_done, peer_links = [], 0.0, 0, 0
+    links, serial_links, decode_ms, turns_done, peer_links = [], [], 0.0, 0, 0
     tokens_decoded = 0
     for turn in range(a.turns + 1):  # turn 0 is the warm-up round
         timed = turn > 0
@@ -105,20 +116,44 @@ def main():
         bad = [r for r in res if isinstance(r, Exception)]
         if bad:
             raise bad[0]
-        seqs = []
+        reqs = []
         for s in mine:
             o = owner[s]
             ck = [f"instr@{o}", f"schema@{o}"] + ([prev[s]] if prev[s] else []) + [keys[s]]
             query = [rng.randrange(V) for _ in range(64)]
+            reqs.append(({"cache_keys": ck, "recompute_initial_tokens": 32, "recompute_first_block": True}, query))
+            if timed:
+                peer_links += int(o != rank)
+        seqs = []
+        if a.arm in ("serial", "both"):
+            # the round's Links arrive together and run one per forward: the
+            # k-th one's TTFT includes the k - 1 before it
+            waited = 0.0
+            for plan, query in reqs:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                seq = eng.link(dict(plan), query)
+                e1.record()
+                e1.synchronize()
+                waited += e0.elapsed_time(e1)
+                if timed:
+                    serial_links.append(waited)
+                if a.arm == "serial":
+                    seqs.append(seq)
+                else:
+                    eng.free(seq)
+        if a.arm in ("batched", "both"):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            seq = eng.link({"cache_keys": ck, "recompute_initial_tokens": 32, "recompute_first_block": True}, query)
+            out = eng.link_batch([(dict(plan), query) for plan, query in reqs])
             e1.record()
             e1.synchronize()
+            bad = [r for r in out if isinstance(r, Exception)]
+            if bad:
+                raise bad[0]
             if timed:
-                links.append(e0.elapsed_time(e1))
-                peer_links += int(o != rank)
-            seqs.append(seq)
+                links.extend([e0.elapsed_time(e1)] * len(out))
+            seqs = list(out)
         d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         d0.record()
         eng.decode(seqs, a.decode - 1)
@@ -134,22 +169,35 @@ def main():
             if prev[s]:
                 eng.unregister_block(prev[s])  # published: withdrawn from the directory first
             prev[s] = keys[s]
-    total_ms = sum(links) + decode_ms
-    stats = torch.tensor([statistics.median(links), sorted(links)[int(0.95 * (len(links) - 1))], decode_ms,
-                          total_ms], dtype=torch.float64, device=dev)
-    sums = torch.tensor([tokens_decoded / (decode_ms / 1e3), turns_done, peer_links, len(links)],
+    primary = links if links else serial_links
+    n = max(1, len(mine))
+    if links:  # a round's batched step is counted once per Link in it
+        link_round_ms = sum(links) / n
+    else:  # the last Link of a round waited for the whole round
+        link_round_ms = sum(serial_links[n - 1::n])
+    total_ms = link_round_ms + decode_ms
+
+    def pct(xs, q):
+        return sorted(xs)[int(q * (len(xs) - 1))] if xs else 0.0
+
+    stats = torch.tensor([statistics.median(primary), pct(primary, 0.95), decode_ms, total_ms,
+                          statistics.median(serial_links) if serial_links else 0.0, pct(serial_links, 0.95)],
+                         dtype=torch.float64, device=dev)
+    sums = torch.tensor([tokens_decoded / (decode_ms / 1e3), turns_done, peer_links, len(primary)],
                         dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
         dist.all_reduce(sums, op=dist.ReduceOp.SUM)
-    p50, p95, dec_ms_max, total_max = stats.tolist()
+    p50, p95, dec_ms_max, total_max, s50, s95 = stats.tolist()
     tok_s, turns_all, peers, nlinks = sums.tolist()
     if rank == 0:
         print(json.dumps({
             "metric": "DP replicas sharing one block registry: Link TTFT and decode tok/s",
             "model": f"{a.model} (random init)", "replicas": world, "sessions": a.sessions, "turns": a.turns,
             "decode_tokens": a.decode, "peer_block_fraction": round(peers / max(nlinks, 1), 3),
-            "link_ttft_ms_p50": round(p50, 3), "link_ttft_ms_p95": round(p95, 3),
+            "arm": a.arm, "link_ttft_ms_p50": round(p50, 3), "link_ttft_ms_p95": round(p95, 3),
+            **({"serial_link_ttft_ms_p50": round(s50, 3), "serial_link_ttft_ms_p95": round(s95, 3)}
+               if a.arm == "both" else {}),
             "decode_tok_s": round(tok_s, 1), "turns_per_s": round(turns_all / (total_max / 1e3), 2),
             "timing": "CUDA events per replica, max over replicas (tok/s summed)",
             "history": "one previous tool output per turn",
