@@ -14,7 +14,8 @@ reduces with NCCL.
 
     torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m sglang_legolink_b200.benchmarks.tp_link
 
-Prints one JSON line (rank 0).
+Prints one JSON line (rank 0), with the per-rank roofline of the Link and
+of a decode step and the achieved fraction of each.
 """
 
 from __future__ import annotations
@@ -26,6 +27,42 @@ import os
 import random
 import statistics
 import time
+
+
+NVLINK_GBS = 770.0
+
+
+def rooflines(cfg, world: int, plan, batch: int, ctx: int, pk: dict) -> dict:
+    """Per-rank roofline of one Link and of one batch decode step.
+
+    Link: the slower of (GEMM + attention FLOPs of the repair rows at the
+    measured bf16 peak, plus the KV link's HBM bytes at the measured copy
+    bandwidth) and (bytes the fused layer boundaries move over NVLink: 2 x
+    (W-1)/W x rows x hidden x 2 per boundary, two per layer, at 770 GB/s).
+    Decode step: this rank's weight bytes plus the K/V bytes of ``batch``
+    contexts of ``ctx`` tokens, at the measured copy bandwidth."""
+    L, H, D, I, V = cfg.num_layers, cfg.hidden_size, cfg.head_dim, cfg.intermediate_size, cfg.vocab_size
+    hq, hkv = cfg.num_heads // world, max(1, cfg.num_kv_heads // world)
+    rows = list(plan.recompute_positions)
+    T = len(rows)
+    gemm = 2 * T * H * ((hq + 2 * hkv) * D + hq * D + 2 * I // world + I // world) * L
+    attn = 4 * D * hq * float(sum(p + 1 for p in rows)) * L
+    linked = plan.total_token_count - T
+    kv_link_bytes = linked * L * hkv * D * 2 * 2 * 2
+    compute_ms = (gemm + attn) / (pk["bf16_tflops"] * 1e9) + kv_link_bytes / (pk["hbm_gbs"] * 1e6)
+    nvlink_ms = (2 * 2 * (world - 1) / world * T * H * 2 * L) / (NVLINK_GBS * 1e6) if world > 1 else 0.0
+    w_bytes = 2 * L * H * ((hq + 2 * hkv) * D + hq * D + 2 * I // world + I // world) + 2 * H * V // world
+    kv_bytes = batch * ctx * L * hkv * D * 2 * 2
+    return {"link_roofline_ms": round(max(compute_ms, nvlink_ms), 3),
+            "link_roofline_terms_ms": {"compute_and_kv_link": round(compute_ms, 3), "nvlink": round(nvlink_ms, 3)},
+            "decode_roofline_ms_per_step": round((w_bytes + kv_bytes) / (pk["hbm_gbs"] * 1e6), 3),
+            "peaks": pk["src"]}
+
+
+def peaks() -> dict:
+    from .kernels import peaks as _p
+
+    return _p()
 
 
 def main():
@@ -146,6 +183,9 @@ def main():
         "timing": "CUDA events, max over ranks", "data": "synthetic agent contexts (seeded), random-init weights",
         "init_s": round(init_s, 1),
     }
+    out.update(rooflines(cfg, world, seqs[-1].link_plan, a.batch, a.context + 64, peaks()))
+    out["link_frac_of_roofline"] = round(out["link_roofline_ms"] / out["link_ttft_ms_p50"], 3)
+    out["decode_frac_of_roofline"] = round(out["decode_roofline_ms_per_step"] / out["decode_ms_per_step"], 3)
     if comm is not None and hasattr(comm, "stats"):
         out["fused_stats"] = dict(comm.stats)
     if rank == 0:
