@@ -91,13 +91,15 @@ class FusedTPComm(NcclTPComm):
         self._hdc = symm_mem.rendezvous(self.dcnt, gname)
         self.dpart_ptrs = [int(p) for p in self._hdp.buffer_ptrs]
         self.dcnt_ptrs = [int(p) for p in self._hdc.buffer_ptrs]
-        # NVLS (SGLANG_PIC_TP_NVLS=1, where the switch supports it): the
-        # decode boundary sums the ranks' partial rows with one multimem load
-        # through the multicast address of the partial buffers
+        # NVLS (wherever the buffers have a multicast address, unless
+        # SGLANG_PIC_TP_NVLS=0): the decode boundary sums the ranks' partial
+        # rows with one multimem load through the multicast address instead
+        # of one peer load per rank (TP=4, batch 16: 14.99 vs 28.96 ms/step;
+        # NCCL 21.59 ms on the same box)
         import os
 
         mc = int(getattr(self._hdp, "multicast_ptr", 0) or 0)
-        self.dpart_mc = mc if (os.getenv("SGLANG_PIC_TP_NVLS", "0") == "1" and mc) else 0
+        self.dpart_mc = mc if (os.getenv("SGLANG_PIC_TP_NVLS", "1") != "0" and mc) else 0
         self._dparity = 0
         # greedy over the vocab shards: per-row (max, index) records pushed
         # to every rank ([2 parities][MAX_DECODE_ROWS][8 ranks][pair, tag])
