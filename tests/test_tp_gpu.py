@@ -33,3 +33,20 @@ def test_tp2_fused_gpu():
     r = subprocess.run(cmd, capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "TP_FUSED_OK" in r.stdout
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_tp2_fused_nvls_gpu():
+    """The same checks with multicast available: the decode boundary reads
+    the ranks' partial rows through NVLS multimem loads (no rank is lost in
+    this test)."""
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29542",
+           os.path.join(ROOT, "tests", "tp_fused_worker.py")]
+    env = {k: v for k, v in os.environ.items() if k != "TORCH_SYMM_MEM_DISABLE_MULTICAST"}
+    env["SGLANG_PIC_TP_NVLS"] = "1"
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "TP_FUSED_OK" in r.stdout
+
