@@ -11,11 +11,14 @@ the smallest cases).  Reported against the roofline:
   direction) and the bytes written to local HBM.
 
     python -m sglang_legolink_b200.benchmarks.kv_link_sweep            # local, 1 GPU
-    torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m sglang_legolink_b200.benchmarks.kv_link_sweep --peer
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 -m sglang_legolink_b200.benchmarks.kv_link_sweep --peer
 
-With ``--peer`` rank 1 links blocks that live in rank 0's symmetric-memory
-pool (P2P loads by the link kernel, no TMA multicast); every rank takes the
-same collective steps, and rank 0 prints.
+With ``--peer`` on N ranks every rank links, at the same time, blocks that
+live in the symmetric-memory pool of rank (r + 1) mod N (P2P loads by the
+link kernel, no TMA multicast), so at N = 8 all eight GPUs read over NVSwitch
+at once; with N = 2 and ``--one-way`` only rank 1 links (from rank 0).  Every
+rank takes the same collective steps; the time is the max over the linking
+ranks, and rank 0 prints.
 """
 
 from __future__ import annotations
@@ -88,7 +91,8 @@ def timed(fn, reps=10):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--peer", action="store_true", help="sources on a peer GPU (2 ranks under torchrun)")
+    ap.add_argument("--peer", action="store_true", help="sources on a peer GPU (N >= 2 ranks under torchrun)")
+    ap.add_argument("--one-way", action="store_true", help="with --peer: only rank 1 links (from rank 0)")
     ap.add_argument("--quick", action="store_true")
     a = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -100,8 +104,8 @@ def main():
     cs = ref.rope_cos_sin_table(32768 + 8192 + 64, D, 1e6).to(dev)
     dist = None
     if a.peer:
-        if world != 2:
-            raise SystemExit("--peer runs on exactly 2 ranks")
+        if world < 2:
+            raise SystemExit("--peer runs on 2 or more ranks")
         from datetime import timedelta
 
         import torch.distributed as dist
@@ -129,14 +133,14 @@ def main():
             del kp, vp
         else:
             pool = SharedKVPool(L, pages, HKV, ps, D, torch.bfloat16, dev)
-            if rank == 0:
-                pool.k.normal_()
-                pool.v.normal_()
+            pool.k.normal_()
+            pool.v.normal_()
             torch.cuda.synchronize()
             dist.barrier()
             ms = 0.0
-            if rank == 1:
-                kp_ptr, vp_ptr, sps, sls = pool.peer(0)
+            linking = rank == 1 if a.one_way else True
+            if linking:
+                kp_ptr, vp_ptr, sps, sls = pool.peer(0 if a.one_way else (rank + 1) % world)
                 ms = timed(lambda: ops.kv_link_rope(pool.k, pool.v, s, d, lpt, gpt, cs, src_k_ptr=kp_ptr,
                                                     src_v_ptr=vp_ptr, src_page_size=sps, src_layer_stride=sls))
             t = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -145,8 +149,11 @@ def main():
             remote = 2 * n * row_bytes
             roof_ms = max(remote / (NVLINK_GBS * 1e6), remote / (pk["hbm_gbs"] * 1e6))
             if rank == 0:
-                print(json.dumps({**base, "source": "peer_gpu", "ms": round(ms, 4),
-                                  "nvlink_gbs": round(remote / ms / 1e6, 1), "roofline_ms": round(roof_ms, 4),
+                nlink = 1 if a.one_way else world
+                print(json.dumps({**base, "source": "peer_gpu", "world": world, "linking_ranks": nlink, "ms": round(ms, 4),
+                                  "nvlink_gbs": round(remote / ms / 1e6, 1),
+                                  "aggregate_nvlink_gbs": round(nlink * remote / ms / 1e6, 1),
+                                  "roofline_ms": round(roof_ms, 4),
                                   "frac_of_roofline": round(roof_ms / ms, 3), "nvlink_ref_gbs": NVLINK_GBS,
                                   "timing": "max over ranks"}), flush=True)
             dist.barrier()
