@@ -16,6 +16,13 @@ reduces with NCCL.
 
 Prints one JSON line (rank 0), with the per-rank roofline of the Link and
 of a decode step and the achieved fraction of each.
+
+``--shard W`` on ONE process runs one rank's share of TP = W with no
+communication (heads, KV heads, intermediate and vocabulary divided by W), to
+separate a rank's own kernels from the collectives.  ``--profile`` then
+prints, per phase (a Link, eight decode steps), each kernel's share of the
+device time and the device idle time between kernels, from the CUDA activity
+trace of ``torch.profiler``.
 """
 
 from __future__ import annotations
@@ -76,6 +83,8 @@ def main():
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--shard", type=int, default=1, help="one process: one rank's share of TP = SHARD, no comm")
+    ap.add_argument("--profile", action="store_true", help="per-kernel breakdown of a Link and 8 decode steps")
     a = ap.parse_args()
 
     import torch
@@ -104,6 +113,15 @@ def main():
 
             comm = NcclTPComm()
     cfg = PRESETS[a.model]
+    if a.shard > 1:
+        if world > 1:
+            raise SystemExit("--shard runs on one process")
+        import dataclasses
+
+        cfg = dataclasses.replace(cfg, num_heads=cfg.num_heads // a.shard,
+                                  num_kv_heads=max(1, cfg.num_kv_heads // a.shard),
+                                  intermediate_size=cfg.intermediate_size // a.shard,
+                                  vocab_size=cfg.vocab_size // a.shard, name=f"{cfg.name}/shard{a.shard}")
     t0 = time.time()
     model = QwenModel.random_init(cfg, seed=a.seed, device=dev, dtype=torch.bfloat16, tp_rank=rank, tp_size=world,
                                   comm=comm)
@@ -118,7 +136,7 @@ def main():
     per_seq = pages_for(a.context + 64 + a.decode + 16, ps)
     compiled = sum(pages_for(n, ps) for n in lens[:n_link])
     eng = Engine(model, page_size=ps, max_context=a.context + a.decode + 1024,
-                 num_pages=a.batch * per_seq + compiled + 64)
+                 num_pages=(a.batch + int(a.profile)) * per_seq + compiled + 64)
     init_s = time.time() - t0
     subs = [[rng.randrange(cfg.vocab_size) for _ in range(n)] for n in lens]
     for i in range(n_link):
@@ -174,7 +192,8 @@ def main():
     dec_ms = maxr([dec_ms])[0]
     out = {
         "metric": "Link-request p50 TTFT and decode tok/s, Qwen3-32B TP",
-        "model": f"{a.model} (random init)", "tp": world, "comm": a.comm if world > 1 else "none",
+        "model": f"{cfg.name} (random init)", "tp": world, "comm": a.comm if world > 1 else "none",
+        "shard": a.shard,
         "context": a.context, "subcontexts": a.subcontexts, "linked": n_link, "repair_window": a.repair,
         "recompute_rows": rows, "batch": a.batch, "decode_tokens": a.decode,
         "link_ttft_ms_p50": round(statistics.median(links), 3), "link_ttft_ms_max": round(max(links), 3),
@@ -190,6 +209,30 @@ def main():
         out["fused_stats"] = dict(comm.stats)
     if rank == 0:
         print(json.dumps(out), flush=True)
+    if a.profile:
+        from torch.profiler import ProfilerActivity, profile, record_function
+
+        from .link_profile import summarize, timeline
+
+        plan, suffix = request(10_000)
+        barrier()
+        with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+            with record_function("link_call"):
+                s = eng.link(plan, suffix)
+            torch.cuda.synchronize()
+        if rank == 0:
+            summarize(prof, "link")
+            print("   timeline:", timeline(prof, "link_call"), flush=True)
+        eng.free(s)
+        barrier()
+        with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+            with record_function("decode_call"):
+                eng.decode(seqs, 8)
+            torch.cuda.synchronize()
+        if rank == 0:
+            summarize(prof, f"decode x8, batch {a.batch}")
+            print("   timeline:", timeline(prof, "decode_call"), flush=True)
+        barrier()
     for s in seqs:
         eng.free(s)
     torch.cuda.synchronize()
