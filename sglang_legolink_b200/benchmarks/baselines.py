@@ -88,7 +88,7 @@ def link_workload():
     bench = importlib.import_module("bench")
     from ..runtime.link_plan import resolve_link_plan
 
-    subs = bench.synthetic_context(12, 16384, 152064, 0)
+    subs = bench.context_tokens(bench.context_lengths(12, 16384, 0), 152064, 0, 0)
     rng = random.Random(1)
     order = list(range(10))
     rng.shuffle(order)

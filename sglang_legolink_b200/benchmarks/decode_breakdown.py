@@ -1,12 +1,17 @@
-"""Per-op device time of one decode step (batch 1, Qwen2.5-7B, 16K context)
-measured the way the step runs: each op is captured into a CUDA graph as 28
-launches (one per layer, on that layer's own weights / KV, so every launch
-streams from HBM like the real step), replayed, and timed with CUDA events.
+"""Per-op device time of one decode step (default: batch 1, Qwen2.5-7B, 16K
+context) measured the way the step runs: each op is captured into a CUDA
+graph as one launch per layer (on that layer's own weights / KV, so every
+launch streams from HBM like the real step), replayed, and timed with CUDA
+events.
 
     python -m sglang_legolink_b200.benchmarks.decode_breakdown [--context 16640]
+    python -m sglang_legolink_b200.benchmarks.decode_breakdown --model qwen3-32b --shard 8 --batch 16 --context 32832
 
-Prints one JSON line per op: microseconds per layer and the fraction of the
-measured HBM bandwidth its bytes would take.
+``--batch B`` decodes B requests of ``--context`` keys each; ``--shard W``
+takes one rank's share of TP = W (heads, KV heads, intermediate size and
+vocabulary divided by W) with no communication.  Prints one JSON line per
+op: microseconds per layer and the fraction of the measured HBM bandwidth
+its bytes (weights, and K/V for attention) would take.
 """
 
 from __future__ import annotations
@@ -49,41 +54,51 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="qwen2.5-7b")
     ap.add_argument("--context", type=int, default=16640)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--shard", type=int, default=1)
     a = ap.parse_args()
     cfg = PRESETS[a.model]
+    if a.shard > 1:
+        import dataclasses
+
+        cfg = dataclasses.replace(cfg, num_heads=cfg.num_heads // a.shard,
+                                  num_kv_heads=max(1, cfg.num_kv_heads // a.shard),
+                                  intermediate_size=cfg.intermediate_size // a.shard,
+                                  vocab_size=cfg.vocab_size // a.shard, name=f"{cfg.name}/shard{a.shard}")
+    B = a.batch
     dev = torch.device("cuda")
     m = QwenModel.random_init(cfg, seed=0, device=dev, dtype=torch.bfloat16)
     L, H, D = cfg.num_layers, cfg.hidden_size, cfg.head_dim
     hq, hkv, inter = m.hq, m.hkv, m.inter
     n, ps = a.context, 16
-    pages = (n + ps - 1) // ps
+    pps = (n + ps - 1) // ps  # pages per request
+    pages = B * pps
     kpool = torch.randn(L, pages, hkv, ps, D, device=dev, dtype=torch.bfloat16)
     vpool = torch.randn_like(kpool)
-    pt = torch.arange(pages, device=dev, dtype=torch.int32)[None]
-    kvl = torch.tensor([n], device=dev, dtype=torch.int32)
-    pos = torch.tensor([n - 1], device=dev, dtype=torch.int32)
-    slot = torch.tensor([n - 1], device=dev, dtype=torch.int64)
-    x = torch.randn(1, H, device=dev, dtype=torch.bfloat16)
-    res = torch.randn(1, H, device=dev, dtype=torch.bfloat16)
-    qkv = torch.empty(1, (hq + 2 * hkv) * D, device=dev, dtype=torch.bfloat16)
-    q = torch.randn(1, hq, D, device=dev, dtype=torch.bfloat16)
-    attn = torch.empty(1, hq * D, device=dev, dtype=torch.bfloat16)
-    o = torch.empty(1, H, device=dev, dtype=torch.bfloat16)
-    gu = torch.empty(1, 2 * inter, device=dev, dtype=torch.bfloat16)
-    mlp = torch.randn(1, inter, device=dev, dtype=torch.bfloat16)
-    nsplit = ops.decode_splits(1, hkv, n)
+    pt = torch.arange(pages, device=dev, dtype=torch.int32).view(B, pps)
+    kvl = torch.full((B,), n, device=dev, dtype=torch.int32)
+    pos = torch.full((B,), n - 1, device=dev, dtype=torch.int32)
+    slot = torch.arange(B, device=dev, dtype=torch.int64) * (pps * ps) + (n - 1)
+    x = torch.randn(B, H, device=dev, dtype=torch.bfloat16)
+    res = torch.randn(B, H, device=dev, dtype=torch.bfloat16)
+    qkv = torch.empty(B, (hq + 2 * hkv) * D, device=dev, dtype=torch.bfloat16)
+    q = torch.randn(B, hq, D, device=dev, dtype=torch.bfloat16)
+    attn = torch.empty(B, hq * D, device=dev, dtype=torch.bfloat16)
+    gu = torch.empty(B, 2 * inter, device=dev, dtype=torch.bfloat16)
+    mlp = torch.randn(B, inter, device=dev, dtype=torch.bfloat16)
+    nsplit = ops.decode_splits(B, hkv, n)
     ops.workspace(dev).reserve_decode(hq, nsplit, D)
     for lw in m.layers[:1]:  # reserve GEMM workspaces outside capture
         ops.linear(x, lw.gu_w, out=gu)
         ops.linear(x, lw.qkv_w, out=qkv)
     scale = 1.0 / math.sqrt(D)
     pk = peaks()
-    kvb = n * hkv * D * 2 * 2
+    kvb = B * n * hkv * D * 2 * 2
     # the five kernels of the fused decode layer (QwenModel._forward_decode_fused)
     eps = cfg.rms_norm_eps
-    ss = ops.sumsq_from_values(torch.full((1,), float(H), device=dev))
-    sq = ops.sumsq_buffer(1, dev)
-    hp = torch.empty(1, H, device=dev, dtype=torch.bfloat16)
+    ss = ops.sumsq_from_values(torch.full((B,), float(H), device=dev))
+    sq = ops.sumsq_buffer(B, dev)
+    hp = torch.empty(B, H, device=dev, dtype=torch.bfloat16)
     cases = {
         "gemv_qkv_rope": (lambda: [ops.gemv_qkv_rope(x, lw.qkv_w, lw.qkv_b, pos, slot, m.cos_sin, q, kpool[i],
                                                      vpool[i], hq, hkv, lw.q_norm, lw.k_norm, eps, scale_sumsq=ss)
@@ -103,10 +118,11 @@ def main():
         us = ms * 1e3 / L
         total += us
         roof_us = bytes_per_layer / (pk["hbm_gbs"] * 1e3)
-        print(json.dumps({"op": name, "us_per_layer": round(us, 2), "us_per_token": round(us * L, 1),
+        print(json.dumps({"op": name, "model": cfg.name, "batch": B, "context": n, "nsplit": nsplit,
+                          "us_per_layer": round(us, 2), "us_per_step": round(us * L, 1),
                           "roofline_us_per_layer": round(roof_us, 2), "frac_of_hbm": round(roof_us / us, 3),
                           "peaks": pk["src"]}), flush=True)
-    print(json.dumps({"op": "sum_of_layer_ops", "ms_per_token": round(total * L / 1e3, 3)}), flush=True)
+    print(json.dumps({"op": "sum_of_layer_ops", "ms_per_step": round(total * L / 1e3, 3)}), flush=True)
     lm = graph_time(lambda: ops.linear(x, m.lm_head))
     print(json.dumps({"op": "gemv_lm_head", "us": round(lm * 1e3, 1),
                       "frac_of_hbm": round(m.lm_head.numel() * 2 / (pk["hbm_gbs"] * 1e3) / (lm * 1e3), 3)}))

@@ -45,3 +45,22 @@ def test_sources_name_no_notes_file_or_machine_path():
             if n in text:
                 bad.append(f"{f.relative_to(ROOT)}: {n}")
     assert not bad, bad
+
+
+def test_benchmark_modules_import_and_share_the_headline_workload():
+    """Every benchmark module with a ``main`` imports on CPU (``ncu_cases``
+    is a script that runs its case on import), and the library-baseline
+    bench builds the same Link layout as the headline bench (5087 repair rows
+    of a 16416-token request)."""
+    import importlib
+    import sys
+
+    sys.path.insert(0, str(ROOT))
+    pkg = ROOT / "sglang_legolink_b200" / "benchmarks"
+    for f in sorted(pkg.glob("*.py")):
+        if f.stem != "__init__" and "def main(" in f.read_text():
+            importlib.import_module(f"sglang_legolink_b200.benchmarks.{f.stem}")
+    from sglang_legolink_b200.benchmarks.baselines import link_workload
+
+    plan = link_workload()
+    assert len(plan.recompute_positions) == 5087 and plan.total_token_count == 16416
