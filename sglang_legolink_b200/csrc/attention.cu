@@ -573,6 +573,15 @@ static bool decode_tma_enabled() {
   return v == 1;
 }
 
+// Combine of split-KV partials: rows x nsplit partials [rows][nsplit][128]
+// (fp32) with (max log2, sum) each -> out [rows][128] (bf16).
+extern "C" int ll_attn_combine(bf16* out, const float* ws_o, const float* ws_ml, int rows, int nsplit,
+                               cudaStream_t stream) {
+  if (rows <= 0 || nsplit < 1 || nsplit > CB_MAX_SPLITS) return -3;
+  launch_pdl(attn_combine_kernel, dim3(rows), dim3(CB_THREADS), 0, stream, out, ws_o, ws_ml, nsplit);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
 extern "C" int ll_attn_decode(const bf16* q, const bf16* kpool, const bf16* vpool, int num_pages,
                               const int* page_table, int pt_stride, const int* kv_lens, bf16* out, float* ws_o,
                               float* ws_ml, int B, int Hq, int Hkv, int head_dim, int page_size, int nsplit,

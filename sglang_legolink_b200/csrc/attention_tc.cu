@@ -218,7 +218,8 @@ __global__ void __launch_bounds__(TcCfg<CS>::THREADS, 1)
                            const bf16* __restrict__ q, const int* __restrict__ q_indptr,
                            const int* __restrict__ q_pos, const int* __restrict__ page_table, int pt_stride,
                            const int4* __restrict__ tiles, bf16* __restrict__ out, int Hq, int Hkv, int ps,
-                           int layer, float scale_log2, int* err) {
+                           int layer, float scale_log2, int* err, int nsplit_arg, float* __restrict__ ws_o,
+                           float* __restrict__ ws_ml) {
   using Cfg = TcCfg<CS>;
   constexpr int NC = Cfg::NC;
   extern __shared__ uint8_t smem_raw[];
@@ -241,11 +242,23 @@ __global__ void __launch_bounds__(TcCfg<CS>::THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int4 tile = tiles[blockIdx.x];
-  const int b = tile.x, hk = tile.y, row0 = tile.z, max_pos = tile.w;
+  // tile.y = kv head | split << 8 | split count << 16 (split count 0 = 1):
+  // with a split count S > 1 this CTA walks the split-th of S equal key
+  // ranges of the tile and writes an unnormalised partial (fp32 O, running
+  // max in the log2 domain, row sum) for attn_combine_kernel.
+  const int b = tile.x, hk = tile.y & 0xff, row0 = tile.z, max_pos = tile.w;
+  const int split = (tile.y >> 8) & 0xff, nsplit = max(1, tile.y >> 16);
+  if (nsplit != max(1, nsplit_arg) || (nsplit > 1 && (ws_o == nullptr || ws_ml == nullptr))) {
+    if (threadIdx.x == 0) record_error(err, kErrBadIndex);  // work list and launch disagree: nothing written
+    return;
+  }
   const int g = Hq / Hkv;
   const int s0 = q_indptr[b];
   const int nrows = (q_indptr[b + 1] - s0) * g;
-  const int nb = max_pos / TC_BN + 1;
+  const int nb_all = max_pos / TC_BN + 1;
+  const int chunk = (nb_all + nsplit - 1) / nsplit;
+  const int jb = min(nb_all, split * chunk);   // first key block of this CTA
+  const int nb = min(nb_all, jb + chunk) - jb;  // its key blocks (0 for an empty split)
   const int* pt = page_table + (size_t)b * pt_stride;
 
   if (threadIdx.x == 0) {
@@ -304,10 +317,10 @@ __global__ void __launch_bounds__(TcCfg<CS>::THREADS, 1)
         }
       };
       bool ok = true;
-      int y_next = page_of(0);
-      for (int j = 0; j < nb; ++j) {
+      int y_next = nb > 0 ? page_of(jb) : -1;
+      for (int j = 0; j < nb; ++j) {  // j: block of this CTA's range (ring index); jb + j: key block
         const int y = y_next;
-        if (j + 1 < nb) y_next = page_of(j + 1);
+        if (j + 1 < nb) y_next = page_of(jb + j + 1);
         const int sk = j % TC_KS, sv = j % TC_VS;
         bool w = true;
         if (lane == 0) w = mbar_wait(&k_empty[sk], ((j / TC_KS) & 1) ^ 1, err, kErrSmemEmptyTimeout);
@@ -376,7 +389,7 @@ __global__ void __launch_bounds__(TcCfg<CS>::THREADS, 1)
           if (!ok) break;
           umma_commit(&k_empty[sk]);
         }
-        if (ok) {
+        if (ok && nb > 0) {
           const int i = nb - 1;
           for (int t = 0; t < TC_NT && ok; ++t) {
             if (!mbar_wait(&p_full[t], i & 1, err, kErrTmemFullTimeout)) { ok = false; break; }
@@ -460,7 +473,7 @@ __global__ void __launch_bounds__(TcCfg<CS>::THREADS, 1)
       tmem_ld_wait();
       if (r == 0 && h == 0) TC_TR(j, 3 * t + 1);
       if (MASK) {
-        const int lim = pos - j * TC_BN - h * NC;  // scores with index > lim are masked
+        const int lim = pos - (jb + j) * TC_BN - h * NC;  // scores with index > lim are masked
 #pragma unroll
         for (int i = 0; i < NC; ++i)
           if (i > lim) s[i] = __float_as_uint(-INFINITY);
@@ -562,8 +575,8 @@ __global__ void __launch_bounds__(TcCfg<CS>::THREADS, 1)
       return true;
     };
     bool ok = true;
-    int j = 0;
-    for (; j < jd && ok; ++j) ok = step(j, std::false_type{});
+    int j = 0;  // block of this CTA's range; jb + j is the key block
+    for (; j < nb && jb + j < jd && ok; ++j) ok = step(j, std::false_type{});
     for (; j < nb && ok; ++j) ok = step(j, std::true_type{});
     // ----------------------------------------------------------- epilogue
     if (ok && mbar_wait(o_full, 0, err, kErrTmemFullTimeout)) {
@@ -574,10 +587,35 @@ __global__ void __launch_bounds__(TcCfg<CS>::THREADS, 1)
         l_tot += other;
       }
       tc_fence_after();
+      if (nsplit > 1) {
+        // partial of this key range: O as accumulated (fp32, not divided by
+        // the row sum) and (running max, row sum); an empty range writes
+        // zeros and a max of -inf, which the combine weighs by 0
+        const size_t prow = ((size_t)tok * Hq + head) * nsplit + split;
+        float4* po = reinterpret_cast<float4*>(ws_o + prow * TC_D + h * (TC_D / CS));
+#pragma unroll 1
+        for (int c = 0; c < TC_D / CS; c += 32) {
+          uint32_t o[32];
+          if (nb > 0) {
+            tmem_ld_32x32b_x32(o_col + c, o);
+            tmem_ld_wait();
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = 0u;
+          }
+          if (valid) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              po[c / 4 + i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                          __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
+          }
+        }
+        if (valid && h == 0) reinterpret_cast<float2*>(ws_ml)[prow] = make_float2(m_run, l_tot);
+      }
       const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
       bf16* dst = out + ((size_t)tok * Hq + head) * TC_D + h * (TC_D / CS);
 #pragma unroll 1
-      for (int c = 0; c < TC_D / CS && ok; c += 32) {
+      for (int c = 0; c < TC_D / CS && ok && nsplit == 1; c += 32) {
         uint32_t o[32];
         tmem_ld_32x32b_x32(o_col + c, o);
         tmem_ld_wait();
@@ -648,7 +686,7 @@ static int make_pool_run_map(CUtensorMap* tm, const void* base, int L, int pages
 }
 
 typedef void (*Kern)(CUtensorMap, CUtensorMap, const bf16*, const int*, const int*, const int*, int, const int4*,
-                     bf16*, int, int, int, int, float, int*);
+                     bf16*, int, int, int, int, float, int*, int, float*, float*);
 // Builds of the kernel, LL_ATTN_VARIANT=<index> selects one:
 //   0  CS = 1, exp2 on MUFU        3  CS = 2, exp2 on MUFU
 //   1  CS = 1, bf16 pack on ALU    4  CS = 2, 2 of 8 exp2 on the FMA pipe
@@ -1045,12 +1083,22 @@ __global__ void __launch_bounds__(DT_THREADS)
 using namespace ll;
 
 // k_pool / v_pool: whole pools [L, pages, Hkv, ps, 128]; `layer` selects the layer.
+extern "C" int ll_attn_combine(bf16* out, const float* ws_o, const float* ws_ml, int rows, int nsplit,
+                               cudaStream_t stream);
+
+// tiles: one int4 per CTA (see the kernel).  nsplit > 1: every tile appears
+// as nsplit work items over equal key ranges, each writes a partial for row
+// (token * Hq + head) into ws_o [rows][nsplit][128] / ws_ml [rows][nsplit][2],
+// and the combine (rows = tokens * Hq) writes `out`.
 extern "C" int ll_attn_prefill_tc(const bf16* q, const bf16* k_pool, const bf16* v_pool, int L, int pages, int layer,
                                   const int* q_indptr, const int* q_pos, const int* page_table, int pt_stride,
                                   const int* tiles, int ntiles, bf16* out, int Hq, int Hkv, int head_dim,
-                                  int page_size, float scale, int* err, cudaStream_t stream) {
+                                  int page_size, float scale, int* err, int nsplit, float* ws_o, float* ws_ml,
+                                  int combine_rows, cudaStream_t stream) {
   if (ntiles <= 0) return 0;
-  if (head_dim != TC_D || Hq % Hkv) return -3;
+  if (head_dim != TC_D || Hq % Hkv || Hkv > 256) return -3;
+  if (nsplit < 1 || nsplit > 255 || (nsplit > 1 && (ws_o == nullptr || ws_ml == nullptr || combine_rows <= 0)))
+    return -3;
   if (page_size < 4 || page_size > TC_BN || TC_BN % page_size) return -3;  // one producer lane per page
   if (Hq / Hkv > TC_BM) return -3;
   CUtensorMap tk, tv;
@@ -1074,8 +1122,10 @@ extern "C" int ll_attn_prefill_tc(const bf16* q, const bf16* k_pool, const bf16*
   if (fits[v] != 1) return -7;
   kern<<<ntiles, bd.threads, bd.smem, stream>>>(tk, tv, q, q_indptr, q_pos, page_table, pt_stride,
                                                 reinterpret_cast<const int4*>(tiles), out, Hq, Hkv, page_size, layer,
-                                                scale * 1.4426950408889634f, err);
-  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+                                                scale * 1.4426950408889634f, err, nsplit, ws_o, ws_ml);
+  if (cudaGetLastError() != cudaSuccess) return -5;
+  if (nsplit > 1) return ll_attn_combine(out, ws_o, ws_ml, combine_rows, nsplit, stream);
+  return 0;
 }
 
 // Selects the build (kVariants index) for later launches; -2 goes back to

@@ -45,7 +45,7 @@ int ll_attn_decode(const bf16* q, const bf16* kpool, const bf16* vpool, int num_
 int ll_attn_prefill_tc(const bf16* q, const bf16* k_pool, const bf16* v_pool, int L, int pages, int layer,
                        const int* q_indptr, const int* q_pos, const int* page_table, int pt_stride, const int* tiles,
                        int ntiles, bf16* out, int Hq, int Hkv, int head_dim, int page_size, float scale, int* err,
-                       cudaStream_t stream);
+                       int nsplit, float* ws_o, float* ws_ml, int combine_rows, cudaStream_t stream);
 int ll_attn_prefill_tc_set_variant(int v);
 int ll_attn_prefill_tc_trace(unsigned long long* host, int n);
 }
@@ -434,18 +434,31 @@ void attn_prefill(const at::Tensor& q, const at::Tensor& k_pool_l, const at::Ten
 // k_pool / v_pool: whole pools [L, pages, Hkv, ps, D]; `layer` selects one.
 void attn_prefill_tc(const at::Tensor& q, const at::Tensor& k_pool, const at::Tensor& v_pool, int64_t layer,
                      const at::Tensor& q_indptr, const at::Tensor& q_pos, const at::Tensor& page_table,
-                     const at::Tensor& tiles, at::Tensor& out, double scale, const at::Tensor& err) {
+                     const at::Tensor& tiles, at::Tensor& out, double scale, const at::Tensor& err, int64_t nsplit,
+                     const c10::optional<at::Tensor>& ws_o, const c10::optional<at::Tensor>& ws_ml) {
   CHECK_CUDA(q); CHECK_BF16(q); CHECK_CONTIG(q); CHECK_BF16(k_pool); CHECK_BF16(v_pool); CHECK_CONTIG(k_pool);
   CHECK_CONTIG(v_pool); CHECK_I32(q_indptr); CHECK_I32(q_pos); CHECK_I32(page_table); CHECK_I32(tiles);
   CHECK_CONTIG(tiles); CHECK_ALIGN16(tiles); CHECK_CONTIG(out);
   TORCH_CHECK(k_pool.dim() == 5 && k_pool.sizes() == v_pool.sizes());
   TORCH_CHECK(layer >= 0 && layer < k_pool.size(0));
-  const int Hq = q.size(1), D = q.size(2);
+  const int T = q.size(0), Hq = q.size(1), D = q.size(2);
+  float* wo = nullptr;
+  float* wml = nullptr;
+  if (nsplit > 1) {
+    TORCH_CHECK(ws_o.has_value() && ws_ml.has_value(), "split attention needs its workspaces");
+    TORCH_CHECK(ws_o->scalar_type() == at::kFloat && ws_ml->scalar_type() == at::kFloat);
+    TORCH_CHECK(ws_o->is_contiguous() && ws_ml->is_contiguous());
+    TORCH_CHECK(ws_o->numel() >= (int64_t)T * Hq * nsplit * D && ws_ml->numel() >= (int64_t)T * Hq * nsplit * 2,
+                "split attention workspace too small");
+    wo = ws_o->data_ptr<float>();
+    wml = ws_ml->data_ptr<float>();
+  }
   c10::cuda::CUDAGuard g(q.device());
   check_rc(ll_attn_prefill_tc(bp(q), bp(k_pool), bp(v_pool), k_pool.size(0), k_pool.size(1), (int)layer,
                               q_indptr.data_ptr<int>(), q_pos.data_ptr<int>(), page_table.data_ptr<int>(),
                               page_table.stride(0), tiles.data_ptr<int>(), tiles.size(0), bp(out), Hq,
-                              k_pool.size(2), D, k_pool.size(3), (float)scale, err.data_ptr<int>(), cur_stream()),
+                              k_pool.size(2), D, k_pool.size(3), (float)scale, err.data_ptr<int>(), (int)nsplit, wo,
+                              wml, T * Hq, cur_stream()),
            "ll_attn_prefill_tc");
 }
 

@@ -44,6 +44,7 @@ class ForwardBatch:
     kv_lens: torch.Tensor  # [B] int32   keys visible to request b after this step's writes
     logit_rows: Optional[torch.Tensor] = None  # [R] int64 rows whose logits are returned
     tiles: Optional[torch.Tensor] = None  # prefill attention work list
+    tiles_nsplit: int = 1  # its key-range split count (ops.tiles_split_count)
     decode_nsplit: Optional[int] = None
     # grouped execution rows of one extend forward (row-wise repair compute):
     # {"batch_execution_unit_size": n, "repair_ranges": [{"start", "end"}], ...}
@@ -262,9 +263,9 @@ class QwenModel:
         qkv = self._buf("qkv", (T, qkv_n))
         mlp = self._buf("mlp", (T, self.inter))
         o = self._buf("o", (T, H))
-        tiles = fb.tiles
+        tiles, tiles_nsplit = fb.tiles, fb.tiles_nsplit
         if fb.mode == "extend" and tiles is None and fb.input_ids.is_cuda:
-            tiles = ops.prefill_tiles(fb.q_indptr.cpu(), fb.positions.cpu(), self.hq, self.hkv).to(self.device)
+            tiles, tiles_nsplit = self._attn_tiles(fb)
         rw_o = rw_ffn = ()
         if fb.mode == "extend" and fb.repair_meta is not None:
             from ..runtime.repair_diagnostics import rowwise_slices
@@ -295,7 +296,7 @@ class QwenModel:
                                          nsplit=fb.decode_nsplit, out=attn)
                 else:
                     ops.attention_prefill(q, kv.k, kv.v, li, fb.q_indptr, fb.positions, fb.page_table, fb.kv_lens,
-                                          self.scale, tiles=tiles, out=attn)
+                                          self.scale, tiles=tiles, out=attn, nsplit=tiles_nsplit)
                     if cmp_attn:  # diagnostic: native kernel vs the fp32 torch statement, sampled rows
                         from ..runtime.repair_diagnostics import compare_attention
                         from ..utils.trace import emit_trace
@@ -371,6 +372,12 @@ class QwenModel:
         return (self.embed.is_cuda and (self.tp_size == 1 or self.comm is None) and T <= ops.SMALL_M_MAX
                 and self.cfg.head_dim == 128 and self.cfg.rotary_dim == 128 and self.cfg.hidden_size % 32 == 0)
 
+    def _attn_tiles(self, fb: ForwardBatch):
+        """Prefill attention work list (with its key-range split count) for a
+        batch built without one."""
+        host = ops.prefill_tiles(fb.q_indptr.cpu(), fb.positions.cpu(), self.hq, self.hkv, split=True)
+        return host.to(self.device), ops.tiles_split_count(host)
+
     def _forward_decode_fused(self, fb: ForwardBatch, kv) -> torch.Tensor:
         """Decode step as five kernels per layer: the qkv GEMV writes Q and
         the new K/V (per-head norm and RoPE in its stores), attention, and
@@ -437,16 +444,16 @@ class QwenModel:
             attn[T:].zero_()
         qkv = self._buf("tp_qkv", (Tp, qkv_n))
         mlp = self._buf("tp_mlp", (Tp, self.inter))
-        tiles = fb.tiles
+        tiles, tiles_nsplit = fb.tiles, fb.tiles_nsplit
         if tiles is None:
-            tiles = ops.prefill_tiles(fb.q_indptr.cpu(), fb.positions.cpu(), self.hq, self.hkv).to(self.device)
+            tiles, tiles_nsplit = self._attn_tiles(fb)
         nl = len(self.layers)
         for li, lw in enumerate(self.layers):
             comm.gemm_from_gather(lw.qkv_w, lw.qkv_b, qkv, T)
             ops.rope_qkv_write(qkv[:T], fb.positions, fb.slots, self.cos_sin, q, kv.k[li], kv.v[li], self.hq,
                                self.hkv, D, lw.q_norm, lw.k_norm, c.rms_norm_eps)
             ops.attention_prefill(q, kv.k, kv.v, li, fb.q_indptr, fb.positions, fb.page_table, fb.kv_lens,
-                                  self.scale, tiles=tiles, out=attn[:T])
+                                  self.scale, tiles=tiles, out=attn[:T], nsplit=tiles_nsplit)
             comm.gemm_scatter(attn, lw.o_w, T)
             comm.reduce_norm_gather(res, lw.post_norm, c.rms_norm_eps, T)
             comm.gemm_from_gather(lw.gu_w, None, mlp, T, swiglu=True)

@@ -47,6 +47,8 @@ class _Workspace:
         self.tickets = torch.zeros(4096, dtype=torch.int32, device=device)
         self.dec_o = torch.empty(0, dtype=torch.float32, device=device)
         self.dec_ml = torch.empty(0, dtype=torch.float32, device=device)
+        self.pre_o = torch.empty(0, dtype=torch.float32, device=device)
+        self.pre_ml = torch.empty(0, dtype=torch.float32, device=device)
 
     def reserve_gemm(self, floats: int, tiles: int = 0) -> None:
         if self.gemm_ws.numel() < floats:
@@ -55,6 +57,15 @@ class _Workspace:
         if self.tickets.numel() < tiles:
             self._retired.append(self.tickets)
             self.tickets = torch.zeros(tiles, dtype=torch.int32, device=self.device)
+
+    def reserve_prefill_split(self, rows: int, nsplit: int, head_dim: int = 128) -> None:
+        """Partials of split prefill attention ([rows][nsplit][head_dim] fp32
+        + [rows][nsplit][2]); grown, never shrunk."""
+        need = rows * nsplit
+        if self.pre_o.numel() < need * head_dim:
+            self._retired += [self.pre_o, self.pre_ml]
+            self.pre_o = torch.empty(need * head_dim, dtype=torch.float32, device=self.device)
+            self.pre_ml = torch.empty(need * 2, dtype=torch.float32, device=self.device)
 
     def reserve_decode(self, rows: int, nsplit: int, head_dim: int = 128) -> None:
         need = rows * nsplit
@@ -315,44 +326,91 @@ def rope_qkv_write(qkv, positions, slots, cos_sin, q_out, k_pool_l, v_pool_l, nu
 
 
 PREFILL_ROWS_PER_TILE = 256  # packed (token, head) rows per CTA of the tcgen05 kernel (2 tiles of 128)
+PREFILL_BLOCK_KEYS = 128     # keys per block step of that kernel
+# Timing model of the tcgen05 prefill kernel on B200 (one CTA per SM): a
+# block step of a CTA (2 x 128 rows x 128 keys) takes ~2.2 us (a ~4.1-4.3K
+# cycle period at ~1.9 GHz); a CTA's start-up and epilogue ~1.5 block steps;
+# a split adds its partials' write + the combine's read (520 B per row and
+# split each way at ~6.5 TB/s) and one ~3 us combine launch.
+_PF_BLOCK_US, _PF_ITEM_BLOCKS, _PF_COMBINE_US = 2.2, 1.5, 3.0
+PREFILL_SPLIT_CHOICES = (1, 2, 3, 4, 6, 8)
+PREFILL_SPLIT_MAX_WS_BYTES = 256 << 20
+
+
+def prefill_split_count(blocks, packed_rows: int, num_sms: int = 148) -> int:
+    """Key-range split count for a prefill launch whose tiles have ``blocks``
+    key blocks each: the one with the smallest modelled time, kept only when
+    it is at least 5 % faster than no split.  Splitting pays when there are
+    too few tiles to fill the SMs (few KV heads per rank under tensor
+    parallelism, short repair sets over long contexts); the makespan of the
+    longest-first schedule is estimated as max(total / SMs + mean item / 2,
+    largest item) in block steps."""
+    import numpy as np
+
+    nb = np.asarray(blocks, dtype=np.float64)
+    if nb.size == 0:
+        return 1
+
+    def cost(S: int) -> float:
+        ch = np.ceil(nb / S)
+        items = np.clip(nb[:, None] - ch[:, None] * np.arange(S)[None, :], 0.0, ch[:, None]).ravel()
+        items = np.where(items > 0, items + _PF_ITEM_BLOCKS, 0.5)
+        span = max(items.sum() / num_sms + items.mean() / 2, items.max()) * _PF_BLOCK_US
+        if S > 1:
+            span += _PF_COMBINE_US + packed_rows * S * 1040 / 6.5e6
+        return span
+
+    base, best, best_c = cost(1), 1, None
+    for S in PREFILL_SPLIT_CHOICES[1:]:
+        if packed_rows * S * 520 > PREFILL_SPLIT_MAX_WS_BYTES:
+            break
+        c = cost(S)
+        if best_c is None or c < best_c:
+            best, best_c = S, c
+    return best if best_c is not None and best_c < 0.95 * base else 1
+
+
+def _split_items(t, S: int):
+    """Expands tiles [n, 4] (int64 numpy) into S key-range items each (kv
+    head | split << 8 | S << 16 in column 1), longest item first."""
+    import numpy as np
+
+    nb = t[:, 3] // PREFILL_BLOCK_KEYS + 1
+    ch = (nb + S - 1) // S
+    rep = np.repeat(t, S, axis=0)
+    sp = np.tile(np.arange(S, dtype=np.int64), len(t))
+    size = np.clip(np.repeat(nb, S) - np.repeat(ch, S) * sp, 0, np.repeat(ch, S))
+    rep[:, 1] = rep[:, 1] | (sp << 8) | (S << 16)
+    order = np.argsort(-size, kind="stable")
+    return rep[order]
+
+
+def tiles_split_count(tiles) -> int:
+    """Split count encoded in a work list built by :func:`prefill_tiles`
+    (host tensor or array)."""
+    if len(tiles) == 0:
+        return 1
+    return max(1, int(tiles[0][1]) >> 16)
 
 
 def prefill_tiles(q_indptr_host: torch.Tensor, q_pos_host: torch.Tensor, num_heads: int, num_kv_heads: int,
-                  rows_per_tile: int = PREFILL_ROWS_PER_TILE) -> torch.Tensor:
+                  rows_per_tile: int = PREFILL_ROWS_PER_TILE, split: bool = False) -> torch.Tensor:
     """Work list for the prefill/repair attention kernels: one int4
     ``(request, kv_head, first_packed_row, max_position_in_tile)`` per CTA,
     longest (largest max position) first.  Packed row ``r`` of a request is
-    (token ``r // g``, q-head ``kv_head*g + r % g``), ``g = Hq / Hkv``."""
-    g = num_heads // num_kv_heads
-    qi = q_indptr_host.to(torch.int64)
-    qp = q_pos_host.to(torch.int64)
-    B = qi.numel() - 1
-    out = []
-    for b in range(B):
-        s, e = int(qi[b]), int(qi[b + 1])
-        nrows = (e - s) * g
-        if nrows <= 0:
-            continue
-        r0 = torch.arange(0, nrows, rows_per_tile, dtype=torch.int64)
-        last_tok = s + (torch.clamp(r0 + rows_per_tile, max=nrows) - 1) // g
-        # positions are ascending within a request, so the tile max is its last token's
-        mp = qp[last_tok]
-        n = r0.numel()
-        t = torch.empty(n * num_kv_heads, 4, dtype=torch.int64)
-        t[:, 0] = b
-        t[:, 1] = torch.arange(num_kv_heads).repeat(n)
-        t[:, 2] = r0.repeat_interleave(num_kv_heads)
-        t[:, 3] = mp.repeat_interleave(num_kv_heads)
-        out.append(t)
-    if not out:
-        return torch.zeros(0, 4, dtype=torch.int32)
-    t = torch.cat(out)
-    order = torch.argsort(t[:, 3], descending=True, stable=True)
-    return t[order].to(torch.int32).contiguous()
+    (token ``r // g``, q-head ``kv_head*g + r % g``), ``g = Hq / Hkv``.
+    ``split`` (tcgen05 kernel only): each tile may become S items over equal
+    key ranges, S from :func:`prefill_split_count` when ``split`` is True, or
+    S = ``split`` when it is an int >= 2 (read it back with
+    :func:`tiles_split_count`)."""
+    import numpy as np
+
+    return torch.from_numpy(prefill_tiles_np(q_indptr_host.cpu().numpy(), q_pos_host.cpu().numpy(), num_heads,
+                                             num_kv_heads, rows_per_tile, split))
 
 
 def prefill_tiles_np(q_indptr, q_pos, num_heads: int, num_kv_heads: int,
-                     rows_per_tile: int = PREFILL_ROWS_PER_TILE):
+                     rows_per_tile: int = PREFILL_ROWS_PER_TILE, split: bool = False):
     """numpy form of :func:`prefill_tiles` (int32 [n, 4]) for the host-side
     batch build."""
     import numpy as np
@@ -379,14 +437,27 @@ def prefill_tiles_np(q_indptr, q_pos, num_heads: int, num_kv_heads: int,
         return np.zeros((0, 4), dtype=np.int32)
     t = np.concatenate(out)
     order = np.argsort(-t[:, 3], kind="stable")
-    return t[order].astype(np.int32)
+    t = t[order]
+    if split:
+        if split is True:
+            S = prefill_split_count(t[:, 3] // PREFILL_BLOCK_KEYS + 1, int(qi[-1] - qi[0]) * num_heads)
+        else:
+            S = int(split)
+            if not 1 <= S <= 255:
+                raise ValueError(f"split count {S} outside [1, 255]")
+        if S > 1:
+            t = _split_items(t, S)
+    return np.ascontiguousarray(t.astype(np.int32))
 
 
 def attention_prefill(q, k_pool, v_pool, layer, q_indptr, q_pos, page_table, kv_lens, scale, tiles=None,
-                      out=None) -> torch.Tensor:
+                      out=None, nsplit: int = 1) -> torch.Tensor:
     """q [T, Hq, D] -> [T, Hq*D]; rows attend to positions [0, q_pos] of their
     request (positions ascending within a request).  ``k_pool``/``v_pool`` are
-    the whole pools; ``layer`` selects one.  CUDA: tcgen05 kernel."""
+    the whole pools; ``layer`` selects one.  CUDA: tcgen05 kernel.  With
+    ``tiles`` given, ``nsplit`` is its split count (:func:`tiles_split_count`
+    of the host copy); without, the work list is built here with the split
+    model."""
     if not q.is_cuda:
         y = ref.paged_attention(q, k_pool[layer], v_pool[layer], q_indptr, q_pos, page_table, kv_lens, scale)
         if out is not None:
@@ -397,9 +468,17 @@ def attention_prefill(q, k_pool, v_pool, layer, q_indptr, q_pos, page_table, kv_
     if out is None:
         out = torch.empty(T, Hq * D, dtype=q.dtype, device=q.device)
     if tiles is None:
-        tiles = prefill_tiles(q_indptr.cpu(), q_pos.cpu(), Hq, k_pool.shape[2]).to(q.device)
-    _cuda().attn_prefill_tc(q, k_pool, v_pool, layer, q_indptr, q_pos, page_table, tiles, out, scale,
-                            workspace(q.device).err)
+        host = prefill_tiles(q_indptr.cpu(), q_pos.cpu(), Hq, k_pool.shape[2], split=True)
+        nsplit = tiles_split_count(host)
+        tiles = host.to(q.device)
+    ws = workspace(q.device)
+    if nsplit > 1:
+        ws.reserve_prefill_split(T * Hq, nsplit, D)
+        _cuda().attn_prefill_tc(q, k_pool, v_pool, layer, q_indptr, q_pos, page_table, tiles, out, scale, ws.err,
+                                nsplit, ws.pre_o, ws.pre_ml)
+    else:
+        _cuda().attn_prefill_tc(q, k_pool, v_pool, layer, q_indptr, q_pos, page_table, tiles, out, scale, ws.err,
+                                1, None, None)
     return out
 
 

@@ -341,8 +341,11 @@ class Engine:
         last_rows = (qptr[1:] - 1).astype(np.int64)
         pos32 = pos.astype(np.int32)
         parts32 = [ids, pos32, qptr, pt.reshape(-1), kvl]
+        tiles_nsplit = 1
         if self.is_cuda:
-            parts32.append(ops.prefill_tiles_np(qptr, pos32, self.model.hq, self.model.hkv).reshape(-1))
+            tl = ops.prefill_tiles_np(qptr, pos32, self.model.hq, self.model.hkv, split=True)
+            tiles_nsplit = ops.tiles_split_count(tl)
+            parts32.append(tl.reshape(-1))
         # every segment starts on a 256-byte boundary: kernels read some of
         # them (the prefill tile list) with 16-byte vector loads
         sizes32 = [a.size for a in parts32]
@@ -372,6 +375,7 @@ class Engine:
             kv_lens=view[4],
             logit_rows=d64[off64:],
             tiles=view[5].view(-1, 4) if self.is_cuda else None,
+            tiles_nsplit=tiles_nsplit,
         )
 
     def _kernel_check(self, what: str) -> None:

@@ -317,6 +317,66 @@ def test_attention_prefill_builds_match_fp32(variant):
     assert _rel(out.cpu(), exp) < 1.5e-2
 
 
+@pytest.mark.parametrize("variant", [7, 0, 3])
+@pytest.mark.parametrize("S", [2, 3, 5])
+def test_attention_prefill_key_range_splits_match_fp32(variant, S):
+    """Each tile as S work items over equal key ranges, partials merged by
+    the combine kernel: one KV head with 8 query heads per kv head (a tensor
+    parallel rank's share of Qwen3-32B), rows near the start (their tiles
+    have fewer key blocks than S: empty items) and rows deep in a 6K context
+    (ranges that mask every key of some rows), queries scaled up so running
+    maxima grow mid-range; against the fp32 statement."""
+    ext = ops._cuda()
+    D, Hq, Hkv, ps = 128, 8, 1, 16
+    lens = [6000, 700]
+    kp, vp, pt = _paged_setup(2, lens, Hkv, D, ps, seed=21)
+    g = torch.Generator().manual_seed(22)
+    rows0 = sorted(set(range(0, 48)) | set(range(2000, 2060)) | set(range(5900, 6000)))
+    rows1 = list(range(0, 30)) + list(range(650, 700))
+    qptr = [0, len(rows0), len(rows0) + len(rows1)]
+    rows = rows0 + rows1
+    q = torch.randn(len(rows), Hq, D, generator=g)
+    q[: len(rows0) // 2] *= 4.0
+    q = q.to(torch.bfloat16)
+    qpos = torch.tensor(rows, dtype=torch.int32)
+    qi = torch.tensor(qptr, dtype=torch.int32)
+    kvl = torch.tensor(lens, dtype=torch.int32)
+    scale = 1 / math.sqrt(D)
+    exp = ref.paged_attention(q.float(), kp.float(), vp.float(), qi, qpos, pt, kvl, scale)
+    host = ops.prefill_tiles(qi, qpos, Hq, Hkv, split=S)
+    assert ops.tiles_split_count(host) == S and len(host) % S == 0
+    try:
+        ext.attn_prefill_tc_set_variant(variant)
+        out = ops.attention_prefill(q.to(DEV), kp[None].to(DEV), vp[None].to(DEV), 0, qi.to(DEV), qpos.to(DEV),
+                                    pt.to(DEV), kvl.to(DEV), scale, tiles=host.to(DEV), nsplit=S)
+        torch.cuda.synchronize()
+    finally:
+        ext.attn_prefill_tc_set_variant(-2)
+    assert ops.check_errors(DEV) == 0
+    assert _rel(out.cpu(), exp) < 1.5e-2
+
+
+def test_attention_prefill_split_work_list_mismatch_is_refused():
+    """A work list whose encoded split count differs from the launch's is
+    recorded as an error and writes nothing (no partial goes to a missing
+    workspace)."""
+    D, Hq, Hkv, ps = 128, 8, 1, 16
+    lens = [600]
+    kp, vp, pt = _paged_setup(1, lens, Hkv, D, ps, seed=23)
+    rows = list(range(500, 600))
+    q = torch.randn(len(rows), Hq, D).to(torch.bfloat16).to(DEV)
+    qi = torch.tensor([0, len(rows)], dtype=torch.int32)
+    qpos = torch.tensor(rows, dtype=torch.int32)
+    host = ops.prefill_tiles(qi, qpos, Hq, Hkv, split=3)
+    out = torch.full((len(rows), Hq * D), 7.0, device=DEV).to(torch.bfloat16)
+    ops.attention_prefill(q, kp[None].to(DEV), vp[None].to(DEV), 0, qi.to(DEV), qpos.to(DEV), pt.to(DEV),
+                          torch.tensor(lens, dtype=torch.int32, device=DEV), 0.1, tiles=host.to(DEV), out=out,
+                          nsplit=1)
+    torch.cuda.synchronize()
+    assert ops.check_errors(DEV) != 0
+    assert bool((out.float() == 7.0).all())
+
+
 @pytest.mark.parametrize("B,Hq,Hkv,n,contiguous", [(1, 28, 4, 16000, False), (1, 28, 4, 16000, True),
                                                    (3, 28, 4, 1000, True), (16, 8, 1, 3000, False),
                                                    (2, 64, 8, 77, False)])
