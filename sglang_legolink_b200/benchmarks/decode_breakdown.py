@@ -71,6 +71,7 @@ def main():
     L, H, D = cfg.num_layers, cfg.hidden_size, cfg.head_dim
     hq, hkv, inter = m.hq, m.hkv, m.inter
     n, ps = a.context, 16
+    m.ensure_rope_positions(n + 1)  # contexts past the model's table, as the engine does
     pps = (n + ps - 1) // ps  # pages per request
     pages = B * pps
     kpool = torch.randn(L, pages, hkv, ps, D, device=dev, dtype=torch.bfloat16)
@@ -115,6 +116,9 @@ def main():
     total = 0.0
     for name, (fn, bytes_per_layer) in cases.items():
         ms = graph_time(fn)
+        err = ops.check_errors(dev)
+        if err:
+            raise SystemExit(f"{name}: device error {err} (the timing would be of abandoned work)")
         us = ms * 1e3 / L
         total += us
         roof_us = bytes_per_layer / (pk["hbm_gbs"] * 1e3)
