@@ -573,12 +573,66 @@ static bool decode_tma_enabled() {
   return v == 1;
 }
 
+// Few splits per row (the prefill key-range splits): one warp per row, lane
+// l owns columns [4l, 4l + 4); every split's (max, sum) and 16-byte slice of
+// O are loaded before any is used, so a warp has all its loads in flight at
+// once; 8 rows per CTA.
+constexpr int CW_ROWS = 8;
+template <int MAXS>
+__global__ void __launch_bounds__(32 * CW_ROWS) attn_combine_warp_kernel(bf16* __restrict__ out,
+                                                                         const float* __restrict__ ws_o,
+                                                                         const float* __restrict__ ws_ml, int rows,
+                                                                         int nsplit) {
+  pdl_trigger();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const size_t row = (size_t)blockIdx.x * CW_ROWS + (threadIdx.x >> 5);
+  if (row >= (size_t)rows) return;
+  const float2* ml = reinterpret_cast<const float2*>(ws_ml) + row * nsplit;
+  const float4* o = reinterpret_cast<const float4*>(ws_o + row * (size_t)nsplit * AT_D) + lane;
+  float2 m[MAXS];
+  float4 v[MAXS];
+#pragma unroll
+  for (int sp = 0; sp < MAXS; ++sp) {
+    if (sp < nsplit) {
+      m[sp] = __ldcg(ml + sp);
+      v[sp] = __ldcg(o + (size_t)sp * (AT_D / 4));
+    }
+  }
+  float M = -INFINITY;
+#pragma unroll
+  for (int sp = 0; sp < MAXS; ++sp)
+    if (sp < nsplit) M = fmaxf(M, m[sp].x);
+  float den = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int sp = 0; sp < MAXS; ++sp) {
+    if (sp < nsplit) {
+      const float wt = (m[sp].x == -INFINITY || M == -INFINITY) ? 0.f : exp2f(m[sp].x - M);
+      den += wt * m[sp].y;
+      acc.x += wt * v[sp].x;
+      acc.y += wt * v[sp].y;
+      acc.z += wt * v[sp].z;
+      acc.w += wt * v[sp].w;
+    }
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  *reinterpret_cast<uint2*>(out + row * AT_D + 4 * lane) =
+      make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
+}
+
 // Combine of split-KV partials: rows x nsplit partials [rows][nsplit][128]
 // (fp32) with (max log2, sum) each -> out [rows][128] (bf16).
 extern "C" int ll_attn_combine(bf16* out, const float* ws_o, const float* ws_ml, int rows, int nsplit,
                                cudaStream_t stream) {
   if (rows <= 0 || nsplit < 1 || nsplit > CB_MAX_SPLITS) return -3;
-  launch_pdl(attn_combine_kernel, dim3(rows), dim3(CB_THREADS), 0, stream, out, ws_o, ws_ml, nsplit);
+  const dim3 grid((rows + CW_ROWS - 1) / CW_ROWS), block(32 * CW_ROWS);
+  if (nsplit <= 8)
+    launch_pdl(attn_combine_warp_kernel<8>, grid, block, 0, stream, out, ws_o, ws_ml, rows, nsplit);
+  else if (nsplit <= 16)
+    launch_pdl(attn_combine_warp_kernel<16>, grid, block, 0, stream, out, ws_o, ws_ml, rows, nsplit);
+  else
+    launch_pdl(attn_combine_kernel, dim3(rows), dim3(CB_THREADS), 0, stream, out, ws_o, ws_ml, nsplit);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 

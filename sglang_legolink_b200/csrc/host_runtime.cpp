@@ -9,6 +9,7 @@
 //    clear :1449, legolink_stats :732-752, capacity eviction score :1937-1965.
 //  * radix prefix cache: radix_cache.py match_prefix/insert/evict :1457,:1517,:1657.
 #include <pybind11/pybind11.h>
+#include <pybind11/numpy.h>
 #include <pybind11/stl.h>
 
 #include <algorithm>
@@ -18,6 +19,7 @@
 #include <map>
 #include <memory>
 #include <optional>
+#include <queue>
 #include <stdexcept>
 #include <string>
 #include <unordered_map>
@@ -574,10 +576,32 @@ class RadixIndex {
   int64_t indexed_pages_ = 0;
 };
 
+// Makespan of list scheduling: items taken in the given order, each onto the
+// worker that becomes free first.  With one CTA per SM this is how the
+// GPU's block scheduler places the CTAs of one launch, so it models a
+// kernel's duration from its per-CTA work (the prefill attention's split
+// choice).
+double list_schedule_makespan(py::array_t<double, py::array::c_style | py::array::forcecast> items, int workers) {
+  if (workers <= 0) throw std::invalid_argument("workers must be positive");
+  auto it = items.unchecked<1>();
+  std::priority_queue<double, std::vector<double>, std::greater<double>> free_at;
+  for (int i = 0; i < workers; ++i) free_at.push(0.0);
+  double end = 0.0;
+  for (py::ssize_t i = 0; i < it.shape(0); ++i) {
+    const double w = it(i);
+    const double t = free_at.top() + w;
+    free_at.pop();
+    free_at.push(t);
+    end = std::max(end, t);
+  }
+  return end;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "LegoLink B200 runtime core: page allocator, block registry, radix prefix index";
+  m.def("list_schedule_makespan", &list_schedule_makespan, py::arg("items"), py::arg("workers"));
   py::class_<PageAllocator>(m, "PageAllocator")
       .def(py::init<int64_t>())
       .def_property_readonly("num_pages", &PageAllocator::num_pages)

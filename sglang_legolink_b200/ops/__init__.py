@@ -327,47 +327,54 @@ def rope_qkv_write(qkv, positions, slots, cos_sin, q_out, k_pool_l, v_pool_l, nu
 
 PREFILL_ROWS_PER_TILE = 256  # packed (token, head) rows per CTA of the tcgen05 kernel (2 tiles of 128)
 PREFILL_BLOCK_KEYS = 128     # keys per block step of that kernel
-# Timing model of the tcgen05 prefill kernel on B200 (one CTA per SM): a
-# block step of a CTA (2 x 128 rows x 128 keys) takes ~2.2 us (a ~4.1-4.3K
-# cycle period at ~1.9 GHz); a CTA's start-up and epilogue ~1.5 block steps;
-# a split adds its partials' write + the combine's read (520 B per row and
-# split each way at ~6.5 TB/s) and one ~3 us combine launch.
-_PF_BLOCK_US, _PF_ITEM_BLOCKS, _PF_COMBINE_US = 2.2, 1.5, 3.0
-PREFILL_SPLIT_CHOICES = (1, 2, 3, 4, 6, 8)
+# Timing model of the tcgen05 prefill kernel on B200 (one CTA per SM, CTAs
+# placed in list order onto the SM that frees first): a block step of a CTA
+# (2 x 128 rows x 128 keys) ~2.0 us; a CTA's start-up, pipeline fill/drain and
+# epilogue ~4 block steps; a split writes fp32 partials (520 B per row and
+# split) that the combine reads back, ~5.5 TB/s each way, plus one ~3 us
+# combine launch.
+_PF_BLOCK_US, _PF_ITEM_BLOCKS, _PF_COMBINE_US, _PF_BYTES_PER_US = 2.0, 4.0, 3.0, 5.5e6
+PREFILL_SPLIT_CHOICES = (1, 2, 3, 4, 6, 8, 12, 16)
 PREFILL_SPLIT_MAX_WS_BYTES = 256 << 20
+
+
+def prefill_split_time_us(blocks, packed_rows: int, S: int, num_sms: int = 148) -> float:
+    """Modelled duration (us) of one prefill attention launch whose tiles
+    have ``blocks`` key blocks each, every tile split into S equal key
+    ranges (S = 1: no split), including the partials' traffic and the
+    combine."""
+    import numpy as np
+
+    from . import _ext
+
+    nb = np.asarray(blocks, dtype=np.int64)
+    ch = -(-nb // S)
+    sizes = np.clip(nb[:, None] - ch[:, None] * np.arange(S)[None, :], 0, ch[:, None]).ravel()
+    sizes = np.sort(sizes)[::-1]
+    work = np.where(sizes > 0, sizes + _PF_ITEM_BLOCKS, 0.5)
+    t = _ext.host().list_schedule_makespan(work, num_sms) * _PF_BLOCK_US
+    if S > 1:
+        t += _PF_COMBINE_US + packed_rows * (S * 520 * 2 + 256) / _PF_BYTES_PER_US
+    return t
 
 
 def prefill_split_count(blocks, packed_rows: int, num_sms: int = 148) -> int:
     """Key-range split count for a prefill launch whose tiles have ``blocks``
-    key blocks each: the one with the smallest modelled time, kept only when
-    it is at least 5 % faster than no split.  Splitting pays when there are
-    too few tiles to fill the SMs (few KV heads per rank under tensor
-    parallelism, short repair sets over long contexts); the makespan of the
-    longest-first schedule is estimated as max(total / SMs + mean item / 2,
-    largest item) in block steps."""
-    import numpy as np
-
-    nb = np.asarray(blocks, dtype=np.float64)
-    if nb.size == 0:
+    key blocks each: the one with the smallest modelled time
+    (:func:`prefill_split_time_us`), kept only when it is at least 10 %
+    faster than no split.  Splitting pays when there are too few tiles to
+    fill the SMs (few KV heads per rank under tensor parallelism, short
+    repair sets over long contexts)."""
+    if len(blocks) == 0 or len(blocks) >= 3 * num_sms:  # three or more waves of tiles: no split
         return 1
-
-    def cost(S: int) -> float:
-        ch = np.ceil(nb / S)
-        items = np.clip(nb[:, None] - ch[:, None] * np.arange(S)[None, :], 0.0, ch[:, None]).ravel()
-        items = np.where(items > 0, items + _PF_ITEM_BLOCKS, 0.5)
-        span = max(items.sum() / num_sms + items.mean() / 2, items.max()) * _PF_BLOCK_US
-        if S > 1:
-            span += _PF_COMBINE_US + packed_rows * S * 1040 / 6.5e6
-        return span
-
-    base, best, best_c = cost(1), 1, None
+    base, best, best_t = prefill_split_time_us(blocks, packed_rows, 1, num_sms), 1, None
     for S in PREFILL_SPLIT_CHOICES[1:]:
         if packed_rows * S * 520 > PREFILL_SPLIT_MAX_WS_BYTES:
             break
-        c = cost(S)
-        if best_c is None or c < best_c:
-            best, best_c = S, c
-    return best if best_c is not None and best_c < 0.95 * base else 1
+        t = prefill_split_time_us(blocks, packed_rows, S, num_sms)
+        if best_t is None or t < best_t:
+            best, best_t = S, t
+    return best if best_t is not None and best_t < 0.9 * base else 1
 
 
 def _split_items(t, S: int):

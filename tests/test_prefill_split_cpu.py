@@ -64,3 +64,17 @@ def test_the_workspace_cap_limits_the_split():
     assert ops.prefill_split_count(nb, 1000) > 1
     rows_over_cap = ops.PREFILL_SPLIT_MAX_WS_BYTES // (2 * 520) + 1  # even S = 2 would exceed the cap
     assert ops.prefill_split_count(nb, rows_over_cap) == 1
+
+
+def test_list_schedule_makespan_places_each_item_on_the_first_free_worker():
+    from sglang_legolink_b200.ops import _ext
+
+    h = _ext.host()
+    assert h.list_schedule_makespan(np.array([3.0, 3.0, 2.0, 2.0, 2.0]), 2) == 7.0
+    assert h.list_schedule_makespan(np.array([5.0]), 148) == 5.0
+    assert h.list_schedule_makespan(np.zeros(0), 4) == 0.0
+    with pytest.raises(ValueError):
+        h.list_schedule_makespan(np.array([1.0]), 0)
+    # the model of a launch: splitting 100 long tiles over 148 SMs pays, 600 tiles do not split
+    assert ops.prefill_split_count(np.full(100, 250), 100 * 256) > 1
+    assert ops.prefill_split_count(np.full(600, 250), 600 * 256) == 1
