@@ -328,12 +328,13 @@ def rope_qkv_write(qkv, positions, slots, cos_sin, q_out, k_pool_l, v_pool_l, nu
 PREFILL_ROWS_PER_TILE = 256  # packed (token, head) rows per CTA of the tcgen05 kernel (2 tiles of 128)
 PREFILL_BLOCK_KEYS = 128     # keys per block step of that kernel
 # Timing model of the tcgen05 prefill kernel on B200 (one CTA per SM, CTAs
-# placed in list order onto the SM that frees first): a block step of a CTA
-# (2 x 128 rows x 128 keys) ~2.0 us; a CTA's start-up, pipeline fill/drain and
-# epilogue ~4 block steps; a split writes fp32 partials (520 B per row and
-# split) that the combine reads back, ~5.5 TB/s each way, plus one ~3 us
-# combine launch.
-_PF_BLOCK_US, _PF_ITEM_BLOCKS, _PF_COMBINE_US, _PF_BYTES_PER_US = 2.0, 4.0, 3.0, 5.5e6
+# placed in list order onto the SM that frees first), fitted to the split
+# sweep of benchmarks/attn_split.py (TP = 1/2/4/8 shares of the Qwen3-32B
+# Link, S = 1..16): a block step of a CTA (2 x 128 rows x 128 keys) ~2.1 us,
+# a CTA's start-up and epilogue ~1 block step, and a split's partials (the
+# fp32 write, the combine's read: 520 B per row and split each way) at an
+# effective ~2 TB/s plus one ~3 us combine launch.
+_PF_BLOCK_US, _PF_ITEM_BLOCKS, _PF_COMBINE_US, _PF_BYTES_PER_US = 2.1, 1.0, 3.0, 2.0e6
 PREFILL_SPLIT_CHOICES = (1, 2, 3, 4, 6, 8, 12, 16)
 PREFILL_SPLIT_MAX_WS_BYTES = 256 << 20
 
@@ -361,8 +362,9 @@ def prefill_split_time_us(blocks, packed_rows: int, S: int, num_sms: int = 148) 
 def prefill_split_count(blocks, packed_rows: int, num_sms: int = 148) -> int:
     """Key-range split count for a prefill launch whose tiles have ``blocks``
     key blocks each: the one with the smallest modelled time
-    (:func:`prefill_split_time_us`), kept only when it is at least 10 %
-    faster than no split.  Splitting pays when there are too few tiles to
+    (:func:`prefill_split_time_us`), kept only when it is at least 15 %
+    faster than no split (the model's error on the sweep it was fitted to is
+    up to ~8 %).  Splitting pays when there are too few tiles to
     fill the SMs (few KV heads per rank under tensor parallelism, short
     repair sets over long contexts)."""
     if len(blocks) == 0 or len(blocks) >= 3 * num_sms:  # three or more waves of tiles: no split
@@ -374,7 +376,7 @@ def prefill_split_count(blocks, packed_rows: int, num_sms: int = 148) -> int:
         t = prefill_split_time_us(blocks, packed_rows, S, num_sms)
         if best_t is None or t < best_t:
             best, best_t = S, t
-    return best if best_t is not None and best_t < 0.9 * base else 1
+    return best if best_t is not None and best_t < 0.85 * base else 1
 
 
 def _split_items(t, S: int):

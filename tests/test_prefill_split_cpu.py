@@ -75,6 +75,6 @@ def test_list_schedule_makespan_places_each_item_on_the_first_free_worker():
     assert h.list_schedule_makespan(np.zeros(0), 4) == 0.0
     with pytest.raises(ValueError):
         h.list_schedule_makespan(np.array([1.0]), 0)
-    # the model of a launch: splitting 100 long tiles over 148 SMs pays, 600 tiles do not split
-    assert ops.prefill_split_count(np.full(100, 250), 100 * 256) > 1
+    # the model of a launch: 74 long tiles leave half of 148 SMs idle and are split; 600 tiles are not
+    assert ops.prefill_split_count(np.full(74, 250), 74 * 256) > 1
     assert ops.prefill_split_count(np.full(600, 250), 600 * 256) == 1
