@@ -113,6 +113,9 @@ def main():
         "gemv_down_residual": (lambda: [ops.gemv_residual(mlp, lw.down_w, res, lw.in_norm, x, sq, eps=eps)
                                         for lw in m.layers], m.layers[0].down_w.numel() * 2),
     }
+    ws = ops.workspace(dev)
+    gemv_nk = {"gemv_qkv_rope": ((hq + 2 * hkv) * D, H), "gemv_o_proj_residual": (H, hq * D),
+               "gemv_gate_up_swiglu": (2 * inter, H), "gemv_down_residual": (H, inter)}
     total = 0.0
     for name, (fn, bytes_per_layer) in cases.items():
         ms = graph_time(fn)
@@ -122,7 +125,8 @@ def main():
         us = ms * 1e3 / L
         total += us
         roof_us = bytes_per_layer / (pk["hbm_gbs"] * 1e3)
-        print(json.dumps({"op": name, "model": cfg.name, "batch": B, "context": n, "nsplit": nsplit,
+        extra = {"gemv_splits": ops._small_m_splits(ws, B, *gemv_nk[name])} if name in gemv_nk else {"nsplit": nsplit}
+        print(json.dumps({"op": name, "model": cfg.name, "batch": B, "context": n, **extra,
                           "us_per_layer": round(us, 2), "us_per_step": round(us * L, 1),
                           "roofline_us_per_layer": round(roof_us, 2), "frac_of_hbm": round(roof_us / us, 3),
                           "peaks": pk["src"]}), flush=True)

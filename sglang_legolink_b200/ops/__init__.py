@@ -15,6 +15,7 @@ Conventions
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -165,8 +166,16 @@ def _small_m(ext, ws, x, w, bias, out, swiglu: bool = False):
 EPI_STORE, EPI_SWIGLU, EPI_RESIDUAL, EPI_QKV_ROPE = 0, 1, 2, 3
 
 
+# LL_SMALL_M_MAX_SPLITS=<n> caps the split-K count of the small-M GEMM
+# (a measurement knob for benchmarks/decode_breakdown.py; unset: no cap
+# beyond the kernel's own).
+_SMALL_M_MAX_SPLITS = int(os.environ.get("LL_SMALL_M_MAX_SPLITS", "0") or 0)
+
+
 def _small_m_splits(ws, M: int, N: int, K: int) -> int:
     splits = _cuda().gemm_small_m_splits(N, K)
+    if _SMALL_M_MAX_SPLITS > 0 and splits > _SMALL_M_MAX_SPLITS:
+        splits = _SMALL_M_MAX_SPLITS
     if splits > 1:
         need = splits * M * N
         if ws.gemm_ws.numel() < need or ws.tickets.numel() < (N + 127) // 128:
