@@ -412,7 +412,7 @@ def tiles_split_count(tiles) -> int:
 
 
 def prefill_tiles(q_indptr_host: torch.Tensor, q_pos_host: torch.Tensor, num_heads: int, num_kv_heads: int,
-                  rows_per_tile: int = PREFILL_ROWS_PER_TILE, split: bool = False) -> torch.Tensor:
+                  rows_per_tile: int = PREFILL_ROWS_PER_TILE, split: bool | int = False) -> torch.Tensor:
     """Work list for the prefill/repair attention kernels: one int4
     ``(request, kv_head, first_packed_row, max_position_in_tile)`` per CTA,
     longest (largest max position) first.  Packed row ``r`` of a request is
@@ -428,7 +428,7 @@ def prefill_tiles(q_indptr_host: torch.Tensor, q_pos_host: torch.Tensor, num_hea
 
 
 def prefill_tiles_np(q_indptr, q_pos, num_heads: int, num_kv_heads: int,
-                     rows_per_tile: int = PREFILL_ROWS_PER_TILE, split: bool = False):
+                     rows_per_tile: int = PREFILL_ROWS_PER_TILE, split: bool | int = False):
     """numpy form of :func:`prefill_tiles` (int32 [n, 4]) for the host-side
     batch build."""
     import numpy as np
