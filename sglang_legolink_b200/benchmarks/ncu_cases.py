@@ -1,7 +1,7 @@
 """Small single-kernel cases sized for `ncu --set full` captures (a few
 launches, a few hundred MB on the device), one per hot kernel:
 
-    python -m sglang_legolink_b200.benchmarks.ncu_cases {gemm,gemm_link,gemm_link_cublas,attn,gemv,gemv_residual,decode,link,rmsnorm,rope_qkv,tp_reduce,tp_scatter,tp_decode}
+    python -m sglang_legolink_b200.benchmarks.ncu_cases {gemm,gemm_link,gemm_link_cublas,attn,gemv,gemv_residual,gemv_qkv_rope,decode,link,rmsnorm,rope_qkv,tp_reduce,tp_scatter,tp_decode}
 """
 import sys, os, math
 
@@ -26,6 +26,21 @@ elif case == "gemv_residual":  # o_proj GEMV + residual epilogue: 4 launches at 
         h = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
         sq = ops.sumsq_buffer(M, "cuda")
         for _ in range(4): ops.gemv_residual(x, w, res, nw, h, sq)
+    torch.cuda.synchronize()
+elif case == "gemv_qkv_rope":  # one Qwen3-32B TP=8 rank's qkv GEMV + QK-norm + RoPE + KV write: 4 launches at M = 16, then 4 at M = 1
+    H, hq, hkv, ctx, ps = 5120, 8, 1, 32832, 16
+    w = ops.tile_weight((torch.randn((hq + 2 * hkv) * 128, H, device="cuda") * 0.02).to(torch.bfloat16))
+    qn = (torch.rand(128, device="cuda") + 0.5).to(torch.bfloat16)
+    kn = (torch.rand(128, device="cuda") + 0.5).to(torch.bfloat16)
+    cs = ref.rope_cos_sin_table(ctx + 64, 128, 1e6).to("cuda")
+    for M in (16, 1):
+        x = torch.randn(M, H, device="cuda", dtype=torch.bfloat16)
+        pos = torch.full((M,), ctx - 1, device="cuda", dtype=torch.int32)
+        slot = torch.arange(M, device="cuda", dtype=torch.int64) * ps
+        kp = torch.zeros(M, hkv, ps, 128, device="cuda", dtype=torch.bfloat16)
+        vp = torch.zeros_like(kp)
+        q = torch.empty(M, hq, 128, device="cuda", dtype=torch.bfloat16)
+        for _ in range(4): ops.gemv_qkv_rope(x, w, None, pos, slot, cs, q, kp, vp, hq, hkv, qn, kn, 1e-6)
     torch.cuda.synchronize()
 elif case == "gemm":
     M, N, K = 2048, 37888, 3584
