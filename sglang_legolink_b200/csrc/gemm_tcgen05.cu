@@ -309,13 +309,18 @@ struct SwapCfg {
 // kRowPrefetch (M > 1): the epilogue loads the per-row operands and split-K
 // partials of kRowChunk rows before emitting any of them.  M == 1 launches
 // the plain epilogue, a separate instantiation, so the batch-1 decode kernel
-// keeps its smaller code and register count.
-template <int BNX, int RING_KB, bool kRowPrefetch>
+// keeps its smaller code and register count.  MODE >= 0 compiles a single
+// epilogue mode (the decode instantiations, M <= 16): the kernel then holds
+// only that mode's code, so a launch fetches less cold code (instruction
+// fetch stalls led the 16-row epilogue's stall profile); MODE = -1 takes the
+// mode from `epi` at run time.
+template <int BNX, int RING_KB, bool kRowPrefetch, int MODE = -1>
 __global__ void __launch_bounds__(192, 2)
     gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                        bf16* __restrict__ C, const bf16* __restrict__ bias, int M, int N, int K, int ldc,
                        int kb_per_split, float* __restrict__ ws, int* __restrict__ tickets, int* err,
                        int w_tiled, const __grid_constant__ LLSmallMEpi epi) {
+  const int mode = MODE >= 0 ? MODE : epi.mode;
   using Cfg = SwapCfg<BNX, RING_KB>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -434,10 +439,10 @@ __global__ void __launch_bounds__(192, 2)
     float pf_res0 = 0.f, pf_w = 0.f, pf_c0 = 0.f, pf_s0 = 0.f;
     int pf_pos = 0;
     int64_t pf_slot = 0;
-    if (epi.mode == LL_EPI_RESIDUAL && feat < N) {
+    if (mode == LL_EPI_RESIDUAL && feat < N) {
       pf_res0 = __bfloat162float(epi.res[feat]);
       pf_w = __bfloat162float(epi.norm_w[feat]);
-    } else if (epi.mode == LL_EPI_QKV_ROPE) {
+    } else if (mode == LL_EPI_QKV_ROPE) {
       if (lane < M) {
         pf_pos = epi.positions[lane];
         pf_slot = epi.slots[lane];
@@ -472,9 +477,9 @@ __global__ void __launch_bounds__(192, 2)
         const float rs = __shfl_sync(0xffffffffu, pf_rstd, m & 31);
         p.rs = m < 32 ? rs : (m < M ? rsqrtf(sumsq_value(__ldcg(epi.scale_sumsq + m)) / (float)K + epi.scale_eps) : 1.f);
       }
-      if (epi.mode == LL_EPI_RESIDUAL) {
+      if (mode == LL_EPI_RESIDUAL) {
         if (m < M && feat < N) p.res = m == 0 ? pf_res0 : __bfloat162float(epi.res[(size_t)m * epi.ld + feat]);
-      } else if (epi.mode == LL_EPI_QKV_ROPE) {
+      } else if (mode == LL_EPI_QKV_ROPE) {
         const int pm0 = __shfl_sync(0xffffffffu, pf_pos, m & 31);
         const int64_t sl = __shfl_sync(0xffffffffu, pf_slot, m & 31);
         p.pos = m < 32 ? pm0 : (m < M ? epi.positions[m] : 0);
@@ -493,14 +498,14 @@ __global__ void __launch_bounds__(192, 2)
     auto emit = [&](int m, float v, const RowPf& p) {
       if (epi.scale_sumsq != nullptr) v *= p.rs;
       v += pf_bias;
-      if (epi.mode == LL_EPI_STORE) {
+      if (mode == LL_EPI_STORE) {
         if (feat < N) C[(size_t)m * ldc + feat] = __float2bfloat16(v);
-      } else if (epi.mode == LL_EPI_SWIGLU) {
+      } else if (mode == LL_EPI_SWIGLU) {
         // gate/up interleaved in groups of 16: lanes 0-15 hold gate
         // features, lanes 16-31 the matching up features
         const float u = __shfl_down_sync(0xffffffffu, v, 16);
         if (lane < 16 && feat < N) C[(size_t)m * ldc + (feat >> 5) * 16 + lane] = __float2bfloat16(silu_f(v) * u);
-      } else if (epi.mode == LL_EPI_RESIDUAL) {
+      } else if (mode == LL_EPI_RESIDUAL) {
         float r = 0.f;
         if (feat < N) {
           const size_t i = (size_t)m * epi.ld + feat;
@@ -1344,6 +1349,17 @@ static int small_m_ring_kb() {
   return v;
 }
 
+// LL_GEMV_MODE_KERNELS=0 launches the runtime-mode decode kernels instead of
+// the per-mode ones (an A/B switch; default on).
+static bool small_m_mode_kernels() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("LL_GEMV_MODE_KERNELS");
+    v = (e != nullptr && atoi(e) == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
 static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc, const bf16* bias, int M,
                           int N, int K, int splits, float* ws, size_t ws_floats, int* tickets, int* err, int w_tiled,
                           const LLSmallMEpi& epi, cudaStream_t stream) {
@@ -1383,9 +1399,9 @@ static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* 
   if (w_tiled ? make_tmap_w_tiled(&tW, W, N, K) : make_tmap_2d(&tW, W, N, K, ldw, GEMM_BM)) return -2;
   if (make_tmap_2d(&tX, A, M, K, lda, BNX)) return -2;
   dim3 grid(ntiles, splits);
-#define LL_LAUNCH_S(BNX_, RING_, PF_)                                                                    \
+#define LL_LAUNCH_SM(BNX_, RING_, PF_, MODE_)                                                            \
   do {                                                                                                   \
-    auto kern = gemm_swapab_kernel<BNX_, RING_, PF_>;                                                    \
+    auto kern = gemm_swapab_kernel<BNX_, RING_, PF_, MODE_>;                                             \
     using C_ = SwapCfg<BNX_, RING_>;                                                                     \
     if (C_::SMEM > max_smem_optin()) return -7;                                                          \
     static bool init = false;                                                                            \
@@ -1395,6 +1411,17 @@ static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* 
     }                                                                                                    \
     launch_pdl(kern, grid, dim3(192), C_::SMEM, stream, tW, tX, C, bias, M, N, K, ldc, kb_per, ws, tickets, \
                err, w_tiled, epi);                                                                       \
+  } while (0)
+#define LL_LAUNCH_S(BNX_, RING_, PF_) LL_LAUNCH_SM(BNX_, RING_, PF_, -1)
+// the decode sizes (M <= 16) on the default ring: one instantiation per epilogue mode
+#define LL_LAUNCH_S16(PF_)                                     \
+  do {                                                         \
+    switch (epi.mode) {                                        \
+      case LL_EPI_STORE: LL_LAUNCH_SM(16, 108, PF_, LL_EPI_STORE); break;       \
+      case LL_EPI_SWIGLU: LL_LAUNCH_SM(16, 108, PF_, LL_EPI_SWIGLU); break;     \
+      case LL_EPI_RESIDUAL: LL_LAUNCH_SM(16, 108, PF_, LL_EPI_RESIDUAL); break; \
+      default: LL_LAUNCH_SM(16, 108, PF_, LL_EPI_QKV_ROPE); break;              \
+    }                                                          \
   } while (0)
   if (small_m_ring_kb() == 72) {
     switch (BNX) {
@@ -1409,15 +1436,23 @@ static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* 
   } else {
     switch (BNX) {
       case 16:
-        if (M == 1) LL_LAUNCH_S(16, 108, false);
-        else LL_LAUNCH_S(16, 108, true);
+        if (small_m_mode_kernels()) {
+          if (M == 1) LL_LAUNCH_S16(false);
+          else LL_LAUNCH_S16(true);
+        } else if (M == 1) {
+          LL_LAUNCH_S(16, 108, false);
+        } else {
+          LL_LAUNCH_S(16, 108, true);
+        }
         break;
       case 32: LL_LAUNCH_S(32, 108, true); break;
       case 64: LL_LAUNCH_S(64, 108, true); break;
       default: LL_LAUNCH_S(128, 108, true); break;
     }
   }
+#undef LL_LAUNCH_S16
 #undef LL_LAUNCH_S
+#undef LL_LAUNCH_SM
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
