@@ -289,6 +289,178 @@ __device__ __forceinline__ float sumsq_value(unsigned long long x) {
   return __ull2float_rn(x) * (1.f / LL_SUMSQ_ONE);
 }
 
+// Four consecutive bf16 <-> float (8-byte accesses; the caller guarantees
+// the alignment).
+__device__ __forceinline__ void ld_bf16x4(const bf16* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
+  const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+  v[0] = __low2float(a);
+  v[1] = __high2float(a);
+  v[2] = __low2float(b);
+  v[3] = __high2float(b);
+}
+__device__ __forceinline__ void st_bf16x4(bf16* p, float v0, float v1, float v2, float v3) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(v0, v1), b = __floats2bfloat162_rn(v2, v3);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t*>(&a);
+  u.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+// Sum over a 32-feature group held as 4 consecutive features by each of 8
+// lanes (lanes 8g..8g+7 hold features 32g..32g+31).  The additions pair the
+// same features in the same order as warp_sum() over one feature per lane
+// (feature distance 16, 8, 4 across lanes, then 2 and 1 inside the thread),
+// so the result has the same bits as the one-feature-per-lane epilogue.
+__device__ __forceinline__ float group32_sum(float y0, float y1, float y2, float y3) {
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) {
+    y0 += __shfl_xor_sync(0xffffffffu, y0, o);
+    y1 += __shfl_xor_sync(0xffffffffu, y1, o);
+    y2 += __shfl_xor_sync(0xffffffffu, y2, o);
+    y3 += __shfl_xor_sync(0xffffffffu, y3, o);
+  }
+  return (y0 + y2) + (y1 + y3);
+}
+
+// Tile epilogue of the small-M kernel for 2 <= M <= 16 rows.  The four
+// epilogue warps hold the 16 x 128 output tile as warp q = rows 4q..4q+3,
+// lane = features 4*lane..4*lane+3, so every row of the tile lives in ONE
+// warp: a row's sums over the tile (QK-norm, the residual epilogue's sum of
+// squares) and the RoPE rotate-half partner (feature f +- 64 = lane ^ 16) are
+// warp shuffles, and the four warps emit their rows at the same time with no
+// block barrier.  The split-K fix-up loads each thread's 4 rows x 4 features
+// of up to four splits at once (16-byte loads).  The per-element arithmetic
+// and the order of every sum are those of the one-row-at-a-time epilogue, so
+// both give the same bits.
+template <int MODE>
+struct TileEpi {
+  int q, lane, f0, feat0, m0;
+  bool fvalid;
+  float tb[4], tw[4];        // bias, norm weight (residual: norm_w; qkv: q/k norm)
+  float rs[4];               // per-row scale
+  float tres[4][4];          // residual rows
+  float tc[4][4], ts[4][4];  // RoPE cos / sin of the four rows
+  int tpos[4];
+  int64_t tslot[4];
+
+  // Operands that do not depend on the product (call after pdl_wait).
+  __device__ __forceinline__ void prefetch(const bf16* __restrict__ bias, int M, int N, int K, int nb,
+                                           const LLSmallMEpi& epi) {
+    fvalid = feat0 < N;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) tb[c] = tw[c] = 0.f;
+    if (bias != nullptr && fvalid) ld_bf16x4(bias + feat0, tb);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int m = m0 + j;
+      rs[j] = (epi.scale_sumsq != nullptr && m < M)
+                  ? rsqrtf(sumsq_value(__ldcg(epi.scale_sumsq + m)) / (float)K + epi.scale_eps)
+                  : 1.f;
+    }
+    if constexpr (MODE == LL_EPI_RESIDUAL) {
+      if (fvalid) ld_bf16x4(epi.norm_w + feat0, tw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tres[j][c] = 0.f;
+        if (m0 + j < M && fvalid) ld_bf16x4(epi.res + (size_t)(m0 + j) * epi.ld + feat0, tres[j]);
+      }
+    }
+    if constexpr (MODE == LL_EPI_QKV_ROPE) {
+      const bf16* nw = nb < epi.Hq ? epi.q_norm_w : (nb < epi.Hq + epi.Hkv ? epi.k_norm_w : nullptr);
+      if (nw != nullptr) ld_bf16x4(nw + f0, tw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int m = m0 + j;
+        tpos[j] = m < M ? epi.positions[m] : 0;
+        tslot[j] = m < M ? epi.slots[m] : 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tc[j][c] = ts[j][c] = 0.f;
+        if (m < M && nb < epi.Hq + epi.Hkv && tpos[j] >= 0 && tpos[j] < epi.max_pos) {
+          const float4 cv = *reinterpret_cast<const float4*>(epi.cos_sin + (size_t)tpos[j] * 128 + (f0 & 63));
+          const float4 sv = *reinterpret_cast<const float4*>(epi.cos_sin + (size_t)tpos[j] * 128 + 64 + (f0 & 63));
+          tc[j][0] = cv.x, tc[j][1] = cv.y, tc[j][2] = cv.z, tc[j][3] = cv.w;
+          ts[j][0] = sv.x, ts[j][1] = sv.y, ts[j][2] = sv.z, ts[j][3] = sv.w;
+        }
+      }
+    }
+  }
+
+  // Emits row j (m = m0 + j < M) from its four accumulator values.  Called
+  // by the whole warp (shuffles); lanes past N store nothing.
+  __device__ __forceinline__ void emit(int j, const float (&a)[4], bf16* __restrict__ C, int ldc, int M, int nb,
+                                       const LLSmallMEpi& epi, int* err) {
+    const int m = m0 + j;
+    float v[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      v[c] = a[c];
+      if (epi.scale_sumsq != nullptr) v[c] *= rs[j];
+      v[c] += tb[c];
+    }
+    if constexpr (MODE == LL_EPI_STORE) {
+      if (fvalid) st_bf16x4(C + (size_t)m * ldc + feat0, v[0], v[1], v[2], v[3]);
+    } else if constexpr (MODE == LL_EPI_SWIGLU) {
+      // gate features on lanes 8g..8g+3, the matching up features on lane ^ 4
+      float u[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) u[c] = __shfl_xor_sync(0xffffffffu, v[c], 4);
+      if ((lane & 4) == 0 && fvalid)
+        st_bf16x4(C + (size_t)m * ldc + (feat0 >> 5) * 16 + (feat0 & 15), silu_f(v[0]) * u[0], silu_f(v[1]) * u[1],
+                  silu_f(v[2]) * u[2], silu_f(v[3]) * u[3]);
+    } else if constexpr (MODE == LL_EPI_RESIDUAL) {
+      float r[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) r[c] = fvalid ? bf16_round(v[c]) + tres[j][c] : 0.f;
+      if (fvalid) {
+        const size_t i = (size_t)m * epi.ld + feat0;
+        st_bf16x4(epi.res + i, r[0], r[1], r[2], r[3]);
+        st_bf16x4(epi.h_out + i, r[0] * tw[0], r[1] * tw[1], r[2] * tw[2], r[3] * tw[3]);
+      }
+      const float ss = group32_sum(r[0] * r[0], r[1] * r[1], r[2] * r[2], r[3] * r[3]);
+      if ((lane & 7) == 0 && fvalid) atomicAdd(epi.sumsq_out + m, __float2ull_rn(ss * LL_SUMSQ_ONE));
+    } else {  // LL_EPI_QKV_ROPE: this tile is head nb of [Hq | Hkv keys | Hkv values]
+      const int64_t slot = tslot[j];
+      const int pos_m = tpos[j];
+      if (slot < 0 || slot >= epi.slot_limit || pos_m < 0 || pos_m >= epi.max_pos) {
+        if (lane == 0) record_error(err, kErrBadIndex);
+        return;
+      }
+      float x[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) x[c] = bf16_round(v[c]);
+      const int64_t page = slot / epi.page_size, off = slot % epi.page_size;
+      bf16* dst;
+      if (nb < epi.Hq + epi.Hkv) {
+        const bf16* nw = nb < epi.Hq ? epi.q_norm_w : epi.k_norm_w;
+        if (nw != nullptr) {
+          const float gs = group32_sum(x[0] * x[0], x[1] * x[1], x[2] * x[2], x[3] * x[3]);
+          const float s0 = __shfl_sync(0xffffffffu, gs, 0), s1 = __shfl_sync(0xffffffffu, gs, 8);
+          const float s2 = __shfl_sync(0xffffffffu, gs, 16), s3 = __shfl_sync(0xffffffffu, gs, 24);
+          const float tot = (s0 + s1) + (s2 + s3);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) x[c] = x[c] * rsqrtf(tot / 128.f + epi.eps) * tw[c];
+        }
+        float p[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) p[c] = __shfl_xor_sync(0xffffffffu, x[c], 16);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float cc = tc[j][c], sn = ts[j][c];
+          x[c] = f0 < 64 ? x[c] * cc - p[c] * sn : x[c] * cc + p[c] * sn;
+        }
+        dst = nb < epi.Hq ? epi.q_out + ((size_t)m * epi.Hq + nb) * 128
+                          : epi.k_pool + (((size_t)page * epi.Hkv + (nb - epi.Hq)) * epi.page_size + off) * 128;
+      } else {
+        dst = epi.v_pool + (((size_t)page * epi.Hkv + (nb - epi.Hq - epi.Hkv)) * epi.page_size + off) * 128;
+      }
+      st_bf16x4(dst + f0, x[0], x[1], x[2], x[3]);
+    }
+  }
+};
+
 // Small-M (swap-AB, split-K) kernel.
 //   D^T[128 features, BNX rows] = W_tile[128, K] . A[BNX, K]^T
 // grid = (feature tiles, splits); each CTA does k-blocks [kb0, kb1).
@@ -314,7 +486,10 @@ struct SwapCfg {
 // only that mode's code, so a launch fetches less cold code (instruction
 // fetch stalls led the 16-row epilogue's stall profile); MODE = -1 takes the
 // mode from `epi` at run time.
-template <int BNX, int RING_KB, bool kRowPrefetch, int MODE = -1>
+//
+// kTile (BNX == 16, 2 <= M <= 16, MODE >= 0): the tile epilogue (TileEpi)
+// instead of the one-row-at-a-time one.
+template <int BNX, int RING_KB, bool kRowPrefetch, int MODE = -1, bool kTile = false>
 __global__ void __launch_bounds__(192, 2)
     gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                        bf16* __restrict__ C, const bf16* __restrict__ bias, int M, int N, int K, int ldc,
@@ -423,6 +598,96 @@ __global__ void __launch_bounds__(192, 2)
       umma_commit(tfull);
     }
     __syncwarp();
+  } else if constexpr (kTile) {
+    static_assert(BNX == 16 && MODE >= 0, "tile epilogue: 16-row kernels of one mode");
+    const int q = warp & 3;
+    TileEpi<MODE> te;
+    te.q = q;
+    te.lane = lane;
+    te.f0 = 4 * lane;
+    te.feat0 = nb * GEMM_BM + te.f0;
+    te.m0 = 4 * q;
+    pdl_wait();  // outputs / workspace may still be in use by the previous kernel
+    te.prefetch(bias, M, N, K, nb, epi);
+    const bool ok = bar_and_128(mbar_wait(tfull, 0, err, kErrTmemFullTimeout));
+    tc_fence_after();
+    // this warp's TMEM lanes: features q*32 .. q*32+31, columns = rows
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tmem_base + (uint32_t(q * 32) << 16), r);  // columns >= 16 unused
+    tmem_ld_wait();
+    float acc[4][4];
+    bool emit_rows = ok;
+    if (nsplit == 1) {
+      // Transpose through stage 0 of the ring (every MMA that read it has
+      // completed: tfull was committed after the last one).
+      float* sT = reinterpret_cast<float*>(sW);
+#pragma unroll
+      for (int m = 0; m < 16; ++m) sT[m * GEMM_BM + q * 32 + lane] = __uint_as_float(r[m]);
+      bar_sync_128();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 t = *reinterpret_cast<const float4*>(sT + (te.m0 + j) * GEMM_BM + te.f0);
+        acc[j][0] = t.x, acc[j][1] = t.y, acc[j][2] = t.z, acc[j][3] = t.w;
+      }
+    } else {
+      const int feat = nb * GEMM_BM + q * 32 + lane;
+      if (feat < N) {
+        float* w = ws + ((size_t)split * M) * N;
+        const bool empty_split = (kb1 <= kb0);
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+          if (m < M) w[(size_t)m * N + feat] = empty_split ? 0.f : __uint_as_float(r[m]);
+      }
+      // Split-K fix-up: the last CTA of this feature tile reduces all splits.
+      __threadfence();
+      bar_sync_128();
+      if (threadIdx.x == 64) {
+        const int prev = atomicAdd(&tickets[nb], 1);
+        s_last = (prev == nsplit - 1);
+      }
+      bar_sync_128();
+      emit_rows = ok && s_last;
+      if (s_last) {
+        __threadfence();
+        const size_t sstride = (size_t)M * N;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc[j][c] = 0.f;
+        if (te.fvalid) {
+          // four splits of the thread's four rows in flight at a time, each
+          // element summed in split order
+#pragma unroll 1
+          for (int s0 = 0; s0 < nsplit; s0 += 4) {
+            float4 part[4][4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+              for (int sp = 0; sp < 4; ++sp)
+                part[j][sp] = (te.m0 + j < M && s0 + sp < nsplit)
+                                  ? __ldcg(reinterpret_cast<const float4*>(
+                                        ws + (s0 + sp) * sstride + (size_t)(te.m0 + j) * N + te.feat0))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+              for (int sp = 0; sp < 4; ++sp)
+                if (s0 + sp < nsplit) {
+                  acc[j][0] += part[j][sp].x;
+                  acc[j][1] += part[j][sp].y;
+                  acc[j][2] += part[j][sp].z;
+                  acc[j][3] += part[j][sp].w;
+                }
+          }
+        }
+        if (threadIdx.x == 64) tickets[nb] = 0;  // ready for the next launch / graph replay
+      }
+    }
+    if (emit_rows) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (te.m0 + j < M) te.emit(j, acc[j], C, ldc, M, nb, epi, err);
+    }
   } else {
     const int q = warp & 3;
     const int f = q * 32 + lane;             // feature within the tile
@@ -1360,6 +1625,38 @@ static bool small_m_mode_kernels() {
   return v == 1;
 }
 
+// LL_GEMV_TILE_EPI=0 keeps 2..16-row launches on the one-row-at-a-time
+// epilogue (an A/B switch; default: the tile epilogue).
+static bool small_m_tile_epi() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("LL_GEMV_TILE_EPI");
+    v = (e != nullptr && atoi(e) == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
+static bool aligned_to(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// Whether a 2..16-row launch meets the tile epilogue's vector widths: four
+// consecutive features per thread (8-byte bf16 and 16-byte fp32 accesses).
+static bool small_m_tile_ok(const bf16* C, int ldc, const bf16* bias, int M, int N, const float* ws,
+                            const LLSmallMEpi& epi) {
+  if (M < 2 || M > 16 || (N % 32) || !aligned_to(ws, 16) || !aligned_to(bias, 8)) return false;
+  switch (epi.mode) {
+    case LL_EPI_STORE:
+    case LL_EPI_SWIGLU:
+      return (ldc % 4) == 0 && aligned_to(C, 8);
+    case LL_EPI_RESIDUAL:
+      return (epi.ld % 4) == 0 && aligned_to(epi.res, 8) && aligned_to(epi.h_out, 8) && aligned_to(epi.norm_w, 8);
+    case LL_EPI_QKV_ROPE:
+      return aligned_to(epi.q_out, 8) && aligned_to(epi.k_pool, 8) && aligned_to(epi.v_pool, 8) &&
+             aligned_to(epi.q_norm_w, 8) && aligned_to(epi.k_norm_w, 8) && aligned_to(epi.cos_sin, 16);
+    default:
+      return false;
+  }
+}
+
 static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* C, int ldc, const bf16* bias, int M,
                           int N, int K, int splits, float* ws, size_t ws_floats, int* tickets, int* err, int w_tiled,
                           const LLSmallMEpi& epi, cudaStream_t stream) {
@@ -1399,9 +1696,9 @@ static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* 
   if (w_tiled ? make_tmap_w_tiled(&tW, W, N, K) : make_tmap_2d(&tW, W, N, K, ldw, GEMM_BM)) return -2;
   if (make_tmap_2d(&tX, A, M, K, lda, BNX)) return -2;
   dim3 grid(ntiles, splits);
-#define LL_LAUNCH_SM(BNX_, RING_, PF_, MODE_)                                                            \
+#define LL_LAUNCH_SMT(BNX_, RING_, PF_, MODE_, TILE_)                                                    \
   do {                                                                                                   \
-    auto kern = gemm_swapab_kernel<BNX_, RING_, PF_, MODE_>;                                             \
+    auto kern = gemm_swapab_kernel<BNX_, RING_, PF_, MODE_, TILE_>;                                      \
     using C_ = SwapCfg<BNX_, RING_>;                                                                     \
     if (C_::SMEM > max_smem_optin()) return -7;                                                          \
     static bool init = false;                                                                            \
@@ -1412,7 +1709,18 @@ static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* 
     launch_pdl(kern, grid, dim3(192), C_::SMEM, stream, tW, tX, C, bias, M, N, K, ldc, kb_per, ws, tickets, \
                err, w_tiled, epi);                                                                       \
   } while (0)
+#define LL_LAUNCH_SM(BNX_, RING_, PF_, MODE_) LL_LAUNCH_SMT(BNX_, RING_, PF_, MODE_, false)
 #define LL_LAUNCH_S(BNX_, RING_, PF_) LL_LAUNCH_SM(BNX_, RING_, PF_, -1)
+// 2..16 rows on the tile epilogue, one instantiation per mode
+#define LL_LAUNCH_T16()                                                                  \
+  do {                                                                                   \
+    switch (epi.mode) {                                                                  \
+      case LL_EPI_STORE: LL_LAUNCH_SMT(16, 108, true, LL_EPI_STORE, true); break;       \
+      case LL_EPI_SWIGLU: LL_LAUNCH_SMT(16, 108, true, LL_EPI_SWIGLU, true); break;     \
+      case LL_EPI_RESIDUAL: LL_LAUNCH_SMT(16, 108, true, LL_EPI_RESIDUAL, true); break; \
+      default: LL_LAUNCH_SMT(16, 108, true, LL_EPI_QKV_ROPE, true); break;              \
+    }                                                                                    \
+  } while (0)
 // the decode sizes (M <= 16) on the default ring: one instantiation per epilogue mode
 #define LL_LAUNCH_S16(PF_)                                     \
   do {                                                         \
@@ -1438,6 +1746,7 @@ static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* 
       case 16:
         if (small_m_mode_kernels()) {
           if (M == 1) LL_LAUNCH_S16(false);
+          else if (small_m_tile_epi() && small_m_tile_ok(C, ldc, bias, M, N, ws, epi)) LL_LAUNCH_T16();
           else LL_LAUNCH_S16(true);
         } else if (M == 1) {
           LL_LAUNCH_S(16, 108, false);
@@ -1450,9 +1759,11 @@ static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* 
       default: LL_LAUNCH_S(128, 108, true); break;
     }
   }
+#undef LL_LAUNCH_T16
 #undef LL_LAUNCH_S16
 #undef LL_LAUNCH_S
 #undef LL_LAUNCH_SM
+#undef LL_LAUNCH_SMT
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 

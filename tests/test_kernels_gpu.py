@@ -151,6 +151,64 @@ def test_gemv_qkv_rope_matches_unfused(qk_norm, M):
     assert _rel(q1, qc) < 1e-2 and _rel(pools[0], kc) < 1e-2 and _rel(pools[1], vc) < 1e-2
 
 
+@pytest.mark.parametrize("max_splits", [0, 1])
+@pytest.mark.parametrize("M", [2, 5, 16])
+def test_gemv_tile_epilogue_rows_equal_one_row_launches(M, max_splits, monkeypatch):
+    """2..16-row GEMVs run the tile epilogue (a row per warp, four features
+    per lane); 1-row GEMVs run the one-row epilogue.  Row for row the two
+    give the same bits in all four epilogue modes, with the split-K fix-up
+    (auto split count) and without it (one split)."""
+    monkeypatch.setattr(ops, "_SMALL_M_MAX_SPLITS", max_splits)
+    torch.manual_seed(11)
+    K, N, eps = 1536, 1024, 1e-6
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    bias = torch.randn(N, device=DEV, dtype=torch.bfloat16)
+    ws = ops.workspace(DEV)
+    # plain store with bias
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    ops._small_m(ops._cuda(), ws, x, w, bias, out)
+    for r in range(M):
+        o1 = torch.empty(1, N, device=DEV, dtype=torch.bfloat16)
+        ops._small_m(ops._cuda(), ws, x[r:r + 1], w, bias, o1)
+        assert torch.equal(out[r], o1[0]), r
+    # row-scaled SwiGLU
+    sumsq = ops.sumsq_from_values(torch.rand(M, device=DEV) * K * 3 + 1.0)
+    sw = ops.gemv_rownorm(x, w, None, sumsq, eps, swiglu=True)
+    for r in range(M):
+        assert torch.equal(sw[r], ops.gemv_rownorm(x[r:r + 1], w, None, sumsq[r:r + 1], eps, swiglu=True)[0]), r
+    # residual add + next-norm data + fixed-point sums of squares
+    res0 = torch.randn(M, N, device=DEV, dtype=torch.bfloat16)
+    nw = torch.rand(N, device=DEV, dtype=torch.bfloat16) + 0.5
+    res, h, sq = res0.clone(), torch.empty(M, N, device=DEV, dtype=torch.bfloat16), ops.sumsq_buffer(M, DEV)
+    ops.gemv_residual(x, w, res, nw, h, sq)
+    for r in range(M):
+        res1, h1, sq1 = res0[r:r + 1].clone(), torch.empty(1, N, device=DEV, dtype=torch.bfloat16), ops.sumsq_buffer(1, DEV)
+        ops.gemv_residual(x[r:r + 1], w, res1, nw, h1, sq1)
+        assert torch.equal(res[r], res1[0]) and torch.equal(h[r], h1[0]) and torch.equal(sq[r], sq1[0]), r
+    # qkv with QK-norm, RoPE and the KV write
+    Hq, Hkv, D, ps, pages = 8, 2, 128, 16, 4
+    Nq = (Hq + 2 * Hkv) * D
+    wq = torch.randn(Nq, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    bq = torch.randn(Nq, device=DEV, dtype=torch.bfloat16)
+    pos = torch.randperm(4096, generator=torch.Generator().manual_seed(M))[:M].to(DEV, torch.int32)
+    slots = torch.randperm(pages * ps, generator=torch.Generator().manual_seed(M + 1))[:M].to(DEV)
+    cs = ref.rope_cos_sin_table(4096, 128, 1e6).to(DEV)
+    qn = torch.rand(D, device=DEV, dtype=torch.bfloat16) + 0.5
+    kn = torch.rand(D, device=DEV, dtype=torch.bfloat16) + 0.5
+    pools = [torch.zeros(pages, Hkv, ps, D, device=DEV, dtype=torch.bfloat16) for _ in range(4)]
+    q = torch.empty(M, Hq, D, device=DEV, dtype=torch.bfloat16)
+    ops.gemv_qkv_rope(x, wq, bq, pos, slots, cs, q, pools[0], pools[1], Hq, Hkv, qn, kn, eps)
+    for r in range(M):
+        q1 = torch.empty(1, Hq, D, device=DEV, dtype=torch.bfloat16)
+        ops.gemv_qkv_rope(x[r:r + 1], wq, bq, pos[r:r + 1], slots[r:r + 1], cs, q1, pools[2], pools[3], Hq, Hkv,
+                          qn, kn, eps)
+        assert torch.equal(q[r], q1[0]), r
+    assert torch.equal(pools[0], pools[2]) and torch.equal(pools[1], pools[3])
+    torch.cuda.synchronize()
+    assert ops.check_errors(DEV) == 0
+
+
 @pytest.mark.parametrize("M", [1, 3, 16, 17, 64, 100, 128])
 @pytest.mark.parametrize("N,K", [(4608, 3584), (3584, 18944), (1000, 512)])
 def test_gemm_small_m(M, N, K):
