@@ -172,8 +172,19 @@ EPI_STORE, EPI_SWIGLU, EPI_RESIDUAL, EPI_QKV_ROPE = 0, 1, 2, 3
 _SMALL_M_MAX_SPLITS = int(os.environ.get("LL_SMALL_M_MAX_SPLITS", "0") or 0)
 
 
+# 2..16-row GEMVs (the tile epilogue) take at most 8 splits: the fix-up loads
+# four splits' partials per round.  Measured at 16 rows (2/4/8/automatic
+# splits): the cap takes the qkv GEMV of a Qwen3-32B TP=8 rank from 16 splits
+# and 12.7 us to 10.8 us, and Qwen2.5-7B's o_proj / down from 10 splits and
+# 11.5 / 28.2 us to 10.5 / 27.4 us; 4 splits was up to 8 % faster on some
+# shapes and slower on others.
+_TILE_MAX_SPLITS = 8
+
+
 def _small_m_splits(ws, M: int, N: int, K: int) -> int:
     splits = _cuda().gemm_small_m_splits(N, K)
+    if 1 < M <= 16 and splits > _TILE_MAX_SPLITS:
+        splits = _TILE_MAX_SPLITS
     if _SMALL_M_MAX_SPLITS > 0 and splits > _SMALL_M_MAX_SPLITS:
         splits = _SMALL_M_MAX_SPLITS
     if splits > 1:
