@@ -177,8 +177,9 @@ _SMALL_M_MAX_SPLITS = int(os.environ.get("LL_SMALL_M_MAX_SPLITS", "0") or 0)
 # splits): the cap takes the qkv GEMV of a Qwen3-32B TP=8 rank from 16 splits
 # and 12.7 us to 10.8 us, and Qwen2.5-7B's o_proj / down from 10 splits and
 # 11.5 / 28.2 us to 10.5 / 27.4 us; 4 splits was up to 8 % faster on some
-# shapes and slower on others.
-_TILE_MAX_SPLITS = 8
+# shapes and slower on others.  LL_GEMV_TILE_MAX_SPLITS=<n> overrides the cap
+# (a measurement knob).
+_TILE_MAX_SPLITS = int(os.environ.get("LL_GEMV_TILE_MAX_SPLITS", "8") or 8)
 
 
 def _small_m_splits(ws, M: int, N: int, K: int) -> int:
