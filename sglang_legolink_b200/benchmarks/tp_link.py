@@ -181,6 +181,7 @@ def main():
         links.append(e0.elapsed_time(e1))
         rows = len(s.link_plan.recompute_positions)
         seqs.append(s)
+    eng.warm_decode(seqs)  # the batch's decode graph is captured before the timed region
     barrier()
     d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     d0.record()

@@ -957,6 +957,20 @@ class Engine:
                 if int(t) in stop:
                     s.finished = True
 
+    def warm_decode(self, seqs: list[Sequence_]) -> None:
+        """Captures the CUDA graph that a greedy decode of ``seqs`` replays
+        (the graph of the bucket of ``len(seqs)`` rows) without generating a
+        token, so the first decode of a new batch size does not pay for the
+        capture and its two warm-up forwards.  The warm-up writes row 0's
+        next KV slot, which the first real step overwrites.  No-op without
+        CUDA graphs."""
+        if not self.use_cuda_graphs or not seqs:
+            return
+        with self._lock:
+            for s in seqs:
+                self._ensure_capacity(s, s.length + 1)
+            self._graph(self._bucket(len(seqs)), pages_for(self.max_context, self.page_size), seqs)
+
     def decode_chained(self, seqs: list[Sequence_], steps: int, stop=frozenset()) -> None:
         """``steps`` greedy decode steps with no host round trip between
         them: capacity for all steps is reserved first, every step's

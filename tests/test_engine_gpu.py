@@ -84,6 +84,25 @@ def test_fused_decode_step_matches_unfused(name, monkeypatch):
     assert ((kf.float() - kp.float()).norm() / kp.float().norm()).item() < 1e-2
 
 
+def test_warm_decode_captures_the_graph_and_changes_no_tokens():
+    """warm_decode captures the batch's decode graph before any token is
+    generated (page boundaries included: one prompt ends on a page edge);
+    the decode that follows replays it and gives the tokens of a decode
+    without the warm-up."""
+    cfg, eng, subs, suffix = _setup("small-qwen2", seed=5)
+    prompts = [subs[0] + suffix, subs[2][:32], subs[1] + suffix]
+    seqs = [eng.prefill(p) for p in prompts]
+    eng.warm_decode(seqs)
+    assert eng._bucket(3) in eng._graphs
+    g = eng._graphs[eng._bucket(3)]["graph"]
+    eng.decode(seqs, 8)
+    assert eng._graphs[eng._bucket(3)]["graph"] is g
+    for p, ref in zip(prompts, seqs):
+        s = eng.prefill(p)
+        eng.decode([s], 8)
+        assert s.output_ids == ref.output_ids
+
+
 def test_padded_decode_bucket_keeps_row0_kv():
     """Three sequences in the bucket of four: the padded row writes the
     pool's scratch page, so every sequence decodes as it does alone."""
