@@ -294,7 +294,8 @@ __device__ __forceinline__ void res_add_norm_store(const uint4 (&res_v)[VPT], co
 // WMAX: compile-time bound on the world size, so that the loads of every
 // rank's partial row are issued together after the wait (one NVLink round
 // trip instead of one per pair of ranks).  The residual row and the norm
-// weights do not depend on the other ranks and are loaded before the wait.
+// weights do not depend on the other ranks and are loaded before the wait
+// for their arrivals.
 template <int VPT, int WMAX>
 __global__ void __launch_bounds__(TPD)
     tp_decode_allreduce_norm_kernel(bf16* __restrict__ residual, const bf16* __restrict__ w, bf16* __restrict__ out,
@@ -306,13 +307,23 @@ __global__ void __launch_bounds__(TPD)
   const int row = blockIdx.x;
   const bool live = row < rows;
   uint4* rr = reinterpret_cast<uint4*>(residual + (size_t)row * H);
+  // The next GEMV may launch now: its CTAs stream their weights while this
+  // boundary waits for the other ranks, and read our output only after
+  // their own pdl_wait (this grid complete).
+  pdl_trigger();
   uint4 res_v[VPT], w_v[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {  // norm weights: written by no kernel
+    const int idx = threadIdx.x + i * TPD;
+    w_v[i] = (live && idx < nvec) ? reinterpret_cast<const uint4*>(w)[idx] : make_uint4(0, 0, 0, 0);
+  }
+  // The partial rows, the residual and the epoch are written by earlier
+  // kernels, which may still run while this one is resident.
+  pdl_wait();
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int idx = threadIdx.x + i * TPD;
-    const bool in = live && idx < nvec;
-    res_v[i] = in ? rr[idx] : make_uint4(0, 0, 0, 0);
-    w_v[i] = in ? reinterpret_cast<const uint4*>(w)[idx] : make_uint4(0, 0, 0, 0);
+    res_v[i] = (live && idx < nvec) ? rr[idx] : make_uint4(0, 0, 0, 0);
   }
   if (threadIdx.x == 0) {
     const unsigned long long e = *reinterpret_cast<volatile unsigned long long*>(td.epoch) + 1ull;
@@ -444,7 +455,8 @@ extern "C" int ll_tp_decode_allreduce_norm(void* residual, const void* w, void* 
   bf16* r = static_cast<bf16*>(residual);
   const bf16* wp = static_cast<const bf16*>(w);
   bf16* o = static_cast<bf16*>(out);
-#define LL_TPD(V, W) ll::tp_decode_allreduce_norm_kernel<V, W><<<rows, ll::TPD, 0, stream>>>(r, wp, o, eps, H, rows, *td, err)
+#define LL_TPD(V, W) \
+  ll::launch_pdl(ll::tp_decode_allreduce_norm_kernel<V, W>, dim3(rows), dim3(ll::TPD), 0, stream, r, wp, o, eps, H, rows, *td, err)
 #define LL_TPD_W(V)                    \
   do {                                 \
     if (td->world <= 2) LL_TPD(V, 2);  \

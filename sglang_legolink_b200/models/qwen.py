@@ -351,10 +351,17 @@ class QwenModel:
         mlp = self._buf("mlp", (T, self.inter))
         o = self._buf("o", (T, H))
         n = len(self.layers)
+        # the qkv GEMV writes Q and this step's K/V with QK-norm and RoPE in
+        # its stores (one launch instead of GEMV + rope_qkv_write)
+        qkv_fused = T <= ops.SMALL_M_MAX and D == 128 and c.rotary_dim == 128
         for li, lw in enumerate(self.layers):
-            ops.linear(h, lw.qkv_w, lw.qkv_b, out=qkv)
-            ops.rope_qkv_write(qkv, fb.positions, fb.slots, self.cos_sin, q, kv.k[li], kv.v[li], self.hq, self.hkv,
-                               D, lw.q_norm, lw.k_norm, eps)
+            if qkv_fused:
+                ops.gemv_qkv_rope(h, lw.qkv_w, lw.qkv_b, fb.positions, fb.slots, self.cos_sin, q, kv.k[li],
+                                  kv.v[li], self.hq, self.hkv, lw.q_norm, lw.k_norm, eps)
+            else:
+                ops.linear(h, lw.qkv_w, lw.qkv_b, out=qkv)
+                ops.rope_qkv_write(qkv, fb.positions, fb.slots, self.cos_sin, q, kv.k[li], kv.v[li], self.hq,
+                                   self.hkv, D, lw.q_norm, lw.k_norm, eps)
             with mk.region("Attention", li, q=q):
                 ops.attention_decode(q, kv.k[li], kv.v[li], fb.page_table, fb.kv_lens, self.scale,
                                      nsplit=fb.decode_nsplit, out=attn)

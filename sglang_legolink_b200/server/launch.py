@@ -335,8 +335,12 @@ def rank_main(a, rank: int, world: int, local: int, ready=None) -> None:
         else:
             box = [None]
             dist.broadcast_object_list(box, src=0, group=ctrl)
+        # a stop that stalls prints every thread's stack after 20 s
+        faulthandler.dump_traceback_later(20, repeat=False)
+        print(f"rank {rank}: stop received", flush=True)
         srv.shutdown()
         sch.stop()
+        faulthandler.cancel_dump_traceback_later()
     finally:
         # a shutdown that stalls prints every thread's stack after a minute
         faulthandler.dump_traceback_later(60, repeat=False)

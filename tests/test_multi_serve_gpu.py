@@ -50,7 +50,7 @@ def _msgs(t):
 def _start(flags, port):
     env = {**os.environ, "NCCL_NVLS_ENABLE": "0", "TORCH_SYMM_MEM_DISABLE_MULTICAST": "1",
            "PYTHONPATH": ROOT + os.pathsep + os.environ.get("PYTHONPATH", "")}
-    p = subprocess.Popen(["timeout", "-k", "30", "600", sys.executable, "-m", "sglang_legolink_b200.server.http_server",
+    p = subprocess.Popen(["timeout", "-k", "90", "600", sys.executable, "-m", "sglang_legolink_b200.server.http_server",
                           "--model", "small-qwen3", "--port", str(port), "--context-length", "4096", *flags],
                          cwd=ROOT, env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True,
                          start_new_session=True)
