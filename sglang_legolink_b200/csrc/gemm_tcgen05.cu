@@ -1687,7 +1687,12 @@ static int small_m_launch(const bf16* A, int lda, const bf16* W, int ldw, bf16* 
   }
   const int ntiles = (N + GEMM_BM - 1) / GEMM_BM;
   const int num_kb = (K + GEMM_BK - 1) / GEMM_BK;
-  if (splits <= 0) splits = ll_gemm_small_m_splits(N, K);
+  if (splits <= 0) {
+    splits = ll_gemm_small_m_splits(N, K);
+    // 2..16 rows (the tile epilogue): at most 8 splits, the cap that
+    // ops._small_m_splits applies, so both routes sum in the same order
+    if (M > 1 && M <= 16 && splits > 8) splits = 8;
+  }
   int kb_per = (num_kb + splits - 1) / splits;
   splits = (num_kb + kb_per - 1) / kb_per;
   if (splits > 1 && (ws == nullptr || tickets == nullptr || ws_floats < (size_t)splits * M * N)) return -6;
