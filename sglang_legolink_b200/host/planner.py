@@ -175,6 +175,23 @@ class PolicyContext:
     preceding_model_tokens: int = 0
     planned_repair_model_tokens: Optional[int] = None
     repair_window_source: str = "unspecified"
+    # The compile floor is defined in model tokens: a block counted by an
+    # estimating tokenizer cannot be compared with it unless the caller asks
+    # for estimate-only planning (reference token_accounting.py:44-187).
+    allow_estimated_tokens: bool = False
+
+
+def _require_model_tokens(v: SubContext, ctx: PolicyContext, what: str) -> None:
+    """Compile decisions compare token counts with quantities defined in
+    model tokens; a count from an estimating tokenizer may take part only
+    when the caller asked for estimate-only planning."""
+    if getattr(v, "token_unit", "model") != "model" and not ctx.allow_estimated_tokens:
+        from .audits import TokenAccountingError
+
+        raise TokenAccountingError(
+            f"sub-context {v.sub_context_id}: its {v.token_count} tokens are an estimate ({v.token_unit}); "
+            f"{what} is in model tokens (count with the model's tokenizer, or plan with "
+            "allow_estimated_tokens=True)")
 
 
 class CompilePolicy:
@@ -204,6 +221,7 @@ class CompilePolicy:
                                                        {**prov, **kw.pop("provenance", {})}, kw.get("cost"))
 
     def _decide(self, v, ctx, D):
+        _require_model_tokens(v, ctx, f"the compile floor of {ctx.min_compile_model_tokens}")
         if v.token_count < ctx.min_compile_model_tokens:
             return D(CompileAction.KEEP_MUTABLE, BELOW_COMPILE_FLOOR)
         if ctx.expected_future_reuse < 1:
@@ -259,6 +277,7 @@ class CostBenefitCompilePolicy(CompilePolicy):
     def _decide(self, v, ctx, D):
         from . import compile_cost as cc
 
+        _require_model_tokens(v, ctx, "the measured compile-cost curve")
         if ctx.memory_pressure >= self.memory_pressure_stop:
             return D(CompileAction.KEEP_MUTABLE, "high KV memory pressure")
         try:

@@ -257,3 +257,43 @@ def test_legacy_plan_bridge_is_refused_then_replayed_with_runtime_layout(tmp_pat
     monkeypatch.setenv("SGLANG_PIC_ALLOW_LEGACY_LINK_FIELDS", "1")
     seq = eng.link(dict(plan), query)
     assert list(seq.link_plan.recompute_positions) == list(range(100, 108)) + list(range(160, 165))
+
+
+def _estimated_and_model_contexts():
+    text = [("task_instruction", "sys", "Instruction text. " * 50, {}),
+            ("tool_output", "t1", "tool text " * 80, {}), ("user_request", "u", "go", {})]
+    est = ContextManager("est", tokenizer=RegexTokenizer())
+    est.ingest(text)
+    mod = ContextManager("mod", tokenizer=HashTokenizer(vocab_size=4096))
+    mod.ingest(text)
+    return est, mod
+
+
+def test_compile_floor_refuses_estimated_counts_unless_asked():
+    """The compile floor is in model tokens: a plan over blocks counted by the
+    regex estimator fails closed, plans over model-token counts are
+    unchanged, and estimate-only planning works when the caller asks."""
+    from sglang_legolink_b200.host.planner import PolicyContext
+
+    est, mod = _estimated_and_model_contexts()
+    assert all(v.token_unit == "estimated" for v in est.contexts())
+    with pytest.raises(TokenAccountingError, match="model tokens"):
+        Planner().plan(est.select("go"), est.contexts())
+    plan = Planner().plan(est.select("go"), est.contexts(), policy_context=PolicyContext(allow_estimated_tokens=True))
+    assert plan is not None
+    # model-token counts: the policy decides exactly as before (the floor
+    # still keeps a short block mutable)
+    plan = Planner().plan(mod.select("go"), mod.contexts())
+    assert plan is not None
+
+
+def test_cost_benefit_policy_refuses_estimated_counts():
+    from sglang_legolink_b200.host import compile_cost as cc
+    from sglang_legolink_b200.host.planner import CostBenefitCompilePolicy, PolicyContext
+
+    est, _ = _estimated_and_model_contexts()
+    pol = CostBenefitCompilePolicy(reuse_expectation=cc.FixedReuseExpectation(2.0), fallback="legacy_fixed_64")
+    v = next(v for v in est.contexts() if v.reuse_candidate and not v.is_mutable)
+    with pytest.raises(TokenAccountingError):
+        pol.decide(v, PolicyContext())
+    assert pol.decide(v, PolicyContext(allow_estimated_tokens=True)).policy == "cost_benefit"
