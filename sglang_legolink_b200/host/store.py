@@ -88,9 +88,20 @@ class SubContext:
 
     @classmethod
     def from_dict(cls, d: dict) -> "SubContext":
+        """A stored row's token unit is not taken on its word: the count is
+        a model-token count only if the row says so AND names the tokenizer
+        that produced it, and that tokenizer is not an estimator.  A row
+        without that provenance (older rows have no unit) reads as an
+        estimate, which the compile policies refuse to compare with their
+        model-token floors (reference token_accounting.py:44-187)."""
+        from .tokenizer import RegexTokenizer
+
         d = dict(d)
         d["source_spans"] = tuple(SourceSpan(**s) for s in d["source_spans"])
         d["token_ids"] = tuple(d.get("token_ids") or ())
+        fp = (d.get("metadata") or {}).get("tokenizer_fingerprint")
+        model = d.get("token_unit") == "model" and bool(fp) and fp != RegexTokenizer.fingerprint
+        d["token_unit"] = "model" if model else "estimated"
         return cls(**d)
 
     @classmethod

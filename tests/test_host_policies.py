@@ -297,3 +297,23 @@ def test_cost_benefit_policy_refuses_estimated_counts():
     with pytest.raises(TokenAccountingError):
         pol.decide(v, PolicyContext())
     assert pol.decide(v, PolicyContext(allow_estimated_tokens=True)).policy == "cost_benefit"
+
+
+def test_stored_rows_keep_a_model_unit_only_with_its_provenance():
+    """A stored sub-context serializes its unit; on read a model-token claim
+    stands only with the fingerprint of a model tokenizer, and a row with no
+    unit (an older row) reads as an estimate."""
+    from sglang_legolink_b200.host.store import SubContext
+
+    est, mod = _estimated_and_model_contexts()
+    v = next(iter(mod.contexts()))
+    d = v.to_dict()
+    assert d["token_unit"] == "model" and SubContext.from_dict(d).token_unit == "model"
+    assert SubContext.from_dict(next(iter(est.contexts())).to_dict()).token_unit == "estimated"
+    legacy = dict(d)
+    legacy.pop("token_unit")
+    assert SubContext.from_dict(legacy).token_unit == "estimated"
+    forged = dict(d, metadata={**d["metadata"], "tokenizer_fingerprint": RegexTokenizer.fingerprint})
+    assert SubContext.from_dict(forged).token_unit == "estimated"
+    bare = dict(d, metadata={k: x for k, x in d["metadata"].items() if k != "tokenizer_fingerprint"})
+    assert SubContext.from_dict(bare).token_unit == "estimated"
