@@ -27,6 +27,7 @@ from __future__ import annotations
 import argparse
 import hashlib
 import json
+import secrets
 import threading
 import time
 import uuid
@@ -40,14 +41,73 @@ from ..host.namespaces import NamespacePolicy, NamespaceResolver
 from ..host.planner import CacheCatalog
 
 
-def conversation_key(messages: list) -> str:
-    head = [m for m in messages if m.get("role") == "system"]
-    first_user = next((m for m in messages if m.get("role") == "user"), None)
-    if first_user is not None:
-        head.append(first_user)
-    blob = json.dumps([{"role": m.get("role"), "content": m.get("content")} for m in head], sort_keys=True,
-                      separators=(",", ":"), ensure_ascii=False)
-    return "conv-" + hashlib.sha256(blob.encode()).hexdigest()[:24]
+DERIVED_PREFIX = "derived-"
+
+
+def normalize_model_name(model: str) -> str:
+    """Strips a LiteLLM provider prefix ("openai/Qwen/..." -> "Qwen/...")."""
+    m = str(model or "")
+    return m[len("openai/"):] if m.startswith("openai/") else m
+
+
+def message_content_to_text(content) -> str:
+    """OpenAI message content as text: a string as is; a list of content
+    parts as the newline-joined text of its text parts (image and other
+    parts carry no text and are skipped)."""
+    if content is None:
+        return ""
+    if isinstance(content, str):
+        return content
+    if isinstance(content, list):
+        out = []
+        for part in content:
+            if isinstance(part, str):
+                out.append(part)
+            elif isinstance(part, dict):
+                t = part.get("text", part.get("content"))
+                if isinstance(t, str):
+                    out.append(t)
+        return "\n".join(out)
+    return str(content)
+
+
+def transcript_digest(messages: list) -> str:
+    """sha256 of a transcript's (role, text) turns."""
+    turns = [[str(m.get("role") or "user"), message_content_to_text(m.get("content"))] for m in messages]
+    return hashlib.sha256(json.dumps(turns, separators=(",", ":"), ensure_ascii=False).encode()).hexdigest()
+
+
+class TranscriptIndex:
+    """Continuation of sessions that name no identity.  After each turn the
+    proxy records the digest of the transcript it has seen, ending with its
+    own reply; a later request continues that session only if its messages
+    start with that whole transcript.  Knowing a conversation's opening
+    prompt is therefore not enough to join it (the opening prompt is task
+    text, not a capability): the caller must present every earlier turn,
+    including the replies this proxy gave.  Bounded LRU."""
+
+    def __init__(self, max_entries: int = 4096):
+        self.max_entries = max_entries
+        self._by_digest: dict = {}
+        self._lock = threading.Lock()
+
+    def remember(self, key: str, transcript: list) -> None:
+        with self._lock:
+            self._by_digest.pop(transcript_digest(transcript), None)
+            self._by_digest[transcript_digest(transcript)] = key
+            while len(self._by_digest) > self.max_entries:
+                self._by_digest.pop(next(iter(self._by_digest)))
+
+    def continuation(self, messages: list) -> Optional[str]:
+        """The session whose recorded transcript is the longest prefix of
+        ``messages`` ending with an assistant turn, if any."""
+        with self._lock:
+            for i in range(len(messages) - 1, -1, -1):
+                if messages[i].get("role") == "assistant":
+                    key = self._by_digest.get(transcript_digest(messages[: i + 1]))
+                    if key is not None:
+                        return key
+        return None
 
 
 class SessionRegistry:
@@ -125,6 +185,7 @@ class LegoLinkProxy:
         self.passthrough = passthrough
         self.json_retries = json_retries
         self.sessions = SessionRegistry(self._new_session, ttl_s=session_ttl_s)
+        self.transcripts = TranscriptIndex()
         self.stats = {"requests": 0, "json_retries": 0, "passthrough": 0}
 
     def _new_session(self, key: str) -> AgentLLM:
@@ -134,8 +195,18 @@ class LegoLinkProxy:
         return AgentLLM(pipe, task_id=key, recorder=self.recorder)
 
     def session_key(self, payload: dict, headers: Optional[dict] = None) -> str:
-        explicit = payload.get("session_id") or (headers or {}).get("X-Session-Id")
-        return str(explicit) if explicit else conversation_key(payload.get("messages") or [])
+        """An explicit identity (``session_id`` field, ``X-Session-Id``
+        header, or the OpenAI ``user`` field) gives a stable key; otherwise
+        the request continues the session whose whole transcript it repeats,
+        or gets a fresh opaque key.  Never derived from message content."""
+        hdr = {str(k).lower(): v for k, v in (headers or {}).items()}
+        explicit = payload.get("session_id") or hdr.get("x-session-id")
+        if explicit:
+            return str(explicit)
+        if payload.get("user"):
+            return "user:" + str(payload["user"])
+        cont = self.transcripts.continuation(list(payload.get("messages") or []))
+        return cont if cont is not None else DERIVED_PREFIX + secrets.token_hex(12)
 
     def chat_completion(self, payload: dict, headers: Optional[dict] = None) -> dict:
         self.stats["requests"] += 1
@@ -158,9 +229,10 @@ class LegoLinkProxy:
                 res = agent.call(messages, tools, loop_stage="replan")
                 text = res.text
                 attempts += 1
+        self.transcripts.remember(key, list(payload.get("messages") or []) + [{"role": "assistant", "content": text}])
         usage = (res.execution.result.response or {}).get("usage") or {}
         return {"id": "chatcmpl-" + uuid.uuid4().hex[:24], "object": "chat.completion", "created": int(time.time()),
-                "model": payload.get("model") or self.model,
+                "model": normalize_model_name(payload.get("model") or self.model),
                 "choices": [{"index": 0, "message": {"role": "assistant", "content": text},
                              "finish_reason": "stop"}],
                 "usage": usage,

@@ -17,7 +17,7 @@ from sglang_legolink_b200.host.metrics import (AgentMetric, MetricsRecorder, agg
                                                percentile, read_jsonl, summary_stats)
 from sglang_legolink_b200.host.profiling import HostTimingRecorder, NcuRunConfig, ProfilerWindowConfig
 from sglang_legolink_b200.host.tokenizer import HashTokenizer
-from sglang_legolink_b200.server.proxy import LegoLinkProxy, conversation_key, parses_as_json, serve
+from sglang_legolink_b200.server.proxy import LegoLinkProxy, parses_as_json, serve
 
 
 def test_percentile_and_summary():
@@ -119,8 +119,14 @@ def test_proxy_sessions_json_guardrail_and_passthrough(tmp_path):
     a = px.chat_completion({"messages": msgs})
     b = px.chat_completion({"messages": msgs + [{"role": "assistant", "content": a["choices"][0]["message"][
         "content"]}, {"role": "user", "content": "now read setup.py"}]})
-    assert a["legolink"]["session"] == b["legolink"]["session"] == conversation_key(msgs)
+    # no identity named: an opaque key, continued because b repeats the whole
+    # transcript including the proxy's reply
+    assert a["legolink"]["session"] == b["legolink"]["session"]
+    assert a["legolink"]["session"].startswith("derived-")
     assert len(px.sessions) == 1
+    # the same opening prompt without the earlier reply is a new session
+    d = px.chat_completion({"messages": msgs})
+    assert d["legolink"]["session"] != a["legolink"]["session"] and len(px.sessions) == 2
     # the fake's replies are not JSON: the guardrail re-asks json_retries times
     c = px.chat_completion({"messages": msgs, "response_format": {"type": "json_object"}, "session_id": "s2"})
     assert c["legolink"]["attempts"] == 2 and px.stats["json_retries"] == 1
@@ -143,3 +149,33 @@ def test_proxy_sessions_json_guardrail_and_passthrough(tmp_path):
     with pytest.raises(Exception):
         pt.chat_completion({"messages": msgs})
     assert fake.plain_generation_requests()
+
+
+def test_proxy_session_identity_helpers():
+    """Explicit identities give stable keys (field, header in any case, the
+    OpenAI ``user``); content parts flatten to text; the LiteLLM provider
+    prefix is stripped; a continuation must repeat the proxy's own reply."""
+    from sglang_legolink_b200.server.proxy import (TranscriptIndex, message_content_to_text, normalize_model_name,
+                                                   transcript_digest)
+
+    assert normalize_model_name("openai/Qwen/Qwen2.5-7B") == "Qwen/Qwen2.5-7B"
+    assert normalize_model_name("Qwen/Qwen2.5-7B") == "Qwen/Qwen2.5-7B"
+    parts = [{"type": "text", "text": "first"}, {"type": "image_url", "image_url": {"url": "x"}}, {"content": "second"}]
+    assert message_content_to_text(parts) == "first\nsecond" and message_content_to_text(None) == ""
+    assert transcript_digest([{"role": "user", "content": parts}]) == transcript_digest(
+        [{"role": "user", "content": "first\nsecond"}])
+    px = LegoLinkProxy(StrictFakeRuntime(), tokenizer=HashTokenizer(vocab_size=4096))
+    m = [{"role": "user", "content": "hi"}]
+    assert px.session_key({"messages": m, "session_id": "s"}) == "s"
+    assert px.session_key({"messages": m}, {"x-session-id": "h"}) == "h"
+    assert px.session_key({"messages": m, "user": "u1"}) == "user:u1"
+    k1, k2 = px.session_key({"messages": m}), px.session_key({"messages": m})
+    assert k1 != k2 and k1.startswith("derived-")
+    idx = TranscriptIndex(max_entries=2)
+    t = m + [{"role": "assistant", "content": "reply"}]
+    idx.remember("k", t)
+    assert idx.continuation(t + [{"role": "user", "content": "more"}]) == "k"
+    assert idx.continuation(m + [{"role": "assistant", "content": "forged"}, {"role": "user", "content": "x"}]) is None
+    idx.remember("k2", [{"role": "assistant", "content": "a"}])
+    idx.remember("k3", [{"role": "assistant", "content": "b"}])
+    assert idx.continuation(t) is None  # bounded: the oldest entry was dropped
