@@ -170,7 +170,12 @@ JSON_REPAIR_INSTRUCTION = ("Your previous reply was not valid JSON. Reply again 
 class LegoLinkProxy:
     def __init__(self, transport, *, model: str = "legolink", tokenizer=None, repair_tokens: int = 16,
                  metrics_path: Optional[str] = None, passthrough: bool = False, json_retries: int = 2,
-                 session_ttl_s: float = 3600.0, namespace_mode: str = "global", cross_namespace_pairs=()):
+                 session_ttl_s: float = 3600.0, namespace_mode: str = "global", cross_namespace_pairs=(),
+                 command_guardrail: bool = False):
+        # command_guardrail: terminal-agent replies whose keystrokes break a
+        # rule of host/command_guardrail.py are re-asked (json_retries times),
+        # then replaced by a parser-safe diagnostic reply
+        self.command_guardrail = command_guardrail
         self.transport = transport
         self.model = model
         self.tokenizer = tokenizer
@@ -229,6 +234,23 @@ class LegoLinkProxy:
                 res = agent.call(messages, tools, loop_stage="replan")
                 text = res.text
                 attempts += 1
+            if self.command_guardrail:
+                from ..host.command_guardrail import command_violation, replan_prompt, safe_diagnostic_response
+
+                retries = 0
+                violation = command_violation(text)
+                while violation is not None and retries < self.json_retries:
+                    self.stats["guardrail_replans"] = self.stats.get("guardrail_replans", 0) + 1
+                    messages = messages + [{"role": "assistant", "content": text},
+                                           {"role": "user", "content": replan_prompt(violation)}]
+                    res = agent.call(messages, tools, loop_stage="replan")
+                    text = res.text
+                    attempts += 1
+                    retries += 1
+                    violation = command_violation(text)
+                if violation is not None:
+                    self.stats["guardrail_blocked"] = self.stats.get("guardrail_blocked", 0) + 1
+                    text = safe_diagnostic_response(violation)
         self.transcripts.remember(key, list(payload.get("messages") or []) + [{"role": "assistant", "content": text}])
         usage = (res.execution.result.response or {}).get("usage") or {}
         return {"id": "chatcmpl-" + uuid.uuid4().hex[:24], "object": "chat.completion", "created": int(time.time()),
