@@ -324,6 +324,8 @@ def main():
     ap.add_argument("--metrics", default=None, help="metrics JSONL path")
     ap.add_argument("--passthrough", action="store_true", help="control arm: forward requests unchanged")
     ap.add_argument("--json-retries", type=int, default=2)
+    ap.add_argument("--command-guardrail", action="store_true",
+                    help="re-ask, then block, terminal-agent replies whose keystrokes break a guardrail rule")
     ap.add_argument("--semantic-cache-namespace-mode", default="global",
                     choices=["global", "hard_namespace", "logical_namespace"])
     ap.add_argument("--cross-namespace-pairs", default="",
@@ -335,7 +337,8 @@ def main():
     proxy = LegoLinkProxy(transport, tokenizer=RuntimeTokenizer(a.runtime), repair_tokens=a.repair_tokens,
                           metrics_path=a.metrics, passthrough=a.passthrough, json_retries=a.json_retries,
                           namespace_mode=a.semantic_cache_namespace_mode,
-                          cross_namespace_pairs=[x for x in a.cross_namespace_pairs.split(",") if x.strip()])
+                          cross_namespace_pairs=[x for x in a.cross_namespace_pairs.split(",") if x.strip()],
+                          command_guardrail=a.command_guardrail)
     srv = ThreadingHTTPServer((a.host, a.port), make_handler(proxy))
     print(f"LegoLink proxy on http://{a.host}:{a.port} -> {a.runtime}", flush=True)
     srv.serve_forever()
