@@ -119,3 +119,90 @@ def safe_diagnostic_response(violation: str) -> str:
     return json.dumps({"analysis": "The previous command was blocked by the guardrail.",
                        "plan": "Inspect the workspace before acting.",
                        "commands": [{"keystrokes": ks, "duration": 1.0}], "task_complete": False})
+
+
+# ------------------------------------------------------------ verification
+# A command that changes files silently (a redirect, mkdir, chmod, cp / mv)
+# leaves the terminal pane blank, and small models then repeat it or guess.
+# The probe appended after such a command prints the evidence: the target's
+# listing, its size and its first bytes.  A command whose targets cannot be
+# named (a generated script) gets the task directory's listing instead.
+
+PROBE_MARK = "NOC_VERIFY"
+WORKDIR = "/app"
+PROBE_EXTRA_S = 1.0  # the pane is captured after `duration`: leave the probe time to print
+
+_REDIRECT = re.compile(r"(?<![0-9&])>>?\s*([^\s;&|<>]+)")
+_MUTATORS = {"mkdir": "all", "touch": "all", "chmod": "last", "chown": "last", "cp": "last", "mv": "last",
+             "ln": "last", "tee": "all"}
+_SCRIPT_RUN = re.compile(r"^\s*(python3?|bash|sh|node)\s+\S+")
+
+
+def _targets(ks: str) -> list[str]:
+    """Paths a command line writes: redirect targets, then the operands of
+    mutating commands (the destination of cp / mv / ln / chmod, every
+    operand of mkdir / touch / tee); options, modes and /dev/* are skipped."""
+    out: list[str] = []
+    for line in ks.splitlines():
+        for m in _REDIRECT.finditer(line):
+            out.append(m.group(1).strip("'\""))
+        for seg in re.split(r"&&|\|\||;|\|", line):
+            words = seg.split()
+            if not words or words[0] not in _MUTATORS:
+                continue
+            ops = [w.strip("'\"") for w in words[1:]
+                   if not w.startswith("-") and not re.fullmatch(r"[0-7]{3,4}|[ugoa]*[+-=][rwxXst]+", w)]
+            ops = [w for w in ops if not any(c in w for c in "<>")]
+            if ops:
+                out.extend(ops if _MUTATORS[words[0]] == "all" else ops[-1:])
+    seen, res = set(), []
+    for t in out:
+        if t and not t.startswith("/dev/") and t not in seen:
+            seen.add(t)
+            res.append(t)
+    return res
+
+
+def verification_probe(keystrokes: str) -> Optional[str]:
+    """Shell lines that print what ``keystrokes`` changed, or None for a
+    command that changes nothing observable."""
+    targets = _targets(keystrokes)
+    if not targets:
+        if not any(_SCRIPT_RUN.match(line) for line in keystrokes.splitlines()):
+            return None
+        return f"echo '{PROBE_MARK}: {WORKDIR}'; ls -la '{WORKDIR}'\n"
+    parts = []
+    for t in targets[:4]:
+        parts.append(f"echo '{PROBE_MARK}: {t}'; ls -ld '{t}'; if [ -f '{t}' ]; then "
+                     f"echo \"{PROBE_MARK}_FILE_BYTES $(wc -c < '{t}')\"; echo '{PROBE_MARK}_FILE_HEAD_BEGIN'; "
+                     f"head -c 400 '{t}'; echo; echo '{PROBE_MARK}_FILE_HEAD_END'; fi")
+    return "; ".join(parts) + "\n"
+
+
+def inject_verification(reply: str) -> tuple[str, Optional[str]]:
+    """Appends the probe to each command of a JSON reply that changes files
+    and lengthens its duration so the probe's output is on the captured
+    pane.  Returns (reply, first probed target or None).  Idempotent: a reply
+    that already carries probes, or changes nothing, comes back unchanged."""
+    try:
+        obj = json.loads(reply)
+    except (TypeError, ValueError):
+        return reply, None
+    if not isinstance(obj, dict) or not isinstance(obj.get("commands"), list):
+        return reply, None
+    if any(isinstance(c, dict) and PROBE_MARK in str(c.get("keystrokes", "")) for c in obj["commands"]):
+        return reply, None
+    first = None
+    for c in obj["commands"]:
+        if not isinstance(c, dict) or not isinstance(c.get("keystrokes"), str):
+            continue
+        probe = verification_probe(c["keystrokes"])
+        if probe is None:
+            continue
+        ks = c["keystrokes"] if c["keystrokes"].endswith("\n") else c["keystrokes"] + "\n"
+        c["keystrokes"] = ks + probe
+        c["duration"] = float(c.get("duration") or 0.0) + PROBE_EXTRA_S
+        if first is None:
+            t = _targets(ks)
+            first = t[0] if t else WORKDIR
+    return (json.dumps(obj), first) if first is not None else (reply, None)

@@ -251,6 +251,13 @@ class LegoLinkProxy:
                 if violation is not None:
                     self.stats["guardrail_blocked"] = self.stats.get("guardrail_blocked", 0) + 1
                     text = safe_diagnostic_response(violation)
+                else:
+                    from ..host.command_guardrail import inject_verification
+
+                    # commands that change files silently print what they changed
+                    text, probed = inject_verification(text)
+                    if probed is not None:
+                        self.stats["verification_probes"] = self.stats.get("verification_probes", 0) + 1
         self.transcripts.remember(key, list(payload.get("messages") or []) + [{"role": "assistant", "content": text}])
         usage = (res.execution.result.response or {}).get("usage") or {}
         return {"id": "chatcmpl-" + uuid.uuid4().hex[:24], "object": "chat.completion", "created": int(time.time()),

@@ -63,3 +63,32 @@ def test_proxy_reasks_then_blocks_a_violating_reply(monkeypatch):
     assert len(calls) == 3 and px.stats["guardrail_replans"] == 2 and px.stats["guardrail_blocked"] == 1
     assert "NOC_GUARDRAIL_BLOCKED" in text and cg.command_violation(text) is None
     assert "Do not repeat" in calls[-1][-1]["content"]
+
+
+def test_verification_probe_targets():
+    p = cg.verification_probe("echo 'Hello, world!' > /app/hello.txt\n")
+    assert "NOC_VERIFY" in p and "ls -ld '/app/hello.txt'" in p and "head -c 400 '/app/hello.txt'" in p
+    assert "NOC_VERIFY_FILE_BYTES" in p and "NOC_VERIFY_FILE_HEAD_BEGIN" in p and "NOC_VERIFY_FILE_HEAD_END" in p
+    assert "ls -ld '/app'" in cg.verification_probe("mkdir -p /app\n")
+    assert "ls -ld '/app/run.sh'" in cg.verification_probe("chmod 644 /app/run.sh\n")
+    assert "'644'" not in cg.verification_probe("chmod 644 /app/f.txt\n")
+    cp = cg.verification_probe("cp /app/a.csv /app/b.csv\n")
+    assert "head -c 400 '/app/b.csv'" in cp and "head -c 400 '/app/a.csv'" not in cp  # the destination, not the source
+    assert "ls -la '/app'" in cg.verification_probe("python3 /tmp/solve.py\n")  # unnamed outputs: the task directory
+    for read_only in ("cat /app/schema.json\n", "ls -la /app\n", "grep foo /app/x.txt 2>&1\n", "cmd > /dev/null\n"):
+        assert cg.verification_probe(read_only) is None, read_only
+
+
+def test_inject_verification():
+    o = json.dumps({"analysis": "w", "plan": "e",
+                    "commands": [{"keystrokes": "echo 'Hello, world!' > /app/hello.txt\n", "duration": 1.0}]})
+    i, reason = cg.inject_verification(o)
+    c = json.loads(i)["commands"][0]
+    assert reason == "/app/hello.txt" and c["duration"] > 1.0
+    assert c["keystrokes"].startswith("echo 'Hello, world!' > /app/hello.txt\n") and "NOC_VERIFY" in c["keystrokes"]
+    assert cg.command_violation(i) is None  # the probe never trips the guardrail
+    once, r1 = cg.inject_verification(json.dumps({"commands": [{"keystrokes": "mkdir -p /app\n", "duration": 1.0}]}))
+    twice, r2 = cg.inject_verification(once)
+    assert r1 and r2 is None and twice == once  # idempotent
+    ro = json.dumps({"commands": [{"keystrokes": "cat /app/schema.json\n", "duration": 1.0}]})
+    assert cg.inject_verification(ro) == (ro, None)
